@@ -1,0 +1,417 @@
+#!/usr/bin/env python
+"""Benchmark of the decode-sampling path (BASELINE metric: sampled rows/s and logits GB/s
+against HBM peak at V=262144, plus the p50 step latency at B=1).
+
+Workload (one "step" = one gs_sample over the batch): configuration C4, the throughput
+batch, B=4096 rows x V=262144 float32 logits (4 GiB, larger than L2), soft cap 30,
+256-id penalty history at 1.1/0.5/0.3, a 4096-state constraint bitmask at 2% density,
+temperature 0.8, topK 50, topP 0.95.  Rows are sharded evenly across the N GPUs (strong
+scaling, no collective on the data path).  Launched as one process per GPU (torchrun).
+
+Also reported on rank 0: the bfloat16 variant of C4, the p50/p95 step latency of C1
+(B=1, 256 sequential steps), the end-to-end rate through the host-buffer entry point
+(gs_sample_host), and the CPU oracle timed on the host cores as a baseline.
+
+`--impl reference` times the reference sampler's CPU restatement (oracle/oracle.cpp; the
+reference is TypeScript and there is no Node runtime on the machine) on all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+PKG = "gemma-webgpu-engine_b200"
+VOCAB = 262144
+GLOBAL_BATCH = 4096
+WORKLOAD_DESC = ("C4: B=4096 x V=262144 logits, soft cap 30, 256-id penalty history (1.1/0.5/0.3), "
+                 "4096-state constraint bitmask at 2%, temperature 0.8, topK 50, topP 0.95")
+METRIC = "sampled rows/s at V=262144 (C4 full pipeline)"
+UNIT = "rows/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"])
+    ap.add_argument("--no-extras", action="store_true", help="skip bf16 / latency / e2e / cpu legs")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_row(dtype: str):
+    """DRAM bytes per row of the streaming kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "stream_kernel_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        e = d.get(dtype)
+        return None if e is None else float(e["dram_bytes"]) / float(e["rows"])
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons, sampled every 100 ms into a temp file."""
+
+    FIELDS = ("uuid,timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float):
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 10 or parts[0] != self.uuid:
+                        continue
+                    try:
+                        ts = datetime.datetime.strptime(parts[1], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    except ValueError:
+                        continue
+                    rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
+        except FileNotFoundError:
+            pass
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        if len(inside) < 3:
+            inside = [r for r in rows if t0 - 2.0 <= r[0] <= t1 + 0.5] or rows
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": reasons, "samples": len(inside)}
+
+
+# ------------------------------------------------------------------------ our arm
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    pkg = importlib.import_module(PKG)
+    W = importlib.import_module(PKG + ".workloads")
+    L = pkg._lib
+
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    per = GLOBAL_BATCH // world
+    r0 = rank * per
+    wl = W.make("C4", device=dev, rows=GLOBAL_BATCH)
+    logits = wl.logits[r0:r0 + per].to(dtype).contiguous()
+    hist = wl.history[r0:r0 + per].contiguous()
+    hlen = wl.history_len[r0:r0 + per].contiguous()
+    mstate = wl.mask_state[r0:r0 + per].contiguous()
+    table = wl.mask_table
+    seeds = wl.seeds[r0:r0 + per]
+    del wl
+    torch.cuda.empty_cache()
+    rng = torch.tensor([pkg.SeededRandom(s).state for s in seeds], dtype=torch.float64, device=dev)
+    params = W.base_params(temperature=0.8, topK=50, topP=0.95, repetitionPenalty=1.1, presencePenalty=0.5,
+                           frequencyPenalty=0.3, repetitionWindow=256)
+    sampler = pkg.GpuSampler(local)
+    sampler.reserve(per, VOCAB, 50, hist.shape[1])
+    stream = torch.cuda.current_stream(dev)
+    out = None
+
+    def step():
+        nonlocal out
+        out = sampler.sample(logits, params, softcap=30.0, history=hist, history_len=hlen, mask_table=table,
+                             mask_state=mstate, rng_state=rng, stream=stream.cuda_stream, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    flags = out.flags.cpu().numpy().view(np.uint32)
+    assert not (flags & L.FLAG_ERRORS).any(), "row errors in the benchmark batch"
+
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
+    # timed region
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    L.lib().gs_profile_enable(sampler.handle, 1)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    import ctypes
+    s_ms, s_n, m_ms, m_n = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double(), ctypes.c_int64()
+    L.lib().gs_profile_read(sampler.handle, ctypes.byref(s_ms), ctypes.byref(s_n), ctypes.byref(m_ms),
+                            ctypes.byref(m_n))
+    L.lib().gs_profile_enable(sampler.handle, 0)
+    time.sleep(0.2)
+    clocks.stop()
+    clk = clocks.summary(t_wall0, t_wall1)
+    stream_avg_s = s_ms.value / max(1, s_n.value) / 1e3
+    merge_avg_s = m_ms.value / max(1, m_n.value) / 1e3
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+
+    esz = 2 if args.dtype == "bf16" else 4
+    bytes_per_row = VOCAB * esz + VOCAB // 8 + 4 * hist.shape[1]
+    total_rows = per * world
+    value = total_rows * args.steps / (elapsed_ms / 1e3)
+    peak, peak_kind = measured_peak()
+    achieved = per * bytes_per_row / stream_avg_s / 1e9
+    tpr = traffic_per_row(args.dtype)
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32" if args.dtype == "f32" else "bf16", "data": "synthetic (seeded torch Philox, C4 distributions)",
+        "config": {"workload": WORKLOAD_DESC, "global_batch": GLOBAL_BATCH, "rows_per_gpu": per, "vocab": VOCAB,
+                   "logits_dtype": args.dtype, "parallelism": f"row-sharded x{world} (no collective)",
+                   "l2": "inputs larger than L2 (rows x 1 MiB per GPU)"},
+        "logits_gbps": total_rows * bytes_per_row * args.steps / (elapsed_ms / 1e3) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "gs::stream_kernel", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": None if tpr is None else tpr * per,
+                     "algorithmic_bytes_per_launch": per * bytes_per_row,
+                     "avg_launch_us": stream_avg_s * 1e6, "merge_avg_launch_us": merge_avg_s * 1e6},
+        "gpu_launches": 2 * args.steps * world,
+        "clocks": clk,
+    }
+    if rank == 0 and not args.no_extras:
+        result.update(extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per))
+    sampler.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per):
+    import numpy as np
+    import torch
+
+    res = {}
+    stream = torch.cuda.current_stream(dev)
+    # ---- end to end through gs_sample_host: host (pinned) buffers, copies in the timed region
+    n_e2e = max(3, min(10, args.steps))
+    hx = logits.cpu().pin_memory().numpy() if logits.dtype == torch.float32 else None
+    if hx is None:
+        hx = logits.view(torch.int16).cpu().pin_memory().numpy()
+    hh = hist.cpu().pin_memory().numpy()
+    hl = hlen.cpu().pin_memory().numpy()
+    hs = mstate.cpu().pin_memory().numpy()
+    hr = torch.tensor([pkg.SeededRandom(s).state for s in seeds], dtype=torch.float64).pin_memory().numpy()
+    dt = pkg._lib.GS_DTYPE_F32 if logits.dtype == torch.float32 else pkg._lib.GS_DTYPE_BF16
+    for _ in range(2):
+        sampler.sample_host(hx, params, softcap=30.0, history=hh, history_len=hl, mask_table=table, mask_state=hs,
+                            rng_state=hr, stream=stream.cuda_stream, dtype=dt)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        sampler.sample_host(hx, params, softcap=30.0, history=hh, history_len=hl, mask_table=table, mask_state=hs,
+                            rng_state=hr, stream=stream.cuda_stream, dtype=dt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_s = e0.elapsed_time(e1) / 1e3
+    h2d = hx.nbytes + hh.nbytes + hl.nbytes + hs.nbytes + hr.nbytes
+    d2h = per * (4 + 4 + 8)
+    res["e2e"] = {"value": per * n_e2e / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                  "d2h_bytes_per_step": int(d2h), "steps": n_e2e,
+                  "api": "gs_sample_host (host logits/history/states in pinned memory, ids+flags+states back)"}
+    # ---- bf16 variant of the same batch
+    if args.dtype == "f32":
+        xb = logits.to(torch.bfloat16)
+        rng = torch.tensor([pkg.SeededRandom(s).state for s in seeds], dtype=torch.float64, device=dev)
+        for _ in range(10):
+            o = sampler.sample(xb, params, softcap=30.0, history=hist, history_len=hlen, mask_table=table,
+                               mask_state=mstate, rng_state=rng, stream=stream.cuda_stream)
+        n_b = max(10, min(500, args.steps // 4))
+        e0.record(stream)
+        for _ in range(n_b):
+            o = sampler.sample(xb, params, softcap=30.0, history=hist, history_len=hlen, mask_table=table,
+                               mask_state=mstate, rng_state=rng, stream=stream.cuda_stream, out=o)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        sb = e0.elapsed_time(e1) / 1e3
+        bpr = VOCAB * 2 + VOCAB // 8 + 4 * hist.shape[1]
+        res["bf16"] = {"value": per * n_b / sb, "unit": UNIT, "steps": n_b,
+                       "logits_gbps": per * bpr * n_b / sb / 1e9}
+        del xb
+    # ---- C1 latency: B=1, 256 sequential steps, fresh logits each step, one seeded stream
+    steps = 256
+    lg = torch.empty((steps, VOCAB), dtype=torch.float32, device=dev)
+    for s in range(steps):
+        lg[s] = W.make("C1", device=dev, step=s).logits[0]
+    p1 = W.base_params(temperature=0.8, topK=40, topP=0.95, repetitionWindow=0)
+    st = torch.tensor([pkg.SeededRandom(42).state], dtype=torch.float64, device=dev)
+    o1 = None
+    for s in range(16):
+        o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream, out=o1)
+    st.fill_(pkg.SeededRandom(42).state)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    evs[0].record(stream)
+    for s in range(steps):
+        o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream, out=o1)
+        evs[s + 1].record(stream)
+    torch.cuda.synchronize()
+    lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(steps))
+    res["latency_b1"] = {"workload": "C1: B=1, V=262144, soft cap 30, T=0.8, topK 40, topP 0.95, seed 42, "
+                                     "256 sequential steps",
+                         "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],
+                         "timing": "CUDA events between consecutive gs_sample calls (device time, no graph)"}
+    del lg
+    # ---- CPU baseline: the oracle on a bounded sample of the same rows, all host threads
+    res["cpu_baseline"] = cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per)
+    return res
+
+
+def cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per):
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    n = min(per, max(64, 4 * threads))
+    x = logits[:n].float().cpu().numpy()
+    h = hist[:n].cpu().numpy()
+    hl = hlen[:n].cpu().numpy()
+    ms = mstate[:n].cpu().numpy()
+    used = sorted(set(ms.tolist()))
+    remap = {s: i for i, s in enumerate(used)}
+    tb = table[torch.tensor(used, device=table.device)].cpu().numpy().view(np.uint32)
+    ms2 = np.array([remap[s] for s in ms.tolist()], dtype=np.int32)
+    st = np.array([O.seeded_init(s) for s in seeds[:n]], dtype=np.float64)
+    p = dict(params, repetitionWindow=h.shape[1])
+    t0 = time.perf_counter()
+    O.sample_rows(x, VOCAB, 30.0, h, hl, tb, ms2, [p], rng_state=st, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} rows of C4 (float32), oracle/oracle.cpp restating src/runtime/sampling.ts, "
+                      f"{threads} host threads, {dt:.2f} s wall"}
+
+
+# ------------------------------------------------------------------ reference arm
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    W = importlib.import_module(PKG + ".workloads")
+
+    threads = os.cpu_count() or 1
+    rows = threads  # one row per host thread per step
+    g = torch.Generator().manual_seed(31)
+    x = (torch.randn((rows, VOCAB), generator=g) * 2.0).numpy()
+    hist = torch.randint(0, VOCAB, (rows, 256), generator=g).to(torch.int32).numpy()
+    hlen = np.full(rows, 256, dtype=np.int32)
+    allowed = torch.rand((rows, VOCAB), generator=g) < 0.02
+    table = W.pack_bits(allowed).numpy().view(np.uint32)
+    mstate = np.arange(rows, dtype=np.int32)
+    p = W.base_params(temperature=0.8, topK=50, topP=0.95, repetitionPenalty=1.1, presencePenalty=0.5,
+                      frequencyPenalty=0.3, repetitionWindow=256)
+    st = np.array([O.seeded_init(3000 + i) for i in range(rows)], dtype=np.float64)
+
+    def step():
+        O.sample_rows(x, VOCAB, 30.0, hist, hlen, table, mstate, [p], rng_state=st, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = rows * args.steps / dt
+    sample = (f"{rows} C4-distributed rows per step (one per host thread), oracle/oracle.cpp (C++ restatement of "
+              f"src/runtime/sampling.ts; the TypeScript reference needs Node, which is not installed)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": WORKLOAD_DESC, "global_batch": GLOBAL_BATCH, "vocab": VOCAB,
+                   "parallelism": "host threads, rank 0 only"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

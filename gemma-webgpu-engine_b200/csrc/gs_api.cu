@@ -1,0 +1,665 @@
+// Host side of the C ABI declared in include/gsampler.h.
+#include "gs_internal.cuh"
+#include "../../include/gsampler.h"
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <array>
+#include <vector>
+
+using namespace gs;
+
+struct gs_ctx {
+  int device = 0;
+  std::string err;
+  // device workspace (plans | unit stats | unit candidates)
+  unsigned char* ws = nullptr;
+  size_t ws_bytes = 0;
+  // pinned staging for per-row plans and the event guarding its reuse
+  RowPlan* plans_host = nullptr;
+  size_t plans_cap = 0;
+  cudaEvent_t plans_ev = nullptr;
+  bool plans_ev_live = false;
+  // device staging of gs_sample_host
+  unsigned char* io = nullptr;
+  size_t io_bytes = 0;
+  unsigned long long* digest = nullptr;
+  int32_t* tok_dev = nullptr;
+  double* lp_dev = nullptr;
+  size_t tok_cap = 0;
+  // kernel timing: events around the streaming pass and the merge of each gs_sample
+  bool profile = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<std::array<cudaEvent_t, 3>> ev_live;
+};
+
+namespace {
+
+gs_status fail(gs_ctx* c, gs_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return s;
+}
+
+gs_status cuda_fail(gs_ctx* c, cudaError_t e, const char* what) {
+  return fail(c, GS_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int d) {
+    cudaGetDevice(&prev);
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~DeviceGuard() {
+    int cur;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+gs_status ensure_ws(gs_ctx* c, size_t bytes) {
+  if (bytes <= c->ws_bytes) return GS_OK;
+  if (c->ws) {
+    cudaDeviceSynchronize();
+    cudaFree(c->ws);
+    c->ws = nullptr;
+    c->ws_bytes = 0;
+  }
+  const size_t want = align_up(bytes + bytes / 4, 1 << 20);
+  cudaError_t e = cudaMalloc(&c->ws, want);
+  if (e != cudaSuccess) return fail(c, GS_ENOMEM, "workspace allocation of %zu bytes failed: %s", want, cudaGetErrorString(e));
+  c->ws_bytes = want;
+  return GS_OK;
+}
+
+gs_status ensure_io(gs_ctx* c, size_t bytes) {
+  if (bytes <= c->io_bytes) return GS_OK;
+  if (c->io) {
+    cudaDeviceSynchronize();
+    cudaFree(c->io);
+    c->io = nullptr;
+    c->io_bytes = 0;
+  }
+  const size_t want = align_up(bytes, 1 << 20);
+  cudaError_t e = cudaMalloc(&c->io, want);
+  if (e != cudaSuccess) return fail(c, GS_ENOMEM, "staging allocation of %zu bytes failed: %s", want, cudaGetErrorString(e));
+  c->io_bytes = want;
+  return GS_OK;
+}
+
+gs_status ensure_plans_host(gs_ctx* c, size_t n) {
+  if (c->plans_ev_live) {
+    cudaEventSynchronize(c->plans_ev);  // the previous upload has left the staging buffer
+    c->plans_ev_live = false;
+  }
+  if (n <= c->plans_cap) return GS_OK;
+  if (c->plans_host) cudaFreeHost(c->plans_host);
+  c->plans_host = nullptr;
+  c->plans_cap = 0;
+  cudaError_t e = cudaMallocHost(&c->plans_host, n * sizeof(RowPlan));
+  if (e != cudaSuccess) return cuda_fail(c, e, "pinned plan staging");
+  c->plans_cap = n;
+  return GS_OK;
+}
+
+// validateDecodingConfig (src/runtime/decoding.ts:31-59), for the fields sampleToken reads.
+bool valid_params(const gs_params& p, std::string* why) {
+  std::vector<std::string> errors;
+  if (!std::isfinite(p.temperature) || p.temperature < 0) errors.push_back("temperature must be >= 0");
+  if (p.top_k < 0) errors.push_back("topK must be a non-negative integer");
+  const double v3[3] = {p.top_p, p.min_p, p.typical_p};
+  const char* n3[3] = {"topP", "minP", "typicalP"};
+  for (int i = 0; i < 3; ++i)
+    if (!std::isfinite(v3[i]) || v3[i] < 0 || v3[i] > 1) errors.push_back(std::string(n3[i]) + " must be between 0 and 1");
+  if (!std::isfinite(p.repetition_penalty) || p.repetition_penalty <= 0) errors.push_back("repetitionPenalty must be > 0");
+  if (!std::isfinite(p.frequency_penalty) || p.frequency_penalty < 0)
+    errors.push_back("frequencyPenalty must be finite and non-negative");
+  if (!std::isfinite(p.presence_penalty) || p.presence_penalty < 0)
+    errors.push_back("presencePenalty must be finite and non-negative");
+  if (errors.empty()) return true;
+  std::string s = "Invalid Gemma decoding config: ";
+  for (size_t i = 0; i < errors.size(); ++i) s += (i ? "; " : "") + errors[i];
+  *why = s;
+  return false;
+}
+
+RowPlan make_plan(const gs_params& p, int64_t vocab) {
+  RowPlan r{};
+  r.temperature = p.temperature;
+  r.top_p = p.top_p;
+  r.min_p = p.min_p;
+  r.typical_p = p.typical_p;
+  r.repetition_penalty = p.repetition_penalty;
+  r.presence_penalty = p.presence_penalty;
+  r.frequency_penalty = p.frequency_penalty;
+  r.top_k = p.top_k;
+  if (p.temperature == 0) {
+    r.mode = kModeGreedy;
+    r.k_eff = 1;
+    r.a2 = 0;
+    r.a2_hi = 0;
+    r.a2_lo = FLT_MIN;
+  } else {
+    r.a2 = 1.4426950408889634 / p.temperature;
+    float hi = static_cast<float>(r.a2);
+    if (static_cast<double>(hi) > r.a2) hi = std::nextafter(hi, 0.0f);
+    float lo = static_cast<float>(r.a2 - static_cast<double>(hi));
+    if (!(lo >= FLT_MIN)) lo = FLT_MIN;
+    r.a2_hi = hi;
+    r.a2_lo = lo;
+    if (p.top_k >= 1 && p.top_k <= GS_MAX_TOP_K) {
+      r.mode = kModeSmallK;
+      r.k_eff = static_cast<int32_t>(std::min<int64_t>(p.top_k, vocab));
+    } else {
+      r.mode = kModeLarge;
+      r.k_eff = 0;
+    }
+  }
+  return r;
+}
+
+int pow2ceil(int64_t n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+struct Layout {
+  int splits;
+  int64_t chunk;
+  int kcap;
+  int kc;
+  int kmax;
+  bool any_large;
+  bool any_sample;
+  size_t plans_off, stats_off, cands_off, total;
+  size_t stream_smem, fin_smem, large_smem;
+  int hist_cap, ent_cap, pack_cap;
+};
+
+gs_status plan_layout(gs_ctx* c, const gs_batch* b, const std::vector<RowPlan>& plans, Layout* L) {
+  const int rows = b->rows;
+  int kmax = 0;
+  bool any_large = false, any_sample = false;
+  for (const auto& p : plans) {
+    kmax = std::max(kmax, p.k_eff);
+    any_large |= p.mode == kModeLarge;
+    any_sample |= p.mode != kModeGreedy;
+  }
+  const int nplans = static_cast<int>(plans.size());
+  (void)nplans;
+  // vocabulary splits: enough units to fill the GPU, chunks of >= 4096 ids, and at most
+  // 16384 streamed candidates per row for the merge
+  const int64_t V = b->vocab;
+  const int target_units = 148 * 4;
+  int S = 1;
+  while (static_cast<int64_t>(rows) * S < target_units && V / (2 * S) >= 4096 && 2 * S * std::max(kmax, 1) <= 16384 && S < 256)
+    S *= 2;
+  int64_t chunk = (V + S - 1) / S;
+  chunk = (chunk + 1023) / 1024 * 1024;
+  S = static_cast<int>((V + chunk - 1) / chunk);
+  const int kcap = std::max(kmax, 1);
+  int kc = 256;
+  while (kc < 2 * kmax) kc <<= 1;
+  if (kc > 4096) return fail(c, GS_EUNSUPPORTED, "topK above %d is not supported by the streaming buffer", GS_MAX_TOP_K);
+  L->splits = S;
+  L->chunk = chunk;
+  L->kcap = kcap;
+  L->kc = kc;
+  L->kmax = kmax;
+  L->any_large = any_large;
+  L->any_sample = any_sample;
+  const int64_t units = static_cast<int64_t>(rows) * S;
+  L->plans_off = 0;
+  L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
+  L->cands_off = align_up(L->stats_off + static_cast<size_t>(units) * sizeof(UnitStat), 256);
+  L->total = align_up(L->cands_off + static_cast<size_t>(units) * kcap * 8, 256);
+  L->stream_smem = stream_smem_bytes(chunk, kc);
+  const int64_t hs = b->history ? b->history_stride : 0;
+  L->hist_cap = pow2ceil(std::max<int64_t>(hs, 1));
+  L->pack_cap = S > 1 ? S * kcap : 0;
+  L->ent_cap = pow2ceil(std::max<int64_t>(std::min<int64_t>(static_cast<int64_t>(S) * kcap, kmax) + hs, 1));
+  L->fin_smem = finalize_smem_bytes(L->hist_cap, L->ent_cap, L->pack_cap);
+  if (L->fin_smem > 220 * 1024)
+    return fail(c, GS_EUNSUPPORTED, "merge needs %zu bytes of shared memory (topK %d, history %lld)", L->fin_smem, kmax,
+                static_cast<long long>(hs));
+  L->large_smem = any_large ? large_smem_bytes(V, L->hist_cap) : 0;
+  if (L->large_smem > 220 * 1024) return fail(c, GS_EUNSUPPORTED, "vocabulary too large for the histogram path");
+  return GS_OK;
+}
+
+gs_status check_batch(gs_ctx* c, const gs_batch* b, const gs_outputs* o) {
+  if (!c) return GS_EINVAL;
+  if (!b || !o) return fail(c, GS_EINVAL, "batch and outputs are required");
+  if (b->rows < 0) return fail(c, GS_EINVAL, "rows must be >= 0");
+  if (b->vocab <= 0) return fail(c, GS_EEMPTY, "Cannot sample empty logits");
+  if (b->vocab >= (1ll << 31)) return fail(c, GS_EINVAL, "vocab must be below 2^31");
+  if (b->row_stride < b->vocab) return fail(c, GS_EINVAL, "row_stride must be >= vocab");
+  if (b->dtype != GS_DTYPE_F32 && b->dtype != GS_DTYPE_BF16) return fail(c, GS_EINVAL, "unknown dtype %d", b->dtype);
+  if (b->rows > 0 && !b->logits) return fail(c, GS_EINVAL, "logits is NULL");
+  if (!(b->softcap >= 0) || !std::isfinite(b->softcap)) return fail(c, GS_EINVAL, "softcap must be finite and >= 0");
+  if (!b->params || (b->params_count != 1 && b->params_count != b->rows))
+    return fail(c, GS_EINVAL, "params_count must be 1 or rows");
+  if (b->history && (b->history_stride < 0 || b->history_stride > GS_MAX_HISTORY))
+    return fail(c, GS_EUNSUPPORTED, "history_stride must be in [0, %d]", GS_MAX_HISTORY);
+  if (b->history && !b->history_len) return fail(c, GS_EINVAL, "history_len is required with history");
+  if (b->mask_table) {
+    if (!b->mask_state) return fail(c, GS_EINVAL, "mask_state is required with mask_table");
+    if (b->mask_words < (b->vocab + 31) / 32) return fail(c, GS_EINVAL, "mask_words must be >= ceil(vocab/32)");
+    if (b->mask_states <= 0) return fail(c, GS_EINVAL, "mask_states must be > 0");
+  }
+  if (b->rows > 0 && !o->ids) return fail(c, GS_EINVAL, "outputs.ids is NULL");
+  if (o->cand_ids && o->cand_cap <= 0) return fail(c, GS_EINVAL, "cand_cap must be > 0 with cand_ids");
+  return GS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+gs_status gs_create(int device, gs_ctx** out) {
+  if (!out) return GS_EINVAL;
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || device < 0 || device >= n) return GS_ECUDA;
+  gs_ctx* c = new gs_ctx();
+  c->device = device;
+  DeviceGuard g(device);
+  e = cudaEventCreateWithFlags(&c->plans_ev, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaMalloc(&c->digest, sizeof(unsigned long long));
+  if (e != cudaSuccess) {
+    delete c;
+    return GS_ECUDA;
+  }
+  *out = c;
+  return GS_OK;
+}
+
+gs_status gs_destroy(gs_ctx* c) {
+  if (!c) return GS_OK;
+  DeviceGuard g(c->device);
+  cudaDeviceSynchronize();
+  if (c->ws) cudaFree(c->ws);
+  if (c->io) cudaFree(c->io);
+  if (c->digest) cudaFree(c->digest);
+  if (c->tok_dev) cudaFree(c->tok_dev);
+  if (c->lp_dev) cudaFree(c->lp_dev);
+  if (c->plans_host) cudaFreeHost(c->plans_host);
+  if (c->plans_ev) cudaEventDestroy(c->plans_ev);
+  for (auto& evs : c->ev_live)
+    for (auto ev : evs) cudaEventDestroy(ev);
+  for (auto ev : c->ev_pool) cudaEventDestroy(ev);
+  delete c;
+  return GS_OK;
+}
+
+const char* gs_last_error(const gs_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+gs_status gs_reserve(gs_ctx* c, int32_t rows, int64_t vocab, int32_t max_top_k, int64_t history_stride) {
+  if (!c || rows < 0 || vocab <= 0) return GS_EINVAL;
+  DeviceGuard g(c->device);
+  gs_params p{};
+  p.temperature = 1.0;
+  p.top_k = std::max(1, std::min(max_top_k, GS_MAX_TOP_K));
+  p.top_p = 1;
+  p.repetition_penalty = 1;
+  gs_batch b{};
+  b.rows = rows;
+  b.vocab = vocab;
+  b.row_stride = vocab;
+  b.params = &p;
+  b.params_count = 1;
+  b.history = history_stride > 0 ? reinterpret_cast<const int32_t*>(16) : nullptr;
+  b.history_stride = history_stride;
+  std::vector<RowPlan> plans(1, make_plan(p, vocab));
+  Layout L;
+  gs_status s = plan_layout(c, &b, plans, &L);
+  if (s != GS_OK) return s;
+  // per-row plans may be uploaded: size for rows of them
+  const size_t bytes = std::max(L.total, align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256) + (L.total - L.stats_off));
+  s = ensure_ws(c, bytes);
+  if (s != GS_OK) return s;
+  return ensure_plans_host(c, std::max<size_t>(rows, 1));
+}
+
+gs_status gs_sample(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stream) {
+  gs_status s = check_batch(c, b, o);
+  if (s != GS_OK) return s;
+  if (b->rows == 0) return GS_OK;
+  DeviceGuard g(c->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rows = b->rows;
+  const int np = b->params_count;
+  std::vector<RowPlan> plans(np);
+  for (int i = 0; i < np; ++i) {
+    std::string why;
+    if (!valid_params(b->params[i], &why)) return fail(c, GS_EINVAL, "%s", why.c_str());
+    plans[i] = make_plan(b->params[i], b->vocab);
+  }
+  bool any_sample = false;
+  for (const auto& p : plans) any_sample |= p.mode != kModeGreedy;
+  if (any_sample && !b->rng_state && !b->uniforms) return fail(c, GS_EINVAL, "rng_state or uniforms is required");
+  Layout L;
+  s = plan_layout(c, b, plans, &L);
+  if (s != GS_OK) return s;
+  s = ensure_ws(c, L.total);
+  if (s != GS_OK) return s;
+  const RowPlan* dplans = nullptr;
+  if (np > 1) {
+    s = ensure_plans_host(c, np);
+    if (s != GS_OK) return s;
+    std::memcpy(c->plans_host, plans.data(), np * sizeof(RowPlan));
+    dplans = reinterpret_cast<const RowPlan*>(c->ws + L.plans_off);
+    cudaError_t e = cudaMemcpyAsync(const_cast<RowPlan*>(dplans), c->plans_host, np * sizeof(RowPlan), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "plan upload");
+    cudaEventRecord(c->plans_ev, st);
+    c->plans_ev_live = true;
+  }
+  UnitStat* stats = reinterpret_cast<UnitStat*>(c->ws + L.stats_off);
+  unsigned long long* cands = reinterpret_cast<unsigned long long*>(c->ws + L.cands_off);
+  const float cap = b->softcap;
+  const float inv_cap = cap != 0.0f ? static_cast<float>(1.0 / static_cast<double>(cap)) : 0.0f;
+
+  StreamArgs sa{};
+  sa.logits = b->logits;
+  sa.vocab = b->vocab;
+  sa.row_stride = b->row_stride;
+  sa.vocab_offset = 0;
+  sa.softcap = cap;
+  sa.inv_softcap = inv_cap;
+  sa.want_raw = o->logprob != nullptr;
+  sa.splits = L.splits;
+  sa.chunk = L.chunk;
+  sa.kcap = L.kcap;
+  sa.kc = L.kc;
+  sa.plans = dplans;
+  sa.plan0 = plans[0];
+  sa.history = b->history;
+  sa.history_len = b->history ? b->history_len : nullptr;
+  sa.history_stride = b->history ? b->history_stride : 0;
+  sa.mask_table = b->mask_table;
+  sa.mask_states = b->mask_states;
+  sa.mask_words = b->mask_words;
+  sa.mask_state = b->mask_table ? b->mask_state : nullptr;
+  sa.stats = stats;
+  sa.cands = cands;
+  std::array<cudaEvent_t, 3> evs{};
+  if (c->profile) {
+    for (auto& ev : evs) {
+      if (c->ev_pool.empty()) {
+        cudaEvent_t ne;
+        if (cudaEventCreate(&ne) != cudaSuccess) return fail(c, GS_ECUDA, "event creation");
+        c->ev_pool.push_back(ne);
+      }
+      ev = c->ev_pool.back();
+      c->ev_pool.pop_back();
+    }
+    cudaEventRecord(evs[0], st);
+  }
+  cudaError_t e = launch_stream(sa, b->dtype, rows, L.stream_smem, st);
+  if (e != cudaSuccess) return cuda_fail(c, e, "streaming pass launch");
+
+  FinalizeArgs fa{};
+  fa.logits = b->logits;
+  fa.vocab = b->vocab;
+  fa.row_stride = b->row_stride;
+  fa.softcap = cap;
+  fa.inv_softcap = inv_cap;
+  fa.want_raw = sa.want_raw;
+  fa.splits = L.splits;
+  fa.kcap = L.kcap;
+  fa.hist_cap = L.hist_cap;
+  fa.ent_cap = L.ent_cap;
+  fa.pack_cap = L.pack_cap;
+  fa.plans = dplans;
+  fa.plan0 = plans[0];
+  fa.history = sa.history;
+  fa.history_len = sa.history_len;
+  fa.history_stride = sa.history_stride;
+  fa.mask_table = b->mask_table;
+  fa.mask_states = b->mask_states;
+  fa.mask_words = b->mask_words;
+  fa.mask_state = sa.mask_state;
+  fa.stats = stats;
+  fa.cands = cands;
+  fa.rng_state = b->rng_state;
+  fa.uniforms = b->uniforms;
+  fa.ids = o->ids;
+  fa.logprob = o->logprob;
+  fa.flags = o->flags;
+  fa.cand_ids = o->cand_ids;
+  fa.cand_probs = o->cand_probs;
+  fa.cand_count = o->cand_count;
+  fa.cand_cap = o->cand_cap;
+  bool any_small = false;
+  for (const auto& p : plans) any_small |= p.mode != kModeLarge;
+  if (c->profile) cudaEventRecord(evs[1], st);
+  if (any_small) {
+    e = launch_finalize(fa, b->dtype, rows, L.fin_smem, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "merge launch");
+  }
+  if (L.any_large) {
+    e = launch_large(fa, b->dtype, rows, L.large_smem, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "histogram path launch");
+  }
+  if (c->profile) {
+    cudaEventRecord(evs[2], st);
+    c->ev_live.push_back(evs);
+  }
+  return GS_OK;
+}
+
+gs_status gs_sample_host(gs_ctx* c, const gs_batch* hb, const gs_outputs* ho, void* stream) {
+  gs_status s = check_batch(c, hb, ho);
+  if (s != GS_OK) return s;
+  if (hb->rows == 0) return GS_OK;
+  DeviceGuard g(c->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = hb->rows;
+  const size_t esz = hb->dtype == GS_DTYPE_F32 ? 4 : 2;
+  // staging layout
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  const size_t o_logits = take(static_cast<size_t>(rows) * hb->row_stride * esz);
+  const size_t o_hist = hb->history ? take(static_cast<size_t>(rows) * hb->history_stride * 4) : 0;
+  const size_t o_hlen = hb->history ? take(static_cast<size_t>(rows) * 4) : 0;
+  const size_t o_mstate = hb->mask_table ? take(static_cast<size_t>(rows) * 4) : 0;
+  const size_t o_rng = hb->rng_state ? take(static_cast<size_t>(rows) * 8) : 0;
+  const size_t o_uni = hb->uniforms ? take(static_cast<size_t>(rows) * 8) : 0;
+  const size_t o_ids = take(static_cast<size_t>(rows) * 4);
+  const size_t o_lp = ho->logprob ? take(static_cast<size_t>(rows) * 8) : 0;
+  const size_t o_fl = take(static_cast<size_t>(rows) * 4);
+  const size_t o_cid = ho->cand_ids ? take(static_cast<size_t>(rows) * ho->cand_cap * 4) : 0;
+  const size_t o_cp = ho->cand_probs ? take(static_cast<size_t>(rows) * ho->cand_cap * 8) : 0;
+  const size_t o_cc = ho->cand_count ? take(static_cast<size_t>(rows) * 4) : 0;
+  s = ensure_io(c, off);
+  if (s != GS_OK) return s;
+  unsigned char* io = c->io;
+  auto h2d = [&](size_t at, const void* src, size_t bytes) {
+    return cudaMemcpyAsync(io + at, src, bytes, cudaMemcpyHostToDevice, st);
+  };
+  cudaError_t e = h2d(o_logits, hb->logits, static_cast<size_t>(rows) * hb->row_stride * esz);
+  if (hb->history && e == cudaSuccess) e = h2d(o_hist, hb->history, static_cast<size_t>(rows) * hb->history_stride * 4);
+  if (hb->history && e == cudaSuccess) e = h2d(o_hlen, hb->history_len, static_cast<size_t>(rows) * 4);
+  if (hb->mask_table && e == cudaSuccess) e = h2d(o_mstate, hb->mask_state, static_cast<size_t>(rows) * 4);
+  if (hb->rng_state && e == cudaSuccess) e = h2d(o_rng, hb->rng_state, static_cast<size_t>(rows) * 8);
+  if (hb->uniforms && e == cudaSuccess) e = h2d(o_uni, hb->uniforms, static_cast<size_t>(rows) * 8);
+  if (e != cudaSuccess) return cuda_fail(c, e, "input upload");
+  gs_batch db = *hb;
+  db.logits = io + o_logits;
+  db.history = hb->history ? reinterpret_cast<const int32_t*>(io + o_hist) : nullptr;
+  db.history_len = hb->history ? reinterpret_cast<const int32_t*>(io + o_hlen) : nullptr;
+  db.mask_state = hb->mask_table ? reinterpret_cast<const int32_t*>(io + o_mstate) : nullptr;
+  db.rng_state = hb->rng_state ? reinterpret_cast<double*>(io + o_rng) : nullptr;
+  db.uniforms = hb->uniforms ? reinterpret_cast<const double*>(io + o_uni) : nullptr;
+  gs_outputs dout{};
+  dout.ids = reinterpret_cast<int32_t*>(io + o_ids);
+  dout.logprob = ho->logprob ? reinterpret_cast<double*>(io + o_lp) : nullptr;
+  dout.flags = reinterpret_cast<uint32_t*>(io + o_fl);
+  dout.cand_ids = ho->cand_ids ? reinterpret_cast<int32_t*>(io + o_cid) : nullptr;
+  dout.cand_probs = ho->cand_probs ? reinterpret_cast<double*>(io + o_cp) : nullptr;
+  dout.cand_count = ho->cand_count ? reinterpret_cast<int32_t*>(io + o_cc) : nullptr;
+  dout.cand_cap = ho->cand_cap;
+  s = gs_sample(c, &db, &dout, stream);
+  if (s != GS_OK) return s;
+  std::vector<uint32_t> flags_local;
+  uint32_t* flags_host = ho->flags;
+  if (!flags_host) {
+    flags_local.resize(rows);
+    flags_host = flags_local.data();
+  }
+  auto d2h = [&](void* dst, size_t at, size_t bytes) {
+    return cudaMemcpyAsync(dst, io + at, bytes, cudaMemcpyDeviceToHost, st);
+  };
+  e = d2h(ho->ids, o_ids, rows * 4);
+  if (e == cudaSuccess) e = d2h(flags_host, o_fl, rows * 4);
+  if (ho->logprob && e == cudaSuccess) e = d2h(ho->logprob, o_lp, rows * 8);
+  if (ho->cand_ids && e == cudaSuccess) e = d2h(ho->cand_ids, o_cid, rows * ho->cand_cap * 4);
+  if (ho->cand_probs && e == cudaSuccess) e = d2h(ho->cand_probs, o_cp, rows * ho->cand_cap * 8);
+  if (ho->cand_count && e == cudaSuccess) e = d2h(ho->cand_count, o_cc, rows * 4);
+  if (hb->rng_state && e == cudaSuccess) e = d2h(hb->rng_state, o_rng, rows * 8);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(c, e, "sampling");
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint32_t f = flags_host[r];
+    if (f & GS_FLAG_ERR_DEADEND) return fail(c, GS_EDEADEND, "Generation constraint reached a tokenization dead end");
+    if (f & GS_FLAG_ERR_NONFINITE) return fail(c, GS_ENONFINITE, "row %lld: logits contain NaN or +Infinity", static_cast<long long>(r));
+    if (f & GS_FLAG_ERR_INVALID) return fail(c, GS_EINVAL, "row %lld: mask state out of range", static_cast<long long>(r));
+    if (f & GS_FLAG_ERR_UNSUPPORTED) return fail(c, GS_EUNSUPPORTED, "row %lld: request outside the histogram path", static_cast<long long>(r));
+    if (f & GS_FLAG_ERR_TIMEOUT) return fail(c, GS_ETIMEOUT, "row %lld: device wait timed out", static_cast<long long>(r));
+  }
+  return GS_OK;
+}
+
+gs_status gs_token_log_probability(gs_ctx* c, const void* logits, int32_t dtype, int32_t rows, int64_t vocab,
+                                   int64_t row_stride, float softcap, const int32_t* tokens, double* out, void* stream) {
+  if (!c) return GS_EINVAL;
+  if (rows < 0 || (rows > 0 && (!logits || !tokens || !out))) return fail(c, GS_EINVAL, "bad arguments");
+  if (row_stride < vocab) return fail(c, GS_EINVAL, "row_stride must be >= vocab");
+  DeviceGuard g(c->device);
+  for (int r = 0; r < rows; ++r)
+    if (tokens[r] < 0 || tokens[r] >= vocab)
+      return fail(c, GS_EINVAL, "Token %d is outside logits length %lld", tokens[r], static_cast<long long>(vocab));
+  if (rows == 0) return GS_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (static_cast<size_t>(rows) > c->tok_cap) {
+    if (c->tok_dev) cudaFree(c->tok_dev);
+    if (c->lp_dev) cudaFree(c->lp_dev);
+    c->tok_dev = nullptr;
+    c->lp_dev = nullptr;
+    c->tok_cap = 0;
+    if (cudaMalloc(&c->tok_dev, rows * 4) != cudaSuccess || cudaMalloc(&c->lp_dev, rows * 8) != cudaSuccess)
+      return fail(c, GS_ENOMEM, "log-probability staging");
+    c->tok_cap = rows;
+  }
+  cudaError_t e = cudaMemcpyAsync(c->tok_dev, tokens, rows * 4, cudaMemcpyHostToDevice, st);
+  const float inv = softcap != 0.0f ? static_cast<float>(1.0 / static_cast<double>(softcap)) : 0.0f;
+  if (e == cudaSuccess) e = launch_logprob(logits, dtype, rows, vocab, row_stride, softcap, inv, c->tok_dev, c->lp_dev, nullptr, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, c->lp_dev, rows * 8, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(c, e, "log probability");
+  return GS_OK;
+}
+
+gs_status gs_mask_constraint_logits(gs_ctx* c, const float* raw, int64_t vocab, const int32_t* legal, int64_t n_legal,
+                                    const int32_t* term, int64_t n_term, float* out, void* stream) {
+  if (!c) return GS_EINVAL;
+  if (vocab < 0 || (vocab > 0 && (!raw || !out)) || (n_legal > 0 && !legal) || (n_term > 0 && !term))
+    return fail(c, GS_EINVAL, "bad arguments");
+  DeviceGuard g(c->device);
+  cudaError_t e = launch_mask_logits(raw, vocab, legal, n_legal, term, n_term, out, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GS_OK : cuda_fail(c, e, "mask");
+}
+
+gs_status gs_build_mask_row(gs_ctx* c, int64_t vocab, const int32_t* legal, int64_t n_legal, const int32_t* term,
+                            int64_t n_term, uint32_t* row_out, void* stream) {
+  if (!c) return GS_EINVAL;
+  if (vocab <= 0 || !row_out || (n_legal > 0 && !legal) || (n_term > 0 && !term)) return fail(c, GS_EINVAL, "bad arguments");
+  DeviceGuard g(c->device);
+  cudaError_t e = launch_build_mask_row(vocab, legal, n_legal, term, n_term, row_out, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GS_OK : cuda_fail(c, e, "mask row");
+}
+
+gs_status gs_softcap(gs_ctx* c, const float* in, float* out, int64_t n, float cap, void* stream) {
+  if (!c) return GS_EINVAL;
+  if (n < 0 || (n > 0 && (!in || !out)) || !(cap > 0) || !std::isfinite(cap)) return fail(c, GS_EINVAL, "bad arguments");
+  DeviceGuard g(c->device);
+  const float inv = static_cast<float>(1.0 / static_cast<double>(cap));
+  cudaError_t e = launch_softcap(in, out, n, cap, inv, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GS_OK : cuda_fail(c, e, "softcap");
+}
+
+gs_status gs_softcap_digest(gs_ctx* c, uint64_t lo, uint64_t hi, float cap, uint64_t* digest_host) {
+  if (!c) return GS_EINVAL;
+  if (!digest_host || hi < lo || hi > (1ull << 32) || !(cap > 0)) return fail(c, GS_EINVAL, "bad arguments");
+  DeviceGuard g(c->device);
+  const float inv = static_cast<float>(1.0 / static_cast<double>(cap));
+  cudaError_t e = launch_softcap_digest(lo, hi, cap, inv, c->digest, nullptr);
+  unsigned long long v = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&v, c->digest, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(c, e, "softcap digest");
+  *digest_host = v;
+  return GS_OK;
+}
+
+gs_status gs_profile_enable(gs_ctx* c, int32_t enable) {
+  if (!c) return GS_EINVAL;
+  c->profile = enable != 0;
+  return GS_OK;
+}
+
+gs_status gs_profile_read(gs_ctx* c, double* stream_ms, int64_t* stream_launches, double* merge_ms,
+                          int64_t* merge_launches) {
+  if (!c) return GS_EINVAL;
+  DeviceGuard g(c->device);
+  double s_ms = 0, m_ms = 0;
+  int64_t n = 0;
+  for (auto& evs : c->ev_live) {
+    cudaError_t e = cudaEventSynchronize(evs[2]);
+    if (e != cudaSuccess) return cuda_fail(c, e, "profile read");
+    float a = 0, b = 0;
+    cudaEventElapsedTime(&a, evs[0], evs[1]);
+    cudaEventElapsedTime(&b, evs[1], evs[2]);
+    s_ms += a;
+    m_ms += b;
+    ++n;
+    for (auto ev : evs) c->ev_pool.push_back(ev);
+  }
+  c->ev_live.clear();
+  if (stream_ms) *stream_ms = s_ms;
+  if (stream_launches) *stream_launches = n;
+  if (merge_ms) *merge_ms = m_ms;
+  if (merge_launches) *merge_launches = n;
+  return GS_OK;
+}
+
+int64_t gs_shard_record_bytes(int32_t max_top_k) {
+  return static_cast<int64_t>(sizeof(UnitStat)) + 8ll * std::max(1, max_top_k);
+}
+
+gs_status gs_shard_partials(gs_ctx* c, const gs_batch*, int64_t, int64_t, void*, void*) {
+  return fail(c, GS_EUNSUPPORTED, "vocabulary-sharded mode is not built yet");
+}
+
+gs_status gs_shard_merge(gs_ctx* c, const gs_batch*, int64_t, int32_t, const void*, const gs_outputs*, void*) {
+  return fail(c, GS_EUNSUPPORTED, "vocabulary-sharded mode is not built yet");
+}
+
+}  // extern "C"

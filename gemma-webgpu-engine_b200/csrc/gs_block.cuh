@@ -1,0 +1,242 @@
+// Block-level building blocks for the per-row kernels (sorts, scans, reductions).
+#pragma once
+#include "gs_device.cuh"
+
+namespace gs {
+
+// One candidate of a row: exact double sort key (logit/T, or the logit itself for
+// temperature 0), token id, and whether it came from the penalty history.
+struct Ent {
+  double key;
+  uint32_t id;
+  uint32_t kind;  // 0 = streamed, 1 = penalised, 2 = masked fill, 0xffffffff = padding
+};
+
+// Reference order (src/runtime/sampling.ts:33-35): larger key first, lower id first.
+__device__ __forceinline__ bool ent_before(const Ent& a, const Ent& b) {
+  return a.key > b.key || (a.key == b.key && a.id < b.id);
+}
+
+// In-place bitonic sort of e[0, n2) (n2 a power of two) into ent_before order.
+__device__ inline void bitonic_sort_ent(Ent* e, int n2) {
+  for (int k = 2; k <= n2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const Ent a = e[i], b = e[ixj];
+          const bool up = (i & k) == 0;
+          if (up ? ent_before(b, a) : ent_before(a, b)) {
+            e[i] = b;
+            e[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Ascending bitonic sort of (key, payload) pairs by (key, payload).
+__device__ inline void bitonic_sort_kv(unsigned long long* key, uint32_t* val, int n2) {
+  for (int k = 2; k <= n2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long ka = key[i], kb = key[ixj];
+          const uint32_t va = val[i], vb = val[ixj];
+          const bool a_gt_b = ka > kb || (ka == kb && va > vb);
+          const bool up = (i & k) == 0;
+          if (up ? a_gt_b : !a_gt_b) {
+            key[i] = kb;
+            key[ixj] = ka;
+            val[i] = vb;
+            val[ixj] = va;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Ascending sort of plain 32-bit values.
+__device__ inline void bitonic_sort_u32(uint32_t* v, int n2) {
+  for (int k = 2; k <= n2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t a = v[i], b = v[ixj];
+          const bool up = (i & k) == 0;
+          if (up ? a > b : a < b) {
+            v[i] = b;
+            v[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__device__ __forceinline__ int pow2_ceil(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+// Block-wide sum in a fixed order (deterministic).  `red` holds >= 32 doubles.
+__device__ inline double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double s = 0.0;
+  for (int w = 0; w < nw; ++w) s = __dadd_rn(s, red[w]);
+  __syncthreads();
+  return s;
+}
+
+__device__ inline int block_sum_i(int v, int* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum_i(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  int s = 0;
+  for (int w = 0; w < nw; ++w) s += red[w];
+  __syncthreads();
+  return s;
+}
+
+// Inclusive prefix sums out[i] = in[0] + ... + in[i] for i < n (n <= 4·blockDim),
+// each thread owning 4 consecutive items.  `red` holds >= 32 doubles.
+__device__ inline void block_inclusive_scan_d(const double* in, double* out, int n, double* red) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+  double v[4];
+  double run = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = 4 * t + j;
+    run = __dadd_rn(run, i < n ? in[i] : 0.0);
+    v[j] = run;
+  }
+  double incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double u = __shfl_up_sync(kFullMask, incl, o);
+    if (lane >= o) incl = __dadd_rn(incl, u);
+  }
+  __syncthreads();
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  double wbase = 0.0;
+  for (int w = 0; w < warp; ++w) wbase = __dadd_rn(wbase, red[w]);
+  (void)nw;
+  double excl = __shfl_up_sync(kFullMask, incl, 1);
+  if (lane == 0) excl = 0.0;
+  const double base = __dadd_rn(wbase, excl);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = 4 * t + j;
+    if (i < n) out[i] = __dadd_rn(base, v[j]);
+  }
+  __syncthreads();
+}
+
+// Exclusive prefix count of flags (n <= 4·blockDim); returns the total.
+__device__ inline int block_exclusive_count(const unsigned char* flag, int* pos, int n, int* red) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+  int c[4];
+  int run = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = 4 * t + j;
+    c[j] = run;
+    run += (i < n && flag[i]) ? 1 : 0;
+  }
+  int incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(kFullMask, incl, o);
+    if (lane >= o) incl += u;
+  }
+  __syncthreads();
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  int wbase = 0, total = 0;
+  for (int w = 0; w < nw; ++w) {
+    if (w < warp) wbase += red[w];
+    total += red[w];
+  }
+  const int base = wbase + incl - run;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = 4 * t + j;
+    if (i < n) pos[i] = base + c[j];
+  }
+  __syncthreads();
+  return total;
+}
+
+// Finds the k-th largest of the (distinct) values buf[0, n) as (prefix, mask): exactly k
+// values satisfy (v & mask) >= prefix.  MSB-first radix select, 8-bit digits.  Requires
+// 0 < k < n.  Every thread of the block must call it.
+__device__ inline void select_threshold(const unsigned long long* buf, int n, int k, unsigned int* hist,
+                                 int* s_digit, int* s_above, int* s_binc, unsigned long long& prefix,
+                                 unsigned long long& mask) {
+  prefix = 0;
+  mask = 0;
+  int need = k;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long v = buf[i];
+      if ((v & mask) == prefix) atomicAdd(&hist[(v >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      unsigned c[8];
+      unsigned tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - 8 * lane - j];
+        tot += c[j];
+      }
+      unsigned incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned t = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const unsigned excl = incl - tot;
+      if (excl < static_cast<unsigned>(need) && static_cast<unsigned>(need) <= incl) {
+        unsigned acc = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (acc + c[j] >= static_cast<unsigned>(need)) {
+            *s_digit = 255 - 8 * lane - j;
+            *s_above = static_cast<int>(acc);
+            *s_binc = static_cast<int>(c[j]);
+            break;
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    const int d = *s_digit, above = *s_above, binc = *s_binc;
+    need -= above;
+    prefix |= static_cast<unsigned long long>(d) << shift;
+    mask |= 0xffull << shift;
+    __syncthreads();
+    if (binc == need) break;
+  }
+}
+
+}  // namespace gs

@@ -1,0 +1,361 @@
+// Kernel 2: per-row merge, exact scoring and the draw (one CTA per row).
+//
+// Merges the candidate sets of a row's streaming units with the row's penalised ids
+// (scored here in IEEE double exactly as src/runtime/sampling.ts:26-30 does), orders
+// them by (logit/T desc, id asc) exactly as the reference's stable sort
+// (src/runtime/sampling.ts:33-35), normalises with the full-vocabulary sum
+// (src/runtime/sampling.ts:36-42: the streamed part comes from kernel 1's per-unit
+// (max, sum) partials) and runs top-k, min-p, typical-p, top-p and the seeded draw
+// (src/runtime/sampling.ts:44-64).  Temperature 0 is the argmax of the penalised logits
+// with the lowest id on ties (src/runtime/sampling.ts:31,92-96 and
+// src/webgpu/decode-greedy.ts:181-184).
+#include "gs_device.cuh"
+#include "gs_block.cuh"
+#include "gs_filter.cuh"
+#include "gs_internal.cuh"
+#include "../../include/gsampler.h"
+
+namespace gs {
+
+struct FinShared {
+  unsigned flags;
+  int n_allowed;
+  int n_c;
+  int n_ent;
+  float raw_m;
+  double raw_s;
+  double uniform;
+  int s_int[4];
+  double red_d[32];
+  int red_i[32];
+  unsigned hist[256];
+  int sel_digit;
+  int sel_above;
+  int sel_binc;
+  int fill_base;
+};
+
+__device__ __forceinline__ bool mask_allows(const uint32_t* mrow, uint32_t id) {
+  return (__ldg(mrow + (id >> 5)) >> (id & 31)) & 1u;
+}
+
+// Penalised value of one history id (src/runtime/sampling.ts:28-29), in double.
+__device__ __forceinline__ double penalise(double x, double count, double rp, double pres, double freq) {
+  double v = x < 0 ? __dmul_rn(x, rp) : __ddiv_rn(x, rp);
+  return __dsub_rn(v, __dadd_rn(pres, __dmul_rn(count, freq)));
+}
+
+size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap) {
+  const size_t r1 = std::max<size_t>(static_cast<size_t>(hist_cap) * 4, static_cast<size_t>(pack_cap) * 8);
+  const size_t work = static_cast<size_t>(kMaxCand) * (4 + 8 + 8 + 8 + 4 + 4 + 1);
+  return static_cast<size_t>(ent_cap) * sizeof(Ent) + work + ((r1 + 15) & ~static_cast<size_t>(15)) + 64;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid_constant__ FinalizeArgs A) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  __shared__ FinShared F;
+  const int row = blockIdx.x, tid = threadIdx.x, bs = blockDim.x;
+  const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
+  const int mode = pp->mode;
+  if (mode == kModeLarge) return;
+  const bool greedy = mode == kModeGreedy;
+  const double T = pp->temperature;
+  const int S = A.splits;
+
+  // ---- shared memory carve-up ----
+  unsigned char* p = dsm;
+  Ent* ent = reinterpret_cast<Ent*>(p);
+  p += static_cast<size_t>(A.ent_cap) * sizeof(Ent);
+  FilterWork w;
+  w.cp = reinterpret_cast<double*>(p);
+  p += kMaxCand * 8;
+  w.cum = reinterpret_cast<double*>(p);
+  p += kMaxCand * 8;
+  w.skey = reinterpret_cast<unsigned long long*>(p);
+  p += kMaxCand * 8;
+  w.cid = reinterpret_cast<uint32_t*>(p);
+  p += kMaxCand * 4;
+  w.sval = reinterpret_cast<uint32_t*>(p);
+  p += kMaxCand * 4;
+  w.pos = reinterpret_cast<int*>(p);
+  p += kMaxCand * 4;
+  w.flg = p;
+  p += kMaxCand;
+  p = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~static_cast<uintptr_t>(15));
+  unsigned char* r1 = p;
+  w.red_d = F.red_d;
+  w.red_i = F.red_i;
+  w.s_int = F.s_int;
+  w.s_flags = &F.flags;
+
+  const int32_t state = A.mask_state ? A.mask_state[row] : -1;
+  const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
+  const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
+  const unsigned char* rowbase =
+      static_cast<const unsigned char*>(A.logits) + static_cast<int64_t>(row) * A.row_stride * (DT == GS_DTYPE_F32 ? 4 : 2);
+
+  // ---- 0. unit partials ----
+  if (tid == 0) {
+    unsigned fl = 0;
+    int na = 0, nc = 0;
+    float rm = -INFINITY;
+    for (int u = 0; u < S; ++u) {
+      const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+      fl |= st.flags;
+      na += st.n_allowed;
+      nc += st.n_cand;
+      rm = fmaxf(rm, st.raw_m);
+    }
+    double rs = 0.0;
+    if (A.want_raw)
+      for (int u = 0; u < S; ++u) {
+        const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+        if (st.raw_m > -INFINITY) rs = __dadd_rn(rs, __dmul_rn(st.raw_s, exp(static_cast<double>(st.raw_m) - static_cast<double>(rm))));
+      }
+    if (has_mask && na == 0) fl |= GS_FLAG_ERR_DEADEND;
+    if (greedy) fl |= GS_FLAG_GREEDY;
+    F.flags = fl;
+    F.n_allowed = na;
+    F.n_c = nc;
+    F.n_ent = 0;
+    F.raw_m = rm;
+    F.raw_s = rs;
+  }
+  __syncthreads();
+
+  // ---- 1. penalty history: distinct ids with counts, scored exactly ----
+  if (!(F.flags & GS_FLAG_ERRORS)) {
+    int64_t hl = A.history_len ? A.history_len[row] : 0;
+    if (hl > A.history_stride) hl = A.history_stride;
+    if (hl < 0) hl = 0;
+    if (hl > 0) {
+      uint32_t* hs = reinterpret_cast<uint32_t*>(r1);
+      const int h2 = pow2_ceil(static_cast<int>(hl));
+      const int32_t* h = A.history + static_cast<int64_t>(row) * A.history_stride;
+      for (int i = tid; i < h2; i += bs) hs[i] = i < hl ? static_cast<uint32_t>(h[i]) : 0xffffffffu;
+      __syncthreads();
+      bitonic_sort_u32(hs, h2);
+      const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
+      for (int i = tid; i < hl; i += bs) {
+        const uint32_t v = hs[i];
+        if (v >= static_cast<uint64_t>(A.vocab)) continue;  // negative ids are >= 2^31 here
+        if (i > 0 && hs[i - 1] == v) continue;
+        int cnt = 1;
+        while (i + cnt < hl && hs[i + cnt] == v) ++cnt;
+        if (has_mask && !mask_allows(mrow, v)) continue;  // masked: -inf either way
+        float x = load_logit(rowbase, DT, v);
+        if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
+        if (!(x < INFINITY)) atomicOr(&F.flags, GS_FLAG_ERR_NONFINITE);  // NaN or +inf
+        const double xp = penalise(static_cast<double>(x), static_cast<double>(cnt), rp, pres, freq);
+        const int slot = atomicAdd(&F.n_ent, 1);
+        ent[slot] = Ent{greedy ? xp : __ddiv_rn(xp, T), v, 1u};
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- 2. streamed candidates of the units (top k over all units) ----
+  const int k = greedy ? 1 : pp->k_eff;
+  if (!(F.flags & GS_FLAG_ERRORS)) {
+    const int nc = F.n_c;
+    auto add_pack = [&](unsigned long long v) {
+      const float x = pack_value(v);
+      const uint32_t id = pack_id(v);
+      const int slot = atomicAdd(&F.n_ent, 1);
+      ent[slot] = Ent{greedy ? static_cast<double>(x) : __ddiv_rn(static_cast<double>(x), T), id, 0u};
+    };
+    if (nc > k) {
+      unsigned long long* buf = reinterpret_cast<unsigned long long*>(r1);
+      const int np = S * A.kcap;
+      for (int i = tid; i < np; i += bs) {
+        const int u = i / A.kcap, j = i - u * A.kcap;
+        const int64_t unit = static_cast<int64_t>(row) * S + u;
+        buf[i] = j < A.stats[unit].n_cand ? A.cands[unit * A.kcap + j] : 0ull;
+      }
+      __syncthreads();
+      unsigned long long prefix, mask;
+      select_threshold(buf, np, k, F.hist, &F.sel_digit, &F.sel_above, &F.sel_binc, prefix, mask);
+      for (int i = tid; i < np; i += bs) {
+        const unsigned long long v = buf[i];
+        if (v != 0ull && (v & mask) >= prefix) add_pack(v);
+      }
+    } else {
+      for (int i = tid; i < S * A.kcap; i += bs) {
+        const int u = i / A.kcap, j = i - u * A.kcap;
+        const int64_t unit = static_cast<int64_t>(row) * S + u;
+        if (j < A.stats[unit].n_cand) add_pack(A.cands[unit * A.kcap + j]);
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- 3. exact order ----
+  const int n_ent = F.n_ent;
+  if (!(F.flags & GS_FLAG_ERRORS)) {
+    const int n2 = pow2_ceil(n_ent > 0 ? n_ent : 1);
+    for (int i = n_ent + tid; i < n2; i += bs) ent[i] = Ent{-INFINITY, 0xffffffffu, 0xffffffffu};
+    __syncthreads();
+    bitonic_sort_ent(ent, n2);
+  }
+
+  uint32_t tok = 0xffffffffu;
+  int n_final = 0;
+  if (!(F.flags & GS_FLAG_ERRORS)) {
+    if (greedy) {
+      // argmax over the whole vocabulary: all -inf -> id 0 (sampling.ts:92-96)
+      if (n_ent == 0 || ent[0].key == -INFINITY) {
+        tok = 0;
+      } else {
+        tok = ent[0].id;
+      }
+      if (tid == 0) {
+        w.cid[0] = tok;
+        w.cp[0] = 1.0;
+      }
+      n_final = 1;
+    } else {
+      const int K = pp->top_k;
+      int nC = n_ent < K ? n_ent : K;
+      // Fewer allowed ids than topK: the remaining slots are -inf ids (masked ones and
+      // -inf logits) in ascending id order, exactly as the stable sort leaves them.
+      if (has_mask && n_ent < K && F.n_allowed < A.vocab) {
+        // masked ids in ascending order, up to K of them
+        int* mids = w.pos;
+        const int nwords = static_cast<int>((A.vocab + 31) >> 5);
+        if (tid == 0) F.fill_base = 0;
+        __syncthreads();
+        for (int w0 = 0; w0 < nwords && F.fill_base < K; w0 += bs) {
+          const int wi = w0 + tid;
+          uint32_t zero = 0;
+          if (wi < nwords) {
+            zero = ~__ldg(mrow + wi);
+            if (wi == nwords - 1 && (A.vocab & 31)) zero &= (1u << (A.vocab & 31)) - 1u;
+          }
+          const int c = __popc(zero);
+          // exclusive scan of c over the block
+          int incl = c;
+          for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(kFullMask, incl, o);
+            if ((tid & 31) >= o) incl += u;
+          }
+          if ((tid & 31) == 31) F.red_i[tid >> 5] = incl;
+          __syncthreads();
+          int base = F.fill_base;
+          for (int ww = 0; ww < (tid >> 5); ++ww) base += F.red_i[ww];
+          base += incl - c;
+          for (uint32_t z = zero; z; z &= z - 1) {
+            if (base < K) mids[base] = wi * 32 + __ffs(z) - 1;
+            ++base;
+          }
+          __syncthreads();
+          if (tid == bs - 1) F.fill_base = base;
+          __syncthreads();
+        }
+        const int n_masked = F.fill_base < K ? F.fill_base : K;
+        // merge the -inf tail of ent with the masked ids by id
+        if (tid == 0) {
+          int j0 = 0;
+          while (j0 < n_ent && ent[j0].key > -INFINITY) ++j0;
+          int a = j0, b = 0, o = j0;
+          // ent[j0, n_ent) are -inf entries sorted by id; merge into w.cum..w.skey
+          // (2·kMaxCand·8 bytes = kMaxCand entries, unused at this point)
+          Ent* tail = reinterpret_cast<Ent*>(w.cum);
+          int t = 0;
+          while (o < K && (a < n_ent || b < n_masked)) {
+            if (b >= n_masked || (a < n_ent && ent[a].id < static_cast<uint32_t>(mids[b]))) {
+              tail[t++] = ent[a++];
+            } else {
+              tail[t++] = Ent{-INFINITY, static_cast<uint32_t>(mids[b++]), 2u};
+            }
+            ++o;
+          }
+          for (int i = 0; i < t; ++i) ent[j0 + i] = tail[i];
+          F.s_int[0] = j0 + t;
+        }
+        __syncthreads();
+        nC = F.s_int[0];
+      }
+      const double M = ent[0].key;
+      if (M == -INFINITY) {
+        if (tid == 0) F.flags |= GS_FLAG_ERR_NONFINITE;  // every logit -inf: outside the domain
+      } else {
+        // full-vocabulary normaliser: streamed units + every penalised id
+        double part = 0.0;
+        for (int u = tid; u < S; u += bs) {
+          const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+          if (st.m > -INFINITY)
+            part = __dadd_rn(part, __dmul_rn(st.s, exp(__dsub_rn(__ddiv_rn(static_cast<double>(st.m), T), M))));
+        }
+        for (int i = tid; i < n_ent; i += bs)
+          if (ent[i].kind == 1u) part = __dadd_rn(part, exp(__dsub_rn(ent[i].key, M)));
+        const double total = block_sum_d(part, F.red_d);
+        for (int i = tid; i < nC; i += bs) {
+          w.cid[i] = ent[i].id;
+          w.cp[i] = __ddiv_rn(exp(__dsub_rn(ent[i].key, M)), total);
+        }
+        if (tid == 0) {
+          double r;
+          if (A.uniforms) {
+            r = A.uniforms[row];
+          } else {
+            double st = A.rng_state[row];
+            r = seeded_next(&st);
+            A.rng_state[row] = st;
+          }
+          F.uniform = r;
+        }
+        __syncthreads();
+        tok = filter_and_draw(w, nC, pp->min_p, pp->typical_p, pp->top_p, F.uniform, &n_final);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- outputs ----
+  const unsigned fl = F.flags;
+  const bool err = (fl & GS_FLAG_ERRORS) != 0;
+  if (tid == 0) {
+    A.ids[row] = err ? -1 : static_cast<int32_t>(tok);
+    if (A.flags) A.flags[row] = fl;
+    if (A.cand_count) A.cand_count[row] = err ? 0 : n_final;
+    if (A.logprob) {
+      double lp = NAN;
+      if (!err) {
+        float x = load_logit(rowbase, DT, tok);
+        if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
+        lp = __dsub_rn(__dsub_rn(static_cast<double>(x), static_cast<double>(F.raw_m)), log(F.raw_s));
+      }
+      A.logprob[row] = lp;
+    }
+  }
+  if (A.cand_ids && !err) {
+    const int nw = n_final < A.cand_cap ? n_final : A.cand_cap;
+    for (int i = tid; i < nw; i += bs) {
+      A.cand_ids[static_cast<int64_t>(row) * A.cand_cap + i] = static_cast<int32_t>(w.cid[i]);
+      if (A.cand_probs) A.cand_probs[static_cast<int64_t>(row) * A.cand_cap + i] = w.cp[i];
+    }
+  }
+}
+
+cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  if (dtype == GS_DTYPE_F32) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      attr = true;
+    }
+    finalize_kernel<GS_DTYPE_F32><<<rows, kFinalizeThreads, smem, st>>>(a);
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      attr = true;
+    }
+    finalize_kernel<GS_DTYPE_BF16><<<rows, kFinalizeThreads, smem, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace gs

@@ -1,0 +1,123 @@
+// Internal types shared by the kernels and the host side of libgsampler.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace gs {
+
+enum RowMode : int32_t { kModeSmallK = 0, kModeGreedy = 1, kModeLarge = 2 };
+
+// Per-row plan, derived on the host from gs_params (one DecodingConfig per row).
+struct RowPlan {
+  double temperature;
+  double top_p;
+  double min_p;
+  double typical_p;
+  double repetition_penalty;
+  double presence_penalty;
+  double frequency_penalty;
+  double a2;        // log2(e) / temperature (double); 2^(x·a2) = e^(x/T)
+  float a2_hi;      // a2 rounded toward zero to float
+  float a2_lo;      // a2 - a2_hi (>= FLT_MIN, so (-inf)·a2_lo stays -inf)
+  int32_t top_k;
+  int32_t k_eff;    // candidates each streaming unit keeps: 1 greedy, topK small-K, 0 large
+  int32_t mode;     // RowMode
+  int32_t pad;
+};
+
+// Partial statistics of one streaming unit (row, vocabulary chunk).
+struct UnitStat {
+  float m;          // max over live ids (allowed and not in the penalty history), -inf if none
+  float raw_m;      // max over every id of the chunk (log-probability)
+  double s;         // sum 2^((x - m)·a2) over live ids
+  double raw_s;     // sum e^(x - raw_m) over every id
+  int32_t n_allowed;
+  int32_t n_cand;
+  uint32_t flags;
+  int32_t pad;
+};
+
+struct StreamArgs {
+  const void* logits;
+  int64_t vocab;
+  int64_t row_stride;
+  int64_t vocab_offset;   // global id of local id 0 (vocabulary-sharded mode)
+  float softcap;
+  float inv_softcap;
+  int32_t want_raw;
+  int32_t splits;
+  int64_t chunk;
+  int32_t kcap;           // candidate slots per unit in `cands`
+  int32_t kc;             // shared-memory candidate buffer entries (power of two)
+  const RowPlan* plans;   // per-row plans or nullptr (then plan0)
+  RowPlan plan0;
+  const int32_t* history;
+  const int32_t* history_len;
+  int64_t history_stride;
+  const uint32_t* mask_table;
+  int64_t mask_states;
+  int64_t mask_words;
+  const int32_t* mask_state;
+  UnitStat* stats;
+  unsigned long long* cands;
+};
+
+struct FinalizeArgs {
+  const void* logits;
+  int64_t vocab;          // ids are [0, vocab) of this call
+  int64_t row_stride;
+  float softcap;
+  float inv_softcap;
+  int32_t want_raw;
+  int32_t splits;
+  int32_t kcap;
+  int32_t hist_cap;       // power-of-two shared buffer for the sorted history
+  int32_t ent_cap;        // power-of-two shared buffer for candidate entries
+  int32_t pack_cap;       // shared buffer for unit packs (0 when units already hold <= k)
+  const RowPlan* plans;
+  RowPlan plan0;
+  const int32_t* history;
+  const int32_t* history_len;
+  int64_t history_stride;
+  const uint32_t* mask_table;
+  int64_t mask_states;
+  int64_t mask_words;
+  const int32_t* mask_state;
+  const UnitStat* stats;
+  const unsigned long long* cands;
+  double* rng_state;
+  const double* uniforms;
+  int32_t* ids;
+  double* logprob;
+  uint32_t* flags;
+  int32_t* cand_ids;
+  double* cand_probs;
+  int32_t* cand_count;
+  int32_t cand_cap;
+};
+
+// Launch helpers implemented in gs_kernels.cu.
+cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
+size_t stream_smem_bytes(int64_t chunk, int kc);
+cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
+size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap);
+cudaError_t launch_large(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
+size_t large_smem_bytes(int64_t vocab, int hist_cap);
+cudaError_t launch_logprob(const void* logits, int dtype, int rows, int64_t vocab, int64_t stride,
+                           float softcap, float inv_softcap, const int32_t* tokens, double* out,
+                           int32_t* bad, cudaStream_t st);
+cudaError_t launch_mask_logits(const float* raw, int64_t vocab, const int32_t* legal, int64_t nl,
+                               const int32_t* term, int64_t nt, float* out, cudaStream_t st);
+cudaError_t launch_build_mask_row(int64_t vocab, const int32_t* legal, int64_t nl, const int32_t* term,
+                                  int64_t nt, uint32_t* row, cudaStream_t st);
+cudaError_t launch_softcap(const float* in, float* out, int64_t n, float cap, float inv_cap, cudaStream_t st);
+cudaError_t launch_softcap_digest(uint64_t lo, uint64_t hi, float cap, float inv_cap,
+                                  unsigned long long* acc, cudaStream_t st);
+
+constexpr int kStreamThreads = 512;
+constexpr int kFinalizeThreads = 256;
+constexpr int kLargeThreads = 1024;
+constexpr int kLargeBins = 4096;
+constexpr int kLargeGatherCap = 4096;
+
+}  // namespace gs

@@ -1,0 +1,202 @@
+/*
+ * gsampler — B200 (sm_100a) decode-sampling path, C ABI.
+ *
+ * Drop-in for the full-logit sampling path of aribornstein/gemma-webgpu-engine's
+ * session.generate(): the reference runs it on the JS main thread over a 1 MiB
+ * Float32Array read back per token; here the logits stay in device memory and only the
+ * sampled ids (and optional log-probabilities) come back.
+ *
+ * Each entry point names the reference interface it replaces (file:line in the
+ * reference repository).  All pointers are plain device pointers unless a comment says
+ * "host"; sizes are element counts.  No entry point aborts: failures return a status
+ * and gs_last_error() gives the text.
+ */
+#ifndef GSAMPLER_H_
+#define GSAMPLER_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum gs_status {
+  GS_OK = 0,
+  GS_EINVAL = 1,        /* bad argument (reference: throw new Error(...)) */
+  GS_EDEADEND = 2,      /* a constrained row admits no token
+                           ("Generation constraint reached a tokenization dead end",
+                           src/runtime/gemma-session.ts:1324-1326) */
+  GS_ECUDA = 3,         /* a CUDA runtime call failed */
+  GS_ENCCL = 4,         /* reserved for the vocabulary-sharded exchange */
+  GS_ETIMEOUT = 5,      /* a bounded device wait ran out */
+  GS_ENOMEM = 6,        /* device allocation failed */
+  GS_EUNSUPPORTED = 7,  /* request outside the implemented envelope (see gs_last_error) */
+  GS_EEMPTY = 8,        /* "Cannot sample empty logits" (src/runtime/sampling.ts:19) */
+  GS_ENONFINITE = 9     /* a logit was NaN or +inf (outside the reference's domain) */
+} gs_status;
+
+enum { GS_DTYPE_F32 = 0, GS_DTYPE_BF16 = 1 };
+
+/* Per-row flags written to gs_outputs.flags. */
+enum {
+  GS_FLAG_BOUNDARY_TOP_P = 1u << 0,   /* top-p cumulative within 1e-6 (relative) of topP */
+  GS_FLAG_BOUNDARY_DRAW = 1u << 1,    /* draw cursor within 1e-6 of a CDF step */
+  GS_FLAG_BOUNDARY_MIN_P = 1u << 2,   /* a probability within 1e-6 of the min-p threshold */
+  GS_FLAG_BOUNDARY_TYPICAL = 1u << 3, /* typical-p cut or surprise order within 1e-6 */
+  GS_FLAG_FELL_THROUGH = 1u << 4,     /* draw loop ended without cursor <= 0 (sampling.ts:64) */
+  GS_FLAG_GREEDY = 1u << 5,           /* temperature 0: argmax, no draw consumed */
+  GS_FLAG_LARGE_PATH = 1u << 6,       /* topK == 0 or topK > GS_MAX_TOP_K: histogram path */
+  GS_FLAG_ERR_DEADEND = 1u << 8,
+  GS_FLAG_ERR_NONFINITE = 1u << 9,
+  GS_FLAG_ERR_INVALID = 1u << 10,     /* bad mask state / history id bookkeeping */
+  GS_FLAG_ERR_UNSUPPORTED = 1u << 11, /* see GS_EUNSUPPORTED */
+  GS_FLAG_ERR_TIMEOUT = 1u << 12,
+  GS_FLAG_ERRORS = 0xff00u
+};
+
+#define GS_MAX_TOP_K 1024     /* topK above this (or 0) runs the histogram path */
+#define GS_MAX_HISTORY 4096   /* ids per row after the repetition window is applied */
+
+/*
+ * DecodingConfig fields that sampleToken reads (src/runtime/decoding.ts:1-14).  The
+ * window (repetitionWindow) is applied by the caller when it fills gs_batch.history,
+ * exactly as `history.slice(-config.repetitionWindow)` (src/runtime/sampling.ts:22-24).
+ * Validation (src/runtime/decoding.ts:31-59) is re-checked: GS_EINVAL on violation.
+ */
+typedef struct gs_params {
+  double temperature;
+  double top_p;
+  double min_p;
+  double typical_p;
+  double repetition_penalty;
+  double presence_penalty;
+  double frequency_penalty;
+  int32_t top_k;
+  int32_t reserved;
+} gs_params;
+
+typedef struct gs_batch {
+  const void* logits;         /* [rows, row_stride] raw model logits (f32 or bf16) */
+  int32_t dtype;              /* GS_DTYPE_F32 / GS_DTYPE_BF16 */
+  int32_t rows;
+  int64_t vocab;              /* V (262144 for Gemma) */
+  int64_t row_stride;         /* elements between rows, >= vocab */
+  float softcap;              /* c·tanh(x/c) applied to the logits first; 0 = off */
+  int32_t params_count;       /* 1 = params[0] for every row, else == rows */
+  const gs_params* params;    /* HOST pointer */
+  const int32_t* history;     /* [rows, history_stride] windowed token history, or NULL */
+  const int32_t* history_len; /* [rows] entries used per row, or NULL (no history) */
+  int64_t history_stride;     /* <= GS_MAX_HISTORY */
+  const uint32_t* mask_table; /* [mask_states, mask_words] allowed-token bitmasks, or NULL */
+  int64_t mask_states;
+  int64_t mask_words;         /* words per state row, >= ceil(vocab / 32) */
+  const int32_t* mask_state;  /* [rows] row -> state; < 0 = unconstrained; or NULL */
+  double* rng_state;          /* [rows] SeededRandom states (the JS number), in/out */
+  const double* uniforms;     /* [rows] pre-drawn random() values; overrides rng_state */
+} gs_batch;
+
+typedef struct gs_outputs {
+  int32_t* ids;               /* [rows] sampled token ids (-1 on a row error) */
+  double* logprob;            /* [rows] tokenLogProbability(raw logits, id), or NULL */
+  uint32_t* flags;            /* [rows] GS_FLAG_* bits, or NULL */
+  int32_t* cand_ids;          /* [rows, cand_cap] final candidates in draw order, or NULL */
+  double* cand_probs;         /* [rows, cand_cap] their probabilities, or NULL */
+  int32_t* cand_count;        /* [rows] number of final candidates, or NULL */
+  int32_t cand_cap;
+} gs_outputs;
+
+typedef struct gs_ctx gs_ctx;
+
+/* Creates a context bound to `device`; workspace grows on demand and is never freed
+ * per call (the reference allocates no GPU memory per token, README.md:241-242). */
+gs_status gs_create(int device, gs_ctx** out);
+gs_status gs_destroy(gs_ctx* ctx);
+/* Pre-sizes the workspace so that later gs_sample calls with at most these sizes
+ * allocate nothing (and can be captured in a CUDA graph). */
+gs_status gs_reserve(gs_ctx* ctx, int32_t rows, int64_t vocab, int32_t max_top_k, int64_t history_stride);
+const char* gs_last_error(const gs_ctx* ctx);
+
+/*
+ * Samples one token per row: replaces sampleToken(rawLogits, history, config, random)
+ * (src/runtime/sampling.ts:18-65) as called by GemmaGenerationSession.generate
+ * (src/runtime/gemma-session.ts:686, 705, 1328), including the constraint mask of
+ * selectConstrainedToken/maskConstraintLogits (src/runtime/gemma-session.ts:1305-1329,
+ * src/runtime/constraints.ts:159-173) as a per-state bitmask, and the greedy GPU
+ * argmax route (src/webgpu/decode-greedy.ts:171-249) for temperature 0.  With
+ * out->logprob it also returns tokenLogProbability (src/runtime/sampling.ts:67-80).
+ * Asynchronous on `stream` (a cudaStream_t; NULL = default stream).  Row errors are
+ * reported through out->flags; the call itself fails only on argument or CUDA errors.
+ */
+gs_status gs_sample(gs_ctx* ctx, const gs_batch* batch, const gs_outputs* out, void* stream);
+
+/*
+ * Same as gs_sample with the pointers of `batch` and `out` in HOST memory, except
+ * batch->mask_table, which stays a device pointer (a compiled constraint's table is
+ * uploaded once and kept resident).  Copies the inputs to the device, samples, copies
+ * the outputs (and the advanced rng_state) back and synchronizes.  Returns the first
+ * row error as a status (GS_EDEADEND, GS_ENONFINITE, ...), i.e. the error the reference
+ * would throw.  This is the call a synchronous sampleToken replacement makes.
+ */
+gs_status gs_sample_host(gs_ctx* ctx, const gs_batch* batch, const gs_outputs* out, void* stream);
+
+/* tokenLogProbability (src/runtime/sampling.ts:67-80) for one token per row over the
+ * (soft-capped) raw device logits.  `tokens` and `out` are HOST pointers; the call is
+ * synchronous.  GS_EINVAL ("Token t is outside logits length n") when a token is
+ * outside [0, vocab). */
+gs_status gs_token_log_probability(gs_ctx* ctx, const void* logits, int32_t dtype, int32_t rows,
+                                   int64_t vocab, int64_t row_stride, float softcap,
+                                   const int32_t* tokens, double* out, void* stream);
+
+/* maskConstraintLogits (src/runtime/constraints.ts:159-173): out = -inf except at legal
+ * and termination ids in [0, vocab). */
+gs_status gs_mask_constraint_logits(gs_ctx* ctx, const float* raw_logits, int64_t vocab,
+                                    const int32_t* legal, int64_t n_legal,
+                                    const int32_t* termination, int64_t n_termination,
+                                    float* out, void* stream);
+
+/* Builds one allowed-token bitmask row (ceil(vocab/32) words) from the legal and
+ * termination id lists that selectConstrainedToken passes to maskConstraintLogits
+ * (src/runtime/gemma-session.ts:1315-1327). */
+gs_status gs_build_mask_row(gs_ctx* ctx, int64_t vocab, const int32_t* legal, int64_t n_legal,
+                            const int32_t* termination, int64_t n_termination, uint32_t* row_out,
+                            void* stream);
+
+/* Elementwise soft cap, the same routine the sampling pass applies (no reference
+ * counterpart: the reference never applies its declared cap). */
+gs_status gs_softcap(gs_ctx* ctx, const float* in, float* out, int64_t n, float cap, void* stream);
+
+/* Self-check: order-independent 64-bit digest of gs_softcap over the float bit patterns
+ * [lo, hi), for exhaustive comparison with an independent host implementation. */
+gs_status gs_softcap_digest(gs_ctx* ctx, uint64_t lo, uint64_t hi, float cap, uint64_t* digest_host);
+
+/*
+ * Kernel timing (the counterpart of measureGpuDispatches, src/webgpu/gpu-timestamp.ts:1-56,
+ * which brackets dispatches with timestamp queries).  While enabled, every gs_sample
+ * records CUDA events on its stream around the streaming pass and around the merge;
+ * gs_profile_read waits for them, returns the summed milliseconds and launch counts
+ * since the last read and clears the record.
+ */
+gs_status gs_profile_enable(gs_ctx* ctx, int32_t enable);
+gs_status gs_profile_read(gs_ctx* ctx, double* stream_ms, int64_t* stream_launches, double* merge_ms,
+                          int64_t* merge_launches);
+
+/*
+ * Vocabulary-sharded mode (one process per GPU, each holding ids
+ * [vocab_offset, vocab_offset + shard_vocab) of every row).  gs_shard_partials runs the
+ * streaming pass on the local shard and writes a fixed-size record per row
+ * (gs_shard_record_bytes); the caller all-gathers the records (one NCCL all-gather);
+ * gs_shard_merge merges the gathered records of all shards and samples, identically on
+ * every rank.  Requires 1 <= topK <= GS_MAX_TOP_K (or temperature 0) and no history
+ * ids outside the shard's own bookkeeping (history is applied per shard).
+ */
+int64_t gs_shard_record_bytes(int32_t max_top_k);
+gs_status gs_shard_partials(gs_ctx* ctx, const gs_batch* shard, int64_t vocab_offset,
+                            int64_t vocab_total, void* records, void* stream);
+gs_status gs_shard_merge(gs_ctx* ctx, const gs_batch* shard, int64_t vocab_total, int32_t shards,
+                         const void* gathered_records, const gs_outputs* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GSAMPLER_H_ */

@@ -1,0 +1,456 @@
+// ORACLE — test infrastructure only. Not part of the product.
+//
+// A plain C++17 restatement, in IEEE double arithmetic, of the reference's CPU
+// decode sampler so that the CUDA path can be checked against it on identical
+// inputs.  Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+// --impl reference legs may load this file's shared object.
+//
+// Reference (aribornstein/gemma-webgpu-engine, TypeScript):
+//   src/runtime/sampling.ts:3-16     SeededRandom (Mulberry32 over a JS number state)
+//   src/runtime/sampling.ts:18-65    sampleToken
+//   src/runtime/sampling.ts:67-80    tokenLogProbability
+//   src/runtime/sampling.ts:82-90    cumulativeCut
+//   src/runtime/sampling.ts:92-96    argmax
+//   src/runtime/constraints.ts:159-173 maskConstraintLogits
+//
+// Parity pins: tests/test_oracle_golden.py checks this file against every
+// known-answer test of tests/sampling.spec.ts and tests/constraints.spec.ts:158-161
+// (restated as fixtures in tests/golden/reference_spec_cases.json).  The reference
+// itself cannot run in this container (no Node); see the header of that fixture.
+//
+// JS semantics that matter and how they are restated here:
+//  * Array.prototype.sort is stable (ES2019); a comparator that returns NaN is read as
+//    +0 ("equal").  `right.logit - left.logit` is therefore the strict weak order
+//    "a before b iff a.logit > b.logit" for every non-NaN input (-inf/-inf and +inf/+inf
+//    give NaN = equal).  std::stable_sort with that predicate gives the same order.
+//  * Math.imul / >>> / ^ / | wrap to 32 bits; the SeededRandom state itself is a JS
+//    number that grows by 0x6d2b79f5 per draw without wrapping (sampling.ts:11), so it
+//    is kept here as a double and converted with ToUint32 at each use.
+//  * Float32Array -> Array.from widens exactly (sampling.ts:20).
+//  * NaN logits make the reference's comparator inconsistent (implementation-defined
+//    order); they are outside the domain of this oracle and of the CUDA path.
+//
+// Build: oracle/Makefile (g++ -O2 -ffp-contract=off, so no FMA contraction changes a
+// rounding).
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <vector>
+#include <thread>
+
+namespace {
+
+// ---------------------------------------------------------------- SeededRandom
+// JS ToUint32 of an integral double (state never holds a fraction).
+inline uint32_t to_uint32(double v) {
+  double m = std::fmod(v, 4294967296.0);
+  if (m < 0) m += 4294967296.0;
+  return static_cast<uint32_t>(m);
+}
+
+// sampling.ts:7  `seed >>> 0 || 0x6d2b79f5`
+inline double seeded_init(double seed) {
+  uint32_t s = to_uint32(std::trunc(seed));
+  return s == 0 ? static_cast<double>(0x6d2b79f5u) : static_cast<double>(s);
+}
+
+// sampling.ts:10-15
+inline double seeded_next(double* state) {
+  *state = *state + 1831565813.0;  // 0x6d2b79f5 added to a JS number: no wrap
+  uint32_t v = to_uint32(*state);
+  v = static_cast<uint32_t>(static_cast<uint64_t>(v ^ (v >> 15)) * static_cast<uint64_t>(v | 1u));
+  v ^= v + static_cast<uint32_t>(static_cast<uint64_t>(v ^ (v >> 7)) * static_cast<uint64_t>(v | 61u));
+  return static_cast<double>(v ^ (v >> 14)) / 4294967296.0;
+}
+
+struct Item {
+  int32_t token;
+  double logit;
+  double probability;
+  double surprise;
+};
+
+}  // namespace
+
+extern "C" {
+
+// Same field order and meaning as DecodingConfig (src/runtime/decoding.ts:1-14),
+// minus maxNewTokens / seed / stopTokenIds which sampleToken does not read.
+struct OracleConfig {
+  double temperature;
+  double top_p;
+  double min_p;
+  double typical_p;
+  double repetition_penalty;
+  double presence_penalty;
+  double frequency_penalty;
+  int32_t top_k;
+  int32_t repetition_window;
+};
+
+// Diagnostic margins of the decisions sampleToken took (all relative, >= 0; +inf when
+// the decision did not happen).  Used by tests to count boundary cases.
+struct OracleTrace {
+  double total;          // full-vocabulary normaliser (sampling.ts:37-41)
+  double max_key;        // scaled[0].logit
+  double candidate_total;
+  double uniform;        // the random() value consumed (NaN when none)
+  double margin_top_p;   // |cumulative - topP| / topP at the cut index and the one before
+  double margin_draw;    // distance of the cursor to the chosen CDF step, / candidateTotal
+  double margin_min_p;   // min |p - threshold| / threshold over candidates
+  double margin_typical; // |cumulative - typicalP| / typicalP at the typical cut
+  int32_t n_after_top_k;
+  int32_t n_after_min_p;
+  int32_t n_after_typical;
+  int32_t n_final;
+  int32_t fell_through;  // draw loop ended without cursor <= 0 (sampling.ts:64)
+  int32_t greedy;
+};
+
+double oracle_seeded_init(double seed) { return seeded_init(seed); }
+double oracle_seeded_next(double* state) { return seeded_next(state); }
+
+// sampling.ts:82-90, returning the kept length and the decision margin.
+static size_t cumulative_cut(const std::vector<Item>& items, double threshold, double* margin) {
+  double cumulative = 0;
+  size_t end = 0;
+  double prev = 0;
+  do {
+    prev = cumulative;
+    cumulative += items[end].probability;
+    end += 1;
+  } while (end < items.size() && cumulative < threshold);
+  if (margin) {
+    double m = std::fabs(cumulative - threshold);
+    if (end >= 2) m = std::min(m, std::fabs(prev - threshold));
+    *margin = threshold > 0 ? m / threshold : m;
+  }
+  return std::max<size_t>(1, end);
+}
+
+// sampleToken (sampling.ts:18-65).  `uniform` is the value random() returns; it is
+// read only when temperature != 0 (sampling.ts:31, 59).  Returns the token, or -1 for
+// empty logits (the reference throws "Cannot sample empty logits").
+// cand_ids/cand_probs (capacity cand_cap) receive the final candidate list in draw order.
+int32_t oracle_sample_token(const float* raw_logits, int64_t vocab,
+                            const int32_t* history, int64_t history_len,
+                            const OracleConfig* config, double uniform,
+                            int32_t* cand_ids, double* cand_probs, int32_t* cand_count,
+                            int64_t cand_cap, OracleTrace* trace) {
+  OracleTrace tr;
+  tr.total = tr.max_key = tr.candidate_total = NAN;
+  tr.uniform = NAN;
+  tr.margin_top_p = tr.margin_draw = tr.margin_min_p = tr.margin_typical = INFINITY;
+  tr.n_after_top_k = tr.n_after_min_p = tr.n_after_typical = tr.n_final = 0;
+  tr.fell_through = 0;
+  tr.greedy = 0;
+  if (cand_count) *cand_count = 0;
+  if (vocab <= 0) {
+    if (trace) *trace = tr;
+    return -1;
+  }
+  // sampling.ts:20
+  std::vector<double> logits(static_cast<size_t>(vocab));
+  for (int64_t i = 0; i < vocab; ++i) logits[i] = static_cast<double>(raw_logits[i]);
+  // sampling.ts:21-25 (Map keeps first-insertion order; the per-token updates are
+  // independent, so a sorted map gives the same values)
+  std::map<int32_t, int64_t> counts;
+  if (config->repetition_window != 0) {
+    int64_t start = history_len - config->repetition_window;
+    if (start < 0) start = 0;
+    for (int64_t i = start; i < history_len; ++i) counts[history[i]] += 1;
+  }
+  // sampling.ts:26-30
+  for (const auto& kv : counts) {
+    int32_t token = kv.first;
+    if (token < 0 || token >= vocab) continue;
+    double v = logits[token];
+    v = v < 0 ? v * config->repetition_penalty : v / config->repetition_penalty;
+    v -= config->presence_penalty + static_cast<double>(kv.second) * config->frequency_penalty;
+    logits[token] = v;
+  }
+  // sampling.ts:31, 92-96
+  if (config->temperature == 0) {
+    int64_t best = 0;
+    for (int64_t i = 1; i < vocab; ++i)
+      if (logits[i] > logits[best]) best = i;
+    tr.greedy = 1;
+    tr.n_final = 1;
+    if (cand_count && cand_cap > 0) {
+      cand_ids[0] = static_cast<int32_t>(best);
+      cand_probs[0] = 1.0;
+      *cand_count = 1;
+    }
+    if (trace) *trace = tr;
+    return static_cast<int32_t>(best);
+  }
+  // sampling.ts:33-35
+  std::vector<Item> scaled(static_cast<size_t>(vocab));
+  for (int64_t i = 0; i < vocab; ++i)
+    scaled[i] = Item{static_cast<int32_t>(i), logits[i] / config->temperature, 0.0, 0.0};
+  std::stable_sort(scaled.begin(), scaled.end(),
+                   [](const Item& a, const Item& b) { return a.logit > b.logit; });
+  // sampling.ts:36-42
+  const double maximum = scaled[0].logit;
+  double total = 0;
+  for (auto& item : scaled) {
+    item.probability = std::exp(item.logit - maximum);
+    total += item.probability;
+  }
+  for (auto& item : scaled) item.probability /= total;
+  tr.total = total;
+  tr.max_key = maximum;
+  // sampling.ts:44
+  std::vector<Item> candidates;
+  if (config->top_k > 0) {
+    size_t k = std::min<size_t>(static_cast<size_t>(config->top_k), scaled.size());
+    candidates.assign(scaled.begin(), scaled.begin() + k);
+  } else {
+    candidates = scaled;
+  }
+  tr.n_after_top_k = static_cast<int32_t>(candidates.size());
+  // sampling.ts:45-48
+  if (config->min_p > 0) {
+    const double threshold = candidates[0].probability * config->min_p;
+    std::vector<Item> kept;
+    double m = INFINITY;
+    for (const auto& item : candidates) {
+      if (threshold > 0) m = std::min(m, std::fabs(item.probability - threshold) / threshold);
+      if (item.probability >= threshold) kept.push_back(item);
+    }
+    tr.margin_min_p = m;
+    candidates.swap(kept);
+  }
+  tr.n_after_min_p = static_cast<int32_t>(candidates.size());
+  // sampling.ts:49-55
+  if (config->typical_p < 1) {
+    double entropy = 0;
+    for (const auto& item : candidates) entropy = entropy - item.probability * std::log(item.probability);
+    for (auto& item : candidates) item.surprise = std::fabs(-std::log(item.probability) - entropy);
+    std::stable_sort(candidates.begin(), candidates.end(),
+                     [](const Item& a, const Item& b) { return a.surprise < b.surprise; });
+    size_t keep = cumulative_cut(candidates, config->typical_p, &tr.margin_typical);
+    candidates.resize(keep);
+    std::stable_sort(candidates.begin(), candidates.end(),
+                     [](const Item& a, const Item& b) { return a.probability > b.probability; });
+  }
+  tr.n_after_typical = static_cast<int32_t>(candidates.size());
+  // sampling.ts:56
+  if (config->top_p < 1) {
+    size_t keep = cumulative_cut(candidates, config->top_p, &tr.margin_top_p);
+    candidates.resize(keep);
+  }
+  tr.n_final = static_cast<int32_t>(candidates.size());
+  // sampling.ts:58-64
+  double candidate_total = 0;
+  for (const auto& item : candidates) candidate_total += item.probability;
+  tr.candidate_total = candidate_total;
+  tr.uniform = uniform;
+  double cursor = uniform * candidate_total;
+  int32_t chosen = -1;
+  for (const auto& item : candidates) {
+    double before = cursor;
+    cursor -= item.probability;
+    if (cursor <= 0) {
+      chosen = item.token;
+      double m = std::min(std::fabs(before), std::fabs(cursor));
+      tr.margin_draw = candidate_total > 0 ? m / candidate_total : m;
+      break;
+    }
+  }
+  if (chosen < 0) {
+    chosen = candidates.back().token;
+    tr.fell_through = 1;
+    tr.margin_draw = candidate_total > 0 ? std::fabs(cursor) / candidate_total : std::fabs(cursor);
+  }
+  if (cand_count) {
+    int64_t n = std::min<int64_t>(cand_cap, static_cast<int64_t>(candidates.size()));
+    for (int64_t i = 0; i < n; ++i) {
+      cand_ids[i] = candidates[i].token;
+      cand_probs[i] = candidates[i].probability;
+    }
+    *cand_count = static_cast<int32_t>(candidates.size());
+  }
+  if (trace) *trace = tr;
+  return chosen;
+}
+
+// Same as oracle_sample_token, with random() = SeededRandom.next() over *rng_state
+// (a JS-number state, see seeded_next).  The state advances only when a draw happens.
+int32_t oracle_sample_token_seeded(const float* raw_logits, int64_t vocab,
+                                   const int32_t* history, int64_t history_len,
+                                   const OracleConfig* config, double* rng_state,
+                                   int32_t* cand_ids, double* cand_probs, int32_t* cand_count,
+                                   int64_t cand_cap, OracleTrace* trace) {
+  double u = NAN;
+  if (vocab > 0 && config->temperature != 0) u = seeded_next(rng_state);
+  return oracle_sample_token(raw_logits, vocab, history, history_len, config, u,
+                             cand_ids, cand_probs, cand_count, cand_cap, trace);
+}
+
+// tokenLogProbability (sampling.ts:67-80).  *error = 1 when the token is outside
+// [0, length) (the reference throws `Token ${token} is outside logits length ${n}`).
+double oracle_token_log_probability(const float* raw_logits, int64_t vocab, int64_t token,
+                                    int32_t* error) {
+  *error = 0;
+  if (token < 0 || token >= vocab) {
+    *error = 1;
+    return NAN;
+  }
+  double maximum = -INFINITY;
+  for (int64_t i = 0; i < vocab; ++i) maximum = std::max(maximum, static_cast<double>(raw_logits[i]));
+  double denominator = 0;
+  for (int64_t i = 0; i < vocab; ++i) denominator += std::exp(static_cast<double>(raw_logits[i]) - maximum);
+  return static_cast<double>(raw_logits[token]) - maximum - std::log(denominator);
+}
+
+// maskConstraintLogits (constraints.ts:159-173).
+void oracle_mask_constraint_logits(const float* raw_logits, int64_t vocab,
+                                   const int32_t* legal, int64_t n_legal,
+                                   const int32_t* termination, int64_t n_termination,
+                                   float* out) {
+  for (int64_t i = 0; i < vocab; ++i) out[i] = -INFINITY;
+  for (int64_t i = 0; i < n_legal; ++i)
+    if (legal[i] >= 0 && legal[i] < vocab) out[legal[i]] = raw_logits[legal[i]];
+  for (int64_t i = 0; i < n_termination; ++i)
+    if (termination[i] >= 0 && termination[i] < vocab) out[termination[i]] = raw_logits[termination[i]];
+}
+
+// ------------------------------------------------------------------ softcap
+// 30·tanh(x/30) style logit soft cap in float32, stated as an exact sequence of
+// IEEE single operations so that every compliant implementation gives the same bits.
+// The reference runtime never applies it (the Gemma manifest declares 30, the LM head
+// writes uncapped logits); the benchmark configurations apply it when making inputs.
+// Method: y = x * fl(1/c); |y| < 0.625 uses the odd polynomial y + y^3·Q(y^2) (a
+// least-squares/Lawson minimax fit, coefficients below); 0.625 <= |y| < 9 uses
+// 1 - 2/(e^{2|y|} + 1) with e^z by Cody–Waite reduction z = n·ln2 + r and a degree-6
+// polynomial for e^r; |y| >= 9 gives 1.  The result is c·copysign(t, y).
+static const float kTanhQ[5] = {-0.3333328f, 0.13331442f, -0.05373972f, 0.02063909f, -0.00570499f};
+static const float kExpB[5] = {0.49999994f, 0.1666652f, 0.04166841f, 0.00836891f, 0.00138142f};
+static const float kLn2Hi = 0.693145751953125f;     // 0x3f317200
+static const float kLn2Lo = 1.428606765330187e-06f; // ln2 - kLn2Hi
+static const float kLog2e = 1.44269502162933349609375f;
+
+static inline float f_exp_reduced(float z) {
+  float n = std::rint(z * kLog2e);
+  float r = std::fmaf(-n, kLn2Hi, z);
+  r = std::fmaf(-n, kLn2Lo, r);
+  float p = kExpB[4];
+  p = std::fmaf(p, r, kExpB[3]);
+  p = std::fmaf(p, r, kExpB[2]);
+  p = std::fmaf(p, r, kExpB[1]);
+  p = std::fmaf(p, r, kExpB[0]);
+  float r2 = r * r;
+  float e = std::fmaf(p, r2, r) + 1.0f;
+  int32_t ni = static_cast<int32_t>(n);
+  uint32_t bits = static_cast<uint32_t>(ni + 127) << 23;
+  float scale;
+  std::memcpy(&scale, &bits, 4);
+  return e * scale;
+}
+
+float oracle_softcap(float x, float cap, float inv_cap) {
+  if (x != x) return x;
+  float y = x * inv_cap;
+  float a = std::fabs(y);
+  float t;
+  if (a < 0.625f) {
+    float z = a * a;
+    float q = kTanhQ[4];
+    q = std::fmaf(q, z, kTanhQ[3]);
+    q = std::fmaf(q, z, kTanhQ[2]);
+    q = std::fmaf(q, z, kTanhQ[1]);
+    q = std::fmaf(q, z, kTanhQ[0]);
+    float a3 = a * z;
+    t = std::fmaf(a3, q, a);
+  } else if (a < 9.0f) {
+    float e = f_exp_reduced(a + a);
+    t = 1.0f - 2.0f / (e + 1.0f);
+  } else {
+    t = 1.0f;
+  }
+  return cap * std::copysign(t, y);
+}
+
+void oracle_softcap_array(const float* in, float* out, int64_t n, float cap, float inv_cap) {
+  for (int64_t i = 0; i < n; ++i) out[i] = oracle_softcap(in[i], cap, inv_cap);
+}
+
+// Order-independent 64-bit digest of softcap over the bit patterns [lo, hi) (used to
+// compare the CUDA routine with this one exhaustively without moving 16 GB).
+uint64_t oracle_softcap_digest(uint64_t lo, uint64_t hi, float cap, float inv_cap, int threads) {
+  if (threads < 1) threads = 1;
+  std::vector<uint64_t> part(static_cast<size_t>(threads), 0);
+  std::vector<std::thread> pool;
+  uint64_t span = (hi - lo + threads - 1) / threads;
+  for (int t = 0; t < threads; ++t) {
+    pool.emplace_back([&, t] {
+      uint64_t a = lo + span * t, b = std::min(hi, a + span), acc = 0;
+      for (uint64_t u = a; u < b; ++u) {
+        uint32_t xb = static_cast<uint32_t>(u);
+        float x;
+        std::memcpy(&x, &xb, 4);
+        float y = oracle_softcap(x, cap, inv_cap);
+        uint32_t yb;
+        std::memcpy(&yb, &y, 4);
+        if (y != y) yb = 0x7fc00000u;  // canonical NaN
+        uint64_t h = (static_cast<uint64_t>(xb) << 32) | yb;
+        h ^= h >> 33; h *= 0xff51afd7ed558ccdULL; h ^= h >> 33; h *= 0xc4ceb9fe1a85ec53ULL; h ^= h >> 33;
+        acc += h;
+      }
+      part[t] = acc;
+    });
+  }
+  for (auto& th : pool) th.join();
+  uint64_t s = 0;
+  for (auto p : part) s += p;
+  return s;
+}
+
+// Batched driver used for the timed CPU baseline: rows are independent, so rows are
+// split over `threads` host threads.  history is [rows, history_stride] with per-row
+// lengths; mask_table/mask_state optional (state < 0 = unconstrained): masked ids are
+// -inf before penalties exactly as selectConstrainedToken does
+// (src/runtime/gemma-session.ts:1327-1328).  softcap 0 = off.
+void oracle_sample_rows(const float* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                        float softcap,
+                        const int32_t* history, int64_t history_stride, const int32_t* history_len,
+                        const uint32_t* mask_table, int64_t mask_words, const int32_t* mask_state,
+                        const OracleConfig* configs, int32_t per_row_config,
+                        double* rng_state, const double* uniforms,
+                        int32_t* out_ids, OracleTrace* traces, int threads) {
+  if (threads < 1) threads = 1;
+  std::vector<std::thread> pool;
+  for (int t = 0; t < threads; ++t) {
+    pool.emplace_back([=] {
+      std::vector<float> row(static_cast<size_t>(vocab));
+      float inv = softcap != 0 ? static_cast<float>(1.0 / static_cast<double>(softcap)) : 0.0f;
+      for (int64_t r = t; r < rows; r += threads) {
+        const float* src = logits + r * row_stride;
+        for (int64_t i = 0; i < vocab; ++i) row[i] = softcap != 0 ? oracle_softcap(src[i], softcap, inv) : src[i];
+        if (mask_table && mask_state && mask_state[r] >= 0) {
+          const uint32_t* m = mask_table + static_cast<int64_t>(mask_state[r]) * mask_words;
+          for (int64_t i = 0; i < vocab; ++i)
+            if (!((m[i >> 5] >> (i & 31)) & 1u)) row[i] = -INFINITY;
+        }
+        const OracleConfig* c = configs + (per_row_config ? r : 0);
+        int64_t hl = history_len ? history_len[r] : 0;
+        const int32_t* h = history ? history + r * history_stride : nullptr;
+        OracleTrace tr;
+        int32_t id;
+        if (uniforms) {
+          id = oracle_sample_token(row.data(), vocab, h, hl, c, uniforms[r], nullptr, nullptr, nullptr, 0, &tr);
+        } else {
+          id = oracle_sample_token_seeded(row.data(), vocab, h, hl, c, rng_state + r, nullptr, nullptr, nullptr, 0, &tr);
+        }
+        out_ids[r] = id;
+        if (traces) traces[r] = tr;
+      }
+    });
+  }
+  for (auto& th : pool) th.join();
+}
+
+}  // extern "C"

@@ -1,0 +1,55 @@
+"""The C-ABI library loads on a machine without a GPU and exports every entry point that
+include/gsampler.h declares (no compute call is made here)."""
+import ctypes
+import os
+import re
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    text = open(os.path.join(ROOT, "include", "gsampler.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gs_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_header_declares_expected_symbols(pkg):
+    syms = header_symbols()
+    assert syms == sorted(pkg._lib.EXPORTS)
+
+
+def test_library_exports_every_header_symbol(pkg):
+    lib = pkg._lib.lib()
+    for name in header_symbols():
+        assert hasattr(lib, name), name
+        assert ctypes.cast(getattr(lib, name), ctypes.c_void_p).value
+
+
+def test_structs_match_header_layout(pkg, tmp_path):
+    """ctypes mirrors of gs_params / gs_batch / gs_outputs have the C compiler's layout."""
+    import subprocess
+    structs = {"gs_params": pkg._lib.GsParams, "gs_batch": pkg._lib.GsBatch, "gs_outputs": pkg._lib.GsOutputs}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "gsampler.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for f, _ in cls._fields_:
+            lines.append(f'printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines())
+    for cname, cls in structs.items():
+        assert int(got[cname]) == ctypes.sizeof(cls), cname
+        for f, _ in cls._fields_:
+            assert int(got[f"{cname}.{f}"]) == getattr(cls, f).offset, f"{cname}.{f}"
+
+
+def test_no_cpu_fallback_without_device(pkg):
+    import torch
+    if torch.cuda.is_available():
+        return
+    import pytest
+    with pytest.raises(pkg.SamplerError):
+        pkg.GpuSampler(0)
