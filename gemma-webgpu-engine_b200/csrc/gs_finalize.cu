@@ -329,11 +329,12 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
       A.logprob[row] = lp;
     }
   }
-  if (A.cand_ids && !err) {
-    const int nw = n_final < A.cand_cap ? n_final : A.cand_cap;
-    for (int i = tid; i < nw; i += bs) {
-      A.cand_ids[static_cast<int64_t>(row) * A.cand_cap + i] = static_cast<int32_t>(w.cid[i]);
-      if (A.cand_probs) A.cand_probs[static_cast<int64_t>(row) * A.cand_cap + i] = w.cp[i];
+  if (A.cand_ids) {
+    // final candidates in draw order; unused slots are -1 / 0 so outputs are fully defined
+    const int nw = err ? 0 : (n_final < A.cand_cap ? n_final : A.cand_cap);
+    for (int i = tid; i < A.cand_cap; i += bs) {
+      A.cand_ids[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? static_cast<int32_t>(w.cid[i]) : -1;
+      if (A.cand_probs) A.cand_probs[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? w.cp[i] : 0.0;
     }
   }
 }

@@ -86,6 +86,13 @@ def params_from_config(config: dict) -> GsParams:
                     int(top_k) if top_k < 2**31 else 2**31 - 1, 0)
 
 
+def _params_array(params):
+    """One gs_params per entry of `params` (a config dict, a GsParams, or a list of them)."""
+    if isinstance(params, (dict, GsParams)):
+        params = [params]
+    return (GsParams * len(params))(*[p if isinstance(p, GsParams) else params_from_config(p) for p in params])
+
+
 def windowed_history(history: Sequence[int], window: int) -> list:
     """history.slice(-config.repetitionWindow), or [] for a zero window (sampling.ts:22-24)."""
     if window == 0:
@@ -158,9 +165,7 @@ class GpuSampler:
         if logits.stride(1) != 1:
             raise ValueError("logits rows must be contiguous")
         rows, vocab = logits.shape
-        if isinstance(params, dict):
-            params = [params]
-        parr = (GsParams * len(params))(*[p if isinstance(p, GsParams) else params_from_config(p) for p in params])
+        parr = _params_array(params)
         b = GsBatch()
         b.logits = logits.data_ptr()
         b.dtype = dtype
@@ -168,7 +173,7 @@ class GpuSampler:
         b.vocab = vocab
         b.row_stride = logits.stride(0) if rows > 1 else vocab
         b.softcap = float(softcap)
-        b.params_count = len(params)
+        b.params_count = len(parr)
         b.params = ctypes.cast(parr, ctypes.c_void_p)
         if history is not None:
             b.history = history.data_ptr()
@@ -231,9 +236,7 @@ class GpuSampler:
         if logits.ndim != 2:
             raise ValueError("logits must be [rows, vocab]")
         rows, vocab = logits.shape
-        if isinstance(params, dict):
-            params = [params]
-        parr = (GsParams * len(params))(*[p if isinstance(p, GsParams) else params_from_config(p) for p in params])
+        parr = _params_array(params)
         b = GsBatch()
         b.logits = logits.ctypes.data
         b.dtype = dtype
@@ -241,7 +244,7 @@ class GpuSampler:
         b.vocab = vocab if dtype == _lib.GS_DTYPE_F32 else vocab
         b.row_stride = logits.strides[0] // logits.itemsize
         b.softcap = float(softcap)
-        b.params_count = len(params)
+        b.params_count = len(parr)
         b.params = ctypes.cast(parr, ctypes.c_void_p)
         if history is not None:
             b.history = history.ctypes.data
