@@ -1,5 +1,6 @@
 // Host side of the C ABI declared in include/gsampler.h.
 #include "gs_internal.cuh"
+#include "gs_plan.cuh"
 #include "../../include/gsampler.h"
 
 #include <algorithm>
@@ -67,8 +68,6 @@ struct DeviceGuard {
   }
 };
 
-size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-
 gs_status ensure_ws(gs_ctx* c, size_t bytes) {
   if (bytes <= c->ws_bytes) return GS_OK;
   if (c->ws) {
@@ -111,157 +110,6 @@ gs_status ensure_plans_host(gs_ctx* c, size_t n) {
   cudaError_t e = cudaMallocHost(&c->plans_host, n * sizeof(RowPlan));
   if (e != cudaSuccess) return cuda_fail(c, e, "pinned plan staging");
   c->plans_cap = n;
-  return GS_OK;
-}
-
-// validateDecodingConfig (src/runtime/decoding.ts:31-59), for the fields sampleToken reads.
-bool valid_params(const gs_params& p, std::string* why) {
-  std::vector<std::string> errors;
-  if (!std::isfinite(p.temperature) || p.temperature < 0) errors.push_back("temperature must be >= 0");
-  if (p.top_k < 0) errors.push_back("topK must be a non-negative integer");
-  const double v3[3] = {p.top_p, p.min_p, p.typical_p};
-  const char* n3[3] = {"topP", "minP", "typicalP"};
-  for (int i = 0; i < 3; ++i)
-    if (!std::isfinite(v3[i]) || v3[i] < 0 || v3[i] > 1) errors.push_back(std::string(n3[i]) + " must be between 0 and 1");
-  if (!std::isfinite(p.repetition_penalty) || p.repetition_penalty <= 0) errors.push_back("repetitionPenalty must be > 0");
-  if (!std::isfinite(p.frequency_penalty) || p.frequency_penalty < 0)
-    errors.push_back("frequencyPenalty must be finite and non-negative");
-  if (!std::isfinite(p.presence_penalty) || p.presence_penalty < 0)
-    errors.push_back("presencePenalty must be finite and non-negative");
-  if (errors.empty()) return true;
-  std::string s = "Invalid Gemma decoding config: ";
-  for (size_t i = 0; i < errors.size(); ++i) s += (i ? "; " : "") + errors[i];
-  *why = s;
-  return false;
-}
-
-RowPlan make_plan(const gs_params& p, int64_t vocab) {
-  RowPlan r{};
-  r.temperature = p.temperature;
-  r.top_p = p.top_p;
-  r.min_p = p.min_p;
-  r.typical_p = p.typical_p;
-  r.repetition_penalty = p.repetition_penalty;
-  r.presence_penalty = p.presence_penalty;
-  r.frequency_penalty = p.frequency_penalty;
-  r.top_k = p.top_k;
-  if (p.temperature == 0) {
-    r.mode = kModeGreedy;
-    r.k_eff = 1;
-    r.a2 = 0;
-    r.a2_hi = 0;
-    r.a2_lo = FLT_MIN;
-  } else {
-    r.a2 = 1.4426950408889634 / p.temperature;
-    float hi = static_cast<float>(r.a2);
-    if (static_cast<double>(hi) > r.a2) hi = std::nextafter(hi, 0.0f);
-    float lo = static_cast<float>(r.a2 - static_cast<double>(hi));
-    if (!(lo >= FLT_MIN)) lo = FLT_MIN;
-    r.a2_hi = hi;
-    r.a2_lo = lo;
-    if (p.top_k >= 1 && p.top_k <= GS_MAX_TOP_K) {
-      r.mode = kModeSmallK;
-      r.k_eff = static_cast<int32_t>(std::min<int64_t>(p.top_k, vocab));
-    } else {
-      r.mode = kModeLarge;
-      r.k_eff = 0;
-    }
-  }
-  return r;
-}
-
-int pow2ceil(int64_t n) {
-  int p = 1;
-  while (p < n) p <<= 1;
-  return p;
-}
-
-struct Layout {
-  int splits;
-  int64_t chunk;
-  int kcap;
-  int kc;
-  int kmax;
-  bool any_large;
-  bool any_sample;
-  size_t plans_off, stats_off, cands_off, total;
-  size_t stream_smem, fin_smem, large_smem;
-  int hist_cap, ent_cap, pack_cap;
-};
-
-gs_status plan_layout(gs_ctx* c, const gs_batch* b, const std::vector<RowPlan>& plans, Layout* L) {
-  const int rows = b->rows;
-  int kmax = 0;
-  bool any_large = false, any_sample = false;
-  for (const auto& p : plans) {
-    kmax = std::max(kmax, p.k_eff);
-    any_large |= p.mode == kModeLarge;
-    any_sample |= p.mode != kModeGreedy;
-  }
-  const int nplans = static_cast<int>(plans.size());
-  (void)nplans;
-  // vocabulary splits: enough units to fill the GPU, chunks of >= 4096 ids, and at most
-  // 16384 streamed candidates per row for the merge
-  const int64_t V = b->vocab;
-  const int target_units = 148 * 4;
-  int S = 1;
-  while (static_cast<int64_t>(rows) * S < target_units && V / (2 * S) >= 4096 && 2 * S * std::max(kmax, 1) <= 16384 && S < 256)
-    S *= 2;
-  int64_t chunk = (V + S - 1) / S;
-  chunk = (chunk + 1023) / 1024 * 1024;
-  S = static_cast<int>((V + chunk - 1) / chunk);
-  const int kcap = std::max(kmax, 1);
-  int kc = 256;
-  while (kc < 2 * kmax) kc <<= 1;
-  if (kc > 4096) return fail(c, GS_EUNSUPPORTED, "topK above %d is not supported by the streaming buffer", GS_MAX_TOP_K);
-  L->splits = S;
-  L->chunk = chunk;
-  L->kcap = kcap;
-  L->kc = kc;
-  L->kmax = kmax;
-  L->any_large = any_large;
-  L->any_sample = any_sample;
-  const int64_t units = static_cast<int64_t>(rows) * S;
-  L->plans_off = 0;
-  L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
-  L->cands_off = align_up(L->stats_off + static_cast<size_t>(units) * sizeof(UnitStat), 256);
-  L->total = align_up(L->cands_off + static_cast<size_t>(units) * kcap * 8, 256);
-  L->stream_smem = stream_smem_bytes(chunk, kc);
-  const int64_t hs = b->history ? b->history_stride : 0;
-  L->hist_cap = pow2ceil(std::max<int64_t>(hs, 1));
-  L->pack_cap = S > 1 ? S * kcap : 0;
-  L->ent_cap = pow2ceil(std::max<int64_t>(std::min<int64_t>(static_cast<int64_t>(S) * kcap, kmax) + hs, 1));
-  L->fin_smem = finalize_smem_bytes(L->hist_cap, L->ent_cap, L->pack_cap);
-  if (L->fin_smem > 220 * 1024)
-    return fail(c, GS_EUNSUPPORTED, "merge needs %zu bytes of shared memory (topK %d, history %lld)", L->fin_smem, kmax,
-                static_cast<long long>(hs));
-  L->large_smem = any_large ? large_smem_bytes(V, L->hist_cap) : 0;
-  if (L->large_smem > 220 * 1024) return fail(c, GS_EUNSUPPORTED, "vocabulary too large for the histogram path");
-  return GS_OK;
-}
-
-gs_status check_batch(gs_ctx* c, const gs_batch* b, const gs_outputs* o) {
-  if (!c) return GS_EINVAL;
-  if (!b || !o) return fail(c, GS_EINVAL, "batch and outputs are required");
-  if (b->rows < 0) return fail(c, GS_EINVAL, "rows must be >= 0");
-  if (b->vocab <= 0) return fail(c, GS_EEMPTY, "Cannot sample empty logits");
-  if (b->vocab >= (1ll << 31)) return fail(c, GS_EINVAL, "vocab must be below 2^31");
-  if (b->row_stride < b->vocab) return fail(c, GS_EINVAL, "row_stride must be >= vocab");
-  if (b->dtype != GS_DTYPE_F32 && b->dtype != GS_DTYPE_BF16) return fail(c, GS_EINVAL, "unknown dtype %d", b->dtype);
-  if (b->rows > 0 && !b->logits) return fail(c, GS_EINVAL, "logits is NULL");
-  if (!(b->softcap >= 0) || !std::isfinite(b->softcap)) return fail(c, GS_EINVAL, "softcap must be finite and >= 0");
-  if (!b->params || (b->params_count != 1 && b->params_count != b->rows))
-    return fail(c, GS_EINVAL, "params_count must be 1 or rows");
-  if (b->history && (b->history_stride < 0 || b->history_stride > GS_MAX_HISTORY))
-    return fail(c, GS_EUNSUPPORTED, "history_stride must be in [0, %d]", GS_MAX_HISTORY);
-  if (b->history && !b->history_len) return fail(c, GS_EINVAL, "history_len is required with history");
-  if (b->mask_table) {
-    if (!b->mask_state) return fail(c, GS_EINVAL, "mask_state is required with mask_table");
-    if (b->mask_words < (b->vocab + 31) / 32) return fail(c, GS_EINVAL, "mask_words must be >= ceil(vocab/32)");
-    if (b->mask_states <= 0) return fail(c, GS_EINVAL, "mask_states must be > 0");
-  }
-  if (b->rows > 0 && !o->ids) return fail(c, GS_EINVAL, "outputs.ids is NULL");
-  if (o->cand_ids && o->cand_cap <= 0) return fail(c, GS_EINVAL, "cand_cap must be > 0 with cand_ids");
   return GS_OK;
 }
 
@@ -322,80 +170,50 @@ gs_status gs_reserve(gs_ctx* c, int32_t rows, int64_t vocab, int32_t max_top_k, 
   b.row_stride = vocab;
   b.params = &p;
   b.params_count = 1;
-  b.history = history_stride > 0 ? reinterpret_cast<const int32_t*>(16) : nullptr;
   b.history_stride = history_stride;
-  std::vector<RowPlan> plans(1, make_plan(p, vocab));
+  PlanSummary ps;
+  ps.add(make_plan(p, vocab));
   Layout L;
-  gs_status s = plan_layout(c, &b, plans, &L);
+  const int32_t dummy = 0;
+  if (history_stride > 0) b.history = &dummy;
+  gs_status s = plan_layout(&b, ps, &L, &c->err);
   if (s != GS_OK) return s;
-  // per-row plans may be uploaded: size for rows of them
-  const size_t bytes = std::max(L.total, align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256) + (L.total - L.stats_off));
-  s = ensure_ws(c, bytes);
+  s = ensure_ws(c, L.total);
   if (s != GS_OK) return s;
   return ensure_plans_host(c, std::max<size_t>(rows, 1));
 }
 
 gs_status gs_sample(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stream) {
-  gs_status s = check_batch(c, b, o);
+  if (!c) return GS_EINVAL;
+  gs_status s = check_batch(b, o, &c->err);
   if (s != GS_OK) return s;
   if (b->rows == 0) return GS_OK;
   DeviceGuard g(c->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int rows = b->rows;
   const int np = b->params_count;
-  std::vector<RowPlan> plans(np);
-  for (int i = 0; i < np; ++i) {
-    std::string why;
-    if (!valid_params(b->params[i], &why)) return fail(c, GS_EINVAL, "%s", why.c_str());
-    plans[i] = make_plan(b->params[i], b->vocab);
-  }
-  bool any_sample = false;
-  for (const auto& p : plans) any_sample |= p.mode != kModeGreedy;
-  if (any_sample && !b->rng_state && !b->uniforms) return fail(c, GS_EINVAL, "rng_state or uniforms is required");
+  PlanSummary ps;
+  for (int i = 0; i < np; ++i) ps.add(make_plan(b->params[i], b->vocab));
+  if (ps.any_sample && !b->rng_state && !b->uniforms) return fail(c, GS_EINVAL, "rng_state or uniforms is required");
   Layout L;
-  s = plan_layout(c, b, plans, &L);
+  s = plan_layout(b, ps, &L, &c->err);
   if (s != GS_OK) return s;
   s = ensure_ws(c, L.total);
   if (s != GS_OK) return s;
+  const RowPlan plan0 = make_plan(b->params[0], b->vocab);
   const RowPlan* dplans = nullptr;
   if (np > 1) {
     s = ensure_plans_host(c, np);
     if (s != GS_OK) return s;
-    std::memcpy(c->plans_host, plans.data(), np * sizeof(RowPlan));
+    for (int i = 0; i < np; ++i) c->plans_host[i] = make_plan(b->params[i], b->vocab);
     dplans = reinterpret_cast<const RowPlan*>(c->ws + L.plans_off);
-    cudaError_t e = cudaMemcpyAsync(const_cast<RowPlan*>(dplans), c->plans_host, np * sizeof(RowPlan), cudaMemcpyHostToDevice, st);
+    cudaError_t e = cudaMemcpyAsync(const_cast<RowPlan*>(dplans), c->plans_host, np * sizeof(RowPlan),
+                                    cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_fail(c, e, "plan upload");
     cudaEventRecord(c->plans_ev, st);
     c->plans_ev_live = true;
   }
   UnitStat* stats = reinterpret_cast<UnitStat*>(c->ws + L.stats_off);
   unsigned long long* cands = reinterpret_cast<unsigned long long*>(c->ws + L.cands_off);
-  const float cap = b->softcap;
-  const float inv_cap = cap != 0.0f ? static_cast<float>(1.0 / static_cast<double>(cap)) : 0.0f;
-
-  StreamArgs sa{};
-  sa.logits = b->logits;
-  sa.vocab = b->vocab;
-  sa.row_stride = b->row_stride;
-  sa.vocab_offset = 0;
-  sa.softcap = cap;
-  sa.inv_softcap = inv_cap;
-  sa.want_raw = o->logprob != nullptr;
-  sa.splits = L.splits;
-  sa.chunk = L.chunk;
-  sa.kcap = L.kcap;
-  sa.kc = L.kc;
-  sa.plans = dplans;
-  sa.plan0 = plans[0];
-  sa.history = b->history;
-  sa.history_len = b->history ? b->history_len : nullptr;
-  sa.history_stride = b->history ? b->history_stride : 0;
-  sa.mask_table = b->mask_table;
-  sa.mask_states = b->mask_states;
-  sa.mask_words = b->mask_words;
-  sa.mask_state = b->mask_table ? b->mask_state : nullptr;
-  sa.stats = stats;
-  sa.cands = cands;
   std::array<cudaEvent_t, 3> evs{};
   if (c->profile) {
     for (auto& ev : evs) {
@@ -407,63 +225,16 @@ gs_status gs_sample(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* str
       ev = c->ev_pool.back();
       c->ev_pool.pop_back();
     }
-    cudaEventRecord(evs[0], st);
   }
-  cudaError_t e = launch_stream(sa, b->dtype, rows, L.stream_smem, st);
-  if (e != cudaSuccess) return cuda_fail(c, e, "streaming pass launch");
-
-  FinalizeArgs fa{};
-  fa.logits = b->logits;
-  fa.vocab = b->vocab;
-  fa.row_stride = b->row_stride;
-  fa.softcap = cap;
-  fa.inv_softcap = inv_cap;
-  fa.want_raw = sa.want_raw;
-  fa.splits = L.splits;
-  fa.kcap = L.kcap;
-  fa.hist_cap = L.hist_cap;
-  fa.ent_cap = L.ent_cap;
-  fa.pack_cap = L.pack_cap;
-  fa.plans = dplans;
-  fa.plan0 = plans[0];
-  fa.history = sa.history;
-  fa.history_len = sa.history_len;
-  fa.history_stride = sa.history_stride;
-  fa.mask_table = b->mask_table;
-  fa.mask_states = b->mask_states;
-  fa.mask_words = b->mask_words;
-  fa.mask_state = sa.mask_state;
-  fa.stats = stats;
-  fa.cands = cands;
-  fa.rng_state = b->rng_state;
-  fa.uniforms = b->uniforms;
-  fa.ids = o->ids;
-  fa.logprob = o->logprob;
-  fa.flags = o->flags;
-  fa.cand_ids = o->cand_ids;
-  fa.cand_probs = o->cand_probs;
-  fa.cand_count = o->cand_count;
-  fa.cand_cap = o->cand_cap;
-  bool any_small = false;
-  for (const auto& p : plans) any_small |= p.mode != kModeLarge;
-  if (c->profile) cudaEventRecord(evs[1], st);
-  if (any_small) {
-    e = launch_finalize(fa, b->dtype, rows, L.fin_smem, st);
-    if (e != cudaSuccess) return cuda_fail(c, e, "merge launch");
-  }
-  if (L.any_large) {
-    e = launch_large(fa, b->dtype, rows, L.large_smem, st);
-    if (e != cudaSuccess) return cuda_fail(c, e, "histogram path launch");
-  }
-  if (c->profile) {
-    cudaEventRecord(evs[2], st);
-    c->ev_live.push_back(evs);
-  }
+  s = launch_sampling(b, o, L, plan0, dplans, stats, cands, st, c->profile ? evs.data() : nullptr, &c->err);
+  if (s != GS_OK) return s;
+  if (c->profile) c->ev_live.push_back(evs);
   return GS_OK;
 }
 
 gs_status gs_sample_host(gs_ctx* c, const gs_batch* hb, const gs_outputs* ho, void* stream) {
-  gs_status s = check_batch(c, hb, ho);
+  if (!c) return GS_EINVAL;
+  gs_status s = check_batch(hb, ho, &c->err);
   if (s != GS_OK) return s;
   if (hb->rows == 0) return GS_OK;
   DeviceGuard g(c->device);

@@ -1,0 +1,201 @@
+// Host-side planning shared by gs_sample, gs_sample_host and gs_sample_noalloc.
+#include "gs_plan.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <vector>
+
+namespace gs {
+
+namespace {
+
+gs_status fmt(std::string* err, gs_status s, const char* f, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, f);
+  vsnprintf(buf, sizeof(buf), f, ap);
+  va_end(ap);
+  if (err) *err = buf;
+  return s;
+}
+
+int pow2ceil(int64_t n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+bool valid_params(const gs_params& p, std::string* why) {
+  std::vector<std::string> errors;
+  if (!std::isfinite(p.temperature) || p.temperature < 0) errors.push_back("temperature must be >= 0");
+  if (p.top_k < 0) errors.push_back("topK must be a non-negative integer");
+  const double v3[3] = {p.top_p, p.min_p, p.typical_p};
+  const char* n3[3] = {"topP", "minP", "typicalP"};
+  for (int i = 0; i < 3; ++i)
+    if (!std::isfinite(v3[i]) || v3[i] < 0 || v3[i] > 1) errors.push_back(std::string(n3[i]) + " must be between 0 and 1");
+  if (!std::isfinite(p.repetition_penalty) || p.repetition_penalty <= 0) errors.push_back("repetitionPenalty must be > 0");
+  if (!std::isfinite(p.frequency_penalty) || p.frequency_penalty < 0)
+    errors.push_back("frequencyPenalty must be finite and non-negative");
+  if (!std::isfinite(p.presence_penalty) || p.presence_penalty < 0)
+    errors.push_back("presencePenalty must be finite and non-negative");
+  if (errors.empty()) return true;
+  std::string s = "Invalid Gemma decoding config: ";
+  for (size_t i = 0; i < errors.size(); ++i) s += (i ? "; " : "") + errors[i];
+  if (why) *why = s;
+  return false;
+}
+
+gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err) {
+  if (!b || !o) return fmt(err, GS_EINVAL, "batch and outputs are required");
+  if (b->rows < 0) return fmt(err, GS_EINVAL, "rows must be >= 0");
+  if (b->vocab <= 0) return fmt(err, GS_EEMPTY, "Cannot sample empty logits");
+  if (b->vocab >= (1ll << 31)) return fmt(err, GS_EINVAL, "vocab must be below 2^31");
+  if (b->row_stride < b->vocab) return fmt(err, GS_EINVAL, "row_stride must be >= vocab");
+  if (b->dtype != GS_DTYPE_F32 && b->dtype != GS_DTYPE_BF16) return fmt(err, GS_EINVAL, "unknown dtype %d", b->dtype);
+  if (b->rows > 0 && !b->logits) return fmt(err, GS_EINVAL, "logits is NULL");
+  if (!(b->softcap >= 0) || !std::isfinite(b->softcap)) return fmt(err, GS_EINVAL, "softcap must be finite and >= 0");
+  if (!b->params || (b->params_count != 1 && b->params_count != b->rows))
+    return fmt(err, GS_EINVAL, "params_count must be 1 or rows");
+  if (b->history && (b->history_stride < 0 || b->history_stride > GS_MAX_HISTORY))
+    return fmt(err, GS_EUNSUPPORTED, "history_stride must be in [0, %d]", GS_MAX_HISTORY);
+  if (b->history && !b->history_len) return fmt(err, GS_EINVAL, "history_len is required with history");
+  if (b->mask_table) {
+    if (!b->mask_state) return fmt(err, GS_EINVAL, "mask_state is required with mask_table");
+    if (b->mask_words < (b->vocab + 31) / 32) return fmt(err, GS_EINVAL, "mask_words must be >= ceil(vocab/32)");
+    if (b->mask_states <= 0) return fmt(err, GS_EINVAL, "mask_states must be > 0");
+  }
+  if (b->rows > 0 && !o->ids) return fmt(err, GS_EINVAL, "outputs.ids is NULL");
+  if (o->cand_ids && o->cand_cap <= 0) return fmt(err, GS_EINVAL, "cand_cap must be > 0 with cand_ids");
+  for (int i = 0; i < b->params_count; ++i)
+    if (!valid_params(b->params[i], err)) return GS_EINVAL;
+  return GS_OK;
+}
+
+gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::string* err) {
+  const int rows = b->rows;
+  const int kmax = ps.kmax;
+  // Vocabulary splits: enough units to fill the GPU, chunks of >= 4096 ids, and at most
+  // 16384 streamed candidates per row for the merge.
+  const int64_t V = b->vocab;
+  const int target_units = 148 * 4;
+  int S = 1;
+  while (static_cast<int64_t>(rows) * S < target_units && V / (2 * S) >= 4096 && 2 * S * std::max(kmax, 1) <= 16384 &&
+         S < 256)
+    S *= 2;
+  int64_t chunk = (V + S - 1) / S;
+  chunk = (chunk + 1023) / 1024 * 1024;
+  S = static_cast<int>((V + chunk - 1) / chunk);
+  const int kcap = std::max(kmax, 1);
+  int kc = 256;
+  while (kc < 2 * kmax) kc <<= 1;
+  if (kc > 4096) return fmt(err, GS_EUNSUPPORTED, "topK above %d is not supported by the streaming buffer", GS_MAX_TOP_K);
+  L->splits = S;
+  L->chunk = chunk;
+  L->kcap = kcap;
+  L->kc = kc;
+  L->kmax = kmax;
+  L->any_large = ps.any_large;
+  L->any_small = ps.any_small;
+  L->any_sample = ps.any_sample;
+  const int64_t units = static_cast<int64_t>(rows) * S;
+  L->plans_off = 0;
+  L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
+  L->cands_off = align_up(L->stats_off + static_cast<size_t>(units) * sizeof(UnitStat), 256);
+  L->total = align_up(L->cands_off + static_cast<size_t>(units) * kcap * 8, 256);
+  L->stream_smem = stream_smem_bytes(chunk, kc);
+  const int64_t hs = b->history ? b->history_stride : 0;
+  L->hist_cap = pow2ceil(std::max<int64_t>(hs, 1));
+  L->pack_cap = S > 1 ? S * kcap : 0;
+  L->ent_cap = pow2ceil(std::max<int64_t>(std::min<int64_t>(static_cast<int64_t>(S) * kcap, kmax) + hs, 1));
+  L->fin_smem = finalize_smem_bytes(L->hist_cap, L->ent_cap, L->pack_cap);
+  if (L->fin_smem > 220 * 1024)
+    return fmt(err, GS_EUNSUPPORTED, "merge needs %zu bytes of shared memory (topK %d, history %lld)", L->fin_smem, kmax,
+               static_cast<long long>(hs));
+  L->large_smem = ps.any_large ? large_smem_bytes(V, L->hist_cap) : 0;
+  if (L->large_smem > 220 * 1024) return fmt(err, GS_EUNSUPPORTED, "vocabulary too large for the histogram path");
+  return GS_OK;
+}
+
+gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
+                          const RowPlan* dplans, UnitStat* stats, unsigned long long* cands, cudaStream_t st,
+                          cudaEvent_t* events, std::string* err) {
+  const int rows = b->rows;
+  const float cap = b->softcap;
+  const float inv_cap = cap != 0.0f ? static_cast<float>(1.0 / static_cast<double>(cap)) : 0.0f;
+  StreamArgs sa{};
+  sa.logits = b->logits;
+  sa.vocab = b->vocab;
+  sa.row_stride = b->row_stride;
+  sa.vocab_offset = 0;
+  sa.softcap = cap;
+  sa.inv_softcap = inv_cap;
+  sa.want_raw = o->logprob != nullptr;
+  sa.splits = L.splits;
+  sa.chunk = L.chunk;
+  sa.kcap = L.kcap;
+  sa.kc = L.kc;
+  sa.plans = dplans;
+  sa.plan0 = plan0;
+  sa.history = b->history;
+  sa.history_len = b->history ? b->history_len : nullptr;
+  sa.history_stride = b->history ? b->history_stride : 0;
+  sa.mask_table = b->mask_table;
+  sa.mask_states = b->mask_states;
+  sa.mask_words = b->mask_words;
+  sa.mask_state = b->mask_table ? b->mask_state : nullptr;
+  sa.stats = stats;
+  sa.cands = cands;
+  if (events) cudaEventRecord(events[0], st);
+  cudaError_t e = launch_stream(sa, b->dtype, rows, L.stream_smem, st);
+  if (e != cudaSuccess) return fmt(err, GS_ECUDA, "streaming pass launch: %s", cudaGetErrorString(e));
+  if (events) cudaEventRecord(events[1], st);
+
+  FinalizeArgs fa{};
+  fa.logits = b->logits;
+  fa.vocab = b->vocab;
+  fa.row_stride = b->row_stride;
+  fa.softcap = cap;
+  fa.inv_softcap = inv_cap;
+  fa.want_raw = sa.want_raw;
+  fa.splits = L.splits;
+  fa.kcap = L.kcap;
+  fa.hist_cap = L.hist_cap;
+  fa.ent_cap = L.ent_cap;
+  fa.pack_cap = L.pack_cap;
+  fa.plans = dplans;
+  fa.plan0 = plan0;
+  fa.history = sa.history;
+  fa.history_len = sa.history_len;
+  fa.history_stride = sa.history_stride;
+  fa.mask_table = b->mask_table;
+  fa.mask_states = b->mask_states;
+  fa.mask_words = b->mask_words;
+  fa.mask_state = sa.mask_state;
+  fa.stats = stats;
+  fa.cands = cands;
+  fa.rng_state = b->rng_state;
+  fa.uniforms = b->uniforms;
+  fa.ids = o->ids;
+  fa.logprob = o->logprob;
+  fa.flags = o->flags;
+  fa.cand_ids = o->cand_ids;
+  fa.cand_probs = o->cand_probs;
+  fa.cand_count = o->cand_count;
+  fa.cand_cap = o->cand_cap;
+  if (L.any_small) {
+    e = launch_finalize(fa, b->dtype, rows, L.fin_smem, st);
+    if (e != cudaSuccess) return fmt(err, GS_ECUDA, "merge launch: %s", cudaGetErrorString(e));
+  }
+  if (L.any_large) {
+    e = launch_large(fa, b->dtype, rows, L.large_smem, st);
+    if (e != cudaSuccess) return fmt(err, GS_ECUDA, "histogram path launch: %s", cudaGetErrorString(e));
+  }
+  if (events) cudaEventRecord(events[2], st);
+  return GS_OK;
+}
+
+}  // namespace gs

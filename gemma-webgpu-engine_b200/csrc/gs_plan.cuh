@@ -1,0 +1,91 @@
+// Planning shared by the entry points: per-row plans, work layout, argument checks and
+// the launch sequence of one sampling call.
+#pragma once
+#include <cfloat>
+#include <cstddef>
+#include <string>
+
+#include "gs_internal.cuh"
+#include "../../include/gsampler.h"
+
+namespace gs {
+
+// Per-row plan from one DecodingConfig (the fields sampleToken reads).
+__host__ __device__ inline RowPlan make_plan(const gs_params& p, int64_t vocab) {
+  RowPlan r{};
+  r.temperature = p.temperature;
+  r.top_p = p.top_p;
+  r.min_p = p.min_p;
+  r.typical_p = p.typical_p;
+  r.repetition_penalty = p.repetition_penalty;
+  r.presence_penalty = p.presence_penalty;
+  r.frequency_penalty = p.frequency_penalty;
+  r.top_k = p.top_k;
+  if (p.temperature == 0) {
+    r.mode = kModeGreedy;
+    r.k_eff = 1;
+    r.a2 = 0;
+    r.a2_hi = 0;
+    r.a2_lo = FLT_MIN;
+  } else {
+    r.a2 = 1.4426950408889634 / p.temperature;
+    float hi = static_cast<float>(r.a2);
+    if (static_cast<double>(hi) > r.a2) hi = nextafterf(hi, 0.0f);
+    float lo = static_cast<float>(r.a2 - static_cast<double>(hi));
+    if (!(lo >= FLT_MIN)) lo = FLT_MIN;
+    r.a2_hi = hi;
+    r.a2_lo = lo;
+    if (p.top_k >= 1 && p.top_k <= GS_MAX_TOP_K) {
+      r.mode = kModeSmallK;
+      r.k_eff = static_cast<int32_t>(p.top_k < vocab ? p.top_k : vocab);
+    } else {
+      r.mode = kModeLarge;
+      r.k_eff = 0;
+    }
+  }
+  return r;
+}
+
+struct Layout {
+  int splits;
+  int64_t chunk;
+  int kcap;
+  int kc;
+  int kmax;
+  bool any_large;
+  bool any_small;
+  bool any_sample;
+  size_t plans_off, stats_off, cands_off, total;
+  size_t stream_smem, fin_smem, large_smem;
+  int hist_cap, ent_cap, pack_cap;
+};
+
+// Summary of the rows' plans that the layout depends on.
+struct PlanSummary {
+  int kmax = 0;
+  bool any_large = false;
+  bool any_small = false;
+  bool any_sample = false;
+  void add(const RowPlan& p) {
+    kmax = p.k_eff > kmax ? p.k_eff : kmax;
+    any_large |= p.mode == kModeLarge;
+    any_small |= p.mode != kModeLarge;
+    any_sample |= p.mode != kModeGreedy;
+  }
+};
+
+// validateDecodingConfig (src/runtime/decoding.ts:31-59) for the fields sampleToken reads.
+bool valid_params(const gs_params& p, std::string* why);
+gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err);
+gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::string* err);
+
+// Launches the streaming pass, the merge and (when a row needs it) the histogram path.
+// `events` (3 entries or nullptr) are recorded before the stream pass, before the
+// merge, and at the end.
+gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
+                          const RowPlan* dplans, UnitStat* stats, unsigned long long* cands, cudaStream_t st,
+                          cudaEvent_t* events, std::string* err);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace gs
