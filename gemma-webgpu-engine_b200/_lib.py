@@ -49,8 +49,10 @@ EXPORTS = (
     "gs_create", "gs_destroy", "gs_reserve", "gs_last_error", "gs_sample", "gs_sample_host",
     "gs_token_log_probability", "gs_mask_constraint_logits", "gs_build_mask_row", "gs_softcap",
     "gs_softcap_digest", "gs_shard_record_bytes", "gs_shard_partials", "gs_shard_merge", "gs_profile_enable",
-    "gs_profile_read",
+    "gs_profile_read", "gs_sample_noalloc",
 )
+
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 class GsParams(ctypes.Structure):
@@ -139,6 +141,7 @@ def lib() -> ctypes.CDLL:
     L.gs_shard_record_bytes.restype = i64
     L.gs_shard_partials.argtypes = [P, ctypes.POINTER(GsBatch), i64, i64, P, P]
     L.gs_shard_merge.argtypes = [P, ctypes.POINTER(GsBatch), i64, i32, P, ctypes.POINTER(GsOutputs), P]
+    L.gs_sample_noalloc.argtypes = [ctypes.POINTER(GsBatch), ctypes.POINTER(GsOutputs), P]
     L.gs_profile_enable.argtypes = [P, i32]
     L.gs_profile_read.argtypes = [P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
                                   ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64)]

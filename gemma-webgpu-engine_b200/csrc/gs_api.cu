@@ -154,7 +154,7 @@ gs_status gs_destroy(gs_ctx* c) {
   return GS_OK;
 }
 
-const char* gs_last_error(const gs_ctx* c) { return c ? c->err.c_str() : "null context"; }
+const char* gs_last_error(const gs_ctx* c) { return c ? c->err.c_str() : noalloc_last_error(); }
 
 gs_status gs_reserve(gs_ctx* c, int32_t rows, int64_t vocab, int32_t max_top_k, int64_t history_stride) {
   if (!c || rows < 0 || vocab <= 0) return GS_EINVAL;

@@ -86,6 +86,9 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
                           const RowPlan* dplans, UnitStat* stats, unsigned long long* cands, cudaStream_t st,
                           cudaEvent_t* events, std::string* err);
 
+// Message of this thread's last failed gs_sample_noalloc call.
+const char* noalloc_last_error();
+
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace gs

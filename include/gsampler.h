@@ -115,6 +115,7 @@ gs_status gs_destroy(gs_ctx* ctx);
 /* Pre-sizes the workspace so that later gs_sample calls with at most these sizes
  * allocate nothing (and can be captured in a CUDA graph). */
 gs_status gs_reserve(gs_ctx* ctx, int32_t rows, int64_t vocab, int32_t max_top_k, int64_t history_stride);
+/* Message of the last failure on `ctx` (NULL: this thread's last gs_sample_noalloc failure). */
 const char* gs_last_error(const gs_ctx* ctx);
 
 /*
@@ -169,6 +170,26 @@ gs_status gs_softcap(gs_ctx* ctx, const float* in, float* out, int64_t n, float 
 /* Self-check: order-independent 64-bit digest of gs_softcap over the float bit patterns
  * [lo, hi), for exhaustive comparison with an independent host implementation. */
 gs_status gs_softcap_digest(gs_ctx* ctx, uint64_t lo, uint64_t hi, float cap, uint64_t* digest_host);
+
+/*
+ * Allocation-free sampling.  No counterpart in the reference: its sampler runs on the JS
+ * main thread and never holds device memory.  Some callers of this library cannot
+ * allocate device memory: a serving runtime whose memory pool already owns the device,
+ * a real-time decode loop that cannot take the device-wide synchronisation cudaMalloc /
+ * cudaFree imply, or an embedding that only lends its own input and output buffers.
+ * gs_sample_noalloc runs the same kernels as gs_sample without a context and without
+ * allocating: its per-call scratch (per-row plans, the streaming units' partial sums and
+ * candidates: about 2.1 MiB for 4096 rows at topK 50, 1.1 MiB for 8 rows at topK 1024)
+ * lives in one fixed device array of GS_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU
+ * which loads the library keeps until the process exits.  Larger requests fail with
+ * GS_EUNSUPPORTED.  It runs on the current device; its first call on a device looks up
+ * the array's device address.  All calls share the array (the previous call's contents
+ * stay in it; nothing needs clearing, every call writes what it reads), so calls whose
+ * kernels overlap on the GPU race.  After a failure, gs_last_error(NULL) returns this
+ * thread's message.
+ */
+#define GS_NOALLOC_SCRATCH_BYTES (8u << 20)
+gs_status gs_sample_noalloc(const gs_batch* batch, const gs_outputs* out, void* stream);
 
 /*
  * Kernel timing (the counterpart of measureGpuDispatches, src/webgpu/gpu-timestamp.ts:1-56,
