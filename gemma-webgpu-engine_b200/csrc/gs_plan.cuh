@@ -35,9 +35,13 @@ __host__ __device__ inline RowPlan make_plan(const gs_params& p, int64_t vocab) 
     if (!(lo >= FLT_MIN)) lo = FLT_MIN;
     r.a2_hi = hi;
     r.a2_lo = lo;
-    if (p.top_k >= 1 && p.top_k <= GS_MAX_TOP_K) {
+    // topK 0 (disabled) or topK >= V keeps the whole vocabulary (sampling.ts:44), which is
+    // the same as topK = V; small vocabularies therefore stay on the exact candidate path.
+    const int64_t k = (p.top_k == 0 || p.top_k > vocab) ? vocab : p.top_k;
+    if (k <= GS_MAX_TOP_K) {
       r.mode = kModeSmallK;
-      r.k_eff = static_cast<int32_t>(p.top_k < vocab ? p.top_k : vocab);
+      r.top_k = static_cast<int32_t>(k);
+      r.k_eff = static_cast<int32_t>(k);
     } else {
       r.mode = kModeLarge;
       r.k_eff = 0;

@@ -112,13 +112,13 @@ def case(spec_seed, name, rows, vocab, kind, params, **extra):
         assert res.token == ids[r]
         cand_ids.append(res.candidates)
         cand_probs.append(res.probabilities)
-        cand_n.append(len(res.candidates))
-    cap = max(max(cand_n), 1)
+        cand_n.append(res.trace.n_final)  # full count; at most 2048 ids are stored
+    cap = max(max(len(c) for c in cand_ids), 1)
     cid = np.full((rows, cap), -1, dtype=np.int32)
     cpr = np.zeros((rows, cap), dtype=np.float64)
     for r in range(rows):
-        cid[r, :cand_n[r]] = cand_ids[r]
-        cpr[r, :cand_n[r]] = cand_probs[r]
+        cid[r, :len(cand_ids[r])] = cand_ids[r]
+        cpr[r, :len(cand_probs[r])] = cand_probs[r]
     margins = np.array([[t.margin_top_p, t.margin_draw, t.margin_min_p, t.margin_typical] for t in traces])
     out = {
         f"{name}/rng_state": rng_state, f"{name}/rng_state_after": new_state, f"{name}/ids": ids,

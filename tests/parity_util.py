@@ -72,7 +72,7 @@ def oracle_rows(O, logits_np, vocab, softcap, params, *, history=None, history_l
             else:
                 res, _ = O.sample_token(row, h, p, rng_state=rng_state[r], cand_cap=cand_cap)
             assert res.token == ids[r]
-            cands.append((res.candidates, res.probabilities))
+            cands.append((res.candidates, res.probabilities, res.trace.n_final))
     margins = np.array([min(t.margin_top_p, t.margin_draw, t.margin_min_p, t.margin_typical) for t in traces])
     return ids, margins, cands, st
 
@@ -91,10 +91,11 @@ def compare(gpu: GpuOut, ids, margins, cands, *, rng_after=None, label=""):
             boundary_diffs += 1
             continue
         if cands and not flagged:
-            cid, cpr = cands[r]
+            cid, cpr = cands[r][0], cands[r][1]
+            total = cands[r][2] if len(cands[r]) > 2 else len(cid)
             n = int(gpu.cand_count[r])
-            assert n == len(cid), f"{label} row {r}: {n} candidates vs {len(cid)}"
-            m = min(n, gpu.cand_ids.shape[1])
+            assert n == total, f"{label} row {r}: {n} candidates vs {total}"
+            m = min(n, gpu.cand_ids.shape[1], len(cid))
             assert gpu.cand_ids[r, :m].tolist() == list(cid[:m]), f"{label} row {r}: candidate order"
             ref = np.asarray(cpr[:m])
             got = gpu.cand_probs[r, :m]

@@ -96,7 +96,7 @@ def test_golden_case(sampler, index):
     cc = GOLD[f"{name}/cand_count"]
     for r in range(inp["rows"]):
         n = int(cc[r])
-        cands.append((GOLD[f"{name}/cand_ids"][r, :n].tolist(), GOLD[f"{name}/cand_probs"][r, :n].tolist()))
+        cands.append((GOLD[f"{name}/cand_ids"][r, :n].tolist(), GOLD[f"{name}/cand_probs"][r, :n].tolist(), n))
     margins = GOLD[f"{name}/margins"].min(axis=1)
     diffs = PU.compare(gpu, GOLD[f"{name}/ids"], margins, cands, rng_after=GOLD[f"{name}/rng_state_after"], label=name)
     assert diffs <= max(1, inp["rows"] // 8)
