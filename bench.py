@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-extras", action="store_true", help="skip bf16 / latency / e2e / cpu legs")
+    ap.add_argument("--rows", type=int, default=GLOBAL_BATCH,
+                    help="global batch (default 4096 = C4); smaller values are for profiler captures")
     return ap.parse_args()
 
 
@@ -152,9 +154,9 @@ def run_ours(args, rank, world, local):
     L = pkg._lib
 
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
-    per = GLOBAL_BATCH // world
+    per = args.rows // world
     r0 = rank * per
-    wl = W.make("C4", device=dev, rows=GLOBAL_BATCH)
+    wl = W.make("C4", device=dev, rows=args.rows)
     logits = wl.logits[r0:r0 + per].to(dtype).contiguous()
     hist = wl.history[r0:r0 + per].contiguous()
     hlen = wl.history_len[r0:r0 + per].contiguous()
@@ -230,7 +232,7 @@ def run_ours(args, rank, world, local):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32" if args.dtype == "f32" else "bf16", "data": "synthetic (seeded torch Philox, C4 distributions)",
-        "config": {"workload": WORKLOAD_DESC, "global_batch": GLOBAL_BATCH, "rows_per_gpu": per, "vocab": VOCAB,
+        "config": {"workload": WORKLOAD_DESC, "global_batch": per * world, "rows_per_gpu": per, "vocab": VOCAB,
                    "logits_dtype": args.dtype, "parallelism": f"row-sharded x{world} (no collective)",
                    "l2": "inputs larger than L2 (rows x 1 MiB per GPU)"},
         "logits_gbps": total_rows * bytes_per_row * args.steps / (elapsed_ms / 1e3) / 1e9,

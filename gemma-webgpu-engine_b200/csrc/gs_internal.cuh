@@ -49,6 +49,7 @@ struct StreamArgs {
   int64_t chunk;
   int32_t kcap;           // candidate slots per unit in `cands`
   int32_t kc;             // shared-memory candidate buffer entries (power of two)
+  int32_t kmax;           // largest k_eff of the batch
   const RowPlan* plans;   // per-row plans or nullptr (then plan0)
   RowPlan plan0;
   const int32_t* history;

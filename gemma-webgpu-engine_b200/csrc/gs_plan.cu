@@ -9,6 +9,9 @@
 
 namespace gs {
 
+int pipe_max_k();
+int64_t pipe_max_chunk();
+
 namespace {
 
 gs_status fmt(std::string* err, gs_status s, const char* f, ...) {
@@ -78,16 +81,34 @@ gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err) 
 gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::string* err) {
   const int rows = b->rows;
   const int kmax = ps.kmax;
-  // Vocabulary splits: enough units to fill the GPU, chunks of >= 4096 ids, and at most
+  // Vocabulary splits.  The warp-per-unit streaming kernel (small topK, aligned rows)
+  // wants about four units per warp of the GPU, chunks of 2048..65536 ids; the general
+  // kernel wants about four CTAs per SM and chunks of >= 4096 ids.  Both keep at most
   // 16384 streamed candidates per row for the merge.
   const int64_t V = b->vocab;
-  const int target_units = 148 * 4;
+  const int esz = b->dtype == GS_DTYPE_F32 ? 4 : 2;
+  const bool aligned = (reinterpret_cast<uintptr_t>(b->logits) & 15) == 0 && ((b->row_stride * esz) & 15) == 0 &&
+                       (!b->mask_table || ((reinterpret_cast<uintptr_t>(b->mask_table) & 15) == 0 && (b->mask_words & 3) == 0));
+  const bool warp_kernel = kmax <= pipe_max_k() && aligned;
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int target_units = warp_kernel ? sms * 16 * 4 : sms * 4;
+  const int64_t min_chunk = warp_kernel ? 2048 : 4096;
+  const int64_t granule = warp_kernel ? 1024 : 4096;
   int S = 1;
-  while (static_cast<int64_t>(rows) * S < target_units && V / (2 * S) >= 4096 && 2 * S * std::max(kmax, 1) <= 16384 &&
-         S < 256)
+  while (static_cast<int64_t>(rows) * S < target_units && V / (2 * S) >= min_chunk && 2 * S * std::max(kmax, 1) <= 16384 &&
+         S < 1024)
     S *= 2;
+  if (warp_kernel) {
+    const int64_t need = (V + pipe_max_chunk() - 1) / pipe_max_chunk();
+    while (S < need) S *= 2;
+  }
   int64_t chunk = (V + S - 1) / S;
-  chunk = (chunk + 1023) / 1024 * 1024;
+  chunk = (chunk + granule - 1) / granule * granule;
   S = static_cast<int>((V + chunk - 1) / chunk);
   const int kcap = std::max(kmax, 1);
   int kc = 256;
@@ -138,6 +159,7 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   sa.chunk = L.chunk;
   sa.kcap = L.kcap;
   sa.kc = L.kc;
+  sa.kmax = L.kmax;
   sa.plans = dplans;
   sa.plan0 = plan0;
   sa.history = b->history;

@@ -440,9 +440,32 @@ size_t stream_smem_bytes(int64_t chunk, int kc) {
   return nwords_pad * 4 + static_cast<size_t>(kc) * 8;
 }
 
+bool stream2_eligible(const StreamArgs& a, int dtype, int rows);
+int pipe_max_k();
+size_t stream2_smem_bytes(int64_t chunk);
+cudaError_t launch_stream2(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st, int num_sms);
+
+namespace {
+int sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = n > 0 ? n : 148;
+  }
+  return counts[dev];
+}
+}  // namespace
+
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
   const int units = rows * a.splits;
   if (units == 0) return cudaSuccess;
+  // pipelined kernel for small topK on aligned rows; the general kernel otherwise
+  if (a.kmax <= pipe_max_k() && stream2_eligible(a, dtype, rows))
+    return launch_stream2(a, dtype, rows, stream2_smem_bytes(a.chunk), st, sm_count());
   if (dtype == GS_DTYPE_F32) {
     static bool attr = false;
     if (!attr) {

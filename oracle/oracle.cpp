@@ -323,10 +323,11 @@ void oracle_mask_constraint_logits(const float* raw_logits, int64_t vocab,
 // IEEE single operations so that every compliant implementation gives the same bits.
 // The reference runtime never applies it (the Gemma manifest declares 30, the LM head
 // writes uncapped logits); the benchmark configurations apply it when making inputs.
-// Method: y = x * fl(1/c); |y| < 0.625 uses the odd polynomial y + y^3·Q(y^2) (a
-// least-squares/Lawson minimax fit, coefficients below); 0.625 <= |y| < 9 uses
-// 1 - 2/(e^{2|y|} + 1) with e^z by Cody–Waite reduction z = n·ln2 + r and a degree-6
-// polynomial for e^r; |y| >= 9 gives 1.  The result is c·copysign(t, y).
+// Method: y = x * fl(1/c), z = fl(y·y).  z < 0.390625 (exactly |y| < 0.625) uses the
+// odd polynomial evaluated on the signed y, c·fma(y·z, Q(z), y) (a least-squares/Lawson
+// minimax fit, coefficients below; a zero y gives +0); otherwise 0.625 <= |y| < 9 uses
+// t = 1 - 2/(e^{2|y|} + 1) with e^z by Cody–Waite reduction z = n·ln2 + r and a
+// degree-6 polynomial for e^r, |y| >= 9 gives t = 1, and the result is c·copysign(t, y).
 static const float kTanhQ[5] = {-0.3333328f, 0.13331442f, -0.05373972f, 0.02063909f, -0.00570499f};
 static const float kExpB[5] = {0.49999994f, 0.1666652f, 0.04166841f, 0.00836891f, 0.00138142f};
 static const float kLn2Hi = 0.693145751953125f;     // 0x3f317200
@@ -354,18 +355,18 @@ static inline float f_exp_reduced(float z) {
 float oracle_softcap(float x, float cap, float inv_cap) {
   if (x != x) return x;
   float y = x * inv_cap;
-  float a = std::fabs(y);
-  float t;
-  if (a < 0.625f) {
-    float z = a * a;
+  float z = y * y;
+  if (z < 0.390625f) {
     float q = kTanhQ[4];
     q = std::fmaf(q, z, kTanhQ[3]);
     q = std::fmaf(q, z, kTanhQ[2]);
     q = std::fmaf(q, z, kTanhQ[1]);
     q = std::fmaf(q, z, kTanhQ[0]);
-    float a3 = a * z;
-    t = std::fmaf(a3, q, a);
-  } else if (a < 9.0f) {
+    return cap * std::fmaf(y * z, q, y);
+  }
+  float a = std::fabs(y);
+  float t;
+  if (a < 9.0f) {
     float e = f_exp_reduced(a + a);
     t = 1.0f - 2.0f / (e + 1.0f);
   } else {

@@ -259,6 +259,59 @@ def test_empty_logits_and_bad_config(pkg, sampler):
                                           "repetitionWindow": 0}, lambda: 0.5)
 
 
+def _pack_words(allowed):
+    s, v = allowed.shape
+    bits = allowed.reshape(s, v // 32, 32).astype(np.uint64) << np.arange(32, dtype=np.uint64)
+    return bits.sum(axis=-1).astype(np.uint32)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("k,temp,logprob", [(1, 0.0, False), (1, 0.7, False), (50, 0.8, False), (112, 1.1, False),
+                                            (50, 0.8, True)], ids=["greedy", "topk1", "k50", "k112", "k50-logprob"])
+def test_stream_tile_modes(pkg, oracle, sampler, dtype, k, temp, logprob):
+    """Masks of graded density in one batch (tiles with few allowed ids are gathered
+    vector by vector, the others bulk-copied; a requested log-probability reads every
+    tile), unmasked rows, a history concentrated in one vocabulary chunk (more penalised
+    ids than the per-unit sorted list holds) beside spread-out histories with repeats,
+    greedy, topK 1 and the largest topK of the warp-pipelined pass."""
+    import torch
+    rng = np.random.default_rng(100 + k + (7 if logprob else 0))
+    V, rows, H = 65536, 14, 700
+    x = (rng.standard_normal((rows, V)) * 2.5).astype(np.float32)
+    if dtype == "bf16":
+        x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    dens = [0.002, 0.01, 0.03, 0.08, 0.2, 0.5, 1.0]
+    allowed = rng.random((len(dens), V)) < np.array(dens)[:, None]
+    allowed[:, 7] = True
+    table = _pack_words(allowed)
+    mstate = np.array([(i % (len(dens) + 1)) - 1 for i in range(rows)], dtype=np.int32)
+    hist = np.zeros((rows, H), dtype=np.int32)
+    hlen = np.zeros(rows, dtype=np.int32)
+    for r in range(rows):
+        if r % 3 == 0:
+            h = rng.choice(3000, H, replace=False)            # one chunk, > 256 distinct ids
+        elif r % 3 == 1:
+            h = rng.integers(0, V, H)                           # spread, with repeats
+        else:
+            h = rng.integers(0, 64, H // 2)                     # few ids, many repeats
+        hist[r, :len(h)] = h
+        hlen[r] = len(h)
+    p = {"temperature": temp, "topK": k, "topP": 0.95, "minP": 0.0, "typicalP": 1.0, "repetitionPenalty": 1.2,
+         "presencePenalty": 0.4, "frequencyPenalty": 0.2, "repetitionWindow": H}
+    u = rng.random(rows)
+    gpu = PU.run_gpu(sampler, x, [p], softcap=30.0, history=hist, history_len=hlen, mask_table=table,
+                     mask_state=mstate, uniforms=u, logprob=logprob,
+                     dtype=torch.bfloat16 if dtype == "bf16" else None)
+    ids, margins, cands, _ = PU.oracle_rows(oracle, x, V, 30.0, [p], history=hist, history_len=hlen,
+                                            mask_table=table, mask_state=mstate, uniforms=u)
+    diffs = PU.compare(gpu, ids, margins, cands, label=f"tiles-{dtype}-k{k}")
+    assert diffs <= 1
+    if logprob:
+        for r in range(rows):
+            ref = oracle.token_log_probability(oracle.softcap(x[r], 30.0), int(gpu.ids[r]))
+            assert abs(gpu.logprob[r] - ref) <= 1e-6 * max(1.0, abs(ref)), r
+
+
 def test_unaligned_row_stride(pkg, oracle, sampler):
     """Rows whose start is not 16-byte aligned take the scalar path; results unchanged."""
     import torch
