@@ -33,6 +33,8 @@ struct FinShared {
   int sel_above;
   int sel_binc;
   int fill_base;
+  int n_sort;
+  unsigned long long min_pack;
 };
 
 __device__ __forceinline__ bool mask_allows(const uint32_t* mrow, uint32_t id) {
@@ -45,10 +47,12 @@ __device__ __forceinline__ double penalise(double x, double count, double rp, do
   return __dsub_rn(v, __dadd_rn(pres, __dmul_rn(count, freq)));
 }
 
-size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap) {
+// Entries (twice: all scored entries, then those that can reach the top k), the filter
+// work arrays (work_cap each) and the history / pack scratch.
+size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap, int work_cap) {
   const size_t r1 = std::max<size_t>(static_cast<size_t>(hist_cap) * 4, static_cast<size_t>(pack_cap) * 8);
-  const size_t work = static_cast<size_t>(kMaxCand) * (4 + 8 + 8 + 8 + 4 + 4 + 1);
-  return static_cast<size_t>(ent_cap) * sizeof(Ent) + work + ((r1 + 15) & ~static_cast<size_t>(15)) + 64;
+  const size_t work = (static_cast<size_t>(work_cap) * (4 + 8 + 8 + 8 + 4 + 4 + 1) + 15) & ~static_cast<size_t>(15);
+  return 2 * static_cast<size_t>(ent_cap) * sizeof(Ent) + work + ((r1 + 15) & ~static_cast<size_t>(15)) + 64;
 }
 
 template <int DT>
@@ -65,23 +69,26 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
 
   // ---- shared memory carve-up ----
   unsigned char* p = dsm;
-  Ent* ent = reinterpret_cast<Ent*>(p);
+  Ent* ent_all = reinterpret_cast<Ent*>(p);  // every scored entry (normaliser)
   p += static_cast<size_t>(A.ent_cap) * sizeof(Ent);
+  Ent* ent = reinterpret_cast<Ent*>(p);      // those that can reach the top k, sorted
+  p += static_cast<size_t>(A.ent_cap) * sizeof(Ent);
+  const int wc = A.work_cap;
   FilterWork w;
   w.cp = reinterpret_cast<double*>(p);
-  p += kMaxCand * 8;
+  p += wc * 8;
   w.cum = reinterpret_cast<double*>(p);
-  p += kMaxCand * 8;
+  p += wc * 8;
   w.skey = reinterpret_cast<unsigned long long*>(p);
-  p += kMaxCand * 8;
+  p += wc * 8;
   w.cid = reinterpret_cast<uint32_t*>(p);
-  p += kMaxCand * 4;
+  p += wc * 4;
   w.sval = reinterpret_cast<uint32_t*>(p);
-  p += kMaxCand * 4;
+  p += wc * 4;
   w.pos = reinterpret_cast<int*>(p);
-  p += kMaxCand * 4;
+  p += wc * 4;
   w.flg = p;
-  p += kMaxCand;
+  p += wc;
   p = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~static_cast<uintptr_t>(15));
   unsigned char* r1 = p;
   w.red_d = F.red_d;
@@ -119,6 +126,8 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
     F.n_allowed = na;
     F.n_c = nc;
     F.n_ent = 0;
+    F.n_sort = 0;
+    F.min_pack = ~0ull;
     F.raw_m = rm;
     F.raw_s = rs;
   }
@@ -137,20 +146,24 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
       __syncthreads();
       bitonic_sort_u32(hs, h2);
       const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
+      // entry i belongs to sorted history position i (a fixed slot, so the normaliser's
+      // summation order does not depend on thread timing); unused slots have kind ~0
       for (int i = tid; i < hl; i += bs) {
         const uint32_t v = hs[i];
-        if (v >= static_cast<uint64_t>(A.vocab)) continue;  // negative ids are >= 2^31 here
-        if (i > 0 && hs[i - 1] == v) continue;
-        int cnt = 1;
-        while (i + cnt < hl && hs[i + cnt] == v) ++cnt;
-        if (has_mask && !mask_allows(mrow, v)) continue;  // masked: -inf either way
-        float x = load_logit(rowbase, DT, v);
-        if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
-        if (!(x < INFINITY)) atomicOr(&F.flags, GS_FLAG_ERR_NONFINITE);  // NaN or +inf
-        const double xp = penalise(static_cast<double>(x), static_cast<double>(cnt), rp, pres, freq);
-        const int slot = atomicAdd(&F.n_ent, 1);
-        ent[slot] = Ent{greedy ? xp : __ddiv_rn(xp, T), v, 1u};
+        Ent e{-INFINITY, 0xffffffffu, 0xffffffffu};
+        const bool first = v < static_cast<uint64_t>(A.vocab) && !(i > 0 && hs[i - 1] == v);  // negative ids are >= 2^31
+        if (first && !(has_mask && !mask_allows(mrow, v))) {  // masked: -inf either way
+          int cnt = 1;
+          while (i + cnt < hl && hs[i + cnt] == v) ++cnt;
+          float x = load_logit(rowbase, DT, v);
+          if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
+          if (!(x < INFINITY)) atomicOr(&F.flags, GS_FLAG_ERR_NONFINITE);  // NaN or +inf
+          const double xp = penalise(static_cast<double>(x), static_cast<double>(cnt), rp, pres, freq);
+          e = Ent{greedy ? xp : __ddiv_rn(xp, T), v, 1u};
+        }
+        ent_all[i] = e;
       }
+      if (tid == 0) F.n_ent = static_cast<int>(hl);
     }
     __syncthreads();
   }
@@ -159,11 +172,13 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
   const int k = greedy ? 1 : pp->k_eff;
   if (!(F.flags & GS_FLAG_ERRORS)) {
     const int nc = F.n_c;
+    unsigned long long my_min = ~0ull;  // smallest unit pack this thread adds
     auto add_pack = [&](unsigned long long v) {
       const float x = pack_value(v);
       const uint32_t id = pack_id(v);
       const int slot = atomicAdd(&F.n_ent, 1);
-      ent[slot] = Ent{greedy ? static_cast<double>(x) : __ddiv_rn(static_cast<double>(x), T), id, 0u};
+      ent_all[slot] = Ent{greedy ? static_cast<double>(x) : __ddiv_rn(static_cast<double>(x), T), id, 0u};
+      my_min = v < my_min ? v : my_min;
     };
     if (nc > k) {
       unsigned long long* buf = reinterpret_cast<unsigned long long*>(r1);
@@ -187,14 +202,28 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
         if (j < A.stats[unit].n_cand) add_pack(A.cands[unit * A.kcap + j]);
       }
     }
+    if (my_min != ~0ull) atomicMin(&F.min_pack, my_min);
     __syncthreads();
   }
 
-  // ---- 3. exact order ----
-  const int n_ent = F.n_ent;
+  // ---- 3. exact order of the entries that can reach the top k ----
+  // With k streamed candidates kept, an entry below the k-th of them has at least k
+  // entries before it; only the others are sorted (all still count in the normaliser).
+  const int n_all = F.n_ent;
   if (!(F.flags & GS_FLAG_ERRORS)) {
-    const int n2 = pow2_ceil(n_ent > 0 ? n_ent : 1);
-    for (int i = n_ent + tid; i < n2; i += bs) ent[i] = Ent{-INFINITY, 0xffffffffu, 0xffffffffu};
+    double thr = -INFINITY;
+    if (F.n_c >= k && F.min_pack != ~0ull) {
+      const double x = static_cast<double>(pack_value(F.min_pack));
+      thr = greedy ? x : __ddiv_rn(x, T);
+    }
+    for (int i = tid; i < n_all; i += bs) {
+      const Ent e = ent_all[i];
+      if (e.kind != 0xffffffffu && e.key >= thr) ent[atomicAdd(&F.n_sort, 1)] = e;
+    }
+    __syncthreads();
+    const int ns = F.n_sort;
+    const int n2 = pow2_ceil(ns > 0 ? ns : 1);
+    for (int i = ns + tid; i < n2; i += bs) ent[i] = Ent{-INFINITY, 0xffffffffu, 0xffffffffu};
     __syncthreads();
     bitonic_sort_ent(ent, n2);
   }
@@ -202,6 +231,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
   uint32_t tok = 0xffffffffu;
   int n_final = 0;
   if (!(F.flags & GS_FLAG_ERRORS)) {
+    const int n_ent = F.n_sort;
     if (greedy) {
       // argmax over the whole vocabulary: all -inf -> id 0 (sampling.ts:92-96)
       if (n_ent == 0 || ent[0].key == -INFINITY) {
@@ -259,7 +289,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
           while (j0 < n_ent && ent[j0].key > -INFINITY) ++j0;
           int a = j0, b = 0, o = j0;
           // ent[j0, n_ent) are -inf entries sorted by id; merge into w.cum..w.skey
-          // (2·kMaxCand·8 bytes = kMaxCand entries, unused at this point)
+          // (2·work_cap·8 bytes = work_cap entries, unused at this point)
           Ent* tail = reinterpret_cast<Ent*>(w.cum);
           int t = 0;
           while (o < K && (a < n_ent || b < n_masked)) {
@@ -287,8 +317,8 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
           if (st.m > -INFINITY)
             part = __dadd_rn(part, __dmul_rn(st.s, exp(__dsub_rn(__ddiv_rn(static_cast<double>(st.m), T), M))));
         }
-        for (int i = tid; i < n_ent; i += bs)
-          if (ent[i].kind == 1u) part = __dadd_rn(part, exp(__dsub_rn(ent[i].key, M)));
+        for (int i = tid; i < n_all; i += bs)
+          if (ent_all[i].kind == 1u) part = __dadd_rn(part, exp(__dsub_rn(ent_all[i].key, M)));
         const double total = block_sum_d(part, F.red_d);
         for (int i = tid; i < nC; i += bs) {
           w.cid[i] = ent[i].id;
@@ -342,18 +372,14 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
 cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   if (dtype == GS_DTYPE_F32) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      attr = true;
-    }
+    const cudaError_t e = cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
     finalize_kernel<GS_DTYPE_F32><<<rows, kFinalizeThreads, smem, st>>>(a);
   } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      attr = true;
-    }
+    const cudaError_t e = cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
     finalize_kernel<GS_DTYPE_BF16><<<rows, kFinalizeThreads, smem, st>>>(a);
   }
   return cudaGetLastError();

@@ -75,6 +75,7 @@ struct FinalizeArgs {
   int32_t hist_cap;       // power-of-two shared buffer for the sorted history
   int32_t ent_cap;        // power-of-two shared buffer for candidate entries
   int32_t pack_cap;       // shared buffer for unit packs (0 when units already hold <= k)
+  int32_t work_cap;       // entries of the filter work arrays (power of two >= the batch's topK)
   const RowPlan* plans;
   RowPlan plan0;
   const int32_t* history;
@@ -101,7 +102,7 @@ struct FinalizeArgs {
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
 size_t stream_smem_bytes(int64_t chunk, int kc);
 cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
-size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap);
+size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap, int work_cap);
 cudaError_t launch_large(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
 size_t large_smem_bytes(int64_t vocab, int hist_cap);
 cudaError_t launch_logprob(const void* logits, int dtype, int rows, int64_t vocab, int64_t stride,

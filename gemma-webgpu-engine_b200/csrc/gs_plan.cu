@@ -132,7 +132,8 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   L->hist_cap = pow2ceil(std::max<int64_t>(hs, 1));
   L->pack_cap = S > 1 ? S * kcap : 0;
   L->ent_cap = pow2ceil(std::max<int64_t>(std::min<int64_t>(static_cast<int64_t>(S) * kcap, kmax) + hs, 1));
-  L->fin_smem = finalize_smem_bytes(L->hist_cap, L->ent_cap, L->pack_cap);
+  L->work_cap = std::min(pow2ceil(std::max(kmax, 1)), 1024);
+  L->fin_smem = finalize_smem_bytes(L->hist_cap, L->ent_cap, L->pack_cap, L->work_cap);
   if (L->fin_smem > 220 * 1024)
     return fmt(err, GS_EUNSUPPORTED, "merge needs %zu bytes of shared memory (topK %d, history %lld)", L->fin_smem, kmax,
                static_cast<long long>(hs));
@@ -188,6 +189,7 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   fa.hist_cap = L.hist_cap;
   fa.ent_cap = L.ent_cap;
   fa.pack_cap = L.pack_cap;
+  fa.work_cap = L.work_cap;
   fa.plans = dplans;
   fa.plan0 = plan0;
   fa.history = sa.history;

@@ -61,7 +61,7 @@ struct Layout {
   bool any_sample;
   size_t plans_off, stats_off, cands_off, total;
   size_t stream_smem, fin_smem, large_smem;
-  int hist_cap, ent_cap, pack_cap;
+  int hist_cap, ent_cap, pack_cap, work_cap;
 };
 
 // Summary of the rows' plans that the layout depends on.

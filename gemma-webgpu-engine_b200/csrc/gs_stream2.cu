@@ -45,6 +45,7 @@ constexpr int kStageBytes = kTileBytes + kMaskBytes;
 constexpr int kPenCap = 256;                   // sorted penalised ids per unit (else scan mode)
 constexpr int kWarpCand = 256;                 // per-warp candidate buffer
 constexpr int kListCap = 128;                  // gather mode: live offsets per batch
+constexpr int kGatherIds = kTileBytes * 8;     // gather mode: ids per stage (2 KB of mask words)
 constexpr int kWarpBytes = kStages * kStageBytes + kPenCap * 4 + kWarpCand * 8 + 256 * 4 + kListCap * 4;
 constexpr int kPipeMaxK = 112;
 
@@ -265,13 +266,15 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
   constexpr int VE = LD::kVec;                 // ids per 16-byte vector
   constexpr int ESZ = DT == GS_DTYPE_F32 ? 4 : 2;
   constexpr int TE = kTileBytes / ESZ;         // ids per tile
-  constexpr int VPL = TE / VE / 32;            // vectors per lane per tile
+  constexpr int NSUB = TE / 512;               // sub-tiles of 512 ids per tile
+  constexpr int VPS = 512 / VE / 32;           // vectors per lane per sub-tile
   constexpr uint32_t kFull = (1u << VE) - 1u;
   constexpr int kPer = kListCap / 32;          // gather mode: values per lane per batch
-  static_assert(VPL * VE <= 32, "candidate bits of a lane fit one word");
+  static_assert(VPS * VE == 16 && NSUB <= 2, "candidate bits of a lane fit one word");
   static_assert(TE / 32 <= 32 && TE / 32 * 4 <= kMaskBytes, "mask words of a tile: one per lane");
   extern __shared__ __align__(128) unsigned char dsm[];
   __shared__ unsigned long long bars_s[kWarps][kStages];
+  __shared__ unsigned char smode[kWarps][kStages];  // 1: the stage holds a gather-mode mask tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_warps = gridDim.x * kWarps;
@@ -292,22 +295,26 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
   __syncwarp();
 
-  // ---- producer: a cursor over the warp's ring tiles (gather-mode units are skipped) ----
-  int c_unit = first_unit, c_tile = 0;
+  // ---- producer: a cursor over the warp's stages, one refill per consumed stage ----
+  // A ring-mode unit is a sequence of logit tiles; a gather-mode unit is a sequence of
+  // mask tiles (its constraint words, kGatherIds ids per stage).  The stage's mode byte
+  // tells the consumer which (every unit has at least one stage).
+  int c_unit = first_unit, c_tile = 0, c_ntiles = 0;
+  bool c_gather = false;
   Geom cg;
-  auto enter_unit = [&]() {  // from c_unit: the first ring-mode unit at or after it
+  auto enter_unit = [&]() {
     c_tile = 0;
-    while (c_unit < n_units) {
+    if (c_unit < n_units) {
       cg = geom(A, c_unit, TE);
-      if (!gather_mode(A, cg, lane)) break;
-      c_unit += total_warps;
+      c_gather = gather_mode(A, cg, lane);
+      c_ntiles = c_gather ? (cg.n + kGatherIds - 1) / kGatherIds : cg.ntiles;
     }
   };
   enter_unit();
-  uint32_t c_word = 0xffffffffu;  // this lane's mask word of the cursor tile, loaded ahead
+  uint32_t c_word = 0xffffffffu;  // ring tiles of masked units: this lane's mask word, loaded ahead
   auto load_word = [&]() {
     c_word = 0xffffffffu;
-    if (c_unit < n_units && cg.masked) {
+    if (c_unit < n_units && cg.masked && !c_gather) {
       const int t0 = c_tile * TE;
       const int cnt = cg.n - t0 < TE ? cg.n - t0 : TE;
       if (lane < ((cnt + 31) >> 5))
@@ -320,22 +327,38 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     if (c_unit >= n_units) return;  // warp-uniform
     const int s = static_cast<int>(issued & (kStages - 1));
     unsigned char* st = ring + s * kStageBytes;
-    uint32_t* smw = reinterpret_cast<uint32_t*>(st + kTileBytes);
-    const int t0 = c_tile * TE;
-    const int cnt = cg.n - t0 < TE ? cg.n - t0 : TE;
-    const int words = (cnt + 31) >> 5;
-    uint32_t w = c_word;
-    if (lane == words - 1 && (cnt & 31)) w &= (1u << (cnt & 31)) - 1u;
-    if (lane < words) smw[lane] = w;
-    if (lane == 0) {
-      const unsigned char* src = logits + (static_cast<int64_t>(cg.row) * A.row_stride + cg.lo + t0) * ESZ;
-      const uint32_t bytes = static_cast<uint32_t>(cnt / VE) * 16u;  // whole 16-byte vectors
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_expect_tx(bars + s, bytes);
-      if (bytes) bulk_g2s(st, src, bytes, bars + s);
+    if (c_gather) {
+      if (lane == 0) {
+        const int nwords = (cg.n + 31) >> 5;
+        const int w0 = c_tile * (kGatherIds / 32);
+        const int wn = nwords - w0 < kGatherIds / 32 ? nwords - w0 : kGatherIds / 32;
+        // (rounding up to 16 bytes stays inside the mask row: mask_words % 4 == 0)
+        const uint32_t bytes = (static_cast<uint32_t>(wn) * 4u + 15u) & ~15u;
+        const uint32_t* src = A.mask_table + static_cast<int64_t>(cg.state) * A.mask_words + (cg.lo >> 5) + w0;
+        smode[warp][s] = 1;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bars + s, bytes);
+        bulk_g2s(st, src, bytes, bars + s);
+      }
+    } else {
+      uint32_t* smw = reinterpret_cast<uint32_t*>(st + kTileBytes);
+      const int t0 = c_tile * TE;
+      const int cnt = cg.n - t0 < TE ? cg.n - t0 : TE;
+      const int words = (cnt + 31) >> 5;
+      uint32_t w = c_word;
+      if (lane == words - 1 && (cnt & 31)) w &= (1u << (cnt & 31)) - 1u;
+      if (lane < words) smw[lane] = w;
+      if (lane == 0) {
+        const unsigned char* src = logits + (static_cast<int64_t>(cg.row) * A.row_stride + cg.lo + t0) * ESZ;
+        const uint32_t bytes = static_cast<uint32_t>(cnt / VE) * 16u;  // whole 16-byte vectors
+        smode[warp][s] = 0;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bars + s, bytes);
+        if (bytes) bulk_g2s(st, src, bytes, bars + s);
+      }
     }
     ++issued;
-    if (++c_tile >= cg.ntiles) {
+    if (++c_tile >= c_ntiles) {
       c_unit += total_warps;
       enter_unit();
     }
@@ -433,162 +456,166 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     };
 
     // ================================ ring mode ================================
-    // Full tile, straight-line over the lane's VPL vectors.  Returns the candidate bits
-    // (bit j*VE+i: live value at or above the running threshold).
+    // Full tile, as NSUB sub-tiles of 512 ids, each straight-line over the lane's VPS
+    // vectors.  Returns the candidate bits (bit sub*16 + j*VE + i: live value at or above
+    // the running threshold).
     auto dense_tile = [&](auto masked_tag, const unsigned char* st, const uint32_t* smw, int t, int t0) -> uint32_t {
       constexpr bool MASKED = decltype(masked_tag)::value;
-      float x[VPL][VE];
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) LD::vec(st + (j * 32 + lane) * 16, x[j]);
-      if (cap != 0.0f) {
-        float zm = 0.0f;
-#pragma unroll
-        for (int j = 0; j < VPL; ++j)
-#pragma unroll
-          for (int i = 0; i < VE; i += 2) {
-            float2 z;
-            const float2 c = softcap2_poly(make_float2(x[j][i], x[j][i + 1]), cap, inv_cap, &z);
-            x[j][i] = c.x;
-            x[j][i + 1] = c.y;
-            zm = fmaxf(zm, fmaxf(z.x, z.y));  // (NaN inputs stay NaN through the polynomial)
-          }
-        if (!(zm < kSoftcapPolyZ)) {
-          // rare: values outside the polynomial range take the full routine
-#pragma unroll
-          for (int j = 0; j < VPL; ++j) {
-            float r[VE];
-            LD::vec(st + (j * 32 + lane) * 16, r);
-#pragma unroll
-            for (int i = 0; i < VE; ++i) {
-              const float y = __fmul_rn(r[i], inv_cap);
-              if (!(__fmul_rn(y, y) < kSoftcapPolyZ)) x[j][i] = softcap_slow(r[i], cap, inv_cap);
-            }
-          }
-        }
-      }
-      uint32_t bu[VPL];
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        if constexpr (MASKED) {
-          const int e = (j * 32 + lane) * VE;
-          bu[j] = (smw[e >> 5] >> (e & 31)) & kFull;
-#pragma unroll
-          for (int i = 0; i < VE; ++i)
-            if (!((bu[j] >> i) & 1u)) x[j][i] = -INFINITY;
-        } else {
-          bu[j] = kFull;
-        }
-      }
-      float vmx[VPL];
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        float v = x[j][0];
-#pragma unroll
-        for (int i = 1; i < VE; ++i) v = fmaxf(v, x[j][i]);
-        vmx[j] = v;
-        tmax = fmaxf(tmax, v);
-      }
       uint32_t cm = 0;
-      if (k_eff == 1) {
-        if (tmax > bx || (bp == 0ull && tmax == tmax)) {
-          // first live position of the lane's tile maximum (ids ascend with (j, i))
-          int fj = -1, fi = 0;
-#pragma unroll
-          for (int j = VPL - 1; j >= 0; --j)
-#pragma unroll
-            for (int i = VE - 1; i >= 0; --i)
-              if (((bu[j] >> i) & 1u) && x[j][i] == tmax) {
-                fj = j;
-                fi = i;
-              }
-          if (fj >= 0) {
-            bx = tmax;
-            bp = make_pack(tmax, id_base + static_cast<uint32_t>(t0 + (fj * 32 + lane) * VE + fi));
-          }
-        }
-      } else if (k_eff > 1) {
-        if (t == 0) {
-          // Threshold from the unit's first tile: the largest key K found by a binary
-          // search such that at least k live values of the tile are >= value(K).  Those
-          // values belong to the unit, so its k-th largest is >= value(K).
-          int nlv = TE;
-          if constexpr (MASKED) {
-            int c = 0;
-#pragma unroll
-            for (int j = 0; j < VPL; ++j) c += __popc(bu[j]);
-            nlv = static_cast<int>(__reduce_add_sync(kFullMask, static_cast<unsigned>(c)));
-          }
-          if (nlv >= k_eff) {
-            const uint32_t kneg = key32(-INFINITY);
-            uint32_t klo = kneg, khi = key32(warp_max(tmax)) + 1u;
 #pragma unroll 1
-            for (int it = 0; it < 14 && khi - klo > 1u; ++it) {
-              const uint32_t mid = klo + ((khi - klo) >> 1);
-              const float v = key32_value(mid);  // > -inf: dead (-inf) and NaN values never count
-              int c = 0;
+      for (int sub = 0; sub < NSUB; ++sub) {
+        float x[VPS][VE];
 #pragma unroll
-              for (int j = 0; j < VPL; ++j)
+        for (int j = 0; j < VPS; ++j) LD::vec(st + ((sub * VPS + j) * 32 + lane) * 16, x[j]);
+        if (cap != 0.0f) {
+          float zm = 0.0f;
 #pragma unroll
-                for (int i = 0; i < VE; ++i) c += x[j][i] >= v ? 1 : 0;
-              c = static_cast<int>(__reduce_add_sync(kFullMask, static_cast<unsigned>(c)));
-              if (c >= k_eff) {
-                klo = mid;
-              } else {
-                khi = mid;
-              }
-            }
-            if (klo != kneg) {
-              // pack > t0b  <=>  key >= klo
-              const unsigned long long t0b = (static_cast<unsigned long long>(klo) << 32) - 1ull;
-              wtau = t0b > wtau ? t0b : wtau;
-            }
-          }
-        }
-        const float tau_x = tau_value();
-        bool any = false;
-#pragma unroll
-        for (int j = 0; j < VPL; ++j) any |= vmx[j] >= tau_x;
-        if (any) {
-#pragma unroll
-          for (int j = 0; j < VPL; ++j)
-            if (vmx[j] >= tau_x) {
-#pragma unroll
-              for (int i = 0; i < VE; ++i)
-                if (((bu[j] >> i) & 1u) && x[j][i] >= tau_x) cm |= 1u << (j * VE + i);
-            }
-        }
-      }
-      if (do_sum) {
-        rescale(warp_max(tmax));
-        if (m_t > -INFINITY) {
-          // NaN and +inf reach the sum (as NaN); dead ids are -inf and add 0
-          float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-          const float2 nm = make_float2(-m_t, -m_t);
-          const float2 ah = make_float2(a2_hi, a2_hi), al = make_float2(a2_lo, a2_lo);
-#pragma unroll
-          for (int j = 0; j < VPL; ++j)
+          for (int j = 0; j < VPS; ++j)
 #pragma unroll
             for (int i = 0; i < VE; i += 2) {
-              const float2 d = __fadd2_rn(make_float2(x[j][i], x[j][i + 1]), nm);
-              const float2 tt = __ffma2_rn(d, al, __fmul2_rn(d, ah));
-              const float2 e = make_float2(ex2_approx(tt.x), ex2_approx(tt.y));
-              if ((j * VE + i) & 2) {
-                acc1 = __fadd2_rn(acc1, e);
-              } else {
-                acc0 = __fadd2_rn(acc0, e);
+              float2 z;
+              const float2 c = softcap2_poly(make_float2(x[j][i], x[j][i + 1]), cap, inv_cap, &z);
+              x[j][i] = c.x;
+              x[j][i + 1] = c.y;
+              zm = fmaxf(zm, fmaxf(z.x, z.y));  // (NaN inputs stay NaN through the polynomial)
+            }
+          if (!(zm < kSoftcapPolyZ)) {
+            // rare: values outside the polynomial range take the full routine
+#pragma unroll
+            for (int j = 0; j < VPS; ++j) {
+              float r[VE];
+              LD::vec(st + ((sub * VPS + j) * 32 + lane) * 16, r);
+#pragma unroll
+              for (int i = 0; i < VE; ++i) {
+                const float y = __fmul_rn(r[i], inv_cap);
+                if (!(__fmul_rn(y, y) < kSoftcapPolyZ)) x[j][i] = softcap_slow(r[i], cap, inv_cap);
               }
             }
-          s_t += static_cast<double>((acc0.x + acc0.y) + (acc1.x + acc1.y));
+          }
         }
-      }
-      if (!do_sum || !(m_t > -INFINITY)) {
-        // no sum to carry a NaN: look for one explicitly
+        uint32_t bu[VPS];
 #pragma unroll
-        for (int j = 0; j < VPL; ++j)
+        for (int j = 0; j < VPS; ++j) {
+          if constexpr (MASKED) {
+            const int e = ((sub * VPS + j) * 32 + lane) * VE;
+            bu[j] = (smw[e >> 5] >> (e & 31)) & kFull;
 #pragma unroll
-          for (int i = 0; i < VE; ++i)
-            if (x[j][i] != x[j][i]) bad = 1u;  // (dead ids are -inf)
+            for (int i = 0; i < VE; ++i)
+              if (!((bu[j] >> i) & 1u)) x[j][i] = -INFINITY;
+          } else {
+            bu[j] = kFull;
+          }
+        }
+        float vmx[VPS];
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < VPS; ++j) {
+          float v = x[j][0];
+#pragma unroll
+          for (int i = 1; i < VE; ++i) v = fmaxf(v, x[j][i]);
+          vmx[j] = v;
+          tmax = fmaxf(tmax, v);
+        }
+        if (k_eff == 1) {
+          if (tmax > bx || (bp == 0ull && tmax == tmax)) {
+            // first live position of the lane's maximum (ids ascend with (j, i))
+            int fj = -1, fi = 0;
+#pragma unroll
+            for (int j = VPS - 1; j >= 0; --j)
+#pragma unroll
+              for (int i = VE - 1; i >= 0; --i)
+                if (((bu[j] >> i) & 1u) && x[j][i] == tmax) {
+                  fj = j;
+                  fi = i;
+                }
+            if (fj >= 0) {
+              bx = tmax;
+              bp = make_pack(tmax, id_base + static_cast<uint32_t>(t0 + ((sub * VPS + fj) * 32 + lane) * VE + fi));
+            }
+          }
+        } else if (k_eff > 1) {
+          if (t == 0 && sub == 0) {
+            // Threshold from the unit's first 512 ids: the largest key K found by a
+            // binary search such that at least k live values there are >= value(K).
+            // Those values belong to the unit, so its k-th largest is >= value(K).
+            int nlv = 512;
+            if constexpr (MASKED) {
+              int c = 0;
+#pragma unroll
+              for (int j = 0; j < VPS; ++j) c += __popc(bu[j]);
+              nlv = static_cast<int>(__reduce_add_sync(kFullMask, static_cast<unsigned>(c)));
+            }
+            if (nlv >= k_eff) {
+              const uint32_t kneg = key32(-INFINITY);
+              uint32_t klo = kneg, khi = key32(warp_max(tmax)) + 1u;
+#pragma unroll 1
+              for (int it = 0; it < 14 && khi - klo > 1u; ++it) {
+                const uint32_t mid = klo + ((khi - klo) >> 1);
+                const float v = key32_value(mid);  // > -inf: dead (-inf) and NaN values never count
+                int c = 0;
+#pragma unroll
+                for (int j = 0; j < VPS; ++j)
+#pragma unroll
+                  for (int i = 0; i < VE; ++i) c += x[j][i] >= v ? 1 : 0;
+                c = static_cast<int>(__reduce_add_sync(kFullMask, static_cast<unsigned>(c)));
+                if (c >= k_eff) {
+                  klo = mid;
+                } else {
+                  khi = mid;
+                }
+              }
+              if (klo != kneg) {
+                // pack > t0b  <=>  key >= klo
+                const unsigned long long t0b = (static_cast<unsigned long long>(klo) << 32) - 1ull;
+                wtau = t0b > wtau ? t0b : wtau;
+              }
+            }
+          }
+          const float tau_x = tau_value();
+          bool any = false;
+#pragma unroll
+          for (int j = 0; j < VPS; ++j) any |= vmx[j] >= tau_x;
+          if (any) {
+#pragma unroll
+            for (int j = 0; j < VPS; ++j)
+              if (vmx[j] >= tau_x) {
+#pragma unroll
+                for (int i = 0; i < VE; ++i)
+                  if (((bu[j] >> i) & 1u) && x[j][i] >= tau_x) cm |= 1u << (sub * 16 + j * VE + i);
+              }
+          }
+        }
+        if (do_sum) {
+          rescale(warp_max(tmax));
+          if (m_t > -INFINITY) {
+            // NaN and +inf reach the sum (as NaN); dead ids are -inf and add 0
+            float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+            const float2 nm = make_float2(-m_t, -m_t);
+            const float2 ah = make_float2(a2_hi, a2_hi), al = make_float2(a2_lo, a2_lo);
+#pragma unroll
+            for (int j = 0; j < VPS; ++j)
+#pragma unroll
+              for (int i = 0; i < VE; i += 2) {
+                const float2 d = __fadd2_rn(make_float2(x[j][i], x[j][i + 1]), nm);
+                const float2 tt = __ffma2_rn(d, al, __fmul2_rn(d, ah));
+                const float2 e = make_float2(ex2_approx(tt.x), ex2_approx(tt.y));
+                if ((j * VE + i) & 2) {
+                  acc1 = __fadd2_rn(acc1, e);
+                } else {
+                  acc0 = __fadd2_rn(acc0, e);
+                }
+              }
+            s_t += static_cast<double>((acc0.x + acc0.y) + (acc1.x + acc1.y));
+          }
+        }
+        if (!do_sum || !(m_t > -INFINITY)) {
+          // no sum to carry a NaN: look for one explicitly
+#pragma unroll
+          for (int j = 0; j < VPS; ++j)
+#pragma unroll
+            for (int i = 0; i < VE; ++i)
+              if (x[j][i] != x[j][i]) bad = 1u;  // (dead ids are -inf)
+        }
       }
       return cm;
     };
@@ -670,44 +697,78 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     };
 
     // ================================ gather mode ================================
-    int nl = 0;  // live offsets listed, not yet processed
-    // Processes the listed offsets: four independent loads per lane, then the values.
-    auto flush = [&]() {
+    // Live offsets are listed in order (a warp scan gives each lane its ranks); a full
+    // list's loads are issued at once (kPer per lane) and its values processed only when
+    // the next list is full, so the loads are in flight while mask words are scanned.
+    int nl = 0;               // offsets listed
+    bool inflight = false;    // a launched batch awaits processing
+    float pv[kPer];           // its values (loads in flight) ...
+    uint32_t po[kPer];        // ... and unit offsets (~0u: empty slot)
+    auto launch = [&]() {
       __syncwarp();
-      float xv[kPer];
-      uint32_t ov[kPer];
 #pragma unroll
       for (int q = 0; q < kPer; ++q) {
         const int i = q * 32 + lane;
-        ov[q] = i < nl ? loffs[i] : 0xffffffffu;
+        po[q] = i < nl ? loffs[i] : 0xffffffffu;
       }
+      __syncwarp();  // the list may be refilled from here on
 #pragma unroll
-      for (int q = 0; q < kPer; ++q) xv[q] = ov[q] != 0xffffffffu ? LD::global(rowp, ov[q]) : -INFINITY;
+      for (int q = 0; q < kPer; ++q) pv[q] = po[q] != 0xffffffffu ? LD::global(rowp, po[q]) : 0.0f;
+      inflight = true;
+      nl = 0;
+    };
+    auto finish = [&]() {
+      float xv[kPer];
+      if (cap != 0.0f) {
+        float zm = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kPer; q += 2) {
+          float2 z;
+          const float2 c = softcap2_poly(make_float2(pv[q], pv[q + 1]), cap, inv_cap, &z);
+          xv[q] = c.x;
+          xv[q + 1] = c.y;
+          zm = fmaxf(zm, fmaxf(z.x, z.y));
+        }
+        if (!(zm < kSoftcapPolyZ)) {
+#pragma unroll
+          for (int q = 0; q < kPer; ++q) {
+            const float y = __fmul_rn(pv[q], inv_cap);
+            if (!(__fmul_rn(y, y) < kSoftcapPolyZ)) xv[q] = softcap_slow(pv[q], cap, inv_cap);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) xv[q] = pv[q];
+      }
       float lmax = -INFINITY;
 #pragma unroll
-      for (int q = 0; q < kPer; ++q)
-        if (ov[q] != 0xffffffffu) {
-          if (cap != 0.0f) xv[q] = softcap(xv[q], cap, inv_cap);
-          if (xv[q] != xv[q]) bad = 1u;
-          lmax = fmaxf(lmax, xv[q]);
-        }
+      for (int q = 0; q < kPer; ++q) {
+        if (po[q] == 0xffffffffu) xv[q] = -INFINITY;
+        if (xv[q] != xv[q]) bad = 1u;
+        lmax = fmaxf(lmax, xv[q]);
+      }
       if (do_sum) {
         rescale(warp_max(lmax));
         if (m_t > -INFINITY) {
-          float acc = 0.0f;
+          float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll
           for (int q = 0; q < kPer; ++q) {
-            const float d = xv[q] - m_t;  // (unused slots are -inf and add 0)
-            acc += ex2_approx(fmaf(d, a2_lo, d * a2_hi));
+            const float d = xv[q] - m_t;  // (empty slots are -inf and add 0)
+            const float e = ex2_approx(fmaf(d, a2_lo, d * a2_hi));
+            if (q & 1) {
+              acc1 += e;
+            } else {
+              acc0 += e;
+            }
           }
-          s_t += static_cast<double>(acc);
+          s_t += static_cast<double>(acc0 + acc1);
         }
       }
       if (k_eff == 1) {
 #pragma unroll
         for (int q = 0; q < kPer; ++q)
-          if (ov[q] != 0xffffffffu && xv[q] == xv[q]) {
-            const unsigned long long pk = make_pack(xv[q], id_base + ov[q]);
+          if (po[q] != 0xffffffffu && xv[q] == xv[q]) {
+            const unsigned long long pk = make_pack(xv[q], id_base + po[q]);
             if (pk > bp) {
               bp = pk;
               bx = xv[q];
@@ -717,54 +778,91 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
 #pragma unroll
         for (int q = 0; q < kPer; ++q) {
           const float tau_x = tau_value();
-          bool pend = ov[q] != 0xffffffffu && xv[q] >= tau_x;
-          const unsigned long long pk = pend ? make_pack(xv[q], id_base + ov[q]) : 0ull;
+          bool pend = po[q] != 0xffffffffu && xv[q] >= tau_x;
+          const unsigned long long pk = pend ? make_pack(xv[q], id_base + po[q]) : 0ull;
           while (__any_sync(kFullMask, pend)) pend = !offer(pend, pk);
         }
       }
-      nl = 0;
-      __syncwarp();
+      inflight = false;
     };
-    auto gather_unit = [&]() {
-      const uint32_t* mrow = A.mask_table + static_cast<int64_t>(g.state) * A.mask_words + (g.lo >> 5);
-      const int nwords = (g.n + 31) >> 5;
-      const int ngroups = (nwords + 31) >> 5;
-      uint32_t wn = lane < nwords ? __ldg(mrow + lane) : 0u;
-      for (int c = 0; c < ngroups; ++c) {
-        const int wi = c * 32 + lane;
-        uint32_t w = wn;
-        if (c + 1 < ngroups) wn = wi + 32 < nwords ? __ldg(mrow + wi + 32) : 0u;  // next group ahead
-        if (wi == nwords - 1 && (g.n & 31)) w &= (1u << (g.n & 31)) - 1u;
-        na += __popc(w);
-        // clear the penalised ids of the group
-        if (pen_scan) {
-          for (int64_t j = 0; j < hl; ++j) {
-            const int64_t off = static_cast<int64_t>(hrow[j]) - A.vocab_offset - g.lo;
-            if ((off >> 5) == wi) w &= ~(1u << (off & 31));
-          }
-        } else {
-          const uint32_t gend = static_cast<uint32_t>(c + 1) * 1024u;
-          while (pen_cur < pen_n && pen[pen_cur] < gend) {  // warp-uniform
-            const uint32_t off = pen[pen_cur];
-            if (static_cast<int>(off >> 5) == wi) w &= ~(1u << (off & 31));
-            ++pen_cur;
-          }
+    // Appends the live offsets of word wi (this lane's w) in id order, launching full lists.
+    auto list_word = [&](uint32_t w, int wi) {
+      const int c = __popc(w);
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int total = __shfl_sync(kFullMask, incl, 31);
+      int r = incl - c;  // rank of this lane's next offset within the 32 words
+      int done = 0;
+      while (done < total) {  // warp-uniform
+        const int room = kListCap - nl;
+        const int hi = done + room;
+        uint32_t* dst = loffs + (nl - done);
+        while (w != 0u && r < hi) {
+          dst[r] = static_cast<uint32_t>(wi * 32 + __ffs(w) - 1);
+          w &= w - 1u;
+          ++r;
         }
-        // list the live offsets
-        while (__any_sync(kFullMask, w != 0u)) {
-          const bool has = w != 0u;
-          const uint32_t off = static_cast<uint32_t>(wi * 32 + __ffs(w) - 1);
-          if (has) w &= w - 1u;
-          const unsigned hb = __ballot_sync(kFullMask, has);
-          if (nl + __popc(hb) > kListCap) flush();
-          if (has) loffs[nl + __popc(hb & lane_lt)] = off;
-          nl += __popc(hb);
+        const int take = total - done < room ? total - done : room;
+        nl += take;
+        done += take;
+        if (nl == kListCap) {
+          if (inflight) finish();
+          launch();
         }
       }
-      if (nl > 0) flush();
+    };
+    auto gather_unit = [&]() {
+      const int nwords = (g.n + 31) >> 5;
+      const int ntl = (g.n + kGatherIds - 1) / kGatherIds;
+      for (int t = 0; t < ntl; ++t) {
+        if (!mbar_wait(bars + cs, cph, kWaitNs)) {
+          uflags |= GS_FLAG_ERR_TIMEOUT;
+          mbar_wait(bars + cs, cph, kWaitNs);
+        }
+        const uint32_t* mw = reinterpret_cast<const uint32_t*>(ring + cs * kStageBytes);
+        const int w0 = t * (kGatherIds / 32);
+        const int ngr = (nwords - w0 + 31) >> 5 < kGatherIds / 1024 ? (nwords - w0 + 31) >> 5 : kGatherIds / 1024;
+        for (int q = 0; q < ngr; ++q) {
+          const int wl = q * 32 + lane;  // word within the stage
+          const int wi = w0 + wl;        // word within the unit
+          uint32_t w = wi < nwords ? mw[wl] : 0u;
+          if (wi == nwords - 1 && (g.n & 31)) w &= (1u << (g.n & 31)) - 1u;
+          na += __popc(w);
+          // clear the penalised ids of these 32 words
+          if (pen_scan) {
+            for (int64_t j = 0; j < hl; ++j) {
+              const int64_t off = static_cast<int64_t>(hrow[j]) - A.vocab_offset - g.lo;
+              if ((off >> 5) == wi) w &= ~(1u << (off & 31));
+            }
+          } else {
+            const uint32_t gend = static_cast<uint32_t>(w0 + (q + 1) * 32) * 32u;
+            while (pen_cur < pen_n && pen[pen_cur] < gend) {  // warp-uniform
+              const uint32_t off = pen[pen_cur];
+              if (static_cast<int>(off >> 5) == wi) w &= ~(1u << (off & 31));
+              ++pen_cur;
+            }
+          }
+          list_word(w, wi);
+        }
+        // release the stage
+        __syncwarp();
+        cs = (cs + 1) & (kStages - 1);
+        if (cs == 0) cph ^= 1u;
+        produce();
+      }
+      if (inflight) finish();
+      if (nl > 0) {
+        launch();
+        finish();
+      }
     };
 
-    if (gather_mode(A, g, lane)) {
+    __syncwarp();
+    if (smode[warp][cs]) {
       gather_unit();
     } else {
       for (int t = 0; t < g.ntiles; ++t) {
@@ -822,7 +920,8 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
           unsigned long long pk = 0;
           if (has) {
             const int b = __ffs(cm) - 1;
-            const int e = ((b / VE) * 32 + lane) * VE + (b % VE);
+            const int r = b & 15;
+            const int e = (((b >> 4) * VPS + r / VE) * 32 + lane) * VE + (r % VE);
             float x = LD::one(st + e * ESZ);
             if (cap != 0.0f) x = softcap(x, cap, inv_cap);
             pk = make_pack(x, id_base + static_cast<uint32_t>(t0 + e));
