@@ -137,10 +137,10 @@ def lib() -> ctypes.CDLL:
     L.gs_build_mask_row.argtypes = [P, i64, P, i64, P, i64, P, P]
     L.gs_softcap.argtypes = [P, P, P, i64, f32, P]
     L.gs_softcap_digest.argtypes = [P, u64, u64, f32, ctypes.POINTER(u64)]
-    L.gs_shard_record_bytes.argtypes = [i32]
+    L.gs_shard_record_bytes.argtypes = [ctypes.POINTER(GsParams), i32, i64, i64]
     L.gs_shard_record_bytes.restype = i64
-    L.gs_shard_partials.argtypes = [P, ctypes.POINTER(GsBatch), i64, i64, P, P]
-    L.gs_shard_merge.argtypes = [P, ctypes.POINTER(GsBatch), i64, i32, P, ctypes.POINTER(GsOutputs), P]
+    L.gs_shard_partials.argtypes = [P, ctypes.POINTER(GsBatch), i64, i64, i32, P, P]
+    L.gs_shard_merge.argtypes = [P, ctypes.POINTER(GsBatch), i32, P, ctypes.POINTER(GsOutputs), P]
     L.gs_sample_noalloc.argtypes = [ctypes.POINTER(GsBatch), ctypes.POINTER(GsOutputs), P]
     L.gs_profile_enable.argtypes = [P, i32]
     L.gs_profile_read.argtypes = [P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),

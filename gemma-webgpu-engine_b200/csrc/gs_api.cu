@@ -183,28 +183,37 @@ gs_status gs_reserve(gs_ctx* c, int32_t rows, int64_t vocab, int32_t max_top_k, 
   return ensure_plans_host(c, std::max<size_t>(rows, 1));
 }
 
-gs_status gs_sample(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stream) {
-  if (!c) return GS_EINVAL;
-  gs_status s = check_batch(b, o, &c->err);
-  if (s != GS_OK) return s;
+}  // extern "C"
+
+namespace {
+
+// One sampling call: per-row plans (made against `plan_vocab`, the full vocabulary for
+// a shard), the work layout, the plan upload and the launches.  `sh` selects a
+// vocabulary-sharded mode (nullptr: an ordinary call).
+gs_status run_call(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stream, const ShardInfo* sh,
+                   int64_t plan_vocab) {
   if (b->rows == 0) return GS_OK;
   DeviceGuard g(c->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int np = b->params_count;
   PlanSummary ps;
-  for (int i = 0; i < np; ++i) ps.add(make_plan(b->params[i], b->vocab));
-  if (ps.any_sample && !b->rng_state && !b->uniforms) return fail(c, GS_EINVAL, "rng_state or uniforms is required");
+  for (int i = 0; i < np; ++i) ps.add(make_plan(b->params[i], plan_vocab));
+  const int smode = sh ? sh->mode : 0;
+  if (smode != 1 && ps.any_sample && !b->rng_state && !b->uniforms)
+    return fail(c, GS_EINVAL, "rng_state or uniforms is required");
+  if (smode && ps.any_large)
+    return fail(c, GS_EUNSUPPORTED, "vocabulary-sharded mode needs 1 <= topK <= %d (or temperature 0)", GS_MAX_TOP_K);
   Layout L;
-  s = plan_layout(b, ps, &L, &c->err);
+  gs_status s = smode == 2 ? plan_merge_layout(b, ps, *sh, &L, &c->err) : plan_layout(b, ps, &L, &c->err);
   if (s != GS_OK) return s;
   s = ensure_ws(c, L.total);
   if (s != GS_OK) return s;
-  const RowPlan plan0 = make_plan(b->params[0], b->vocab);
+  const RowPlan plan0 = make_plan(b->params[0], plan_vocab);
   const RowPlan* dplans = nullptr;
   if (np > 1) {
     s = ensure_plans_host(c, np);
     if (s != GS_OK) return s;
-    for (int i = 0; i < np; ++i) c->plans_host[i] = make_plan(b->params[i], b->vocab);
+    for (int i = 0; i < np; ++i) c->plans_host[i] = make_plan(b->params[i], plan_vocab);
     dplans = reinterpret_cast<const RowPlan*>(c->ws + L.plans_off);
     cudaError_t e = cudaMemcpyAsync(const_cast<RowPlan*>(dplans), c->plans_host, np * sizeof(RowPlan),
                                     cudaMemcpyHostToDevice, st);
@@ -226,10 +235,33 @@ gs_status gs_sample(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* str
       c->ev_pool.pop_back();
     }
   }
-  s = launch_sampling(b, o, L, plan0, dplans, stats, cands, st, c->profile ? evs.data() : nullptr, &c->err);
+  gs_outputs none{};
+  s = launch_sampling(b, o ? o : &none, L, plan0, dplans, stats, cands, st, c->profile ? evs.data() : nullptr,
+                      &c->err, sh);
   if (s != GS_OK) return s;
   if (c->profile) c->ev_live.push_back(evs);
   return GS_OK;
+}
+
+// Record geometry of a vocabulary-sharded batch: packs = the largest k of its rows,
+// penalised slots = the history stride.
+void shard_geometry(const gs_batch* b, int64_t vocab_total, ShardInfo* sh) {
+  int k = 1;
+  for (int i = 0; i < b->params_count; ++i) k = std::max(k, make_plan(b->params[i], vocab_total).k_eff);
+  sh->rec_kcap = k;
+  sh->rec_hcap = b->history ? static_cast<int>(b->history_stride) : 0;
+  sh->rec_bytes = shard_record_bytes(sh->rec_kcap, sh->rec_hcap);
+}
+
+}  // namespace
+
+extern "C" {
+
+gs_status gs_sample(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stream) {
+  if (!c) return GS_EINVAL;
+  gs_status s = check_batch(b, o, &c->err);
+  if (s != GS_OK) return s;
+  return run_call(c, b, o, stream, nullptr, b->vocab);
 }
 
 gs_status gs_sample_host(gs_ctx* c, const gs_batch* hb, const gs_outputs* ho, void* stream) {
@@ -421,16 +453,52 @@ gs_status gs_profile_read(gs_ctx* c, double* stream_ms, int64_t* stream_launches
   return GS_OK;
 }
 
-int64_t gs_shard_record_bytes(int32_t max_top_k) {
-  return static_cast<int64_t>(sizeof(UnitStat)) + 8ll * std::max(1, max_top_k);
+int64_t gs_shard_record_bytes(const gs_params* params, int32_t params_count, int64_t vocab_total,
+                              int64_t history_stride) {
+  if (!params || params_count <= 0 || vocab_total <= 0 || history_stride < 0) return -1;
+  gs_batch b{};
+  b.params = params;
+  b.params_count = params_count;
+  b.history_stride = history_stride;
+  const int32_t dummy = 0;
+  if (history_stride > 0) b.history = &dummy;
+  ShardInfo sh;
+  shard_geometry(&b, vocab_total, &sh);
+  return sh.rec_bytes;
 }
 
-gs_status gs_shard_partials(gs_ctx* c, const gs_batch*, int64_t, int64_t, void*, void*) {
-  return fail(c, GS_EUNSUPPORTED, "vocabulary-sharded mode is not built yet");
+gs_status gs_shard_partials(gs_ctx* c, const gs_batch* shard, int64_t vocab_offset, int64_t vocab_total,
+                            int32_t want_logprob, void* records, void* stream) {
+  if (!c) return GS_EINVAL;
+  gs_status s = check_batch(shard, nullptr, &c->err, kCheckNoOutputs);
+  if (s != GS_OK) return s;
+  if (!records && shard->rows > 0) return fail(c, GS_EINVAL, "records is NULL");
+  if (vocab_offset < 0 || vocab_offset % 4096 != 0 || vocab_offset + shard->vocab > vocab_total ||
+      vocab_total >= (1ll << 31))
+    return fail(c, GS_EINVAL, "a shard starts at a multiple of 4096 ids inside [0, vocab_total)");
+  if (shard->mask_table && shard->mask_words * 32 < vocab_total)
+    return fail(c, GS_EINVAL, "mask_words must cover the whole vocabulary (>= ceil(vocab_total/32))");
+  ShardInfo sh;
+  sh.mode = 1;
+  sh.vocab_offset = vocab_offset;
+  shard_geometry(shard, vocab_total, &sh);
+  sh.records = static_cast<unsigned char*>(records);
+  sh.want_raw = want_logprob != 0;
+  return run_call(c, shard, nullptr, stream, &sh, vocab_total);
 }
 
-gs_status gs_shard_merge(gs_ctx* c, const gs_batch*, int64_t, int32_t, const void*, const gs_outputs*, void*) {
-  return fail(c, GS_EUNSUPPORTED, "vocabulary-sharded mode is not built yet");
+gs_status gs_shard_merge(gs_ctx* c, const gs_batch* full, int32_t shards, const void* gathered,
+                         const gs_outputs* out, void* stream) {
+  if (!c) return GS_EINVAL;
+  gs_status s = check_batch(full, out, &c->err, kCheckNoLogits);
+  if (s != GS_OK) return s;
+  if (shards < 1 || (!gathered && full->rows > 0)) return fail(c, GS_EINVAL, "shards >= 1 and gathered records are required");
+  ShardInfo sh;
+  sh.mode = 2;
+  sh.shards = shards;
+  shard_geometry(full, full->vocab, &sh);
+  sh.records = static_cast<unsigned char*>(const_cast<void*>(gathered));
+  return run_call(c, full, out, stream, &sh, full->vocab);
 }
 
 }  // extern "C"

@@ -35,6 +35,8 @@ struct FinShared {
   int fill_base;
   int n_sort;
   unsigned long long min_pack;
+  int rec_nc;
+  float tok_raw;
 };
 
 __device__ __forceinline__ bool mask_allows(const uint32_t* mrow, uint32_t id) {
@@ -100,7 +102,22 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
   const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
   const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
   const unsigned char* rowbase =
-      static_cast<const unsigned char*>(A.logits) + static_cast<int64_t>(row) * A.row_stride * (DT == GS_DTYPE_F32 ? 4 : 2);
+      A.logits ? static_cast<const unsigned char*>(A.logits) + static_cast<int64_t>(row) * A.row_stride * (DT == GS_DTYPE_F32 ? 4 : 2)
+               : nullptr;
+  // Sources of the row's units: the streaming pass's statistics and packs, or (merge of
+  // a vocabulary-sharded row) the gathered shard records, one per shard.
+  const bool part_mode = A.shard_mode == 1, merge_mode = A.shard_mode == 2;
+  auto rec_of = [&](int u) -> const unsigned char* {
+    return A.records + (static_cast<int64_t>(u) * gridDim.x + row) * A.rec_bytes;
+  };
+  auto unit_stat = [&](int u) -> const UnitStat& {
+    return merge_mode ? *reinterpret_cast<const UnitStat*>(rec_of(u)) : A.stats[static_cast<int64_t>(row) * S + u];
+  };
+  auto unit_pack = [&](int u, int j) -> unsigned long long {
+    return merge_mode ? reinterpret_cast<const unsigned long long*>(rec_of(u) + sizeof(UnitStat))[j]
+                      : A.cands[(static_cast<int64_t>(row) * S + u) * A.kcap + j];
+  };
+  unsigned char* my_rec = part_mode ? A.records + static_cast<int64_t>(row) * A.rec_bytes : nullptr;
 
   // ---- 0. unit partials ----
   if (tid == 0) {
@@ -108,7 +125,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
     int na = 0, nc = 0;
     float rm = -INFINITY;
     for (int u = 0; u < S; ++u) {
-      const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+      const UnitStat& st = unit_stat(u);
       fl |= st.flags;
       na += st.n_allowed;
       nc += st.n_cand;
@@ -117,10 +134,27 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
     double rs = 0.0;
     if (A.want_raw)
       for (int u = 0; u < S; ++u) {
-        const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+        const UnitStat& st = unit_stat(u);
         if (st.raw_m > -INFINITY) rs = __dadd_rn(rs, __dmul_rn(st.raw_s, exp(static_cast<double>(st.raw_m) - static_cast<double>(rm))));
       }
-    if (has_mask && na == 0) fl |= GS_FLAG_ERR_DEADEND;
+    if (part_mode) {
+      // the shard's combined (max, sum): the merge combines shards the same way
+      float m = -INFINITY;
+      for (int u = 0; u < S; ++u) m = fmaxf(m, unit_stat(u).m);
+      double sm = 0.0;
+      for (int u = 0; u < S; ++u) {
+        const UnitStat& st = unit_stat(u);
+        if (st.m > -INFINITY)
+          sm = __dadd_rn(sm, __dmul_rn(st.s, exp2(__dmul_rn(static_cast<double>(st.m) - static_cast<double>(m), pp->a2))));
+      }
+      UnitStat* h = reinterpret_cast<UnitStat*>(my_rec);
+      h->m = m;
+      h->s = m > -INFINITY ? sm : 0.0;
+      h->raw_m = rm;
+      h->raw_s = rs;
+      h->n_allowed = na;
+    }
+    if (has_mask && na == 0 && !part_mode) fl |= GS_FLAG_ERR_DEADEND;
     if (greedy) fl |= GS_FLAG_GREEDY;
     F.flags = fl;
     F.n_allowed = na;
@@ -128,13 +162,26 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
     F.n_ent = 0;
     F.n_sort = 0;
     F.min_pack = ~0ull;
+    F.rec_nc = 0;
     F.raw_m = rm;
     F.raw_s = rs;
   }
   __syncthreads();
 
   // ---- 1. penalty history: distinct ids with counts, scored exactly ----
-  if (!(F.flags & GS_FLAG_ERRORS)) {
+  if (merge_mode && !(F.flags & GS_FLAG_ERRORS)) {
+    // the shards scored their own penalised ids; slot (shard, j) keeps a fixed position
+    const int hc = A.rec_hcap;
+    for (int i = tid; i < S * hc; i += bs) {
+      const int u = i / hc, j = i - u * hc;
+      const unsigned char* r = rec_of(u) + sizeof(UnitStat) + 8ll * A.rec_kcap;
+      const uint32_t id = reinterpret_cast<const uint32_t*>(r + 8ll * hc)[j];
+      ent_all[i] = id == 0xffffffffu ? Ent{-INFINITY, 0xffffffffu, 0xffffffffu}
+                                     : Ent{reinterpret_cast<const double*>(r)[j], id, 1u};
+    }
+    if (tid == 0) F.n_ent = S * hc;
+    __syncthreads();
+  } else if (!(F.flags & GS_FLAG_ERRORS)) {
     int64_t hl = A.history_len ? A.history_len[row] : 0;
     if (hl > A.history_stride) hl = A.history_stride;
     if (hl < 0) hl = 0;
@@ -149,21 +196,33 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
       // entry i belongs to sorted history position i (a fixed slot, so the normaliser's
       // summation order does not depend on thread timing); unused slots have kind ~0
       for (int i = tid; i < hl; i += bs) {
-        const uint32_t v = hs[i];
+        const uint32_t v = hs[i];  // global id (negative ids are >= 2^31 here)
+        const int64_t lv = static_cast<int64_t>(v) - A.vocab_offset;  // local to this call's logits
         Ent e{-INFINITY, 0xffffffffu, 0xffffffffu};
-        const bool first = v < static_cast<uint64_t>(A.vocab) && !(i > 0 && hs[i - 1] == v);  // negative ids are >= 2^31
-        if (first && !(has_mask && !mask_allows(mrow, v))) {  // masked: -inf either way
+        float x = 0.0f;
+        const bool first = lv >= 0 && lv < A.vocab && !(i > 0 && hs[i - 1] == v);
+        if (first && !(has_mask && !mask_allows(mrow, static_cast<uint32_t>(lv)))) {  // masked: -inf either way
           int cnt = 1;
           while (i + cnt < hl && hs[i + cnt] == v) ++cnt;
-          float x = load_logit(rowbase, DT, v);
+          x = load_logit(rowbase, DT, lv);
           if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
           if (!(x < INFINITY)) atomicOr(&F.flags, GS_FLAG_ERR_NONFINITE);  // NaN or +inf
           const double xp = penalise(static_cast<double>(x), static_cast<double>(cnt), rp, pres, freq);
           e = Ent{greedy ? xp : __ddiv_rn(xp, T), v, 1u};
         }
         ent_all[i] = e;
+        if (part_mode) {
+          unsigned char* r = my_rec + sizeof(UnitStat) + 8ll * A.rec_kcap;
+          reinterpret_cast<double*>(r)[i] = e.key;
+          reinterpret_cast<uint32_t*>(r + 8ll * A.rec_hcap)[i] = e.id;
+          reinterpret_cast<float*>(r + 12ll * A.rec_hcap)[i] = x;
+        }
       }
       if (tid == 0) F.n_ent = static_cast<int>(hl);
+    }
+    if (part_mode) {
+      unsigned char* r = my_rec + sizeof(UnitStat) + 8ll * A.rec_kcap;
+      for (int i = static_cast<int>(hl) + tid; i < A.rec_hcap; i += bs) reinterpret_cast<uint32_t*>(r + 8ll * A.rec_hcap)[i] = 0xffffffffu;
     }
     __syncthreads();
   }
@@ -174,6 +233,10 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
     const int nc = F.n_c;
     unsigned long long my_min = ~0ull;  // smallest unit pack this thread adds
     auto add_pack = [&](unsigned long long v) {
+      if (part_mode) {  // the shard's top k go to its record
+        reinterpret_cast<unsigned long long*>(my_rec + sizeof(UnitStat))[atomicAdd(&F.rec_nc, 1)] = v;
+        return;
+      }
       const float x = pack_value(v);
       const uint32_t id = pack_id(v);
       const int slot = atomicAdd(&F.n_ent, 1);
@@ -185,8 +248,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
       const int np = S * A.kcap;
       for (int i = tid; i < np; i += bs) {
         const int u = i / A.kcap, j = i - u * A.kcap;
-        const int64_t unit = static_cast<int64_t>(row) * S + u;
-        buf[i] = j < A.stats[unit].n_cand ? A.cands[unit * A.kcap + j] : 0ull;
+        buf[i] = j < unit_stat(u).n_cand ? unit_pack(u, j) : 0ull;
       }
       __syncthreads();
       unsigned long long prefix, mask;
@@ -198,12 +260,20 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
     } else {
       for (int i = tid; i < S * A.kcap; i += bs) {
         const int u = i / A.kcap, j = i - u * A.kcap;
-        const int64_t unit = static_cast<int64_t>(row) * S + u;
-        if (j < A.stats[unit].n_cand) add_pack(A.cands[unit * A.kcap + j]);
+        if (j < unit_stat(u).n_cand) add_pack(unit_pack(u, j));
       }
     }
     if (my_min != ~0ull) atomicMin(&F.min_pack, my_min);
     __syncthreads();
+  }
+  if (part_mode) {  // the record is complete: the rest runs in gs_shard_merge
+    if (tid == 0) {
+      UnitStat* h = reinterpret_cast<UnitStat*>(my_rec);
+      h->n_cand = F.rec_nc;
+      h->flags = F.flags;
+      h->pad = A.want_raw ? 1 : 0;  // bit 0: raw sums recorded
+    }
+    return;
   }
 
   // ---- 3. exact order of the entries that can reach the top k ----
@@ -313,7 +383,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
         // full-vocabulary normaliser: streamed units + every penalised id
         double part = 0.0;
         for (int u = tid; u < S; u += bs) {
-          const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+          const UnitStat& st = unit_stat(u);
           if (st.m > -INFINITY)
             part = __dadd_rn(part, __dmul_rn(st.s, exp(__dsub_rn(__ddiv_rn(static_cast<double>(st.m), T), M))));
         }
@@ -345,6 +415,24 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
   // ---- outputs ----
   const unsigned fl = F.flags;
   const bool err = (fl & GS_FLAG_ERRORS) != 0;
+  if (merge_mode && A.logprob && !err) {
+    // the drawn id's soft-capped logit, from the shard that holds it
+    if (tid == 0) F.tok_raw = __int_as_float(0x7fffffff);
+    __syncthreads();
+    const int per = A.rec_kcap + A.rec_hcap;
+    for (int i = tid; i < S * per; i += bs) {
+      const int u = i / per, j = i - u * per;
+      if (j < A.rec_kcap) {
+        if (j < unit_stat(u).n_cand && pack_id(unit_pack(u, j)) == tok) F.tok_raw = pack_value(unit_pack(u, j));
+      } else {
+        const unsigned char* r = rec_of(u) + sizeof(UnitStat) + 8ll * A.rec_kcap;
+        const int jj = j - A.rec_kcap;
+        if (reinterpret_cast<const uint32_t*>(r + 8ll * A.rec_hcap)[jj] == tok)
+          F.tok_raw = reinterpret_cast<const float*>(r + 12ll * A.rec_hcap)[jj];
+      }
+    }
+    __syncthreads();
+  }
   if (tid == 0) {
     A.ids[row] = err ? -1 : static_cast<int32_t>(tok);
     if (A.flags) A.flags[row] = fl;
@@ -352,8 +440,17 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
     if (A.logprob) {
       double lp = NAN;
       if (!err) {
-        float x = load_logit(rowbase, DT, tok);
-        if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
+        float x;
+        if (merge_mode) {
+          // NaN when the drawn id is a masked filler (no shard holds its logit) or a shard
+          // recorded no raw sums
+          x = F.tok_raw;
+          for (int u = 0; u < S; ++u)
+            if (!(unit_stat(u).pad & 1)) x = __int_as_float(0x7fffffff);
+        } else {
+          x = load_logit(rowbase, DT, tok);
+          if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
+        }
         lp = __dsub_rn(__dsub_rn(static_cast<double>(x), static_cast<double>(F.raw_m)), log(F.raw_s));
       }
       A.logprob[row] = lp;

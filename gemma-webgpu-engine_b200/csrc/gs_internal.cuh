@@ -96,7 +96,25 @@ struct FinalizeArgs {
   double* cand_probs;
   int32_t* cand_count;
   int32_t cand_cap;
+  // vocabulary-sharded mode (0: sample the row here)
+  int32_t shard_mode;     // 1: write this shard's per-row record; 2: merge gathered records
+  int32_t shards;         // mode 2: records per row (one per shard)
+  int64_t vocab_offset;   // mode 1: global id of local id 0
+  int64_t rec_bytes;      // bytes per record (ShardRecord layout)
+  int32_t rec_kcap;       // candidate packs per record
+  int32_t rec_hcap;       // penalised-entry slots per record
+  unsigned char* records; // mode 1: out [rows] records; mode 2: in [shards][rows] records
 };
+
+// Per-row record of one vocabulary shard (gs_shard_partials writes, gs_shard_merge reads):
+//   UnitStat (the shard's combined statistics; n_cand packs follow),
+//   packs[rec_kcap]   top-k candidate packs of the shard (global ids),
+//   pen_key[rec_hcap] penalised entries' exact keys (double), pen_id[rec_hcap] their
+//   global ids (0xffffffff: empty slot), pen_raw[rec_hcap] their soft-capped logits.
+inline int64_t shard_record_bytes(int kcap, int hcap) {
+  const int64_t b = static_cast<int64_t>(sizeof(UnitStat)) + 8ll * kcap + 16ll * hcap;
+  return (b + 15) & ~15ll;
+}
 
 // Launch helpers implemented in gs_kernels.cu.
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);

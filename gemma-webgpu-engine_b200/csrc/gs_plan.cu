@@ -52,14 +52,14 @@ bool valid_params(const gs_params& p, std::string* why) {
   return false;
 }
 
-gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err) {
-  if (!b || !o) return fmt(err, GS_EINVAL, "batch and outputs are required");
+gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err, unsigned what) {
+  if (!b || (!o && !(what & kCheckNoOutputs))) return fmt(err, GS_EINVAL, "batch and outputs are required");
   if (b->rows < 0) return fmt(err, GS_EINVAL, "rows must be >= 0");
   if (b->vocab <= 0) return fmt(err, GS_EEMPTY, "Cannot sample empty logits");
   if (b->vocab >= (1ll << 31)) return fmt(err, GS_EINVAL, "vocab must be below 2^31");
   if (b->row_stride < b->vocab) return fmt(err, GS_EINVAL, "row_stride must be >= vocab");
   if (b->dtype != GS_DTYPE_F32 && b->dtype != GS_DTYPE_BF16) return fmt(err, GS_EINVAL, "unknown dtype %d", b->dtype);
-  if (b->rows > 0 && !b->logits) return fmt(err, GS_EINVAL, "logits is NULL");
+  if (b->rows > 0 && !b->logits && !(what & kCheckNoLogits)) return fmt(err, GS_EINVAL, "logits is NULL");
   if (!(b->softcap >= 0) || !std::isfinite(b->softcap)) return fmt(err, GS_EINVAL, "softcap must be finite and >= 0");
   if (!b->params || (b->params_count != 1 && b->params_count != b->rows))
     return fmt(err, GS_EINVAL, "params_count must be 1 or rows");
@@ -71,8 +71,10 @@ gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err) 
     if (b->mask_words < (b->vocab + 31) / 32) return fmt(err, GS_EINVAL, "mask_words must be >= ceil(vocab/32)");
     if (b->mask_states <= 0) return fmt(err, GS_EINVAL, "mask_states must be > 0");
   }
-  if (b->rows > 0 && !o->ids) return fmt(err, GS_EINVAL, "outputs.ids is NULL");
-  if (o->cand_ids && o->cand_cap <= 0) return fmt(err, GS_EINVAL, "cand_cap must be > 0 with cand_ids");
+  if (o) {
+    if (b->rows > 0 && !o->ids) return fmt(err, GS_EINVAL, "outputs.ids is NULL");
+    if (o->cand_ids && o->cand_cap <= 0) return fmt(err, GS_EINVAL, "cand_cap must be > 0 with cand_ids");
+  }
   for (int i = 0; i < b->params_count; ++i)
     if (!valid_params(b->params[i], err)) return GS_EINVAL;
   return GS_OK;
@@ -142,9 +144,37 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   return GS_OK;
 }
 
+gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const ShardInfo& sh, Layout* L,
+                            std::string* err) {
+  const int rows = b->rows;
+  L->splits = sh.shards;
+  L->chunk = 0;
+  L->kcap = sh.rec_kcap;
+  L->kc = 0;
+  L->kmax = ps.kmax;
+  L->any_large = ps.any_large;
+  L->any_small = ps.any_small;
+  L->any_sample = ps.any_sample;
+  L->plans_off = 0;
+  L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
+  L->cands_off = L->stats_off;
+  L->total = L->stats_off;
+  L->stream_smem = 0;
+  L->hist_cap = 1;
+  L->pack_cap = sh.shards * sh.rec_kcap;
+  L->ent_cap = pow2ceil(std::max<int64_t>(static_cast<int64_t>(sh.shards) * sh.rec_hcap + ps.kmax, 1));
+  L->work_cap = std::min(pow2ceil(std::max(ps.kmax, 1)), 1024);
+  L->fin_smem = finalize_smem_bytes(L->hist_cap, L->ent_cap, L->pack_cap, L->work_cap);
+  L->large_smem = 0;
+  if (L->fin_smem > 220 * 1024)
+    return fmt(err, GS_EUNSUPPORTED, "merge of %d shards needs %zu bytes of shared memory", sh.shards, L->fin_smem);
+  return GS_OK;
+}
+
 gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
                           const RowPlan* dplans, UnitStat* stats, unsigned long long* cands, cudaStream_t st,
-                          cudaEvent_t* events, std::string* err) {
+                          cudaEvent_t* events, std::string* err, const ShardInfo* shard) {
+  const int smode = shard ? shard->mode : 0;
   const int rows = b->rows;
   const float cap = b->softcap;
   const float inv_cap = cap != 0.0f ? static_cast<float>(1.0 / static_cast<double>(cap)) : 0.0f;
@@ -152,10 +182,10 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   sa.logits = b->logits;
   sa.vocab = b->vocab;
   sa.row_stride = b->row_stride;
-  sa.vocab_offset = 0;
+  sa.vocab_offset = smode == 1 ? shard->vocab_offset : 0;
   sa.softcap = cap;
   sa.inv_softcap = inv_cap;
-  sa.want_raw = o->logprob != nullptr;
+  sa.want_raw = smode == 1 ? shard->want_raw : o->logprob != nullptr;
   sa.splits = L.splits;
   sa.chunk = L.chunk;
   sa.kcap = L.kcap;
@@ -166,15 +196,20 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   sa.history = b->history;
   sa.history_len = b->history ? b->history_len : nullptr;
   sa.history_stride = b->history ? b->history_stride : 0;
-  sa.mask_table = b->mask_table;
+  // (a shard reads its own words of each state's row: the table pointer moves, the row
+  // stride stays)
+  sa.mask_table = b->mask_table && smode == 1 ? b->mask_table + (shard->vocab_offset >> 5) : b->mask_table;
   sa.mask_states = b->mask_states;
   sa.mask_words = b->mask_words;
   sa.mask_state = b->mask_table ? b->mask_state : nullptr;
   sa.stats = stats;
   sa.cands = cands;
   if (events) cudaEventRecord(events[0], st);
-  cudaError_t e = launch_stream(sa, b->dtype, rows, L.stream_smem, st);
-  if (e != cudaSuccess) return fmt(err, GS_ECUDA, "streaming pass launch: %s", cudaGetErrorString(e));
+  cudaError_t e = cudaSuccess;
+  if (smode != 2) {
+    e = launch_stream(sa, b->dtype, rows, L.stream_smem, st);
+    if (e != cudaSuccess) return fmt(err, GS_ECUDA, "streaming pass launch: %s", cudaGetErrorString(e));
+  }
   if (events) cudaEventRecord(events[1], st);
 
   FinalizeArgs fa{};
@@ -195,7 +230,7 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   fa.history = sa.history;
   fa.history_len = sa.history_len;
   fa.history_stride = sa.history_stride;
-  fa.mask_table = b->mask_table;
+  fa.mask_table = sa.mask_table;
   fa.mask_states = b->mask_states;
   fa.mask_words = b->mask_words;
   fa.mask_state = sa.mask_state;
@@ -210,6 +245,25 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   fa.cand_probs = o->cand_probs;
   fa.cand_count = o->cand_count;
   fa.cand_cap = o->cand_cap;
+  if (smode) {
+    fa.shard_mode = smode;
+    fa.shards = shard->shards;
+    fa.vocab_offset = smode == 1 ? shard->vocab_offset : 0;
+    fa.rec_bytes = shard->rec_bytes;
+    fa.rec_kcap = shard->rec_kcap;
+    fa.rec_hcap = shard->rec_hcap;
+    fa.records = shard->records;
+    if (smode == 1) {  // partials: the merge writes only the records
+      fa.ids = nullptr;
+      fa.logprob = nullptr;
+      fa.flags = nullptr;
+      fa.cand_ids = nullptr;
+      fa.cand_probs = nullptr;
+      fa.cand_count = nullptr;
+      fa.rng_state = nullptr;
+      fa.uniforms = nullptr;
+    }
+  }
   if (L.any_small) {
     e = launch_finalize(fa, b->dtype, rows, L.fin_smem, st);
     if (e != cudaSuccess) return fmt(err, GS_ECUDA, "merge launch: %s", cudaGetErrorString(e));

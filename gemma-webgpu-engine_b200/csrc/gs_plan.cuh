@@ -80,15 +80,32 @@ struct PlanSummary {
 
 // validateDecodingConfig (src/runtime/decoding.ts:31-59) for the fields sampleToken reads.
 bool valid_params(const gs_params& p, std::string* why);
-gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err);
+enum : unsigned { kCheckNoOutputs = 1u, kCheckNoLogits = 2u };
+gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err, unsigned what = 0);
 gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::string* err);
+
+// Vocabulary-sharded calls: mode 1 streams a shard and writes its per-row records,
+// mode 2 merges the gathered records (no streaming pass).
+struct ShardInfo {
+  int mode = 0;
+  int64_t vocab_offset = 0;
+  int shards = 1;
+  int rec_kcap = 1, rec_hcap = 0;
+  int64_t rec_bytes = 0;
+  unsigned char* records = nullptr;
+  bool want_raw = false;  // mode 1: record the raw sums (log-probabilities)
+};
+
+// Layout of a merge of `shards` gathered records per row (mode 2).
+gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const ShardInfo& sh, Layout* L,
+                            std::string* err);
 
 // Launches the streaming pass, the merge and (when a row needs it) the histogram path.
 // `events` (3 entries or nullptr) are recorded before the stream pass, before the
-// merge, and at the end.
+// merge, and at the end.  `shard` (nullptr: an ordinary call) selects a sharded mode.
 gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
                           const RowPlan* dplans, UnitStat* stats, unsigned long long* cands, cudaStream_t st,
-                          cudaEvent_t* events, std::string* err);
+                          cudaEvent_t* events, std::string* err, const ShardInfo* shard = nullptr);
 
 // Message of this thread's last failed gs_sample_noalloc call.
 const char* noalloc_last_error();

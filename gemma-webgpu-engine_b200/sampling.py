@@ -226,6 +226,99 @@ class GpuSampler:
             _raise(st, self._ctx)
         return out
 
+    # ---------------------------------------------------------------- vocabulary shards
+    def shard_record_bytes(self, params, vocab_total: int, history_stride: int = 0) -> int:
+        """Bytes of one row's shard record (gs_shard_record_bytes)."""
+        parr = _params_array(params)
+        n = self._L.gs_shard_record_bytes(parr, len(parr), int(vocab_total), int(history_stride))
+        if n < 0:
+            raise ValueError("invalid shard record geometry")
+        return int(n)
+
+    def shard_partials(self, logits, params, *, vocab_offset: int, vocab_total: int, softcap: float = 0.0,
+                       history=None, history_len=None, mask_table=None, mask_state=None, logprob: bool = False,
+                       records=None, stream=None):
+        """Streams this GPU's vocabulary shard ``logits`` [rows, shard_vocab] (global ids
+        [vocab_offset, vocab_offset + shard_vocab)) and returns its per-row records, a uint8
+        device tensor [rows, record_bytes] (gs_shard_partials).  History ids are global and
+        ``mask_table`` covers the whole vocabulary; ``logprob`` records the raw sums a merge
+        with log-probabilities needs."""
+        import torch
+        b, keep = self.make_batch(logits, params, softcap=softcap, history=history, history_len=history_len,
+                                  mask_table=mask_table, mask_state=mask_state)
+        hstride = b.history_stride if history is not None else 0
+        nbytes = self.shard_record_bytes(params, vocab_total, hstride)
+        rows = logits.shape[0]
+        if records is None:
+            records = torch.empty((rows, nbytes), dtype=torch.uint8, device=logits.device)
+        if records.numel() < rows * nbytes:
+            raise ValueError("records buffer too small")
+        if stream is None:
+            stream = torch.cuda.current_stream(logits.device).cuda_stream
+        st = self._L.gs_shard_partials(self._ctx, ctypes.byref(b), int(vocab_offset), int(vocab_total),
+                                       1 if logprob else 0, ctypes.c_void_p(records.data_ptr()),
+                                       ctypes.c_void_p(stream))
+        del keep
+        if st != _lib.GS_OK:
+            _raise(st, self._ctx)
+        return records
+
+    def shard_merge(self, gathered, params, *, rows: int, shards: int, vocab_total: int, history_stride: int = 0,
+                    mask_table=None, mask_state=None, rng_state=None, uniforms=None, logprob: bool = False,
+                    candidates: int = 0, stream=None) -> SampleResult:
+        """Merges the all-gathered shard records ([shards][rows] records, uint8 device
+        tensor) and samples the rows exactly as ``sample`` would on whole rows
+        (gs_shard_merge).  Every rank passing the same records gets the same result."""
+        import torch
+        dev = gathered.device
+        parr = _params_array(params)
+        b = GsBatch()
+        b.dtype = _lib.GS_DTYPE_F32
+        b.rows = rows
+        b.vocab = int(vocab_total)
+        b.row_stride = int(vocab_total)
+        b.params_count = len(parr)
+        b.params = ctypes.cast(parr, ctypes.c_void_p)
+        hist_dummy = None
+        if history_stride > 0:
+            hist_dummy = torch.zeros(1, dtype=torch.int32, device=dev)  # record layout only
+            b.history = hist_dummy.data_ptr()
+            b.history_len = hist_dummy.data_ptr()
+            b.history_stride = int(history_stride)
+        if mask_table is not None:
+            b.mask_table = mask_table.data_ptr()
+            b.mask_states = mask_table.shape[0]
+            b.mask_words = mask_table.stride(0) if mask_table.shape[0] > 1 else mask_table.shape[1]
+            b.mask_state = mask_state.data_ptr()
+        if rng_state is not None:
+            b.rng_state = rng_state.data_ptr()
+        if uniforms is not None:
+            b.uniforms = uniforms.data_ptr()
+        out = SampleResult(
+            ids=torch.empty(rows, dtype=torch.int32, device=dev),
+            flags=torch.empty(rows, dtype=torch.int32, device=dev),
+            logprob=torch.empty(rows, dtype=torch.float64, device=dev) if logprob else None,
+            cand_ids=torch.empty((rows, candidates), dtype=torch.int32, device=dev) if candidates else None,
+            cand_probs=torch.empty((rows, candidates), dtype=torch.float64, device=dev) if candidates else None,
+            cand_count=torch.empty(rows, dtype=torch.int32, device=dev) if candidates else None,
+        )
+        o = GsOutputs()
+        o.ids = _ptr(out.ids)
+        o.flags = _ptr(out.flags)
+        o.logprob = _ptr(out.logprob)
+        o.cand_ids = _ptr(out.cand_ids)
+        o.cand_probs = _ptr(out.cand_probs)
+        o.cand_count = _ptr(out.cand_count)
+        o.cand_cap = candidates
+        if stream is None:
+            stream = torch.cuda.current_stream(dev).cuda_stream
+        st = self._L.gs_shard_merge(self._ctx, ctypes.byref(b), int(shards), ctypes.c_void_p(gathered.data_ptr()),
+                                    ctypes.byref(o), ctypes.c_void_p(stream))
+        del hist_dummy
+        if st != _lib.GS_OK:
+            _raise(st, self._ctx)
+        return out
+
     def sample_host(self, logits: np.ndarray, params, *, softcap: float = 0.0, history: np.ndarray | None = None,
                     history_len: np.ndarray | None = None, mask_table=None, mask_state: np.ndarray | None = None,
                     rng_state: np.ndarray | None = None, uniforms: np.ndarray | None = None, logprob: bool = False,

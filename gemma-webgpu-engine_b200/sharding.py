@@ -1,0 +1,125 @@
+"""Multi-GPU sampling: one process per GPU, torch.distributed for the plumbing.
+
+Two layouts (the reference samples one row on one device, src/runtime/sampling.ts:18;
+these are the B200 deployment of the same call):
+
+* row-sharded (large batches, e.g. C4): contiguous row blocks per rank, each rank runs
+  ``GpuSampler.sample`` on its block; there is no collective on the data path.  The ids
+  come back to every rank with one all-gather when the caller wants them there.
+* vocabulary-sharded (small batches, e.g. C5): every rank holds a slice of every row's
+  logits; ``GpuSampler.shard_partials`` streams the slice into a fixed-size record per row,
+  one all-gather exchanges the records, and ``GpuSampler.shard_merge`` samples from them,
+  identically on every rank.
+
+The partition rules and the exchange are plain host logic (tested with gloo on CPU);
+the device work is the library's.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+VOCAB_GRANULE = 4096  # shard starts are multiples of this many ids (TMA-aligned mask words)
+
+
+def row_shards(rows: int, world: int) -> list:
+    """(start, count) of each rank's contiguous row block; the first ``rows % world``
+    ranks take one extra row."""
+    if rows < 0 or world < 1:
+        raise ValueError("rows >= 0 and world >= 1")
+    base, extra = divmod(rows, world)
+    out, start = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append((start, n))
+        start += n
+    return out
+
+
+def vocab_shards(vocab: int, world: int, granule: int = VOCAB_GRANULE) -> list:
+    """(offset, size) of each rank's vocabulary slice: equal slices rounded to whole
+    granules, the last rank taking the remainder (every offset a multiple of ``granule``)."""
+    if vocab <= 0 or world < 1:
+        raise ValueError("vocab > 0 and world >= 1")
+    per = -(-vocab // world)
+    per = -(-per // granule) * granule
+    out = []
+    for r in range(world):
+        off = min(r * per, vocab)
+        out.append((off, max(0, min(per, vocab - off))))
+    if any(size == 0 for _, size in out):
+        raise ValueError(f"vocabulary {vocab} too small for {world} shards of {granule}-id granules")
+    return out
+
+
+def exchange_records(local, group=None):
+    """All-gathers each rank's record buffer (a contiguous uint8 tensor of equal size on
+    every rank) into one tensor in rank order: [world * local.numel()] bytes, i.e.
+    [shards][rows][record] for shard records.  NCCL for CUDA tensors, gloo for CPU."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    flat = local.reshape(-1).contiguous()
+    out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
+    if flat.device.type == "cuda":
+        dist.all_gather_into_tensor(out, flat, group=group)
+    else:
+        parts = list(out.view(world, -1).unbind(0))
+        dist.all_gather(parts, flat, group=group)
+    return out
+
+
+def gather_rows(local, rows_total: int, group=None):
+    """Row-sharded results (``local`` = this rank's block of a per-row tensor, blocks laid
+    out by ``row_shards``) gathered on every rank into [rows_total, ...]."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    shards = row_shards(rows_total, world)
+    width = max(n for _, n in shards)
+    tail = tuple(local.shape[1:])
+    pad = torch.zeros((width,) + tail, dtype=local.dtype, device=local.device)
+    pad[:local.shape[0]] = local
+    flat = exchange_records(pad.view(torch.uint8) if pad.dtype != torch.uint8 else pad, group)
+    blocks = flat.view(world, -1).view(pad.dtype).view((world, width) + tail)
+    return torch.cat([blocks[r, :n] for r, (_, n) in enumerate(shards)], dim=0)
+
+
+@dataclass
+class ShardPlan:
+    rank: int
+    world: int
+    vocab_total: int
+    offset: int
+    size: int
+
+
+class VocabShardedSampler:
+    """Vocabulary-sharded sampling over ``torch.distributed`` (one process per GPU)."""
+
+    def __init__(self, sampler, vocab_total: int, group=None):
+        import torch.distributed as dist
+        self.sampler = sampler
+        self.group = group
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        off, size = vocab_shards(vocab_total, world)[rank]
+        self.plan = ShardPlan(rank, world, vocab_total, off, size)
+
+    def sample(self, local_logits, params, *, softcap: float = 0.0, history=None, history_len=None,
+               mask_table=None, mask_state=None, rng_state=None, uniforms=None, logprob: bool = False,
+               candidates: int = 0, stream=None):
+        """``local_logits`` [rows, plan.size] holds this rank's slice; the other arguments
+        are the whole rows' (global history ids, full mask table, per-row PRNG states:
+        every rank advances its copy identically)."""
+        p = self.plan
+        if local_logits.shape[1] != p.size:
+            raise ValueError(f"rank {p.rank} holds {p.size} ids, got {local_logits.shape[1]}")
+        rec = self.sampler.shard_partials(local_logits, params, vocab_offset=p.offset, vocab_total=p.vocab_total,
+                                          softcap=softcap, history=history, history_len=history_len,
+                                          mask_table=mask_table, mask_state=mask_state, logprob=logprob,
+                                          stream=stream)
+        gathered = exchange_records(rec, self.group)
+        hstride = 0 if history is None else (history.stride(0) if history.shape[0] > 1 else history.shape[1])
+        return self.sampler.shard_merge(gathered, params, rows=local_logits.shape[0], shards=p.world,
+                                        vocab_total=p.vocab_total, history_stride=hstride, mask_table=mask_table,
+                                        mask_state=mask_state, rng_state=rng_state, uniforms=uniforms,
+                                        logprob=logprob, candidates=candidates, stream=stream)

@@ -203,19 +203,34 @@ gs_status gs_profile_read(gs_ctx* ctx, double* stream_ms, int64_t* stream_launch
                           int64_t* merge_launches);
 
 /*
- * Vocabulary-sharded mode (one process per GPU, each holding ids
- * [vocab_offset, vocab_offset + shard_vocab) of every row).  gs_shard_partials runs the
- * streaming pass on the local shard and writes a fixed-size record per row
- * (gs_shard_record_bytes); the caller all-gathers the records (one NCCL all-gather);
- * gs_shard_merge merges the gathered records of all shards and samples, identically on
- * every rank.  Requires 1 <= topK <= GS_MAX_TOP_K (or temperature 0) and no history
- * ids outside the shard's own bookkeeping (history is applied per shard).
+ * Vocabulary-sharded mode: no reference counterpart (the reference samples one row on
+ * one device, src/runtime/sampling.ts:18).  For small batches whose rows are split by
+ * vocabulary over several GPUs (one process per GPU; shard g holds ids
+ * [vocab_offset, vocab_offset + shard->vocab) of every row, vocab_offset a multiple of
+ * 4096):
+ *   1. gs_shard_partials streams the local shard and writes one fixed-size record per
+ *      row into `records` (device, rows x gs_shard_record_bytes): the shard's maximum
+ *      and sum of e^(x/T) over live ids, its top-k candidates (global ids) and the exact
+ *      penalised scores of the history ids it holds.  History ids are global; the mask
+ *      table covers the whole vocabulary (mask_words >= ceil(vocab_total/32)).
+ *      want_logprob != 0 also records the raw sums a merge with outputs.logprob needs
+ *      (otherwise that merge writes NaN log-probabilities).
+ *   2. the caller all-gathers the records (one collective, e.g. ncclAllGather) into
+ *      [shards][rows] order;
+ *   3. gs_shard_merge merges them and samples exactly as gs_sample would on the whole
+ *      rows (`full`: rows, params, the full mask table and states, rng_state or
+ *      uniforms, history / history_stride for the record layout only, vocab =
+ *      vocab_total; logits may be NULL), identically on every rank.
+ * Requires 1 <= topK <= GS_MAX_TOP_K or temperature 0 (GS_EUNSUPPORTED otherwise).
+ * gs_shard_record_bytes returns the record size for a batch's params (-1 on bad input);
+ * every rank must pass the same params and history_stride.
  */
-int64_t gs_shard_record_bytes(int32_t max_top_k);
-gs_status gs_shard_partials(gs_ctx* ctx, const gs_batch* shard, int64_t vocab_offset,
-                            int64_t vocab_total, void* records, void* stream);
-gs_status gs_shard_merge(gs_ctx* ctx, const gs_batch* shard, int64_t vocab_total, int32_t shards,
-                         const void* gathered_records, const gs_outputs* out, void* stream);
+int64_t gs_shard_record_bytes(const gs_params* params, int32_t params_count, int64_t vocab_total,
+                              int64_t history_stride);
+gs_status gs_shard_partials(gs_ctx* ctx, const gs_batch* shard, int64_t vocab_offset, int64_t vocab_total,
+                            int32_t want_logprob, void* records, void* stream);
+gs_status gs_shard_merge(gs_ctx* ctx, const gs_batch* full, int32_t shards, const void* gathered_records,
+                         const gs_outputs* out, void* stream);
 
 #ifdef __cplusplus
 }
