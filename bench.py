@@ -244,8 +244,13 @@ def run_ours(args, rank, world, local):
         "gpu_launches": 2 * args.steps * world,
         "clocks": clk,
     }
+    if not args.no_extras:
+        # end to end on every rank (whole-job rows over the slowest rank's time)
+        result["e2e"] = e2e_leg(args, pkg, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per,
+                                world)
     if rank == 0 and not args.no_extras:
-        result.update(extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per))
+        result.update(extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per,
+                             world))
     sampler.close()
     if world > 1:
         dist.barrier()
@@ -254,13 +259,11 @@ def run_ours(args, rank, world, local):
         print(json.dumps(result), flush=True)
 
 
-def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per):
-    import numpy as np
+def e2e_leg(args, pkg, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per, world):
+    """gs_sample_host with pinned host buffers: host->device copies of the step's inputs and
+    device->host copies of its outputs inside the timed region, on every rank."""
     import torch
-
-    res = {}
     stream = torch.cuda.current_stream(dev)
-    # ---- end to end through gs_sample_host: host (pinned) buffers, copies in the timed region
     n_e2e = max(3, min(10, args.steps))
     hx = logits.cpu().pin_memory().numpy() if logits.dtype == torch.float32 else None
     if hx is None:
@@ -274,6 +277,9 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
         sampler.sample_host(hx, params, softcap=30.0, history=hh, history_len=hl, mask_table=table, mask_state=hs,
                             rng_state=hr, stream=stream.cuda_stream, dtype=dt)
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -283,11 +289,27 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_s = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
     h2d = hx.nbytes + hh.nbytes + hl.nbytes + hs.nbytes + hr.nbytes
     d2h = per * (4 + 4 + 8)
-    res["e2e"] = {"value": per * n_e2e / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-                  "d2h_bytes_per_step": int(d2h), "steps": n_e2e,
-                  "api": "gs_sample_host (host logits/history/states in pinned memory, ids+flags+states back)"}
+    return {"value": per * world * n_e2e / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(h2d * world),
+            "d2h_bytes_per_step": int(d2h * world), "steps": n_e2e,
+            "api": "gs_sample_host (host logits/history/states in pinned memory, ids+flags+states back), "
+                   "every rank, slowest rank's time"}
+
+
+def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per, world):
+    import numpy as np
+    import torch
+
+    res = {}
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
     # ---- bf16 variant of the same batch
     if args.dtype == "f32":
         xb = logits.to(torch.bfloat16)
@@ -330,8 +352,9 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
                          "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],
                          "timing": "CUDA events between consecutive gs_sample calls (device time, no graph)"}
     del lg
-    # ---- CPU baseline: the oracle on a bounded sample of the same rows, all host threads
-    res["cpu_baseline"] = cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per)
+    # ---- CPU baseline (N = 1 only): the oracle on a bounded sample of the same rows
+    if world == 1:
+        res["cpu_baseline"] = cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per)
     return res
 
 
