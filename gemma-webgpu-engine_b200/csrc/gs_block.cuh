@@ -100,6 +100,19 @@ __device__ inline double block_sum_d(double v, double* red) {
   return s;
 }
 
+// Block-wide maximum (fmaxf: NaN inputs are ignored).  `red` holds >= 32 floats.
+__device__ inline float block_max_f(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float m = -INFINITY;
+  for (int w = 0; w < nw; ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  return m;
+}
+
 __device__ inline int block_sum_i(int v, int* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   v = warp_sum_i(v);
@@ -182,21 +195,55 @@ __device__ inline int block_exclusive_count(const unsigned char* flag, int* pos,
   return total;
 }
 
-// Finds the k-th largest of the (distinct) values buf[0, n) as (prefix, mask): exactly k
-// values satisfy (v & mask) >= prefix.  MSB-first radix select, 8-bit digits.  Requires
-// 0 < k < n.  Every thread of the block must call it.
+// Threshold of the k largest non-zero values of buf[0, n) (zero slots are empty; at
+// least k non-zero values): on return, the kept values are those with
+// (v & mask) >= prefix.  MSB-first radix select with 8-bit digits, starting at the
+// highest bit in which the non-zero values differ (the common high bits would put every
+// value in one histogram bin), stopping as soon as the bin holding the k-th value is
+// kept whole.  `hist` holds 256 counters; the s_* scalars are shared.
 __device__ inline void select_threshold(const unsigned long long* buf, int n, int k, unsigned int* hist,
                                  int* s_digit, int* s_above, int* s_binc, unsigned long long& prefix,
                                  unsigned long long& mask) {
-  prefix = 0;
-  mask = 0;
+  __shared__ unsigned long long s_ref, s_dif;
+  if (threadIdx.x == 0) {
+    s_ref = 0;
+    s_dif = 0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (buf[i] != 0ull) {
+      atomicMax(&s_ref, buf[i]);
+      break;
+    }
+  __syncthreads();
+  const unsigned long long ref = s_ref;
+  unsigned long long dif = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (buf[i] != 0ull) dif |= buf[i] ^ ref;
+  dif |= __shfl_xor_sync(kFullMask, dif, 16);
+  dif |= __shfl_xor_sync(kFullMask, dif, 8);
+  dif |= __shfl_xor_sync(kFullMask, dif, 4);
+  dif |= __shfl_xor_sync(kFullMask, dif, 2);
+  dif |= __shfl_xor_sync(kFullMask, dif, 1);
+  if ((threadIdx.x & 31) == 0 && dif) atomicOr(&s_dif, dif);
+  __syncthreads();
+  dif = s_dif;
+  if (dif == 0ull) {  // one distinct non-zero value
+    prefix = ref;
+    mask = ~0ull;
+    return;
+  }
+  const int hb = 63 - __clzll(static_cast<long long>(dif));
+  mask = hb == 63 ? 0ull : (~0ull << (hb + 1));
+  prefix = ref & mask;
+  int shift = hb >= 7 ? hb - 7 : 0;
   int need = k;
-  for (int shift = 56; shift >= 0; shift -= 8) {
+  for (;;) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       const unsigned long long v = buf[i];
-      if ((v & mask) == prefix) atomicAdd(&hist[(v >> shift) & 255u], 1u);
+      if (v != 0ull && (v & mask) == prefix) atomicAdd(&hist[(v >> shift) & 255u], 1u);
     }
     __syncthreads();
     if (threadIdx.x < 32) {
@@ -232,11 +279,114 @@ __device__ inline void select_threshold(const unsigned long long* buf, int n, in
     __syncthreads();
     const int d = *s_digit, above = *s_above, binc = *s_binc;
     need -= above;
+    // (with shift clamped to 0 the digit overlaps bits already in the prefix; the
+    // counted values agree with it there, so the OR is consistent)
     prefix |= static_cast<unsigned long long>(d) << shift;
     mask |= 0xffull << shift;
     __syncthreads();
-    if (binc == need) break;
+    if (binc == need || shift == 0) break;
+    shift = shift >= 8 ? shift - 8 : 0;
   }
+}
+
+// Keeps the k largest of buf[0, n) (distinct values, k < n) at the front of buf, in
+// order, and returns the smallest kept value (the k-th largest).  MSB-first radix select
+// with 8-bit digits over a per-warp 256-bin histogram, starting at the highest bit in
+// which the values differ (so the first digit already spreads them over the bins).
+// Out of line (rare in the streaming pass); one copy per translation unit.
+static __device__ __noinline__ unsigned long long warp_select_packs(unsigned long long* buf, int n, int k, unsigned* hist, int lane) {
+  const unsigned long long ref = buf[0];
+  unsigned long long dif = 0;
+  for (int i = lane; i < n; i += 32) dif |= buf[i] ^ ref;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dif |= __shfl_xor_sync(kFullMask, dif, o);
+  unsigned long long prefix, mask;
+  if (dif == 0ull) {
+    // all equal (not reached for distinct packs): keep the first k
+    prefix = ref;
+    mask = ~0ull;
+  } else {
+    const int hb = 63 - __clzll(static_cast<long long>(dif));
+    mask = hb == 63 ? 0ull : (~0ull << (hb + 1));
+    prefix = ref & mask;
+    int shift = hb >= 7 ? hb - 7 : 0;
+    int need = k;
+    for (;;) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
+      __syncwarp();
+      for (int i = lane; i < n; i += 32) {
+        const unsigned long long v = buf[i];
+        if ((v & mask) == prefix) atomicAdd(&hist[(v >> shift) & 255u], 1u);
+      }
+      __syncwarp();
+      // lane l owns digits 255-8l .. 248-8l (descending)
+      unsigned c[8];
+      unsigned tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - 8 * lane - j];
+        tot += c[j];
+      }
+      unsigned incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned t = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const unsigned excl = incl - tot;
+      int digit = -1, above = 0, binc = 0;
+      if (excl < static_cast<unsigned>(need) && static_cast<unsigned>(need) <= incl) {
+        unsigned acc = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (digit < 0 && acc + c[j] >= static_cast<unsigned>(need)) {
+            digit = 255 - 8 * lane - j;
+            above = static_cast<int>(acc);
+            binc = static_cast<int>(c[j]);
+          }
+          acc += c[j];
+        }
+      }
+      const unsigned owner = __ballot_sync(kFullMask, digit >= 0);
+      const int src = __ffs(owner) - 1;
+      digit = __shfl_sync(kFullMask, digit, src);
+      above = __shfl_sync(kFullMask, above, src);
+      binc = __shfl_sync(kFullMask, binc, src);
+      need -= above;
+      // (when shift was clamped to 0 the digit overlaps bits already in the prefix; the
+      // counted values agree with the prefix there, so the OR is consistent)
+      prefix |= static_cast<unsigned long long>(digit) << shift;
+      mask |= 0xffull << shift;
+      __syncwarp();
+      if (binc == need || shift == 0) break;
+      shift = shift >= 8 ? shift - 8 : 0;
+    }
+  }
+  // order-preserving compaction of the kept values to the front
+  unsigned long long kth = ~0ull;
+  int base = 0;
+  for (int i0 = 0; i0 < n && base < k; i0 += 32) {
+    const int i = i0 + lane;
+    const unsigned long long v = i < n ? buf[i] : 0ull;
+    const bool keep0 = i < n && (v & mask) >= prefix;
+    const unsigned b0 = __ballot_sync(kFullMask, keep0);
+    const int rank = __popc(b0 & ((1u << lane) - 1u));
+    const bool keep = keep0 && base + rank < k;
+    __syncwarp();
+    if (keep) {
+      buf[base + rank] = v;
+      kth = v < kth ? v : kth;
+    }
+    base += __popc(b0);
+    __syncwarp();
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(kFullMask, kth, o);
+    kth = t < kth ? t : kth;
+  }
+  return kth;
 }
 
 }  // namespace gs

@@ -28,6 +28,7 @@ struct FinShared {
   int s_int[4];
   double red_d[32];
   int red_i[32];
+  float red_f[32];
   unsigned hist[256];
   int sel_digit;
   int sel_above;
@@ -58,7 +59,7 @@ size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap, int work_cap
 }
 
 template <int DT>
-__global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid_constant__ FinalizeArgs A) {
+__global__ void __launch_bounds__(kFinalizeMaxThreads) finalize_kernel(const __grid_constant__ FinalizeArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ FinShared F;
   const int row = blockIdx.x, tid = threadIdx.x, bs = blockDim.x;
@@ -119,54 +120,68 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
   };
   unsigned char* my_rec = part_mode ? A.records + static_cast<int64_t>(row) * A.rec_bytes : nullptr;
 
-  // ---- 0. unit partials ----
-  if (tid == 0) {
+  // ---- 0. unit partials (the units spread over the threads: rows can have many) ----
+  {
     unsigned fl = 0;
     int na = 0, nc = 0;
-    float rm = -INFINITY;
-    for (int u = 0; u < S; ++u) {
+    float rm = -INFINITY, um = -INFINITY;
+    for (int u = tid; u < S; u += bs) {
       const UnitStat& st = unit_stat(u);
       fl |= st.flags;
       na += st.n_allowed;
       nc += st.n_cand;
       rm = fmaxf(rm, st.raw_m);
+      um = fmaxf(um, st.m);
     }
+    if (tid == 0) F.flags = 0;
+    __syncthreads();
+    if (fl) atomicOr(&F.flags, fl);
+    na = block_sum_i(na, F.red_i);
+    nc = block_sum_i(nc, F.red_i);
+    rm = block_max_f(rm, F.red_f);
     double rs = 0.0;
-    if (A.want_raw)
-      for (int u = 0; u < S; ++u) {
+    if (A.want_raw) {
+      for (int u = tid; u < S; u += bs) {
         const UnitStat& st = unit_stat(u);
         if (st.raw_m > -INFINITY) rs = __dadd_rn(rs, __dmul_rn(st.raw_s, exp(static_cast<double>(st.raw_m) - static_cast<double>(rm))));
       }
+      rs = block_sum_d(rs, F.red_d);
+    }
     if (part_mode) {
       // the shard's combined (max, sum): the merge combines shards the same way
-      float m = -INFINITY;
-      for (int u = 0; u < S; ++u) m = fmaxf(m, unit_stat(u).m);
+      const float m = block_max_f(um, F.red_f);
       double sm = 0.0;
-      for (int u = 0; u < S; ++u) {
+      for (int u = tid; u < S; u += bs) {
         const UnitStat& st = unit_stat(u);
         if (st.m > -INFINITY)
           sm = __dadd_rn(sm, __dmul_rn(st.s, exp2(__dmul_rn(static_cast<double>(st.m) - static_cast<double>(m), pp->a2))));
       }
-      UnitStat* h = reinterpret_cast<UnitStat*>(my_rec);
-      h->m = m;
-      h->s = m > -INFINITY ? sm : 0.0;
-      h->raw_m = rm;
-      h->raw_s = rs;
-      h->n_allowed = na;
+      sm = block_sum_d(sm, F.red_d);
+      if (tid == 0) {
+        UnitStat* h = reinterpret_cast<UnitStat*>(my_rec);
+        h->m = m;
+        h->s = m > -INFINITY ? sm : 0.0;
+        h->raw_m = rm;
+        h->raw_s = rs;
+        h->n_allowed = na;
+      }
     }
-    if (has_mask && na == 0 && !part_mode) fl |= GS_FLAG_ERR_DEADEND;
-    if (greedy) fl |= GS_FLAG_GREEDY;
-    F.flags = fl;
-    F.n_allowed = na;
-    F.n_c = nc;
-    F.n_ent = 0;
-    F.n_sort = 0;
-    F.min_pack = ~0ull;
-    F.rec_nc = 0;
-    F.raw_m = rm;
-    F.raw_s = rs;
+    if (tid == 0) {
+      fl = F.flags;
+      if (has_mask && na == 0 && !part_mode) fl |= GS_FLAG_ERR_DEADEND;
+      if (greedy) fl |= GS_FLAG_GREEDY;
+      F.flags = fl;
+      F.n_allowed = na;
+      F.n_c = nc;
+      F.n_ent = 0;
+      F.n_sort = 0;
+      F.min_pack = ~0ull;
+      F.rec_nc = 0;
+      F.raw_m = rm;
+      F.raw_s = rs;
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
   // ---- 1. penalty history: distinct ids with counts, scored exactly ----
   if (merge_mode && !(F.flags & GS_FLAG_ERRORS)) {
@@ -468,16 +483,18 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const __grid
 
 cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
+  // Few rows (fewer CTAs than SMs): more threads per row shorten each row's chain.
+  const int threads = rows < sm_count() ? kFinalizeMaxThreads : kFinalizeThreads;
   if (dtype == GS_DTYPE_F32) {
     const cudaError_t e = cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    finalize_kernel<GS_DTYPE_F32><<<rows, kFinalizeThreads, smem, st>>>(a);
+    finalize_kernel<GS_DTYPE_F32><<<rows, threads, smem, st>>>(a);
   } else {
     const cudaError_t e = cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    finalize_kernel<GS_DTYPE_BF16><<<rows, kFinalizeThreads, smem, st>>>(a);
+    finalize_kernel<GS_DTYPE_BF16><<<rows, threads, smem, st>>>(a);
   }
   return cudaGetLastError();
 }

@@ -118,8 +118,12 @@ inline int64_t shard_record_bytes(int kcap, int hcap) {
 
 // Launch helpers implemented in gs_kernels.cu.
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
+int sm_count();  // SMs of the current device
 size_t stream_smem_bytes(int64_t chunk, int kc);
 cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
+// Warp-per-row merge (topK <= 128, history stride <= 512, not a shard call).
+bool finalize_warp_eligible(const FinalizeArgs& a, int kmax, size_t* smem);
+cudaError_t launch_finalize_warp(const FinalizeArgs& a, int dtype, int rows, int kmax, cudaStream_t st);
 size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap, int work_cap);
 cudaError_t launch_large(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
 size_t large_smem_bytes(int64_t vocab, int hist_cap);
@@ -136,6 +140,7 @@ cudaError_t launch_softcap_digest(uint64_t lo, uint64_t hi, float cap, float inv
 
 constexpr int kStreamThreads = 512;
 constexpr int kFinalizeThreads = 256;
+constexpr int kFinalizeMaxThreads = 1024;  // merge threads per row when rows are few
 constexpr int kLargeThreads = 1024;
 constexpr int kLargeBins = 4096;
 constexpr int kLargeGatherCap = 4096;

@@ -265,7 +265,14 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
     }
   }
   if (L.any_small) {
-    e = launch_finalize(fa, b->dtype, rows, L.fin_smem, st);
+    // One warp per row pays off when the rows fill the GPU (at least two per SM); a few
+    // rows merge faster with a whole CTA each.
+    size_t wsmem = 0;
+    if (rows >= 2 * sm_count() && finalize_warp_eligible(fa, L.kmax, &wsmem)) {
+      e = launch_finalize_warp(fa, b->dtype, rows, L.kmax, st);
+    } else {
+      e = launch_finalize(fa, b->dtype, rows, L.fin_smem, st);
+    }
     if (e != cudaSuccess) return fmt(err, GS_ECUDA, "merge launch: %s", cudaGetErrorString(e));
   }
   if (L.any_large) {

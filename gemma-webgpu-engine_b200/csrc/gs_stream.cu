@@ -445,7 +445,6 @@ int pipe_max_k();
 size_t stream2_smem_bytes(int64_t chunk);
 cudaError_t launch_stream2(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st, int num_sms);
 
-namespace {
 int sm_count() {
   static int counts[64] = {};
   int dev = 0;
@@ -458,8 +457,6 @@ int sm_count() {
   }
   return counts[dev];
 }
-}  // namespace
-
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
   const int units = rows * a.splits;
   if (units == 0) return cudaSuccess;

@@ -55,106 +55,6 @@ static_assert((kStages & (kStages - 1)) == 0, "stage index wraps by mask");
 // Out-of-line soft cap for the rare values outside the polynomial range.
 __device__ __noinline__ float softcap_slow(float x, float cap, float inv_cap) { return softcap(x, cap, inv_cap); }
 
-// Keeps the k largest of buf[0, n) (distinct values, k < n) at the front of buf, in
-// order, and returns the smallest kept value (the k-th largest).  MSB-first radix select
-// with 8-bit digits over a per-warp 256-bin histogram, starting at the highest bit in
-// which the values differ (so the first digit already spreads them over the bins).
-// Rare: kept out of line.
-__device__ __noinline__ unsigned long long warp_select(unsigned long long* buf, int n, int k, unsigned* hist, int lane) {
-  const unsigned long long ref = buf[0];
-  unsigned long long dif = 0;
-  for (int i = lane; i < n; i += 32) dif |= buf[i] ^ ref;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) dif |= __shfl_xor_sync(kFullMask, dif, o);
-  unsigned long long prefix, mask;
-  if (dif == 0ull) {
-    // all equal (not reached for distinct packs): keep the first k
-    prefix = ref;
-    mask = ~0ull;
-  } else {
-    const int hb = 63 - __clzll(static_cast<long long>(dif));
-    mask = hb == 63 ? 0ull : (~0ull << (hb + 1));
-    prefix = ref & mask;
-    int shift = hb >= 7 ? hb - 7 : 0;
-    int need = k;
-    for (;;) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
-      __syncwarp();
-      for (int i = lane; i < n; i += 32) {
-        const unsigned long long v = buf[i];
-        if ((v & mask) == prefix) atomicAdd(&hist[(v >> shift) & 255u], 1u);
-      }
-      __syncwarp();
-      // lane l owns digits 255-8l .. 248-8l (descending)
-      unsigned c[8];
-      unsigned tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[255 - 8 * lane - j];
-        tot += c[j];
-      }
-      unsigned incl = tot;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const unsigned t = __shfl_up_sync(kFullMask, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const unsigned excl = incl - tot;
-      int digit = -1, above = 0, binc = 0;
-      if (excl < static_cast<unsigned>(need) && static_cast<unsigned>(need) <= incl) {
-        unsigned acc = excl;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (digit < 0 && acc + c[j] >= static_cast<unsigned>(need)) {
-            digit = 255 - 8 * lane - j;
-            above = static_cast<int>(acc);
-            binc = static_cast<int>(c[j]);
-          }
-          acc += c[j];
-        }
-      }
-      const unsigned owner = __ballot_sync(kFullMask, digit >= 0);
-      const int src = __ffs(owner) - 1;
-      digit = __shfl_sync(kFullMask, digit, src);
-      above = __shfl_sync(kFullMask, above, src);
-      binc = __shfl_sync(kFullMask, binc, src);
-      need -= above;
-      // (when shift was clamped to 0 the digit overlaps bits already in the prefix; the
-      // counted values agree with the prefix there, so the OR is consistent)
-      prefix |= static_cast<unsigned long long>(digit) << shift;
-      mask |= 0xffull << shift;
-      __syncwarp();
-      if (binc == need || shift == 0) break;
-      shift = shift >= 8 ? shift - 8 : 0;
-    }
-  }
-  // order-preserving compaction of the kept values to the front
-  unsigned long long kth = ~0ull;
-  int base = 0;
-  for (int i0 = 0; i0 < n && base < k; i0 += 32) {
-    const int i = i0 + lane;
-    const unsigned long long v = i < n ? buf[i] : 0ull;
-    const bool keep0 = i < n && (v & mask) >= prefix;
-    const unsigned b0 = __ballot_sync(kFullMask, keep0);
-    const int rank = __popc(b0 & ((1u << lane) - 1u));
-    const bool keep = keep0 && base + rank < k;
-    __syncwarp();
-    if (keep) {
-      buf[base + rank] = v;
-      kth = v < kth ? v : kth;
-    }
-    base += __popc(b0);
-    __syncwarp();
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long t = __shfl_xor_sync(kFullMask, kth, o);
-    kth = t < kth ? t : kth;
-  }
-  return kth;
-}
-
 // Ascending bitonic sort of n2 (power of two, <= kPenCap) 32-bit values by one warp.
 __device__ __noinline__ void warp_sort_u32(uint32_t* v, int n2, int lane) {
   for (int k = 2; k <= n2; k <<= 1)
@@ -422,7 +322,7 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
 
     auto compact = [&]() {
       __syncwarp();
-      const unsigned long long kth = warp_select(wbuf, wcnt, k_eff, whist, lane);
+      const unsigned long long kth = warp_select_packs(wbuf, wcnt, k_eff, whist, lane);
       wtau = kth > wtau ? kth : wtau;
       wcnt = k_eff;
     };

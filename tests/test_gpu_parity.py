@@ -170,12 +170,13 @@ def test_c2_large_path_top_p_full_vocab(pkg, oracle, sampler):
 
 # ------------------------------------------------------------------------ properties
 
-def test_deterministic_replay(pkg, sampler):
-    """Two runs on the same inputs give bitwise identical outputs."""
+@pytest.mark.parametrize("rows", [64, 320], ids=["block-merge", "warp-merge"])
+def test_deterministic_replay(pkg, sampler, rows):
+    """Two runs on the same inputs give bitwise identical outputs (both merge kernels)."""
     import importlib
     import torch
     W = importlib.import_module("gemma-webgpu-engine_b200.workloads")
-    wl = W.make("C4", device="cuda", rows=64)
+    wl = W.make("C4", device="cuda", rows=rows)
     outs = []
     for _ in range(2):
         rng = wl.rng_state("cuda")
@@ -310,6 +311,44 @@ def test_stream_tile_modes(pkg, oracle, sampler, dtype, k, temp, logprob):
         for r in range(rows):
             ref = oracle.token_log_probability(oracle.softcap(x[r], 30.0), int(gpu.ids[r]))
             assert abs(gpu.logprob[r] - ref) <= 1e-6 * max(1.0, abs(ref)), r
+
+
+def test_warp_merge_many_rows(pkg, oracle, sampler):
+    """Enough rows for the warp-per-row merge (>= 2 per SM), per-row params mixing
+    greedy, topK 1..128, min-p, typical-p and top-p, with histories (repeats, masked and
+    out-of-range ids) and masks of graded density, including states allowing fewer ids
+    than topK (the masked-id filler)."""
+    import torch
+    rng = np.random.default_rng(77)
+    V, rows, H = 32768, 320, 96
+    x = (rng.standard_normal((rows, V)) * 2.5).astype(np.float32)
+    x[5, 100:140] = 11.0  # exact ties
+    dens = [0.0004, 0.003, 0.05, 0.5]
+    allowed = rng.random((len(dens), V)) < np.array(dens)[:, None]
+    allowed[0] = False
+    allowed[0, [3, 77, 4000, 30000]] = True  # 4 allowed ids: fewer than most topK
+    table = _pack_words(allowed)
+    mstate = np.array([(i % (len(dens) + 2)) - 2 for i in range(rows)], dtype=np.int32)
+    hist = rng.integers(-5, V + 5, (rows, H)).astype(np.int32)
+    hist[::3, : H // 2] = hist[::3, H // 2:]  # repeats
+    hlen = rng.integers(0, H + 1, rows).astype(np.int32)
+    ps = []
+    for i in range(rows):
+        t = [0.0, 0.7, 1.0, 1.3][i % 4]
+        ps.append({"temperature": t, "topK": [1, 10, 50, 128][(i // 4) % 4], "topP": [0.9, 1.0, 0.5][i % 3],
+                   "minP": [0.0, 0.05][(i // 2) % 2], "typicalP": [1.0, 0.9][(i // 8) % 2],
+                   "repetitionPenalty": 1.15, "presencePenalty": 0.3, "frequencyPenalty": 0.1,
+                   "repetitionWindow": H})
+    u = rng.random(rows)
+    gpu = PU.run_gpu(sampler, x, ps, softcap=30.0, history=hist, history_len=hlen, mask_table=table,
+                     mask_state=mstate, uniforms=u, cand_cap=128)
+    ids, margins, cands, _ = PU.oracle_rows(oracle, x, V, 30.0, ps, history=hist, history_len=hlen,
+                                            mask_table=table, mask_state=mstate, uniforms=u, cand_cap=128)
+    assert PU.compare(gpu, ids, margins, cands, label="warp-merge") <= 3
+    for r in range(rows):
+        ref = oracle.token_log_probability(oracle.softcap(x[r], 30.0), int(gpu.ids[r]))
+        assert abs(gpu.logprob[r] - ref) <= 1e-6 * max(1.0, abs(ref)), r
+    del torch
 
 
 def test_unaligned_row_stride(pkg, oracle, sampler):
