@@ -602,6 +602,7 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     // the next list is full, so the loads are in flight while mask words are scanned.
     int nl = 0;               // offsets listed
     bool inflight = false;    // a launched batch awaits processing
+    bool first_batch = true;  // the unit's first batch sets the top-k threshold
     float pv[kPer];           // its values (loads in flight) ...
     uint32_t po[kPer];        // ... and unit offsets (~0u: empty slot)
     auto launch = [&]() {
@@ -641,11 +642,44 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
         for (int q = 0; q < kPer; ++q) xv[q] = pv[q];
       }
       float lmax = -INFINITY;
+      int nvalid = 0;
 #pragma unroll
       for (int q = 0; q < kPer; ++q) {
-        if (po[q] == 0xffffffffu) xv[q] = -INFINITY;
+        if (po[q] == 0xffffffffu) {
+          xv[q] = -INFINITY;
+        } else {
+          ++nvalid;
+        }
         if (xv[q] != xv[q]) bad = 1u;
         lmax = fmaxf(lmax, xv[q]);
+      }
+      if (k_eff > 1 && first_batch) {
+        // threshold from the unit's first batch (as for a dense unit's first 512 ids): the
+        // largest key K with at least k of the batch's values >= value(K)
+        first_batch = false;
+        nvalid = static_cast<int>(__reduce_add_sync(kFullMask, static_cast<unsigned>(nvalid)));
+        if (nvalid >= k_eff) {
+          const uint32_t kneg = key32(-INFINITY);
+          uint32_t klo = kneg, khi = key32(warp_max(lmax)) + 1u;
+#pragma unroll 1
+          for (int it = 0; it < 14 && khi - klo > 1u; ++it) {
+            const uint32_t mid = klo + ((khi - klo) >> 1);
+            const float v = key32_value(mid);  // > -inf: empty slots and NaN never count
+            int c = 0;
+#pragma unroll
+            for (int q = 0; q < kPer; ++q) c += xv[q] >= v ? 1 : 0;
+            c = static_cast<int>(__reduce_add_sync(kFullMask, static_cast<unsigned>(c)));
+            if (c >= k_eff) {
+              klo = mid;
+            } else {
+              khi = mid;
+            }
+          }
+          if (klo != kneg) {
+            const unsigned long long t0b = (static_cast<unsigned long long>(klo) << 32) - 1ull;
+            wtau = t0b > wtau ? t0b : wtau;
+          }
+        }
       }
       if (do_sum) {
         rescale(warp_max(lmax));
@@ -675,12 +709,18 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
             }
           }
       } else if (k_eff > 1) {
+        const float tau0 = tau_value();
+        bool any = false;
 #pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-          const float tau_x = tau_value();
-          bool pend = po[q] != 0xffffffffu && xv[q] >= tau_x;
-          const unsigned long long pk = pend ? make_pack(xv[q], id_base + po[q]) : 0ull;
-          while (__any_sync(kFullMask, pend)) pend = !offer(pend, pk);
+        for (int q = 0; q < kPer; ++q) any |= xv[q] >= tau0;
+        if (__any_sync(kFullMask, any)) {
+#pragma unroll
+          for (int q = 0; q < kPer; ++q) {
+            const float tau_x = tau_value();
+            bool pend = po[q] != 0xffffffffu && xv[q] >= tau_x;
+            const unsigned long long pk = pend ? make_pack(xv[q], id_base + po[q]) : 0ull;
+            while (__any_sync(kFullMask, pend)) pend = !offer(pend, pk);
+          }
         }
       }
       inflight = false;
