@@ -278,6 +278,11 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     const bool do_sum = pp->mode != kModeGreedy;
     const double a2 = pp->a2;
     const float a2_hi = pp->a2_hi, a2_lo = pp->a2_lo;
+    // Terms are taken against the running reference m_t while no value exceeds it by more
+    // than dlim (then a term is at most 2^2 and its exponent keeps full float accuracy);
+    // the warp-wide maximum and the rescale run only when some lane crosses that limit,
+    // and the unit's true maximum is settled once, at its end.
+    const float dlim = do_sum ? static_cast<float>(2.0 / a2) : 0.0f;
     const unsigned char* rowp = logits + (static_cast<int64_t>(row) * A.row_stride + g.lo) * ESZ;
     uint32_t uflags = (A.mask_table != nullptr && g.state >= A.mask_states) ? GS_FLAG_ERR_INVALID : 0u;
     const uint32_t id_base = static_cast<uint32_t>(A.vocab_offset + g.lo);
@@ -309,7 +314,8 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     __syncwarp();
     int pen_cur = 0;
 
-    float m_t = -INFINITY, rm_t = -INFINITY;  // warp-uniform running maxima
+    float m_t = -INFINITY, rm_t = -INFINITY;  // warp-uniform running maxima (m_t: the sum's reference)
+    float lmx = -INFINITY;                    // this lane's maximum of the live values
     double s_t = 0.0, rs_t = 0.0;             // per-lane sums relative to m_t / rm_t
     uint32_t bad = 0;
     int na = 0;
@@ -486,7 +492,8 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
           }
         }
         if (do_sum) {
-          rescale(warp_max(tmax));
+          lmx = fmaxf(lmx, tmax);
+          if (__any_sync(kFullMask, tmax > m_t + dlim)) rescale(warp_max(tmax));
           if (m_t > -INFINITY) {
             // NaN and +inf reach the sum (as NaN); dead ids are -inf and add 0
             float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
@@ -532,7 +539,10 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
         }
         rmax = fmaxf(rmax, x);
       }
-      if (do_sum) rescale(warp_max(lmax));
+      if (do_sum) {
+        lmx = fmaxf(lmx, lmax);
+        rescale(warp_max(lmax));
+      }
       if (want_raw) rescale_raw(warp_max(rmax));
       float acc = 0.0f, racc = 0.0f;
       for (int i0 = 0; i0 < cnt; i0 += 32) {  // warp-uniform
@@ -682,7 +692,8 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
         }
       }
       if (do_sum) {
-        rescale(warp_max(lmax));
+        lmx = fmaxf(lmx, lmax);
+        if (__any_sync(kFullMask, lmax > m_t + dlim)) rescale(warp_max(lmax));
         if (m_t > -INFINITY) {
           float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll
@@ -898,6 +909,7 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
       ncand = b != 0ull ? 1 : 0;
       if (lane == 0 && b != 0ull) A.cands[static_cast<int64_t>(unit) * A.kcap] = b;
     }
+    if (do_sum) rescale(warp_max(lmx));  // the unit's true maximum (s_t rescaled onto it)
     const double c = warp_sum(s_t);
     const double rc = warp_sum(rs_t);
     na = g.masked ? warp_sum_i(na) : na;
