@@ -293,15 +293,24 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     if (hl < 0) hl = 0;
     const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
     int pen_n = 0;
-    for (int64_t j0 = 0; j0 < hl; j0 += 32) {
-      const int64_t j = j0 + lane;
-      int64_t off = -1;
-      if (j < hl) off = static_cast<int64_t>(hrow[j]) - A.vocab_offset - g.lo;
-      const bool in = off >= 0 && off < g.n;
-      const unsigned b = __ballot_sync(kFullMask, in);
-      const int at = pen_n + __popc(b & lane_lt);
-      if (in && at < kPenCap) pen[at] = static_cast<uint32_t>(off);
-      pen_n += __popc(b);
+    for (int64_t j0 = 0; j0 < hl; j0 += 128) {  // four loads per lane in flight
+      int32_t hv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int64_t j = j0 + q * 32 + lane;
+        hv[q] = j < hl ? hrow[j] : 0;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int64_t j = j0 + q * 32 + lane;
+        int64_t off = -1;
+        if (j < hl) off = static_cast<int64_t>(hv[q]) - A.vocab_offset - g.lo;
+        const bool in = off >= 0 && off < g.n;
+        const unsigned b = __ballot_sync(kFullMask, in);
+        const int at = pen_n + __popc(b & lane_lt);
+        if (in && at < kPenCap) pen[at] = static_cast<uint32_t>(off);
+        pen_n += __popc(b);
+      }
     }
     const bool pen_scan = pen_n > kPenCap;
     if (!pen_scan && pen_n > 1) {

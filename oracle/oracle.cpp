@@ -323,12 +323,14 @@ void oracle_mask_constraint_logits(const float* raw_logits, int64_t vocab,
 // IEEE single operations so that every compliant implementation gives the same bits.
 // The reference runtime never applies it (the Gemma manifest declares 30, the LM head
 // writes uncapped logits); the benchmark configurations apply it when making inputs.
-// Method: y = x * fl(1/c), z = fl(y·y).  z < 0.390625 (exactly |y| < 0.625) uses the
-// odd polynomial evaluated on the signed y, c·fma(y·z, Q(z), y) (a least-squares/Lawson
-// minimax fit, coefficients below; a zero y gives +0); otherwise 0.625 <= |y| < 9 uses
-// t = 1 - 2/(e^{2|y|} + 1) with e^z by Cody–Waite reduction z = n·ln2 + r and a
-// degree-6 polynomial for e^r, |y| >= 9 gives t = 1, and the result is c·copysign(t, y).
-static const float kTanhQ[5] = {-0.3333328f, 0.13331442f, -0.05373972f, 0.02063909f, -0.00570499f};
+// Method: y = x * fl(1/c), z = fl(y·y).  z < 1 (exactly |y| < 1) uses the odd
+// polynomial evaluated on the signed y, c·fma(y·z, Q(z), y) with Q of degree 6 (a
+// least-squares/Lawson minimax fit, coefficients below; a zero y gives +0); otherwise
+// 1 <= |y| < 9 uses t = 1 - 2/(e^{2|y|} + 1) with e^z by Cody–Waite reduction
+// z = n·ln2 + r and a degree-6 polynomial for e^r, |y| >= 9 gives t = 1, and the result
+// is c·copysign(t, y).
+static const float kTanhQ[7] = {-0.33333296f, 0.13332345f, -0.0538798f, 0.021486657f,
+                                -0.007946107f, 0.0023013647f, -0.00035845203f};
 static const float kExpB[5] = {0.49999994f, 0.1666652f, 0.04166841f, 0.00836891f, 0.00138142f};
 static const float kLn2Hi = 0.693145751953125f;     // 0x3f317200
 static const float kLn2Lo = 1.428606765330187e-06f; // ln2 - kLn2Hi
@@ -356,8 +358,10 @@ float oracle_softcap(float x, float cap, float inv_cap) {
   if (x != x) return x;
   float y = x * inv_cap;
   float z = y * y;
-  if (z < 0.390625f) {
-    float q = kTanhQ[4];
+  if (z < 1.0f) {
+    float q = kTanhQ[6];
+    q = std::fmaf(q, z, kTanhQ[5]);
+    q = std::fmaf(q, z, kTanhQ[4]);
     q = std::fmaf(q, z, kTanhQ[3]);
     q = std::fmaf(q, z, kTanhQ[2]);
     q = std::fmaf(q, z, kTanhQ[1]);
@@ -377,6 +381,51 @@ float oracle_softcap(float x, float cap, float inv_cap) {
 
 void oracle_softcap_array(const float* in, float* out, int64_t n, float cap, float inv_cap) {
   for (int64_t i = 0; i < n; ++i) out[i] = oracle_softcap(in[i], cap, inv_cap);
+}
+
+// Exhaustive check of softcap over every positive float32 input (the routine is odd):
+// the largest error in ulps of the float32 result against c·tanh(x/c) in double (where
+// x/c is a normal float), and the number of adjacent inputs whose results decrease
+// (0: monotone).
+void oracle_softcap_check(float cap, int threads, double* max_ulp, uint64_t* decreases) {
+  const float inv = static_cast<float>(1.0 / static_cast<double>(cap));
+  if (threads < 1) threads = 1;
+  const uint64_t lo = 0, hi = 0x7f800000ull;  // +0 .. largest finite
+  std::vector<double> worst(static_cast<size_t>(threads), 0.0);
+  std::vector<uint64_t> dec(static_cast<size_t>(threads), 0);
+  std::vector<std::thread> pool;
+  const uint64_t span = (hi - lo + threads - 1) / threads;
+  for (int t = 0; t < threads; ++t) {
+    pool.emplace_back([&, t] {
+      const uint64_t a = lo + span * t, b = std::min(hi, a + span);
+      double w = 0.0;
+      uint64_t d = 0;
+      float prev = 0.0f;
+      for (uint64_t u = a; u <= b && u < hi; ++u) {  // (b: the next chunk's first input)
+        const uint32_t xb = static_cast<uint32_t>(u);
+        float x;
+        std::memcpy(&x, &xb, 4);
+        const float y = oracle_softcap(x, cap, inv);
+        if (u > a && y < prev) ++d;
+        prev = y;
+        if (x < 1e-30f) continue;
+        const double ref = static_cast<double>(cap) * std::tanh(static_cast<double>(x) / static_cast<double>(cap));
+        const float rf = static_cast<float>(ref);
+        const double ulp = static_cast<double>(std::nextafter(std::fabs(rf), INFINITY) - std::fabs(rf));
+        const double e = std::fabs(static_cast<double>(y) - ref) / ulp;
+        if (e > w) w = e;
+      }
+      worst[t] = w;
+      dec[t] = d;
+    });
+  }
+  for (auto& th : pool) th.join();
+  *max_ulp = 0.0;
+  *decreases = 0;
+  for (int t = 0; t < threads; ++t) {
+    *max_ulp = std::max(*max_ulp, worst[t]);
+    *decreases += dec[t];
+  }
 }
 
 // Order-independent 64-bit digest of softcap over the bit patterns [lo, hi) (used to

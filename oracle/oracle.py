@@ -87,6 +87,9 @@ def lib():
         L.oracle_softcap_array.argtypes = [P, P, ctypes.c_int64, ctypes.c_float, ctypes.c_float]
         L.oracle_softcap_digest.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float, ctypes.c_int]
         L.oracle_softcap_digest.restype = ctypes.c_uint64
+        L.oracle_softcap_check.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
+                                           ctypes.POINTER(ctypes.c_uint64)]
+        L.oracle_softcap_check.restype = None
         L.oracle_sample_rows.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                          P, ctypes.c_int64, P, P, ctypes.c_int64, P,
                                          P, ctypes.c_int32, P, P, P, P, ctypes.c_int]
@@ -190,6 +193,16 @@ def softcap_digest(lo: int, hi: int, cap: float, threads: int = 0) -> int:
     if threads <= 0:
         threads = os.cpu_count() or 1
     return int(lib().oracle_softcap_digest(lo, hi, float(np.float32(cap)), float(inv), threads))
+
+
+def softcap_check(cap: float, threads: int = 0) -> tuple[float, int]:
+    """(largest error in ulps against cap·tanh(x/cap), number of decreasing steps) over
+    every positive float32 input."""
+    if threads <= 0:
+        threads = os.cpu_count() or 1
+    u, d = ctypes.c_double(), ctypes.c_uint64()
+    lib().oracle_softcap_check(float(np.float32(cap)), threads, ctypes.byref(u), ctypes.byref(d))
+    return u.value, int(d.value)
 
 
 def sample_rows(logits: np.ndarray, vocab: int, softcap_value: float, history: np.ndarray | None,
