@@ -221,8 +221,6 @@ gs_status run_call(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stre
     cudaEventRecord(c->plans_ev, st);
     c->plans_ev_live = true;
   }
-  UnitStat* stats = reinterpret_cast<UnitStat*>(c->ws + L.stats_off);
-  unsigned long long* cands = reinterpret_cast<unsigned long long*>(c->ws + L.cands_off);
   std::array<cudaEvent_t, 3> evs{};
   if (c->profile) {
     for (auto& ev : evs) {
@@ -236,8 +234,7 @@ gs_status run_call(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stre
     }
   }
   gs_outputs none{};
-  s = launch_sampling(b, o ? o : &none, L, plan0, dplans, stats, cands, st, c->profile ? evs.data() : nullptr,
-                      &c->err, sh);
+  s = launch_sampling(b, o ? o : &none, L, plan0, dplans, c->ws, st, c->profile ? evs.data() : nullptr, &c->err, sh);
   if (s != GS_OK) return s;
   if (c->profile) c->ev_live.push_back(evs);
   return GS_OK;

@@ -104,6 +104,10 @@ struct FinalizeArgs {
   int32_t rec_kcap;       // candidate packs per record
   int32_t rec_hcap;       // penalised-entry slots per record
   unsigned char* records; // mode 1: out [rows] records; mode 2: in [shards][rows] records
+  // histogram path (topK 0 or > GS_MAX_TOP_K): per-row workspace
+  unsigned char* lws;     // [rows] blocks of lrow_bytes
+  int64_t lrow_bytes;
+  int32_t lslots;         // penalised-entry slots per row (the history stride)
 };
 
 // Per-row record of one vocabulary shard (gs_shard_partials writes, gs_shard_merge reads):
@@ -125,8 +129,10 @@ cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t s
 bool finalize_warp_eligible(const FinalizeArgs& a, int kmax, size_t* smem);
 cudaError_t launch_finalize_warp(const FinalizeArgs& a, int dtype, int rows, int kmax, cudaStream_t st);
 size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap, int work_cap);
-cudaError_t launch_large(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
-size_t large_smem_bytes(int64_t vocab, int hist_cap);
+// Histogram path: hist (clusters of 8 CTAs), select, gather and resolve launches.
+cudaError_t launch_large(const FinalizeArgs& a, int dtype, int rows, size_t select_smem, cudaStream_t st);
+size_t large_row_bytes(int64_t slots);                  // per-row workspace of the histogram path
+size_t large_select_smem_bytes(int64_t history_stride); // shared memory of its select kernel
 cudaError_t launch_logprob(const void* logits, int dtype, int rows, int64_t vocab, int64_t stride,
                            float softcap, float inv_softcap, const int32_t* tokens, double* out,
                            int32_t* bad, cudaStream_t st);
@@ -141,8 +147,5 @@ cudaError_t launch_softcap_digest(uint64_t lo, uint64_t hi, float cap, float inv
 constexpr int kStreamThreads = 512;
 constexpr int kFinalizeThreads = 256;
 constexpr int kFinalizeMaxThreads = 1024;  // merge threads per row when rows are few
-constexpr int kLargeThreads = 1024;
-constexpr int kLargeBins = 4096;
-constexpr int kLargeGatherCap = 4096;
 
 }  // namespace gs

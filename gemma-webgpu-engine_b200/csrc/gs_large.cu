@@ -1,60 +1,112 @@
 // Kernel 3: the histogram path, for rows whose candidate list is not bounded by a small
-// topK (topK == 0 or topK > GS_MAX_TOP_K with V > GS_MAX_TOP_K).  One CTA per row.
+// topK (topK == 0 or topK > GS_MAX_TOP_K with V > GS_MAX_TOP_K).
 //
 // The reference keeps the whole sorted vocabulary as candidates (src/runtime/sampling.ts:44)
 // and then cuts prefixes of it: min-p (:45-48, a prefix because p falls along the order),
 // top-p (:56, cumulativeCut :82-90) and the draw (:58-64).  Every one of these is a
 // position in the sorted order where a running count or a running probability crosses a
-// value.  Instead of sorting 262144 entries, this kernel:
-//   1. builds a histogram of count and probability mass over 2048 bins of logit distance
-//      below the row maximum (monotone in the sort key, so bins hold contiguous ranges of
-//      the reference's order);
-//   2. finds the bin where the running value crosses the target;
-//   3. gathers only that bin's elements, sorts them exactly (logit/T desc, id asc) and
-//      resolves the crossing with exact double probabilities.
-// Masses are accumulated in 2^-44 fixed point so that the sums are order-independent and
-// the result is bit-reproducible.  Decisions within 1e-6 of a boundary are flagged.
+// value.  Instead of sorting 262144 entries, the path finds the crossings from a
+// histogram and sorts only the few bins that hold them.  Four launches follow the
+// streaming pass (which has produced each unit's live maximum and sum):
+//   hist     a cluster of 8 CTAs per row, each streaming an eighth of the row into a
+//            4096-bin histogram over logit/T distance below the row's live maximum
+//            (monotone in the sort key, so a bin holds a contiguous range of the
+//            reference's order): per bin the count of live values and the sum of
+//            q = round((1 - e^-delta)·2^qbits), delta the value's key distance below the
+//            bin's top, so that the bin's mass is e^(top - M)·(count - sum q·2^-qbits)
+//            with 32-bit shared-memory atomics only.  The eight histograms are summed
+//            through distributed shared memory;
+//   select   one CTA per row: the penalised ids (distinct history ids counted in a
+//            shared-memory hash table, scored exactly in double), the row maximum M, the
+//            full-vocabulary normaliser, the binned masses and their prefix sums, and the
+//            bins that can hold each crossing (min-p, topK, top-p, the draw, the head of
+//            the candidate list);
+//   gather   many CTAs per row append the live ids of the selected bins to a row list;
+//   resolve  one CTA per row places the list bin by bin, sorts each bin exactly
+//            (logit/T descending, lower id first) and resolves the crossings with exact
+//            double probabilities, walking from the binned prefix at each bin's start.
+// Sums are integer (fixed point) or taken in a fixed order, so the result is
+// bit-reproducible.  Decisions within 1e-6 of a boundary are flagged.
+#include <cooperative_groups.h>
+
+#include <climits>
+
 #include "gs_device.cuh"
 #include "gs_block.cuh"
 #include "gs_internal.cuh"
 #include "../../include/gsampler.h"
 
+namespace cg = cooperative_groups;
+
 namespace gs {
 
 namespace {
 
-constexpr int kNB = 2048;             // histogram bins
-constexpr double kRangeKeys = 48.0;   // bins span 48 units of logit/T below the maximum
-constexpr double kFix = 17592186044416.0;  // 2^44
+constexpr int kNB = 4096;              // histogram bins
+constexpr double kRangeKeys = 40.0;    // bins span 40 units of logit/T below the maximum
+constexpr int kCluster = 8;            // histogram CTAs per row (one cluster)
+constexpr int kHistThreads = 512;
+constexpr int kHistSub = 32768;        // ids per live-bitmap pass of a histogram CTA
+constexpr int kSelectThreads = 1024;
+constexpr int kGatherThreads = 256;
+constexpr int kGatherIds = 16384;      // ids per gather CTA
+constexpr int kResolveThreads = 1024;
+constexpr int kGCap = 8192;            // entries of the selected bins per row
+constexpr int kWarpSortMax = 1024;     // larger bins are sorted by the whole CTA
 constexpr double kBoundary = 1e-6;
+constexpr double kSelMargin = 4e-6;    // relative slack when bins are picked from binned masses
+constexpr float kMaxDelta = 0.0105f;   // bin width (40/4096 key units) plus slack
+constexpr size_t kSelUnion = (static_cast<size_t>(kNB + 1) * 12 + 15) / 16 * 16;  // select: start of its union
+static_assert(kNB / kCluster == kHistThreads, "one reduced bin per thread and cluster rank");
+static_assert(kNB == 4 * kSelectThreads && kNB == 4 * kResolveThreads, "four bins per thread");
 
-struct LShared {
+// Per-row header shared by the four kernels (256-byte slot).
+struct LargeRow {
   unsigned flags;
-  int n_allowed;
-  int n_pen;
-  int g_n;
-  int g_lo;
-  int g_hi;
-  int n_neginf;
-  float Mx;
+  int32_t n_allowed;
+  int32_t n_slots;   // penalised-entry slots (the row's history length)
+  int32_t n_fin;     // finite candidates: live values and penalised entries
+  int32_t g_count;   // entries the gather kernel appended
+  int32_t g_need;    // entries (live and penalised) of the selected bins
+  int32_t mp_lo;     // min-p bins [mp_lo, mp_hi], -1 without min-p
+  int32_t mp_hi;
+  float Mx;          // maximum over live values (allowed and not penalised)
   float raw_m;
   double raw_s;
-  double M;
-  double total;
-  double f0;
-  double uniform;
-  int sres[8];
-  double sresd[4];
-  double red_d[32];
-  int red_i[32];
-  unsigned long long red_u[32];
+  double M;          // maximum key (logit/T) over live values and penalised entries
+  double total;      // full-vocabulary normaliser relative to M
+  double uniform;    // the draw's uniform
+  double rng_next;   // the PRNG state after the draw
+};
+static_assert(sizeof(LargeRow) <= 256, "header fits its slot");
+
+// Per-row workspace: header | selected-bin bitmap | count prefix | mass prefix |
+// penalised entries | gathered entries.
+constexpr size_t kOffSel = 256;
+constexpr size_t kOffCpre = kOffSel + kNB / 8;
+constexpr size_t kOffPpre = (kOffCpre + (kNB + 1) * 4 + 15) / 16 * 16;
+constexpr size_t kOffPen = (kOffPpre + (kNB + 1) * 8 + 15) / 16 * 16;
+
+struct RowWs {
+  LargeRow* hdr;
+  uint32_t* sel;   // [kNB / 32]
+  uint32_t* cpre;  // [kNB + 1] entries before bin b (the hist kernel leaves counts here)
+  double* ppre;    // [kNB + 1] probability before bin b (the hist kernel leaves q sums here)
+  Ent* pen;        // [n_slots] penalised entries (id 0xffffffff: empty slot)
+  uint2* gath;     // [kGCap] {float bits of the soft-capped logit, id}
 };
 
-struct LArgs {
-  int nwords;
-  int pen_cap;
-  int gcap;
-};
+__device__ __forceinline__ RowWs row_ws(const FinalizeArgs& A, int row) {
+  unsigned char* b = A.lws + static_cast<size_t>(row) * A.lrow_bytes;
+  RowWs w;
+  w.hdr = reinterpret_cast<LargeRow*>(b);
+  w.sel = reinterpret_cast<uint32_t*>(b + kOffSel);
+  w.cpre = reinterpret_cast<uint32_t*>(b + kOffCpre);
+  w.ppre = reinterpret_cast<double*>(b + kOffPpre);
+  w.pen = reinterpret_cast<Ent*>(b + kOffPen);
+  w.gath = reinterpret_cast<uint2*>(b + kOffPen + static_cast<size_t>(A.lslots) * sizeof(Ent));
+  return w;
+}
 
 __device__ __forceinline__ int bin_of(float x, float Mx, float scale) {
   const float d = Mx - x;
@@ -63,566 +115,1171 @@ __device__ __forceinline__ int bin_of(float x, float Mx, float scale) {
   return b >= static_cast<float>(kNB - 1) ? kNB - 1 : static_cast<int>(b);
 }
 
-}  // namespace
+__device__ __forceinline__ float bin_scale(double T) { return static_cast<float>(static_cast<double>(kNB) / (kRangeKeys * T)); }
+__device__ __forceinline__ float bin_width_logit(double T) { return static_cast<float>(kRangeKeys * T / kNB); }
 
-size_t large_smem_bytes(int64_t vocab, int hist_cap) {
-  const size_t nwords = (static_cast<size_t>((vocab + 31) / 32) + 3) & ~static_cast<size_t>(3);
-  const size_t pen = static_cast<size_t>(hist_cap) * sizeof(Ent);
-  const size_t bins = (kNB + 1) * 4 + (kNB + 1) * 8;
-  const size_t gather = static_cast<size_t>(kLargeGatherCap) * (sizeof(Ent) + 8);
-  return nwords * 4 + ((bins + 15) & ~static_cast<size_t>(15)) + pen + gather + 64;
+// Ids of a histogram CTA: an eighth of the row, a multiple of 128.
+__host__ __device__ inline int64_t hist_chunk(int64_t V) {
+  const int64_t c = (V + kCluster - 1) / kCluster;
+  return (c + 127) / 128 * 128;
 }
 
+// Bits of q (see the file comment): a histogram CTA sums at most hist_chunk(V) values of
+// q <= kMaxDelta · 2^qbits in 32 bits.
+__host__ __device__ inline int q_bits(int64_t V) {
+  const int64_t hc = hist_chunk(V);
+  int lg = 0;
+  while ((1ll << lg) < hc) ++lg;
+  return lg <= 15 ? 22 : 37 - lg;
+}
+
+__device__ __forceinline__ uint32_t hash_id(uint32_t v) { return v * 2654435761u; }
+
+__device__ __forceinline__ double block_max_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFullMask, v, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double m = -INFINITY;
+  for (int w = 0; w < nw; ++w) m = fmax(m, red[w]);
+  __syncthreads();
+  return m;
+}
+
+__device__ __forceinline__ int block_min_i(int v, int* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(kFullMask, v, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  int m = INT_MAX;
+  for (int w = 0; w < nw; ++w) m = min(m, red[w]);
+  __syncthreads();
+  return m;
+}
+
+// Live bits of ids [lo, lo + n) of a row: allowed by the mask and not in the history.
+__device__ __forceinline__ void build_live(uint32_t* live, const uint32_t* mrow, int64_t lo, int n, const int32_t* hrow,
+                                           int64_t hl, int t, int nt) {
+  const int words = (n + 31) >> 5;
+  for (int w = t; w < words; w += nt) {
+    uint32_t m = mrow ? __ldg(mrow + (lo >> 5) + w) : 0xffffffffu;
+    if (w == words - 1 && (n & 31)) m &= (1u << (n & 31)) - 1u;
+    live[w] = m;
+  }
+  __syncthreads();
+  for (int64_t j = t; j < hl; j += nt) {
+    const int64_t off = static_cast<int64_t>(hrow[j]) - lo;
+    if (off >= 0 && off < n) atomicAnd(&live[off >> 5], ~(1u << (off & 31)));
+  }
+  __syncthreads();
+}
+
+// In-place sort of e[0, n) into ent_before order by threads t of nt: a bitonic network
+// whose every comparator puts the earlier entry at the lower index, so that entries
+// past n behave as padding that sorts last and their comparators can be skipped.
+template <bool kBlock>
+__device__ void seg_sort(Ent* e, int n, int t, int nt) {
+  if (n < 2) return;
+  int lg = 0;
+  while ((1 << lg) < n) ++lg;
+  const int half_n2 = 1 << (lg - 1);
+  for (int lk = 1; lk <= lg; ++lk) {
+    for (int lj = lk - 1; lj >= 0; --lj) {
+      // lj == lk - 1: the flip stage (partner i ^ (2^lk - 1)); below it the half-cleaners
+      for (int q = t; q < half_n2; q += nt) {
+        const int i = ((q >> lj) << (lj + 1)) | (q & ((1 << lj) - 1));
+        const int p = lj == lk - 1 ? (i ^ ((1 << lk) - 1)) : (i + (1 << lj));
+        if (p < n) {
+          const Ent a = e[i], b = e[p];
+          if (ent_before(b, a)) {
+            e[i] = b;
+            e[p] = a;
+          }
+        }
+      }
+      if (kBlock) __syncthreads();
+      else __syncwarp();
+    }
+  }
+}
+
+}  // namespace
+
+size_t large_row_bytes(int64_t slots) {
+  const size_t gath = kOffPen + static_cast<size_t>(slots) * sizeof(Ent);
+  return (gath + static_cast<size_t>(kGCap) * 8 + 255) / 256 * 256;
+}
+
+size_t large_select_smem_bytes(int64_t history_stride) {
+  int64_t h2 = 64;
+  while (h2 < 2 * history_stride) h2 <<= 1;
+  const size_t hash = static_cast<size_t>(h2) * 12;
+  const size_t pen_bins = static_cast<size_t>(kNB) * 12;  // fixed-point masses and counts of penalised entries
+  return kSelUnion + (hash > pen_bins ? hash : pen_bins);
+}
+
+// ============================================================================ hist
+// One cluster of kCluster CTAs per row.  Each CTA streams hist_chunk(V) ids of the row;
+// rank r then sums bins [r·512, (r+1)·512) of the cluster's histograms and writes them to
+// the row's workspace (counts over the count prefix array, q sums over the mass prefix
+// array; the select kernel reads both and rewrites them with the prefix sums).
 template <int DT>
-__global__ void __launch_bounds__(kLargeThreads) large_kernel(const __grid_constant__ FinalizeArgs A) {
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads)
+    large_hist_kernel(const __grid_constant__ FinalizeArgs A) {
+  __shared__ uint32_t cnt[kNB];
+  __shared__ uint32_t qs[kNB];
+  __shared__ uint32_t live[kHistSub / 32];
+  __shared__ float red_f[32];
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = static_cast<int>(cl.block_rank());
+  const int row = blockIdx.x / kCluster;
+  const int tid = threadIdx.x, bs = blockDim.x;
+  const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
+  if (pp->mode != kModeLarge || pp->typical_p < 1) return;  // the whole cluster (one row)
+  const RowWs W = row_ws(A, row);
+  // the row's live maximum from the streaming pass's unit statistics
+  const int S = A.splits;
+  float mx = -INFINITY;
+  int err = 0;
+  for (int u = tid; u < S; u += bs) {
+    const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+    mx = fmaxf(mx, st.m);
+    err |= (st.flags & GS_FLAG_ERRORS) != 0;
+  }
+  if (__syncthreads_or(err)) return;  // the same decision in every CTA of the cluster
+  const float Mx = block_max_f(mx, red_f);
+  const double T = pp->temperature;
+  const float scale = bin_scale(T), width = bin_width_logit(T), invT = static_cast<float>(1.0 / T);
+  const float qmul = static_cast<float>(ldexp(1.0, q_bits(A.vocab)));
+  const int64_t V = A.vocab;
+  const int64_t hc = hist_chunk(V);
+  const int64_t lo = rank * hc;
+  const int n = static_cast<int>(V - lo < 0 ? 0 : (V - lo < hc ? V - lo : hc));
+  const int32_t state = A.mask_state ? A.mask_state[row] : -1;
+  const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
+  const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
+  constexpr int ESZ = DT == GS_DTYPE_F32 ? 4 : 2;
+  constexpr int VE = 16 / ESZ;
+  const unsigned char* rowbase = static_cast<const unsigned char*>(A.logits) + static_cast<int64_t>(row) * A.row_stride * ESZ;
+  const float cap = A.softcap, inv_cap = A.inv_softcap;
+  int64_t hl = A.history_len ? A.history_len[row] : 0;
+  if (hl > A.history_stride) hl = A.history_stride;
+  if (hl < 0) hl = 0;
+  const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
+
+  for (int b = tid; b < kNB; b += bs) {
+    cnt[b] = 0;
+    qs[b] = 0;
+  }
+  // one live value: its bin's count and q
+  auto add = [&](float raw) {
+    const float x = cap != 0.0f ? softcap(raw, cap, inv_cap) : raw;
+    if (!(x > -INFINITY)) return;  // -inf: not a finite candidate (NaN rows are flagged)
+    const float d = Mx - x;
+    int b = 0;
+    if (d > 0.0f) {
+      const float t = d * scale;
+      b = t >= static_cast<float>(kNB - 1) ? kNB - 1 : static_cast<int>(t);
+    }
+    atomicAdd(&cnt[b], 1u);
+    if (b < kNB - 1) {  // the deepest bin's mass (below e^-40 of the top) is taken as 0
+      float dl = fmaf(-static_cast<float>(b), width, d) * invT;
+      dl = fminf(fmaxf(dl, 0.0f), kMaxDelta);
+      // 1 - e^-dl by its Taylor series (dl <= 0.0105: the truncation is below 1e-12)
+      const float om = dl * (1.0f - 0.5f * dl * (1.0f - (1.0f / 3.0f) * dl * (1.0f - 0.25f * dl)));
+      const uint32_t q = __float2uint_rn(om * qmul);
+      if (q) atomicAdd(&qs[b], q);
+    }
+  };
+  for (int s0 = 0; s0 < n; s0 += kHistSub) {
+    const int sn = n - s0 < kHistSub ? n - s0 : kHistSub;
+    __syncthreads();
+    build_live(live, mrow, lo + s0, sn, hrow, hl, tid, bs);
+    const unsigned char* base = rowbase + (lo + s0) * ESZ;
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+      const int nv = sn / VE;
+      const uint4* v4 = reinterpret_cast<const uint4*>(base);
+      for (int v0 = tid; v0 < nv; v0 += 4 * bs) {  // four vectors per thread in flight
+        uint4 r[4];
+        uint32_t bits[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int vi = v0 + u * bs;
+          bits[u] = vi < nv ? (live[(vi * VE) >> 5] >> ((vi * VE) & 31)) & ((1u << VE) - 1u) : 0u;
+          if (bits[u]) r[u] = ld_stream_u4(v4 + vi);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (!bits[u]) continue;
+          const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+          for (int i = 0; i < VE; ++i)
+            if ((bits[u] >> i) & 1u)
+              add(DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1])));
+        }
+      }
+      done = nv * VE;
+    }
+    for (int i = done + tid; i < sn; i += bs)
+      if ((live[i >> 5] >> (i & 31)) & 1u) add(load_logit(base, DT, i));
+  }
+  cl.sync();
+  {
+    const int b = rank * kHistThreads + tid;
+    uint32_t c = 0;
+    unsigned long long q = 0;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) {
+      c += cl.map_shared_rank(cnt, r)[b];
+      q += cl.map_shared_rank(qs, r)[b];
+    }
+    W.cpre[b] = c;
+    reinterpret_cast<unsigned long long*>(W.ppre)[b] = q;
+  }
+  cl.sync();  // every CTA keeps its shared memory until its peers have read it
+}
+
+// ============================================================================ select
+// One CTA per row: the row's statistics, its penalised entries, the binned masses and
+// their prefix sums, and the bins that can hold a crossing.
+template <int DT>
+__global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __grid_constant__ FinalizeArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  __shared__ LShared Z;
+  double* md = reinterpret_cast<double*>(dsm);                // [kNB + 1] masses, then their prefix
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(md + kNB + 1);  // [kNB + 1] counts, then their prefix
+  unsigned char* un = dsm + kSelUnion;                        // history hash, then penalised bins
+  __shared__ double red_d[32];
+  __shared__ float red_f[32];
+  __shared__ int red_i[32];
+  __shared__ unsigned s_flags;
+  __shared__ int s_rng[2][8];
+  __shared__ int s_nr, s_cb;
   const int row = blockIdx.x, tid = threadIdx.x, bs = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5;
   const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
   if (pp->mode != kModeLarge) return;
+  const RowWs W = row_ws(A, row);
   const double T = pp->temperature;
   const int S = A.splits;
   const int64_t V = A.vocab;
-  const int nwords = static_cast<int>((V + 31) / 32);
-  const int nwords_pad = (nwords + 3) & ~3;
-  const int GCAP = kLargeGatherCap;
-
-  // ---- shared memory carve-up ----
-  unsigned char* p = dsm;
-  uint32_t* live = reinterpret_cast<uint32_t*>(p);
-  p += static_cast<size_t>(nwords_pad) * 4;
-  unsigned long long* bmass = reinterpret_cast<unsigned long long*>(p);  // [kNB + 1]
-  p += (kNB + 1) * 8;
-  uint32_t* bcnt = reinterpret_cast<uint32_t*>(p);  // [kNB + 1]
-  p += (kNB + 1) * 4;
-  p = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~static_cast<uintptr_t>(15));
-  Ent* pen = reinterpret_cast<Ent*>(p);
-  p += static_cast<size_t>(A.hist_cap) * sizeof(Ent);
-  Ent* G = reinterpret_cast<Ent*>(p);
-  p += static_cast<size_t>(GCAP) * sizeof(Ent);
-  double* gp = reinterpret_cast<double*>(p);  // exact probabilities of G, then running sums
-
   const int32_t state = A.mask_state ? A.mask_state[row] : -1;
   const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
   const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
   const unsigned char* rowbase =
       static_cast<const unsigned char*>(A.logits) + static_cast<int64_t>(row) * A.row_stride * (DT == GS_DTYPE_F32 ? 4 : 2);
   const float cap = A.softcap, inv_cap = A.inv_softcap;
+  if (tid == 0) s_flags = GS_FLAG_LARGE_PATH;
+  __syncthreads();
 
-  // ---- 0. unit partials ----
-  if (tid == 0) {
-    unsigned fl = GS_FLAG_LARGE_PATH;
-    int na = 0;
-    float mx = -INFINITY, rm = -INFINITY;
-    for (int u = 0; u < S; ++u) {
+  // ---- unit statistics of the streaming pass ----
+  unsigned fl = 0;
+  int na = 0;
+  float mx = -INFINITY, rm = -INFINITY;
+  for (int u = tid; u < S; u += bs) {
+    const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+    fl |= st.flags;
+    na += st.n_allowed;
+    mx = fmaxf(mx, st.m);
+    rm = fmaxf(rm, st.raw_m);
+  }
+  if (fl) atomicOr(&s_flags, fl);
+  na = block_sum_i(na, red_i);
+  mx = block_max_f(mx, red_f);
+  rm = block_max_f(rm, red_f);
+  double rs = 0.0;
+  if (A.want_raw) {
+    for (int u = tid; u < S; u += bs) {
       const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
-      fl |= st.flags;
-      na += st.n_allowed;
-      mx = fmaxf(mx, st.m);
-      rm = fmaxf(rm, st.raw_m);
+      if (st.raw_m > -INFINITY)
+        rs = __dadd_rn(rs, __dmul_rn(st.raw_s, exp(static_cast<double>(st.raw_m) - static_cast<double>(rm))));
     }
-    double rs = 0.0;
-    if (A.want_raw)
-      for (int u = 0; u < S; ++u) {
-        const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
-        if (st.raw_m > -INFINITY) rs = __dadd_rn(rs, __dmul_rn(st.raw_s, exp(static_cast<double>(st.raw_m) - static_cast<double>(rm))));
-      }
-    if (has_mask && na == 0) fl |= GS_FLAG_ERR_DEADEND;
-    if (pp->typical_p < 1) fl |= GS_FLAG_ERR_UNSUPPORTED;  // typical-p over > 1024 candidates
-    Z.flags = fl;
-    Z.n_allowed = na;
-    Z.Mx = mx;
-    Z.raw_m = rm;
-    Z.raw_s = rs;
-    Z.n_pen = 0;
-    Z.n_neginf = 0;
+    rs = block_sum_d(rs, red_d);
   }
-  __syncthreads();
 
-  // ---- 1. live bitmap: allowed and not penalised ----
-  for (int w = tid; w < nwords; w += bs) {
-    uint32_t m = has_mask ? __ldg(mrow + w) : 0xffffffffu;
-    if (w == nwords - 1 && (V & 31)) m &= (1u << (V & 31)) - 1u;
-    live[w] = m;
-  }
-  __syncthreads();
+  // ---- distinct history ids with their counts and first positions (hash table) ----
   int64_t hl = A.history_len ? A.history_len[row] : 0;
   if (hl > A.history_stride) hl = A.history_stride;
   if (hl < 0) hl = 0;
   const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
-  for (int64_t j = tid; j < hl; j += bs) {
-    const int32_t h = hrow[j];
-    if (h >= 0 && h < V) atomicAnd(&live[h >> 5], ~(1u << (h & 31)));
+  int h2 = 64;
+  while (h2 < 2 * hl) h2 <<= 1;
+  uint32_t* hkey = reinterpret_cast<uint32_t*>(un);
+  int* hcnt = reinterpret_cast<int*>(hkey + h2);
+  int* hfirst = hcnt + h2;
+  for (int i = tid; i < h2; i += bs) {
+    hkey[i] = 0xffffffffu;
+    hcnt[i] = 0;
+    hfirst[i] = INT_MAX;
   }
-  // ---- 2. penalised ids: distinct, with counts, scored exactly ----
-  if (hl > 0) {
-    uint32_t* hs = reinterpret_cast<uint32_t*>(G);  // the gather area is free until step 4
-    const int h2 = pow2_ceil(static_cast<int>(hl));
-    for (int i = tid; i < h2; i += bs) hs[i] = i < hl ? static_cast<uint32_t>(hrow[i]) : 0xffffffffu;
-    __syncthreads();
-    bitonic_sort_u32(hs, h2);
-    const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
-    for (int i = tid; i < hl; i += bs) {
-      const uint32_t v = hs[i];
-      if (v >= static_cast<uint64_t>(V)) continue;
-      if (i > 0 && hs[i - 1] == v) continue;
-      int cnt = 1;
-      while (i + cnt < hl && hs[i + cnt] == v) ++cnt;
-      if (has_mask && !((__ldg(mrow + (v >> 5)) >> (v & 31)) & 1u)) continue;
-      float x = load_logit(rowbase, DT, v);
-      if (cap != 0.0f) x = softcap(x, cap, inv_cap);
-      if (!(x < INFINITY)) atomicOr(&Z.flags, GS_FLAG_ERR_NONFINITE);
-      double xp = static_cast<double>(x);
-      xp = xp < 0 ? __dmul_rn(xp, rp) : __ddiv_rn(xp, rp);
-      xp = __dsub_rn(xp, __dadd_rn(pres, __dmul_rn(static_cast<double>(cnt), freq)));
-      const int slot = atomicAdd(&Z.n_pen, 1);
-      // kind holds the float32 rounding of the penalised logit, used only for binning
-      pen[slot] = Ent{__ddiv_rn(xp, T), v, __float_as_uint(static_cast<float>(xp))};
+  __syncthreads();
+  auto find_slot = [&](uint32_t v, bool insert) -> int {
+    uint32_t s = hash_id(v) & static_cast<uint32_t>(h2 - 1);
+    for (;;) {  // the table is at most half full
+      const uint32_t k = insert ? atomicCAS(&hkey[s], 0xffffffffu, v) : hkey[s];
+      if (k == 0xffffffffu || k == v) return static_cast<int>(s);
+      s = (s + 1) & static_cast<uint32_t>(h2 - 1);
     }
+  };
+  for (int64_t j = tid; j < hl; j += bs) {
+    const int32_t v = hrow[j];
+    if (v < 0 || v >= V) continue;
+    const int s = find_slot(static_cast<uint32_t>(v), true);
+    atomicAdd(&hcnt[s], 1);
+    atomicMin(&hfirst[s], static_cast<int>(j));
   }
   __syncthreads();
 
-  const int n_pen = Z.n_pen;
-  // ---- 3. maximum key and full-vocabulary normaliser ----
-  {
-    double pm = -INFINITY;
-    for (int i = tid; i < n_pen; i += bs) pm = fmax(pm, pen[i].key);
-    for (int o = 16; o > 0; o >>= 1) pm = fmax(pm, __shfl_xor_sync(kFullMask, pm, o));
-    if ((tid & 31) == 0) Z.red_d[tid >> 5] = pm;
-    __syncthreads();
-    if (tid == 0) {
-      double m = Z.Mx > -INFINITY ? __ddiv_rn(static_cast<double>(Z.Mx), T) : -INFINITY;
-      for (int w = 0; w < (bs >> 5); ++w) m = fmax(m, Z.red_d[w]);
-      Z.M = m;
-      if (m == -INFINITY) Z.flags |= GS_FLAG_ERR_NONFINITE;
-      Z.f0 = Z.Mx > -INFINITY ? exp(__dsub_rn(__ddiv_rn(static_cast<double>(Z.Mx), T), m)) : 0.0;
+  // ---- penalised entries: slot j holds the id first seen at history position j ----
+  const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
+  double pmax = -INFINITY;
+  for (int64_t j = tid; j < hl; j += bs) {
+    Ent e{-INFINITY, 0xffffffffu, 0u};
+    const int32_t v = hrow[j];
+    if (v >= 0 && v < V) {
+      const int s = find_slot(static_cast<uint32_t>(v), false);
+      if (hfirst[s] == j && (!has_mask || ((__ldg(mrow + (v >> 5)) >> (v & 31)) & 1u))) {
+        float x = load_logit(rowbase, DT, v);
+        if (cap != 0.0f) x = softcap(x, cap, inv_cap);
+        if (!(x < INFINITY)) atomicOr(&s_flags, GS_FLAG_ERR_NONFINITE);
+        // src/runtime/sampling.ts:21-30: divide positive / multiply negative logits by the
+        // repetition penalty, then subtract presence + count · frequency
+        double xp = static_cast<double>(x);
+        xp = xp < 0 ? __dmul_rn(xp, rp) : __ddiv_rn(xp, rp);
+        xp = __dsub_rn(xp, __dadd_rn(pres, __dmul_rn(static_cast<double>(hcnt[s]), freq)));
+        // kind holds the float32 rounding of the penalised logit, used only for binning
+        e = Ent{__ddiv_rn(xp, T), static_cast<uint32_t>(v), __float_as_uint(static_cast<float>(xp))};
+        pmax = fmax(pmax, e.key);
+      }
     }
-    __syncthreads();
+    W.pen[j] = e;
   }
-  const double M = Z.M;
-  if (!(Z.flags & GS_FLAG_ERRORS)) {
-    double part = 0.0;
+  pmax = block_max_d(pmax, red_d);
+  const double mxk = mx > -INFINITY ? __ddiv_rn(static_cast<double>(mx), T) : -INFINITY;
+  const double M = fmax(mxk, pmax);
+
+  // ---- full-vocabulary normaliser relative to M (fixed summation order) ----
+  double part = 0.0;
+  if (M > -INFINITY) {
     for (int u = tid; u < S; u += bs) {
       const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
-      if (st.m > -INFINITY) part = __dadd_rn(part, __dmul_rn(st.s, exp(__dsub_rn(__ddiv_rn(static_cast<double>(st.m), T), M))));
+      if (st.m > -INFINITY)
+        part = __dadd_rn(part, __dmul_rn(st.s, exp(__dsub_rn(__ddiv_rn(static_cast<double>(st.m), T), M))));
     }
-    for (int i = tid; i < n_pen; i += bs) part = __dadd_rn(part, exp(__dsub_rn(pen[i].key, M)));
-    const double total = block_sum_d(part, Z.red_d);
-    if (tid == 0) Z.total = total;
-    __syncthreads();
+    for (int64_t j = tid; j < hl; j += bs) {
+      const Ent e = W.pen[j];
+      if (e.id != 0xffffffffu && e.key > -INFINITY) part = __dadd_rn(part, exp(__dsub_rn(e.key, M)));
+    }
   }
-
-  const float Mx = Z.Mx;
-  const float scale = static_cast<float>(static_cast<double>(kNB) / (kRangeKeys * T));
-  const float f0 = static_cast<float>(Z.f0);
-  const float a2_hi = pp->a2_hi, a2_lo = pp->a2_lo;
-  const double total = Z.total;
-  const bool vec_ok = (reinterpret_cast<uintptr_t>(rowbase) & 15) == 0 && DT == GS_DTYPE_F32;
-
-  // Visits every live (allowed, unpenalised) id of the row with its soft-capped logit.
-  auto for_each_live = [&](auto&& fn) {
-    if (vec_ok) {
-      const float4* r4 = reinterpret_cast<const float4*>(rowbase);
-      const int64_t nv = V / 4;
-      for (int64_t vi = tid; vi < nv; vi += bs) {
-        const int64_t id0 = vi * 4;
-        const uint32_t bits = (live[id0 >> 5] >> (id0 & 31)) & 15u;
-        if (!bits) continue;
-        const float4 v = __ldg(r4 + vi);
-        const float xs[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if ((bits >> i) & 1u) fn(cap != 0.0f ? softcap(xs[i], cap, inv_cap) : xs[i], static_cast<uint32_t>(id0 + i));
-      }
-      for (int64_t id = nv * 4 + tid; id < V; id += bs)
-        if ((live[id >> 5] >> (id & 31)) & 1u) {
-          float x = load_logit(rowbase, DT, id);
-          fn(cap != 0.0f ? softcap(x, cap, inv_cap) : x, static_cast<uint32_t>(id));
-        }
-    } else {
-      for (int64_t id = tid; id < V; id += bs)
-        if ((live[id >> 5] >> (id & 31)) & 1u) {
-          float x = load_logit(rowbase, DT, id);
-          fn(cap != 0.0f ? softcap(x, cap, inv_cap) : x, static_cast<uint32_t>(id));
-        }
-    }
-  };
-
-  // ---- 4. histogram of count and mass ----
-  if (!(Z.flags & GS_FLAG_ERRORS)) {
-    for (int b = tid; b <= kNB; b += bs) {
-      bcnt[b] = 0;
-      bmass[b] = 0;
-    }
-    __syncthreads();
-    int neginf = 0;
-    for_each_live([&](float x, uint32_t) {
-      if (x == -INFINITY) {
-        ++neginf;
-        return;
-      }
-      const int b = bin_of(x, Mx, scale);
-      const float d = x - Mx;
-      const float e = ex2_approx(fmaf(d, a2_lo, d * a2_hi)) * f0;
-      atomicAdd(&bcnt[b], 1u);
-      atomicAdd(&bmass[b], static_cast<unsigned long long>(__fmul_rn(e, 17592186044416.0f) + 0.5f));
-    });
-    for (int i = tid; i < n_pen; i += bs) {
-      if (pen[i].key == -INFINITY) {
-        ++neginf;
-        continue;
-      }
-      const int b = bin_of(__uint_as_float(pen[i].kind), Mx, scale);
-      const double e = exp(__dsub_rn(pen[i].key, M));
-      atomicAdd(&bcnt[b], 1u);
-      atomicAdd(&bmass[b], static_cast<unsigned long long>(e * kFix + 0.5));
-    }
-    neginf = block_sum_i(neginf, Z.red_i);
-    // exclusive prefix over the bins (2 per thread; kNB == 2 * 1024)
-    {
-      const int b0 = 2 * tid;
-      const uint32_t c0 = bcnt[b0], c1 = bcnt[b0 + 1];
-      const unsigned long long m0 = bmass[b0], m1 = bmass[b0 + 1];
-      uint32_t ci = c0 + c1;
-      unsigned long long mi = m0 + m1;
-      const int lane = tid & 31, warp = tid >> 5;
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t uc = __shfl_up_sync(kFullMask, ci, o);
-        const unsigned long long um = __shfl_up_sync(kFullMask, mi, o);
-        if (lane >= o) {
-          ci += uc;
-          mi += um;
-        }
-      }
-      __syncthreads();
-      if (lane == 31) {
-        Z.red_i[warp] = static_cast<int>(ci);
-        Z.red_u[warp] = mi;
-      }
-      __syncthreads();
-      uint32_t cb = 0;
-      unsigned long long mb = 0;
-      for (int w = 0; w < warp; ++w) {
-        cb += static_cast<uint32_t>(Z.red_i[w]);
-        mb += Z.red_u[w];
-      }
-      const uint32_t ce = cb + ci - (c0 + c1);
-      const unsigned long long me = mb + mi - (m0 + m1);
-      __syncthreads();
-      bcnt[b0] = ce;
-      bcnt[b0 + 1] = ce + c0;
-      bmass[b0] = me;
-      bmass[b0 + 1] = me + m0;
-      if (tid == bs - 1) {
-        bcnt[kNB] = ce + c0 + c1;
-        bmass[kNB] = me + m0 + m1;
-      }
-      __syncthreads();
-    }
-    if (tid == 0) Z.n_neginf = neginf;
-    __syncthreads();
-  }
-
-  const int n_fin = static_cast<int>(bcnt[kNB]);
-  const double inv_fix_total = 1.0 / (kFix * total);
-  auto massP = [&](int b) { return static_cast<double>(bmass[b]) * inv_fix_total; };  // p-units before bin b
-
-  // Gathers bins [lo, hi] into G (exact keys), sorts them in the reference order and sets
-  // gp[i] = p_i.  Leaves Z.g_n = count (or flags unsupported when it exceeds GCAP).
-  auto gather = [&](int lo, int hi) {
-    if (Z.g_lo == lo && Z.g_hi == hi) return;
-    __syncthreads();
-    if (tid == 0) Z.g_n = 0;
-    __syncthreads();
-    for_each_live([&](float x, uint32_t id) {
-      if (x == -INFINITY) return;
-      const int b = bin_of(x, Mx, scale);
-      if (b < lo || b > hi) return;
-      const int slot = atomicAdd(&Z.g_n, 1);
-      if (slot < GCAP) G[slot] = Ent{__ddiv_rn(static_cast<double>(x), T), id, 0u};
-    });
-    for (int i = tid; i < n_pen; i += bs) {
-      if (pen[i].key == -INFINITY) continue;
-      const int b = bin_of(__uint_as_float(pen[i].kind), Mx, scale);
-      if (b < lo || b > hi) continue;
-      const int slot = atomicAdd(&Z.g_n, 1);
-      if (slot < GCAP) G[slot] = Ent{pen[i].key, pen[i].id, 1u};
-    }
-    __syncthreads();
-    int n = Z.g_n;
-    if (n > GCAP) {
-      if (tid == 0) Z.flags |= GS_FLAG_ERR_UNSUPPORTED;  // more than GCAP ids in one bin
-      n = GCAP;
-    }
-    const int n2 = pow2_ceil(n > 0 ? n : 1);
-    for (int i = n + tid; i < n2; i += bs) G[i] = Ent{-INFINITY, 0xffffffffu, 0xffffffffu};
-    __syncthreads();
-    bitonic_sort_ent(G, n2);
-    for (int i = tid; i < n; i += bs) gp[i] = __ddiv_rn(exp(__dsub_rn(G[i].key, M)), total);
-    __syncthreads();
-    if (tid == 0) {
-      Z.g_lo = lo;
-      Z.g_hi = hi;
-      Z.g_n = n;
-    }
-    __syncthreads();
-  };
+  const double total = block_sum_d(part, red_d);
   if (tid == 0) {
-    Z.g_lo = -1;
-    Z.g_hi = -1;
+    unsigned f = s_flags;
+    if (has_mask && na == 0) f |= GS_FLAG_ERR_DEADEND;
+    if (!(M > -INFINITY)) f |= GS_FLAG_ERR_NONFINITE;
+    if (pp->typical_p < 1) f |= GS_FLAG_ERR_UNSUPPORTED;  // typical-p over > 1024 candidates
+    double u = 0.0, st_next = 0.0;
+    if (!(f & GS_FLAG_ERRORS)) {
+      if (A.uniforms) {
+        u = A.uniforms[row];
+      } else {
+        st_next = A.rng_state[row];
+        u = seeded_next(&st_next);
+      }
+    }
+    LargeRow* H = W.hdr;
+    H->flags = f;
+    H->n_allowed = na;
+    H->n_slots = static_cast<int32_t>(hl);
+    H->n_fin = 0;
+    H->g_count = 0;
+    H->g_need = 0;
+    H->mp_lo = -1;
+    H->mp_hi = -1;
+    H->Mx = mx;
+    H->raw_m = rm;
+    H->raw_s = rs;
+    H->M = M;
+    H->total = total;
+    H->uniform = u;
+    H->rng_next = st_next;
+    s_flags = f;
   }
   __syncthreads();
+  if (s_flags & GS_FLAG_ERRORS) return;
 
-  // First rank j < limit with (running probability through j) >= target; -1 if none.
-  // Writes the running sums at j and j-1 to Z.sresd[0..1].
-  auto locate_mass = [&](double target, int limit) -> int {
-    // first bin whose end reaches the target
-    int cand = kNB;
-    for (int b = tid; b < kNB; b += bs)
-      if (massP(b + 1) >= target && massP(b) < target) cand = min(cand, b);
-    for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(kFullMask, cand, o));
-    __syncthreads();
-    if ((tid & 31) == 0) Z.red_i[tid >> 5] = cand;
-    __syncthreads();
-    int b = kNB;
-    for (int w = 0; w < (bs >> 5); ++w) b = min(b, Z.red_i[w]);
-    __syncthreads();
-    if (massP(0) >= target) b = 0;
-    // The exact running sum inside the bin may fall just short of the binned estimate;
-    // then the crossing is in one of the following bins.  Such a target is within ~1e-7
-    // of a bin edge; after a few bins the search stops and flags a draw boundary.
-    int tries = 0;
-    for (; b < kNB; ++b) {
-      if (static_cast<int>(bcnt[b]) >= limit) return -1;
-      if (bcnt[b + 1] == bcnt[b]) continue;
-      if (++tries > 4) {
-        if (tid == 0) Z.flags |= GS_FLAG_BOUNDARY_DRAW;
-        return -1;
+  // ---- binned masses relative to M: live values from the histogram, then the
+  //      penalised entries (fixed point, so that their sums are order-independent) ----
+  const float Mx = mx, scale = bin_scale(T), width = bin_width_logit(T);
+  const double qunit = ldexp(1.0, -q_bits(V));
+  unsigned long long* pfix = reinterpret_cast<unsigned long long*>(un);  // (the hash table is done)
+  uint32_t* pcnt = reinterpret_cast<uint32_t*>(pfix + kNB);
+  for (int b = tid; b < kNB; b += bs) {
+    const uint32_t c = W.cpre[b];
+    const unsigned long long q = reinterpret_cast<const unsigned long long*>(W.ppre)[b];
+    double m = 0.0;
+    if (c && b < kNB - 1) {
+      const double top = __dsub_rn(
+          __ddiv_rn(__dsub_rn(static_cast<double>(Mx), static_cast<double>(b) * static_cast<double>(width)), T), M);
+      m = __dmul_rn(exp(top), __dsub_rn(static_cast<double>(c), static_cast<double>(q) * qunit));
+    }
+    cnt[b] = c;
+    md[b] = m;
+    pfix[b] = 0;
+    pcnt[b] = 0;
+  }
+  __syncthreads();
+  for (int64_t j = tid; j < hl; j += bs) {
+    const Ent e = W.pen[j];
+    if (e.id == 0xffffffffu || !(e.key > -INFINITY)) continue;
+    const int b = bin_of(__uint_as_float(e.kind), Mx, scale);
+    atomicAdd(&pcnt[b], 1u);
+    atomicAdd(&pfix[b], static_cast<unsigned long long>(__dmul_rn(exp(__dsub_rn(e.key, M)), 17592186044416.0) + 0.5));
+  }
+  __syncthreads();
+  // exclusive prefix over the bins, 4 consecutive bins per thread (fixed order)
+  {
+    constexpr int kPer = kNB / kSelectThreads;
+    double m[kPer];
+    uint32_t c[kPer];
+    double tm = 0.0;
+    uint32_t tc = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int b = tid * kPer + i;
+      m[i] = __dadd_rn(md[b], static_cast<double>(pfix[b]) * 5.684341886080802e-14);  // 2^-44
+      c[i] = cnt[b] + pcnt[b];
+      tm = __dadd_rn(tm, m[i]);
+      tc += c[i];
+    }
+    double im = tm;
+    uint32_t ic = tc;
+    for (int o = 1; o < 32; o <<= 1) {
+      const double um = __shfl_up_sync(kFullMask, im, o);
+      const uint32_t uc = __shfl_up_sync(kFullMask, ic, o);
+      if (lane >= o) {
+        im = __dadd_rn(um, im);
+        ic += uc;
       }
-      gather(b, b);
-      const int n = Z.g_n;
-      if (tid == 0) {
-        double c = massP(b);
-        int found = -1;
-        double prev = c;
-        for (int i = 0; i < n && static_cast<int>(bcnt[b]) + i < limit; ++i) {
-          prev = c;
-          c = __dadd_rn(c, gp[i]);
-          if (c >= target) {
-            found = i;
+    }
+    if (lane == 31) {
+      red_d[warp] = im;
+      red_i[warp] = static_cast<int>(ic);
+    }
+    __syncthreads();
+    double bm = 0.0;
+    uint32_t bc = 0;
+    for (int w = 0; w < warp; ++w) {
+      bm = __dadd_rn(bm, red_d[w]);
+      bc += static_cast<uint32_t>(red_i[w]);
+    }
+    double lm = __shfl_up_sync(kFullMask, im, 1);  // the lanes before this one
+    uint32_t lc = __shfl_up_sync(kFullMask, ic, 1);
+    if (lane == 0) {
+      lm = 0.0;
+      lc = 0;
+    }
+    bm = __dadd_rn(bm, lm);
+    bc += lc;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int b = tid * kPer + i;
+      md[b] = bm;
+      cnt[b] = bc;
+      bm = __dadd_rn(bm, m[i]);
+      bc += c[i];
+    }
+    if (tid == bs - 1) {
+      md[kNB] = bm;
+      cnt[kNB] = bc;
+    }
+    __syncthreads();
+  }
+  for (int b = tid; b <= kNB; b += bs) {
+    W.cpre[b] = cnt[b];
+    W.ppre[b] = __ddiv_rn(md[b], total);
+  }
+
+  // ---- bins that can hold a crossing (thread 0) ----
+  // Bins that must be gathered: the min-p threshold's neighbourhood, the bin where the
+  // binned running mass reaches topP, the bins of the ranks L1 - 1 can take when no
+  // top-p crossing is certain below L1, and the bins the draw's cursor can reach.  Bins
+  // within the slack of those edges (where the exact running sum could fall on either
+  // side) are added while the list stays within the gather capacity.
+  if (tid == 0) {
+    auto P = [&](int b) { return __ddiv_rn(md[b], total); };
+    auto bstart = [&](double t) {  // first bin b with P(b + 1) >= t, kNB if none
+      int l = 0, h = kNB;
+      while (l < h) {
+        const int m = (l + h) >> 1;
+        if (P(m + 1) >= t) h = m;
+        else l = m + 1;
+      }
+      return l;
+    };
+    auto bin_of_rank = [&](int64_t r) {  // the bin holding rank r (0 <= r < n_fin)
+      int l = 0, h = kNB - 1;
+      while (l < h) {
+        const int m = (l + h) >> 1;
+        if (static_cast<int64_t>(cnt[m + 1]) > r) h = m;
+        else l = m + 1;
+      }
+      return l;
+    };
+    const int64_t n_fin = cnt[kNB];
+    int nr = 0;
+    int64_t used = 0;
+    auto rc = [&](int a, int b) -> int64_t { return a <= b ? static_cast<int64_t>(cnt[b + 1]) - cnt[a] : 0; };
+    auto fits = [&](int a, int b) { return used + rc(a, b) <= kGCap; };
+    auto add = [&](int a, int b) {
+      if (nr < 8 && a <= b) {
+        s_rng[0][nr] = a;
+        s_rng[1][nr] = b;
+        ++nr;
+        used += rc(a, b);
+      }
+    };
+    const int last_bin = n_fin > 0 ? bin_of_rank(n_fin - 1) : 0;
+    const int64_t K = pp->top_k;
+    const int64_t klim = (K > 0 && K < V) ? K : V;
+    int64_t L1_lo = klim, L1_hi = klim;
+    int mp_lo = -1, mp_hi = -1;
+    if (pp->min_p > 0) {
+      // p_i >= p_0·minP with p_0 = 1/total: key >= M + ln(minP)
+      const float xth = static_cast<float>(T * (M + log(pp->min_p)));
+      const int bt = bin_of(xth, Mx, scale);
+      mp_lo = bt > 0 ? bt - 1 : 0;
+      mp_hi = bt < kNB - 1 ? bt + 1 : kNB - 1;
+      add(mp_lo, mp_hi);
+      if (L1_lo > cnt[mp_lo]) L1_lo = cnt[mp_lo];
+      if (L1_hi > cnt[mp_hi + 1]) L1_hi = cnt[mp_hi + 1];
+    }
+    double ct_lo = INFINITY, ct_hi = -INFINITY;
+    bool tp_sure = false;
+    int tp_hi = -1;
+    if (pp->top_p < 1 && n_fin > 0) {
+      const double t = pp->top_p;
+      const int b0 = bstart(t);
+      if (b0 < kNB && cnt[b0] < L1_hi) {
+        tp_hi = b0;
+        for (int ext = 0; ext < 4 && t >= P(tp_hi + 1) - kSelMargin * t; ++ext) {
+          if (static_cast<int64_t>(cnt[tp_hi + 1]) >= n_fin) break;
+          const int nb = bin_of_rank(cnt[tp_hi + 1]);
+          if (cnt[nb] >= L1_hi || !fits(b0, nb)) break;
+          tp_hi = nb;
+        }
+        add(b0, tp_hi);
+        ct_lo = P(b0);
+        ct_hi = P(tp_hi + 1);
+        tp_sure = cnt[tp_hi + 1] <= L1_lo && t < P(tp_hi + 1) - kSelMargin * t;
+      }
+    }
+    if (!tp_sure && n_fin > 0) {
+      // L = L1: C(L) is the running sum through rank L1 - 1; from n_fin on it is the
+      // binned total of every finite candidate
+      if (L1_hi >= n_fin) {
+        ct_lo = fmin(ct_lo, P(kNB));
+        ct_hi = fmax(ct_hi, P(kNB));
+      }
+      const int64_t r_hi = (L1_hi < n_fin ? L1_hi : n_fin - 1) - 1;
+      if (L1_lo >= 1 && L1_lo - 1 <= r_hi) {
+        const int rl = bin_of_rank(L1_lo - 1), rh = bin_of_rank(r_hi);
+        add(rl, rh);
+        ct_lo = fmin(ct_lo, P(rl));
+        ct_hi = fmax(ct_hi, P(rh + 1));
+      }
+    }
+    // the draw: cursor = uniform · C(L) with C(L) in [ct_lo, ct_hi]
+    if (ct_lo <= ct_hi && n_fin > 0) {
+      const double u = W.hdr->uniform;
+      auto clampb = [&](int b) { return b > last_bin ? last_bin : b; };
+      const int e0 = clampb(bstart(u * ct_lo)), e1 = clampb(bstart(u * ct_hi));
+      add(e0, e1);
+      const int m0 = clampb(bstart(u * ct_lo * (1 - kSelMargin)));
+      const int m1 = clampb(bstart(u * ct_hi * (1 + kSelMargin)));
+      if (m0 < e0 && fits(m0, e0 - 1)) add(m0, e0 - 1);
+      if (m1 > e1 && fits(e1 + 1, m1)) add(e1 + 1, m1);
+    }
+    // head of the candidate list (kept when it fits beside the bins above)
+    int cb = -1;
+    if (A.cand_ids && A.cand_cap > 0 && n_fin > 0) {
+      int64_t l_hi = L1_hi;
+      if (tp_hi >= 0 && static_cast<int64_t>(cnt[tp_hi + 1]) > l_hi) l_hi = cnt[tp_hi + 1];
+      if (tp_sure) l_hi = cnt[tp_hi + 1];
+      int64_t m = A.cand_cap;
+      if (m > n_fin) m = n_fin;
+      if (m > l_hi) m = l_hi;
+      if (m > 0) cb = bin_of_rank(m - 1);
+    }
+    s_nr = nr;
+    s_cb = cb;
+    W.hdr->mp_lo = mp_lo;
+    W.hdr->mp_hi = mp_hi;
+    W.hdr->n_fin = static_cast<int32_t>(n_fin);
+  }
+  __syncthreads();
+  // bitmap of the selected bins and its entry count; the candidate range goes in last,
+  // and only when the total stays within the gather capacity
+  const int nr = s_nr;
+  auto mark = [&](bool with_cand) {
+    int cntsel = 0;
+    for (int w = tid; w < kNB / 32; w += bs) {
+      uint32_t m = 0;
+      for (int r = 0; r < nr; ++r) {
+        const int a = s_rng[0][r], b = s_rng[1][r];
+        for (int i = 0; i < 32; ++i) {
+          const int bin = w * 32 + i;
+          if (bin >= a && bin <= b) m |= 1u << i;
+        }
+      }
+      if (with_cand && s_cb >= 0)
+        for (int i = 0; i < 32; ++i)
+          if (w * 32 + i <= s_cb) m |= 1u << i;
+      W.sel[w] = m;
+      for (int i = 0; i < 32; ++i)
+        if ((m >> i) & 1u) cntsel += static_cast<int>(cnt[w * 32 + i + 1] - cnt[w * 32 + i]);
+    }
+    return block_sum_i(cntsel, red_i);
+  };
+  int need = mark(true);
+  if (need > kGCap && s_cb >= 0) need = mark(false);
+  if (tid == 0) {
+    W.hdr->g_need = need;
+    if (need > kGCap) W.hdr->flags = s_flags | GS_FLAG_ERR_UNSUPPORTED;  // crossing bins beyond the gather capacity
+  }
+}
+
+// ============================================================================ gather
+template <int DT>
+__global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __grid_constant__ FinalizeArgs A, int parts) {
+  __shared__ uint32_t sel[kNB / 32];
+  __shared__ uint32_t live[kGatherIds / 32];
+  const int row = blockIdx.x / parts, part = blockIdx.x % parts;
+  const int tid = threadIdx.x, bs = blockDim.x, lane = tid & 31;
+  const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
+  if (pp->mode != kModeLarge) return;
+  const RowWs W = row_ws(A, row);
+  LargeRow* Hp = W.hdr;
+  if ((Hp->flags & GS_FLAG_ERRORS) || Hp->g_need == 0) return;
+  const int64_t V = A.vocab;
+  const int64_t lo = static_cast<int64_t>(part) * kGatherIds;
+  if (lo >= V) return;
+  const int n = static_cast<int>(V - lo < kGatherIds ? V - lo : kGatherIds);
+  const float Mx = Hp->Mx, scale = bin_scale(pp->temperature);
+  const int32_t state = A.mask_state ? A.mask_state[row] : -1;
+  const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
+  const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
+  constexpr int ESZ = DT == GS_DTYPE_F32 ? 4 : 2;
+  constexpr int VE = 16 / ESZ;
+  const unsigned char* base =
+      static_cast<const unsigned char*>(A.logits) + (static_cast<int64_t>(row) * A.row_stride + lo) * ESZ;
+  const float cap = A.softcap, inv_cap = A.inv_softcap;
+  int64_t hl = A.history_len ? A.history_len[row] : 0;
+  if (hl > A.history_stride) hl = A.history_stride;
+  if (hl < 0) hl = 0;
+  const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
+  for (int w = tid; w < kNB / 32; w += bs) sel[w] = W.sel[w];
+  build_live(live, mrow, lo, n, hrow, hl, tid, bs);
+  const unsigned lane_lt = (1u << lane) - 1u;
+  auto wanted = [&](float x) {
+    if (!(x > -INFINITY)) return false;
+    const int b = bin_of(x, Mx, scale);
+    return ((sel[b >> 5] >> (b & 31)) & 1u) != 0;
+  };
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+    const int nv = n / VE;
+    const uint4* v4 = reinterpret_cast<const uint4*>(base);
+    for (int v0 = 0; v0 < nv; v0 += 4 * bs) {  // trip count uniform over the CTA
+      // four vectors per thread in flight; their selected values are counted, one warp
+      // scan and one atomic reserve the warp's slots, and each thread writes its own
+      uint4 r[4];
+      uint32_t bits[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int vi = v0 + u * bs + tid;
+        bits[u] = vi < nv ? (live[(vi * VE) >> 5] >> ((vi * VE) & 31)) & ((1u << VE) - 1u) : 0u;
+        r[u] = bits[u] ? ld_stream_u4(v4 + vi) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      float xs[4 * VE];
+      uint32_t tmask = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+        for (int i = 0; i < VE; ++i) {
+          float x = DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]));
+          if ((bits[u] >> i) & 1u) {
+            if (cap != 0.0f) x = softcap(x, cap, inv_cap);
+            if (wanted(x)) tmask |= 1u << (u * VE + i);
+          }
+          xs[u * VE + i] = x;
+        }
+      }
+      const int c = __popc(tmask);
+      int inc = c;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(kFullMask, inc, o);
+        if (lane >= o) inc += t;
+      }
+      const int wtot = __shfl_sync(kFullMask, inc, 31);
+      int at = 0;
+      if (lane == 31 && wtot) at = atomicAdd(&Hp->g_count, wtot);
+      at = __shfl_sync(kFullMask, at, 31) + inc - c;
+#pragma unroll
+      for (int k = 0; k < 4 * VE; ++k) {
+        if ((tmask >> k) & 1u) {
+          const int id = (v0 + (k / VE) * bs + tid) * VE + (k % VE);
+          if (at < kGCap) W.gath[at] = make_uint2(__float_as_uint(xs[k]), static_cast<uint32_t>(lo + id));
+          ++at;
+        }
+      }
+    }
+    done = nv * VE;
+  }
+  for (int i0 = done; i0 < n; i0 += bs) {  // (trip count uniform over the CTA)
+    const int i = i0 + tid;
+    bool take = false;
+    float x = 0.0f;
+    if (i < n && ((live[i >> 5] >> (i & 31)) & 1u)) {
+      x = load_logit(base, DT, i);
+      if (cap != 0.0f) x = softcap(x, cap, inv_cap);
+      take = wanted(x);
+    }
+    const unsigned bal = __ballot_sync(kFullMask, take);
+    if (bal) {
+      const int leader = __ffs(bal) - 1;
+      int at = 0;
+      if (lane == leader) at = atomicAdd(&Hp->g_count, __popc(bal));
+      at = __shfl_sync(kFullMask, at, leader) + __popc(bal & lane_lt);
+      if (take && at < kGCap) W.gath[at] = make_uint2(__float_as_uint(x), static_cast<uint32_t>(lo + i));
+    }
+  }
+}
+
+// ============================================================================ resolve
+template <int DT>
+__global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __grid_constant__ FinalizeArgs A) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  Ent* E = reinterpret_cast<Ent*>(dsm);               // [kGCap] selected bins, bin by bin
+  double* gp = reinterpret_cast<double*>(E + kGCap);  // [kGCap] exact probabilities
+  int* seg = reinterpret_cast<int*>(gp + kGCap);      // [kNB + 1] start of each bin in E
+  __shared__ uint32_t sel[kNB / 32];
+  __shared__ uint32_t nesel[kNB / 32];  // selected and non-empty
+  __shared__ unsigned s_flags;
+  __shared__ int red_i[32];
+  __shared__ int s_nl;
+  __shared__ long long s_res[2];
+  __shared__ double s_resd[3];
+  const int row = blockIdx.x, tid = threadIdx.x, bs = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = bs >> 5;
+  const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
+  if (pp->mode != kModeLarge) return;
+  const RowWs W = row_ws(A, row);
+  const LargeRow H = *W.hdr;
+  const double T = pp->temperature, M = H.M, total = H.total;
+  const float Mx = H.Mx, scale = bin_scale(T);
+  const int64_t V = A.vocab;
+  const int32_t state = A.mask_state ? A.mask_state[row] : -1;
+  const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
+  const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
+  const unsigned char* rowbase =
+      static_cast<const unsigned char*>(A.logits) + static_cast<int64_t>(row) * A.row_stride * (DT == GS_DTYPE_F32 ? 4 : 2);
+  const float cap = A.softcap, inv_cap = A.inv_softcap;
+  if (tid == 0) s_flags = H.flags;
+  __syncthreads();
+  const uint32_t* C = W.cpre;
+  const double* P = W.ppre;
+  auto selected = [&](int b) { return ((sel[b >> 5] >> (b & 31)) & 1u) != 0; };
+
+  uint32_t tok = 0xffffffffu;
+  int64_t L = 0;
+  const int64_t n_fin = H.n_fin;
+  if (!(H.flags & GS_FLAG_ERRORS)) {
+    // ---- place the selected bins' entries: bin b occupies E[seg[b], seg[b + 1]) ----
+    for (int w = tid; w < kNB / 32; w += bs) sel[w] = W.sel[w];
+    __syncthreads();
+    {
+      constexpr int kPer = kNB / kResolveThreads;
+      int c[kPer];
+      int tcount = 0;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int b = tid * kPer + i;
+        c[i] = selected(b) ? static_cast<int>(C[b + 1] - C[b]) : 0;
+        tcount += c[i];
+      }
+      int inc = tcount;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(kFullMask, inc, o);
+        if (lane >= o) inc += u;
+      }
+      if (lane == 31) red_i[warp] = inc;
+      __syncthreads();
+      int bsum = inc - tcount;
+      for (int w = 0; w < warp; ++w) bsum += red_i[w];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        seg[tid * kPer + i] = bsum;
+        bsum += c[i];
+      }
+      if (tid == bs - 1) seg[kNB] = bsum;
+      __syncthreads();
+    }
+    const int n_tot = seg[kNB];
+    for (int w = tid; w < kNB / 32; w += bs) {
+      uint32_t m = 0;
+      for (int i = 0; i < 32; ++i)
+        if (seg[w * 32 + i + 1] > seg[w * 32 + i]) m |= 1u << i;
+      nesel[w] = m;
+    }
+    int* cur = reinterpret_cast<int*>(gp);  // fill counters during placement
+    for (int b = tid; b < kNB; b += bs) cur[b] = 0;
+    __syncthreads();
+    int bad = n_tot > kGCap ? 1 : 0;
+    if (!bad) {
+      const int gn = H.g_count < kGCap ? H.g_count : kGCap;
+      for (int i = tid; i < gn; i += bs) {
+        const uint2 g = W.gath[i];
+        const float x = __uint_as_float(g.x);
+        const int b = bin_of(x, Mx, scale);
+        const int pos = selected(b) ? seg[b] + atomicAdd(&cur[b], 1) : INT_MAX;
+        if (pos < seg[b + 1]) E[pos] = Ent{__ddiv_rn(static_cast<double>(x), T), g.y, 0u};
+        else bad = 1;
+      }
+      for (int j = tid; j < H.n_slots; j += bs) {
+        const Ent e = W.pen[j];
+        if (e.id == 0xffffffffu || !(e.key > -INFINITY)) continue;
+        const int b = bin_of(__uint_as_float(e.kind), Mx, scale);
+        if (!selected(b)) continue;
+        const int pos = seg[b] + atomicAdd(&cur[b], 1);
+        if (pos < seg[b + 1]) E[pos] = Ent{e.key, e.id, 1u};
+        else bad = 1;
+      }
+    }
+    __syncthreads();
+    if (!bad)
+      for (int b = tid; b < kNB; b += bs)
+        if (cur[b] != seg[b + 1] - seg[b]) bad = 1;
+    if (__syncthreads_or(bad)) {
+      if (tid == 0) s_flags |= GS_FLAG_ERR_UNSUPPORTED;  // list overflowed (more than kGCap entries)
+    } else {
+      // list of the selected bins with more than one entry, then one warp per bin sorts it
+      int* lst = cur;
+      if (tid == 0) s_nl = 0;
+      __syncthreads();
+      for (int b = tid; b < kNB; b += bs)
+        if (seg[b + 1] - seg[b] > 1) lst[atomicAdd(&s_nl, 1)] = b;
+      __syncthreads();
+      const int nl = s_nl;
+      for (int q = warp; q < nl; q += nwarps) {
+        const int b = lst[q];
+        const int off = seg[b], nb = seg[b + 1] - off;
+        if (nb <= kWarpSortMax) seg_sort<false>(E + off, nb, lane, 32);
+      }
+      __syncthreads();
+      for (int q = 0; q < nl; ++q) {
+        const int b = lst[q];
+        const int off = seg[b], nb = seg[b + 1] - off;
+        if (nb > kWarpSortMax) seg_sort<true>(E + off, nb, tid, bs);
+      }
+      __syncthreads();
+      for (int i = tid; i < n_tot; i += bs) gp[i] = __ddiv_rn(exp(__dsub_rn(E[i].key, M)), total);
+      __syncthreads();
+    }
+  }
+
+  // first bin b with P(b + 1) >= t (kNB if none), all threads
+  auto bstart = [&](double t) {
+    int c = kNB;
+    for (int b = tid; b < kNB; b += bs)
+      if (P[b + 1] >= t) c = min(c, b);
+    return block_min_i(c, red_i);
+  };
+  // the bin holding rank r, all threads
+  auto bin_of_rank = [&](int64_t r) {
+    int c = kNB - 1;
+    for (int b = tid; b < kNB; b += bs)
+      if (static_cast<int64_t>(C[b + 1]) > r) c = min(c, b);
+    return block_min_i(c, red_i);
+  };
+  // First rank j < limit whose running probability reaches `target` (-1 if none),
+  // walking the selected bins from the binned prefix at each bin's start (the
+  // reference's running sums, sampling.ts:58-64 and :82-90).  s_resd[0..1] get the
+  // running sums through j and j - 1.
+  auto locate = [&](double target, int64_t limit) -> int64_t {
+    int b = bstart(target);
+    if (warp == 0) {  // one warp: a scan of 32 probabilities per step
+      long long found = -1;
+      double c_at = 0.0, c_prev = 0.0;
+      int tries = 0;
+      bool fail = false;
+      while (b < kNB) {
+        if (static_cast<int64_t>(C[b]) >= limit) break;
+        const int nb = static_cast<int>(C[b + 1] - C[b]);
+        if (nb > 0) {
+          if (++tries > 4 || !selected(b)) {
+            fail = true;
+            break;
+          }
+          const int off = seg[b];
+          const int64_t room = limit - static_cast<int64_t>(C[b]);
+          const int nl = nb < room ? nb : static_cast<int>(room);
+          double c = P[b];
+          for (int i0 = 0; i0 < nl; i0 += 32) {
+            const int i = i0 + lane;
+            double v = i < nl ? gp[off + i] : 0.0;
+            for (int o = 1; o < 32; o <<= 1) {
+              const double t = __shfl_up_sync(kFullMask, v, o);
+              if (lane >= o) v = __dadd_rn(t, v);
+            }
+            const double cl = __dadd_rn(c, v);
+            const unsigned hit = __ballot_sync(kFullMask, i < nl && cl >= target);
+            if (hit) {
+              const int f = __ffs(hit) - 1;
+              found = static_cast<long long>(C[b]) + i0 + f;
+              c_at = __shfl_sync(kFullMask, cl, f);
+              const double pv = __shfl_sync(kFullMask, cl, f > 0 ? f - 1 : 0);
+              c_prev = f > 0 ? pv : c;
+              break;
+            }
+            c = __shfl_sync(kFullMask, cl, 31);
+          }
+          if (found >= 0) break;
+        }
+        // next bin: the next selected non-empty one, unless an unselected non-empty bin
+        // comes first
+        if (static_cast<int64_t>(C[b + 1]) >= n_fin) break;
+        int nbn = kNB;
+        for (int w = (b + 1) >> 5; w < kNB / 32; ++w) {
+          uint32_t m = nesel[w];
+          if (w == ((b + 1) >> 5)) m &= ~((1u << ((b + 1) & 31)) - 1u);
+          if (m) {
+            nbn = w * 32 + __ffs(m) - 1;
             break;
           }
         }
-        Z.sres[0] = found;
-        Z.sresd[0] = c;
-        Z.sresd[1] = prev;
+        if (nbn >= kNB || C[nbn] != C[b + 1]) {
+          // the walk would enter a bin that was not gathered
+          if (static_cast<int64_t>(C[b + 1]) < limit) fail = true;
+          break;
+        }
+        b = nbn;
       }
-      __syncthreads();
-      const int f = Z.sres[0];
-      if (f >= 0) return static_cast<int>(bcnt[b]) + f;
-      __syncthreads();
-    }
-    return -1;
-  };
-
-  // Id and running sum (through it) of rank r (0 <= r < n_fin).
-  auto rank_info = [&](int r, uint32_t* id, double* cum_through) {
-    int cand = kNB;
-    for (int b = tid; b < kNB; b += bs)
-      if (static_cast<int>(bcnt[b]) <= r && r < static_cast<int>(bcnt[b + 1])) cand = b;
-    for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(kFullMask, cand, o));
-    __syncthreads();
-    if ((tid & 31) == 0) Z.red_i[tid >> 5] = cand;
-    __syncthreads();
-    int b = kNB;
-    for (int w = 0; w < (bs >> 5); ++w) b = min(b, Z.red_i[w]);
-    __syncthreads();
-    gather(b, b);
-    if (tid == 0) {
-      const int i = r - static_cast<int>(bcnt[b]);
-      double c = massP(b);
-      for (int j = 0; j <= i && j < Z.g_n; ++j) c = __dadd_rn(c, gp[j]);
-      Z.sres[1] = static_cast<int>(G[i < Z.g_n ? i : Z.g_n - 1].id);
-      Z.sresd[2] = c;
+      if (lane == 0) {
+        if (fail) s_flags |= GS_FLAG_BOUNDARY_DRAW;
+        s_res[0] = found;
+        s_resd[0] = c_at;
+        s_resd[1] = c_prev;
+      }
     }
     __syncthreads();
-    *id = static_cast<uint32_t>(Z.sres[1]);
-    *cum_through = Z.sresd[2];
+    const int64_t r = s_res[0];
+    __syncthreads();
+    return r;
   };
 
-  uint32_t tok = 0xffffffffu;
-  int L = 0;
-  if (!(Z.flags & GS_FLAG_ERRORS)) {
-    const int K = pp->top_k;
-    const int64_t klim64 = (K > 0 && K < V) ? K : V;
-    int L1 = static_cast<int>(klim64);
+  __syncthreads();
+  if (!(s_flags & GS_FLAG_ERRORS)) {
+    const int64_t K = pp->top_k;
+    int64_t L1 = (K > 0 && K < V) ? K : V;
     // ---- min-p (sampling.ts:45-48): p_i >= p_0·minP, with p_0 = 1/total ----
     if (pp->min_p > 0) {
       const double theta = __dmul_rn(__ddiv_rn(1.0, total), pp->min_p);
-      const float xth = static_cast<float>(T * (M + log(pp->min_p)));
-      const int bt = bin_of(xth, Mx, scale);
-      const int lo = bt > 0 ? bt - 1 : 0, hi = bt < kNB - 1 ? bt + 1 : kNB - 1;
-      gather(lo, hi);
       int kept = 0, near = 0;
-      for (int i = tid; i < Z.g_n; i += bs) {
-        kept += gp[i] >= theta ? 1 : 0;
-        if (fabs(gp[i] - theta) <= kBoundary * theta) near = 1;
+      for (int b = H.mp_lo; b <= H.mp_hi; ++b) {
+        const int off = seg[b], nb = seg[b + 1] - off;
+        for (int i = tid; i < nb; i += bs) {
+          kept += gp[off + i] >= theta ? 1 : 0;
+          if (fabs(gp[off + i] - theta) <= kBoundary * theta) near = 1;
+        }
       }
-      kept = block_sum_i(kept, Z.red_i);
-      if (__syncthreads_or(near) && tid == 0) Z.flags |= GS_FLAG_BOUNDARY_MIN_P;
-      const int Lm = static_cast<int>(bcnt[lo]) + kept;
+      kept = block_sum_i(kept, red_i);
+      if (__syncthreads_or(near) && tid == 0) s_flags |= GS_FLAG_BOUNDARY_MIN_P;
+      const int64_t Lm = static_cast<int64_t>(C[H.mp_lo]) + kept;
       L1 = L1 < Lm ? L1 : Lm;
     }
     // ---- top-p (sampling.ts:56) ----
     L = L1;
     if (pp->top_p < 1) {
-      const int j = locate_mass(pp->top_p, L1);
+      const int64_t j = locate(pp->top_p, L1);
       if (j >= 0) {
         L = j + 1;
         if (tid == 0) {
-          const double m = fmin(fabs(Z.sresd[0] - pp->top_p), j > 0 ? fabs(Z.sresd[1] - pp->top_p) : INFINITY);
-          if (m <= kBoundary * pp->top_p) Z.flags |= GS_FLAG_BOUNDARY_TOP_P;
+          const double m = fmin(fabs(s_resd[0] - pp->top_p), j > 0 ? fabs(s_resd[1] - pp->top_p) : INFINITY);
+          if (m <= kBoundary * pp->top_p) s_flags |= GS_FLAG_BOUNDARY_TOP_P;
         }
       }
     }
     __syncthreads();
-    // ---- candidate total C(L) ----
+    // ---- candidate total C(L) and the last candidate ----
     double CT;
-    uint32_t last_id = 0;
-    if (L <= n_fin) {
-      rank_info(L - 1, &last_id, &CT);
+    uint32_t last_id = 0xffffffffu;
+    bool last_known = true;
+    if (L < n_fin) {
+      const int b = bin_of_rank(L - 1);
+      if (warp == 0) {
+        if (!selected(b)) {
+          if (lane == 0) {
+            s_flags |= GS_FLAG_ERR_UNSUPPORTED;
+            s_resd[2] = 0.0;
+            s_res[1] = 0xffffffffll;
+          }
+        } else {
+          const int i = static_cast<int>(L - 1 - C[b]), off = seg[b];
+          double v = 0.0;
+          for (int q = lane; q <= i; q += 32) v = __dadd_rn(v, gp[off + q]);
+          v = warp_sum(v);
+          if (lane == 0) {
+            s_resd[2] = __dadd_rn(P[b], v);
+            s_res[1] = E[off + i].id;
+          }
+        }
+      }
+      __syncthreads();
+      CT = s_resd[2];
+      last_id = static_cast<uint32_t>(s_res[1]);
+      __syncthreads();
     } else {
-      CT = massP(kNB);
-      last_id = 0xffffffffu;  // in the -inf group: resolved below if the draw falls through
+      // every finite candidate: the binned total (within the boundary tolerance of the
+      // exact running sum); the -inf group adds nothing
+      CT = P[kNB];
+      if (L == n_fin) {
+        // the last finite candidate, needed only if the draw falls through
+        last_known = false;
+        if (n_fin > 0) {
+          const int b = bin_of_rank(n_fin - 1);
+          if (selected(b)) {
+            last_id = E[seg[b + 1] - 1].id;
+            last_known = true;
+          }
+        }
+      }
     }
     // ---- draw (sampling.ts:58-64) ----
-    if (tid == 0) {
-      double r;
-      if (A.uniforms) {
-        r = A.uniforms[row];
-      } else {
-        double st = A.rng_state[row];
-        r = seeded_next(&st);
-        A.rng_state[row] = st;
-      }
-      Z.uniform = r;
-    }
-    __syncthreads();
-    const double cursor = __dmul_rn(Z.uniform, CT);
-    const int lim = L < n_fin ? L : n_fin;
-    const int j = locate_mass(cursor, lim);
-    if (j >= 0) {
-      tok = G[j - static_cast<int>(bcnt[Z.g_lo])].id;
-      if (tid == 0) {
-        const double m = fmin(fabs(Z.sresd[0] - cursor), j > 0 ? fabs(Z.sresd[1] - cursor) : INFINITY);
-        if (m <= kBoundary * CT) Z.flags |= GS_FLAG_BOUNDARY_DRAW;
-      }
-    } else {
-      if (tid == 0) Z.flags |= GS_FLAG_FELL_THROUGH;
-      if (last_id != 0xffffffffu) {
-        tok = last_id;
-      } else {
-        // the (L - 1 - n_fin)-th id, in ascending order, of the ids whose key is -inf
-        const int want = L - 1 - n_fin;
-        if (tid == 0) Z.sres[2] = 0;
-        __syncthreads();
-        int base = 0;
-        for (int64_t id0 = 0; id0 < V; id0 += bs) {
-          const int64_t id = id0 + tid;
-          bool neg = false;
-          if (id < V) {
-            const bool allowed = !has_mask || ((__ldg(mrow + (id >> 5)) >> (id & 31)) & 1u);
-            if (!allowed) {
-              neg = true;
-            } else {
-              float x = load_logit(rowbase, DT, id);
-              if (cap != 0.0f) x = softcap(x, cap, inv_cap);
-              neg = x == -INFINITY;
-            }
-          }
-          const unsigned bal = __ballot_sync(kFullMask, neg);
-          if ((tid & 31) == 0) Z.red_i[tid >> 5] = __popc(bal);
-          __syncthreads();
-          int before = base;
-          for (int w = 0; w < (tid >> 5); ++w) before += Z.red_i[w];
-          before += __popc(bal & ((1u << (tid & 31)) - 1u));
-          if (neg && before == want) Z.sres[2] = static_cast<int>(id);
-          int sum = 0;
-          for (int w = 0; w < (bs >> 5); ++w) sum += Z.red_i[w];
-          __syncthreads();
-          base += sum;
-          if (base > want) break;
+    if (!(s_flags & GS_FLAG_ERRORS)) {
+      const double cursor = __dmul_rn(H.uniform, CT);
+      const int64_t lim = L < n_fin ? L : n_fin;
+      const int64_t j = locate(cursor, lim);
+      if (j >= 0) {
+        const int b = bin_of_rank(j);
+        tok = E[seg[b] + static_cast<int>(j - C[b])].id;
+        if (tid == 0) {
+          const double m = fmin(fabs(s_resd[0] - cursor), j > 0 ? fabs(s_resd[1] - cursor) : INFINITY);
+          if (m <= kBoundary * CT) s_flags |= GS_FLAG_BOUNDARY_DRAW;
         }
-        __syncthreads();
-        tok = static_cast<uint32_t>(Z.sres[2]);
+      } else {
+        if (tid == 0) s_flags |= GS_FLAG_FELL_THROUGH;
+        if (!last_known) {
+          if (tid == 0) s_flags |= GS_FLAG_ERR_UNSUPPORTED;  // the last candidate's bin was not gathered
+        } else if (last_id != 0xffffffffu) {
+          tok = last_id;
+        } else {
+          // the (L - 1 - n_fin)-th id, in ascending order, of the ids whose key is -inf
+          const int64_t want = L - 1 - n_fin;
+          if (tid == 0) s_res[1] = 0;
+          __syncthreads();
+          int64_t base = 0;
+          for (int64_t id0 = 0; id0 < V; id0 += bs) {
+            const int64_t id = id0 + tid;
+            bool neg = false;
+            if (id < V) {
+              const bool allowed = !has_mask || ((__ldg(mrow + (id >> 5)) >> (id & 31)) & 1u);
+              if (!allowed) {
+                neg = true;
+              } else {
+                float x = load_logit(rowbase, DT, id);
+                if (cap != 0.0f) x = softcap(x, cap, inv_cap);
+                neg = x == -INFINITY;
+              }
+            }
+            const unsigned bal = __ballot_sync(kFullMask, neg);
+            if (lane == 0) red_i[warp] = __popc(bal);
+            __syncthreads();
+            int64_t before = base;
+            for (int w = 0; w < warp; ++w) before += red_i[w];
+            before += __popc(bal & ((1u << lane) - 1u));
+            if (neg && before == want) s_res[1] = id;
+            int sum = 0;
+            for (int w = 0; w < nwarps; ++w) sum += red_i[w];
+            __syncthreads();
+            base += sum;
+            if (base > want) break;
+          }
+          __syncthreads();
+          tok = static_cast<uint32_t>(s_res[1]);
+        }
       }
     }
     __syncthreads();
   }
 
   // ---- outputs ----
-  const unsigned fl = Z.flags;
+  const unsigned fl = s_flags;
   const bool err = (fl & GS_FLAG_ERRORS) != 0;
   if (tid == 0) {
     A.ids[row] = err ? -1 : static_cast<int32_t>(tok);
     if (A.flags) A.flags[row] = fl;
-    if (A.cand_count) A.cand_count[row] = err ? 0 : L;
+    if (A.cand_count) A.cand_count[row] = err ? 0 : static_cast<int32_t>(L);
+    if (!err && !A.uniforms && A.rng_state) A.rng_state[row] = H.rng_next;
     if (A.logprob) {
       double lp = NAN;
       if (!err) {
         float x = load_logit(rowbase, DT, tok);
         if (cap != 0.0f) x = softcap(x, cap, inv_cap);
-        lp = __dsub_rn(__dsub_rn(static_cast<double>(x), static_cast<double>(Z.raw_m)), log(Z.raw_s));
+        lp = __dsub_rn(__dsub_rn(static_cast<double>(x), static_cast<double>(H.raw_m)), log(H.raw_s));
       }
       A.logprob[row] = lp;
     }
   }
   if (A.cand_ids) {
-    // the first min(L, cand_cap) candidates in order, when they fit one gather
-    int m = err ? 0 : (L < A.cand_cap ? L : A.cand_cap);
+    // the first min(L, cand_cap) candidates in order, when their bins were gathered
+    int64_t m = err ? 0 : (L < A.cand_cap ? L : A.cand_cap);
     if (m > n_fin) m = n_fin;
     int nw = 0;
     if (m > 0) {
-      int cand = kNB;
-      for (int b = tid; b < kNB; b += bs)
-        if (static_cast<int>(bcnt[b]) <= m - 1 && m - 1 < static_cast<int>(bcnt[b + 1])) cand = b;
-      for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(kFullMask, cand, o));
-      __syncthreads();
-      if ((tid & 31) == 0) Z.red_i[tid >> 5] = cand;
-      __syncthreads();
-      int b = kNB;
-      for (int w = 0; w < (bs >> 5); ++w) b = min(b, Z.red_i[w]);
-      __syncthreads();
-      if (static_cast<int>(bcnt[b + 1]) <= GCAP) {
-        gather(0, b);
-        nw = m;
-      }
+      const int b = bin_of_rank(m - 1);
+      if (seg[b + 1] == static_cast<int>(C[b + 1])) nw = static_cast<int>(m);  // bins 0..b all gathered
     }
     for (int i = tid; i < A.cand_cap; i += bs) {
-      A.cand_ids[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? static_cast<int32_t>(G[i].id) : -1;
+      A.cand_ids[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? static_cast<int32_t>(E[i].id) : -1;
       if (A.cand_probs) A.cand_probs[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? gp[i] : 0.0;
     }
   }
 }
 
-cudaError_t launch_large(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
-  if (rows == 0) return cudaSuccess;
-  if (dtype == GS_DTYPE_F32) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(large_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      attr = true;
-    }
-    large_kernel<GS_DTYPE_F32><<<rows, kLargeThreads, smem, st>>>(a);
-  } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(large_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      attr = true;
-    }
-    large_kernel<GS_DTYPE_BF16><<<rows, kLargeThreads, smem, st>>>(a);
+namespace {
+
+template <class Kern>
+void set_smem(Kern k, size_t bytes) {
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+template <int DT>
+cudaError_t launch_large_t(const FinalizeArgs& a, int rows, size_t select_smem, cudaStream_t st) {
+  const size_t res_smem = static_cast<size_t>(kGCap) * (sizeof(Ent) + 8) + (kNB + 1) * 4;
+  static bool attr = false;
+  if (!attr) {
+    set_smem(large_select_kernel<DT>, large_select_smem_bytes(GS_MAX_HISTORY));
+    set_smem(large_resolve_kernel<DT>, res_smem);
+    attr = true;
   }
+  large_hist_kernel<DT><<<rows * kCluster, kHistThreads, 0, st>>>(a);
+  large_select_kernel<DT><<<rows, kSelectThreads, select_smem, st>>>(a);
+  const int parts = static_cast<int>((a.vocab + kGatherIds - 1) / kGatherIds);
+  large_gather_kernel<DT><<<rows * parts, kGatherThreads, 0, st>>>(a, parts);
+  large_resolve_kernel<DT><<<rows, kResolveThreads, res_smem, st>>>(a);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_large(const FinalizeArgs& a, int dtype, int rows, size_t select_smem, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  return dtype == GS_DTYPE_F32 ? launch_large_t<GS_DTYPE_F32>(a, rows, select_smem, st)
+                               : launch_large_t<GS_DTYPE_BF16>(a, rows, select_smem, st);
 }
 
 }  // namespace gs

@@ -82,7 +82,8 @@ extern "C" gs_status gs_sample_noalloc(const gs_batch* b, const gs_outputs* o, v
   Layout L;
   s = plan_layout(b, ps, &L, &err);
   if (s != GS_OK) return set_error(s, err);
-  // scratch: [gs_params of every row, when per-row] [layout: plans | unit stats | candidates]
+  // scratch: [gs_params of every row, when per-row] [layout: plans | unit stats | candidates |
+  //          histogram-path rows' workspace]
   const int np = b->params_count;
   const size_t params_bytes = np > 1 ? align_up(static_cast<size_t>(np) * sizeof(gs_params), 256) : 0;
   const size_t need = params_bytes + L.total;
@@ -108,9 +109,7 @@ extern "C" gs_status gs_sample_noalloc(const gs_batch* b, const gs_outputs* o, v
     if (e != cudaSuccess) return set_error(GS_ECUDA, std::string("plan kernel: ") + cudaGetErrorString(e));
     dplans = plans;
   }
-  UnitStat* stats = reinterpret_cast<UnitStat*>(scratch + params_bytes + L.stats_off);
-  unsigned long long* cands = reinterpret_cast<unsigned long long*>(scratch + params_bytes + L.cands_off);
-  s = launch_sampling(b, o, L, plan0, dplans, stats, cands, st, nullptr, &err);
+  s = launch_sampling(b, o, L, plan0, dplans, scratch + params_bytes, st, nullptr, &err);
   if (s != GS_OK) return set_error(s, err);
   return GS_OK;
 }

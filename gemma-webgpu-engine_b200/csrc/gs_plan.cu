@@ -128,7 +128,9 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   L->plans_off = 0;
   L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
   L->cands_off = align_up(L->stats_off + static_cast<size_t>(units) * sizeof(UnitStat), 256);
-  L->total = align_up(L->cands_off + static_cast<size_t>(units) * kcap * 8, 256);
+  L->large_off = align_up(L->cands_off + static_cast<size_t>(units) * kcap * 8, 256);
+  L->large_row = ps.any_large ? large_row_bytes(b->history ? b->history_stride : 0) : 0;
+  L->total = L->large_off + static_cast<size_t>(rows) * L->large_row;
   L->stream_smem = stream_smem_bytes(chunk, kc);
   const int64_t hs = b->history ? b->history_stride : 0;
   L->hist_cap = pow2ceil(std::max<int64_t>(hs, 1));
@@ -139,8 +141,7 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   if (L->fin_smem > 220 * 1024)
     return fmt(err, GS_EUNSUPPORTED, "merge needs %zu bytes of shared memory (topK %d, history %lld)", L->fin_smem, kmax,
                static_cast<long long>(hs));
-  L->large_smem = ps.any_large ? large_smem_bytes(V, L->hist_cap) : 0;
-  if (L->large_smem > 220 * 1024) return fmt(err, GS_EUNSUPPORTED, "vocabulary too large for the histogram path");
+  L->large_smem = ps.any_large ? large_select_smem_bytes(hs) : 0;
   return GS_OK;
 }
 
@@ -158,6 +159,8 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
   L->plans_off = 0;
   L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
   L->cands_off = L->stats_off;
+  L->large_off = L->stats_off;
+  L->large_row = 0;
   L->total = L->stats_off;
   L->stream_smem = 0;
   L->hist_cap = 1;
@@ -172,8 +175,10 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
 }
 
 gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
-                          const RowPlan* dplans, UnitStat* stats, unsigned long long* cands, cudaStream_t st,
-                          cudaEvent_t* events, std::string* err, const ShardInfo* shard) {
+                          const RowPlan* dplans, unsigned char* ws, cudaStream_t st, cudaEvent_t* events,
+                          std::string* err, const ShardInfo* shard) {
+  UnitStat* stats = reinterpret_cast<UnitStat*>(ws + L.stats_off);
+  unsigned long long* cands = reinterpret_cast<unsigned long long*>(ws + L.cands_off);
   const int smode = shard ? shard->mode : 0;
   const int rows = b->rows;
   const float cap = b->softcap;
@@ -245,6 +250,9 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   fa.cand_probs = o->cand_probs;
   fa.cand_count = o->cand_count;
   fa.cand_cap = o->cand_cap;
+  fa.lws = ws + L.large_off;
+  fa.lrow_bytes = static_cast<int64_t>(L.large_row);
+  fa.lslots = static_cast<int32_t>(sa.history_stride);
   if (smode) {
     fa.shard_mode = smode;
     fa.shards = shard->shards;

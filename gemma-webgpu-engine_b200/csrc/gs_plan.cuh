@@ -59,7 +59,8 @@ struct Layout {
   bool any_large;
   bool any_small;
   bool any_sample;
-  size_t plans_off, stats_off, cands_off, total;
+  size_t plans_off, stats_off, cands_off, large_off, total;
+  size_t large_row;  // per-row workspace of the histogram path (0: no such row)
   size_t stream_smem, fin_smem, large_smem;
   int hist_cap, ent_cap, pack_cap, work_cap;
 };
@@ -103,9 +104,10 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
 // Launches the streaming pass, the merge and (when a row needs it) the histogram path.
 // `events` (3 entries or nullptr) are recorded before the stream pass, before the
 // merge, and at the end.  `shard` (nullptr: an ordinary call) selects a sharded mode.
+// `ws` is the call's workspace (the layout's offsets are relative to it).
 gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
-                          const RowPlan* dplans, UnitStat* stats, unsigned long long* cands, cudaStream_t st,
-                          cudaEvent_t* events, std::string* err, const ShardInfo* shard = nullptr);
+                          const RowPlan* dplans, unsigned char* ws, cudaStream_t st, cudaEvent_t* events,
+                          std::string* err, const ShardInfo* shard = nullptr);
 
 // Message of this thread's last failed gs_sample_noalloc call.
 const char* noalloc_last_error();
