@@ -24,6 +24,7 @@ from .sampling import (  # noqa: F401
     default_sampler,
     mask_constraint_logits,
     params_from_config,
+    prepare_params,
     sample_token,
     token_log_probability,
     windowed_history,

@@ -21,11 +21,14 @@ struct gs_ctx {
   // device workspace (plans | unit stats | unit candidates)
   unsigned char* ws = nullptr;
   size_t ws_bytes = 0;
-  // pinned staging for per-row plans and the event guarding its reuse
-  RowPlan* plans_host = nullptr;
-  size_t plans_cap = 0;
-  cudaEvent_t plans_ev = nullptr;
-  bool plans_ev_live = false;
+  // pinned staging for per-row plans: a ring of buffers, each with the event guarding its
+  // reuse, so that a call waits only for the upload issued kPlanSlots calls earlier
+  static constexpr int kPlanSlots = 4;
+  RowPlan* plans_host[kPlanSlots] = {};
+  size_t plans_cap[kPlanSlots] = {};
+  cudaEvent_t plans_ev[kPlanSlots] = {};
+  bool plans_ev_live[kPlanSlots] = {};
+  int plans_next = 0;
   // device staging of gs_sample_host
   unsigned char* io = nullptr;
   size_t io_bytes = 0;
@@ -98,18 +101,19 @@ gs_status ensure_io(gs_ctx* c, size_t bytes) {
   return GS_OK;
 }
 
-gs_status ensure_plans_host(gs_ctx* c, size_t n) {
-  if (c->plans_ev_live) {
-    cudaEventSynchronize(c->plans_ev);  // the previous upload has left the staging buffer
-    c->plans_ev_live = false;
+// Staging slot k for n plans, once the upload that last used it has completed.
+gs_status ensure_plans_slot(gs_ctx* c, int k, size_t n) {
+  if (c->plans_ev_live[k]) {
+    cudaEventSynchronize(c->plans_ev[k]);
+    c->plans_ev_live[k] = false;
   }
-  if (n <= c->plans_cap) return GS_OK;
-  if (c->plans_host) cudaFreeHost(c->plans_host);
-  c->plans_host = nullptr;
-  c->plans_cap = 0;
-  cudaError_t e = cudaMallocHost(&c->plans_host, n * sizeof(RowPlan));
+  if (n <= c->plans_cap[k]) return GS_OK;
+  if (c->plans_host[k]) cudaFreeHost(c->plans_host[k]);
+  c->plans_host[k] = nullptr;
+  c->plans_cap[k] = 0;
+  cudaError_t e = cudaMallocHost(&c->plans_host[k], n * sizeof(RowPlan));
   if (e != cudaSuccess) return cuda_fail(c, e, "pinned plan staging");
-  c->plans_cap = n;
+  c->plans_cap[k] = n;
   return GS_OK;
 }
 
@@ -126,7 +130,8 @@ gs_status gs_create(int device, gs_ctx** out) {
   gs_ctx* c = new gs_ctx();
   c->device = device;
   DeviceGuard g(device);
-  e = cudaEventCreateWithFlags(&c->plans_ev, cudaEventDisableTiming);
+  for (int k = 0; k < gs_ctx::kPlanSlots && e == cudaSuccess; ++k)
+    e = cudaEventCreateWithFlags(&c->plans_ev[k], cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMalloc(&c->digest, sizeof(unsigned long long));
   if (e != cudaSuccess) {
     delete c;
@@ -145,8 +150,10 @@ gs_status gs_destroy(gs_ctx* c) {
   if (c->digest) cudaFree(c->digest);
   if (c->tok_dev) cudaFree(c->tok_dev);
   if (c->lp_dev) cudaFree(c->lp_dev);
-  if (c->plans_host) cudaFreeHost(c->plans_host);
-  if (c->plans_ev) cudaEventDestroy(c->plans_ev);
+  for (int k = 0; k < gs_ctx::kPlanSlots; ++k) {
+    if (c->plans_host[k]) cudaFreeHost(c->plans_host[k]);
+    if (c->plans_ev[k]) cudaEventDestroy(c->plans_ev[k]);
+  }
   for (auto& evs : c->ev_live)
     for (auto ev : evs) cudaEventDestroy(ev);
   for (auto ev : c->ev_pool) cudaEventDestroy(ev);
@@ -178,9 +185,26 @@ gs_status gs_reserve(gs_ctx* c, int32_t rows, int64_t vocab, int32_t max_top_k, 
   if (history_stride > 0) b.history = &dummy;
   gs_status s = plan_layout(&b, ps, &L, &c->err);
   if (s != GS_OK) return s;
-  s = ensure_ws(c, L.total);
+  size_t total = L.total;
+  if ((max_top_k == 0 || max_top_k > GS_MAX_TOP_K) && vocab > GS_MAX_TOP_K) {
+    // rows on the histogram path also need its per-row workspace
+    gs_params pl = p;
+    pl.top_k = 0;
+    PlanSummary pls;
+    pls.add(make_plan(pl, vocab));
+    Layout LL;
+    b.params = &pl;
+    s = plan_layout(&b, pls, &LL, &c->err);
+    if (s != GS_OK) return s;
+    total = std::max(total, LL.total);
+  }
+  s = ensure_ws(c, total);
   if (s != GS_OK) return s;
-  return ensure_plans_host(c, std::max<size_t>(rows, 1));
+  for (int k = 0; k < gs_ctx::kPlanSlots; ++k) {
+    s = ensure_plans_slot(c, k, std::max<size_t>(rows, 1));
+    if (s != GS_OK) return s;
+  }
+  return GS_OK;
 }
 
 }  // extern "C"
@@ -211,15 +235,18 @@ gs_status run_call(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stre
   const RowPlan plan0 = make_plan(b->params[0], plan_vocab);
   const RowPlan* dplans = nullptr;
   if (np > 1) {
-    s = ensure_plans_host(c, np);
+    const int k = c->plans_next;
+    c->plans_next = (k + 1) % gs_ctx::kPlanSlots;
+    s = ensure_plans_slot(c, k, np);
     if (s != GS_OK) return s;
-    for (int i = 0; i < np; ++i) c->plans_host[i] = make_plan(b->params[i], plan_vocab);
+    RowPlan* staged = c->plans_host[k];
+    for (int i = 0; i < np; ++i) staged[i] = make_plan(b->params[i], plan_vocab);
     dplans = reinterpret_cast<const RowPlan*>(c->ws + L.plans_off);
-    cudaError_t e = cudaMemcpyAsync(const_cast<RowPlan*>(dplans), c->plans_host, np * sizeof(RowPlan),
+    cudaError_t e = cudaMemcpyAsync(const_cast<RowPlan*>(dplans), staged, np * sizeof(RowPlan),
                                     cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_fail(c, e, "plan upload");
-    cudaEventRecord(c->plans_ev, st);
-    c->plans_ev_live = true;
+    cudaEventRecord(c->plans_ev[k], st);
+    c->plans_ev_live[k] = true;
   }
   std::array<cudaEvent_t, 3> evs{};
   if (c->profile) {

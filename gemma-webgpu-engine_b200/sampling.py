@@ -86,11 +86,43 @@ def params_from_config(config: dict) -> GsParams:
                     int(top_k) if top_k < 2**31 else 2**31 - 1, 0)
 
 
-def _params_array(params):
-    """One gs_params per entry of `params` (a config dict, a GsParams, or a list of them)."""
+_PARAMS_DTYPE = None
+
+
+def _params_dtype():
+    global _PARAMS_DTYPE
+    if _PARAMS_DTYPE is None:
+        import numpy as np
+        _PARAMS_DTYPE = np.dtype([(n, np.float64) for n in ("temperature", "top_p", "min_p", "typical_p",
+                                                            "repetition_penalty", "presence_penalty",
+                                                            "frequency_penalty")] +
+                                 [("top_k", np.int32), ("reserved", np.int32)])
+        assert _PARAMS_DTYPE.itemsize == ctypes.sizeof(GsParams)
+    return _PARAMS_DTYPE
+
+
+def prepare_params(params):
+    """The gs_params array of ``params`` (a config dict, a GsParams, or a list of them, one
+    per row).  Every sampling call accepts the returned array in place of the list, so a
+    decode loop whose per-row configs stay fixed converts them once instead of per step."""
+    if isinstance(params, ctypes.Array):
+        return params
     if isinstance(params, (dict, GsParams)):
         params = [params]
+    if all(isinstance(p, dict) for p in params):
+        import numpy as np
+        keys = ("temperature", "topP", "minP", "typicalP", "repetitionPenalty", "presencePenalty",
+                "frequencyPenalty")
+        rec = np.empty(len(params), dtype=_params_dtype())
+        for i, k in enumerate(keys):
+            rec[rec.dtype.names[i]] = [p[k] for p in params]
+        rec["top_k"] = np.minimum(np.array([p["topK"] for p in params], dtype=np.int64), 2**31 - 1)
+        rec["reserved"] = 0
+        return (GsParams * len(params)).from_buffer(rec)
     return (GsParams * len(params))(*[p if isinstance(p, GsParams) else params_from_config(p) for p in params])
+
+
+_params_array = prepare_params
 
 
 def windowed_history(history: Sequence[int], window: int) -> list:

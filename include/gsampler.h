@@ -113,7 +113,8 @@ typedef struct gs_ctx gs_ctx;
 gs_status gs_create(int device, gs_ctx** out);
 gs_status gs_destroy(gs_ctx* ctx);
 /* Pre-sizes the workspace so that later gs_sample calls with at most these sizes
- * allocate nothing (and can be captured in a CUDA graph). */
+ * allocate nothing (and can be captured in a CUDA graph).  max_top_k 0 (or above
+ * GS_MAX_TOP_K) also reserves the per-row workspace of the histogram path. */
 gs_status gs_reserve(gs_ctx* ctx, int32_t rows, int64_t vocab, int32_t max_top_k, int64_t history_stride);
 /* Message of the last failure on `ctx` (NULL: this thread's last gs_sample_noalloc failure). */
 const char* gs_last_error(const gs_ctx* ctx);

@@ -53,3 +53,17 @@ def test_no_cpu_fallback_without_device(pkg):
     import pytest
     with pytest.raises(pkg.SamplerError):
         pkg.GpuSampler(0)
+
+
+def test_prepare_params_matches_per_config_conversion():
+    """prepare_params (the vectorised conversion a decode loop can do once) gives the same
+    gs_params bytes as converting each DecodingConfig on its own."""
+    import importlib
+    S = importlib.import_module("gemma-webgpu-engine_b200.sampling")
+    ps = [dict(temperature=0.1 * i, topK=[0, 40, 2**40][i % 3], topP=0.9, minP=0.01 * (i % 5), typicalP=1.0,
+               repetitionPenalty=1.0 + 0.1 * i, presencePenalty=0.5, frequencyPenalty=0.25, repetitionWindow=64)
+          for i in range(37)]
+    a = S.prepare_params(ps)
+    b = (S.GsParams * len(ps))(*[S.params_from_config(p) for p in ps])
+    assert bytes(a) == bytes(b)
+    assert S.prepare_params(a) is a
