@@ -177,8 +177,9 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
   __shared__ unsigned char smode[kWarps][kStages];  // 1: the stage holds a gather-mode mask tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_warps = gridDim.x * kWarps;
-  const int first_unit = blockIdx.x * kWarps + warp;
+  const int nwarps = blockDim.x >> 5;  // warps per CTA (kWarps, fewer for small batches)
+  const int total_warps = gridDim.x * nwarps;
+  const int first_unit = blockIdx.x * nwarps + warp;
   if (first_unit >= n_units) return;  // whole warp; the kernel has no block-wide barrier
   unsigned char* ring = dsm + warp * kWarpBytes;
   uint32_t* pen = reinterpret_cast<uint32_t*>(ring + kStages * kStageBytes);
@@ -952,19 +953,24 @@ bool stream2_eligible(const StreamArgs& a, int dtype, int rows) {
 cudaError_t launch_stream2(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st, int num_sms) {
   const int units = rows * a.splits;
   if (units == 0) return cudaSuccess;
-  int grid = (units + kWarps - 1) / kWarps;
+  // Batches with fewer units than the GPU's warp slots spread them over every SM (fewer
+  // warps per CTA, so that each warp gets a larger share of its SM's issue slots).
+  int wpc = kWarps;
+  if (units < num_sms * kWarps) wpc = (units + num_sms - 1) / num_sms;
+  int grid = (units + wpc - 1) / wpc;
   if (grid > num_sms) grid = num_sms;
+  smem = static_cast<size_t>(wpc) * kWarpBytes;
   // (the attribute is set to the exact size: the per-block limit also counts static smem)
   if (dtype == GS_DTYPE_F32) {
     cudaError_t e = cudaFuncSetAttribute(stream2_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    stream2_kernel<GS_DTYPE_F32><<<grid, kThreads3, smem, st>>>(a, units);
+    stream2_kernel<GS_DTYPE_F32><<<grid, wpc * 32, smem, st>>>(a, units);
   } else {
     cudaError_t e = cudaFuncSetAttribute(stream2_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    stream2_kernel<GS_DTYPE_BF16><<<grid, kThreads3, smem, st>>>(a, units);
+    stream2_kernel<GS_DTYPE_BF16><<<grid, wpc * 32, smem, st>>>(a, units);
   }
   return cudaGetLastError();
 }
