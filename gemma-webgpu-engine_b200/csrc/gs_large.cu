@@ -70,6 +70,7 @@ struct LargeRow {
   int32_t g_need;    // entries (live and penalised) of the selected bins
   int32_t mp_lo;     // min-p bins [mp_lo, mp_hi], -1 without min-p
   int32_t mp_hi;
+  float gat_lo;      // raw logits below this lie below every selected bin
   float Mx;          // maximum over live values (allowed and not penalised)
   float raw_m;
   double raw_s;
@@ -176,6 +177,21 @@ __device__ __forceinline__ void build_live(uint32_t* live, const uint32_t* mrow,
   __syncthreads();
 }
 
+// A raw-logit bound r such that every raw value v < r has softcap(v) < x (the soft cap
+// is monotone over all float32 inputs), checked with the routine itself; -inf when no
+// useful bound exists.  Lets a pass skip the soft cap of values that cannot matter.
+__device__ float raw_below(float x, float cap, float inv_cap) {
+  if (cap == 0.0f) return x;
+  const double t = static_cast<double>(x) / static_cast<double>(cap);
+  if (!(t > -1.0) || !(t < 0.999999)) return -INFINITY;
+  float r = static_cast<float>(static_cast<double>(cap) * atanh(t));
+  for (int i = 0; i < 16; ++i) {
+    if (softcap(r, cap, inv_cap) < x) return r;
+    r -= fmaxf(fabsf(r) * 9.765625e-4f, 9.765625e-4f);
+  }
+  return -INFINITY;
+}
+
 // In-place sort of e[0, n) into ent_before order by threads t of nt: a bitonic network
 // whose every comparator puts the earlier entry at the lower index, so that entries
 // past n behave as padding that sorts last and their comparators can be skipped.
@@ -226,7 +242,7 @@ size_t large_select_smem_bytes(int64_t history_stride) {
 // the row's workspace (counts over the count prefix array, q sums over the mass prefix
 // array; the select kernel reads both and rewrites them with the prefix sums).
 template <int DT>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads)
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads, 3)
     large_hist_kernel(const __grid_constant__ FinalizeArgs A) {
   __shared__ uint32_t cnt[kNB];
   __shared__ uint32_t qs[kNB];
@@ -273,24 +289,41 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads)
     cnt[b] = 0;
     qs[b] = 0;
   }
-  // one live value: its bin's count and q
-  auto add = [&](float raw) {
-    const float x = cap != 0.0f ? softcap(raw, cap, inv_cap) : raw;
-    if (!(x > -INFINITY)) return;  // -inf: not a finite candidate (NaN rows are flagged)
-    const float d = Mx - x;
-    int b = 0;
-    if (d > 0.0f) {
-      const float t = d * scale;
-      b = t >= static_cast<float>(kNB - 1) ? kNB - 1 : static_cast<int>(t);
+  // Two values at once (packed f32x2 arithmetic); l0 / l1: the value is live.  Per live
+  // value: its bin's count, and q (the deepest bin's mass, below e^-40 of the top, is
+  // taken as 0).
+  const float2 c_width = make_float2(width, width), c_invT = make_float2(invT, invT);
+  auto add2 = [&](float r0, float r1, bool l0, bool l1) {
+    float2 x = make_float2(r0, r1);
+    if (cap != 0.0f) {
+      float2 z;
+      x = softcap2_poly(x, cap, inv_cap, &z);
+      if (!(z.x < kSoftcapPolyZ)) x.x = softcap(r0, cap, inv_cap);  // |x| >= c (and NaN)
+      if (!(z.y < kSoftcapPolyZ)) x.y = softcap(r1, cap, inv_cap);
     }
-    atomicAdd(&cnt[b], 1u);
-    if (b < kNB - 1) {  // the deepest bin's mass (below e^-40 of the top) is taken as 0
-      float dl = fmaf(-static_cast<float>(b), width, d) * invT;
-      dl = fminf(fmaxf(dl, 0.0f), kMaxDelta);
-      // 1 - e^-dl by its Taylor series (dl <= 0.0105: the truncation is below 1e-12)
-      const float om = dl * (1.0f - 0.5f * dl * (1.0f - (1.0f / 3.0f) * dl * (1.0f - 0.25f * dl)));
-      const uint32_t q = __float2uint_rn(om * qmul);
-      if (q) atomicAdd(&qs[b], q);
+    l0 = l0 && x.x > -INFINITY;  // -inf: not a finite candidate (NaN rows are flagged)
+    l1 = l1 && x.y > -INFINITY;
+    const float d0 = fmaxf(Mx - x.x, 0.0f), d1 = fmaxf(Mx - x.y, 0.0f);
+    const int b0 = static_cast<int>(fminf(d0 * scale, static_cast<float>(kNB - 1)));
+    const int b1 = static_cast<int>(fminf(d1 * scale, static_cast<float>(kNB - 1)));
+    // 1 - e^-dl by its Taylor series (dl <= 0.0105: the truncation is below 1e-12)
+    float2 dl = __fmul2_rn(__ffma2_rn(make_float2(-static_cast<float>(b0), -static_cast<float>(b1)), c_width,
+                                      make_float2(d0, d1)), c_invT);
+    dl.x = fminf(fmaxf(dl.x, 0.0f), kMaxDelta);
+    dl.y = fminf(fmaxf(dl.y, 0.0f), kMaxDelta);
+    float2 h = __ffma2_rn(dl, make_float2(-1.0f / 24.0f, -1.0f / 24.0f), make_float2(1.0f / 6.0f, 1.0f / 6.0f));
+    h = __ffma2_rn(dl, h, make_float2(-0.5f, -0.5f));
+    h = __ffma2_rn(dl, h, make_float2(1.0f, 1.0f));
+    const float2 om = __fmul2_rn(__fmul2_rn(dl, h), make_float2(qmul, qmul));
+    const uint32_t q0 = b0 < kNB - 1 ? __float2uint_rn(om.x) : 0u;
+    const uint32_t q1 = b1 < kNB - 1 ? __float2uint_rn(om.y) : 0u;
+    if (l0) {
+      atomicAdd(&cnt[b0], 1u);
+      if (q0) atomicAdd(&qs[b0], q0);
+    }
+    if (l1) {
+      atomicAdd(&cnt[b1], 1u);
+      if (q1) atomicAdd(&qs[b1], q1);
     }
   };
   for (int s0 = 0; s0 < n; s0 += kHistSub) {
@@ -316,15 +349,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads)
           if (!bits[u]) continue;
           const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
 #pragma unroll
-          for (int i = 0; i < VE; ++i)
-            if ((bits[u] >> i) & 1u)
-              add(DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1])));
+          for (int i = 0; i < VE; i += 2) {
+            const float a0 = DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : bf16_lo(w[i >> 1]);
+            const float a1 = DT == GS_DTYPE_F32 ? __uint_as_float(w[(i + 1) & 3]) : bf16_hi(w[i >> 1]);
+            add2(a0, a1, (bits[u] >> i) & 1u, (bits[u] >> (i + 1)) & 1u);
+          }
         }
       }
       done = nv * VE;
     }
     for (int i = done + tid; i < sn; i += bs)
-      if ((live[i >> 5] >> (i & 31)) & 1u) add(load_logit(base, DT, i));
+      if ((live[i >> 5] >> (i & 31)) & 1u) add2(load_logit(base, DT, i), 0.0f, true, false);
   }
   cl.sync();
   {
@@ -744,8 +779,18 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
     return block_sum_i(cntsel, red_i);
   };
   int need = mark(true);
-  if (need > kGCap && s_cb >= 0) need = mark(false);
+  bool with_cand = true;
+  if (need > kGCap && s_cb >= 0) {
+    need = mark(false);
+    with_cand = false;
+  }
   if (tid == 0) {
+    // the deepest selected bin bounds what the gather pass must soft-cap and bin (one bin
+    // of slack for the binning's rounding)
+    int bhi = with_cand ? s_cb : -1;
+    for (int r = 0; r < nr; ++r) bhi = s_rng[1][r] > bhi ? s_rng[1][r] : bhi;
+    W.hdr->gat_lo = bhi >= 0 && bhi < kNB - 2 ? raw_below(Mx - static_cast<float>(bhi + 2) * width, cap, inv_cap)
+                                              : -INFINITY;
     W.hdr->g_need = need;
     if (need > kGCap) W.hdr->flags = s_flags | GS_FLAG_ERR_UNSUPPORTED;  // crossing bins beyond the gather capacity
   }
@@ -754,8 +799,10 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
 // ============================================================================ gather
 template <int DT>
 __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __grid_constant__ FinalizeArgs A, int parts) {
+  constexpr int kParkVals = DT == GS_DTYPE_F32 ? 16 : 32;  // values a thread holds per step
   __shared__ uint32_t sel[kNB / 32];
   __shared__ uint32_t live[kGatherIds / 32];
+  __shared__ float park[kParkVals][kGatherThreads];
   const int row = blockIdx.x / parts, part = blockIdx.x % parts;
   const int tid = threadIdx.x, bs = blockDim.x, lane = tid & 31;
   const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
@@ -767,7 +814,7 @@ __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __gr
   const int64_t lo = static_cast<int64_t>(part) * kGatherIds;
   if (lo >= V) return;
   const int n = static_cast<int>(V - lo < kGatherIds ? V - lo : kGatherIds);
-  const float Mx = Hp->Mx, scale = bin_scale(pp->temperature);
+  const float Mx = Hp->Mx, scale = bin_scale(pp->temperature), glo = Hp->gat_lo;
   const int32_t state = A.mask_state ? A.mask_state[row] : -1;
   const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
   const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
@@ -788,53 +835,51 @@ __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __gr
     const int b = bin_of(x, Mx, scale);
     return ((sel[b >> 5] >> (b & 31)) & 1u) != 0;
   };
+  // Appends (x, id) for the lanes whose `take` is set (the whole warp calls).
+  auto append = [&](bool take, float x, uint32_t id) {
+    const unsigned bal = __ballot_sync(kFullMask, take);
+    if (!bal) return;
+    const int leader = __ffs(bal) - 1;
+    int at = 0;
+    if (lane == leader) at = atomicAdd(&Hp->g_count, __popc(bal));
+    at = __shfl_sync(kFullMask, at, leader) + __popc(bal & lane_lt);
+    if (take && at < kGCap) W.gath[at] = make_uint2(__float_as_uint(x), id);
+  };
   int done = 0;
   if ((reinterpret_cast<uintptr_t>(base) & 15) == 0) {
     const int nv = n / VE;
     const uint4* v4 = reinterpret_cast<const uint4*>(base);
     for (int v0 = 0; v0 < nv; v0 += 4 * bs) {  // trip count uniform over the CTA
-      // four vectors per thread in flight; their selected values are counted, one warp
-      // scan and one atomic reserve the warp's slots, and each thread writes its own
-      uint4 r[4];
-      uint32_t bits[4];
+      // Four vectors per thread in flight.  The values that can reach a selected bin
+      // (live, raw >= glo: a few percent) are parked in shared memory and then taken one
+      // per lane per round, so that the warp soft-caps and bins only those.
+      uint32_t pm = 0;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int vi = v0 + u * bs + tid;
-        bits[u] = vi < nv ? (live[(vi * VE) >> 5] >> ((vi * VE) & 31)) & ((1u << VE) - 1u) : 0u;
-        r[u] = bits[u] ? ld_stream_u4(v4 + vi) : make_uint4(0u, 0u, 0u, 0u);
-      }
-      float xs[4 * VE];
-      uint32_t tmask = 0;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+        const uint32_t bits = vi < nv ? (live[(vi * VE) >> 5] >> ((vi * VE) & 31)) & ((1u << VE) - 1u) : 0u;
+        uint4 r = make_uint4(0u, 0u, 0u, 0u);
+        if (bits) r = ld_stream_u4(v4 + vi);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
         for (int i = 0; i < VE; ++i) {
-          float x = DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]));
-          if ((bits[u] >> i) & 1u) {
-            if (cap != 0.0f) x = softcap(x, cap, inv_cap);
-            if (wanted(x)) tmask |= 1u << (u * VE + i);
-          }
-          xs[u * VE + i] = x;
+          const float x = DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]));
+          park[u * VE + i][tid] = x;
+          if (((bits >> i) & 1u) && x >= glo) pm |= 1u << (u * VE + i);
         }
       }
-      const int c = __popc(tmask);
-      int inc = c;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(kFullMask, inc, o);
-        if (lane >= o) inc += t;
-      }
-      const int wtot = __shfl_sync(kFullMask, inc, 31);
-      int at = 0;
-      if (lane == 31 && wtot) at = atomicAdd(&Hp->g_count, wtot);
-      at = __shfl_sync(kFullMask, at, 31) + inc - c;
-#pragma unroll
-      for (int k = 0; k < 4 * VE; ++k) {
-        if ((tmask >> k) & 1u) {
-          const int id = (v0 + (k / VE) * bs + tid) * VE + (k % VE);
-          if (at < kGCap) W.gath[at] = make_uint2(__float_as_uint(xs[k]), static_cast<uint32_t>(lo + id));
-          ++at;
+      while (__any_sync(kFullMask, pm != 0)) {
+        const bool has = pm != 0;
+        const int k = has ? __ffs(pm) - 1 : 0;
+        pm &= pm - 1u;
+        float x = 0.0f;
+        bool take = false;
+        if (has) {
+          x = park[k][tid];
+          if (cap != 0.0f) x = softcap(x, cap, inv_cap);
+          take = wanted(x);
         }
+        append(take, x, static_cast<uint32_t>(lo + (v0 + (k / VE) * bs + tid) * VE + (k % VE)));
       }
     }
     done = nv * VE;
@@ -845,17 +890,12 @@ __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __gr
     float x = 0.0f;
     if (i < n && ((live[i >> 5] >> (i & 31)) & 1u)) {
       x = load_logit(base, DT, i);
-      if (cap != 0.0f) x = softcap(x, cap, inv_cap);
-      take = wanted(x);
+      if (x >= glo) {
+        if (cap != 0.0f) x = softcap(x, cap, inv_cap);
+        take = wanted(x);
+      }
     }
-    const unsigned bal = __ballot_sync(kFullMask, take);
-    if (bal) {
-      const int leader = __ffs(bal) - 1;
-      int at = 0;
-      if (lane == leader) at = atomicAdd(&Hp->g_count, __popc(bal));
-      at = __shfl_sync(kFullMask, at, leader) + __popc(bal & lane_lt);
-      if (take && at < kGCap) W.gath[at] = make_uint2(__float_as_uint(x), static_cast<uint32_t>(lo + i));
-    }
+    append(take, x, static_cast<uint32_t>(lo + i));
   }
 }
 
