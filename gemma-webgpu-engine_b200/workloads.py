@@ -166,3 +166,39 @@ def make(name: str, device="cuda", rows: int | None = None, vocab: int = VOCAB, 
     if dtype is not None:
         wl.logits = wl.logits.to(dtype)
     return wl
+
+
+def run(name: str, rows: int | None = None, calls: int = 2, dtype=None, candidates: int = 0, prepared: bool = True):
+    """Samples configuration `name` `calls` times through GpuSampler on cuda:0 and
+    returns the last result (the driver the profiling summaries run under a profiler)."""
+    import importlib
+    import torch
+    pkg = importlib.import_module(__package__)
+    dev = torch.device("cuda", 0)
+    wl = make(name, device=dev, rows=rows, dtype=dtype)
+    sampler = pkg.GpuSampler(0)
+    params = pkg.prepare_params(wl.params) if prepared else wl.params
+    kw = dict(softcap=wl.softcap, rng_state=wl.rng_state(dev), candidates=candidates)
+    if wl.history is not None:
+        kw.update(history=wl.history, history_len=wl.history_len)
+    if wl.mask_table is not None:
+        kw.update(mask_table=wl.mask_table, mask_state=wl.mask_state)
+    res = None
+    for _ in range(calls):
+        res = sampler.sample(wl.logits, params, **kw)
+    torch.cuda.synchronize()
+    return res
+
+
+if __name__ == "__main__":
+    import argparse
+    ap = argparse.ArgumentParser(description="sample one of the configurations C1-C5 on cuda:0")
+    ap.add_argument("name", choices=["C1", "C2", "C3", "C4", "C5"])
+    ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--calls", type=int, default=2)
+    ap.add_argument("--bf16", action="store_true")
+    ap.add_argument("--candidates", type=int, default=0)
+    a = ap.parse_args()
+    import torch
+    r = run(a.name, a.rows, a.calls, torch.bfloat16 if a.bf16 else None, a.candidates)
+    print(a.name, "rows", r.ids.shape[0], "first ids", r.ids[:4].tolist())
