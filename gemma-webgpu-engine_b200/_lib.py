@@ -49,7 +49,8 @@ EXPORTS = (
     "gs_create", "gs_destroy", "gs_reserve", "gs_last_error", "gs_sample", "gs_sample_host",
     "gs_token_log_probability", "gs_mask_constraint_logits", "gs_build_mask_row", "gs_softcap",
     "gs_softcap_digest", "gs_shard_record_bytes", "gs_shard_partials", "gs_shard_merge", "gs_profile_enable",
-    "gs_profile_read", "gs_sample_noalloc",
+    "gs_profile_read", "gs_sample_noalloc", "gs_constraint_create", "gs_constraint_destroy",
+    "gs_constraint_last_error", "gs_constraint_build_masks",
 )
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -66,6 +67,25 @@ class GsParams(ctypes.Structure):
         ("frequency_penalty", ctypes.c_double),
         ("top_k", ctypes.c_int32),
         ("reserved", ctypes.c_int32),
+    ]
+
+
+class GsDfaDesc(ctypes.Structure):
+    _fields_ = [
+        ("nodes", ctypes.c_int32),
+        ("range_offsets", ctypes.c_void_p),
+        ("range_lo", ctypes.c_void_p),
+        ("range_hi", ctypes.c_void_p),
+        ("range_target", ctypes.c_void_p),
+        ("final", ctypes.c_void_p),
+    ]
+
+
+class GsVocabBytesDesc(ctypes.Structure):
+    _fields_ = [
+        ("vocab", ctypes.c_int64),
+        ("offsets", ctypes.c_void_p),
+        ("bytes", ctypes.c_void_p),
     ]
 
 
@@ -135,6 +155,12 @@ def lib() -> ctypes.CDLL:
     L.gs_token_log_probability.argtypes = [P, P, i32, i32, i64, i64, f32, P, P, P]
     L.gs_mask_constraint_logits.argtypes = [P, P, i64, P, i64, P, i64, P, P]
     L.gs_build_mask_row.argtypes = [P, i64, P, i64, P, i64, P, P]
+    L.gs_constraint_create.argtypes = [P, ctypes.POINTER(GsDfaDesc), ctypes.POINTER(GsVocabBytesDesc),
+                                       ctypes.POINTER(P)]
+    L.gs_constraint_destroy.argtypes = [P]
+    L.gs_constraint_last_error.argtypes = [P]
+    L.gs_constraint_last_error.restype = ctypes.c_char_p
+    L.gs_constraint_build_masks.argtypes = [P, i32, P, P, P, P, i64, P, i64, P, i64, P, P]
     L.gs_softcap.argtypes = [P, P, P, i64, f32, P]
     L.gs_softcap_digest.argtypes = [P, u64, u64, f32, ctypes.POINTER(u64)]
     L.gs_shard_record_bytes.argtypes = [ctypes.POINTER(GsParams), i32, i64, i64]
@@ -146,7 +172,7 @@ def lib() -> ctypes.CDLL:
     L.gs_profile_read.argtypes = [P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
                                   ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64)]
     for name in EXPORTS:
-        if name not in ("gs_last_error", "gs_shard_record_bytes"):
+        if name not in ("gs_last_error", "gs_shard_record_bytes", "gs_constraint_last_error"):
             getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L

@@ -119,6 +119,11 @@ gs_status ensure_plans_slot(gs_ctx* c, int k, size_t n) {
 
 }  // namespace
 
+namespace gs {
+int ctx_device(const gs_ctx* c) { return c->device; }
+void ctx_set_error(gs_ctx* c, const char* msg) { c->err = msg; }
+}  // namespace gs
+
 extern "C" {
 
 gs_status gs_create(int device, gs_ctx** out) {

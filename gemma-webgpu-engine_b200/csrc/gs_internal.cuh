@@ -3,6 +3,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+struct gs_ctx;
+
 namespace gs {
 
 enum RowMode : int32_t { kModeSmallK = 0, kModeGreedy = 1, kModeLarge = 2 };
@@ -123,6 +125,8 @@ inline int64_t shard_record_bytes(int kcap, int hcap) {
 // Launch helpers implemented in gs_kernels.cu.
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
 int sm_count();  // SMs of the current device
+int ctx_device(const gs_ctx* c);                 // the device a context is bound to
+void ctx_set_error(gs_ctx* c, const char* msg);  // the message gs_last_error returns
 size_t stream_smem_bytes(int64_t chunk, int kc);
 cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
 // Warp-per-row merge (topK <= 128, history stride <= 512, not a shard call).

@@ -164,6 +164,48 @@ gs_status gs_build_mask_row(gs_ctx* ctx, int64_t vocab, const int32_t* legal, in
                             const int32_t* termination, int64_t n_termination, uint32_t* row_out,
                             void* stream);
 
+/* ---- Constraint bitmask builder: the [S, mask_words] table from a compiled DFA ----
+ * Replaces CompiledGenerationConstraint.legalTokenIds (src/runtime/constraints.ts:56-92,
+ * transitionByte :222-247, isViableConstraintState :254-292, findViableStates :294-314)
+ * over the token-byte trie (src/runtime/token-byte-trie.ts:16-40), and the legal-set rule
+ * of selectConstrainedToken (src/runtime/gemma-session.ts:1315-1326): row s allows the
+ * tokens legal from constraint state s, plus `extra_legal`, minus `termination`, plus
+ * `termination` when the state accepts; dead_end[s] = 1 when the row allows nothing.
+ * The DFA works on Unicode code points: node n's transitions are the ranges
+ * [range_offsets[n], range_offsets[n+1]) of (range_lo, range_hi, range_target), sorted
+ * and disjoint, range_hi inclusive.  A constraint state is a node plus the pending bytes
+ * of an incomplete UTF-8 sequence (0-3 bytes). */
+typedef struct gs_dfa_desc {
+  int32_t nodes;
+  const int32_t* range_offsets; /* [nodes + 1], host memory */
+  const uint32_t* range_lo;
+  const uint32_t* range_hi;
+  const int32_t* range_target;
+  const uint8_t* final;         /* [nodes]: 1 = accepting */
+} gs_dfa_desc;
+
+typedef struct gs_vocab_bytes_desc {
+  int64_t vocab;
+  const int64_t* offsets;       /* [vocab + 1], host: token v is bytes[offsets[v], offsets[v+1]) */
+  const uint8_t* bytes;         /* an empty token is never legal (not in the trie) */
+} gs_vocab_bytes_desc;
+
+typedef struct gs_constraint gs_constraint;
+
+/* Uploads a DFA and a vocabulary to the context's device (set-up; allocates). */
+gs_status gs_constraint_create(gs_ctx* ctx, const gs_dfa_desc* dfa, const gs_vocab_bytes_desc* vocab,
+                               gs_constraint** out);
+gs_status gs_constraint_destroy(gs_constraint* c);
+const char* gs_constraint_last_error(const gs_constraint* c);
+/* Builds rows [0, n_states) of `table` (device, [n_states, mask_words] uint32) for the
+ * states (node[s], pending_len[s], pending_bytes[3s..3s+2]); node, pending and the id
+ * lists are host memory, dead_end device memory (or NULL).  At most 65535 states. */
+gs_status gs_constraint_build_masks(gs_constraint* c, int32_t n_states, const int32_t* node,
+                                    const uint8_t* pending_len, const uint8_t* pending_bytes,
+                                    const int32_t* termination, int64_t n_termination,
+                                    const int32_t* extra_legal, int64_t n_extra, uint32_t* table,
+                                    int64_t mask_words, int32_t* dead_end, void* stream);
+
 /* Elementwise soft cap, the same routine the sampling pass applies (no reference
  * counterpart: the reference never applies its declared cap). */
 gs_status gs_softcap(gs_ctx* ctx, const float* in, float* out, int64_t n, float cap, void* stream);

@@ -504,3 +504,198 @@ void oracle_sample_rows(const float* logits, int64_t rows, int64_t vocab, int64_
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ constraint masks
+// Restates CompiledGenerationConstraint.legalTokenIds (src/runtime/constraints.ts:56-92)
+// with its helpers transitionByte (:222-247), transitionCharacter (:249-252),
+// isViableConstraintState (:254-267), pendingUtf8CompletionRange (:269-292),
+// decodeUtf8CodePoint (:294-300) and findViableStates (:302-321), over the token-byte
+// trie of src/runtime/token-byte-trie.ts:16-40, then the legal-set rule of
+// selectConstrainedToken (src/runtime/gemma-session.ts:1315-1326).  The DFA is given as
+// per-node code-point ranges (range_lo..range_hi inclusive -> target), the form a refa
+// DFA node's `out` CharMap takes.
+namespace {
+
+struct OState {
+  int32_t node;
+  std::vector<int> pending;
+};
+
+struct ODfa {
+  const int32_t* off;
+  const uint32_t* lo;
+  const uint32_t* hi;
+  const int32_t* target;
+  std::vector<char> viable;
+};
+
+int o_transition_character(const ODfa& d, int32_t node, uint32_t ch) {
+  for (int64_t r = d.off[node]; r < d.off[node + 1]; ++r)
+    if (d.lo[r] <= ch && ch <= d.hi[r]) return d.target[r];
+  return -1;
+}
+
+uint32_t o_decode(const std::vector<int>& bytes) {
+  const size_t n = bytes.size();
+  uint32_t cp = static_cast<uint32_t>(bytes[0]) & (n == 2 ? 0x1f : n == 3 ? 0x0f : 0x07);
+  for (size_t i = 1; i < n; ++i) cp = (cp << 6) | (static_cast<uint32_t>(bytes[i]) & 0x3f);
+  return cp;
+}
+
+bool o_transition_byte(const ODfa& d, const OState& s, int byte, OState* out) {
+  if (s.pending.empty()) {
+    if (byte <= 0x7f) {
+      const int t = o_transition_character(d, s.node, static_cast<uint32_t>(byte));
+      if (t < 0) return false;
+      *out = OState{t, {}};
+      return true;
+    }
+    if ((byte >= 0xc2 && byte <= 0xdf) || (byte >= 0xe0 && byte <= 0xef) || (byte >= 0xf0 && byte <= 0xf4)) {
+      *out = OState{s.node, {byte}};
+      return true;
+    }
+    return false;
+  }
+  if (byte < 0x80 || byte > 0xbf) return false;
+  std::vector<int> bytes = s.pending;
+  bytes.push_back(byte);
+  const size_t expected = s.pending[0] <= 0xdf ? 2 : s.pending[0] <= 0xef ? 3 : 4;
+  if (bytes.size() < expected) {
+    *out = OState{s.node, bytes};
+    return true;
+  }
+  if ((bytes[0] == 0xe0 && bytes[1] < 0xa0) || (bytes[0] == 0xed && bytes[1] > 0x9f) ||
+      (bytes[0] == 0xf0 && bytes[1] < 0x90) || (bytes[0] == 0xf4 && bytes[1] > 0x8f))
+    return false;
+  const int t = o_transition_character(d, s.node, o_decode(bytes));
+  if (t < 0) return false;
+  *out = OState{t, {}};
+  return true;
+}
+
+bool o_completion(const std::vector<int>& pending, uint32_t* mn, uint32_t* mx) {
+  if (pending.empty()) return false;
+  const int lead = pending[0];
+  const size_t length = lead <= 0xdf ? 2 : lead <= 0xef ? 3 : 4;
+  if (pending.size() >= length) return false;
+  const int second_min = lead == 0xe0 ? 0xa0 : lead == 0xf0 ? 0x90 : 0x80;
+  const int second_max = lead == 0xed ? 0x9f : lead == 0xf4 ? 0x8f : 0xbf;
+  if (pending.size() > 1 && (pending[1] < second_min || pending[1] > second_max)) return false;
+  for (size_t i = 2; i < pending.size(); ++i)
+    if (pending[i] < 0x80 || pending[i] > 0xbf) return false;
+  std::vector<int> lo = pending, hi = pending;
+  while (lo.size() < length) {
+    const size_t i = lo.size();
+    lo.push_back(i == 1 ? second_min : 0x80);
+    hi.push_back(i == 1 ? second_max : 0xbf);
+  }
+  *mn = o_decode(lo);
+  *mx = o_decode(hi);
+  return true;
+}
+
+bool o_viable_state(const ODfa& d, const OState& s) {
+  if (s.pending.empty()) return d.viable[s.node] != 0;
+  uint32_t mn, mx;
+  if (!o_completion(s.pending, &mn, &mx)) return false;
+  for (int64_t r = d.off[s.node]; r < d.off[s.node + 1]; ++r)
+    if (d.viable[d.target[r]] && d.lo[r] <= mx && d.hi[r] >= mn) return true;
+  return false;
+}
+
+struct OTrieNode {
+  std::map<int, int> children;  // byte -> node index
+  std::vector<int32_t> tokens;
+};
+
+}  // namespace
+
+extern "C" {
+
+void oracle_constraint_masks(int32_t nodes, const int32_t* range_off, const uint32_t* range_lo,
+                             const uint32_t* range_hi, const int32_t* range_target, const uint8_t* final,
+                             int64_t vocab, const int64_t* tok_off, const uint8_t* tok_bytes, int32_t n_states,
+                             const int32_t* node, const uint8_t* pending_len, const uint8_t* pending_bytes,
+                             const int32_t* term, int64_t n_term, const int32_t* extra, int64_t n_extra,
+                             uint32_t* table, int64_t mask_words, int32_t* dead_end) {
+  ODfa d{range_off, range_lo, range_hi, range_target, std::vector<char>(static_cast<size_t>(nodes), 0)};
+  // findViableStates: the finals and their predecessors, transitively
+  std::vector<std::vector<int32_t>> reverse(static_cast<size_t>(nodes));
+  for (int32_t n = 0; n < nodes; ++n)
+    for (int64_t r = range_off[n]; r < range_off[n + 1]; ++r) reverse[range_target[r]].push_back(n);
+  std::vector<int32_t> stack;
+  for (int32_t n = 0; n < nodes; ++n)
+    if (final[n]) {
+      d.viable[n] = 1;
+      stack.push_back(n);
+    }
+  while (!stack.empty()) {
+    const int32_t t = stack.back();
+    stack.pop_back();
+    for (int32_t p : reverse[t])
+      if (!d.viable[p]) {
+        d.viable[p] = 1;
+        stack.push_back(p);
+      }
+  }
+  // TokenByteTrie: every non-empty token under the path of its bytes
+  std::vector<OTrieNode> trie(1);
+  for (int64_t v = 0; v < vocab; ++v) {
+    if (tok_off[v + 1] == tok_off[v]) continue;
+    int cur = 0;
+    for (int64_t i = tok_off[v]; i < tok_off[v + 1]; ++i) {
+      const int b = tok_bytes[i];
+      auto it = trie[cur].children.find(b);
+      if (it == trie[cur].children.end()) {
+        trie.push_back(OTrieNode{});
+        const int nn = static_cast<int>(trie.size()) - 1;
+        trie[cur].children[b] = nn;
+        cur = nn;
+      } else {
+        cur = it->second;
+      }
+    }
+    trie[cur].tokens.push_back(static_cast<int32_t>(v));
+  }
+  for (int32_t s = 0; s < n_states; ++s) {
+    OState start{node[s], {}};
+    const int pl = pending_len ? pending_len[s] : 0;
+    for (int i = 0; i < pl; ++i) start.pending.push_back(pending_bytes[3 * s + i]);
+    // legalTokenIds: depth-first over the trie, children only through viable states
+    std::vector<int32_t> legal;
+    std::vector<std::pair<int, OState>> dfs{{0, start}};
+    while (!dfs.empty()) {
+      auto cur = dfs.back();
+      dfs.pop_back();
+      if (!trie[cur.first].tokens.empty() && o_viable_state(d, cur.second))
+        legal.insert(legal.end(), trie[cur.first].tokens.begin(), trie[cur.first].tokens.end());
+      for (const auto& kv : trie[cur.first].children) {
+        OState next;
+        if (o_transition_byte(d, cur.second, kv.first, &next) && o_viable_state(d, next))
+          dfs.push_back({kv.second, next});
+      }
+    }
+    // selectConstrainedToken: (legal ∪ extra) − termination, + termination when accepting
+    std::vector<char> allow(static_cast<size_t>(vocab), 0);
+    for (int32_t v : legal) allow[v] = 1;
+    for (int64_t i = 0; i < n_extra; ++i)
+      if (extra[i] >= 0 && extra[i] < vocab) allow[extra[i]] = 1;
+    for (int64_t i = 0; i < n_term; ++i)
+      if (term[i] >= 0 && term[i] < vocab) allow[term[i]] = 0;
+    const bool accepting = start.pending.empty() && final[start.node];
+    if (accepting)
+      for (int64_t i = 0; i < n_term; ++i)
+        if (term[i] >= 0 && term[i] < vocab) allow[term[i]] = 1;
+    uint32_t* row = table + static_cast<int64_t>(s) * mask_words;
+    bool any = false;
+    for (int64_t w = 0; w < mask_words; ++w) row[w] = 0;
+    for (int64_t v = 0; v < vocab; ++v)
+      if (allow[v]) {
+        row[v >> 5] |= 1u << (v & 31);
+        any = true;
+      }
+    if (dead_end) dead_end[s] = any ? 0 : 1;
+  }
+}
+
+}  // extern "C"

@@ -90,6 +90,9 @@ def lib():
         L.oracle_softcap_check.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
                                            ctypes.POINTER(ctypes.c_uint64)]
         L.oracle_softcap_check.restype = None
+        L.oracle_constraint_masks.argtypes = [ctypes.c_int32, P, P, P, P, P, ctypes.c_int64, P, P, ctypes.c_int32,
+                                              P, P, P, P, ctypes.c_int64, P, ctypes.c_int64, P, ctypes.c_int64, P]
+        L.oracle_constraint_masks.restype = None
         L.oracle_sample_rows.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                          P, ctypes.c_int64, P, P, ctypes.c_int64, P,
                                          P, ctypes.c_int32, P, P, P, P, ctypes.c_int]
@@ -203,6 +206,35 @@ def softcap_check(cap: float, threads: int = 0) -> tuple[float, int]:
     u, d = ctypes.c_double(), ctypes.c_uint64()
     lib().oracle_softcap_check(float(np.float32(cap)), threads, ctypes.byref(u), ctypes.byref(d))
     return u.value, int(d.value)
+
+
+def constraint_masks(dfa, vocab, node, pending_len=None, pending_bytes=None, termination=(), extra=(),
+                     mask_words=None):
+    """Bitmask rows [states, mask_words] and dead-end flags of the constraint states
+    (legalTokenIds over the token-byte trie, then selectConstrainedToken's rule).
+    `dfa` is (range_offsets, range_lo, range_hi, range_target, final) and `vocab`
+    (offsets, bytes), numpy arrays."""
+    off, lo, hi, tgt, fin = (np.ascontiguousarray(dfa[0], np.int32), np.ascontiguousarray(dfa[1], np.uint32),
+                             np.ascontiguousarray(dfa[2], np.uint32), np.ascontiguousarray(dfa[3], np.int32),
+                             np.ascontiguousarray(dfa[4], np.uint8))
+    toff, tb = np.ascontiguousarray(vocab[0], np.int64), np.ascontiguousarray(vocab[1], np.uint8)
+    V = len(toff) - 1
+    node = np.ascontiguousarray(node, np.int32)
+    S = len(node)
+    plen = np.zeros(S, np.uint8) if pending_len is None else np.ascontiguousarray(pending_len, np.uint8)
+    pb = np.zeros(3 * S, np.uint8) if pending_bytes is None else np.ascontiguousarray(pending_bytes, np.uint8)
+    term = np.ascontiguousarray(termination, np.int32)
+    ext = np.ascontiguousarray(extra, np.int32)
+    W = mask_words or (V + 31) // 32
+    table = np.zeros((S, W), np.uint32)
+    dead = np.zeros(S, np.int32)
+    tb_ptr = tb.ctypes.data if tb.size else None
+    lib().oracle_constraint_masks(len(fin), off.ctypes.data, lo.ctypes.data, hi.ctypes.data, tgt.ctypes.data,
+                                  fin.ctypes.data, V, toff.ctypes.data, tb_ptr, S, node.ctypes.data,
+                                  plen.ctypes.data, pb.ctypes.data, term.ctypes.data if term.size else None,
+                                  term.size, ext.ctypes.data if ext.size else None, ext.size, table.ctypes.data, W,
+                                  dead.ctypes.data)
+    return table, dead
 
 
 def sample_rows(logits: np.ndarray, vocab: int, softcap_value: float, history: np.ndarray | None,
