@@ -355,7 +355,43 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     # ---- CPU baseline (N = 1 only): the oracle on a bounded sample of the same rows
     if world == 1:
         res["cpu_baseline"] = cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per)
+        res["mask_builder"] = mask_builder_leg(pkg, W, sampler)
     return res
+
+
+def mask_builder_leg(pkg, W, sampler):
+    """The constraint bitmask builder at the size of C3/C4's tables: 4096 states x V."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    C = importlib.import_module(PKG + ".constraints")
+    off, b = W.synthetic_token_bytes(VOCAB)
+    tr, fi = W.synthetic_dfa(4096)
+    dfa = C.Dfa.from_transitions(tr, fi)
+    g = C.GpuConstraint(sampler, dfa, (off, b))
+    states = list(range(4096))
+    table, dead = g.build_masks(states)
+    torch.cuda.synchronize()
+    reps = 5
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        table, dead = g.build_masks(states, table=table)
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / reps
+    allowed = int(np.unpackbits(table.cpu().numpy().view(np.uint8)).sum())
+    g.close()
+    node, plen, pb = C.pack_states(states[:4])
+    c0 = time.perf_counter()
+    O.constraint_masks(dfa.arrays(), (off, b), node, plen, pb)
+    cdt = time.perf_counter() - c0
+    words = (VOCAB + 31) // 32
+    return {"states": 4096, "vocab": VOCAB, "ms_per_table": dt * 1e3, "rows_per_s": 4096 / dt,
+            "table_gbs": 4096 * words * 4 / dt / 1e9, "allowed_fraction": allowed / (4096 * VOCAB),
+            "timing": "wall clock around gs_constraint_build_masks (state upload, walk and post kernels, sync)",
+            "cpu_oracle": {"rows_per_s": 4 / cdt, "cores": 1, "sample": "4 states, oracle/oracle.cpp trie DFS "
+                                                                          "restating legalTokenIds (trie build included)"},
+            "data": "synthetic: seeded token bytes (workloads.synthetic_token_bytes) and a 4096-node code-point DFA "
+                    "(workloads.synthetic_dfa); the Gemma tokenizer's bytes are not available"}
 
 
 def cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per):

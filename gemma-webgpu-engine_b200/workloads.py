@@ -168,6 +168,66 @@ def make(name: str, device="cuda", rows: int | None = None, vocab: int = VOCAB, 
     return wl
 
 
+def synthetic_token_bytes(vocab: int = VOCAB, seed: int = 51):
+    """(offsets, bytes) of a seeded stand-in for a SentencePiece vocabulary's token bytes
+    (the Gemma tokenizer's bytes are not available here): lengths 1-16 bytes (mean about
+    6), mostly ASCII letters, digits, punctuation and a leading space, about 15 % of the
+    tokens with 2-4-byte UTF-8 characters, and 256 single raw-byte tokens at the front."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    ascii_pool = np.frombuffer(b" abcdefghijklmnopqrstuvwxyzABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789.,:;\"'{}[]()-_",
+                               dtype=np.uint8)
+    parts = [bytes([b]) for b in range(256)]
+    lens = np.clip(rng.geometric(0.18, vocab - 256), 1, 16)
+    for n in lens.tolist():
+        if rng.random() < 0.15:
+            s = ""
+            while len(s.encode("utf-8")) < n:
+                r = rng.random()
+                cp = int(rng.integers(0x80, 0x800)) if r < 0.5 else int(rng.integers(0x800, 0xD800)) if r < 0.9 \
+                    else int(rng.integers(0x10000, 0x20000))
+                s += chr(cp)
+            parts.append(s.encode("utf-8"))
+        else:
+            parts.append(ascii_pool[rng.integers(0, len(ascii_pool), n)].tobytes())
+    off = np.zeros(vocab + 1, np.int64)
+    off[1:] = np.cumsum([len(x) for x in parts])
+    return off, np.frombuffer(b"".join(parts), np.uint8).copy()
+
+
+def synthetic_dfa(nodes: int = 4096, seed: int = 52):
+    """A seeded code-point DFA standing in for a compiled grammar: a third of the nodes
+    are string interiors (every character except '"' and '\\' loops back; '"' leaves),
+    the rest have 1-8 ranges of ASCII or other Unicode characters to random nodes; a fifth
+    of the nodes accept.  Returns the transitions and the accepting nodes, the input of
+    constraints.Dfa.from_transitions."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    transitions = []
+    for n in range(nodes):
+        if n % 3 == 0:
+            out = int(rng.integers(0, nodes))
+            transitions.append([(0x20, 0x21, n), (0x22, 0x22, out), (0x23, 0x5B, n), (0x5D, 0x10FFFF, n)])
+            continue
+        cuts, ranges, last = set(), [], -1
+        for _ in range(int(rng.integers(1, 9))):
+            if rng.random() < 0.8:
+                lo = int(rng.integers(0x20, 0x7F))
+                hi = min(0x7E, lo + int(rng.integers(0, 12)))
+            else:
+                lo = int(rng.integers(0x80, 0x30000))
+                hi = lo + int(rng.integers(0, 5000))
+            cuts.add((lo, hi))
+        for lo, hi in sorted(cuts):
+            if lo <= last:
+                continue
+            ranges.append((lo, hi, int(rng.integers(0, nodes))))
+            last = hi
+        transitions.append(ranges)
+    finals = [n for n in range(nodes) if rng.random() < 0.2]
+    return transitions, finals
+
+
 def run(name: str, rows: int | None = None, calls: int = 2, dtype=None, candidates: int = 0, prepared: bool = True):
     """Samples configuration `name` `calls` times through GpuSampler on cuda:0 and
     returns the last result (the driver the profiling summaries run under a profiler)."""
