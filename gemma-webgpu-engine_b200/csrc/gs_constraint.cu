@@ -38,6 +38,9 @@ struct gs_constraint {
   uint8_t* node_flags = nullptr;  // [nodes] bit 0 final, bit 1 viable
   uint32_t* tok_off = nullptr;    // [vocab + 1]
   uint8_t* tok_bytes = nullptr;
+  int32_t* ascii = nullptr;       // [nodes][128] target of each ASCII character, -1: none
+  uint4* tok16 = nullptr;         // [vocab] the first 16 bytes of each token
+  uint16_t* tok_len = nullptr;    // [vocab] byte lengths (capped at 65535)
   // per-call staging (grown on demand)
   unsigned char* stage = nullptr;
   size_t stage_bytes = 0;
@@ -48,10 +51,12 @@ namespace gs {
 namespace {
 
 constexpr int kWalkThreads = 256;
+constexpr int kStatesPerBlock = 16;  // states one walk thread visits with its token's bytes in registers
 constexpr int kPostThreads = 256;
 constexpr int kMaxTokenBytes = 1 << 16;  // a longer token is rejected at set-up
 
 struct DfaDev {
+  const int32_t* ascii;  // [nodes][128]
   const int32_t* off;
   const uint32_t* lo;
   const uint32_t* hi;
@@ -124,7 +129,7 @@ __device__ bool pending_viable(const DfaDev& D, int n, uint32_t p, int plen) {
 __device__ bool step_byte(const DfaDev& D, int& n, uint32_t& p, int& plen, uint32_t b) {
   if (plen == 0) {
     if (b <= 0x7f) {
-      n = step_char(D, n, b);
+      n = D.ascii[n * 128 + static_cast<int>(b)];
       return n >= 0;
     }
     if ((b >= 0xc2 && b <= 0xdf) || (b >= 0xe0 && b <= 0xef) || (b >= 0xf0 && b <= 0xf4)) {
@@ -149,31 +154,67 @@ __device__ bool step_byte(const DfaDev& D, int& n, uint32_t& p, int& plen, uint3
   return n >= 0;
 }
 
-// Table word w of state s: bit i set when token 32·w + i is legal from the state.
-__global__ void __launch_bounds__(kWalkThreads) walk_kernel(DfaDev D, const uint32_t* __restrict__ tok_off,
+// Table words of kStatesPerBlock states for 256 consecutive tokens.  Each thread holds
+// its token's first 16 bytes in registers and walks them from each of the block's states
+// in turn, one byte per loop iteration: when a walk ends (a dead or non-viable state, or
+// the token's last byte) the lane records the result and starts the next state at once,
+// so that the lanes of a warp stay busy until all of them have walked every state.  Warp
+// ballots then make each state's word (bit i set: token 32·w + i is legal).
+__global__ void __launch_bounds__(kWalkThreads) walk_kernel(DfaDev D, const uint4* __restrict__ tok16,
+                                                            const uint16_t* __restrict__ tok_len,
+                                                            const uint32_t* __restrict__ tok_off,
                                                             const uint8_t* __restrict__ tok_bytes, int64_t vocab,
-                                                            const StateDev* __restrict__ states, uint32_t* table,
-                                                            int64_t mask_words) {
-  const int s = blockIdx.y;
+                                                            const StateDev* __restrict__ states, int n_states,
+                                                            uint32_t* table, int64_t mask_words) {
+  __shared__ StateDev sst[kStatesPerBlock];
   const int64_t v = static_cast<int64_t>(blockIdx.x) * kWalkThreads + threadIdx.x;
-  const StateDev st = states[s];
-  bool legal = false;
+  const int s0 = blockIdx.y * kStatesPerBlock;
+  const int nk = n_states - s0 < kStatesPerBlock ? n_states - s0 : kStatesPerBlock;
+  if (threadIdx.x < nk) sst[threadIdx.x] = states[s0 + threadIdx.x];
+  __syncthreads();
+  int len = 0;
+  uint4 t = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t a = 0;
   if (v < vocab) {
-    const uint32_t a = tok_off[v], e = tok_off[v + 1];
-    legal = e > a;  // an empty token is never in the trie
+    len = tok_len[v];
+    if (len <= 16) t = tok16[v];
+    else a = tok_off[v];
+    if (len == 0xffff) len = static_cast<int>(tok_off[v + 1] - a);  // (lengths above 65534)
+  }
+  uint32_t res = 0;  // bit k: the token is legal from state s0 + k
+  if (len > 0) {     // (an empty token is never in the trie)
+    int k = 0, i = 0;
+    StateDev st = sst[0];
     int n = st.node, plen = st.plen;
     uint32_t p = st.pending;
-    for (uint32_t i = a; i < e && legal; ++i) {
-      if (!step_byte(D, n, p, plen, tok_bytes[i])) {
-        legal = false;
-        break;
+    while (k < nk) {
+      uint32_t b;
+      if (len <= 16) {
+        const uint32_t wv = i < 4 ? t.x : i < 8 ? t.y : i < 12 ? t.z : t.w;
+        b = (wv >> (8 * (i & 3))) & 0xffu;
+      } else {
+        b = tok_bytes[a + i];
       }
-      legal = plen == 0 ? node_viable(D, n) : pending_viable(D, n, p, plen);
+      bool ok = step_byte(D, n, p, plen, b);
+      if (ok) ok = plen == 0 ? node_viable(D, n) : pending_viable(D, n, p, plen);
+      const bool last = ++i == len;
+      if (!ok || last) {
+        res |= static_cast<uint32_t>(ok) << k;
+        if (++k < nk) {
+          st = sst[k];
+          n = st.node;
+          plen = st.plen;
+          p = st.pending;
+          i = 0;
+        }
+      }
     }
   }
-  const unsigned word = __ballot_sync(kFullMask, legal);
-  const int64_t w = v >> 5;
-  if ((threadIdx.x & 31) == 0 && w < mask_words) table[static_cast<int64_t>(s) * mask_words + w] = word;
+  const int64_t word = v >> 5;
+  for (int k = 0; k < nk; ++k) {
+    const unsigned bits = __ballot_sync(kFullMask, (res >> k) & 1u);
+    if ((threadIdx.x & 31) == 0 && word < mask_words) table[static_cast<int64_t>(s0 + k) * mask_words + word] = bits;
+  }
 }
 
 // Per state: extra legal ids in, termination ids out (back in when the state accepts),
@@ -233,6 +274,9 @@ void release(gs_constraint* c) {
   cudaFree(c->node_flags);
   cudaFree(c->tok_off);
   cudaFree(c->tok_bytes);
+  cudaFree(c->ascii);
+  cudaFree(c->tok16);
+  cudaFree(c->tok_len);
   cudaFree(c->stage);
 }
 
@@ -312,6 +356,19 @@ gs_status gs_constraint_create(gs_ctx* ctx, const gs_dfa_desc* dfa, const gs_voc
   }
   std::vector<uint32_t> toff(static_cast<size_t>(V) + 1);
   for (int64_t v = 0; v <= V; ++v) toff[v] = static_cast<uint32_t>(vb->offsets[v]);
+  // dense ASCII transitions and the tokens' first 16 bytes (one vector load per token)
+  std::vector<int32_t> ascii(static_cast<size_t>(N) * 128, -1);
+  for (int32_t n = 0; n < N; ++n)
+    for (int64_t r = dfa->range_offsets[n]; r < dfa->range_offsets[n + 1]; ++r)
+      for (uint32_t ch = dfa->range_lo[r]; ch <= dfa->range_hi[r] && ch < 128; ++ch)
+        ascii[static_cast<size_t>(n) * 128 + ch] = dfa->range_target[r];
+  std::vector<uint4> t16(static_cast<size_t>(V), make_uint4(0u, 0u, 0u, 0u));
+  std::vector<uint16_t> tlen(static_cast<size_t>(V));
+  for (int64_t v = 0; v < V; ++v) {
+    const int64_t len = vb->offsets[v + 1] - vb->offsets[v];
+    tlen[v] = static_cast<uint16_t>(len < 0xffff ? len : 0xffff);
+    if (len <= 16) std::memcpy(&t16[v], vb->bytes + vb->offsets[v], static_cast<size_t>(len));
+  }
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != c->device) cudaSetDevice(c->device);
@@ -322,6 +379,9 @@ gs_status gs_constraint_create(gs_ctx* ctx, const gs_dfa_desc* dfa, const gs_voc
   if (e == cudaSuccess) e = upload(&c->node_flags, flags.data(), flags.size());
   if (e == cudaSuccess) e = upload(&c->tok_off, toff.data(), toff.size());
   if (e == cudaSuccess) e = upload(&c->tok_bytes, vb->bytes, static_cast<size_t>(toff[V]));
+  if (e == cudaSuccess) e = upload(&c->ascii, ascii.data(), ascii.size());
+  if (e == cudaSuccess) e = upload(&c->tok16, t16.data(), t16.size());
+  if (e == cudaSuccess) e = upload(&c->tok_len, tlen.data(), tlen.size());
   if (prev >= 0 && prev != c->device) cudaSetDevice(prev);
   if (e != cudaSuccess) {
     ctx_set_error(ctx, (std::string("constraint upload: ") + cudaGetErrorString(e)).c_str());
@@ -415,9 +475,11 @@ gs_status gs_constraint_build_masks(gs_constraint* c, int32_t n_states, const in
   const StateDev* dst = reinterpret_cast<const StateDev*>(c->stage);
   const int32_t* dterm = reinterpret_cast<const int32_t*>(c->stage + b_st);
   const int32_t* dextra = reinterpret_cast<const int32_t*>(c->stage + b_st + b_term);
-  DfaDev D{c->range_off, c->range_lo, c->range_hi, c->range_target, c->node_flags, c->nodes};
-  dim3 grid(static_cast<unsigned>((c->vocab + kWalkThreads - 1) / kWalkThreads), static_cast<unsigned>(n_states));
-  walk_kernel<<<grid, kWalkThreads, 0, sm>>>(D, c->tok_off, c->tok_bytes, c->vocab, dst, table, mask_words);
+  DfaDev D{c->ascii, c->range_off, c->range_lo, c->range_hi, c->range_target, c->node_flags, c->nodes};
+  dim3 grid(static_cast<unsigned>((c->vocab + kWalkThreads - 1) / kWalkThreads),
+            static_cast<unsigned>((n_states + kStatesPerBlock - 1) / kStatesPerBlock));
+  walk_kernel<<<grid, kWalkThreads, 0, sm>>>(D, c->tok16, c->tok_len, c->tok_off, c->tok_bytes, c->vocab, dst,
+                                             n_states, table, mask_words);
   post_kernel<<<n_states, kPostThreads, 0, sm>>>(dst, c->node_flags, c->vocab, dextra, n_extra, dterm, n_termination,
                                                   table, mask_words, dead_end);
   e = cudaGetLastError();
