@@ -866,11 +866,10 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
             const uint32_t lw = lane < words ? smw[lane] : 0u;
             full = __reduce_add_sync(kFullMask, static_cast<unsigned>(__popc(lw))) == static_cast<unsigned>(TE);
           }
-          if (full) {
-            cm = dense_tile(std::false_type{}, st, smw, t, t0);
-          } else {
-            cm = dense_tile(std::true_type{}, st, smw, t, t0);
-          }
+          // one instantiation for every tile (its mask bits are all set when `full`): the
+          // loop body stays small enough for the instruction cache
+          (void)full;
+          cm = dense_tile(std::true_type{}, st, smw, t, t0);
           if (want_raw) raw_tile(st);
         } else {
           scalar_tile(smw, t0, cnt);
