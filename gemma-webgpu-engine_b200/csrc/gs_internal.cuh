@@ -63,6 +63,9 @@ struct StreamArgs {
   const int32_t* mask_state;
   UnitStat* stats;
   unsigned long long* cands;
+  // per-row bound shared by the row's units (zeroed per call, or nullptr): every unit's
+  // k-th best pack, and its first-tile threshold, bound the row's k-th best from below
+  unsigned long long* row_tau;
 };
 
 struct FinalizeArgs {

@@ -128,7 +128,8 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   L->plans_off = 0;
   L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
   L->cands_off = align_up(L->stats_off + static_cast<size_t>(units) * sizeof(UnitStat), 256);
-  L->large_off = align_up(L->cands_off + static_cast<size_t>(units) * kcap * 8, 256);
+  L->rowtau_off = align_up(L->cands_off + static_cast<size_t>(units) * kcap * 8, 256);
+  L->large_off = align_up(L->rowtau_off + static_cast<size_t>(rows) * 8, 256);
   L->large_row = ps.any_large ? large_row_bytes(b->history ? b->history_stride : 0) : 0;
   L->total = L->large_off + static_cast<size_t>(rows) * L->large_row;
   L->stream_smem = stream_smem_bytes(chunk, kc);
@@ -159,6 +160,7 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
   L->plans_off = 0;
   L->stats_off = align_up(static_cast<size_t>(rows) * sizeof(RowPlan), 256);
   L->cands_off = L->stats_off;
+  L->rowtau_off = L->stats_off;
   L->large_off = L->stats_off;
   L->large_row = 0;
   L->total = L->stats_off;
@@ -209,6 +211,11 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   sa.mask_state = b->mask_table ? b->mask_state : nullptr;
   sa.stats = stats;
   sa.cands = cands;
+  sa.row_tau = nullptr;
+  if (smode != 2 && L.kmax > 1) {
+    sa.row_tau = reinterpret_cast<unsigned long long*>(ws + L.rowtau_off);
+    cudaMemsetAsync(sa.row_tau, 0, static_cast<size_t>(rows) * 8, st);
+  }
   if (events) cudaEventRecord(events[0], st);
   cudaError_t e = cudaSuccess;
   if (smode != 2) {

@@ -59,7 +59,7 @@ struct Layout {
   bool any_large;
   bool any_small;
   bool any_sample;
-  size_t plans_off, stats_off, cands_off, large_off, total;
+  size_t plans_off, stats_off, cands_off, rowtau_off, large_off, total;
   size_t large_row;  // per-row workspace of the histogram path (0: no such row)
   size_t stream_smem, fin_smem, large_smem;
   int hist_cap, ent_cap, pack_cap, work_cap;

@@ -336,11 +336,16 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     int wcap = 4 * k_eff + 64;
     wcap = wcap > kWarpCand - 32 ? kWarpCand - 32 : wcap;
 
+    unsigned long long* rtau = A.row_tau ? A.row_tau + row : nullptr;
+    auto publish = [&](unsigned long long b) {  // raise the row's shared bound
+      if (rtau && lane == 0) atomicMax(rtau, b);
+    };
     auto compact = [&]() {
       __syncwarp();
       const unsigned long long kth = warp_select_packs(wbuf, wcnt, k_eff, whist, lane);
       wtau = kth > wtau ? kth : wtau;
       wcnt = k_eff;
+      publish(kth);
     };
     // One pack per lane into the candidate buffer (called by the whole warp).  Returns
     // true when this lane's pack is settled (stored, below the threshold, or none);
@@ -484,6 +489,7 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
                 // pack > t0b  <=>  key >= klo
                 const unsigned long long t0b = (static_cast<unsigned long long>(klo) << 32) - 1ull;
                 wtau = t0b > wtau ? t0b : wtau;
+                publish(t0b);
               }
             }
           }
@@ -826,7 +832,13 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     if (smode[warp][cs]) {
       gather_unit();
     } else {
+      // the row's shared bound, read one tile ahead (its load overlaps the tile's work)
+      unsigned long long rt_next = rtau && k_eff > 1 ? *reinterpret_cast<volatile unsigned long long*>(rtau) : 0ull;
       for (int t = 0; t < g.ntiles; ++t) {
+        if (rtau && k_eff > 1) {
+          wtau = rt_next > wtau ? rt_next : wtau;
+          rt_next = *reinterpret_cast<volatile unsigned long long*>(rtau);
+        }
         if (!mbar_wait(bars + cs, cph, kWaitNs)) {
           uflags |= GS_FLAG_ERR_TIMEOUT;
           mbar_wait(bars + cs, cph, kWaitNs);
