@@ -54,6 +54,11 @@ static __device__ __noinline__ float softcap_tail(float a) {
 // (a zero y gives +0).  z < 1 exactly when |y| < 1 (the largest float below 1 squares
 // to 1 − 2^-23).
 constexpr float kSoftcapPolyZ = 1.0f;
+
+// log2(e) as a float pair (hi + lo): e^d = 2^(d·hi + d·lo) with the product's error
+// carried by the second term.
+constexpr float kL2eHi = 1.44269502162933349609375f;
+constexpr float kL2eLo = 1.925963033500011e-08f;
 #define GS_SOFTCAP_Q6 -0.00035845203f
 #define GS_SOFTCAP_Q5 0.0023013647f
 #define GS_SOFTCAP_Q4 -0.007946107f

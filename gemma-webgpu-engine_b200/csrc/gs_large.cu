@@ -47,6 +47,11 @@ constexpr double kRangeKeys = 40.0;    // bins span 40 units of logit/T below th
 constexpr int kCluster = 8;            // histogram CTAs per row (one cluster)
 constexpr int kHistThreads = 512;
 constexpr int kHistSub = 32768;        // ids per live-bitmap pass of a histogram CTA
+#ifndef GS_HIST_MIN_BLOCKS
+#define GS_HIST_MIN_BLOCKS 3
+#endif
+constexpr int kHistMinBlocks = GS_HIST_MIN_BLOCKS;  // resident histogram CTAs per SM
+constexpr int kHistQueue = 8192;       // live values a histogram CTA keeps in shared memory
 constexpr int kSelectThreads = 1024;
 constexpr int kGatherThreads = 256;
 constexpr int kGatherIds = 16384;      // ids per gather CTA
@@ -81,15 +86,17 @@ struct LargeRow {
 };
 static_assert(sizeof(LargeRow) <= 256, "header fits its slot");
 
-// Per-row workspace: header | selected-bin bitmap | count prefix | mass prefix |
-// penalised entries | gathered entries.
-constexpr size_t kOffSel = 256;
+// Per-row workspace: header | the histogram CTAs' row statistics | selected-bin bitmap |
+// count prefix | mass prefix | penalised entries | gathered entries.
+constexpr size_t kOffStats = 256;
+constexpr size_t kOffSel = kOffStats + kCluster * sizeof(UnitStat);
 constexpr size_t kOffCpre = kOffSel + kNB / 8;
 constexpr size_t kOffPpre = (kOffCpre + (kNB + 1) * 4 + 15) / 16 * 16;
 constexpr size_t kOffPen = (kOffPpre + (kNB + 1) * 8 + 15) / 16 * 16;
 
 struct RowWs {
   LargeRow* hdr;
+  UnitStat* hstat; // [kCluster] live maximum / sum, raw maximum / sum, allowed count, flags
   uint32_t* sel;   // [kNB / 32]
   uint32_t* cpre;  // [kNB + 1] entries before bin b (the hist kernel leaves counts here)
   double* ppre;    // [kNB + 1] probability before bin b (the hist kernel leaves q sums here)
@@ -101,6 +108,7 @@ __device__ __forceinline__ RowWs row_ws(const FinalizeArgs& A, int row) {
   unsigned char* b = A.lws + static_cast<size_t>(row) * A.lrow_bytes;
   RowWs w;
   w.hdr = reinterpret_cast<LargeRow*>(b);
+  w.hstat = reinterpret_cast<UnitStat*>(b + kOffStats);
   w.sel = reinterpret_cast<uint32_t*>(b + kOffSel);
   w.cpre = reinterpret_cast<uint32_t*>(b + kOffCpre);
   w.ppre = reinterpret_cast<double*>(b + kOffPpre);
@@ -148,6 +156,28 @@ __device__ __forceinline__ double block_max_d(double v, double* red) {
   return m;
 }
 
+// Exclusive prefix sum of v over the block's threads (in thread order); *total: the sum.
+__device__ __forceinline__ int block_excl_scan_i(int v, int* red, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFullMask, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) red[warp] = x;
+  __syncthreads();
+  int before = 0, tot = 0;
+  for (int w = 0; w < nw; ++w) {
+    const int t = red[w];
+    if (w < warp) before += t;
+    tot += t;
+  }
+  __syncthreads();
+  *total = tot;
+  return before + x - v;
+}
+
 __device__ __forceinline__ int block_min_i(int v, int* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(kFullMask, v, o));
@@ -160,14 +190,16 @@ __device__ __forceinline__ int block_min_i(int v, int* red) {
   return m;
 }
 
-// Live bits of ids [lo, lo + n) of a row: allowed by the mask and not in the history.
+// Live bits of ids [lo, lo + n) of a row: allowed by the mask and not in the history
+// (and, when `n_allowed` is given, this thread's count of allowed ids added to it).
 __device__ __forceinline__ void build_live(uint32_t* live, const uint32_t* mrow, int64_t lo, int n, const int32_t* hrow,
-                                           int64_t hl, int t, int nt) {
+                                           int64_t hl, int t, int nt, int* n_allowed = nullptr) {
   const int words = (n + 31) >> 5;
   for (int w = t; w < words; w += nt) {
     uint32_t m = mrow ? __ldg(mrow + (lo >> 5) + w) : 0xffffffffu;
     if (w == words - 1 && (n & 31)) m &= (1u << (n & 31)) - 1u;
     live[w] = m;
+    if (n_allowed) *n_allowed += __popc(m);
   }
   __syncthreads();
   for (int64_t j = t; j < hl; j += nt) {
@@ -237,37 +269,41 @@ size_t large_select_smem_bytes(int64_t history_stride) {
 }
 
 // ============================================================================ hist
-// One cluster of kCluster CTAs per row.  Each CTA streams hist_chunk(V) ids of the row;
-// rank r then sums bins [r·512, (r+1)·512) of the cluster's histograms and writes them to
-// the row's workspace (counts over the count prefix array, q sums over the mass prefix
-// array; the select kernel reads both and rewrites them with the prefix sums).
-template <int DT>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads, 3)
+// One cluster of kCluster CTAs per row, each owning hist_chunk(V) ids of the row.  The
+// kernel takes the row statistics too (the streaming pass skips these rows):
+//   phase 0: the maximum of the live (allowed, unpenalised) raw values; the soft cap is
+//            monotone, so the capped maximum is the cap of the raw one (a raw -inf caps
+//            to -cap, a finite value).  A chunk with at most kHistQueue live ids copies
+//            their raw values into shared memory (the queue) on the way; a denser chunk
+//            is read again in phase 1 (from L2).  The cluster combines the eight CTAs'
+//            maxima through distributed shared memory.
+//   phase 1: per live value its bin's count and q, and the sum of e^((x - Mx)/T) (and,
+//            for log-probabilities, of e^(x - raw max) over every id).
+// Rank r then sums bins [r·512, (r+1)·512) of the cluster's histograms into the row's
+// workspace (counts over the count prefix array, q sums over the mass prefix array; the
+// select kernel rewrites both with the prefix sums), and each CTA writes its statistics.
+// RAW: the log-probability is wanted (phase 0 visits every id, and there is no queue).
+template <int DT, bool RAW>
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads, kHistMinBlocks)
     large_hist_kernel(const __grid_constant__ FinalizeArgs A) {
   __shared__ uint32_t cnt[kNB];
   __shared__ uint32_t qs[kNB];
   __shared__ uint32_t live[kHistSub / 32];
   __shared__ float red_f[32];
+  __shared__ int red_i[32];
+  __shared__ double red_d[32];
+  __shared__ float s_max[4];  // this CTA's raw maxima of the live / all values, any live / any value
+  extern __shared__ float queue[];  // [kHistQueue] live raw values of a sparse chunk
   cg::cluster_group cl = cg::this_cluster();
   const int rank = static_cast<int>(cl.block_rank());
   const int row = blockIdx.x / kCluster;
   const int tid = threadIdx.x, bs = blockDim.x;
   const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
-  if (pp->mode != kModeLarge || pp->typical_p < 1) return;  // the whole cluster (one row)
+  if (pp->mode != kModeLarge) return;  // the whole cluster (one row)
   const RowWs W = row_ws(A, row);
-  // the row's live maximum from the streaming pass's unit statistics
-  const int S = A.splits;
-  float mx = -INFINITY;
-  int err = 0;
-  for (int u = tid; u < S; u += bs) {
-    const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
-    mx = fmaxf(mx, st.m);
-    err |= (st.flags & GS_FLAG_ERRORS) != 0;
-  }
-  if (__syncthreads_or(err)) return;  // the same decision in every CTA of the cluster
-  const float Mx = block_max_f(mx, red_f);
   const double T = pp->temperature;
   const float scale = bin_scale(T), width = bin_width_logit(T), invT = static_cast<float>(1.0 / T);
+  const float a2_hi = pp->a2_hi, a2_lo = pp->a2_lo;
   const float qmul = static_cast<float>(ldexp(1.0, q_bits(A.vocab)));
   const int64_t V = A.vocab;
   const int64_t hc = hist_chunk(V);
@@ -278,22 +314,150 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
   constexpr int ESZ = DT == GS_DTYPE_F32 ? 4 : 2;
   constexpr int VE = 16 / ESZ;
+  constexpr uint32_t kVecBits = (1u << VE) - 1u;
   const unsigned char* rowbase = static_cast<const unsigned char*>(A.logits) + static_cast<int64_t>(row) * A.row_stride * ESZ;
   const float cap = A.softcap, inv_cap = A.inv_softcap;
+  // a raw value x is an error (NaN, or +inf without a soft cap) when !(x <= lim)
+  const float lim = cap != 0.0f ? INFINITY : 3.40282347e38f;  // (the largest finite float)
   int64_t hl = A.history_len ? A.history_len[row] : 0;
   if (hl > A.history_stride) hl = A.history_stride;
   if (hl < 0) hl = 0;
   const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
+  const bool one_pass_bits = n <= kHistSub;  // the live bits stay valid for phase 1
 
+  // ---- phase 0: maxima, allowed count, non-finite values (and the queue) ----
+  float lmax = -INFINITY, rmax = -INFINITY;
+  int nallow = 0, bad = 0, any_l = 0, any_v = 0;
+  int qn = -1;  // queued values; -1: phase 1 reads the chunk again
+  for (int s0 = 0; s0 < n; s0 += kHistSub) {
+    const int sn = n - s0 < kHistSub ? n - s0 : kHistSub;
+    const unsigned char* base = rowbase + (lo + s0) * ESZ;
+    __syncthreads();
+    build_live(live, mrow, lo + s0, sn, hrow, hl, tid, bs, &nallow);
+    if (!RAW && one_pass_bits) {
+      // each thread takes a run of live words; their values land at its scan offset
+      const int words = (sn + 31) >> 5;
+      const int wpt = (words + bs - 1) / bs;
+      const int w_lo = min(tid * wpt, words), w_hi = min(w_lo + wpt, words);
+      int c = 0;
+      for (int w = w_lo; w < w_hi; ++w) c += __popc(live[w]);
+      int total = 0;
+      int off = block_excl_scan_i(c, red_i, &total);
+      if (total <= kHistQueue) {  // (block-uniform)
+        qn = total;
+        for (int w = w_lo; w < w_hi; ++w) {
+          uint32_t bits = live[w];
+          while (bits) {  // eight loads in flight
+            float v[8];
+            int k = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (bits) {
+                const int b = __ffs(bits) - 1;
+                bits &= bits - 1u;
+                v[j] = load_logit(base, DT, w * 32 + b);
+                k = j + 1;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (j < k) queue[off + j] = v[j];
+            off += k;
+          }
+        }
+        break;  // (one sub-chunk)
+      }
+    }
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+      const int nv = sn / VE;
+      const uint4* v4 = reinterpret_cast<const uint4*>(base);
+      for (int v0 = tid; v0 < nv; v0 += 4 * bs) {  // four vectors per thread in flight
+        uint4 r[4];
+        uint32_t lb[4];
+        bool in[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int vi = v0 + u * bs;
+          in[u] = vi < nv;
+          lb[u] = in[u] ? (live[(vi * VE) >> 5] >> ((vi * VE) & 31)) & kVecBits : 0u;
+          if (RAW ? in[u] : lb[u] != 0u) r[u] = ld_stream_u4(v4 + vi);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (!(RAW ? in[u] : lb[u] != 0u)) continue;
+          any_l |= lb[u] != 0u;
+          any_v = 1;
+          const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+          for (int i = 0; i < VE; ++i) {
+            const float x = DT == GS_DTYPE_F32 ? __uint_as_float(w[i]) : ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]));
+            const bool l = (lb[u] >> i) & 1u;
+            lmax = fmaxf(lmax, l ? x : -INFINITY);
+            if (RAW) {
+              rmax = fmaxf(rmax, x);
+              bad |= !(x <= lim);
+            } else {
+              bad |= l && !(x <= lim);
+            }
+          }
+        }
+      }
+      done = nv * VE;
+    }
+    for (int i = done + tid; i < sn; i += bs) {
+      const bool l = (live[i >> 5] >> (i & 31)) & 1u;
+      if (!(RAW || l)) continue;
+      const float x = load_logit(base, DT, i);
+      any_l |= l;
+      any_v = 1;
+      if (l) lmax = fmaxf(lmax, x);
+      if (RAW) rmax = fmaxf(rmax, x);
+      if (RAW || l) bad |= !(x <= lim);
+    }
+  }
+  if (qn >= 0) {
+    __syncthreads();
+    for (int i = tid; i < qn; i += bs) {
+      const float x = queue[i];
+      lmax = fmaxf(lmax, x);
+      bad |= !(x <= lim);
+    }
+    any_l = qn > 0;
+  }
+  lmax = block_max_f(lmax, red_f);
+  if (RAW) rmax = block_max_f(rmax, red_f);
+  nallow = block_sum_i(nallow, red_i);
+  bad = __syncthreads_or(bad);
+  any_l = __syncthreads_or(any_l);
+  any_v = __syncthreads_or(any_v);
+  if (tid == 0) {
+    s_max[0] = lmax;
+    s_max[1] = rmax;
+    s_max[2] = static_cast<float>(any_l);
+    s_max[3] = static_cast<float>(any_v);
+  }
   for (int b = tid; b < kNB; b += bs) {
     cnt[b] = 0;
     qs[b] = 0;
   }
-  // Two values at once (packed f32x2 arithmetic); l0 / l1: the value is live.  Per live
-  // value: its bin's count, and q (the deepest bin's mass, below e^-40 of the top, is
-  // taken as 0).
-  const float2 c_width = make_float2(width, width), c_invT = make_float2(invT, invT);
-  auto add2 = [&](float r0, float r1, bool l0, bool l1) {
+  cl.sync();
+  float Mraw = -INFINITY, Rraw = -INFINITY;
+  bool row_l = false, row_v = false;
+#pragma unroll
+  for (int r = 0; r < kCluster; ++r) {
+    const float* pm = cl.map_shared_rank(s_max, r);
+    Mraw = fmaxf(Mraw, pm[0]);
+    Rraw = fmaxf(Rraw, pm[1]);
+    row_l |= pm[2] != 0.0f;
+    row_v |= pm[3] != 0.0f;
+  }
+  const float Mx = cap != 0.0f ? (row_l ? softcap(Mraw, cap, inv_cap) : -INFINITY) : Mraw;
+  const float Rm = cap != 0.0f ? (row_v ? softcap(Rraw, cap, inv_cap) : -INFINITY) : Rraw;
+
+  // ---- phase 1: histogram and sums ----
+  // Capped values, two at once (packed f32x2 arithmetic).
+  auto cap2 = [&](float r0, float r1) {
     float2 x = make_float2(r0, r1);
     if (cap != 0.0f) {
       float2 z;
@@ -301,9 +465,18 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
       if (!(z.x < kSoftcapPolyZ)) x.x = softcap(r0, cap, inv_cap);  // |x| >= c (and NaN)
       if (!(z.y < kSoftcapPolyZ)) x.y = softcap(r1, cap, inv_cap);
     }
-    l0 = l0 && x.x > -INFINITY;  // -inf: not a finite candidate (NaN rows are flagged)
+    return x;
+  };
+  // Two capped values; l0 / l1: the value is live.  Per live value: e^((x - Mx)/T) (as
+  // 2^(d·a2), a2 split in two products) into `acc`, its bin's count, and q (the deepest
+  // bin's mass, below e^-40 of the top, is taken as 0).
+  const float2 c_width = make_float2(width, width), c_invT = make_float2(invT, invT);
+  auto hist2 = [&](float2 x, bool l0, bool l1, float& acc) {
+    l0 = l0 && x.x > -INFINITY;  // -inf (no soft cap): not a finite candidate
     l1 = l1 && x.y > -INFINITY;
     const float d0 = fmaxf(Mx - x.x, 0.0f), d1 = fmaxf(Mx - x.y, 0.0f);
+    const float e0 = ex2_approx(fmaf(-d0, a2_lo, -d0 * a2_hi)), e1 = ex2_approx(fmaf(-d1, a2_lo, -d1 * a2_hi));
+    acc += (l0 ? e0 : 0.0f) + (l1 ? e1 : 0.0f);
     const int b0 = static_cast<int>(fminf(d0 * scale, static_cast<float>(kNB - 1)));
     const int b1 = static_cast<int>(fminf(d1 * scale, static_cast<float>(kNB - 1)));
     // 1 - e^-dl by its Taylor series (dl <= 0.0105: the truncation is below 1e-12)
@@ -326,40 +499,84 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
       if (q1) atomicAdd(&qs[b1], q1);
     }
   };
-  for (int s0 = 0; s0 < n; s0 += kHistSub) {
-    const int sn = n - s0 < kHistSub ? n - s0 : kHistSub;
-    __syncthreads();
-    build_live(live, mrow, lo + s0, sn, hrow, hl, tid, bs);
-    const unsigned char* base = rowbase + (lo + s0) * ESZ;
-    int done = 0;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) == 0) {
-      const int nv = sn / VE;
-      const uint4* v4 = reinterpret_cast<const uint4*>(base);
-      for (int v0 = tid; v0 < nv; v0 += 4 * bs) {  // four vectors per thread in flight
-        uint4 r[4];
-        uint32_t bits[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int vi = v0 + u * bs;
-          bits[u] = vi < nv ? (live[(vi * VE) >> 5] >> ((vi * VE) & 31)) & ((1u << VE) - 1u) : 0u;
-          if (bits[u]) r[u] = ld_stream_u4(v4 + vi);
+  // (a thread adds at most 64 terms of at most 1 in float per sub-chunk, as the streaming
+  // pass does per tile; the sub-chunk sums add in double)
+  double ssum = 0.0, rsum = 0.0;
+  if (qn >= 0) {
+    float sacc = 0.0f;
+    for (int i = 2 * tid; i < qn; i += 2 * bs) {
+      const bool has1 = i + 1 < qn;
+      hist2(cap2(queue[i], has1 ? queue[i + 1] : 0.0f), true, has1, sacc);
+    }
+    ssum = static_cast<double>(sacc);
+  } else {
+    for (int s0 = 0; s0 < n; s0 += kHistSub) {
+      const int sn = n - s0 < kHistSub ? n - s0 : kHistSub;
+      const unsigned char* base = rowbase + (lo + s0) * ESZ;
+      if (!one_pass_bits) {
+        __syncthreads();
+        build_live(live, mrow, lo + s0, sn, hrow, hl, tid, bs);
+      }
+      float sacc = 0.0f, racc = 0.0f;
+      // per pair of values: capped, raw sum (every id), histogram (live ids)
+      auto pair = [&](float r0, float r1, bool v1, uint32_t lbits) {
+        const float2 x = cap2(r0, r1);
+        if (RAW) {
+          const float g0 = x.x - Rm, g1 = x.y - Rm;
+          racc += ex2_approx(fmaf(g0, kL2eLo, g0 * kL2eHi)) + (v1 ? ex2_approx(fmaf(g1, kL2eLo, g1 * kL2eHi)) : 0.0f);
         }
+        if (lbits & 3u) hist2(x, lbits & 1u, (lbits >> 1) & 1u, sacc);
+      };
+      int done = 0;
+      if ((reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+        const int nv = sn / VE;
+        const uint4* v4 = reinterpret_cast<const uint4*>(base);
+        for (int v0 = tid; v0 < nv; v0 += 4 * bs) {
+          uint4 r[4];
+          uint32_t lb[4];
+          bool in[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (!bits[u]) continue;
-          const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+          for (int u = 0; u < 4; ++u) {
+            const int vi = v0 + u * bs;
+            in[u] = vi < nv;
+            lb[u] = in[u] ? (live[(vi * VE) >> 5] >> ((vi * VE) & 31)) & kVecBits : 0u;
+            if (RAW ? in[u] : lb[u] != 0u) r[u] = ld_stream_u4(v4 + vi);
+          }
 #pragma unroll
-          for (int i = 0; i < VE; i += 2) {
-            const float a0 = DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : bf16_lo(w[i >> 1]);
-            const float a1 = DT == GS_DTYPE_F32 ? __uint_as_float(w[(i + 1) & 3]) : bf16_hi(w[i >> 1]);
-            add2(a0, a1, (bits[u] >> i) & 1u, (bits[u] >> (i + 1)) & 1u);
+          for (int u = 0; u < 4; ++u) {
+            if (!(RAW ? in[u] : lb[u] != 0u)) continue;
+            const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+            for (int i = 0; i < VE; i += 2) {
+              const float a0 = DT == GS_DTYPE_F32 ? __uint_as_float(w[i & 3]) : bf16_lo(w[i >> 1]);
+              const float a1 = DT == GS_DTYPE_F32 ? __uint_as_float(w[(i + 1) & 3]) : bf16_hi(w[i >> 1]);
+              pair(a0, a1, true, lb[u] >> i);
+            }
           }
         }
+        done = nv * VE;
       }
-      done = nv * VE;
+      for (int i = done + tid; i < sn; i += bs) {
+        const uint32_t l = (live[i >> 5] >> (i & 31)) & 1u;
+        if (RAW || l) pair(load_logit(base, DT, i), 0.0f, false, l);
+      }
+      ssum += static_cast<double>(sacc);
+      rsum += static_cast<double>(racc);
     }
-    for (int i = done + tid; i < sn; i += bs)
-      if ((live[i >> 5] >> (i & 31)) & 1u) add2(load_logit(base, DT, i), 0.0f, true, false);
+  }
+  ssum = block_sum_d(ssum, red_d);
+  if (RAW) rsum = block_sum_d(rsum, red_d);
+  if (tid == 0) {
+    UnitStat u{};
+    u.m = Mx;
+    u.raw_m = Rm;
+    u.s = Mx > -INFINITY ? ssum : 0.0;
+    u.raw_s = Rm > -INFINITY ? rsum : 0.0;
+    u.n_allowed = nallow;
+    u.n_cand = 0;
+    u.flags = (bad || ssum != ssum) ? GS_FLAG_ERR_NONFINITE : 0u;
+    if (A.mask_table != nullptr && state >= A.mask_states) u.flags |= GS_FLAG_ERR_INVALID;
+    W.hstat[rank] = u;
   }
   cl.sync();
   {
@@ -398,7 +615,8 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   if (pp->mode != kModeLarge) return;
   const RowWs W = row_ws(A, row);
   const double T = pp->temperature;
-  const int S = A.splits;
+  const int S = kCluster;              // the histogram CTAs' row statistics
+  const UnitStat* ustats = W.hstat;
   const int64_t V = A.vocab;
   const int32_t state = A.mask_state ? A.mask_state[row] : -1;
   const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
@@ -409,12 +627,12 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   if (tid == 0) s_flags = GS_FLAG_LARGE_PATH;
   __syncthreads();
 
-  // ---- unit statistics of the streaming pass ----
+  // ---- row statistics (the histogram kernel's CTAs) ----
   unsigned fl = 0;
   int na = 0;
   float mx = -INFINITY, rm = -INFINITY;
   for (int u = tid; u < S; u += bs) {
-    const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+    const UnitStat& st = ustats[u];
     fl |= st.flags;
     na += st.n_allowed;
     mx = fmaxf(mx, st.m);
@@ -427,7 +645,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   double rs = 0.0;
   if (A.want_raw) {
     for (int u = tid; u < S; u += bs) {
-      const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+      const UnitStat& st = ustats[u];
       if (st.raw_m > -INFINITY)
         rs = __dadd_rn(rs, __dmul_rn(st.raw_s, exp(static_cast<double>(st.raw_m) - static_cast<double>(rm))));
     }
@@ -499,7 +717,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   double part = 0.0;
   if (M > -INFINITY) {
     for (int u = tid; u < S; u += bs) {
-      const UnitStat& st = A.stats[static_cast<int64_t>(row) * S + u];
+      const UnitStat& st = ustats[u];
       if (st.m > -INFINITY)
         part = __dadd_rn(part, __dmul_rn(st.s, exp(__dsub_rn(__ddiv_rn(static_cast<double>(st.m), T), M))));
     }
@@ -1304,9 +1522,15 @@ cudaError_t launch_large_t(const FinalizeArgs& a, int rows, size_t select_smem, 
   if (!attr) {
     set_smem(large_select_kernel<DT>, large_select_smem_bytes(GS_MAX_HISTORY));
     set_smem(large_resolve_kernel<DT>, res_smem);
+    set_smem(large_hist_kernel<DT, false>, static_cast<size_t>(kHistQueue) * sizeof(float));
+    set_smem(large_hist_kernel<DT, true>, static_cast<size_t>(kHistQueue) * sizeof(float));
     attr = true;
   }
-  large_hist_kernel<DT><<<rows * kCluster, kHistThreads, 0, st>>>(a);
+  const size_t hq_smem = static_cast<size_t>(kHistQueue) * sizeof(float);
+  if (a.want_raw)
+    large_hist_kernel<DT, true><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
+  else
+    large_hist_kernel<DT, false><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
   large_select_kernel<DT><<<rows, kSelectThreads, select_smem, st>>>(a);
   const int parts = static_cast<int>((a.vocab + kGatherIds - 1) / kGatherIds);
   large_gather_kernel<DT><<<rows * parts, kGatherThreads, 0, st>>>(a, parts);

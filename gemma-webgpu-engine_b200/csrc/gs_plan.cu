@@ -212,13 +212,16 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   sa.stats = stats;
   sa.cands = cands;
   sa.row_tau = nullptr;
-  if (smode != 2 && L.kmax > 1) {
+  // (rows on the histogram path take no streaming pass: the histogram kernel computes
+  // their statistics; with no other rows the pass is not launched)
+  const bool stream_pass = smode != 2 && L.any_small;
+  if (stream_pass && L.kmax > 1) {
     sa.row_tau = reinterpret_cast<unsigned long long*>(ws + L.rowtau_off);
     cudaMemsetAsync(sa.row_tau, 0, static_cast<size_t>(rows) * 8, st);
   }
   if (events) cudaEventRecord(events[0], st);
   cudaError_t e = cudaSuccess;
-  if (smode != 2) {
+  if (stream_pass) {
     e = launch_stream(sa, b->dtype, rows, L.stream_smem, st);
     if (e != cudaSuccess) return fmt(err, GS_ECUDA, "streaming pass launch: %s", cudaGetErrorString(e));
   }

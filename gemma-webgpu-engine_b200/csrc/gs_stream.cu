@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) stream_kernel(const __grid_
   const int part = unit - row * A.splits;
   const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
   const int mode = pp->mode;
+  if (mode == kModeLarge) return;  // the histogram kernel takes this row's statistics
   const int k_eff = pp->k_eff;
   const double a2 = pp->a2;
   const float a2_hi = pp->a2_hi;

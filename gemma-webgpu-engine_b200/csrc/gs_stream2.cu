@@ -112,9 +112,6 @@ struct Ld<GS_DTYPE_BF16> {
   }
 };
 
-constexpr float kL2eHi = 1.44269502162933349609375f;
-constexpr float kL2eLo = 1.925963033500011e-08f;
-
 struct Geom {
   int row;
   int n;        // ids in the unit
@@ -135,6 +132,16 @@ __device__ __forceinline__ Geom geom(const StreamArgs& A, int unit, int te) {
   g.state = A.mask_state ? A.mask_state[g.row] : -1;
   g.masked = A.mask_table != nullptr && g.state >= 0 && g.state < A.mask_states;
   return g;
+}
+
+// The first unit from u on (in steps of `step`) whose row is not on the histogram path
+// (those rows' statistics come from the histogram kernel).
+__device__ __forceinline__ int next_unit(const StreamArgs& A, int u, int n_units, int step) {
+  for (; u < n_units; u += step) {
+    const int row = u / A.splits;
+    if ((A.plans ? A.plans[row].mode : A.plan0.mode) != kModeLarge) break;
+  }
+  return u;
 }
 
 // Gather mode for a unit: a masked unit (without a requested log-probability) whose
@@ -200,7 +207,7 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
   // A ring-mode unit is a sequence of logit tiles; a gather-mode unit is a sequence of
   // mask tiles (its constraint words, kGatherIds ids per stage).  The stage's mode byte
   // tells the consumer which (every unit has at least one stage).
-  int c_unit = first_unit, c_tile = 0, c_ntiles = 0;
+  int c_unit = next_unit(A, first_unit, n_units, total_warps), c_tile = 0, c_ntiles = 0;
   bool c_gather = false;
   Geom cg;
   auto enter_unit = [&]() {
@@ -260,7 +267,7 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
     }
     ++issued;
     if (++c_tile >= c_ntiles) {
-      c_unit += total_warps;
+      c_unit = next_unit(A, c_unit + total_warps, n_units, total_warps);
       enter_unit();
     }
     load_word();
@@ -271,7 +278,8 @@ __global__ void __launch_bounds__(kThreads3, 1) stream2_kernel(const __grid_cons
   // ---- consumer ----
   int cs = 0;        // stage of the next ring tile
   uint32_t cph = 0;  // its mbarrier phase parity
-  for (int unit = first_unit; unit < n_units; unit += total_warps) {
+  for (int unit = next_unit(A, first_unit, n_units, total_warps); unit < n_units;
+       unit = next_unit(A, unit + total_warps, n_units, total_warps)) {
     const Geom g = geom(A, unit, TE);
     const int row = g.row;
     const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
