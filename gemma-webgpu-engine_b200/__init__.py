@@ -8,6 +8,7 @@ and only token ids come back.  The C ABI is include/gsampler.h; this package is 
 Python host side.
 """
 from . import _lib  # noqa: F401
+from .lm_head import GpuLmHead  # noqa: F401
 from .decoding import (  # noqa: F401
     DEFAULT_DECODING_CONFIG,
     DEFAULT_GENERATION_CONFIG,

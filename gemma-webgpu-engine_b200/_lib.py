@@ -50,7 +50,8 @@ EXPORTS = (
     "gs_token_log_probability", "gs_mask_constraint_logits", "gs_build_mask_row", "gs_softcap",
     "gs_softcap_digest", "gs_shard_record_bytes", "gs_shard_partials", "gs_shard_merge", "gs_profile_enable",
     "gs_profile_read", "gs_sample_noalloc", "gs_constraint_create", "gs_constraint_destroy",
-    "gs_constraint_last_error", "gs_constraint_build_masks",
+    "gs_constraint_last_error", "gs_constraint_build_masks", "gs_lm_head_create", "gs_lm_head_destroy",
+    "gs_lm_head_last_error", "gs_lm_head_logits", "gs_lm_head_check",
 )
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -86,6 +87,17 @@ class GsVocabBytesDesc(ctypes.Structure):
         ("vocab", ctypes.c_int64),
         ("offsets", ctypes.c_void_p),
         ("bytes", ctypes.c_void_p),
+    ]
+
+
+class GsLmHeadDesc(ctypes.Structure):
+    _fields_ = [
+        ("vocab", ctypes.c_int64),
+        ("hidden", ctypes.c_int32),
+        ("packed", ctypes.c_void_p),
+        ("row_scales", ctypes.c_void_p),
+        ("input_scale", ctypes.c_float),
+        ("output_scale", ctypes.c_float),
     ]
 
 
@@ -161,6 +173,12 @@ def lib() -> ctypes.CDLL:
     L.gs_constraint_last_error.argtypes = [P]
     L.gs_constraint_last_error.restype = ctypes.c_char_p
     L.gs_constraint_build_masks.argtypes = [P, i32, P, P, P, P, i64, P, i64, P, i64, P, P]
+    L.gs_lm_head_create.argtypes = [P, ctypes.POINTER(GsLmHeadDesc), ctypes.POINTER(P)]
+    L.gs_lm_head_destroy.argtypes = [P]
+    L.gs_lm_head_last_error.argtypes = [P]
+    L.gs_lm_head_last_error.restype = ctypes.c_char_p
+    L.gs_lm_head_logits.argtypes = [P, P, i64, P, i32, P, i64, P]
+    L.gs_lm_head_check.argtypes = [P, ctypes.POINTER(i32)]
     L.gs_softcap.argtypes = [P, P, P, i64, f32, P]
     L.gs_softcap_digest.argtypes = [P, u64, u64, f32, ctypes.POINTER(u64)]
     L.gs_shard_record_bytes.argtypes = [ctypes.POINTER(GsParams), i32, i64, i64]
@@ -172,7 +190,7 @@ def lib() -> ctypes.CDLL:
     L.gs_profile_read.argtypes = [P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
                                   ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64)]
     for name in EXPORTS:
-        if name not in ("gs_last_error", "gs_shard_record_bytes", "gs_constraint_last_error"):
+        if name not in ("gs_last_error", "gs_shard_record_bytes", "gs_constraint_last_error", "gs_lm_head_last_error"):
             getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L

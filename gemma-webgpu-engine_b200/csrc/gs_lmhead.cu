@@ -1,0 +1,810 @@
+// int2 LM head on the 5th-generation tensor cores: the logits the sampler consumes,
+// computed from the final activations and the model's packed 2-bit output weights.
+//
+// Reference: src/webgpu/decode-lm-head.ts.  Packed weights are V rows of hidden/16 u32
+// words; code j of word w (bits 2j..2j+1) multiplies activation element 16w + j and the
+// weight is (code - 2)·rowScale (createGemmaLmHeadShader, :176-256):
+//   logit = srq(rowScale · fma(Σ_j (code_j / 255)·a_j, 255, -(2·sumA)), outputScale)
+// with srq(x, s) = s == 0 ? x : clamp(round(x / s), -128, 127)·s (:196-199).  The
+// activations come from decode-ple-proj-norm-codes.ts:251-258, already on the srq grid of
+// the model's final input scale (a = q·inScale, q an int8 code), with sumA their sum.
+//
+// Here the dot product is exact: with inScale != 0 the activations are read as their
+// int8 codes q = clamp(rint(a / inScale), -128, 127), the weights as int8 (code - 2), and
+// tcgen05.mma kind::i8 accumulates Σ (code - 2)·q in s32 in tensor memory; Σ code·q is that
+// plus 2·Σq, and t = fma(inScale, Σ code·q, -2·sumA) rounds once.  (inScale == 0 keeps the
+// activations in float32: a CUDA-core kernel sums code·a in double, element by element.)
+// The reference's f32 evaluation differs from this exact value by its own rounding.
+//
+// Device layout of the weights (repacked once at creation): tile-major, 128 vocab rows
+// per tile, the hidden axis cut in 128-code chunks: [tile][chunk][128 rows][8 words] —
+// every (tile, chunk) block is 4 KB, one bulk copy.  The activation codes are written per
+// call as the smem image the MMA reads: [pass][chunk][64 rows][128 bytes], 128-byte
+// swizzled, with the 16 codes of each packed word in the order the expansion produces.
+//
+// Kernel (one CTA per SM, persistent over vocab tiles; grid.y: passes of N batch rows):
+//   warp 1      producer: the pass's activation image (once), then every (tile, chunk)
+//               packed block into a ring of 24-40 stages (cp.async.bulk, mbarrier tx
+//               counts): the weight bytes in flight from HBM
+//   warps 8-15  expanders, two groups of four warps: packed 2-bit codes -> int8
+//               (code - 2), one vocab row per thread written straight to its TMEM lane
+//               (tcgen05.st): the weight operand never touches shared memory, whose
+//               bandwidth the 4x inflated codes would otherwise saturate
+//   warp 0      MMA issuer (one elected lane): 4 × tcgen05.mma (K = 32, A from TMEM,
+//               B = the activation image from shared memory) per chunk into a
+//               128 × N s32 accumulator (N = 16 or 64 batch columns), two accumulators in
+//               TMEM (tile i+1 runs while the epilogue drains tile i); also allocates /
+//               frees the TMEM columns
+//   warps 4-7   epilogue: tcgen05.ld of their 32 TMEM lanes (one vocab row per thread,
+//               the batch columns in 16-column loads), then logit = srq(scale · t),
+//               stored coalesced
+// Every wait is bounded (1 s); a timeout sets the handle's error flag and ends the
+// CTA's loops without touching further stages.
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "gs_device.cuh"
+#include "gs_internal.cuh"
+#include "../../include/gsampler.h"
+
+struct gs_lm_head {
+  int device = 0;
+  int64_t vocab = 0;
+  int32_t hidden = 0;
+  int32_t chunks = 0;   // hidden / 128
+  int64_t tiles = 0;    // ceil(vocab / 128)
+  float in_scale = 0.0f;
+  float out_scale = 0.0f;
+  uint32_t* packed = nullptr;  // [tiles][chunks][128][8]
+  float* scales = nullptr;     // [tiles * 128] (0 past vocab)
+  // per-call activation image (grown on demand): [passes][chunks][64][128] | Σq [passes * 64]
+  unsigned char* img = nullptr;
+  size_t img_bytes = 0;
+  int32_t* flag = nullptr;  // device error flag (bit 0: a wait timed out)
+  int num_sms = 0;
+  std::string err;
+};
+
+namespace gs {
+namespace {
+
+constexpr int kLmRows = 128;                    // vocab rows per tile (TMEM lanes)
+constexpr int kLmKC = 128;                      // codes per chunk (one 128-byte swizzle row)
+constexpr int kLmMaxChunks = 12;                // hidden <= 1536
+constexpr int kGroups = 2;                      // expander groups (4 warps, one row each): chunk g -> g % 2
+constexpr int kAStages = 4;                     // weight operand stages in TMEM (32 columns each)
+constexpr int kAColBase = 128;                  // TMEM columns: accumulators [0, 2N), operand stages from 128
+constexpr int kMmaRound = 1;                    // chunks the MMA issuer takes per round
+#ifndef GS_LM_GEMV_ROWS
+#define GS_LM_GEMV_ROWS 4
+#endif
+constexpr int kGemvRows = GS_LM_GEMV_ROWS;      // batches up to this many rows take the dp4a GEMV
+constexpr int kPBytes = kLmRows * kLmKC / 4;    // 4 KB of packed codes per (tile, chunk)
+constexpr int kExpanders = 256;                 // threads expanding packed codes (warps 4-11)
+constexpr int kGroupThreads = kExpanders / kGroups;  // 128: one per vocab row of the tile
+// Warp roles.  The MMA issuer and the producer take the lowest warp ids: the schedulers
+// favour older warps, and the expanders keep their sub-partitions busy in bursts.
+constexpr int kMmaWarp = 0, kProducerWarp = 1;  // (warps 2-3 idle)
+constexpr int kEpiWarp0 = 4;                    // warps 4-7: TMEM lane quadrants 0-3
+constexpr int kExpWarp0 = 8;                    // warps 8-15: two groups of four quadrants
+constexpr int kLmThreads = (kExpWarp0 * 32) + kExpanders;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int kImgRows = 64;                    // rows per pass of the activation image in HBM
+constexpr int kIssue = 8;                       // producer lanes issuing packed-block copies at once
+
+// Shared-memory plan of the kernel for N batch columns (16 or 64): the pass's activation
+// image, then as many packed-block stages as fit (the bytes in flight from HBM per SM),
+// then the barriers.  The expanded weight operand lives in TMEM, not here.
+template <int N>
+struct LmPlan {
+  static constexpr int kQChunk = N * kLmKC;                    // activation codes per chunk
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffP = kOffQ + kLmMaxChunks * kQChunk;
+  static constexpr int kPStages = ((kSmemLimit - kOffP - 1024 - 1024) / kPBytes > 40 ? 40
+                                   : (kSmemLimit - kOffP - 1024 - 1024) / kPBytes) / kIssue * kIssue;
+  static constexpr int kOffBar = kOffP + kPStages * kPBytes;
+  static constexpr int kSmem = kOffBar + 1024 + 1024;          // barriers + alignment slack
+  static constexpr int kTmemCols = 256;                        // two accumulators + operand stages
+  // Instruction descriptor of tcgen05.mma kind::i8: D s32 (bits 4-5 = 2), A and B signed
+  // 8-bit (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+  static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+                                     (static_cast<uint32_t>(kLmRows >> 4) << 24);
+  static_assert(kOffP % 1024 == 0 && 2 * N <= kAColBase, "aligned stages; accumulators below the operands");
+  static_assert(kSmem <= kSmemLimit, "shared memory");
+  static_assert(kPStages >= 2 * kIssue && kPStages % kIssue == 0, "whole producer rounds per ring");
+  static_assert((1 + 2 * kPStages + 2 * kAStages + 5) * 8 + 8 <= 1024, "barriers fit their 1 KB");
+};
+
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte swizzle layout:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset), start address
+// >> 4 in bits 0-13, leading byte offset 1 (unused by this layout), version 1 (bit 46),
+// layout SWIZZLE_128B (2 << 61).  The K = 32 steps inside a row add 32 bytes to the start
+// (the swizzle applies to the absolute address bits, the groups being 1024-aligned).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// Bounded wait that first tests the phase without blocking (mbarrier.test_wait): the
+// pipeline's consumers usually find their phase complete already.
+__device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0 || mbar_wait(bar, parity, kWaitNs);
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// D (TMEM) += A (TMEM: lane m = row m, 4 int8 of K per 32-bit column) × B^T (smem desc).
+__device__ __forceinline__ void tc_mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// One lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p = 0;
+  asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}" : "=r"(p));
+  return p != 0;
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 16 consecutive s32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t* r) {
+  uint32_t v[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = static_cast<int32_t>(v[i]);
+}
+
+// srq(x, s) of decode-lm-head.ts:196-199 (round half to even, IEEE division).
+__device__ __forceinline__ float srq(float x, float s) {
+  if (s == 0.0f) return x;
+  float r = rintf(__fdiv_rn(x, s));
+  r = fminf(fmaxf(r, -128.0f), 127.0f);
+  return __fmul_rn(r, s);
+}
+
+struct LmArgs {
+  const uint32_t* packed;
+  const float* scales;
+  const unsigned char* img;  // activation codes, [passes][chunks][64][128]
+  const int32_t* qsum;       // [passes * 64] Σ q per batch row
+  int32_t pass_rows;         // batch rows per pass (the kernel's N)
+  const float* act_sum;      // [rows]
+  float* logits;
+  int64_t ld;
+  int64_t vocab;
+  int64_t tiles;
+  int32_t chunks;
+  int32_t rows;
+  float in_scale;
+  float out_scale;
+  int32_t* flag;
+};
+
+// Activation codes of one batch row (block b of rows padded to whole passes) in the MMA's
+// smem image: chunk c, 16-byte slot w (swizzled by the row within its 8-row group), byte
+// 4P + k = code of element 16w + 4k + P (the order the expansion writes weight codes).
+__global__ void __launch_bounds__(256) lm_quant_kernel(const float* __restrict__ act, int64_t ld_act, int rows,
+                                                       int hidden, float in_scale, unsigned char* __restrict__ img,
+                                                       int32_t* __restrict__ qsum) {
+  __shared__ int red[8];
+  const int b = blockIdx.x;
+  const int p = b / kImgRows, r = b % kImgRows;
+  const int chunks = hidden / kLmKC;
+  int s = 0;
+  constexpr int kPer = kLmMaxChunks * kLmKC / 256;  // image bytes per thread (loads issued together)
+  float x[kPer];
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int j = threadIdx.x + 256 * u;  // j: byte position in the image row
+    const int e = (j & ~15) + 4 * (j & 3) + ((j & 15) >> 2);
+    x[u] = (b < rows && j < hidden) ? __ldg(act + static_cast<int64_t>(b) * ld_act + e) : 0.0f;
+  }
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int j = threadIdx.x + 256 * u;
+    if (j >= hidden) break;
+    const int c = j / kLmKC, w = (j % kLmKC) >> 4, pos = j & 15;
+    const int q = static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(x[u], in_scale)), -128.0f), 127.0f));
+    s += q;
+    img[(static_cast<size_t>(p) * chunks + c) * (kImgRows * kLmKC) + r * kLmKC + ((w ^ (r & 7)) << 4) + pos] =
+        static_cast<unsigned char>(static_cast<int8_t>(q));
+  }
+  s = warp_sum_i(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int i = 0; i < (blockDim.x >> 5); ++i) t += red[i];
+    qsum[b] = t;
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(kLmThreads, 1) lm_mma_kernel(const __grid_constant__ LmArgs A) {
+  using P = LmPlan<N>;
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte aligned base (the swizzled operand groups need it)
+  const uint32_t raw = smem_addr(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P::kOffBar);
+  uint64_t* qfull = bars;                      // [1]
+  uint64_t* pfull = bars + 1;                  // [kPStages]
+  uint64_t* pfree = pfull + P::kPStages;       // [kPStages]
+  uint64_t* afull = pfree + P::kPStages;       // [kAStages]
+  uint64_t* afree = afull + kAStages;          // [kAStages]
+  uint64_t* accfull = afree + kAStages;        // [2]
+  uint64_t* accfree = accfull + 2;             // [2]
+  uint64_t* mdone = accfree + 2;               // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pass = blockIdx.y;
+  const int C = A.chunks;
+  const int64_t my_tiles = A.tiles > blockIdx.x ? (A.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qfull, 1);
+    for (int s = 0; s < P::kPStages; ++s) {
+      mbar_init(pfull + s, 1);
+      mbar_init(pfree + s, kGroupThreads);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(afull + s, kGroupThreads);  // (the 128 rows of a chunk)
+      mbar_init(afree + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(accfull + s, 1);
+      mbar_init(accfree + s, 128);
+    }
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+  }
+  if (warp == kMmaWarp) {  // TMEM columns for the two accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(P::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto give_up = [&]() {
+    *abort_flag = 1;
+    atomicOr(A.flag, 1);
+  };
+
+  if (warp == kProducerWarp) {
+    // ---------------- producer ----------------
+    // Lanes 0..kIssue-1 each copy one of kIssue consecutive chunks per round (the copies
+    // of one instruction go out together).
+    if (lane == 0) {
+      // the pass's N image rows of every chunk (the HBM image holds kImgRows per chunk)
+      mbar_expect_tx(qfull, static_cast<uint32_t>(C * P::kQChunk));
+      for (int c = 0; c < C; ++c)
+        bulk_g2s(sm + P::kOffQ + c * P::kQChunk,
+                 A.img + (static_cast<size_t>(pass) * C + c) * (kImgRows * kLmKC), P::kQChunk, qfull);
+    }
+    __syncwarp();
+    const int64_t total = my_tiles * C;
+    for (int64_t g0 = 0; g0 < total && !*abort_flag; g0 += kIssue) {
+      const int64_t g = g0 + lane;
+      bool ok = true;
+      if (lane < kIssue && g < total) {
+        const int s = static_cast<int>(g % P::kPStages);  // (kIssue consecutive chunks: distinct stages)
+        const int64_t k = g / P::kPStages;
+        if (k > 0) ok = lm_wait(pfree + s, static_cast<uint32_t>((k - 1) & 1));
+        if (ok) {
+          const int64_t t = blockIdx.x + (g / C) * gridDim.x;
+          const int c = static_cast<int>(g % C);
+          mbar_expect_tx(pfull + s, kPBytes);
+          bulk_g2s(sm + P::kOffP + s * kPBytes, A.packed + (static_cast<size_t>(t) * C + c) * (kPBytes / 4), kPBytes,
+                   pfull + s);
+        }
+      }
+      if (!__all_sync(kFullMask, ok)) {
+        give_up();
+        break;
+      }
+    }
+  } else if (warp >= kExpWarp0) {
+    // ---------------- expanders ----------------
+    // Group k (four warps, one vocab row of the tile per thread: the TMEM lane its warp
+    // may write) expands chunks k, k + 2, ... into operand stage g % 4: the row's 8 packed
+    // words -> 32 columns of int8 (code - 2), column 4w + P holding the codes of elements
+    // 16w + 4k + P in byte k (the order of the activation image).
+    const int et = threadIdx.x - kExpWarp0 * 32;  // 0 .. kExpanders - 1
+    const int grp = et / kGroupThreads, row = et % kGroupThreads;  // row = 32·(warp % 4) + lane
+    const int64_t total = my_tiles * C;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(row & ~31) << 16);
+    for (int64_t g = grp; g < total && !*abort_flag; g += kGroups) {
+      const int s = static_cast<int>(g % P::kPStages), a = static_cast<int>(g % kAStages);
+      const int64_t kp = g / P::kPStages, ka = g / kAStages;
+      const bool ok = lm_wait(pfull + s, static_cast<uint32_t>(kp & 1)) &&
+                      (ka == 0 || lm_wait(afree + a, static_cast<uint32_t>((ka - 1) & 1)));
+      if (!__all_sync(kFullMask, ok)) {  // (the warp leaves together; TMEM stores are warp-collective)
+        give_up();
+        break;
+      }
+      const uint4* src = reinterpret_cast<const uint4*>(sm + P::kOffP + s * kPBytes) + row * 2;
+      const uint4 p0 = src[0], p1 = src[1];
+      mbar_arrive(pfree + s);  // (the row's packed words are in registers)
+      const uint32_t x[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      uint32_t o[32];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        // byte k of word P = code 4k + P, mapped 0..3 -> -2..1: ((v + 0x7E) ^ 0x80) per byte
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[4 * w + q] = (((x[w] >> (2 * q)) & 0x03030303u) + 0x7E7E7E7Eu) ^ 0x80808080u;
+      }
+      tmem_st32(lane_base + static_cast<uint32_t>(kAColBase + 32 * a), o);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(afull + a);
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer ----------------
+    // The whole warp runs the loop (its descriptors stay warp-uniform); one elected lane
+    // issues the MMAs and the commits that track them.
+    const bool leader = elect_one();
+    bool ok = __all_sync(kFullMask, lm_wait(qfull, 0));
+    if (!ok) give_up();
+    int64_t g = 0;
+    const uint64_t qd0 = sw128_desc(smem_addr(sm + P::kOffQ));
+    for (int64_t i = 0; ok && i < my_tiles && !*abort_flag; ++i) {
+      const int j = static_cast<int>(i & 1);
+      const int64_t kacc = i >> 1;
+      if (kacc > 0 && !__all_sync(kFullMask, lm_wait(accfree + j, static_cast<uint32_t>((kacc - 1) & 1)))) {
+        give_up();
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + static_cast<uint32_t>(j * N);
+      // chunks in rounds of kMmaRound: one wait per chunk, then all their MMAs (a round
+      // trip through the barriers costs about as much as the MMAs of several chunks)
+      for (int c = 0; c < C; c += kMmaRound) {
+        const int nc = C - c < kMmaRound ? C - c : kMmaRound;
+        bool okw = true;
+        for (int u = 0; u < nc; ++u)
+          okw = okw && lm_wait(afull + static_cast<int>((g + u) % kAStages), static_cast<uint32_t>(((g + u) / kAStages) & 1));
+        if (!__all_sync(kFullMask, okw)) {
+          give_up();
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (leader) {
+          for (int u = 0; u < nc; ++u) {
+            const int a = static_cast<int>((g + u) % kAStages);
+            // K = 32 steps: 8 TMEM columns of A, 32 bytes (2 descriptor units) of B
+            const uint32_t at = tmem + static_cast<uint32_t>(kAColBase + 32 * a);
+            const uint64_t bd = qd0 + static_cast<uint64_t>(((c + u) * P::kQChunk) >> 4);
+#pragma unroll
+            for (int k = 0; k < kLmKC / 32; ++k)
+              tc_mma_i8_ts(d, at + 8 * k, bd + 2 * k, P::kIdesc, ((c + u) | k) != 0 ? 1u : 0u);
+            tc_commit(afree + a);  // the stage is free once these MMAs have read it
+          }
+        }
+        __syncwarp();
+        g += nc;
+      }
+      if (!ok) break;
+      if (leader) tc_commit(accfull + j);
+      __syncwarp();
+    }
+    // every MMA this warp issued has completed before the columns are freed
+    if (leader) tc_commit(mdone);
+    __syncwarp();
+    if (!__all_sync(kFullMask, lm_wait(mdone, 0))) give_up();
+  } else if (warp >= kEpiWarp0) {
+    // ---------------- epilogue (warps 4-7: TMEM lanes 32·(warp - 4) ..) ----------------
+    const int quad = warp - kEpiWarp0;
+    const int n_here = A.rows - pass * N < N ? A.rows - pass * N : N;
+    const int groups = (n_here + 15) >> 4;  // 16-column TMEM loads needed (block-uniform)
+    for (int64_t i = 0; i < my_tiles && !*abort_flag; ++i) {
+      const int64_t t = blockIdx.x + i * gridDim.x;
+      const int j = static_cast<int>(i & 1);
+      // (warp-uniform: the TMEM loads below are warp-collective)
+      if (!__all_sync(kFullMask, lm_wait(accfull + j, static_cast<uint32_t>((i >> 1) & 1)))) {
+        give_up();
+        break;
+      }
+      tc_fence_after();
+      const int64_t v = t * kLmRows + 32 * quad + lane;
+      const bool in = v < A.vocab;
+      const float scale = in ? A.scales[v] : 0.0f;
+      const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(j * N);
+      for (int q = 0; q < groups; ++q) {
+        int32_t acc[16];
+        tmem_ld16(ta + 16 * q, acc);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (q == groups - 1) {
+          tc_fence_before();
+          mbar_arrive(accfree + j);  // the accumulator's columns are in registers
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int n = 16 * q + u;
+          if (n >= n_here) break;  // (uniform)
+          const int b = pass * N + n;
+          const int32_t scq = acc[u] + 2 * A.qsum[b];  // Σ code·q, exact
+          const float tt = __fmaf_rn(A.in_scale, static_cast<float>(scq), -(2.0f * A.act_sum[b]));
+          if (in) A.logits[static_cast<int64_t>(b) * A.ld + v] = srq(__fmul_rn(scale, tt), A.out_scale);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::kTmemCols) : "memory");
+  }
+}
+
+// Few batch rows (a GEMV): the tensor-core MMA streams a whole 128 × 32 expanded weight
+// tile per instruction, so with a handful of columns it is bound by operand traffic;
+// here the packed words come straight from HBM and dp4a accumulates Σ code·q (unsigned
+// codes × signed activation codes, exact in int32).  Warp w of a tile's block reads the
+// 1 KB of its 32 rows per chunk in two fully coalesced 512-byte loads: lane l holds half
+// (l & 1) of rows l >> 1 and 16 + (l >> 1), and the halves meet in a shuffle at the end.
+// Each (persistent) block quantises the activations itself into shared memory first:
+// word 4w + P of a row holds the codes of elements 16w + 4k + P in byte k (the order
+// the code extraction below produces), rows past `rows` zero; they are read four words
+// at a time.
+template <int NB>
+__global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ LmArgs A, const float* __restrict__ act,
+                                                      int64_t ld_act) {
+  __shared__ __align__(16) uint32_t qw[NB][kLmMaxChunks * 32];  // [row][4·(16-code word) + P]
+  const int C = A.chunks;
+  const int rows = A.rows < NB ? A.rows : NB;
+  for (int i = threadIdx.x; i < NB * C * 32; i += blockDim.x) {
+    const int b = i / (C * 32), j = i % (C * 32);  // j = 4w + P
+    uint32_t word = 0;
+    if (b < rows) {
+      const float* ar = act + static_cast<int64_t>(b) * ld_act + 16 * (j >> 2) + (j & 3);
+      float x[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[k] = __ldg(ar + 4 * k);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float r = fminf(fmaxf(rintf(__fdiv_rn(x[k], A.in_scale)), -128.0f), 127.0f);
+        word |= (static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xffu) << (8 * k);
+      }
+    }
+    qw[b][j] = word;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane & 1;
+  for (int64_t t = blockIdx.x; t < A.tiles; t += gridDim.x) {
+  int32_t acc[2][NB];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[h][b] = 0;
+  // this warp's 32 rows of chunk c: 1 KB at ((t·C + c)·128 + 32·warp)·32 bytes
+  const uint4* wbase = reinterpret_cast<const uint4*>(A.packed) + (static_cast<size_t>(t) * C * kLmRows + 32 * warp) * 2;
+  for (int c0 = 0; c0 < C; c0 += 4) {  // four chunks' loads in flight
+    uint4 x[4][2];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c0 + u < C) {
+        const uint4* p = wbase + static_cast<size_t>(c0 + u) * kLmRows * 2;
+        x[u][0] = ld_stream_u4(p + lane);       // rows lane >> 1, half lane & 1
+        x[u][1] = ld_stream_u4(p + 32 + lane);  // rows 16 + (lane >> 1)
+      }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (c0 + u >= C) break;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t wv[4] = {x[u][h].x, x[u][h].y, x[u][h].z, x[u][h].w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {  // packed word 4·half + w of the row's chunk
+          const uint32_t c0w = wv[w] & 0x03030303u, c1w = (wv[w] >> 2) & 0x03030303u;
+          const uint32_t c2w = (wv[w] >> 4) & 0x03030303u, c3w = (wv[w] >> 6) & 0x03030303u;
+          const int qi = (c0 + u) * 32 + 4 * (4 * half + w);
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const uint4 q = *reinterpret_cast<const uint4*>(&qw[b][qi]);  // words P = 0..3
+            int32_t d = acc[h][b];
+            asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(d) : "r"(c0w), "r"(q.x));
+            asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(d) : "r"(c1w), "r"(q.y));
+            asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(d) : "r"(c2w), "r"(q.z));
+            asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(d) : "r"(c3w), "r"(q.w));
+            acc[h][b] = d;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[h][b] += __shfl_xor_sync(kFullMask, acc[h][b], 1);
+  // lane pair (2k, 2k+1) holds rows k and 16 + k: the even lane writes the first, the odd the second
+  const int64_t v = t * kLmRows + 32 * warp + (lane >> 1) + 16 * half;
+  if (v < A.vocab) {
+    const float scale = A.scales[v];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      if (b < rows) {
+        const float tt = __fmaf_rn(A.in_scale, static_cast<float>(half ? acc[1][b] : acc[0][b]), -(2.0f * A.act_sum[b]));
+        A.logits[static_cast<int64_t>(b) * A.ld + v] = srq(__fmul_rn(scale, tt), A.out_scale);
+      }
+    }
+  }
+  }
+}
+
+// Unquantised activations (inScale == 0): one thread per vocab row and batch row, Σ code·a
+// in double element by element (every product exact), t = (float)(Σ - 2·sumA).
+__global__ void __launch_bounds__(128) lm_f64_kernel(const __grid_constant__ LmArgs A, const float* __restrict__ act,
+                                                     int64_t ld_act, int hidden) {
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * 128 + threadIdx.x;
+  const int b = blockIdx.y;
+  if (v >= A.vocab || b >= A.rows) return;
+  const int64_t t = v / kLmRows;
+  const int r = static_cast<int>(v % kLmRows);
+  const float* a = act + static_cast<int64_t>(b) * ld_act;
+  double s = 0.0;
+  for (int c = 0; c < A.chunks; ++c) {
+    const uint32_t* wrow = A.packed + ((static_cast<size_t>(t) * A.chunks + c) * kLmRows + r) * 8;
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t x = wrow[w];
+      const float* aw = a + c * kLmKC + w * 16;
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj)
+        s = __dadd_rn(s, __dmul_rn(static_cast<double>((x >> (2 * jj)) & 3u), static_cast<double>(__ldg(aw + jj))));
+    }
+  }
+  const float tt = static_cast<float>(__dsub_rn(s, 2.0 * static_cast<double>(A.act_sum[b])));
+  A.logits[static_cast<int64_t>(b) * A.ld + v] = srq(__fmul_rn(A.scales[v], tt), A.out_scale);
+}
+
+gs_status lfail(gs_lm_head* h, gs_status s, const std::string& m) {
+  h->err = m;
+  return s;
+}
+
+void release(gs_lm_head* h) {
+  cudaFree(h->packed);
+  cudaFree(h->scales);
+  cudaFree(h->img);
+  cudaFree(h->flag);
+  h->packed = nullptr;
+  h->scales = nullptr;
+  h->img = nullptr;
+  h->flag = nullptr;
+}
+
+}  // namespace
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" {
+
+gs_status gs_lm_head_create(gs_ctx* ctx, const gs_lm_head_desc* d, gs_lm_head** out) {
+  if (!out) return GS_EINVAL;
+  *out = nullptr;
+  if (!ctx || !d) return GS_EINVAL;
+  if (d->vocab <= 0 || d->vocab >= (1ll << 31) || !d->packed || !d->row_scales) {
+    ctx_set_error(ctx, "LM head: vocab in (0, 2^31), packed weights and row scales are required");
+    return GS_EINVAL;
+  }
+  if (d->hidden <= 0 || d->hidden % kLmKC != 0 || d->hidden > kLmKC * kLmMaxChunks) {
+    ctx_set_error(ctx, "LM head: hidden must be a multiple of 128, at most 1536");
+    return GS_EINVAL;
+  }
+  if (!(d->input_scale >= 0.0f) || !(d->output_scale >= 0.0f) || d->input_scale == INFINITY ||
+      d->output_scale == INFINITY) {
+    ctx_set_error(ctx, "LM head: input / output scales must be finite and >= 0");
+    return GS_EINVAL;
+  }
+  auto* h = new gs_lm_head();
+  h->device = ctx_device(ctx);
+  h->vocab = d->vocab;
+  h->hidden = d->hidden;
+  h->chunks = d->hidden / kLmKC;
+  h->tiles = (d->vocab + kLmRows - 1) / kLmRows;
+  h->in_scale = d->input_scale;
+  h->out_scale = d->output_scale;
+  const int words = d->hidden / 16;
+  // tile-major repack (decode-lm-head.ts keeps row-major words; rows past vocab hold code 2,
+  // weight 0, and scale 0)
+  std::vector<uint32_t> tp(static_cast<size_t>(h->tiles) * h->chunks * kLmRows * 8, 0xAAAAAAAAu);
+  for (int64_t v = 0; v < d->vocab; ++v) {
+    const int64_t t = v / kLmRows;
+    const int r = static_cast<int>(v % kLmRows);
+    for (int c = 0; c < h->chunks; ++c)
+      std::memcpy(&tp[((static_cast<size_t>(t) * h->chunks + c) * kLmRows + r) * 8],
+                  d->packed + static_cast<size_t>(v) * words + c * 8, 32);
+  }
+  std::vector<float> sc(static_cast<size_t>(h->tiles) * kLmRows, 0.0f);
+  std::memcpy(sc.data(), d->row_scales, static_cast<size_t>(d->vocab) * sizeof(float));
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != h->device) cudaSetDevice(h->device);
+  cudaError_t e = cudaMalloc(&h->packed, tp.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(h->packed, tp.data(), tp.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&h->scales, sc.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(h->scales, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&h->flag, 4);
+  if (e == cudaSuccess) e = cudaMemset(h->flag, 0, 4);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->device);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(lm_mma_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, LmPlan<16>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(lm_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, LmPlan<64>::kSmem);
+  if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    ctx_set_error(ctx, (std::string("LM head upload: ") + cudaGetErrorString(e)).c_str());
+    release(h);
+    delete h;
+    return GS_ENOMEM;
+  }
+  *out = h;
+  return GS_OK;
+}
+
+gs_status gs_lm_head_destroy(gs_lm_head* h) {
+  if (!h) return GS_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != h->device) cudaSetDevice(h->device);
+  cudaDeviceSynchronize();
+  release(h);
+  if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+  delete h;
+  return GS_OK;
+}
+
+const char* gs_lm_head_last_error(const gs_lm_head* h) { return h ? h->err.c_str() : ""; }
+
+gs_status gs_lm_head_logits(gs_lm_head* h, const float* activation, int64_t ld_activation, const float* activation_sum,
+                            int32_t rows, float* logits, int64_t ld_logits, void* stream) {
+  if (!h) return GS_EINVAL;
+  if (rows < 0 || (rows > 0 && (!activation || !activation_sum || !logits)))
+    return lfail(h, GS_EINVAL, "activation, activation_sum and logits are required");
+  if (ld_activation < h->hidden || ld_logits < h->vocab)
+    return lfail(h, GS_EINVAL, "ld_activation >= hidden and ld_logits >= vocab are required");
+  if (rows > 65535) return lfail(h, GS_EUNSUPPORTED, "at most 65535 rows per call");
+  if (rows == 0) return GS_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != h->device) cudaSetDevice(h->device);
+  auto restore = [&]() {
+    if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+  };
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  LmArgs a{};
+  a.packed = h->packed;
+  a.scales = h->scales;
+  a.act_sum = activation_sum;
+  a.logits = logits;
+  a.ld = ld_logits;
+  a.vocab = h->vocab;
+  a.tiles = h->tiles;
+  a.chunks = h->chunks;
+  a.rows = rows;
+  a.in_scale = h->in_scale;
+  a.out_scale = h->out_scale;
+  a.flag = h->flag;
+  cudaError_t e = cudaSuccess;
+  if (h->in_scale == 0.0f) {
+    dim3 grid(static_cast<unsigned>(h->tiles), static_cast<unsigned>(rows));
+    lm_f64_kernel<<<grid, 128, 0, st>>>(a, activation, ld_activation, h->hidden);
+    e = cudaGetLastError();
+  } else {
+    const int passes = (rows + kImgRows - 1) / kImgRows;
+    const size_t img = static_cast<size_t>(passes) * h->chunks * (kImgRows * kLmKC);
+    const size_t need = img + static_cast<size_t>(passes) * kImgRows * 4;
+    if (need > h->img_bytes) {  // (grown on demand; the first call of a larger batch allocates)
+      cudaStreamSynchronize(st);
+      cudaFree(h->img);
+      h->img = nullptr;
+      h->img_bytes = 0;
+      e = cudaMalloc(&h->img, need);
+      if (e != cudaSuccess) {
+        restore();
+        return lfail(h, GS_ENOMEM, std::string("activation image: ") + cudaGetErrorString(e));
+      }
+      h->img_bytes = need;
+    }
+    a.img = h->img;
+    a.qsum = reinterpret_cast<const int32_t*>(h->img + img);
+    if (rows > kGemvRows)
+      lm_quant_kernel<<<passes * kImgRows, 256, 0, st>>>(activation, ld_activation, rows, h->hidden, h->in_scale,
+                                                         h->img, reinterpret_cast<int32_t*>(h->img + img));
+    const int gx = static_cast<int>(h->tiles < h->num_sms ? h->tiles : h->num_sms);
+    // (up to kGemvRows rows: the dp4a GEMV; a few more: a 16-column accumulator, a smaller
+    // activation image and a deeper packed-block ring; otherwise passes of 64 rows, the
+    // image's pass size)
+    if (rows <= kGemvRows) {
+      // persistent: as many blocks as stay resident (whole waves), each looping over tiles
+      auto gemv = [&](auto kern) {
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, 0);
+        const int64_t g = static_cast<int64_t>(per_sm > 0 ? per_sm : 1) * h->num_sms;
+        kern<<<static_cast<unsigned>(g < h->tiles ? g : h->tiles), 128, 0, st>>>(a, activation, ld_activation);
+      };
+      if (rows <= 1) gemv(lm_gemv_kernel<1>);
+      else if (rows <= 2) gemv(lm_gemv_kernel<2>);
+      else if (rows <= 4) gemv(lm_gemv_kernel<4>);
+      else if (rows <= 8) gemv(lm_gemv_kernel<8>);
+      else gemv(lm_gemv_kernel<16>);
+      static_assert(kGemvRows <= 16, "GEMV instantiations cover up to 16 rows");
+    } else if (rows <= 16) {
+      a.pass_rows = 16;
+      lm_mma_kernel<16><<<dim3(gx, 1), kLmThreads, LmPlan<16>::kSmem, st>>>(a);
+    } else {
+      a.pass_rows = 64;
+      lm_mma_kernel<64><<<dim3(gx, passes), kLmThreads, LmPlan<64>::kSmem, st>>>(a);
+    }
+    e = cudaGetLastError();
+  }
+  restore();
+  if (e != cudaSuccess) return lfail(h, GS_ECUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
+  return GS_OK;
+}
+
+gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out) {
+  if (!h || !timed_out) return GS_EINVAL;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != h->device) cudaSetDevice(h->device);
+  int32_t f = 0;
+  cudaError_t e = cudaMemcpy(&f, h->flag, 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && f) e = cudaMemset(h->flag, 0, 4);
+  if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return lfail(h, GS_ECUDA, std::string("LM head flag: ") + cudaGetErrorString(e));
+  *timed_out = f;
+  return f ? GS_ETIMEOUT : GS_OK;
+}
+
+}  // extern "C"

@@ -206,6 +206,44 @@ gs_status gs_constraint_build_masks(gs_constraint* c, int32_t n_states, const in
                                     const int32_t* extra_legal, int64_t n_extra, uint32_t* table,
                                     int64_t mask_words, int32_t* dead_end, void* stream);
 
+/* ---- int2 LM head: the logits the sampler consumes ----
+ * Replaces the Gemma int2 LM head pass (src/webgpu/decode-lm-head.ts:
+ * createGemmaLmHeadResources :95-166, encodeGemmaLmHead :168-176, the shader :178-256):
+ *   logit[b][v] = srq(row_scales[v] · (Σ_j code_j(v)·a[b][j] - 2·activation_sum[b]),
+ *                     output_scale)
+ * with code_j(v) = (packed[v][j/16] >> 2(j%16)) & 3 (weight code_j - 2) and
+ * srq(x, s) = s == 0 ? x : clamp(round_half_even(x / s), -128, 127)·s.  The dot product
+ * is exact: with input_scale != 0 the activations are read as their int8 srq codes
+ * clamp(rint(a / input_scale), -128, 127) (the grid the producing pass writes them on,
+ * decode-ple-proj-norm-codes.ts:251-258) and Σ code·q is an integer; the bracket is then
+ * fma(input_scale, Σ code·q, -2·sumA) in float32.  With input_scale == 0 the activations
+ * stay float32 and the sum is taken in double in element order.  The reference's f32
+ * evaluation differs from these by its own rounding only. */
+typedef struct gs_lm_head_desc {
+  int64_t vocab;              /* output features (rows of the packed matrix), < 2^31 */
+  int32_t hidden;             /* activation length: a multiple of 128, at most 1536 */
+  const uint32_t* packed;     /* host [vocab][hidden/16] u32, decode-lm-head.ts's row-major layout */
+  const float* row_scales;    /* host [vocab] */
+  float input_scale;          /* srq step of the activations (0: unquantised float32) */
+  float output_scale;         /* srq step of the logits (0: none) */
+} gs_lm_head_desc;
+
+typedef struct gs_lm_head gs_lm_head;
+
+/* Uploads (and repacks) the weights to the context's device (set-up; allocates). */
+gs_status gs_lm_head_create(gs_ctx* ctx, const gs_lm_head_desc* desc, gs_lm_head** out);
+gs_status gs_lm_head_destroy(gs_lm_head* h);
+const char* gs_lm_head_last_error(const gs_lm_head* h);
+/* logits[b * ld_logits + v] for b < rows (device buffers: activation [rows][ld_activation]
+ * float32, activation_sum [rows], logits).  The first call with more rows than before
+ * grows the handle's activation staging (allocates).  Asynchronous on `stream`. */
+gs_status gs_lm_head_logits(gs_lm_head* h, const float* activation, int64_t ld_activation,
+                            const float* activation_sum, int32_t rows, float* logits, int64_t ld_logits,
+                            void* stream);
+/* Reads and clears the device-side error flag (synchronising): GS_ETIMEOUT when a bounded
+ * wait inside the kernel ran out (its logits are then unspecified). */
+gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out);
+
 /* Elementwise soft cap, the same routine the sampling pass applies (no reference
  * counterpart: the reference never applies its declared cap). */
 gs_status gs_softcap(gs_ctx* ctx, const float* in, float* out, int64_t n, float cap, void* stream);

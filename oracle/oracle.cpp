@@ -12,6 +12,7 @@
 //   src/runtime/sampling.ts:82-90    cumulativeCut
 //   src/runtime/sampling.ts:92-96    argmax
 //   src/runtime/constraints.ts:159-173 maskConstraintLogits
+//   src/webgpu/decode-lm-head.ts:176-256 int2 LM head (the producer of the logits)
 //
 // Parity pins: tests/test_oracle_golden.py checks this file against every
 // known-answer test of tests/sampling.spec.ts and tests/constraints.spec.ts:158-161
@@ -695,6 +696,104 @@ void oracle_constraint_masks(int32_t nodes, const int32_t* range_off, const uint
         any = true;
       }
     if (dead_end) dead_end[s] = any ? 0 : 1;
+  }
+}
+
+// ------------------------------------------------------------------ LM head
+// The int2 LM head of src/webgpu/decode-lm-head.ts.  Packed weights: V rows of hidden/16
+// u32 words; code j of word w (bits 2j..2j+1 — unpack4x8unorm of (word >> 2P) & 0x03030303
+// gives the codes of elements 4k + P, k = byte) multiplies activation element 16w + j, and
+// the weight is (code - 2)·scale[v]:
+//   sum   = Σ_j (code_j / 255)·a_j                        (f32, decode-lm-head.ts:219-235)
+//   logit = srq(scale[v]·fma(sum, 255, -(2·sumA)), outputScale)   (:239-247)
+//   srq(x, s) = s == 0 ? x : clamp(round(x / s), -128, 127)·s      (:196-199; round: half
+//               to even)
+// sumA is the sum of the activations the producing kernel writes beside them
+// (decode-ple-proj-norm-codes.ts:251-258).
+
+static float o_srq(float x, float s) {
+  if (s == 0.0f) return x;
+  float r = std::nearbyint(x / s);  // (default rounding mode: nearest, ties to even)
+  r = std::fmin(std::fmax(r, -128.0f), 127.0f);
+  return r * s;
+}
+
+static inline int o_code(const uint32_t* row, int j) { return static_cast<int>((row[j >> 4] >> (2 * (j & 15))) & 3u); }
+
+// The row-major-subgroups shader (decode-lm-head.ts:176-256) in its own f32 association:
+// lane l of a 32-wide subgroup adds the words l, l+32, ... ((dot0 + dot1) + (dot2 + dot3),
+// each dot summed left to right), then a butterfly subgroupAdd.  WGSL leaves the order of
+// dot() and subgroupAdd open, so this is one legal evaluation, not the only one.
+void oracle_lm_head_shader_f32(const uint32_t* packed, const float* scales, int64_t vocab, int hidden,
+                               const float* act, const float* act_sum, int rows, float out_scale,
+                               float* logits, int64_t ld_logits) {
+  const int words = hidden / 16;
+  for (int b = 0; b < rows; ++b) {
+    const float* a = act + static_cast<int64_t>(b) * hidden;
+    for (int64_t v = 0; v < vocab; ++v) {
+      const uint32_t* row = packed + v * words;
+      float lane[32];
+      for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int w = l; w < words; w += 32) {
+          float d[4];
+          for (int c = 0; c < 4; ++c) {  // values[c] = a[16w + 4c .. 16w + 4c + 3]
+            float t = 0.0f;
+            for (int p = 0; p < 4; ++p) {
+              const float code = static_cast<float>((row[w] >> (8 * c + 2 * p)) & 3u) / 255.0f;
+              t = t + code * a[16 * w + 4 * c + p];
+            }
+            d[c] = t;
+          }
+          acc = acc + ((d[0] + d[1]) + (d[2] + d[3]));
+        }
+        lane[l] = acc;
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        float nx[32];
+        for (int l = 0; l < 32; ++l) nx[l] = lane[l] + lane[l ^ o];
+        for (int l = 0; l < 32; ++l) lane[l] = nx[l];
+      }
+      const float t = std::fmaf(lane[0], 255.0f, -(2.0f * act_sum[b]));
+      logits[static_cast<int64_t>(b) * ld_logits + v] = o_srq(scales[v] * t, out_scale);
+    }
+  }
+}
+
+// The same logits computed exactly, as the CUDA path does.
+//   in_scale != 0: the activations are read as their int8 codes q = clamp(rint(a / in_scale),
+//     -128, 127) (the srq grid the producing kernel writes them on), the dot product
+//     Σ code·q is an exact integer, and t = fma(in_scale, Σ code·q, -2·sumA) rounds once.
+//   in_scale == 0: Σ code·a accumulates in double, element by element in order (every
+//     product is exact), and t = (float)(Σ - 2·sumA).
+// logit = srq(scale[v]·t, outputScale).
+void oracle_lm_head_exact(const uint32_t* packed, const float* scales, int64_t vocab, int hidden,
+                          const float* act, const float* act_sum, int rows, float in_scale, float out_scale,
+                          float* logits, int64_t ld_logits) {
+  const int words = hidden / 16;
+  std::vector<int> q(static_cast<size_t>(hidden));
+  for (int b = 0; b < rows; ++b) {
+    const float* a = act + static_cast<int64_t>(b) * hidden;
+    if (in_scale != 0.0f)
+      for (int j = 0; j < hidden; ++j) {
+        float r = std::nearbyint(a[j] / in_scale);
+        r = std::fmin(std::fmax(r, -128.0f), 127.0f);
+        q[j] = static_cast<int>(r);
+      }
+    for (int64_t v = 0; v < vocab; ++v) {
+      const uint32_t* row = packed + v * words;
+      float t;
+      if (in_scale != 0.0f) {
+        int64_t s = 0;
+        for (int j = 0; j < hidden; ++j) s += static_cast<int64_t>(o_code(row, j)) * q[j];
+        t = std::fmaf(in_scale, static_cast<float>(s), -(2.0f * act_sum[b]));
+      } else {
+        double s = 0.0;
+        for (int j = 0; j < hidden; ++j) s = s + static_cast<double>(o_code(row, j)) * static_cast<double>(a[j]);
+        t = static_cast<float>(s - 2.0 * static_cast<double>(act_sum[b]));
+      }
+      logits[static_cast<int64_t>(b) * ld_logits + v] = o_srq(scales[v] * t, out_scale);
+    }
   }
 }
 

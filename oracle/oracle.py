@@ -96,6 +96,12 @@ def lib():
         L.oracle_sample_rows.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                          P, ctypes.c_int64, P, P, ctypes.c_int64, P,
                                          P, ctypes.c_int32, P, P, P, P, ctypes.c_int]
+        L.oracle_lm_head_shader_f32.argtypes = [P, P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int,
+                                                ctypes.c_float, P, ctypes.c_int64]
+        L.oracle_lm_head_shader_f32.restype = None
+        L.oracle_lm_head_exact.argtypes = [P, P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, ctypes.c_float,
+                                           ctypes.c_float, P, ctypes.c_int64]
+        L.oracle_lm_head_exact.restype = None
         _lib = L
     return _lib
 
@@ -206,6 +212,27 @@ def softcap_check(cap: float, threads: int = 0) -> tuple[float, int]:
     u, d = ctypes.c_double(), ctypes.c_uint64()
     lib().oracle_softcap_check(float(np.float32(cap)), threads, ctypes.byref(u), ctypes.byref(d))
     return u.value, int(d.value)
+
+
+def lm_head(packed, scales, act, act_sum, out_scale: float = 0.0, in_scale: float | None = None) -> np.ndarray:
+    """Logits [rows, V] of the int2 LM head (decode-lm-head.ts): `in_scale` None restates
+    the WGSL shader's f32 arithmetic; a number gives the exact computation the CUDA path
+    performs (int8 activation codes when in_scale != 0, double sums when 0)."""
+    packed = np.ascontiguousarray(packed, np.uint32)
+    V, words = packed.shape
+    sc = _f32(scales)
+    a = np.ascontiguousarray(np.atleast_2d(act), np.float32)
+    rows, hidden = a.shape
+    assert hidden == 16 * words
+    s = _f32(np.atleast_1d(act_sum))
+    out = np.empty((rows, V), np.float32)
+    if in_scale is None:
+        lib().oracle_lm_head_shader_f32(packed.ctypes.data, sc.ctypes.data, V, hidden, a.ctypes.data, s.ctypes.data,
+                                        rows, float(np.float32(out_scale)), out.ctypes.data, V)
+    else:
+        lib().oracle_lm_head_exact(packed.ctypes.data, sc.ctypes.data, V, hidden, a.ctypes.data, s.ctypes.data,
+                                   rows, float(np.float32(in_scale)), float(np.float32(out_scale)), out.ctypes.data, V)
+    return out
 
 
 def constraint_masks(dfa, vocab, node, pending_len=None, pending_bytes=None, termination=(), extra=(),

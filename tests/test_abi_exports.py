@@ -29,7 +29,8 @@ def test_structs_match_header_layout(pkg, tmp_path):
     """ctypes mirrors of gs_params / gs_batch / gs_outputs have the C compiler's layout."""
     import subprocess
     structs = {"gs_params": pkg._lib.GsParams, "gs_batch": pkg._lib.GsBatch, "gs_outputs": pkg._lib.GsOutputs,
-               "gs_dfa_desc": pkg._lib.GsDfaDesc, "gs_vocab_bytes_desc": pkg._lib.GsVocabBytesDesc}
+               "gs_dfa_desc": pkg._lib.GsDfaDesc, "gs_vocab_bytes_desc": pkg._lib.GsVocabBytesDesc,
+               "gs_lm_head_desc": pkg._lib.GsLmHeadDesc}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "gsampler.h"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
