@@ -51,7 +51,7 @@ EXPORTS = (
     "gs_softcap_digest", "gs_shard_record_bytes", "gs_shard_partials", "gs_shard_merge", "gs_profile_enable",
     "gs_profile_read", "gs_sample_noalloc", "gs_constraint_create", "gs_constraint_destroy",
     "gs_constraint_last_error", "gs_constraint_build_masks", "gs_lm_head_create", "gs_lm_head_destroy",
-    "gs_lm_head_last_error", "gs_lm_head_logits", "gs_lm_head_check",
+    "gs_lm_head_last_error", "gs_lm_head_logits", "gs_lm_head_sample", "gs_lm_head_check",
 )
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -179,6 +179,7 @@ def lib() -> ctypes.CDLL:
     L.gs_lm_head_last_error.restype = ctypes.c_char_p
     L.gs_lm_head_logits.argtypes = [P, P, i64, P, i32, P, i64, P]
     L.gs_lm_head_check.argtypes = [P, ctypes.POINTER(i32)]
+    L.gs_lm_head_sample.argtypes = [P, P, i64, P, ctypes.POINTER(GsBatch), ctypes.POINTER(GsOutputs), P]
     L.gs_softcap.argtypes = [P, P, P, i64, f32, P]
     L.gs_softcap_digest.argtypes = [P, u64, u64, f32, ctypes.POINTER(u64)]
     L.gs_shard_record_bytes.argtypes = [ctypes.POINTER(GsParams), i32, i64, i64]

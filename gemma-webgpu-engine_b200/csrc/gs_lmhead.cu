@@ -49,6 +49,7 @@
 #include "../../include/gsampler.h"
 
 struct gs_lm_head {
+  gs_ctx* ctx = nullptr;  // the sampler context the handle was created on (gs_lm_head_sample)
   int device = 0;
   int64_t vocab = 0;
   int32_t hidden = 0;
@@ -62,6 +63,9 @@ struct gs_lm_head {
   unsigned char* img = nullptr;
   size_t img_bytes = 0;
   int32_t* flag = nullptr;  // device error flag (bit 0: a wait timed out)
+  // gs_lm_head_sample's logits (grown on demand): rows × vocab float32
+  float* scratch = nullptr;
+  size_t scratch_bytes = 0;
   int num_sms = 0;
   std::string err;
 };
@@ -616,6 +620,9 @@ void release(gs_lm_head* h) {
   cudaFree(h->scales);
   cudaFree(h->img);
   cudaFree(h->flag);
+  cudaFree(h->scratch);
+  h->scratch = nullptr;
+  h->scratch_bytes = 0;
   h->packed = nullptr;
   h->scales = nullptr;
   h->img = nullptr;
@@ -647,6 +654,7 @@ gs_status gs_lm_head_create(gs_ctx* ctx, const gs_lm_head_desc* d, gs_lm_head** 
     return GS_EINVAL;
   }
   auto* h = new gs_lm_head();
+  h->ctx = ctx;
   h->device = ctx_device(ctx);
   h->vocab = d->vocab;
   h->hidden = d->hidden;
@@ -791,6 +799,43 @@ gs_status gs_lm_head_logits(gs_lm_head* h, const float* activation, int64_t ld_a
   restore();
   if (e != cudaSuccess) return lfail(h, GS_ECUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
   return GS_OK;
+}
+
+gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_activation, const float* activation_sum,
+                            const gs_batch* batch, const gs_outputs* out, void* stream) {
+  if (!h || !batch) return GS_EINVAL;
+  if (batch->logits) return lfail(h, GS_EINVAL, "gs_lm_head_sample computes the logits: batch->logits must be NULL");
+  if (batch->vocab != 0 && batch->vocab != h->vocab) return lfail(h, GS_EINVAL, "batch->vocab must be 0 or the head's vocab");
+  const int32_t rows = batch->rows;
+  if (rows < 0 || rows > 65535) return lfail(h, GS_EINVAL, "rows must be in [0, 65535]");
+  const size_t need = static_cast<size_t>(rows) * static_cast<size_t>(h->vocab) * sizeof(float);
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != h->device) cudaSetDevice(h->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (need > h->scratch_bytes) {  // (grown on demand; the first call of a larger batch allocates)
+    cudaStreamSynchronize(st);
+    cudaFree(h->scratch);
+    h->scratch = nullptr;
+    h->scratch_bytes = 0;
+    cudaError_t e = cudaMalloc(&h->scratch, need > 0 ? need : 4);
+    if (e != cudaSuccess) {
+      if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+      return lfail(h, GS_ENOMEM, std::string("logits scratch: ") + cudaGetErrorString(e));
+    }
+    h->scratch_bytes = need;
+  }
+  if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+  gs_status s = gs_lm_head_logits(h, activation, ld_activation, activation_sum, rows, h->scratch, h->vocab, stream);
+  if (s != GS_OK) return s;
+  gs_batch b = *batch;
+  b.logits = h->scratch;
+  b.dtype = GS_DTYPE_F32;
+  b.vocab = h->vocab;
+  b.row_stride = h->vocab;
+  s = gs_sample(h->ctx, &b, out, stream);
+  if (s != GS_OK) h->err = std::string("sampling: ") + gs_last_error(h->ctx);
+  return s;
 }
 
 gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out) {

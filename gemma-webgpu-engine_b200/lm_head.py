@@ -31,6 +31,7 @@ class GpuLmHead:
         self.vocab, self.hidden = packed.shape[0], packed.shape[1] * 16
         self.input_scale, self.output_scale = float(np.float32(input_scale)), float(np.float32(output_scale))
         self.device = sampler.device
+        self._sampler = sampler  # (keeps the context alive: the head samples on it)
         d = _lib.GsLmHeadDesc(self.vocab, self.hidden, packed.ctypes.data, scales.ctypes.data, self.input_scale,
                               self.output_scale)
         self._h = ctypes.c_void_p()
@@ -69,6 +70,38 @@ class GpuLmHead:
         st = self._L.gs_lm_head_logits(self._h, ctypes.c_void_p(activation.data_ptr()), activation.stride(0),
                                        ctypes.c_void_p(s.data_ptr()), rows, ctypes.c_void_p(out.data_ptr()),
                                        out.stride(0), ctypes.c_void_p(stream))
+        if st != _lib.GS_OK:
+            msg = (self._L.gs_lm_head_last_error(self._h) or b"").decode()
+            raise ValueError(msg) if st == _lib.GS_EINVAL else SamplerError(st, msg)
+        return out
+
+    def sample(self, activation, activation_sum, params, *, softcap: float = 0.0, history=None, history_len=None,
+               mask_table=None, mask_state=None, rng_state=None, uniforms=None, logprob: bool = False,
+               candidates: int = 0, stream=None):
+        """Activations -> sampled tokens in one call (gs_lm_head_sample): the logits of
+        ``logits`` sampled as GpuSampler.sample would, without returning them."""
+        import torch
+        rows = activation.shape[0]
+        if activation.dtype != torch.float32 or activation.dim() != 2 or activation.shape[1] != self.hidden:
+            raise ValueError(f"activation must be float32 [rows, {self.hidden}]")
+        if activation.stride(1) != 1:
+            raise ValueError("activation rows must be contiguous")
+        s = activation_sum.to(torch.float32).contiguous()
+        if s.numel() != rows:
+            raise ValueError("activation_sum must hold one value per row")
+        # the batch without logits (shape only): the head computes them
+        shape_only = torch.empty((rows, self.vocab), dtype=torch.float32, device="meta")
+        b, keep = self._sampler.make_batch(shape_only, params, softcap=softcap, history=history,
+                                           history_len=history_len, mask_table=mask_table, mask_state=mask_state,
+                                           rng_state=rng_state, uniforms=uniforms)
+        b.logits = None
+        out, o = self._sampler.make_outputs(rows, activation.device, logprob, candidates)
+        if stream is None:
+            stream = torch.cuda.current_stream(activation.device).cuda_stream
+        st = self._L.gs_lm_head_sample(self._h, ctypes.c_void_p(activation.data_ptr()), activation.stride(0),
+                                       ctypes.c_void_p(s.data_ptr()), ctypes.byref(b), ctypes.byref(o),
+                                       ctypes.c_void_p(stream))
+        del keep
         if st != _lib.GS_OK:
             msg = (self._L.gs_lm_head_last_error(self._h) or b"").decode()
             raise ValueError(msg) if st == _lib.GS_EINVAL else SamplerError(st, msg)

@@ -222,17 +222,10 @@ class GpuSampler:
             b.uniforms = uniforms.data_ptr()
         return b, parr
 
-    def sample(self, logits, params, *, softcap: float = 0.0, history=None, history_len=None, mask_table=None,
-               mask_state=None, rng_state=None, uniforms=None, logprob: bool = False, candidates: int = 0,
-               stream=None, out: SampleResult | None = None) -> SampleResult:
-        """Batched sampling of device-resident logits [rows, vocab] (gs_sample).  Asynchronous on
-        ``stream`` (torch's current stream when None); outputs are device tensors."""
+    @staticmethod
+    def make_outputs(rows: int, dev, logprob: bool = False, candidates: int = 0, out: SampleResult | None = None):
+        """(SampleResult of device tensors, the gs_outputs pointing at them)."""
         import torch
-        b, keep = self.make_batch(logits, params, softcap=softcap, history=history, history_len=history_len,
-                                  mask_table=mask_table, mask_state=mask_state, rng_state=rng_state,
-                                  uniforms=uniforms)
-        rows = logits.shape[0]
-        dev = logits.device
         if out is None:
             out = SampleResult(
                 ids=torch.empty(rows, dtype=torch.int32, device=dev),
@@ -250,6 +243,19 @@ class GpuSampler:
         o.cand_probs = _ptr(out.cand_probs)
         o.cand_count = _ptr(out.cand_count)
         o.cand_cap = out.cand_ids.shape[1] if out.cand_ids is not None else 0
+        return out, o
+
+    def sample(self, logits, params, *, softcap: float = 0.0, history=None, history_len=None, mask_table=None,
+               mask_state=None, rng_state=None, uniforms=None, logprob: bool = False, candidates: int = 0,
+               stream=None, out: SampleResult | None = None) -> SampleResult:
+        """Batched sampling of device-resident logits [rows, vocab] (gs_sample).  Asynchronous on
+        ``stream`` (torch's current stream when None); outputs are device tensors."""
+        import torch
+        b, keep = self.make_batch(logits, params, softcap=softcap, history=history, history_len=history_len,
+                                  mask_table=mask_table, mask_state=mask_state, rng_state=rng_state,
+                                  uniforms=uniforms)
+        dev = logits.device
+        out, o = self.make_outputs(logits.shape[0], dev, logprob, candidates, out)
         if stream is None:
             stream = torch.cuda.current_stream(dev).cuda_stream
         st = self._L.gs_sample(self._ctx, ctypes.byref(b), ctypes.byref(o), ctypes.c_void_p(stream))

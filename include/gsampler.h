@@ -243,6 +243,16 @@ gs_status gs_lm_head_logits(gs_lm_head* h, const float* activation, int64_t ld_a
 /* Reads and clears the device-side error flag (synchronising): GS_ETIMEOUT when a bounded
  * wait inside the kernel ran out (its logits are then unspecified). */
 gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out);
+/* Activations -> tokens in one call on `stream` (the reference's decode step from the
+ * LM head pass to sampleToken, decode-model.ts:135-139 then sampling.ts:18): the logits
+ * go to a handle-owned scratch (rows × vocab float32, grown on demand; at decode batch
+ * sizes it stays in L2 for the sampling pass that follows) and `batch` is sampled as by
+ * gs_sample on the context the head was created on.  batch->logits must be NULL,
+ * batch->vocab 0 or the head's vocab; dtype and row_stride are set here.  Results are
+ * identical to gs_lm_head_logits followed by gs_sample. */
+gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_activation,
+                            const float* activation_sum, const gs_batch* batch, const gs_outputs* out,
+                            void* stream);
 
 /* Elementwise soft cap, the same routine the sampling pass applies (no reference
  * counterpart: the reference never applies its declared cap). */

@@ -92,3 +92,68 @@ def test_rejects_bad_shapes(sampler):
     packed = np.zeros((64, 112), np.uint32)  # hidden 1792 > 1536
     with pytest.raises(ValueError):
         LM.GpuLmHead(sampler, packed, np.ones(64, np.float32), 0.02)
+
+
+# ---------------------------------------------------------------- activations -> tokens
+from parity_util import compare, oracle_rows  # noqa: E402
+
+C1_PARAMS = dict(temperature=0.8, topK=40, topP=0.95, minP=0.0, typicalP=1.0, repetitionPenalty=1.1,
+                 presencePenalty=0.5, frequencyPenalty=0.3)
+
+
+def _inputs(vocab, rows, seed, in_scale=0.02, hist=16):
+    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, rows, seed=seed, input_scale=in_scale)
+    g = np.random.default_rng(seed + 1)
+    history = g.integers(0, vocab, size=(rows, hist), dtype=np.int64).astype(np.int32)
+    history_len = np.full(rows, hist, np.int32)
+    rng = np.array([float(1000 + r) for r in range(rows)])
+    return packed, scales, act, act_sum, history, history_len, rng
+
+
+@pytest.mark.parametrize("vocab,rows,topk", [(262144, 1, 40), (262144, 3, 40), (8192, 20, 50), (8192, 70, 0)])
+def test_sample_matches_two_step(sampler, vocab, rows, topk):
+    # gs_lm_head_sample == gs_lm_head_logits then gs_sample, bit for bit
+    packed, scales, act, act_sum, history, history_len, rng = _inputs(vocab, rows, vocab + rows)
+    params = [dict(C1_PARAMS, topK=topk)]
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    try:
+        a, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
+        hi, hl = torch.from_numpy(history).cuda(), torch.from_numpy(history_len).cuda()
+        r1 = torch.from_numpy(rng).cuda()
+        r2 = r1.clone()
+        one = h.sample(a, s, params, softcap=30.0, history=hi, history_len=hl, rng_state=r1, logprob=True,
+                       candidates=64)
+        two = sampler.sample(h.logits(a, s), params, softcap=30.0, history=hi, history_len=hl, rng_state=r2,
+                             logprob=True, candidates=64)
+        h.check()
+        torch.cuda.synchronize()
+        for f in ("ids", "flags", "logprob", "cand_ids", "cand_probs", "cand_count"):
+            assert torch.equal(getattr(one, f), getattr(two, f)), f
+        assert torch.equal(r1, r2)
+    finally:
+        h.close()
+
+
+@pytest.mark.parametrize("rows", [1, 6])
+def test_sample_matches_oracle(sampler, rows):
+    # the oracle's exact LM head, then the oracle's sampleToken, against one GPU call
+    vocab = 262144
+    packed, scales, act, act_sum, history, history_len, rng = _inputs(vocab, rows, 77 + rows)
+    params = [C1_PARAMS]
+    logits = O.lm_head(packed, scales, act, act_sum, in_scale=0.02)
+    ids, margins, cands, st = oracle_rows(O, logits, vocab, 30.0, [dict(C1_PARAMS, repetitionWindow=history.shape[1])],
+                                          history=history, history_len=history_len, rng_state=rng)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    try:
+        r = torch.from_numpy(rng).cuda()
+        res = h.sample(torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda(), params, softcap=30.0,
+                       history=torch.from_numpy(history).cuda(), history_len=torch.from_numpy(history_len).cuda(),
+                       rng_state=r, logprob=True, candidates=2048)
+        torch.cuda.synchronize()
+    finally:
+        h.close()
+    from parity_util import GpuOut
+    gpu = GpuOut(ids=res.ids.cpu().numpy(), flags=res.flags.cpu().numpy().view(np.uint32), rng_after=r.cpu().numpy(),
+                 cand_ids=res.cand_ids.cpu().numpy(), cand_probs=res.cand_probs.cpu().numpy(),
+                 cand_count=res.cand_count.cpu().numpy(), logprob=res.logprob.cpu().numpy())
+    compare(gpu, ids, margins, cands, rng_after=st, label="lm_head_sample")
