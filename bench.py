@@ -356,7 +356,72 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     if world == 1:
         res["cpu_baseline"] = cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per)
         res["mask_builder"] = mask_builder_leg(pkg, W, sampler)
+        res["lm_head"] = lm_head_leg(pkg, sampler, stream)
     return res
+
+
+def lm_head_leg(pkg, sampler, stream):
+    """The int2 LM head (decode-lm-head.ts) at the reference's shape: V = 262144 rows of
+    1536 2-bit codes (100.7 MB packed), per batch size the device time of one
+    gs_lm_head_logits call, and activations -> token with gs_lm_head_sample at B = 1."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    LM = importlib.import_module(PKG + ".lm_head")
+    V, H = VOCAB, 1536
+    packed, scales, act, act_sum = LM.synthetic(V, H, 64, seed=91)
+    head = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    peak, peak_kind = measured_peak()
+    out = {"shape": {"vocab": V, "hidden": H, "packed_mb": V * H / 4 / 1e6},
+           "timing": "CUDA events around 20 back-to-back calls on one stream (device time per call, weights "
+                     "100.7 MB > L2 so every call streams them from HBM)", "batches": {}}
+    a_all, s_all = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
+    for B in (1, 4, 16, 64):
+        a, sm = a_all[:B].contiguous(), s_all[:B].contiguous()
+        lg = torch.empty((B, V), dtype=torch.float32, device=a.device)
+        for _ in range(3):
+            head.logits(a, sm, out=lg, stream=stream.cuda_stream)
+        reps = 20
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            head.logits(a, sm, out=lg, stream=stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        head.check()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        alg = V * H // 4 + V * 4 + B * H * 4 + B * V * 4  # packed codes, row scales, activations, logits
+        out["batches"][str(B)] = {
+            "us_per_call": us, "rows_per_s": B / us * 1e6, "int_tops": 2.0 * B * H * V / us / 1e6,
+            "kernel": "dp4a GEMV" if B <= 4 else "tcgen05 kind::i8 MMA (weights expanded into TMEM)",
+            "roofline": {"bound": "hbm", "achieved": alg / us / 1e3, "peak": peak, "unit": "GB/s",
+                         "frac": alg / us / 1e3 / peak, "algorithmic_bytes": alg,
+                         "peak_source": f"{peak_kind} hbm_gbs"}}
+    # activations -> token (C1's sampling parameters), B = 1
+    p1 = [dict(temperature=0.8, topK=40, topP=0.95, minP=0.0, typicalP=1.0, repetitionPenalty=1.0,
+               presencePenalty=0.0, frequencyPenalty=0.0)]
+    st = torch.tensor([pkg.SeededRandom(42).state], dtype=torch.float64, device=a_all.device)
+    a1, s1 = a_all[:1].contiguous(), s_all[:1].contiguous()
+    for _ in range(3):
+        head.sample(a1, s1, p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(65)]
+    evs[0].record(stream)
+    for i in range(64):
+        head.sample(a1, s1, p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream)
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
+    lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(64))
+    out["sample_b1"] = {"p50_us": lat[32], "p95_us": lat[int(64 * 0.95)],
+                        "timing": "CUDA events between consecutive gs_lm_head_sample calls (LM head + sampling)"}
+    head.close()
+    # the oracle's exact LM head on the host (one core), one row
+    c0 = time.perf_counter()
+    O.lm_head(packed[:16384], scales[:16384], act[:1], act_sum[:1], in_scale=0.02)
+    cdt = (time.perf_counter() - c0) * (V / 16384)
+    out["cpu_oracle"] = {"us_per_row": cdt * 1e6, "cores": 1,
+                         "sample": "oracle_lm_head_exact over 16384 of the 262144 rows, one activation row, scaled"}
+    out["data"] = "synthetic: seeded packed codes, row scales and int8-grid activations (lm_head.synthetic)"
+    return out
 
 
 def mask_builder_leg(pkg, W, sampler):

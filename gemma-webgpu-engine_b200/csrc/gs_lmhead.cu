@@ -78,7 +78,7 @@ constexpr int kLmKC = 128;                      // codes per chunk (one 128-byte
 constexpr int kLmMaxChunks = 12;                // hidden <= 1536
 constexpr int kGroups = 2;                      // expander groups (4 warps, one row each): chunk g -> g % 2
 constexpr int kAStages = 4;                     // weight operand stages in TMEM (32 columns each)
-constexpr int kAColBase = 128;                  // TMEM columns: accumulators [0, 2N), operand stages from 128
+// TMEM columns: two accumulators [0, 2N), then the operand stages
 constexpr int kMmaRound = 1;                    // chunks the MMA issuer takes per round
 #ifndef GS_LM_GEMV_ROWS
 #define GS_LM_GEMV_ROWS 4
@@ -109,14 +109,16 @@ struct LmPlan {
                                    : (kSmemLimit - kOffP - 1024 - 1024) / kPBytes) / kIssue * kIssue;
   static constexpr int kOffBar = kOffP + kPStages * kPBytes;
   static constexpr int kSmem = kOffBar + 1024 + 1024;          // barriers + alignment slack
-  static constexpr int kTmemCols = 256;                        // two accumulators + operand stages
+  static constexpr int kAColBase = 2 * N < 128 ? 128 : 2 * N;   // first operand-stage column
+  static constexpr int kTmemCols = kAColBase + kAStages * 32 <= 256 ? 256 : 512;
   // Instruction descriptor of tcgen05.mma kind::i8: D s32 (bits 4-5 = 2), A and B signed
   // 8-bit (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
   static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
                                      (static_cast<uint32_t>(kLmRows >> 4) << 24);
   static_assert(kOffP % 1024 == 0 && 2 * N <= kAColBase, "aligned stages; accumulators below the operands");
+  static_assert(kAColBase + kAStages * 32 <= kTmemCols && kTmemCols <= 512, "TMEM columns");
   static_assert(kSmem <= kSmemLimit, "shared memory");
-  static_assert(kPStages >= 2 * kIssue && kPStages % kIssue == 0, "whole producer rounds per ring");
+  static_assert(kPStages >= kIssue && kPStages % kIssue == 0, "whole producer rounds per ring");
   static_assert((1 + 2 * kPStages + 2 * kAStages + 5) * 8 + 8 <= 1024, "barriers fit their 1 KB");
 };
 
@@ -324,11 +326,15 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_mma_kernel(const __grid_cons
     // Lanes 0..kIssue-1 each copy one of kIssue consecutive chunks per round (the copies
     // of one instruction go out together).
     if (lane == 0) {
-      // the pass's N image rows of every chunk (the HBM image holds kImgRows per chunk)
+      // the pass's N image rows of every chunk (the HBM image holds kImgRows rows per
+      // chunk block: N = 128 takes two consecutive image passes)
       mbar_expect_tx(qfull, static_cast<uint32_t>(C * P::kQChunk));
+      constexpr int kBlocks = N > kImgRows ? N / kImgRows : 1;
+      constexpr int kBlockBytes = (N > kImgRows ? kImgRows : N) * kLmKC;
       for (int c = 0; c < C; ++c)
-        bulk_g2s(sm + P::kOffQ + c * P::kQChunk,
-                 A.img + (static_cast<size_t>(pass) * C + c) * (kImgRows * kLmKC), P::kQChunk, qfull);
+        for (int k = 0; k < kBlocks; ++k)
+          bulk_g2s(sm + P::kOffQ + c * P::kQChunk + k * kBlockBytes,
+                   A.img + (static_cast<size_t>(pass * kBlocks + k) * C + c) * (kImgRows * kLmKC), kBlockBytes, qfull);
     }
     __syncwarp();
     const int64_t total = my_tiles * C;
@@ -382,7 +388,7 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_mma_kernel(const __grid_cons
 #pragma unroll
         for (int q = 0; q < 4; ++q) o[4 * w + q] = (((x[w] >> (2 * q)) & 0x03030303u) + 0x7E7E7E7Eu) ^ 0x80808080u;
       }
-      tmem_st32(lane_base + static_cast<uint32_t>(kAColBase + 32 * a), o);
+      tmem_st32(lane_base + static_cast<uint32_t>(P::kAColBase + 32 * a), o);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(afull + a);
@@ -423,7 +429,7 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_mma_kernel(const __grid_cons
           for (int u = 0; u < nc; ++u) {
             const int a = static_cast<int>((g + u) % kAStages);
             // K = 32 steps: 8 TMEM columns of A, 32 bytes (2 descriptor units) of B
-            const uint32_t at = tmem + static_cast<uint32_t>(kAColBase + 32 * a);
+            const uint32_t at = tmem + static_cast<uint32_t>(P::kAColBase + 32 * a);
             const uint64_t bd = qd0 + static_cast<uint64_t>(((c + u) * P::kQChunk) >> 4);
 #pragma unroll
             for (int k = 0; k < kLmKC / 32; ++k)
@@ -689,6 +695,8 @@ gs_status gs_lm_head_create(gs_ctx* ctx, const gs_lm_head_desc* d, gs_lm_head** 
     e = cudaFuncSetAttribute(lm_mma_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, LmPlan<16>::kSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(lm_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, LmPlan<64>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(lm_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, LmPlan<128>::kSmem);
   if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
   if (e != cudaSuccess) {
     ctx_set_error(ctx, (std::string("LM head upload: ") + cudaGetErrorString(e)).c_str());
@@ -749,7 +757,9 @@ gs_status gs_lm_head_logits(gs_lm_head* h, const float* activation, int64_t ld_a
     lm_f64_kernel<<<grid, 128, 0, st>>>(a, activation, ld_activation, h->hidden);
     e = cudaGetLastError();
   } else {
-    const int passes = (rows + kImgRows - 1) / kImgRows;
+    // N of the tensor-core kernel: the accumulator width, rows per pass
+    const int n_mma = rows <= 16 ? 16 : rows <= 64 ? 64 : 128;
+    const int passes = (rows + n_mma - 1) / n_mma * (n_mma > kImgRows ? n_mma / kImgRows : 1);  // image passes
     const size_t img = static_cast<size_t>(passes) * h->chunks * (kImgRows * kLmKC);
     const size_t need = img + static_cast<size_t>(passes) * kImgRows * 4;
     if (need > h->img_bytes) {  // (grown on demand; the first call of a larger batch allocates)
@@ -787,12 +797,15 @@ gs_status gs_lm_head_logits(gs_lm_head* h, const float* activation, int64_t ld_a
       else if (rows <= 8) gemv(lm_gemv_kernel<8>);
       else gemv(lm_gemv_kernel<16>);
       static_assert(kGemvRows <= 16, "GEMV instantiations cover up to 16 rows");
-    } else if (rows <= 16) {
+    } else if (n_mma == 16) {
       a.pass_rows = 16;
       lm_mma_kernel<16><<<dim3(gx, 1), kLmThreads, LmPlan<16>::kSmem, st>>>(a);
-    } else {
+    } else if (n_mma == 64) {
       a.pass_rows = 64;
       lm_mma_kernel<64><<<dim3(gx, passes), kLmThreads, LmPlan<64>::kSmem, st>>>(a);
+    } else {
+      a.pass_rows = 128;
+      lm_mma_kernel<128><<<dim3(gx, passes / 2), kLmThreads, LmPlan<128>::kSmem, st>>>(a);
     }
     e = cudaGetLastError();
   }

@@ -56,6 +56,7 @@ CASES = [
     (2048, 128, 65, 0.015, 0.0),
     (1536, 512, 130, 0.02, 0.1),
     (40000, 1536, 17, 0.02, 0.0),
+    (3000, 1536, 300, 0.02, 0.0),
     (777, 1536, 2, 0.0, 0.0),
     (300, 256, 5, 0.0, 0.05),
 ]
