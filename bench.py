@@ -5,8 +5,10 @@ against HBM peak at V=262144, plus the p50 step latency at B=1).
 Workload (one "step" = one gs_sample over the batch): configuration C4, the throughput
 batch, B=4096 rows x V=262144 float32 logits (4 GiB, larger than L2), soft cap 30,
 256-id penalty history at 1.1/0.5/0.3, a 4096-state constraint bitmask at 2% density,
-temperature 0.8, topK 50, topP 0.95.  Rows are sharded evenly across the N GPUs (strong
-scaling, no collective on the data path).  Launched as one process per GPU (torchrun).
+temperature 0.8, topK 50, topP 0.95.  Rows are independent (one PRNG stream each), so each
+of the N GPUs samples its own C4 batch of 4096 rows (weak scaling: the work per GPU is
+fixed, the global batch is 4096·N; no collective on the data path).  Launched as one
+process per GPU (torchrun).
 
 Also reported on rank 0: the bfloat16 variant of C4, the p50/p95 step latency of C1
 (B=1, 256 sequential steps), the end-to-end rate through the host-buffer entry point
@@ -49,7 +51,7 @@ def parse_args():
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-extras", action="store_true", help="skip bf16 / latency / e2e / cpu legs")
     ap.add_argument("--rows", type=int, default=GLOBAL_BATCH,
-                    help="global batch (default 4096 = C4); smaller values are for profiler captures")
+                    help="rows per GPU (default 4096 = C4's batch); smaller values are for profiler captures")
     return ap.parse_args()
 
 
@@ -154,15 +156,14 @@ def run_ours(args, rank, world, local):
     L = pkg._lib
 
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
-    per = args.rows // world
-    r0 = rank * per
-    wl = W.make("C4", device=dev, rows=args.rows)
-    logits = wl.logits[r0:r0 + per].to(dtype).contiguous()
-    hist = wl.history[r0:r0 + per].contiguous()
-    hlen = wl.history_len[r0:r0 + per].contiguous()
-    mstate = wl.mask_state[r0:r0 + per].contiguous()
+    per = args.rows  # this GPU's own batch (rank 0's rows are C4's rows)
+    wl = W.make("C4", device=dev, rows=per, shard=rank)
+    logits = wl.logits.to(dtype).contiguous()
+    hist = wl.history.contiguous()
+    hlen = wl.history_len.contiguous()
+    mstate = wl.mask_state.contiguous()
     table = wl.mask_table
-    seeds = wl.seeds[r0:r0 + per]
+    seeds = wl.seeds
     del wl
     torch.cuda.empty_cache()
     rng = torch.tensor([pkg.SeededRandom(s).state for s in seeds], dtype=torch.float64, device=dev)
@@ -230,10 +231,10 @@ def run_ours(args, rank, world, local):
     tpr = traffic_per_row(args.dtype)
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32" if args.dtype == "f32" else "bf16", "data": "synthetic (seeded torch Philox, C4 distributions)",
         "config": {"workload": WORKLOAD_DESC, "global_batch": per * world, "rows_per_gpu": per, "vocab": VOCAB,
-                   "logits_dtype": args.dtype, "parallelism": f"row-sharded x{world} (no collective)",
+                   "logits_dtype": args.dtype, "parallelism": f"rows across {world} GPU(s), {per} per GPU (no collective)",
                    "l2": "inputs larger than L2 (rows x 1 MiB per GPU)"},
         "logits_gbps": total_rows * bytes_per_row * args.steps / (elapsed_ms / 1e3) / 1e9,
         "roofline": {"bound": "hbm", "kernel": "gs::stream2_kernel", "achieved": achieved, "peak": peak,
@@ -522,9 +523,10 @@ def run_reference(args, rank, world):
               f"src/runtime/sampling.ts; the TypeScript reference needs Node, which is not installed)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": WORKLOAD_DESC, "global_batch": GLOBAL_BATCH, "vocab": VOCAB,
+        "config": {"workload": WORKLOAD_DESC, "global_batch": GLOBAL_BATCH * world, "rows_per_gpu": GLOBAL_BATCH,
+                   "vocab": VOCAB,
                    "parallelism": "host threads, rank 0 only"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -110,9 +110,11 @@ def dfa_mask_table(states, vocab, device, seed, lo=0.01, hi=0.05, chunk=256):
 
 
 def make(name: str, device="cuda", rows: int | None = None, vocab: int = VOCAB, step: int = 0,
-         dtype=None) -> Workload:
+         dtype=None, shard: int = 0) -> Workload:
     """Builds configuration `name` (C1..C5).  `rows` overrides the batch (tests use fewer
-    rows of the same distribution); `step` selects the fresh logits of a C1 step."""
+    rows of the same distribution); `step` selects the fresh logits of a C1 step; `shard`
+    (C4) gives another GPU's batch of the same distribution: its own logits, histories,
+    states and row seeds, the constraint table shared (shard 0 is the batch itself)."""
     import torch
     if name == "C1":
         r = rows or 1
@@ -143,14 +145,16 @@ def make(name: str, device="cuda", rows: int | None = None, vocab: int = VOCAB, 
                       seeds=[2000 + i for i in range(r)], vocab=vocab)
     elif name == "C4":
         r = rows or 4096
-        logits = normal_logits(r, vocab, device, seed=31)
+        o = 1000 * shard
+        logits = normal_logits(r, vocab, device, seed=31 + o)
         table = dfa_mask_table(4096, vocab, device, seed=32, lo=0.02, hi=0.02)
-        state = torch.randint(0, 4096, (r,), generator=_gen(device, 33), device=device, dtype=torch.int64).to(torch.int32)
-        hist, hlen = uniform_history(r, 256, vocab, device, seed=34)
+        state = torch.randint(0, 4096, (r,), generator=_gen(device, 33 + o), device=device,
+                              dtype=torch.int64).to(torch.int32)
+        hist, hlen = uniform_history(r, 256, vocab, device, seed=34 + o)
         p = base_params(temperature=0.8, topK=50, topP=0.95, repetitionPenalty=1.1, presencePenalty=0.5,
                         frequencyPenalty=0.3, repetitionWindow=256)
         wl = Workload("C4", logits, [p], history=hist, history_len=hlen, mask_table=table, mask_state=state,
-                      seeds=[3000 + i for i in range(r)], vocab=vocab)
+                      seeds=[3000 + shard * r + i for i in range(r)], vocab=vocab)
     elif name == "C5":
         r = rows or 8
         g = _gen(device, 41)
