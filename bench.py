@@ -217,6 +217,11 @@ def run_ours(args, rank, world, local):
     clk = clocks.summary(t_wall0, t_wall1)
     stream_avg_s = s_ms.value / max(1, s_n.value) / 1e3
     merge_avg_s = m_ms.value / max(1, m_n.value) / 1e3
+    # rows of the last timed step whose draw or cut fell within 1e-6 of a boundary
+    lf = out.flags.cpu().numpy().view(np.uint32)
+    nb = torch.tensor([int(((lf & L.FLAG_BOUNDARY) != 0).sum())], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.all_reduce(nb)
     if world > 1:
         t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -243,6 +248,9 @@ def run_ours(args, rank, world, local):
                      "algorithmic_bytes_per_launch": per * bytes_per_row,
                      "avg_launch_us": stream_avg_s * 1e6, "merge_avg_launch_us": merge_avg_s * 1e6},
         "gpu_launches": 2 * args.steps * world,
+        "boundary_rows": {"count": int(nb.item()), "of": per * world,
+                          "what": "rows of the last timed step flagged GS_FLAG_BOUNDARY_* (a top-p cut, min-p, "
+                                  "typical-p or draw decision within 1e-6 of its boundary)"},
         "clocks": clk,
     }
     if not args.no_extras:

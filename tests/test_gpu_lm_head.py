@@ -111,11 +111,20 @@ def _inputs(vocab, rows, seed, in_scale=0.02, hist=16):
     return packed, scales, act, act_sum, history, history_len, rng
 
 
-@pytest.mark.parametrize("vocab,rows,topk", [(262144, 1, 40), (262144, 3, 40), (8192, 20, 50), (8192, 70, 0)])
-def test_sample_matches_two_step(sampler, vocab, rows, topk):
-    # gs_lm_head_sample == gs_lm_head_logits then gs_sample, bit for bit
+@pytest.mark.parametrize("vocab,rows,topk,masked", [(262144, 1, 40, False), (262144, 3, 40, True), (8192, 20, 50, False),
+                                                    (8192, 70, 0, False), (8192, 9, 50, True)])
+def test_sample_matches_two_step(sampler, vocab, rows, topk, masked):
+    # gs_lm_head_sample == gs_lm_head_logits then gs_sample, bit for bit (with a constraint
+    # bitmask of 64 states admitting ~5 % of the ids when `masked`)
     packed, scales, act, act_sum, history, history_len, rng = _inputs(vocab, rows, vocab + rows)
     params = [dict(C1_PARAMS, topK=topk)]
+    mk = {}
+    if masked:
+        g = np.random.default_rng(vocab + 7 * rows)
+        allowed = g.random((64, vocab)) < 0.05
+        table = np.packbits(allowed, axis=1, bitorder="little").view(np.int32)
+        mk = dict(mask_table=torch.from_numpy(np.ascontiguousarray(table)).cuda(),
+                  mask_state=torch.from_numpy(g.integers(0, 64, rows).astype(np.int32)).cuda())
     h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
     try:
         a, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
@@ -123,9 +132,9 @@ def test_sample_matches_two_step(sampler, vocab, rows, topk):
         r1 = torch.from_numpy(rng).cuda()
         r2 = r1.clone()
         one = h.sample(a, s, params, softcap=30.0, history=hi, history_len=hl, rng_state=r1, logprob=True,
-                       candidates=64)
+                       candidates=64, **mk)
         two = sampler.sample(h.logits(a, s), params, softcap=30.0, history=hi, history_len=hl, rng_state=r2,
-                             logprob=True, candidates=64)
+                             logprob=True, candidates=64, **mk)
         h.check()
         torch.cuda.synchronize()
         for f in ("ids", "flags", "logprob", "cand_ids", "cand_probs", "cand_count"):
