@@ -420,8 +420,25 @@ def lm_head_leg(pkg, sampler, stream):
         evs[i + 1].record(stream)
     torch.cuda.synchronize()
     lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(64))
+    fused = head.fused_calls
+    # the same step as two calls (logits to HBM, then gs_sample), for comparison
+    lg1 = torch.empty((1, V), dtype=torch.float32, device=a_all.device)
+    st2 = st.clone()
+    for _ in range(3):
+        head.logits(a1, s1, out=lg1, stream=stream.cuda_stream)
+        sampler.sample(lg1, p1, softcap=30.0, rng_state=st2, stream=stream.cuda_stream)
+    evs[0].record(stream)
+    for i in range(64):
+        head.logits(a1, s1, out=lg1, stream=stream.cuda_stream)
+        sampler.sample(lg1, p1, softcap=30.0, rng_state=st2, stream=stream.cuda_stream)
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
+    lat2 = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(64))
     out["sample_b1"] = {"p50_us": lat[32], "p95_us": lat[int(64 * 0.95)],
-                        "timing": "CUDA events between consecutive gs_lm_head_sample calls (LM head + sampling)"}
+                        "route": "fused (logits kept on chip, shard-record merge)" if fused >= 64 else "scratch",
+                        "two_step_p50_us": lat2[32],
+                        "timing": "CUDA events between consecutive gs_lm_head_sample calls (LM head + sampling); "
+                                  "two_step: gs_lm_head_logits then gs_sample per step"}
     head.close()
     # the oracle's exact LM head on the host (one core), one row
     c0 = time.perf_counter()

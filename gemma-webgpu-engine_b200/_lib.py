@@ -52,6 +52,7 @@ EXPORTS = (
     "gs_profile_read", "gs_sample_noalloc", "gs_constraint_create", "gs_constraint_destroy",
     "gs_constraint_last_error", "gs_constraint_build_masks", "gs_lm_head_create", "gs_lm_head_destroy",
     "gs_lm_head_last_error", "gs_lm_head_logits", "gs_lm_head_sample", "gs_lm_head_check",
+    "gs_lm_head_fused_calls",
 )
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -179,6 +180,7 @@ def lib() -> ctypes.CDLL:
     L.gs_lm_head_last_error.restype = ctypes.c_char_p
     L.gs_lm_head_logits.argtypes = [P, P, i64, P, i32, P, i64, P]
     L.gs_lm_head_check.argtypes = [P, ctypes.POINTER(i32)]
+    L.gs_lm_head_fused_calls.argtypes = [P]
     L.gs_lm_head_sample.argtypes = [P, P, i64, P, ctypes.POINTER(GsBatch), ctypes.POINTER(GsOutputs), P]
     L.gs_softcap.argtypes = [P, P, P, i64, f32, P]
     L.gs_softcap_digest.argtypes = [P, u64, u64, f32, ctypes.POINTER(u64)]
@@ -191,7 +193,9 @@ def lib() -> ctypes.CDLL:
     L.gs_profile_read.argtypes = [P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
                                   ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64)]
     for name in EXPORTS:
-        if name not in ("gs_last_error", "gs_shard_record_bytes", "gs_constraint_last_error", "gs_lm_head_last_error"):
+        if name not in ("gs_last_error", "gs_shard_record_bytes", "gs_constraint_last_error", "gs_lm_head_last_error",
+                        "gs_lm_head_fused_calls"):
             getattr(L, name).restype = ctypes.c_int
+    L.gs_lm_head_fused_calls.restype = i64
     _lib = L
     return L

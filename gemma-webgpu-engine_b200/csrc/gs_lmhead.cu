@@ -44,8 +44,10 @@
 #include <string>
 #include <vector>
 
+#include "gs_block.cuh"
 #include "gs_device.cuh"
 #include "gs_internal.cuh"
+#include "gs_plan.cuh"
 #include "../../include/gsampler.h"
 
 struct gs_lm_head {
@@ -66,6 +68,10 @@ struct gs_lm_head {
   // gs_lm_head_sample's logits (grown on demand): rows × vocab float32
   float* scratch = nullptr;
   size_t scratch_bytes = 0;
+  // fused gs_lm_head_sample: per (shard, row) records the vocabulary-sharded merge reads
+  unsigned char* records = nullptr;
+  size_t records_bytes = 0;
+  int64_t fused_calls = 0;
   int num_sms = 0;
   std::string err;
 };
@@ -505,12 +511,13 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_mma_kernel(const __grid_cons
 // word 4w + P of a row holds the codes of elements 16w + 4k + P in byte k (the order
 // the code extraction below produces), rows past `rows` zero; they are read four words
 // at a time.
+// Activation codes of rows [0, rows) into qw[b·kLmMaxChunks·32 + j] (zero for rows >= rows):
+// word j = 4w + P packs the int8 codes of elements 16w + 4k + P, k = 0..3 (the order that
+// lines up with the 2-bit codes of a packed weight word w).
 template <int NB>
-__global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ LmArgs A, const float* __restrict__ act,
-                                                      int64_t ld_act) {
-  __shared__ __align__(16) uint32_t qw[NB][kLmMaxChunks * 32];  // [row][4·(16-code word) + P]
+__device__ __forceinline__ void lm_quant_act(uint32_t* qw, const LmArgs& A, const float* __restrict__ act, int64_t ld_act,
+                                             int rows) {
   const int C = A.chunks;
-  const int rows = A.rows < NB ? A.rows : NB;
   for (int i = threadIdx.x; i < NB * C * 32; i += blockDim.x) {
     const int b = i / (C * 32), j = i % (C * 32);  // j = 4w + P
     uint32_t word = 0;
@@ -525,19 +532,23 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
         word |= (static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xffu) << (8 * k);
       }
     }
-    qw[b][j] = word;
+    qw[b * kLmMaxChunks * 32 + j] = word;
   }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+}
+
+// Integer dot products of one warp: rows 32·quad + (lane >> 1) (h = 0) and 16 more (h = 1)
+// of tile t, half the row's words per lane; the lane pair's sum follows the shuffle.
+template <int NB>
+__device__ __forceinline__ void lm_tile_dots(const LmArgs& A, const uint32_t* qw, int64_t t, int quad, int lane,
+                                             int32_t (&acc)[2][NB]) {
+  const int C = A.chunks;
   const int half = lane & 1;
-  for (int64_t t = blockIdx.x; t < A.tiles; t += gridDim.x) {
-  int32_t acc[2][NB];
 #pragma unroll
   for (int h = 0; h < 2; ++h)
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[h][b] = 0;
-  // this warp's 32 rows of chunk c: 1 KB at ((t·C + c)·128 + 32·warp)·32 bytes
-  const uint4* wbase = reinterpret_cast<const uint4*>(A.packed) + (static_cast<size_t>(t) * C * kLmRows + 32 * warp) * 2;
+  // this warp's 32 rows of chunk c: 1 KB at ((t·C + c)·128 + 32·quad)·32 bytes
+  const uint4* wbase = reinterpret_cast<const uint4*>(A.packed) + (static_cast<size_t>(t) * C * kLmRows + 32 * quad) * 2;
   for (int c0 = 0; c0 < C; c0 += 4) {  // four chunks' loads in flight
     uint4 x[4][2];
 #pragma unroll
@@ -560,7 +571,7 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
           const int qi = (c0 + u) * 32 + 4 * (4 * half + w);
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
-            const uint4 q = *reinterpret_cast<const uint4*>(&qw[b][qi]);  // words P = 0..3
+            const uint4 q = *reinterpret_cast<const uint4*>(&qw[b * kLmMaxChunks * 32 + qi]);  // words P = 0..3
             int32_t d = acc[h][b];
             asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(d) : "r"(c0w), "r"(q.x));
             asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(d) : "r"(c1w), "r"(q.y));
@@ -576,6 +587,20 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
   for (int h = 0; h < 2; ++h)
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[h][b] += __shfl_xor_sync(kFullMask, acc[h][b], 1);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ LmArgs A, const float* __restrict__ act,
+                                                      int64_t ld_act) {
+  __shared__ __align__(16) uint32_t qw[NB * kLmMaxChunks * 32];  // [row][4·(16-code word) + P]
+  const int rows = A.rows < NB ? A.rows : NB;
+  lm_quant_act<NB>(qw, A, act, ld_act, rows);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane & 1;
+  for (int64_t t = blockIdx.x; t < A.tiles; t += gridDim.x) {
+  int32_t acc[2][NB];
+  lm_tile_dots<NB>(A, qw, t, warp, lane, acc);
   // lane pair (2k, 2k+1) holds rows k and 16 + k: the even lane writes the first, the odd the second
   const int64_t v = t * kLmRows + 32 * warp + (lane >> 1) + 16 * half;
   if (v < A.vocab) {
@@ -588,6 +613,170 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
       }
     }
   }
+  }
+}
+
+// ---------------------------------------------------------------- fused sampling
+// gs_lm_head_sample for a few rows without a penalty history: the logits never leave the
+// SM.  Block g computes the logits of vocabulary ids [g·R, (g+1)·R) (R = tiles per shard ·
+// 128) for every row with the GEMV's dot products into shared memory, soft-caps them, and
+// writes, per row, the record a vocabulary shard writes in gs_shard_partials: the live
+// (allowed) maximum m and sum Σ 2^((x - m)·log2(e)/T), the maximum and sum of e^(x - max)
+// over every id (log-probability), the allowed count, error flags, and the shard's k best
+// candidate packs (exact: key32(x) and ~id, the radix select of the merge).  The merge of
+// vocabulary-sharded calls then treats the blocks as shards; no logits are stored.
+constexpr int kRecThreads = 512;
+constexpr int kRecMaxK = 64;     // topK the fused path serves (the merge's pack buffer)
+constexpr int kRecMaxRows = 4;   // rows of one fused call (the kernel's NB)
+
+struct RecArgs {
+  LmArgs L;
+  const float* act;
+  int64_t ld_act;
+  RowPlan plan[4];
+  float cap, inv_cap;
+  const uint32_t* mask_table;
+  int64_t mask_states, mask_words;
+  const int32_t* mask_state;
+  unsigned char* records;  // [shard][row] of rec_bytes
+  int64_t rec_bytes;
+  int32_t tps;             // tiles per shard
+  int32_t want_raw;        // log-probabilities requested (a NaN raw sum is then an error)
+};
+
+// shared memory of the records kernel: activation words | logits [NB][R] | packs [R]
+__host__ __device__ inline size_t rec_smem_bytes(int nb, int tps) {
+  return static_cast<size_t>(nb) * kLmMaxChunks * 32 * 4 + static_cast<size_t>(nb) * tps * kLmRows * 4 +
+         static_cast<size_t>(tps) * kLmRows * 8;
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kRecThreads) lm_records_kernel(const __grid_constant__ RecArgs R) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  __shared__ float red_f[32];
+  __shared__ double red_d[32];
+  __shared__ int red_i[32];
+  __shared__ unsigned sel_hist[256];
+  __shared__ int sel_digit, sel_above, sel_binc, n_out;
+  const LmArgs& A = R.L;
+  const int rows = A.rows < NB ? A.rows : NB;
+  const int tps = R.tps;
+  const int rlen = tps * kLmRows;
+  uint32_t* qw = reinterpret_cast<uint32_t*>(dsm);                      // [NB][kLmMaxChunks * 32]
+  float* lg = reinterpret_cast<float*>(dsm + static_cast<size_t>(NB) * kLmMaxChunks * 32 * 4);  // [NB][rlen]
+  unsigned long long* buf = reinterpret_cast<unsigned long long*>(lg + static_cast<size_t>(NB) * rlen);  // [rlen]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = lane & 1;
+  const int64_t t_first = static_cast<int64_t>(blockIdx.x) * tps;
+  const int ntile = static_cast<int>(A.tiles - t_first < tps ? A.tiles - t_first : tps);
+  const int64_t v_lo = t_first * kLmRows;
+  const int nids = static_cast<int>(A.vocab - v_lo < static_cast<int64_t>(ntile) * kLmRows ? A.vocab - v_lo
+                                                                                          : static_cast<int64_t>(ntile) * kLmRows);
+  lm_quant_act<NB>(qw, A, R.act, R.ld_act, rows);
+  __syncthreads();
+  // ---- logits: warp w takes quadrant w & 3 of tiles w >> 2, w >> 2 + 4, ... ----
+  for (int tt = warp >> 2; tt < ntile; tt += kRecThreads / 128) {
+    const int quad = warp & 3;
+    int32_t acc[2][NB];
+    lm_tile_dots<NB>(A, qw, t_first + tt, quad, lane, acc);
+    const int li = tt * kLmRows + 32 * quad + (lane >> 1) + 16 * half;  // local id
+    const int64_t v = v_lo + li;
+    if (v < A.vocab) {
+      const float scale = A.scales[v];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (b < rows) {
+          const float tt2 = __fmaf_rn(A.in_scale, static_cast<float>(half ? acc[1][b] : acc[0][b]),
+                                      -(2.0f * A.act_sum[b]));
+          float xl = srq(__fmul_rn(scale, tt2), A.out_scale);
+          if (R.cap != 0.0f) xl = softcap(xl, R.cap, R.inv_cap);
+          lg[static_cast<size_t>(b) * rlen + li] = xl;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // ---- per row: the shard's record ----
+  for (int b = 0; b < rows; ++b) {
+    const RowPlan& pl = R.plan[b];
+    const bool do_sum = pl.mode != kModeGreedy;  // greedy rows keep no normaliser (as the stream pass)
+    const int32_t state = R.mask_state ? R.mask_state[b] : -1;
+    const bool masked = R.mask_table != nullptr && state >= 0;
+    const bool has_mask = masked && state < R.mask_states;
+    const uint32_t* mrow = has_mask ? R.mask_table + static_cast<int64_t>(state) * R.mask_words : nullptr;
+    const float* x = lg + static_cast<size_t>(b) * rlen;
+    auto allowed = [&](int i) -> bool {
+      if (!mrow) return true;
+      const int64_t v = v_lo + i;
+      return (__ldg(mrow + (v >> 5)) >> (v & 31)) & 1u;
+    };
+    float lmax = -INFINITY, rmax = -INFINITY;
+    int na = 0, bad = 0;
+    for (int i = tid; i < nids; i += blockDim.x) {
+      const float xi = x[i];
+      if (allowed(i)) {
+        lmax = fmaxf(lmax, xi);
+        ++na;
+        bad |= xi != xi;
+      }
+      rmax = fmaxf(rmax, xi);
+    }
+    const float lm = block_max_f(lmax, red_f);
+    const float m = do_sum ? lm : -INFINITY;
+    const float rm = block_max_f(rmax, red_f);
+    na = block_sum_i(na, red_i);
+    bad = __syncthreads_or(bad);
+    float sp = 0.0f, rp = 0.0f;
+    for (int i = tid; i < rlen; i += blockDim.x) {
+      unsigned long long pk = 0ull;
+      if (i < nids) {
+        const float xi = x[i];
+        if (allowed(i)) {
+          if (m > -INFINITY) {
+            const float d = xi - m;
+            sp += ex2_approx(fmaf(d, pl.a2_lo, d * pl.a2_hi));
+          }
+          if (xi == xi) pk = make_pack(xi, static_cast<uint32_t>(v_lo + i));
+        }
+        if (rm > -INFINITY) {
+          const float g = xi - rm;
+          rp += ex2_approx(fmaf(g, kL2eLo, g * kL2eHi));
+        }
+      }
+      buf[i] = pk;
+    }
+    const double ssum = block_sum_d(static_cast<double>(sp), red_d);
+    const double rsum = block_sum_d(static_cast<double>(rp), red_d);
+    unsigned char* rec = R.records + (static_cast<int64_t>(blockIdx.x) * A.rows + b) * R.rec_bytes;
+    unsigned long long* packs = reinterpret_cast<unsigned long long*>(rec + sizeof(UnitStat));
+    const int k = pl.k_eff > 0 ? pl.k_eff : 1;
+    if (tid == 0) n_out = 0;
+    __syncthreads();
+    if (na > k) {
+      unsigned long long prefix, mask;
+      select_threshold(buf, nids, k, sel_hist, &sel_digit, &sel_above, &sel_binc, prefix, mask);
+      for (int i = tid; i < nids; i += blockDim.x) {
+        const unsigned long long v = buf[i];
+        if (v != 0ull && (v & mask) >= prefix) packs[atomicAdd(&n_out, 1)] = v;
+      }
+    } else {
+      for (int i = tid; i < nids; i += blockDim.x)
+        if (buf[i] != 0ull) packs[atomicAdd(&n_out, 1)] = buf[i];
+    }
+    __syncthreads();
+    if (tid == 0) {
+      UnitStat u{};
+      u.m = m;
+      u.raw_m = rm;
+      u.s = m > -INFINITY ? ssum : 0.0;
+      u.raw_s = rm > -INFINITY ? rsum : 0.0;
+      u.n_allowed = na;
+      u.n_cand = n_out;
+      const bool nonfinite = bad || ssum != ssum || (R.want_raw && rsum != rsum) || m == INFINITY;
+      u.flags = (nonfinite ? GS_FLAG_ERR_NONFINITE : 0u) | (masked && !has_mask ? GS_FLAG_ERR_INVALID : 0u);
+      u.pad = 1;  // raw sums recorded
+      *reinterpret_cast<UnitStat*>(rec) = u;
+    }
+    __syncthreads();
   }
 }
 
@@ -629,6 +818,9 @@ void release(gs_lm_head* h) {
   cudaFree(h->scratch);
   h->scratch = nullptr;
   h->scratch_bytes = 0;
+  cudaFree(h->records);
+  h->records = nullptr;
+  h->records_bytes = 0;
   h->packed = nullptr;
   h->scales = nullptr;
   h->img = nullptr;
@@ -821,11 +1013,102 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
   if (batch->vocab != 0 && batch->vocab != h->vocab) return lfail(h, GS_EINVAL, "batch->vocab must be 0 or the head's vocab");
   const int32_t rows = batch->rows;
   if (rows < 0 || rows > 65535) return lfail(h, GS_EINVAL, "rows must be in [0, 65535]");
-  const size_t need = static_cast<size_t>(rows) * static_cast<size_t>(h->vocab) * sizeof(float);
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != h->device) cudaSetDevice(h->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Fused: up to kRecMaxRows rows of int8-grid activations, no penalty history, every row
+  // 1 <= topK <= kRecMaxK or greedy: the LM head writes shard records, the merge samples.
+  bool fused = rows >= 1 && rows <= kRecMaxRows && h->in_scale != 0.0f && !batch->history && batch->params &&
+               (batch->params_count == 1 || batch->params_count == rows);
+  int kcap = 1;
+  RecArgs ra{};
+  if (fused) {
+    for (int i = 0; i < rows && fused; ++i) {
+      const RowPlan pl = make_plan(batch->params[batch->params_count == 1 ? 0 : i], h->vocab);
+      if (pl.mode == kModeLarge || pl.k_eff > kRecMaxK) fused = false;
+      ra.plan[i] = pl;
+      kcap = pl.k_eff > kcap ? pl.k_eff : kcap;
+    }
+  }
+  const int tps = static_cast<int>((h->tiles + h->num_sms - 1) / h->num_sms);
+  const int nb = rows <= 1 ? 1 : rows <= 2 ? 2 : 4;
+  if (fused && rec_smem_bytes(nb, tps) > 200 * 1024) fused = false;
+  if (fused) {
+    // the argument checks of gs_lm_head_logits, then the merge's batch checks, before any launch
+    if (!activation || !activation_sum || ld_activation < h->hidden) {
+      if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+      return lfail(h, GS_EINVAL, !activation || !activation_sum ? "activation, activation_sum and logits are required"
+                                                                 : "ld_activation >= hidden and ld_logits >= vocab are required");
+    }
+    gs_batch b = *batch;
+    b.logits = nullptr;
+    b.dtype = GS_DTYPE_F32;
+    b.vocab = h->vocab;
+    b.row_stride = h->vocab;
+    std::string err;
+    const gs_status cs = check_batch(&b, out, &err, kCheckNoLogits);
+    if (cs != GS_OK) {
+      if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+      return lfail(h, cs, "sampling: " + err);
+    }
+    const int shards = static_cast<int>((h->tiles + tps - 1) / tps);
+    const int64_t rec_bytes = shard_record_bytes(kcap, 0);
+    const size_t rneed = static_cast<size_t>(shards) * rows * rec_bytes;
+    if (rneed > h->records_bytes) {  // (grown on demand; the first call of a larger batch allocates)
+      cudaStreamSynchronize(st);
+      cudaFree(h->records);
+      h->records = nullptr;
+      h->records_bytes = 0;
+      cudaError_t e = cudaMalloc(&h->records, rneed);
+      if (e != cudaSuccess) {
+        if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+        return lfail(h, GS_ENOMEM, std::string("shard records: ") + cudaGetErrorString(e));
+      }
+      h->records_bytes = rneed;
+    }
+    ra.L.packed = h->packed;
+    ra.L.scales = h->scales;
+    ra.L.act_sum = activation_sum;
+    ra.L.vocab = h->vocab;
+    ra.L.tiles = h->tiles;
+    ra.L.chunks = h->chunks;
+    ra.L.rows = rows;
+    ra.L.in_scale = h->in_scale;
+    ra.L.out_scale = h->out_scale;
+    ra.L.flag = h->flag;
+    ra.act = activation;
+    ra.ld_act = ld_activation;
+    ra.cap = batch->softcap;
+    ra.inv_cap = batch->softcap != 0.0f ? static_cast<float>(1.0 / static_cast<double>(batch->softcap)) : 0.0f;
+    ra.mask_table = batch->mask_table;
+    ra.mask_states = batch->mask_states;
+    ra.mask_words = batch->mask_words;
+    ra.mask_state = batch->mask_table ? batch->mask_state : nullptr;
+    ra.records = h->records;
+    ra.rec_bytes = rec_bytes;
+    ra.tps = tps;
+    ra.want_raw = out->logprob != nullptr;
+    const size_t smem = rec_smem_bytes(nb, tps);
+    cudaError_t e = cudaSuccess;
+    auto go = [&](auto kern) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e == cudaSuccess) {
+        kern<<<shards, kRecThreads, smem, st>>>(ra);
+        e = cudaGetLastError();
+      }
+    };
+    if (nb == 1) go(lm_records_kernel<1>);
+    else if (nb == 2) go(lm_records_kernel<2>);
+    else go(lm_records_kernel<4>);
+    if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return lfail(h, GS_ECUDA, std::string("LM head records launch: ") + cudaGetErrorString(e));
+    gs_status s = gs_shard_merge(h->ctx, &b, shards, h->records, out, stream);
+    if (s != GS_OK) h->err = std::string("sampling: ") + gs_last_error(h->ctx);
+    else ++h->fused_calls;
+    return s;
+  }
+  const size_t need = static_cast<size_t>(rows) * static_cast<size_t>(h->vocab) * sizeof(float);
   if (need > h->scratch_bytes) {  // (grown on demand; the first call of a larger batch allocates)
     cudaStreamSynchronize(st);
     cudaFree(h->scratch);
@@ -850,6 +1133,8 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
   if (s != GS_OK) h->err = std::string("sampling: ") + gs_last_error(h->ctx);
   return s;
 }
+
+int64_t gs_lm_head_fused_calls(const gs_lm_head* h) { return h ? h->fused_calls : -1; }
 
 gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out) {
   if (!h || !timed_out) return GS_EINVAL;

@@ -107,6 +107,11 @@ class GpuLmHead:
             raise ValueError(msg) if st == _lib.GS_EINVAL else SamplerError(st, msg)
         return out
 
+    @property
+    def fused_calls(self) -> int:
+        """sample() calls that took the fused route (logits kept on chip, shard-record merge)."""
+        return int(self._L.gs_lm_head_fused_calls(self._h))
+
     def check(self):
         """Raises SamplerError(GS_ETIMEOUT) when a bounded wait inside the kernel ran out
         since the last check (synchronises)."""

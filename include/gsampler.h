@@ -244,15 +244,24 @@ gs_status gs_lm_head_logits(gs_lm_head* h, const float* activation, int64_t ld_a
  * wait inside the kernel ran out (its logits are then unspecified). */
 gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out);
 /* Activations -> tokens in one call on `stream` (the reference's decode step from the
- * LM head pass to sampleToken, decode-model.ts:135-139 then sampling.ts:18): the logits
- * go to a handle-owned scratch (rows × vocab float32, grown on demand; at decode batch
- * sizes it stays in L2 for the sampling pass that follows) and `batch` is sampled as by
+ * LM head pass to sampleToken, decode-model.ts:135-139 then sampling.ts:18), sampled as by
  * gs_sample on the context the head was created on.  batch->logits must be NULL,
- * batch->vocab 0 or the head's vocab; dtype and row_stride are set here.  Results are
- * identical to gs_lm_head_logits followed by gs_sample. */
+ * batch->vocab 0 or the head's vocab; dtype and row_stride are set here.
+ * Fused route (1..4 rows, input_scale != 0, no penalty history, every row greedy or
+ * 1 <= topK <= 64): the logits stay on chip; each block of vocabulary ids writes the
+ * record of a vocabulary shard (its statistics and top-k candidates, as
+ * gs_shard_partials) to a handle-owned buffer and gs_shard_merge samples them.  Candidate
+ * ids and order are those of gs_lm_head_logits + gs_sample; probabilities agree to
+ * float64 summation order (normaliser partials per block instead of per streamed unit).
+ * Other batches: the logits go to a handle-owned scratch (rows × vocab float32) and
+ * gs_sample runs on it, identical to gs_lm_head_logits followed by gs_sample.  Either
+ * buffer grows on the first call that needs more (allocates). */
 gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_activation,
                             const float* activation_sum, const gs_batch* batch, const gs_outputs* out,
                             void* stream);
+/* Number of gs_lm_head_sample calls on `h` that took the fused route (diagnostics; no
+ * reference counterpart).  -1 for a NULL handle. */
+int64_t gs_lm_head_fused_calls(const gs_lm_head* h);
 
 /* Elementwise soft cap, the same routine the sampling pass applies (no reference
  * counterpart: the reference never applies its declared cap). */

@@ -167,3 +167,121 @@ def test_sample_matches_oracle(sampler, rows):
                  cand_ids=res.cand_ids.cpu().numpy(), cand_probs=res.cand_probs.cpu().numpy(),
                  cand_count=res.cand_count.cpu().numpy(), logprob=res.logprob.cpu().numpy())
     compare(gpu, ids, margins, cands, rng_after=st, label="lm_head_sample")
+
+
+# ---------------------------------------------------------------- fused route (no history)
+NOHIST = dict(C1_PARAMS, repetitionPenalty=1.0, presencePenalty=0.0, frequencyPenalty=0.0)
+
+
+def _mask(vocab, rows, seed, density=0.05, states=64):
+    g = np.random.default_rng(seed)
+    allowed = g.random((states, vocab)) < density
+    table = np.packbits(allowed, axis=1, bitorder="little").view(np.uint32)
+    return np.ascontiguousarray(table), g.integers(0, states, rows).astype(np.int32)
+
+
+def _gpu_out(res, r):
+    from parity_util import GpuOut
+    return GpuOut(ids=res.ids.cpu().numpy(), flags=res.flags.cpu().numpy().view(np.uint32), rng_after=r.cpu().numpy(),
+                  cand_ids=res.cand_ids.cpu().numpy(), cand_probs=res.cand_probs.cpu().numpy(),
+                  cand_count=res.cand_count.cpu().numpy(), logprob=res.logprob.cpu().numpy())
+
+
+@pytest.mark.parametrize("vocab,rows,topk,masked", [(262144, 1, 40, False), (262144, 4, 64, True), (262144, 2, 1, False),
+                                                    (5000, 3, 40, False), (8192, 4, 20, True)])
+def test_fused_matches_oracle(sampler, vocab, rows, topk, masked):
+    # activations -> tokens through the fused route (the logits never stored) against the
+    # oracle's exact LM head and sampleToken on the same inputs
+    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, rows, seed=vocab + 3 * rows + topk, input_scale=0.02)
+    rng = np.array([float(5000 + r) for r in range(rows)])
+    params = [dict(NOHIST, topK=topk)]
+    table, state = _mask(vocab, rows, vocab + rows) if masked else (None, None)
+    logits = O.lm_head(packed, scales, act, act_sum, in_scale=0.02)
+    ids, margins, cands, st = oracle_rows(O, logits, vocab, 30.0, [dict(params[0], repetitionWindow=0)],
+                                          mask_table=table, mask_state=state, rng_state=rng)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    try:
+        r = torch.from_numpy(rng).cuda()
+        mk = {} if table is None else dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(),
+                                           mask_state=torch.from_numpy(state).cuda())
+        res = h.sample(torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda(), params, softcap=30.0,
+                       rng_state=r, logprob=True, candidates=2048, **mk)
+        h.check()
+        torch.cuda.synchronize()
+        assert h.fused_calls == 1
+    finally:
+        h.close()
+    compare(_gpu_out(res, r), ids, margins, cands, rng_after=st, label="lm_head_fused")
+
+
+@pytest.mark.parametrize("rows,temperature,topk,masked", [(1, 0.8, 40, False), (3, 0.8, 64, True), (4, 0.0, 40, False),
+                                                          (2, 0.0, 10, True), (1, 1.3, 5, True)])
+def test_fused_matches_two_step(sampler, rows, temperature, topk, masked):
+    # fused route == gs_lm_head_logits + gs_sample: ids, candidate ids and counts and flags
+    # exactly; probabilities and log-probabilities to float64 summation order
+    vocab = 262144
+    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, rows, seed=91 + rows, input_scale=0.02)
+    params = [dict(NOHIST, temperature=temperature, topK=topk)]
+    mk = {}
+    if masked:
+        table, state = _mask(vocab, rows, 17 + rows, density=0.3)
+        mk = dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(), mask_state=torch.from_numpy(state).cuda())
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    try:
+        a, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
+        r1 = torch.tensor([float(70 + i) for i in range(rows)], dtype=torch.float64, device="cuda")
+        r2 = r1.clone()
+        one = h.sample(a, s, params, softcap=30.0, rng_state=r1, logprob=True, candidates=64, **mk)
+        two = sampler.sample(h.logits(a, s), params, softcap=30.0, rng_state=r2, logprob=True, candidates=64, **mk)
+        h.check()
+        torch.cuda.synchronize()
+        assert h.fused_calls == 1
+        for f in ("ids", "flags", "cand_ids", "cand_count"):
+            assert torch.equal(getattr(one, f), getattr(two, f)), f
+        assert torch.equal(r1, r2)
+        np.testing.assert_allclose(one.cand_probs.cpu().numpy(), two.cand_probs.cpu().numpy(), rtol=1e-6, atol=0)
+        np.testing.assert_allclose(one.logprob.cpu().numpy(), two.logprob.cpu().numpy(), rtol=1e-9, atol=1e-12)
+    finally:
+        h.close()
+
+
+def test_fused_error_rows_and_routes(sampler):
+    # rows the fused route cannot sample flag as the two-step route flags them (a mask
+    # state past the table, every logit NaN); batches outside its scope take the scratch route
+    vocab = 8192
+    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, 4, seed=5, input_scale=0.02)
+    act_sum = act_sum.copy()
+    act_sum[2] = np.nan
+    table, state = _mask(vocab, 4, 9, states=8)
+    state[1] = 8  # past the table
+    state[3] = -1  # unconstrained
+    mk = dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(), mask_state=torch.from_numpy(state).cuda())
+    params = [dict(NOHIST, topK=40)]
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    try:
+        a, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
+        r1 = torch.arange(4, dtype=torch.float64, device="cuda")
+        r2 = r1.clone()
+        one = h.sample(a, s, params, softcap=30.0, rng_state=r1, logprob=True, candidates=64, **mk)
+        two = sampler.sample(h.logits(a, s), params, softcap=30.0, rng_state=r2, logprob=True, candidates=64, **mk)
+        torch.cuda.synchronize()
+        assert h.fused_calls == 1
+        for f in ("ids", "flags", "cand_count"):
+            assert torch.equal(getattr(one, f), getattr(two, f)), f
+        L = pkg._lib
+        fl = one.flags.cpu().numpy().view(np.uint32)
+        assert fl[1] & L.FLAG_ERRORS and fl[2] & L.FLAG_ERRORS and not (fl[0] & L.FLAG_ERRORS)
+        # five rows, a penalty history, topK past 64: the scratch route
+        packed5, scales5, act5, sum5 = LM.synthetic(vocab, 1536, 5, seed=6, input_scale=0.02)
+        h.sample(torch.from_numpy(act5).cuda(), torch.from_numpy(sum5).cuda(), params, softcap=30.0,
+                 rng_state=torch.zeros(5, dtype=torch.float64, device="cuda"))
+        hist = torch.zeros((4, 4), dtype=torch.int32, device="cuda")
+        h.sample(a, torch.from_numpy(np.nan_to_num(act_sum)).cuda(), [C1_PARAMS], softcap=30.0, history=hist,
+                 history_len=torch.full((4,), 4, dtype=torch.int32, device="cuda"),
+                 rng_state=torch.zeros(4, dtype=torch.float64, device="cuda"))
+        h.sample(a, torch.from_numpy(np.nan_to_num(act_sum)).cuda(), [dict(NOHIST, topK=100)], softcap=30.0,
+                 rng_state=torch.zeros(4, dtype=torch.float64, device="cuda"))
+        torch.cuda.synchronize()
+        assert h.fused_calls == 1
+    finally:
+        h.close()
