@@ -625,7 +625,6 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
 // over every id (log-probability), the allowed count, error flags, and the shard's k best
 // candidate packs (exact: key32(x) and ~id, the radix select of the merge).  The merge of
 // vocabulary-sharded calls then treats the blocks as shards; no logits are stored.
-constexpr int kRecThreads = 512;
 constexpr int kRecMaxK = 64;     // topK the fused path serves (the merge's pack buffer)
 constexpr int kRecMaxRows = 4;   // rows of one fused call (the kernel's NB)
 
@@ -644,18 +643,20 @@ struct RecArgs {
   int32_t want_raw;        // log-probabilities requested (a NaN raw sum is then an error)
 };
 
-// shared memory of the records kernel: activation words | logits [NB][R] | packs [R]
+// shared memory of the records kernel: activation words | logits [NB][R] | packs [NB][R]
 __host__ __device__ inline size_t rec_smem_bytes(int nb, int tps) {
-  return static_cast<size_t>(nb) * kLmMaxChunks * 32 * 4 + static_cast<size_t>(nb) * tps * kLmRows * 4 +
-         static_cast<size_t>(tps) * kLmRows * 8;
+  return static_cast<size_t>(nb) * kLmMaxChunks * 32 * 4 + static_cast<size_t>(nb) * tps * kLmRows * 12;
 }
 
-template <int NB>
-__global__ void __launch_bounds__(kRecThreads) lm_records_kernel(const __grid_constant__ RecArgs R) {
+template <int NB, int THREADS>
+__global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_constant__ RecArgs R) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  __shared__ float red_f[32];
-  __shared__ double red_d[32];
-  __shared__ int red_i[32];
+  __shared__ float red_f[2][NB][32];
+  __shared__ double red_d[2][NB][32];
+  __shared__ int red_i[2][NB][32];
+  __shared__ float fin_lm[NB], fin_rm[NB];
+  __shared__ double fin_s[NB], fin_rs[NB];
+  __shared__ int fin_na[NB], fin_bad[NB];
   __shared__ unsigned sel_hist[256];
   __shared__ int sel_digit, sel_above, sel_binc, n_out;
   const LmArgs& A = R.L;
@@ -664,7 +665,7 @@ __global__ void __launch_bounds__(kRecThreads) lm_records_kernel(const __grid_co
   const int rlen = tps * kLmRows;
   uint32_t* qw = reinterpret_cast<uint32_t*>(dsm);                      // [NB][kLmMaxChunks * 32]
   float* lg = reinterpret_cast<float*>(dsm + static_cast<size_t>(NB) * kLmMaxChunks * 32 * 4);  // [NB][rlen]
-  unsigned long long* buf = reinterpret_cast<unsigned long long*>(lg + static_cast<size_t>(NB) * rlen);  // [rlen]
+  unsigned long long* buf = reinterpret_cast<unsigned long long*>(lg + static_cast<size_t>(NB) * rlen);  // [NB][rlen]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = lane & 1;
   const int64_t t_first = static_cast<int64_t>(blockIdx.x) * tps;
   const int ntile = static_cast<int>(A.tiles - t_first < tps ? A.tiles - t_first : tps);
@@ -674,7 +675,7 @@ __global__ void __launch_bounds__(kRecThreads) lm_records_kernel(const __grid_co
   lm_quant_act<NB>(qw, A, R.act, R.ld_act, rows);
   __syncthreads();
   // ---- logits: warp w takes quadrant w & 3 of tiles w >> 2, w >> 2 + 4, ... ----
-  for (int tt = warp >> 2; tt < ntile; tt += kRecThreads / 128) {
+  for (int tt = warp >> 2; tt < ntile; tt += THREADS / 128) {
     const int quad = warp & 3;
     int32_t acc[2][NB];
     lm_tile_dots<NB>(A, qw, t_first + tt, quad, lane, acc);
@@ -695,88 +696,185 @@ __global__ void __launch_bounds__(kRecThreads) lm_records_kernel(const __grid_co
     }
   }
   __syncthreads();
-  // ---- per row: the shard's record ----
-  for (int b = 0; b < rows; ++b) {
-    const RowPlan& pl = R.plan[b];
-    const bool do_sum = pl.mode != kModeGreedy;  // greedy rows keep no normaliser (as the stream pass)
-    const int32_t state = R.mask_state ? R.mask_state[b] : -1;
+  // ---- the rows' statistics: two block-wide passes over every row at once ----
+  const int nw = THREADS / 32;
+  const uint32_t* mrow[NB];
+  bool invalid[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int32_t state = (b < rows && R.mask_state) ? R.mask_state[b] : -1;
     const bool masked = R.mask_table != nullptr && state >= 0;
     const bool has_mask = masked && state < R.mask_states;
-    const uint32_t* mrow = has_mask ? R.mask_table + static_cast<int64_t>(state) * R.mask_words : nullptr;
-    const float* x = lg + static_cast<size_t>(b) * rlen;
-    auto allowed = [&](int i) -> bool {
-      if (!mrow) return true;
-      const int64_t v = v_lo + i;
-      return (__ldg(mrow + (v >> 5)) >> (v & 31)) & 1u;
-    };
-    float lmax = -INFINITY, rmax = -INFINITY;
-    int na = 0, bad = 0;
-    for (int i = tid; i < nids; i += blockDim.x) {
-      const float xi = x[i];
-      if (allowed(i)) {
-        lmax = fmaxf(lmax, xi);
-        ++na;
-        bad |= xi != xi;
-      }
-      rmax = fmaxf(rmax, xi);
+    mrow[b] = has_mask ? R.mask_table + static_cast<int64_t>(state) * R.mask_words : nullptr;
+    invalid[b] = masked && !has_mask;
+  }
+  auto allowed = [&](int b, int i) -> bool {
+    if (!mrow[b]) return true;
+    const int64_t v = v_lo + i;
+    return (__ldg(mrow[b] + (v >> 5)) >> (v & 31)) & 1u;
+  };
+  {
+    float lmax[NB], rmax[NB];
+    int na[NB], bad[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      lmax[b] = -INFINITY;
+      rmax[b] = -INFINITY;
+      na[b] = 0;
+      bad[b] = 0;
     }
-    const float lm = block_max_f(lmax, red_f);
-    const float m = do_sum ? lm : -INFINITY;
-    const float rm = block_max_f(rmax, red_f);
-    na = block_sum_i(na, red_i);
-    bad = __syncthreads_or(bad);
-    float sp = 0.0f, rp = 0.0f;
-    for (int i = tid; i < rlen; i += blockDim.x) {
-      unsigned long long pk = 0ull;
-      if (i < nids) {
-        const float xi = x[i];
-        if (allowed(i)) {
-          if (m > -INFINITY) {
-            const float d = xi - m;
-            sp += ex2_approx(fmaf(d, pl.a2_lo, d * pl.a2_hi));
+    for (int i = tid; i < nids; i += THREADS) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (b >= rows) break;
+        const float xi = lg[static_cast<size_t>(b) * rlen + i];
+        if (allowed(b, i)) {
+          lmax[b] = fmaxf(lmax[b], xi);
+          ++na[b];
+          bad[b] |= xi != xi;
+        }
+        rmax[b] = fmaxf(rmax[b], xi);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        lmax[b] = fmaxf(lmax[b], __shfl_xor_sync(kFullMask, lmax[b], o));
+        rmax[b] = fmaxf(rmax[b], __shfl_xor_sync(kFullMask, rmax[b], o));
+        na[b] += __shfl_xor_sync(kFullMask, na[b], o);
+        bad[b] |= __shfl_xor_sync(kFullMask, bad[b], o);
+      }
+      if (lane == 0) {
+        red_f[0][b][warp] = lmax[b];
+        red_f[1][b][warp] = rmax[b];
+        red_i[0][b][warp] = na[b];
+        red_i[1][b][warp] = bad[b];
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        float m0 = lane < nw ? red_f[0][b][lane] : -INFINITY, r0 = lane < nw ? red_f[1][b][lane] : -INFINITY;
+        int n0 = lane < nw ? red_i[0][b][lane] : 0, d0 = lane < nw ? red_i[1][b][lane] : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          m0 = fmaxf(m0, __shfl_xor_sync(kFullMask, m0, o));
+          r0 = fmaxf(r0, __shfl_xor_sync(kFullMask, r0, o));
+          n0 += __shfl_xor_sync(kFullMask, n0, o);
+          d0 |= __shfl_xor_sync(kFullMask, d0, o);
+        }
+        if (lane == 0) {
+          fin_lm[b] = m0;
+          fin_rm[b] = r0;
+          fin_na[b] = n0;
+          fin_bad[b] = d0;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  {
+    float sp[NB], rp[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      sp[b] = 0.0f;
+      rp[b] = 0.0f;
+    }
+    for (int i = tid; i < rlen; i += THREADS) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (b >= rows) break;
+        const RowPlan& pl = R.plan[b];
+        const float m = pl.mode != kModeGreedy ? fin_lm[b] : -INFINITY;  // greedy: no normaliser (as the stream pass)
+        const float rm = fin_rm[b];
+        unsigned long long pk = 0ull;
+        if (i < nids) {
+          const float xi = lg[static_cast<size_t>(b) * rlen + i];
+          if (allowed(b, i)) {
+            if (m > -INFINITY) {
+              const float d = xi - m;
+              sp[b] += ex2_approx(fmaf(d, pl.a2_lo, d * pl.a2_hi));
+            }
+            if (xi == xi) pk = make_pack(xi, static_cast<uint32_t>(v_lo + i));
           }
-          if (xi == xi) pk = make_pack(xi, static_cast<uint32_t>(v_lo + i));
+          if (rm > -INFINITY) {
+            const float g = xi - rm;
+            rp[b] += ex2_approx(fmaf(g, kL2eLo, g * kL2eHi));
+          }
         }
-        if (rm > -INFINITY) {
-          const float g = xi - rm;
-          rp += ex2_approx(fmaf(g, kL2eLo, g * kL2eHi));
+        buf[static_cast<size_t>(b) * rlen + i] = pk;
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      double s0 = sp[b], r0 = rp[b];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(kFullMask, s0, o);
+        r0 += __shfl_xor_sync(kFullMask, r0, o);
+      }
+      if (lane == 0) {
+        red_d[0][b][warp] = s0;
+        red_d[1][b][warp] = r0;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        double s0 = lane < nw ? red_d[0][b][lane] : 0.0, r0 = lane < nw ? red_d[1][b][lane] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          s0 += __shfl_xor_sync(kFullMask, s0, o);
+          r0 += __shfl_xor_sync(kFullMask, r0, o);
+        }
+        if (lane == 0) {
+          fin_s[b] = s0;
+          fin_rs[b] = r0;
         }
       }
-      buf[i] = pk;
     }
-    const double ssum = block_sum_d(static_cast<double>(sp), red_d);
-    const double rsum = block_sum_d(static_cast<double>(rp), red_d);
+    __syncthreads();
+  }
+  // ---- per row: the shard's k best packs, then the record's statistics ----
+  for (int b = 0; b < rows; ++b) {
+    const RowPlan& pl = R.plan[b];
+    const unsigned long long* pb = buf + static_cast<size_t>(b) * rlen;
     unsigned char* rec = R.records + (static_cast<int64_t>(blockIdx.x) * A.rows + b) * R.rec_bytes;
     unsigned long long* packs = reinterpret_cast<unsigned long long*>(rec + sizeof(UnitStat));
     const int k = pl.k_eff > 0 ? pl.k_eff : 1;
     if (tid == 0) n_out = 0;
     __syncthreads();
-    if (na > k) {
+    if (fin_na[b] > k) {
       unsigned long long prefix, mask;
-      select_threshold(buf, nids, k, sel_hist, &sel_digit, &sel_above, &sel_binc, prefix, mask);
-      for (int i = tid; i < nids; i += blockDim.x) {
-        const unsigned long long v = buf[i];
+      select_threshold(pb, nids, k, sel_hist, &sel_digit, &sel_above, &sel_binc, prefix, mask);
+      for (int i = tid; i < nids; i += THREADS) {
+        const unsigned long long v = pb[i];
         if (v != 0ull && (v & mask) >= prefix) packs[atomicAdd(&n_out, 1)] = v;
       }
     } else {
-      for (int i = tid; i < nids; i += blockDim.x)
-        if (buf[i] != 0ull) packs[atomicAdd(&n_out, 1)] = buf[i];
+      for (int i = tid; i < nids; i += THREADS)
+        if (pb[i] != 0ull) packs[atomicAdd(&n_out, 1)] = pb[i];
     }
     __syncthreads();
     if (tid == 0) {
+      const float m = pl.mode != kModeGreedy ? fin_lm[b] : -INFINITY;
+      const float rm = fin_rm[b];
+      const double ssum = fin_s[b], rsum = fin_rs[b];
       UnitStat u{};
       u.m = m;
       u.raw_m = rm;
       u.s = m > -INFINITY ? ssum : 0.0;
       u.raw_s = rm > -INFINITY ? rsum : 0.0;
-      u.n_allowed = na;
+      u.n_allowed = fin_na[b];
       u.n_cand = n_out;
-      const bool nonfinite = bad || ssum != ssum || (R.want_raw && rsum != rsum) || m == INFINITY;
-      u.flags = (nonfinite ? GS_FLAG_ERR_NONFINITE : 0u) | (masked && !has_mask ? GS_FLAG_ERR_INVALID : 0u);
+      const bool nonfinite = fin_bad[b] || ssum != ssum || (R.want_raw && rsum != rsum) || m == INFINITY;
+      u.flags = (nonfinite ? GS_FLAG_ERR_NONFINITE : 0u) | (invalid[b] ? GS_FLAG_ERR_INVALID : 0u);
       u.pad = 1;  // raw sums recorded
       *reinterpret_cast<UnitStat*>(rec) = u;
     }
-    __syncthreads();
   }
 }
 
@@ -1094,13 +1192,13 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
     auto go = [&](auto kern) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e == cudaSuccess) {
-        kern<<<shards, kRecThreads, smem, st>>>(ra);
+        kern<<<shards, 1024, smem, st>>>(ra);
         e = cudaGetLastError();
       }
     };
-    if (nb == 1) go(lm_records_kernel<1>);
-    else if (nb == 2) go(lm_records_kernel<2>);
-    else go(lm_records_kernel<4>);
+    if (nb == 1) go(lm_records_kernel<1, 1024>);
+    else if (nb == 2) go(lm_records_kernel<2, 1024>);
+    else go(lm_records_kernel<4, 1024>);
     if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return lfail(h, GS_ECUDA, std::string("LM head records launch: ") + cudaGetErrorString(e));
     gs_status s = gs_shard_merge(h->ctx, &b, shards, h->records, out, stream);
