@@ -627,6 +627,7 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
 // vocabulary-sharded calls then treats the blocks as shards; no logits are stored.
 constexpr int kRecMaxK = 64;     // topK the fused path serves (the merge's pack buffer)
 constexpr int kRecMaxRows = 4;   // rows of one fused call (the kernel's NB)
+constexpr int kRecCandCap = 512; // packs at or above the per-row bound that one warp selects from
 
 struct RecArgs {
   LmArgs L;
@@ -658,7 +659,8 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
   __shared__ double fin_s[NB], fin_rs[NB];
   __shared__ int fin_na[NB], fin_bad[NB];
   __shared__ unsigned sel_hist[256];
-  __shared__ int sel_digit, sel_above, sel_binc, n_out;
+  __shared__ int sel_digit, sel_above, sel_binc, n_out, n_cl;
+  __shared__ unsigned long long top2[2 * (THREADS / 32)], cl[kRecCandCap], s_tau;
   const LmArgs& A = R.L;
   const int rows = A.rows < NB ? A.rows : NB;
   const int tps = R.tps;
@@ -845,9 +847,81 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
     unsigned char* rec = R.records + (static_cast<int64_t>(blockIdx.x) * A.rows + b) * R.rec_bytes;
     unsigned long long* packs = reinterpret_cast<unsigned long long*>(rec + sizeof(UnitStat));
     const int k = pl.k_eff > 0 ? pl.k_eff : 1;
-    if (tid == 0) n_out = 0;
+    if (tid == 0) {
+      n_out = 0;
+      n_cl = 0;
+    }
     __syncthreads();
-    if (fin_na[b] > k) {
+    bool done = false;
+    if (fin_na[b] > k && 2 * nw >= k) {
+      // A lower bound on the k-th largest pack: the k-th largest of the warps' top-2 packs
+      // (k distinct packs are at or above it).  The packs at or above it (usually a few
+      // times k) go to a short list, ranked by counting: three block barriers in all.
+      unsigned long long t1 = 0ull, t2 = 0ull;
+      for (int i = tid; i < nids; i += THREADS) {
+        const unsigned long long v = pb[i];
+        if (v > t1) {
+          t2 = t1;
+          t1 = v;
+        } else if (v > t2) {
+          t2 = v;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {  // disjoint lane sets at every step: (top, second) of the union
+        const unsigned long long u1 = __shfl_xor_sync(kFullMask, t1, o), u2 = __shfl_xor_sync(kFullMask, t2, o);
+        const unsigned long long lo = t1 < u1 ? t1 : u1, s2 = t2 > u2 ? t2 : u2;
+        t1 = t1 > u1 ? t1 : u1;
+        t2 = lo > s2 ? lo : s2;
+      }
+      if (lane == 0) {
+        top2[2 * warp] = t1;
+        top2[2 * warp + 1] = t2;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        unsigned long long tau = 0ull;
+        for (int j = lane; j < 2 * nw; j += 32) {
+          const unsigned long long v = top2[j];
+          int above = 0;
+#pragma unroll 4
+          for (int q = 0; q < 2 * nw; ++q) above += top2[q] > v;
+          if (v != 0ull && above == k - 1) tau = v;  // distinct non-zero packs: one has rank k
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const unsigned long long u = __shfl_xor_sync(kFullMask, tau, o);
+          tau = u > tau ? u : tau;
+        }
+        if (lane == 0) s_tau = tau;
+      }
+      __syncthreads();
+      const unsigned long long tau = s_tau;
+      if (tau != 0ull) {
+        for (int i = tid; i < nids; i += THREADS) {
+          const unsigned long long v = pb[i];
+          if (v >= tau) {
+            const int slot = atomicAdd(&n_cl, 1);
+            if (slot < kRecCandCap) cl[slot] = v;
+          }
+        }
+        __syncthreads();
+        const int nc = n_cl;
+        if (nc <= kRecCandCap && nc >= k) {  // rank of each listed pack by counting (distinct packs)
+          for (int j = tid; j < nc; j += THREADS) {
+            const unsigned long long v = cl[j];
+            int above = 0;
+#pragma unroll 4
+            for (int q = 0; q < nc; ++q) above += cl[q] > v;
+            if (above < k) packs[above] = v;
+          }
+          if (tid == 0) n_out = k;
+          done = true;
+        }
+      }
+    }
+    if (done) {
+    } else if (fin_na[b] > k) {
       unsigned long long prefix, mask;
       select_threshold(pb, nids, k, sel_hist, &sel_digit, &sel_above, &sel_binc, prefix, mask);
       for (int i = tid; i < nids; i += THREADS) {
