@@ -536,12 +536,11 @@ __device__ __forceinline__ void lm_quant_act(uint32_t* qw, const LmArgs& A, cons
   }
 }
 
-// Integer dot products of one warp over chunks [c_lo, c_hi): rows 32·quad + (lane >> 1)
-// (h = 0) and 16 more (h = 1) of tile t, half the row's words per lane; the lane pair's
-// sum follows the shuffle.
+// Integer dot products of one warp: rows 32·quad + (lane >> 1) (h = 0) and 16 more (h = 1)
+// of tile t, half the row's words per lane; the lane pair's sum follows the shuffle.
 template <int NB>
 __device__ __forceinline__ void lm_tile_dots(const LmArgs& A, const uint32_t* qw, int64_t t, int quad, int lane,
-                                             int32_t (&acc)[2][NB], int c_lo, int c_hi) {
+                                             int32_t (&acc)[2][NB]) {
   const int C = A.chunks;
   const int half = lane & 1;
 #pragma unroll
@@ -550,18 +549,18 @@ __device__ __forceinline__ void lm_tile_dots(const LmArgs& A, const uint32_t* qw
     for (int b = 0; b < NB; ++b) acc[h][b] = 0;
   // this warp's 32 rows of chunk c: 1 KB at ((t·C + c)·128 + 32·quad)·32 bytes
   const uint4* wbase = reinterpret_cast<const uint4*>(A.packed) + (static_cast<size_t>(t) * C * kLmRows + 32 * quad) * 2;
-  for (int c0 = c_lo; c0 < c_hi; c0 += 4) {  // four chunks' loads in flight
+  for (int c0 = 0; c0 < C; c0 += 4) {  // four chunks' loads in flight
     uint4 x[4][2];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      if (c0 + u < c_hi) {
+      if (c0 + u < C) {
         const uint4* p = wbase + static_cast<size_t>(c0 + u) * kLmRows * 2;
         x[u][0] = ld_stream_u4(p + lane);       // rows lane >> 1, half lane & 1
         x[u][1] = ld_stream_u4(p + 32 + lane);  // rows 16 + (lane >> 1)
       }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      if (c0 + u >= c_hi) break;
+      if (c0 + u >= C) break;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const uint32_t wv[4] = {x[u][h].x, x[u][h].y, x[u][h].z, x[u][h].w};
@@ -601,7 +600,7 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
   const int half = lane & 1;
   for (int64_t t = blockIdx.x; t < A.tiles; t += gridDim.x) {
   int32_t acc[2][NB];
-  lm_tile_dots<NB>(A, qw, t, warp, lane, acc, 0, A.chunks);
+  lm_tile_dots<NB>(A, qw, t, warp, lane, acc);
   // lane pair (2k, 2k+1) holds rows k and 16 + k: the even lane writes the first, the odd the second
   const int64_t v = t * kLmRows + 32 * warp + (lane >> 1) + 16 * half;
   if (v < A.vocab) {
@@ -675,41 +674,27 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
   const int64_t v_lo = t_first * kLmRows;
   const int nids = static_cast<int>(A.vocab - v_lo < static_cast<int64_t>(ntile) * kLmRows ? A.vocab - v_lo
                                                                                           : static_cast<int64_t>(ntile) * kLmRows);
-  int32_t* dots = reinterpret_cast<int32_t*>(lg);  // integer dot products, then the logits in place
-  for (int i = tid; i < NB * rlen; i += THREADS) dots[i] = 0;
   lm_quant_act<NB>(qw, A, R.act, R.ld_act, rows);
   __syncthreads();
-  // ---- dot products: units of (tile, quarter of 32 rows, group of chunks), dealt to the
-  // warps in turn; 14 tiles x 4 quarters x 4 groups of 3 chunks = 7 units per warp ----
-  {
-    const int C = A.chunks;
-    const int cg = (C + 3) / 4;       // chunks per unit
-    const int G = (C + cg - 1) / cg;  // units per quarter
-    const int nunits = ntile * 4 * G;
-    for (int u = warp; u < nunits; u += THREADS / 32) {
-      const int tt = u / (4 * G), rem = u - tt * 4 * G, quad = rem / G, g = rem - quad * G;
-      int32_t acc[2][NB];
-      lm_tile_dots<NB>(A, qw, t_first + tt, quad, lane, acc, g * cg, (g + 1) * cg < C ? (g + 1) * cg : C);
-      const int li = tt * kLmRows + 32 * quad + (lane >> 1) + 16 * half;  // local id
-      if (v_lo + li < A.vocab) {
+  // ---- logits: warp w takes quadrant w & 3 of tiles w >> 2, w >> 2 + 4, ... ----
+  for (int tt = warp >> 2; tt < ntile; tt += THREADS / 128) {
+    const int quad = warp & 3;
+    int32_t acc[2][NB];
+    lm_tile_dots<NB>(A, qw, t_first + tt, quad, lane, acc);
+    const int li = tt * kLmRows + 32 * quad + (lane >> 1) + 16 * half;  // local id
+    const int64_t v = v_lo + li;
+    if (v < A.vocab) {
+      const float scale = A.scales[v];
 #pragma unroll
-        for (int b = 0; b < NB; ++b)
-          if (b < rows) atomicAdd(&dots[static_cast<size_t>(b) * rlen + li], half ? acc[1][b] : acc[0][b]);
+      for (int b = 0; b < NB; ++b) {
+        if (b < rows) {
+          const float tt2 = __fmaf_rn(A.in_scale, static_cast<float>(half ? acc[1][b] : acc[0][b]),
+                                      -(2.0f * A.act_sum[b]));
+          float xl = srq(__fmul_rn(scale, tt2), A.out_scale);
+          if (R.cap != 0.0f) xl = softcap(xl, R.cap, R.inv_cap);
+          lg[static_cast<size_t>(b) * rlen + li] = xl;
+        }
       }
-    }
-  }
-  __syncthreads();
-  // ---- logits (the GEMV's epilogue, then the soft cap) ----
-  for (int i = tid; i < nids; i += THREADS) {
-    const float scale = A.scales[v_lo + i];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      if (b >= rows) break;
-      const size_t j = static_cast<size_t>(b) * rlen + i;
-      const float tt2 = __fmaf_rn(A.in_scale, static_cast<float>(dots[j]), -(2.0f * A.act_sum[b]));
-      float xl = srq(__fmul_rn(scale, tt2), A.out_scale);
-      if (R.cap != 0.0f) xl = softcap(xl, R.cap, R.inv_cap);
-      lg[j] = xl;
     }
   }
   __syncthreads();

@@ -187,19 +187,22 @@ def _gpu_out(res, r):
                   cand_count=res.cand_count.cpu().numpy(), logprob=res.logprob.cpu().numpy())
 
 
-@pytest.mark.parametrize("vocab,rows,topk,masked", [(262144, 1, 40, False), (262144, 4, 64, True), (262144, 2, 1, False),
-                                                    (5000, 3, 40, False), (8192, 4, 20, True)])
-def test_fused_matches_oracle(sampler, vocab, rows, topk, masked):
+@pytest.mark.parametrize("vocab,rows,topk,masked,hidden,out_scale", [
+    (262144, 1, 40, False, 1536, 0.0), (262144, 4, 64, True, 1536, 0.0), (262144, 2, 1, False, 1536, 0.0),
+    (5000, 3, 40, False, 1536, 0.0), (8192, 4, 20, True, 1536, 0.0), (40000, 2, 40, False, 256, 0.0),
+    (100000, 3, 30, False, 640, 0.05), (262144, 1, 40, False, 1536, 0.05)])
+def test_fused_matches_oracle(sampler, vocab, rows, topk, masked, hidden, out_scale):
     # activations -> tokens through the fused route (the logits never stored) against the
-    # oracle's exact LM head and sampleToken on the same inputs
-    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, rows, seed=vocab + 3 * rows + topk, input_scale=0.02)
+    # oracle's exact LM head and sampleToken on the same inputs (hidden 256 and 640: other
+    # chunk splits of the dot products; output srq on)
+    packed, scales, act, act_sum = LM.synthetic(vocab, hidden, rows, seed=vocab + 3 * rows + topk, input_scale=0.02)
     rng = np.array([float(5000 + r) for r in range(rows)])
     params = [dict(NOHIST, topK=topk)]
     table, state = _mask(vocab, rows, vocab + rows) if masked else (None, None)
-    logits = O.lm_head(packed, scales, act, act_sum, in_scale=0.02)
+    logits = O.lm_head(packed, scales, act, act_sum, out_scale=out_scale, in_scale=0.02)
     ids, margins, cands, st = oracle_rows(O, logits, vocab, 30.0, [dict(params[0], repetitionWindow=0)],
                                           mask_table=table, mask_state=state, rng_state=rng)
-    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, out_scale)
     try:
         r = torch.from_numpy(rng).cuda()
         mk = {} if table is None else dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(),
