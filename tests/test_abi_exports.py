@@ -57,6 +57,14 @@ def test_no_cpu_fallback_without_device(pkg):
         pkg.GpuSampler(0)
 
 
+def test_lm_head_entry_points_reject_null_handles(pkg):
+    # argument checks that run before any CUDA call (no device needed)
+    L = pkg._lib.lib()
+    assert L.gs_lm_head_fused_calls(None) == -1
+    assert L.gs_lm_head_sample(None, None, 0, None, None, None, None) == pkg._lib.GS_EINVAL
+    assert L.gs_lm_head_logits(None, None, 0, None, 0, None, 0, None) == pkg._lib.GS_EINVAL
+
+
 def test_prepare_params_matches_per_config_conversion():
     """prepare_params (the vectorised conversion a decode loop can do once) gives the same
     gs_params bytes as converting each DecodingConfig on its own."""
