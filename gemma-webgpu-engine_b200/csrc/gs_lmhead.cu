@@ -623,17 +623,18 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
 // writes, per row, the record a vocabulary shard writes in gs_shard_partials: the live
 // (allowed) maximum m and sum Σ 2^((x - m)·log2(e)/T), the maximum and sum of e^(x - max)
 // over every id (log-probability), the allowed count, error flags, and the shard's k best
-// candidate packs (exact: key32(x) and ~id, the radix select of the merge).  The merge of
-// vocabulary-sharded calls then treats the blocks as shards; no logits are stored.
+// candidate packs (key32(x) and ~id, as the streaming pass packs them; chosen exactly).
+// The merge of vocabulary-sharded calls then treats the blocks as shards; no logits are
+// stored.
 constexpr int kRecMaxK = 64;     // topK the fused path serves (the merge's pack buffer)
 constexpr int kRecMaxRows = 4;   // rows of one fused call (the kernel's NB)
-constexpr int kRecCandCap = 512; // packs at or above the per-row bound that one warp selects from
+constexpr int kRecCandCap = 512; // packs at or above the per-row bound, ranked by counting
 
 struct RecArgs {
   LmArgs L;
   const float* act;
   int64_t ld_act;
-  RowPlan plan[4];
+  RowPlan plan[kRecMaxRows];
   float cap, inv_cap;
   const uint32_t* mask_table;
   int64_t mask_states, mask_words;
@@ -676,7 +677,7 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
                                                                                           : static_cast<int64_t>(ntile) * kLmRows);
   lm_quant_act<NB>(qw, A, R.act, R.ld_act, rows);
   __syncthreads();
-  // ---- logits: warp w takes quadrant w & 3 of tiles w >> 2, w >> 2 + 4, ... ----
+  // ---- logits: warp w takes quadrant w & 3 of tiles w >> 2, w >> 2 + THREADS / 128, ... ----
   for (int tt = warp >> 2; tt < ntile; tt += THREADS / 128) {
     const int quad = warp & 3;
     int32_t acc[2][NB];
