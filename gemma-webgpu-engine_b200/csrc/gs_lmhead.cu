@@ -64,7 +64,7 @@ struct gs_lm_head {
   // per-call activation image (grown on demand): [passes][chunks][64][128] | Σq [passes * 64]
   unsigned char* img = nullptr;
   size_t img_bytes = 0;
-  int32_t* flag = nullptr;  // device error flag (bit 0: a wait timed out)
+  int32_t* flag = nullptr;  // device error flag (bit 0: a wait timed out); flag[1]: records kernel's finished-block count
   // gs_lm_head_sample's logits (grown on demand): rows × vocab float32
   float* scratch = nullptr;
   size_t scratch_bytes = 0;
@@ -643,11 +643,17 @@ struct RecArgs {
   int64_t rec_bytes;
   int32_t tps;             // tiles per shard
   int32_t want_raw;        // log-probabilities requested (a NaN raw sum is then an error)
+  int32_t kcap;            // packs per record
+  unsigned* done;          // blocks finished (the last one combines; it resets the count)
+  unsigned char* combined; // [row] of rec_bytes: every shard's record of the row in one (null: no combining)
 };
 
-// shared memory of the records kernel: activation words | logits [NB][R] | packs [NB][R]
-__host__ __device__ inline size_t rec_smem_bytes(int nb, int tps) {
-  return static_cast<size_t>(nb) * kLmMaxChunks * 32 * 4 + static_cast<size_t>(nb) * tps * kLmRows * 12;
+// shared memory of the records kernel: activation words | logits [NB][R] | packs [NB][R];
+// the last block reuses it for every shard's packs of a row and the shards' maxima
+__host__ __device__ inline size_t rec_smem_bytes(int nb, int tps, int shards, int kcap) {
+  const size_t own = static_cast<size_t>(nb) * kLmMaxChunks * 32 * 4 + static_cast<size_t>(nb) * tps * kLmRows * 12;
+  const size_t comb = static_cast<size_t>(shards) * (kcap + 1) * 8;
+  return own > comb ? own : comb;
 }
 
 template <int NB, int THREADS>
@@ -660,7 +666,7 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
   __shared__ double fin_s[NB], fin_rs[NB];
   __shared__ int fin_na[NB], fin_bad[NB];
   __shared__ unsigned sel_hist[256];
-  __shared__ int sel_digit, sel_above, sel_binc, n_out, n_cl;
+  __shared__ int sel_digit, sel_above, sel_binc, n_out, n_cl, s_last, n_tot;
   __shared__ unsigned long long top2[2 * (THREADS / 32)], cl[kRecCandCap], s_tau;
   const LmArgs& A = R.L;
   const int rows = A.rows < NB ? A.rows : NB;
@@ -951,6 +957,195 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
       *reinterpret_cast<UnitStat*>(rec) = u;
     }
   }
+
+  // ---- the last block to finish combines every shard's record of a row into one (the
+  // merge then reads one record per row: its top-k select runs here, over the shards'
+  // packs above a bound, instead of over all 147 x k packs in one CTA).  One block does
+  // it row after row (~12 us a row against ~13 us saved in the merge per call), so the
+  // host asks for it at one row only. ----
+  if (!R.combined) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(R.done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int S = gridDim.x;
+  const int kc = R.kcap;
+  unsigned long long* gp = reinterpret_cast<unsigned long long*>(dsm);  // [S][kc] packs
+  unsigned long long* smax = gp + static_cast<size_t>(S) * kc;           // [S] each shard's best pack
+  auto rec_at = [&](int u, int b) -> const unsigned char* {
+    return R.records + (static_cast<int64_t>(u) * A.rows + b) * R.rec_bytes;
+  };
+  for (int b = 0; b < rows; ++b) {
+    const RowPlan& pl = R.plan[b];
+    const int k = pl.k_eff > 0 ? pl.k_eff : 1;
+    // statistics: maxima, counts and flags, then the sums rescaled to the maxima (the
+    // combination gs_shard_partials applies to its units)
+    float um = -INFINITY, rmx = -INFINITY;
+    int na = 0;
+    unsigned fl = 0;
+    for (int u = tid; u < S; u += THREADS) {
+      const UnitStat* st = reinterpret_cast<const UnitStat*>(rec_at(u, b));
+      um = fmaxf(um, __ldcg(&st->m));
+      rmx = fmaxf(rmx, __ldcg(&st->raw_m));
+      na += __ldcg(&st->n_allowed);
+      fl |= __ldcg(reinterpret_cast<const unsigned*>(&st->flags));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      um = fmaxf(um, __shfl_xor_sync(kFullMask, um, o));
+      rmx = fmaxf(rmx, __shfl_xor_sync(kFullMask, rmx, o));
+      na += __shfl_xor_sync(kFullMask, na, o);
+      fl |= __shfl_xor_sync(kFullMask, fl, o);
+    }
+    if (lane == 0) {
+      red_f[0][0][warp] = um;
+      red_f[1][0][warp] = rmx;
+      red_i[0][0][warp] = na;
+      red_i[1][0][warp] = static_cast<int>(fl);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      float m0 = lane < nw ? red_f[0][0][lane] : -INFINITY, r0 = lane < nw ? red_f[1][0][lane] : -INFINITY;
+      int n0 = lane < nw ? red_i[0][0][lane] : 0;
+      unsigned f0 = lane < nw ? static_cast<unsigned>(red_i[1][0][lane]) : 0u;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(kFullMask, m0, o));
+        r0 = fmaxf(r0, __shfl_xor_sync(kFullMask, r0, o));
+        n0 += __shfl_xor_sync(kFullMask, n0, o);
+        f0 |= __shfl_xor_sync(kFullMask, f0, o);
+      }
+      if (lane == 0) {
+        fin_lm[0] = m0;
+        fin_rm[0] = r0;
+        fin_na[0] = n0;
+        fin_bad[0] = static_cast<int>(f0);
+      }
+    }
+    __syncthreads();
+    const float M = fin_lm[0], RM = fin_rm[0];
+    double sm = 0.0, rs = 0.0;
+    for (int u = tid; u < S; u += THREADS) {
+      const UnitStat* st = reinterpret_cast<const UnitStat*>(rec_at(u, b));
+      const float mu = __ldcg(&st->m), ru = __ldcg(&st->raw_m);
+      if (mu > -INFINITY)
+        sm = __dadd_rn(sm, __dmul_rn(__ldcg(&st->s), exp2(__dmul_rn(static_cast<double>(mu) - static_cast<double>(M), pl.a2))));
+      if (ru > -INFINITY)
+        rs = __dadd_rn(rs, __dmul_rn(__ldcg(&st->raw_s), exp(static_cast<double>(ru) - static_cast<double>(RM))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sm += __shfl_xor_sync(kFullMask, sm, o);
+      rs += __shfl_xor_sync(kFullMask, rs, o);
+    }
+    if (lane == 0) {
+      red_d[0][0][warp] = sm;
+      red_d[1][0][warp] = rs;
+    }
+    // every shard's packs (0: empty slot), then each shard's best
+    for (int i = tid; i < S * kc; i += THREADS) {
+      const int u = i / kc, j = i - u * kc;
+      const unsigned char* r = rec_at(u, b);
+      const int nc = __ldcg(&reinterpret_cast<const UnitStat*>(r)->n_cand);
+      gp[i] = j < nc ? __ldcg(reinterpret_cast<const unsigned long long*>(r + sizeof(UnitStat)) + j) : 0ull;
+    }
+    if (tid == 0) {
+      n_out = 0;
+      n_cl = 0;
+      n_tot = 0;
+      s_tau = 0ull;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      double s0 = lane < nw ? red_d[0][0][lane] : 0.0, r0 = lane < nw ? red_d[1][0][lane] : 0.0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(kFullMask, s0, o);
+        r0 += __shfl_xor_sync(kFullMask, r0, o);
+      }
+      if (lane == 0) {
+        fin_s[0] = s0;
+        fin_rs[0] = r0;
+      }
+    }
+    int npk = 0;
+    for (int u = tid; u < S; u += THREADS) {
+      unsigned long long mx = 0ull;
+      for (int j = 0; j < kc; ++j) mx = gp[u * kc + j] > mx ? gp[u * kc + j] : mx;
+      smax[u] = mx;
+    }
+    for (int i = tid; i < S * kc; i += THREADS) npk += gp[i] != 0ull;
+    if (npk) atomicAdd(&n_tot, npk);
+    __syncthreads();
+    const int total = n_tot;
+    unsigned char* out = R.combined + static_cast<int64_t>(b) * R.rec_bytes;
+    unsigned long long* opk = reinterpret_cast<unsigned long long*>(out + sizeof(UnitStat));
+    bool done = false;
+    if (total <= k) {
+      for (int i = tid; i < S * kc; i += THREADS)
+        if (gp[i] != 0ull) opk[atomicAdd(&n_out, 1)] = gp[i];
+      done = true;
+    } else if (k <= S) {
+      // bound: the k-th largest of the shards' best packs (k distinct packs at or above
+      // it; none when fewer than k shards hold packs)
+      for (int u = tid; u < S; u += THREADS) {
+        const unsigned long long v = smax[u];
+        int above = 0;
+#pragma unroll 4
+        for (int q = 0; q < S; ++q) above += smax[q] > v;
+        if (v != 0ull && above == k - 1) s_tau = v;
+      }
+      __syncthreads();
+      const unsigned long long tau = s_tau;
+      if (tau != 0ull) {
+        for (int i = tid; i < S * kc; i += THREADS) {
+          const unsigned long long v = gp[i];
+          if (v >= tau) {
+            const int slot = atomicAdd(&n_cl, 1);
+            if (slot < kRecCandCap) cl[slot] = v;
+          }
+        }
+        __syncthreads();
+        const int nc = n_cl;
+        if (nc <= kRecCandCap && nc >= k) {
+          for (int j = tid; j < nc; j += THREADS) {
+            const unsigned long long v = cl[j];
+            int above = 0;
+#pragma unroll 4
+            for (int q = 0; q < nc; ++q) above += cl[q] > v;
+            if (above < k) opk[above] = v;
+          }
+          if (tid == 0) n_out = k;
+          done = true;
+        }
+      }
+    }
+    if (!done) {
+      unsigned long long prefix, mask;
+      select_threshold(gp, S * kc, k, sel_hist, &sel_digit, &sel_above, &sel_binc, prefix, mask);
+      for (int i = tid; i < S * kc; i += THREADS) {
+        const unsigned long long v = gp[i];
+        if (v != 0ull && (v & mask) >= prefix) opk[atomicAdd(&n_out, 1)] = v;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      UnitStat u{};
+      u.m = M;
+      u.raw_m = RM;
+      u.s = M > -INFINITY ? fin_s[0] : 0.0;
+      u.raw_s = RM > -INFINITY ? fin_rs[0] : 0.0;
+      u.n_allowed = fin_na[0];
+      u.n_cand = n_out;
+      u.flags = static_cast<unsigned>(fin_bad[0]);
+      u.pad = 1;
+      *reinterpret_cast<UnitStat*>(out) = u;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) *R.done = 0u;  // ready for the next call (stream order)
 }
 
 // Unquantised activations (inScale == 0): one thread per vocab row and batch row, Σ code·a
@@ -1053,8 +1248,8 @@ gs_status gs_lm_head_create(gs_ctx* ctx, const gs_lm_head_desc* d, gs_lm_head** 
   if (e == cudaSuccess) e = cudaMemcpy(h->packed, tp.data(), tp.size() * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMalloc(&h->scales, sc.size() * 4);
   if (e == cudaSuccess) e = cudaMemcpy(h->scales, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMalloc(&h->flag, 4);
-  if (e == cudaSuccess) e = cudaMemset(h->flag, 0, 4);
+  if (e == cudaSuccess) e = cudaMalloc(&h->flag, 8);
+  if (e == cudaSuccess) e = cudaMemset(h->flag, 0, 8);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->device);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(lm_mma_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, LmPlan<16>::kSmem);
@@ -1205,8 +1400,9 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
     }
   }
   const int tps = static_cast<int>((h->tiles + h->num_sms - 1) / h->num_sms);
+  const int shards = static_cast<int>((h->tiles + tps - 1) / tps);
   const int nb = rows <= 1 ? 1 : rows <= 2 ? 2 : 4;
-  if (fused && rec_smem_bytes(nb, tps) > 200 * 1024) fused = false;
+  if (fused && rec_smem_bytes(nb, tps, shards, kcap) > 200 * 1024) fused = false;
   if (fused) {
     // the argument checks of gs_lm_head_logits, then the merge's batch checks, before any launch
     if (!activation || !activation_sum || ld_activation < h->hidden) {
@@ -1225,9 +1421,8 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
       if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
       return lfail(h, cs, "sampling: " + err);
     }
-    const int shards = static_cast<int>((h->tiles + tps - 1) / tps);
     const int64_t rec_bytes = shard_record_bytes(kcap, 0);
-    const size_t rneed = static_cast<size_t>(shards) * rows * rec_bytes;
+    const size_t rneed = static_cast<size_t>(shards + 1) * rows * rec_bytes;  // the shards' records, then the rows' combined
     if (rneed > h->records_bytes) {  // (grown on demand; the first call of a larger batch allocates)
       cudaStreamSynchronize(st);
       cudaFree(h->records);
@@ -1262,7 +1457,10 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
     ra.rec_bytes = rec_bytes;
     ra.tps = tps;
     ra.want_raw = out->logprob != nullptr;
-    const size_t smem = rec_smem_bytes(nb, tps);
+    ra.kcap = kcap;
+    ra.done = reinterpret_cast<unsigned*>(h->flag + 1);
+    ra.combined = rows == 1 ? h->records + static_cast<size_t>(shards) * rows * rec_bytes : nullptr;
+    const size_t smem = rec_smem_bytes(nb, tps, shards, kcap);
     cudaError_t e = cudaSuccess;
     auto go = [&](auto kern) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -1276,7 +1474,8 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
     else go(lm_records_kernel<4, 1024>);
     if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return lfail(h, GS_ECUDA, std::string("LM head records launch: ") + cudaGetErrorString(e));
-    gs_status s = gs_shard_merge(h->ctx, &b, shards, h->records, out, stream);
+    gs_status s = ra.combined ? gs_shard_merge(h->ctx, &b, 1, ra.combined, out, stream)
+                              : gs_shard_merge(h->ctx, &b, shards, h->records, out, stream);
     if (s != GS_OK) h->err = std::string("sampling: ") + gs_last_error(h->ctx);
     else ++h->fused_calls;
     return s;

@@ -176,6 +176,7 @@ NOHIST = dict(C1_PARAMS, repetitionPenalty=1.0, presencePenalty=0.0, frequencyPe
 def _mask(vocab, rows, seed, density=0.05, states=64):
     g = np.random.default_rng(seed)
     allowed = g.random((states, vocab)) < density
+    allowed = np.pad(allowed, ((0, 0), (0, -vocab % 128)))  # whole 16-byte groups of words
     table = np.packbits(allowed, axis=1, bitorder="little").view(np.uint32)
     return np.ascontiguousarray(table), g.integers(0, states, rows).astype(np.int32)
 
@@ -190,11 +191,13 @@ def _gpu_out(res, r):
 @pytest.mark.parametrize("vocab,rows,topk,masked,hidden,out_scale", [
     (262144, 1, 40, False, 1536, 0.0), (262144, 4, 64, True, 1536, 0.0), (262144, 2, 1, False, 1536, 0.0),
     (5000, 3, 40, False, 1536, 0.0), (8192, 4, 20, True, 1536, 0.0), (40000, 2, 40, False, 256, 0.0),
-    (100000, 3, 30, False, 640, 0.05), (262144, 1, 40, False, 1536, 0.05)])
+    (100000, 3, 30, False, 640, 0.05), (262144, 1, 40, False, 1536, 0.05), (5000, 1, 40, True, 1536, 0.0),
+    (3000, 1, 64, False, 1536, 0.0)])
 def test_fused_matches_oracle(sampler, vocab, rows, topk, masked, hidden, out_scale):
     # activations -> tokens through the fused route (the logits never stored) against the
     # oracle's exact LM head and sampleToken on the same inputs (hidden 256 and 640: other
-    # chunk splits of the dot products; output srq on)
+    # chunk splits of the dot products; output srq on; one row: the shards' records
+    # combined in the kernel, by the bound or, with fewer shards than topK, the radix select)
     packed, scales, act, act_sum = LM.synthetic(vocab, hidden, rows, seed=vocab + 3 * rows + topk, input_scale=0.02)
     rng = np.array([float(5000 + r) for r in range(rows)])
     params = [dict(NOHIST, topK=topk)]
