@@ -250,12 +250,14 @@ gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out);
  * Fused route (1..4 rows, input_scale != 0, no penalty history, every row greedy or
  * 1 <= topK <= 64): the logits stay on chip; each block of vocabulary ids writes the
  * record of a vocabulary shard (its statistics and top-k candidates, as
- * gs_shard_partials) to a handle-owned buffer and gs_shard_merge samples them.  Candidate
+ * gs_shard_partials) to a handle-owned buffer (at one row the kernel's last block then
+ * combines them into one record) and gs_shard_merge samples them.  Candidate
  * ids and order are those of gs_lm_head_logits + gs_sample; probabilities agree to
  * float64 summation order (normaliser partials per block instead of per streamed unit).
  * Other batches: the logits go to a handle-owned scratch (rows × vocab float32) and
  * gs_sample runs on it, identical to gs_lm_head_logits followed by gs_sample.  Either
- * buffer grows on the first call that needs more (allocates). */
+ * buffer grows on the first call that needs more (allocates).  The buffers and the
+ * records kernel's block counter belong to the handle: one call in flight per handle. */
 gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_activation,
                             const float* activation_sum, const gs_batch* batch, const gs_outputs* out,
                             void* stream);
