@@ -241,17 +241,9 @@ __device__ inline void select_threshold(const unsigned long long* buf, int n, in
   for (;;) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    // one shared-memory atomic per distinct digit of a warp (values of one row crowd a few
-    // bins: per-value atomics on the same counter serialise)
-    for (int base = threadIdx.x & ~31; base < n; base += blockDim.x) {
-      const int i = base + (threadIdx.x & 31);
-      unsigned dg = 256u;  // no value
-      if (i < n) {
-        const unsigned long long v = buf[i];
-        if (v != 0ull && (v & mask) == prefix) dg = static_cast<unsigned>(v >> shift) & 255u;
-      }
-      const unsigned peers = __match_any_sync(kFullMask, dg);
-      if (dg != 256u && static_cast<int>(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[dg], __popc(peers));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long v = buf[i];
+      if (v != 0ull && (v & mask) == prefix) atomicAdd(&hist[(v >> shift) & 255u], 1u);
     }
     __syncthreads();
     if (threadIdx.x < 32) {
