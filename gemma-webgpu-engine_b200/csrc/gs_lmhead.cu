@@ -627,7 +627,11 @@ __global__ void __launch_bounds__(128) lm_gemv_kernel(const __grid_constant__ Lm
 // The merge of vocabulary-sharded calls then treats the blocks as shards; no logits are
 // stored.
 constexpr int kRecMaxK = 64;     // topK the fused path serves (the merge's pack buffer)
-constexpr int kRecMaxRows = 4;   // rows of one fused call (the kernel's NB)
+// Rows of one fused call (the kernel's NB).  Measured against gs_lm_head_logits +
+// gs_sample (p50 per call, V = 262144, topK 40): 60 vs 76 us at one row, 67 vs 81 at two,
+// 95 vs 96 at three, 101 vs 98 at four (the dot products of more rows are issue-bound in
+// one 1024-thread block per SM, where the GEMV spreads them over nine 128-thread blocks).
+constexpr int kRecMaxRows = 2;
 constexpr int kRecCandCap = 512; // packs at or above the per-row bound, ranked by counting
 
 struct RecArgs {
@@ -1401,7 +1405,7 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
   }
   const int tps = static_cast<int>((h->tiles + h->num_sms - 1) / h->num_sms);
   const int shards = static_cast<int>((h->tiles + tps - 1) / tps);
-  const int nb = rows <= 1 ? 1 : rows <= 2 ? 2 : 4;
+  const int nb = rows <= 1 ? 1 : 2;
   if (fused && rec_smem_bytes(nb, tps, shards, kcap) > 200 * 1024) fused = false;
   if (fused) {
     // the argument checks of gs_lm_head_logits, then the merge's batch checks, before any launch
@@ -1470,8 +1474,7 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
       }
     };
     if (nb == 1) go(lm_records_kernel<1, 1024>);
-    else if (nb == 2) go(lm_records_kernel<2, 1024>);
-    else go(lm_records_kernel<4, 1024>);
+    else go(lm_records_kernel<2, 1024>);
     if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return lfail(h, GS_ECUDA, std::string("LM head records launch: ") + cudaGetErrorString(e));
     gs_status s = ra.combined ? gs_shard_merge(h->ctx, &b, 1, ra.combined, out, stream)

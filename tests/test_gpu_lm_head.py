@@ -189,9 +189,9 @@ def _gpu_out(res, r):
 
 
 @pytest.mark.parametrize("vocab,rows,topk,masked,hidden,out_scale", [
-    (262144, 1, 40, False, 1536, 0.0), (262144, 4, 64, True, 1536, 0.0), (262144, 2, 1, False, 1536, 0.0),
-    (5000, 3, 40, False, 1536, 0.0), (8192, 4, 20, True, 1536, 0.0), (40000, 2, 40, False, 256, 0.0),
-    (100000, 3, 30, False, 640, 0.05), (262144, 1, 40, False, 1536, 0.05), (5000, 1, 40, True, 1536, 0.0),
+    (262144, 1, 40, False, 1536, 0.0), (262144, 2, 64, True, 1536, 0.0), (262144, 2, 1, False, 1536, 0.0),
+    (5000, 2, 40, False, 1536, 0.0), (8192, 2, 20, True, 1536, 0.0), (40000, 2, 40, False, 256, 0.0),
+    (100000, 2, 30, False, 640, 0.05), (262144, 1, 40, False, 1536, 0.05), (5000, 1, 40, True, 1536, 0.0),
     (3000, 1, 64, False, 1536, 0.0)])
 def test_fused_matches_oracle(sampler, vocab, rows, topk, masked, hidden, out_scale):
     # activations -> tokens through the fused route (the logits never stored) against the
@@ -220,7 +220,7 @@ def test_fused_matches_oracle(sampler, vocab, rows, topk, masked, hidden, out_sc
     compare(_gpu_out(res, r), ids, margins, cands, rng_after=st, label="lm_head_fused")
 
 
-@pytest.mark.parametrize("rows,temperature,topk,masked", [(1, 0.8, 40, False), (3, 0.8, 64, True), (4, 0.0, 40, False),
+@pytest.mark.parametrize("rows,temperature,topk,masked", [(1, 0.8, 40, False), (2, 0.8, 64, True), (1, 0.0, 40, False),
                                                           (2, 0.0, 10, True), (1, 1.3, 5, True)])
 def test_fused_matches_two_step(sampler, rows, temperature, topk, masked):
     # fused route == gs_lm_head_logits + gs_sample: ids, candidate ids and counts and flags
@@ -255,39 +255,42 @@ def test_fused_error_rows_and_routes(sampler):
     # rows the fused route cannot sample flag as the two-step route flags them (a mask
     # state past the table, every logit NaN); batches outside its scope take the scratch route
     vocab = 8192
-    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, 4, seed=5, input_scale=0.02)
-    act_sum = act_sum.copy()
-    act_sum[2] = np.nan
-    table, state = _mask(vocab, 4, 9, states=8)
-    state[1] = 8  # past the table
-    state[3] = -1  # unconstrained
-    mk = dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(), mask_state=torch.from_numpy(state).cuda())
-    params = [dict(NOHIST, topK=40)]
+    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, 2, seed=5, input_scale=0.02)
+    table, state = _mask(vocab, 2, 9, states=8)
+    L = pkg._lib
     h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
     try:
-        a, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
-        r1 = torch.arange(4, dtype=torch.float64, device="cuda")
-        r2 = r1.clone()
-        one = h.sample(a, s, params, softcap=30.0, rng_state=r1, logprob=True, candidates=64, **mk)
-        two = sampler.sample(h.logits(a, s), params, softcap=30.0, rng_state=r2, logprob=True, candidates=64, **mk)
+        a = torch.from_numpy(act).cuda()
+        for case in ("state", "nan"):
+            sums, st = act_sum.copy(), state.copy()
+            if case == "state":
+                st[1] = 8  # past the table
+            else:
+                sums[1] = np.nan
+            s = torch.from_numpy(sums).cuda()
+            mk = dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(), mask_state=torch.from_numpy(st).cuda())
+            params = [dict(NOHIST, topK=40)]
+            r1 = torch.arange(2, dtype=torch.float64, device="cuda")
+            r2 = r1.clone()
+            one = h.sample(a, s, params, softcap=30.0, rng_state=r1, logprob=True, candidates=64, **mk)
+            two = sampler.sample(h.logits(a, s), params, softcap=30.0, rng_state=r2, logprob=True, candidates=64, **mk)
+            torch.cuda.synchronize()
+            for f in ("ids", "flags", "cand_count"):
+                assert torch.equal(getattr(one, f), getattr(two, f)), (case, f)
+            fl = one.flags.cpu().numpy().view(np.uint32)
+            assert fl[1] & L.FLAG_ERRORS and not (fl[0] & L.FLAG_ERRORS), case
+        assert h.fused_calls == 2
+        # three rows, a penalty history, topK past 64: the scratch route
+        s = torch.from_numpy(act_sum).cuda()
+        packed3, scales3, act3, sum3 = LM.synthetic(vocab, 1536, 3, seed=6, input_scale=0.02)
+        h.sample(torch.from_numpy(act3).cuda(), torch.from_numpy(sum3).cuda(), [dict(NOHIST, topK=40)], softcap=30.0,
+                 rng_state=torch.zeros(3, dtype=torch.float64, device="cuda"))
+        hist = torch.zeros((2, 4), dtype=torch.int32, device="cuda")
+        h.sample(a, s, [C1_PARAMS], softcap=30.0, history=hist,
+                 history_len=torch.full((2,), 4, dtype=torch.int32, device="cuda"),
+                 rng_state=torch.zeros(2, dtype=torch.float64, device="cuda"))
+        h.sample(a, s, [dict(NOHIST, topK=100)], softcap=30.0, rng_state=torch.zeros(2, dtype=torch.float64, device="cuda"))
         torch.cuda.synchronize()
-        assert h.fused_calls == 1
-        for f in ("ids", "flags", "cand_count"):
-            assert torch.equal(getattr(one, f), getattr(two, f)), f
-        L = pkg._lib
-        fl = one.flags.cpu().numpy().view(np.uint32)
-        assert fl[1] & L.FLAG_ERRORS and fl[2] & L.FLAG_ERRORS and not (fl[0] & L.FLAG_ERRORS)
-        # five rows, a penalty history, topK past 64: the scratch route
-        packed5, scales5, act5, sum5 = LM.synthetic(vocab, 1536, 5, seed=6, input_scale=0.02)
-        h.sample(torch.from_numpy(act5).cuda(), torch.from_numpy(sum5).cuda(), params, softcap=30.0,
-                 rng_state=torch.zeros(5, dtype=torch.float64, device="cuda"))
-        hist = torch.zeros((4, 4), dtype=torch.int32, device="cuda")
-        h.sample(a, torch.from_numpy(np.nan_to_num(act_sum)).cuda(), [C1_PARAMS], softcap=30.0, history=hist,
-                 history_len=torch.full((4,), 4, dtype=torch.int32, device="cuda"),
-                 rng_state=torch.zeros(4, dtype=torch.float64, device="cuda"))
-        h.sample(a, torch.from_numpy(np.nan_to_num(act_sum)).cuda(), [dict(NOHIST, topK=100)], softcap=30.0,
-                 rng_state=torch.zeros(4, dtype=torch.float64, device="cuda"))
-        torch.cuda.synchronize()
-        assert h.fused_calls == 1
+        assert h.fused_calls == 2
     finally:
         h.close()
