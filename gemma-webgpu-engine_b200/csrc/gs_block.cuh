@@ -81,6 +81,12 @@ __device__ inline void bitonic_sort_u32(uint32_t* v, int n2) {
   }
 }
 
+// Penalised value of one history id (src/runtime/sampling.ts:28-29), in double.
+__device__ __forceinline__ double penalise(double x, double count, double rp, double pres, double freq) {
+  double v = x < 0 ? __dmul_rn(x, rp) : __ddiv_rn(x, rp);
+  return __dsub_rn(v, __dadd_rn(pres, __dmul_rn(count, freq)));
+}
+
 __device__ __forceinline__ int pow2_ceil(int n) {
   int p = 1;
   while (p < n) p <<= 1;

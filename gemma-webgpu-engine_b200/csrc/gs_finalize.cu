@@ -44,12 +44,6 @@ __device__ __forceinline__ bool mask_allows(const uint32_t* mrow, uint32_t id) {
   return (__ldg(mrow + (id >> 5)) >> (id & 31)) & 1u;
 }
 
-// Penalised value of one history id (src/runtime/sampling.ts:28-29), in double.
-__device__ __forceinline__ double penalise(double x, double count, double rp, double pres, double freq) {
-  double v = x < 0 ? __dmul_rn(x, rp) : __ddiv_rn(x, rp);
-  return __dsub_rn(v, __dadd_rn(pres, __dmul_rn(count, freq)));
-}
-
 // Entries (twice: all scored entries, then those that can reach the top k), the filter
 // work arrays (work_cap each) and the history / pack scratch.
 size_t finalize_smem_bytes(int hist_cap, int ent_cap, int pack_cap, int work_cap) {

@@ -41,11 +41,6 @@ __device__ __forceinline__ bool w_mask_allows(const uint32_t* mrow, uint32_t id)
   return (__ldg(mrow + (id >> 5)) >> (id & 31)) & 1u;
 }
 
-__device__ __forceinline__ double w_penalise(double x, double count, double rp, double pres, double freq) {
-  double v = x < 0 ? __dmul_rn(x, rp) : __ddiv_rn(x, rp);
-  return __dsub_rn(v, __dadd_rn(pres, __dmul_rn(count, freq)));
-}
-
 __device__ __forceinline__ uint32_t w_hash(uint32_t v, int lg) { return (v * 2654435761u) >> (32 - lg); }
 
 // In-place bitonic sort of e[0, n2) (power of two) into ent_before order by one warp.
@@ -452,7 +447,7 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
             float xc = x[q];
             if (A.softcap != 0.0f) xc = softcap(xc, A.softcap, A.inv_softcap);
             if (!(xc < INFINITY)) nonfinite = true;  // NaN or +inf
-            const double xp = w_penalise(static_cast<double>(xc), static_cast<double>(cnt[q]), rp, pres, freq);
+            const double xp = penalise(static_cast<double>(xc), static_cast<double>(cnt[q]), rp, pres, freq);
             e = Ent{greedy ? xp : __ddiv_rn(xp, T), v[q], 1u};
           }
           ent[i] = e;

@@ -633,6 +633,7 @@ constexpr int kRecMaxK = 64;     // topK the fused path serves (the merge's pack
 // one 1024-thread block per SM, where the GEMV spreads them over nine 128-thread blocks).
 constexpr int kRecMaxRows = 2;
 constexpr int kRecCandCap = 512; // packs at or above the per-row bound, ranked by counting
+constexpr int kRecMaxHistory = 4096;  // penalty-history stride the fused route serves (its sort buffer)
 
 struct RecArgs {
   LmArgs L;
@@ -650,14 +651,30 @@ struct RecArgs {
   int32_t kcap;            // packs per record
   unsigned* done;          // blocks finished (the last one combines; it resets the count)
   unsigned char* combined; // [row] of rec_bytes: every shard's record of the row in one (null: no combining)
+  const int32_t* history;  // [row][history_stride] penalty history (null: none)
+  const int32_t* history_len;
+  int64_t history_stride;
+  int32_t hcap;            // penalised slots per record (history_stride; 0 without history)
+  int32_t hsort;           // sort buffer entries (power of two >= hcap)
+  int64_t hist_off;        // byte offset of the sort buffer and penalised-id bits in shared memory
 };
 
-// shared memory of the records kernel: activation words | logits [NB][R] | packs [NB][R];
-// the last block reuses it for every shard's packs of a row and the shards' maxima
-__host__ __device__ inline size_t rec_smem_bytes(int nb, int tps, int shards, int kcap) {
+inline int pow2_ceil_host(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+// shared memory of the records kernel: activation words | logits [NB][R] | packs [NB][R]
+// (the last block reuses it for every shard's packs of a row and the shards' maxima),
+// then, with a penalty history, its sort buffer and the penalised ids' bits [NB][R / 32]
+__host__ __device__ inline size_t rec_base_bytes(int nb, int tps, int shards, int kcap) {
   const size_t own = static_cast<size_t>(nb) * kLmMaxChunks * 32 * 4 + static_cast<size_t>(nb) * tps * kLmRows * 12;
   const size_t comb = static_cast<size_t>(shards) * (kcap + 1) * 8;
-  return own > comb ? own : comb;
+  return ((own > comb ? own : comb) + 15) & ~static_cast<size_t>(15);
+}
+__host__ __device__ inline size_t rec_smem_bytes(int nb, int tps, int shards, int kcap, int hsort) {
+  return rec_base_bytes(nb, tps, shards, kcap) + (hsort > 0 ? static_cast<size_t>(hsort) * 4 + static_cast<size_t>(nb) * tps * 16 : 0);
 }
 
 template <int NB, int THREADS>
@@ -670,7 +687,8 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
   __shared__ double fin_s[NB], fin_rs[NB];
   __shared__ int fin_na[NB], fin_bad[NB];
   __shared__ unsigned sel_hist[256];
-  __shared__ int sel_digit, sel_above, sel_binc, n_out, n_cl, s_last, n_tot;
+  __shared__ int sel_digit, sel_above, sel_binc, n_out, n_cl, s_last, n_tot, s_hl;
+  __shared__ unsigned pen_fl[NB];
   __shared__ unsigned long long top2[2 * (THREADS / 32)], cl[kRecCandCap], s_tau;
   const LmArgs& A = R.L;
   const int rows = A.rows < NB ? A.rows : NB;
@@ -726,6 +744,63 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
     const int64_t v = v_lo + i;
     return (__ldg(mrow[b] + (v >> 5)) >> (v & 31)) & 1u;
   };
+  // ---- penalty history: the ids of this block's range leave the live set; their exact
+  // penalised scores go to the record's fixed slots (sorted history position), as
+  // gs_shard_partials writes them ----
+  uint32_t* hs = reinterpret_cast<uint32_t*>(dsm + R.hist_off);  // [hsort] sorted history of a row
+  uint32_t* penb = hs + R.hsort;                                 // [NB][rlen / 32]
+  const int pw = rlen / 32;
+  if (tid < NB) pen_fl[tid] = 0u;
+  if (R.history) {
+    for (int i = tid; i < NB * pw; i += THREADS) penb[i] = 0u;
+    for (int b = 0; b < rows; ++b) {
+      int64_t hl = R.history_len ? R.history_len[b] : 0;
+      if (hl > R.history_stride) hl = R.history_stride;
+      if (hl < 0) hl = 0;
+      const int h2 = pow2_ceil(hl > 0 ? static_cast<int>(hl) : 1);
+      const int32_t* hrow = R.history + static_cast<int64_t>(b) * R.history_stride;
+      __syncthreads();
+      for (int i = tid; i < h2; i += THREADS) hs[i] = i < hl ? static_cast<uint32_t>(hrow[i]) : 0xffffffffu;
+      if (tid == 0) s_hl = static_cast<int>(hl);
+      __syncthreads();
+      bitonic_sort_u32(hs, h2);
+      const RowPlan& pl = R.plan[b];
+      unsigned char* r = R.records + (static_cast<int64_t>(blockIdx.x) * A.rows + b) * R.rec_bytes + sizeof(UnitStat) +
+                         8ll * R.kcap;
+      double* pkey = reinterpret_cast<double*>(r);
+      uint32_t* pid = reinterpret_cast<uint32_t*>(r + 8ll * R.hcap);
+      float* praw = reinterpret_cast<float*>(r + 12ll * R.hcap);
+      for (int i = tid; i < R.hcap; i += THREADS) {
+        double key = -INFINITY;
+        uint32_t id = 0xffffffffu;
+        float x = 0.0f;
+        if (i < hl) {
+          const uint32_t v = hs[i];  // negative ids sort past every vocabulary id
+          const int64_t lv = static_cast<int64_t>(v) - v_lo;
+          if (static_cast<int64_t>(v) < A.vocab && lv >= 0 && lv < nids && !(i > 0 && hs[i - 1] == v)) {
+            atomicOr(&penb[b * pw + static_cast<int>(lv >> 5)], 1u << (lv & 31));
+            if (allowed(b, static_cast<int>(lv))) {  // masked: -inf either way
+              int cnt = 1;
+              while (i + cnt < hl && hs[i + cnt] == v) ++cnt;
+              x = lg[static_cast<size_t>(b) * rlen + lv];
+              if (!(x < INFINITY)) atomicOr(&pen_fl[b], GS_FLAG_ERR_NONFINITE);  // NaN or +inf
+              const double xp = penalise(static_cast<double>(x), static_cast<double>(cnt), pl.repetition_penalty,
+                                         pl.presence_penalty, pl.frequency_penalty);
+              key = pl.mode == kModeGreedy ? xp : __ddiv_rn(xp, pl.temperature);
+              id = v;
+            }
+          }
+        }
+        pkey[i] = key;
+        pid[i] = id;
+        praw[i] = x;
+      }
+    }
+  }
+  __syncthreads();
+  auto live = [&](int b, int i) -> bool {  // allowed and not penalised
+    return allowed(b, i) && !(R.history && ((penb[b * pw + (i >> 5)] >> (i & 31)) & 1u));
+  };
   {
     float lmax[NB], rmax[NB];
     int na[NB], bad[NB];
@@ -742,9 +817,11 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
         if (b >= rows) break;
         const float xi = lg[static_cast<size_t>(b) * rlen + i];
         if (allowed(b, i)) {
-          lmax[b] = fmaxf(lmax[b], xi);
           ++na[b];
-          bad[b] |= xi != xi;
+          if (live(b, i)) {
+            lmax[b] = fmaxf(lmax[b], xi);
+            bad[b] |= xi != xi;
+          }
         }
         rmax[b] = fmaxf(rmax[b], xi);
       }
@@ -805,7 +882,7 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
         unsigned long long pk = 0ull;
         if (i < nids) {
           const float xi = lg[static_cast<size_t>(b) * rlen + i];
-          if (allowed(b, i)) {
+          if (live(b, i)) {
             if (m > -INFINITY) {
               const float d = xi - m;
               sp[b] += ex2_approx(fmaf(d, pl.a2_lo, d * pl.a2_hi));
@@ -956,7 +1033,7 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
       u.n_allowed = fin_na[b];
       u.n_cand = n_out;
       const bool nonfinite = fin_bad[b] || ssum != ssum || (R.want_raw && rsum != rsum) || m == INFINITY;
-      u.flags = (nonfinite ? GS_FLAG_ERR_NONFINITE : 0u) | (invalid[b] ? GS_FLAG_ERR_INVALID : 0u);
+      u.flags = (nonfinite ? GS_FLAG_ERR_NONFINITE : 0u) | (invalid[b] ? GS_FLAG_ERR_INVALID : 0u) | pen_fl[b];
       u.pad = 1;  // raw sums recorded
       *reinterpret_cast<UnitStat*>(rec) = u;
     }
@@ -1146,6 +1223,30 @@ __global__ void __launch_bounds__(THREADS) lm_records_kernel(const __grid_consta
       u.flags = static_cast<unsigned>(fin_bad[0]);
       u.pad = 1;
       *reinterpret_cast<UnitStat*>(out) = u;
+    }
+    if (R.history && rows == 1) {
+      // penalised slots: slot i (sorted history position) from the shard that holds its id
+      // (the sort buffer still holds this row's sorted history)
+      const int hl = s_hl;
+      unsigned char* orr = out + sizeof(UnitStat) + 8ll * R.kcap;
+      for (int i = tid; i < R.hcap; i += THREADS) {
+        double key = -INFINITY;
+        uint32_t id = 0xffffffffu;
+        float x = 0.0f;
+        if (i < hl) {
+          const uint32_t v = hs[i];
+          if (static_cast<int64_t>(v) < A.vocab && !(i > 0 && hs[i - 1] == v)) {
+            const int u = static_cast<int>(v / static_cast<uint32_t>(R.tps * kLmRows));
+            const unsigned char* ur = rec_at(u, b) + sizeof(UnitStat) + 8ll * R.kcap;
+            key = __ldcg(reinterpret_cast<const double*>(ur) + i);
+            id = __ldcg(reinterpret_cast<const unsigned*>(ur + 8ll * R.hcap) + i);
+            x = __ldcg(reinterpret_cast<const float*>(ur + 12ll * R.hcap) + i);
+          }
+        }
+        reinterpret_cast<double*>(orr)[i] = key;
+        reinterpret_cast<uint32_t*>(orr + 8ll * R.hcap)[i] = id;
+        reinterpret_cast<float*>(orr + 12ll * R.hcap)[i] = x;
+      }
     }
     __syncthreads();
   }
@@ -1389,10 +1490,15 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
   cudaGetDevice(&prev);
   if (prev != h->device) cudaSetDevice(h->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Fused: up to kRecMaxRows rows of int8-grid activations, no penalty history, every row
-  // 1 <= topK <= kRecMaxK or greedy: the LM head writes shard records, the merge samples.
-  bool fused = rows >= 1 && rows <= kRecMaxRows && h->in_scale != 0.0f && !batch->history && batch->params &&
-               (batch->params_count == 1 || batch->params_count == rows);
+  // Fused: up to kRecMaxRows rows of int8-grid activations (a penalty history at one row),
+  // every row 1 <= topK <= kRecMaxK or greedy: the LM head writes shard records, the merge
+  // samples them.
+  bool fused = rows >= 1 && rows <= kRecMaxRows && h->in_scale != 0.0f && batch->params &&
+               (batch->params_count == 1 || batch->params_count == rows) &&
+               // a penalty history at one row only: the records are then combined into one, and the
+               // merge plans its penalised slots as gs_sample does for one row (147 shards' slots
+               // would not fit its shared memory)
+               (!batch->history || (rows == 1 && batch->history_stride >= 1 && batch->history_stride <= kRecMaxHistory));
   int kcap = 1;
   RecArgs ra{};
   if (fused) {
@@ -1406,7 +1512,9 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
   const int tps = static_cast<int>((h->tiles + h->num_sms - 1) / h->num_sms);
   const int shards = static_cast<int>((h->tiles + tps - 1) / tps);
   const int nb = rows <= 1 ? 1 : 2;
-  if (fused && rec_smem_bytes(nb, tps, shards, kcap) > 200 * 1024) fused = false;
+  const int hcap = batch->history ? static_cast<int>(batch->history_stride) : 0;
+  const int hsort = batch->history ? pow2_ceil_host(hcap) : 0;
+  if (fused && rec_smem_bytes(nb, tps, shards, kcap, hsort) > 200 * 1024) fused = false;
   if (fused) {
     // the argument checks of gs_lm_head_logits, then the merge's batch checks, before any launch
     if (!activation || !activation_sum || ld_activation < h->hidden) {
@@ -1425,7 +1533,7 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
       if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
       return lfail(h, cs, "sampling: " + err);
     }
-    const int64_t rec_bytes = shard_record_bytes(kcap, 0);
+    const int64_t rec_bytes = shard_record_bytes(kcap, hcap);
     const size_t rneed = static_cast<size_t>(shards + 1) * rows * rec_bytes;  // the shards' records, then the rows' combined
     if (rneed > h->records_bytes) {  // (grown on demand; the first call of a larger batch allocates)
       cudaStreamSynchronize(st);
@@ -1463,8 +1571,14 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
     ra.want_raw = out->logprob != nullptr;
     ra.kcap = kcap;
     ra.done = reinterpret_cast<unsigned*>(h->flag + 1);
+    ra.history = batch->history;
+    ra.history_len = batch->history ? batch->history_len : nullptr;
+    ra.history_stride = batch->history ? batch->history_stride : 0;
+    ra.hcap = hcap;
+    ra.hsort = hsort;
+    ra.hist_off = static_cast<int64_t>(rec_base_bytes(nb, tps, shards, kcap));
     ra.combined = rows == 1 ? h->records + static_cast<size_t>(shards) * rows * rec_bytes : nullptr;
-    const size_t smem = rec_smem_bytes(nb, tps, shards, kcap);
+    const size_t smem = rec_smem_bytes(nb, tps, shards, kcap, hsort);
     cudaError_t e = cudaSuccess;
     auto go = [&](auto kern) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

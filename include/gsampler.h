@@ -247,8 +247,8 @@ gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out);
  * LM head pass to sampleToken, decode-model.ts:135-139 then sampling.ts:18), sampled as by
  * gs_sample on the context the head was created on.  batch->logits must be NULL,
  * batch->vocab 0 or the head's vocab; dtype and row_stride are set here.
- * Fused route (1 or 2 rows, input_scale != 0, no penalty history, every row greedy or
- * 1 <= topK <= 64): the logits stay on chip; each block of vocabulary ids writes the
+ * Fused route (1 or 2 rows, input_scale != 0, a penalty history only at one row with a
+ * history_stride of at most 4096, every row greedy or 1 <= topK <= 64): the logits stay on chip; each block of vocabulary ids writes the
  * record of a vocabulary shard (its statistics and top-k candidates, as
  * gs_shard_partials) to a handle-owned buffer (at one row the kernel's last block then
  * combines them into one record) and gs_shard_merge samples them.  Candidate

@@ -137,7 +137,13 @@ def test_sample_matches_two_step(sampler, vocab, rows, topk, masked):
                              logprob=True, candidates=64, **mk)
         h.check()
         torch.cuda.synchronize()
-        for f in ("ids", "flags", "logprob", "cand_ids", "cand_probs", "cand_count"):
+        exact = ("ids", "flags", "cand_ids", "cand_count")
+        if h.fused_calls == 0:  # scratch route: the same kernels on the same logits
+            exact += ("logprob", "cand_probs")
+        else:  # fused route (one row with a history): normaliser partials summed per block
+            np.testing.assert_allclose(one.cand_probs.cpu().numpy(), two.cand_probs.cpu().numpy(), rtol=1e-6, atol=0)
+            np.testing.assert_allclose(one.logprob.cpu().numpy(), two.logprob.cpu().numpy(), rtol=1e-9, atol=1e-12)
+        for f in exact:
             assert torch.equal(getattr(one, f), getattr(two, f)), f
         assert torch.equal(r1, r2)
     finally:
@@ -294,3 +300,36 @@ def test_fused_error_rows_and_routes(sampler):
         assert h.fused_calls == 2
     finally:
         h.close()
+
+
+@pytest.mark.parametrize("topk,masked,temperature", [(40, False, 0.8), (64, True, 0.8), (40, False, 0.0), (5, True, 1.2)])
+def test_fused_history_matches_oracle(sampler, topk, masked, temperature):
+    # one row with a penalty history (repeated ids, the row's best ids, a negative id, ids
+    # masked out) through the fused route against the oracle
+    vocab = 262144
+    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, 1, seed=400 + topk, input_scale=0.02)
+    logits = O.lm_head(packed, scales, act, act_sum, in_scale=0.02)
+    order = np.argsort(-logits[0], kind="stable")
+    g = np.random.default_rng(topk)
+    hist = np.concatenate([order[:3], order[:1], order[5:8], [-5], g.integers(0, vocab, 20)]).astype(np.int32)
+    history, history_len = hist[None, :].copy(), np.array([len(hist)], np.int32)
+    params = [dict(C1_PARAMS, temperature=temperature, topK=topk)]
+    table, state = _mask(vocab, 1, 77, density=0.5) if masked else (None, None)
+    rng = np.array([123.0])
+    ids, margins, cands, st = oracle_rows(O, logits, vocab, 30.0, [dict(params[0], repetitionWindow=len(hist))],
+                                          history=history, history_len=history_len, mask_table=table,
+                                          mask_state=state, rng_state=rng)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    try:
+        r = torch.from_numpy(rng).cuda()
+        mk = {} if table is None else dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(),
+                                           mask_state=torch.from_numpy(state).cuda())
+        res = h.sample(torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda(), params, softcap=30.0,
+                       history=torch.from_numpy(history).cuda(), history_len=torch.from_numpy(history_len).cuda(),
+                       rng_state=r, logprob=True, candidates=2048, **mk)
+        h.check()
+        torch.cuda.synchronize()
+        assert h.fused_calls == 1
+    finally:
+        h.close()
+    compare(_gpu_out(res, r), ids, margins, cands, rng_after=st, label="lm_head_fused_history")
