@@ -10,12 +10,22 @@ of the N GPUs samples its own C4 batch of 4096 rows (weak scaling: the work per 
 fixed, the global batch is 4096·N; no collective on the data path).  Launched as one
 process per GPU (torchrun).
 
-Also reported on rank 0: the bfloat16 variant of C4, the p50/p95 step latency of C1
-(B=1, 256 sequential steps), the end-to-end rate through the host-buffer entry point
-(gs_sample_host), and the CPU oracle timed on the host cores as a baseline.
+Also reported on rank 0: the other configurations at their own batch sizes (C2 on the
+histogram path, C3, C4 without its constraint mask in float32 and bfloat16, C4 bfloat16),
+each with its dominant kernels' HBM roofline; the p50/p95 step latency of C1 (B=1, 256
+sequential steps); the end-to-end rate through the host-buffer entry point
+(gs_sample_host); the CPU oracle timed on the host cores as a baseline; the constraint
+bitmask builder and the int2 LM head.  With N > 1 GPUs, every rank also runs C5 in the
+vocabulary-sharded layout (each GPU one slice of every row, one all-gather of the
+per-shard records per step).
 
 `--impl reference` times the reference sampler's CPU restatement (oracle/oracle.cpp; the
 reference is TypeScript and there is no Node runtime on the machine) on all host threads.
+
+`--only NAME` runs one workload a few times and exits (the driver the profiles/ captures
+run under ncu): C1..C5 (`--rows`, `--calls`, `--no-mask`, `--no-history`, `--topk`,
+`--dtype`), `lm-head` / `lm-head-sample` (`--rows`, `--calls`) or `mask-builder`
+(`--states`, `--calls`).
 """
 from __future__ import annotations
 
@@ -50,8 +60,17 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-extras", action="store_true", help="skip bf16 / latency / e2e / cpu legs")
-    ap.add_argument("--rows", type=int, default=GLOBAL_BATCH,
-                    help="rows per GPU (default 4096 = C4's batch); smaller values are for profiler captures")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="rows per GPU (default: the configuration's batch, 4096 for C4); smaller values are for "
+                         "profiler captures")
+    ap.add_argument("--only", default=None,
+                    choices=["C1", "C2", "C3", "C4", "C5", "lm-head", "lm-head-sample", "mask-builder"],
+                    help="run one workload --calls times and exit (profiling driver)")
+    ap.add_argument("--calls", type=int, default=3)
+    ap.add_argument("--no-mask", action="store_true", help="--only: drop the configuration's constraint table")
+    ap.add_argument("--no-history", action="store_true", help="--only: drop the configuration's penalty history")
+    ap.add_argument("--topk", type=int, default=None, help="--only: override the configuration's topK")
+    ap.add_argument("--states", type=int, default=512, help="--only mask-builder: DFA states")
     return ap.parse_args()
 
 
@@ -72,16 +91,24 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def traffic_per_row(dtype: str):
-    """DRAM bytes per row of the streaming kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "stream_kernel_traffic.json")
+def traffic_per_row(leg: str):
+    """DRAM bytes per row of a leg's dominant kernel(s) from the committed ncu summary
+    (profiles/dram_traffic.json: one capture per leg, scaled by rows)."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        e = d.get(dtype)
+        e = d.get(leg)
         return None if e is None else float(e["dram_bytes"]) / float(e["rows"])
     except Exception:
         return None
+
+
+def bench_config(world: int, per: int, dtype: str) -> dict:
+    """The `config` of the headline line; the reference arm reports the same dict."""
+    return {"workload": WORKLOAD_DESC, "global_batch": per * world, "rows_per_gpu": per, "vocab": VOCAB,
+            "logits_dtype": dtype, "parallelism": f"rows across {world} GPU(s), {per} per GPU (no collective)",
+            "l2": "inputs larger than L2 (rows x 1 MiB per GPU)"}
 
 
 # --------------------------------------------------------------------------- clocks
@@ -156,7 +183,7 @@ def run_ours(args, rank, world, local):
     L = pkg._lib
 
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
-    per = args.rows  # this GPU's own batch (rank 0's rows are C4's rows)
+    per = args.rows or GLOBAL_BATCH  # this GPU's own batch (rank 0's rows are C4's rows)
     wl = W.make("C4", device=dev, rows=per, shard=rank)
     logits = wl.logits.to(dtype).contiguous()
     hist = wl.history.contiguous()
@@ -233,14 +260,12 @@ def run_ours(args, rank, world, local):
     value = total_rows * args.steps / (elapsed_ms / 1e3)
     peak, peak_kind = measured_peak()
     achieved = per * bytes_per_row / stream_avg_s / 1e9
-    tpr = traffic_per_row(args.dtype)
+    tpr = traffic_per_row(f"c4_{args.dtype}")
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32" if args.dtype == "f32" else "bf16", "data": "synthetic (seeded torch Philox, C4 distributions)",
-        "config": {"workload": WORKLOAD_DESC, "global_batch": per * world, "rows_per_gpu": per, "vocab": VOCAB,
-                   "logits_dtype": args.dtype, "parallelism": f"rows across {world} GPU(s), {per} per GPU (no collective)",
-                   "l2": "inputs larger than L2 (rows x 1 MiB per GPU)"},
+        "config": bench_config(world, per, args.dtype),
         "logits_gbps": total_rows * bytes_per_row * args.steps / (elapsed_ms / 1e3) / 1e9,
         "roofline": {"bound": "hbm", "kernel": "gs::stream2_kernel", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
@@ -257,8 +282,13 @@ def run_ours(args, rank, world, local):
         # end to end on every rank (whole-job rows over the slowest rank's time)
         result["e2e"] = e2e_leg(args, pkg, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per,
                                 world)
+    if world > 1 and not args.no_extras:
+        # every rank takes part: one all-gather of shard records per step
+        result["c5_vocab_sharded"] = c5_sharded_leg(pkg, W, sampler, dev, rank, world)
     if rank == 0 and not args.no_extras:
-        result.update(extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per,
+        del logits
+        torch.cuda.empty_cache()
+        result.update(extras(args, pkg, W, sampler, dev, None, hist, hlen, table, mstate, seeds, params, per,
                              world))
     sampler.close()
     if world > 1:
@@ -312,32 +342,21 @@ def e2e_leg(args, pkg, sampler, dev, logits, hist, hlen, table, mstate, seeds, p
 
 
 def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per, world):
-    import numpy as np
+    """Rank 0's other legs (after the headline's logits are freed)."""
     import torch
 
     res = {}
     stream = torch.cuda.current_stream(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    # ---- bf16 variant of the same batch
-    if args.dtype == "f32":
-        xb = logits.to(torch.bfloat16)
-        rng = torch.tensor([pkg.SeededRandom(s).state for s in seeds], dtype=torch.float64, device=dev)
-        for _ in range(10):
-            o = sampler.sample(xb, params, softcap=30.0, history=hist, history_len=hlen, mask_table=table,
-                               mask_state=mstate, rng_state=rng, stream=stream.cuda_stream)
-        n_b = max(10, min(500, args.steps // 4))
-        e0.record(stream)
-        for _ in range(n_b):
-            o = sampler.sample(xb, params, softcap=30.0, history=hist, history_len=hlen, mask_table=table,
-                               mask_state=mstate, rng_state=rng, stream=stream.cuda_stream, out=o)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        sb = e0.elapsed_time(e1) / 1e3
-        bpr = VOCAB * 2 + VOCAB // 8 + 4 * hist.shape[1]
-        res["bf16"] = {"value": per * n_b / sb, "unit": UNIT, "steps": n_b,
-                       "logits_gbps": per * bpr * n_b / sb / 1e9}
-        del xb
+    # ---- the other configurations at their own batch sizes, each with its roofline
+    legs = {}
+    legs["c4_bf16"] = config_leg(pkg, W, sampler, dev, "C4", per, dtype=torch.bfloat16, steps=100)
+    legs["c4_f32_unmasked"] = config_leg(pkg, W, sampler, dev, "C4", per, mask=False, steps=100)
+    legs["c4_bf16_unmasked"] = config_leg(pkg, W, sampler, dev, "C4", per, dtype=torch.bfloat16, mask=False,
+                                          steps=100)
+    legs["c3"] = config_leg(pkg, W, sampler, dev, "C3", 256, steps=200)
+    legs["c2"] = config_leg(pkg, W, sampler, dev, "C2", 64, steps=200)
+    res["configs"] = legs
+    res["bf16"] = {k: legs["c4_bf16"][k] for k in ("value", "unit", "steps", "logits_gbps")}
     # ---- C1 latency: B=1, 256 sequential steps, fresh logits each step, one seeded stream
     steps = 256
     lg = torch.empty((steps, VOCAB), dtype=torch.float32, device=dev)
@@ -359,14 +378,143 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     res["latency_b1"] = {"workload": "C1: B=1, V=262144, soft cap 30, T=0.8, topK 40, topP 0.95, seed 42, "
                                      "256 sequential steps",
                          "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],
-                         "timing": "CUDA events between consecutive gs_sample calls (device time, no graph)"}
+                         "timing": "CUDA events between consecutive gs_sample calls (device time, no graph; "
+                                   "256 distinct 1 MiB rows, 256 MiB > L2)"}
     del lg
     # ---- CPU baseline (N = 1 only): the oracle on a bounded sample of the same rows
     if world == 1:
-        res["cpu_baseline"] = cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per)
+        res["cpu_baseline"] = cpu_baseline(W, dev, per)
         res["mask_builder"] = mask_builder_leg(pkg, W, sampler)
         res["lm_head"] = lm_head_leg(pkg, sampler, stream)
     return res
+
+
+def config_leg(pkg, W, sampler, dev, name, rows, dtype=None, mask=True, history=True, steps=100):
+    """One configuration at `rows` rows: rows/s, the path's kernel time split (streaming
+    pass / merge or histogram path, CUDA events recorded by the library) and the HBM
+    roofline of the dominant launches.  Inputs smaller than twice L2 are replicated and
+    the copies used in turn, so that every step reads its logits from HBM."""
+    import torch
+    import ctypes
+    L = pkg._lib
+    wl = W.make(name, device=dev, rows=rows, dtype=dtype)
+    params = pkg.prepare_params(wl.params)
+    kw = dict(softcap=wl.softcap)
+    if history and wl.history is not None:
+        kw.update(history=wl.history, history_len=wl.history_len)
+    if mask and wl.mask_table is not None:
+        kw.update(mask_table=wl.mask_table, mask_state=wl.mask_state)
+    esz = wl.logits.element_size()
+    in_bytes = wl.logits.numel() * esz
+    copies = min(8, max(1, -(-2 * 126 * 2**20 // in_bytes)))
+    xs = [wl.logits] + [wl.logits.clone() for _ in range(copies - 1)]
+    rng = wl.rng_state(dev)
+    stream = torch.cuda.current_stream(dev)
+    out = None
+    for i in range(5):
+        out = sampler.sample(xs[i % copies], params, rng_state=rng, stream=stream.cuda_stream, out=out, **kw)
+    torch.cuda.synchronize()
+    fl = out.flags.cpu().numpy().view("uint32")
+    errors = int(((fl & L.FLAG_ERRORS) != 0).sum())
+    L.lib().gs_profile_enable(sampler.handle, 1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        out = sampler.sample(xs[i % copies], params, rng_state=rng, stream=stream.cuda_stream, out=out, **kw)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3
+    s_ms, s_n, m_ms, m_n = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double(), ctypes.c_int64()
+    L.lib().gs_profile_read(sampler.handle, ctypes.byref(s_ms), ctypes.byref(s_n), ctypes.byref(m_ms),
+                            ctypes.byref(m_n))
+    L.lib().gs_profile_enable(sampler.handle, 0)
+    stream_us = s_ms.value / max(1, s_n.value) * 1e3
+    merge_us = m_ms.value / max(1, m_n.value) * 1e3
+    large = bool((fl & L.FLAG_LARGE_PATH).all())
+    hl = wl.history.shape[1] if (history and wl.history is not None) else 0
+    bpr = wl.vocab * esz + (wl.vocab // 8 if (mask and wl.mask_table is not None) else 0) + 4 * hl
+    peak, peak_kind = measured_peak()
+    tag = f"{name.lower()}" + ("" if name != "C4" else f"_{'bf16' if esz == 2 else 'f32'}") + \
+        ("_unmasked" if (name == "C4" and not mask) else "")
+    if large:
+        kern, kern_us = "histogram path (large_hist, large_select, large_gather, large_resolve)", merge_us
+    else:
+        kern, kern_us = "gs::stream2_kernel (streaming pass)", stream_us
+    achieved = rows * bpr / (kern_us / 1e6) / 1e9
+    tpr = traffic_per_row(tag)
+    res = {
+        "workload": f"{name} x {rows} rows" + ("" if mask or wl.mask_table is None else ", no constraint mask"),
+        "value": rows * steps / dt, "unit": UNIT, "steps": steps, "us_per_step": dt / steps * 1e6,
+        "logits_dtype": "bf16" if esz == 2 else "f32",
+        "logits_gbps": rows * bpr * steps / dt / 1e9, "row_errors": errors,
+        "l2": f"{copies} copies of the {in_bytes / 2**20:.0f} MiB input used in turn" if copies > 1
+              else "input larger than L2",
+        "kernel_split_us": {"streaming_pass": stream_us, "merge_or_histogram_path": merge_us},
+        "roofline": {"bound": "hbm", "kernel": kern, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                     "algorithmic_bytes_per_launch": rows * bpr, "avg_launch_us": kern_us,
+                     "step_frac": rows * bpr / (dt / steps) / 1e9 / peak,
+                     "traffic": None if tpr is None else tpr * rows},
+    }
+    del xs, wl
+    torch.cuda.empty_cache()
+    return res
+
+
+def c5_sharded_leg(pkg, W, sampler, dev, rank, world, steps=200):
+    """C5 in the vocabulary-sharded layout on every rank: rank g holds ids
+    [g·V/N, (g+1)·V/N) of the 8 rows; per step gs_shard_partials, one all-gather of the
+    records (NCCL) and gs_shard_merge.  Device time per step and of the all-gather alone
+    (CUDA events, slowest rank), and whether every rank's ids equal whole-row sampling."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    SH = importlib.import_module(PKG + ".sharding")
+    wl = W.make("C5", device=dev)
+    rows = wl.rows
+    vs = SH.VocabShardedSampler(sampler, VOCAB)
+    off, size = vs.plan.offset, vs.plan.size
+    local = wl.logits[:, off:off + size].contiguous()
+    params = pkg.prepare_params(wl.params)
+    stream = torch.cuda.current_stream(dev)
+    rng = wl.rng_state(dev)
+    whole = sampler.sample(wl.logits, params, softcap=wl.softcap, rng_state=wl.rng_state(dev))
+    res = vs.sample(local, params, softcap=wl.softcap, rng_state=rng)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(res.ids, whole.ids))
+    ok = torch.tensor([1 if same else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    rec = sampler.shard_partials(local, params, vocab_offset=off, vocab_total=VOCAB, softcap=wl.softcap)
+    rec_bytes = rec.numel()
+    for _ in range(5):
+        vs.sample(local, params, softcap=wl.softcap, rng_state=rng)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        vs.sample(local, params, softcap=wl.softcap, rng_state=rng)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    step_s = e0.elapsed_time(e1) / 1e3 / steps
+    ga = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for _ in range(3):
+        SH.exchange_records(rec)
+    ga[0].record(stream)
+    for _ in range(steps):
+        SH.exchange_records(rec)
+    ga[1].record(stream)
+    torch.cuda.synchronize()
+    ag_s = ga[0].elapsed_time(ga[1]) / 1e3 / steps
+    t = torch.tensor([step_s, ag_s], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_s, ag_s = float(t[0]), float(t[1])
+    del np
+    return {"workload": f"C5: B={rows}, V={VOCAB} split into {world} contiguous shards of {size} ids, Gumbel(0,2) "
+                        "+ 30 planted ties, T 1.5, topK 1024, topP 0.99",
+            "us_per_step": step_s * 1e6, "rows_per_s": rows / step_s, "allgather_us": ag_s * 1e6,
+            "record_bytes_per_rank": rec_bytes, "nccl_ranks": world, "matches_whole_row_sampling": bool(ok.item()),
+            "timing": "CUDA events around steps of partials + NCCL all-gather + merge, slowest rank"}
 
 
 def lm_head_leg(pkg, sampler, stream):
@@ -485,7 +633,7 @@ def mask_builder_leg(pkg, W, sampler):
                     "(workloads.synthetic_dfa); the Gemma tokenizer's bytes are not available"}
 
 
-def cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per):
+def cpu_baseline(W, dev, per):
     import numpy as np
     import torch
     from oracle import oracle as O
@@ -493,16 +641,18 @@ def cpu_baseline(logits, hist, hlen, table, mstate, seeds, params, per):
     threads = os.cpu_count() or 1
     # about 10-30 s of host work: ~25 rows/s per core for C4 rows
     n = min(per, max(64, 25 * threads * 15))
-    x = logits[:n].float().cpu().numpy()
-    h = hist[:n].cpu().numpy()
-    hl = hlen[:n].cpu().numpy()
-    ms = mstate[:n].cpu().numpy()
+    wl = W.make("C4", device=dev, rows=n)
+    x = wl.logits.float().cpu().numpy()
+    h = wl.history.cpu().numpy()
+    hl = wl.history_len.cpu().numpy()
+    ms = wl.mask_state.cpu().numpy()
     used = sorted(set(ms.tolist()))
     remap = {s: i for i, s in enumerate(used)}
-    tb = table[torch.tensor(used, device=table.device)].cpu().numpy().view(np.uint32)
+    tb = wl.mask_table[torch.tensor(used, device=wl.mask_table.device)].cpu().numpy().view(np.uint32)
     ms2 = np.array([remap[s] for s in ms.tolist()], dtype=np.int32)
-    st = np.array([O.seeded_init(s) for s in seeds[:n]], dtype=np.float64)
-    p = dict(params, repetitionWindow=h.shape[1])
+    st = np.array([O.seeded_init(s) for s in wl.seeds[:n]], dtype=np.float64)
+    p = dict(wl.params[0], repetitionWindow=h.shape[1])
+    del wl
     t0 = time.perf_counter()
     O.sample_rows(x, VOCAB, 30.0, h, hl, tb, ms2, [p], rng_state=st, threads=threads)
     dt = time.perf_counter() - t0
@@ -544,18 +694,79 @@ def run_reference(args, rank, world):
         step()
     dt = time.perf_counter() - t0
     value = rows * args.steps / dt
-    sample = (f"{rows} C4-distributed rows per step (one per host thread), oracle/oracle.cpp (C++ restatement of "
-              f"src/runtime/sampling.ts; the TypeScript reference needs Node, which is not installed)")
+    sample = (f"{rows} C4-distributed rows per step (one per host thread) of the {GLOBAL_BATCH}-row C4 batch, "
+              f"rows/s extrapolated from them; oracle/oracle.cpp (C++ restatement of src/runtime/sampling.ts; the "
+              f"TypeScript reference needs Node, which is not installed)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": WORKLOAD_DESC, "global_batch": GLOBAL_BATCH * world, "rows_per_gpu": GLOBAL_BATCH,
-                   "vocab": VOCAB,
-                   "parallelism": "host threads, rank 0 only"},
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded torch CPU generator, C4 distributions)",
+        "config": bench_config(world, GLOBAL_BATCH, "f32"),
+        "sample_rows_per_step": rows,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def run_only(args):
+    """Profiling driver: one workload `--calls` times on cuda:0, then a one-line summary."""
+    import numpy as np
+    import torch
+    pkg = importlib.import_module(PKG)
+    W = importlib.import_module(PKG + ".workloads")
+    dev = torch.device("cuda", 0)
+    sampler = pkg.GpuSampler(0)
+    if args.only in ("C1", "C2", "C3", "C4", "C5"):
+        dtype = torch.bfloat16 if args.dtype == "bf16" else None
+        wl = W.make(args.only, device=dev, rows=args.rows, dtype=dtype)
+        params = [dict(p, topK=args.topk) for p in wl.params] if args.topk is not None else wl.params
+        params = pkg.prepare_params(params)
+        kw = dict(softcap=wl.softcap, rng_state=wl.rng_state(dev))
+        if wl.history is not None and not args.no_history:
+            kw.update(history=wl.history, history_len=wl.history_len)
+        if wl.mask_table is not None and not args.no_mask:
+            kw.update(mask_table=wl.mask_table, mask_state=wl.mask_state)
+        res = None
+        for _ in range(args.calls):
+            res = sampler.sample(wl.logits, params, **kw)
+        torch.cuda.synchronize()
+        fl = res.flags.cpu().numpy().view(np.uint32)
+        print(args.only, "rows", wl.rows, "first ids", res.ids[:4].tolist(), "row errors",
+              int(((fl & pkg._lib.FLAG_ERRORS) != 0).sum()))
+    elif args.only in ("lm-head", "lm-head-sample"):
+        LM = importlib.import_module(PKG + ".lm_head")
+        rows = args.rows or 1
+        packed, scales, act, act_sum = LM.synthetic(VOCAB, 1536, rows, seed=5)
+        head = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+        x, s = torch.from_numpy(act).to(dev), torch.from_numpy(act_sum).to(dev)
+        if args.only == "lm-head-sample":
+            p = [dict(temperature=0.8, topK=40, topP=0.95, minP=0.0, typicalP=1.0, repetitionPenalty=1.0,
+                      presencePenalty=0.0, frequencyPenalty=0.0)]
+            st = torch.arange(rows, dtype=torch.float64, device=dev)
+            for _ in range(args.calls):
+                res = head.sample(x, s, p, softcap=30.0, rng_state=st)
+            head.check()
+            torch.cuda.synchronize()
+            print("rows", rows, "ids", res.ids.tolist(), "fused calls", head.fused_calls)
+        else:
+            out = None
+            for _ in range(args.calls):
+                out = head.logits(x, s, out=out)
+            head.check()
+            torch.cuda.synchronize()
+            print("rows", rows, "logits[0, :4]", out[0, :4].tolist())
+        head.close()
+    else:  # mask-builder
+        C = importlib.import_module(PKG + ".constraints")
+        tr, fi = W.synthetic_dfa(max(args.states, 1))
+        con = C.GpuConstraint(sampler, C.Dfa.from_transitions(tr, fi), W.synthetic_token_bytes())
+        table = None
+        for _ in range(args.calls):
+            table, dead = con.build_masks(list(range(args.states)), table=table)
+        torch.cuda.synchronize()
+        print("states", args.states, "rows with nothing allowed", int(dead.sum()))
+        con.close()
+    sampler.close()
 
 
 def main():
@@ -563,6 +774,8 @@ def main():
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.only:
+        run_only(args)
     else:
         run_ours(args, rank, world, local)
 

@@ -26,6 +26,8 @@ from .sampling import (  # noqa: F401
     mask_constraint_logits,
     params_from_config,
     prepare_params,
+    reasoning_mask_rows,
+    reasoning_mask_state,
     sample_token,
     token_log_probability,
     windowed_history,

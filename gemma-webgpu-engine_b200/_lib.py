@@ -52,7 +52,7 @@ EXPORTS = (
     "gs_profile_read", "gs_sample_noalloc", "gs_constraint_create", "gs_constraint_destroy",
     "gs_constraint_last_error", "gs_constraint_build_masks", "gs_lm_head_create", "gs_lm_head_destroy",
     "gs_lm_head_last_error", "gs_lm_head_logits", "gs_lm_head_sample", "gs_lm_head_check",
-    "gs_lm_head_fused_calls",
+    "gs_lm_head_fused_calls", "gs_build_reasoning_mask_rows",
 )
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -168,6 +168,7 @@ def lib() -> ctypes.CDLL:
     L.gs_token_log_probability.argtypes = [P, P, i32, i32, i64, i64, f32, P, P, P]
     L.gs_mask_constraint_logits.argtypes = [P, P, i64, P, i64, P, i64, P, P]
     L.gs_build_mask_row.argtypes = [P, i64, P, i64, P, i64, P, P]
+    L.gs_build_reasoning_mask_rows.argtypes = [P, i64, P, i32, P, i64, P]
     L.gs_constraint_create.argtypes = [P, ctypes.POINTER(GsDfaDesc), ctypes.POINTER(GsVocabBytesDesc),
                                        ctypes.POINTER(P)]
     L.gs_constraint_destroy.argtypes = [P]

@@ -142,23 +142,3 @@ class GpuConstraint:
             msg = (self._L.gs_constraint_last_error(self._h) or b"").decode()
             raise (ValueError(msg) if st == _lib.GS_EINVAL else SamplerError(st, msg))
         return table, dead
-
-
-if __name__ == "__main__":
-    import argparse
-    import importlib
-    ap = argparse.ArgumentParser(description="build bitmask rows of the synthetic DFA (workloads.synthetic_dfa) "
-                                             "over the synthetic vocabulary on cuda:0")
-    ap.add_argument("--states", type=int, default=512)
-    ap.add_argument("--calls", type=int, default=2)
-    a = ap.parse_args()
-    import torch
-    pkg = importlib.import_module(__package__)
-    W = importlib.import_module(__package__ + ".workloads")
-    tr, fi = W.synthetic_dfa(max(a.states, 1))
-    con = GpuConstraint(pkg.GpuSampler(0), Dfa.from_transitions(tr, fi), W.synthetic_token_bytes())
-    table = None
-    for _ in range(a.calls):
-        table, dead = con.build_masks(list(range(a.states)), table=table)
-    torch.cuda.synchronize()
-    print("states", a.states, "rows with nothing allowed", int(dead.sum()))

@@ -429,6 +429,16 @@ gs_status gs_build_mask_row(gs_ctx* c, int64_t vocab, const int32_t* legal, int6
   return e == cudaSuccess ? GS_OK : cuda_fail(c, e, "mask row");
 }
 
+gs_status gs_build_reasoning_mask_rows(gs_ctx* c, int64_t vocab, const uint8_t* has_bytes, int32_t end_channel_id,
+                                       uint32_t* rows_out, int64_t mask_words, void* stream) {
+  if (!c) return GS_EINVAL;
+  if (vocab <= 0 || !has_bytes || !rows_out || mask_words < (vocab + 31) / 32) return fail(c, GS_EINVAL, "bad arguments");
+  DeviceGuard g(c->device);
+  cudaError_t e = launch_reasoning_rows(vocab, has_bytes, end_channel_id, rows_out, mask_words,
+                                        static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GS_OK : cuda_fail(c, e, "reasoning mask rows");
+}
+
 gs_status gs_softcap(gs_ctx* c, const float* in, float* out, int64_t n, float cap, void* stream) {
   if (!c) return GS_EINVAL;
   if (n < 0 || (n > 0 && (!in || !out)) || !(cap > 0) || !std::isfinite(cap)) return fail(c, GS_EINVAL, "bad arguments");

@@ -147,6 +147,8 @@ cudaError_t launch_mask_logits(const float* raw, int64_t vocab, const int32_t* l
                                const int32_t* term, int64_t nt, float* out, cudaStream_t st);
 cudaError_t launch_build_mask_row(int64_t vocab, const int32_t* legal, int64_t nl, const int32_t* term,
                                   int64_t nt, uint32_t* row, cudaStream_t st);
+cudaError_t launch_reasoning_rows(int64_t vocab, const uint8_t* has_bytes, int32_t end_id, uint32_t* rows,
+                                  int64_t words, cudaStream_t st);
 cudaError_t launch_softcap(const float* in, float* out, int64_t n, float cap, float inv_cap, cudaStream_t st);
 cudaError_t launch_softcap_digest(uint64_t lo, uint64_t hi, float cap, float inv_cap,
                                   unsigned long long* acc, cudaStream_t st);

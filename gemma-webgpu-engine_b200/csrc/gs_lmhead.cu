@@ -1503,7 +1503,14 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
   RecArgs ra{};
   if (fused) {
     for (int i = 0; i < rows && fused; ++i) {
-      const RowPlan pl = make_plan(batch->params[batch->params_count == 1 ? 0 : i], h->vocab);
+      // (a row whose params fail validation leaves the fused route before it is planned;
+      // the other route's batch check then reports the error)
+      const gs_params& pr = batch->params[batch->params_count == 1 ? 0 : i];
+      if (!valid_params(pr, nullptr)) {
+        fused = false;
+        break;
+      }
+      const RowPlan pl = make_plan(pr, h->vocab);
       if (pl.mode == kModeLarge || pl.k_eff > kRecMaxK) fused = false;
       ra.plan[i] = pl;
       kcap = pl.k_eff > kcap ? pl.k_eff : kcap;

@@ -11,14 +11,16 @@
 // The array is a file-scope __device__ object: every GPU that loads this library keeps
 // GS_NOALLOC_SCRATCH_BYTES of it until the process exits.  Host code cannot pass the
 // array's name to a kernel (on the host that name is only a stand-in, not a device
-// address), so the device address is looked up once per device with
-// cudaGetSymbolAddress, with that device current, on the first call made on it.
+// address), so every call looks the device address up with cudaGetSymbolAddress, with
+// the call's device current.  The first call on a device also loads the module there
+// (make it before any stream capture); later lookups are host-side only.  Looking the
+// address up on every call, instead of caching it, keeps the call correct after the
+// device's primary context is reset and created again, when the array can move.
 //
 // Every call writes each scratch byte it later reads, so nothing has to start at zero;
 // the array keeps the previous call's contents.  All calls share the one array: two
 // calls whose kernels overlap on the GPU (different streams, no ordering between them)
 // race on it and produce undefined results.
-#include <mutex>
 #include <string>
 
 #include "gs_plan.cuh"
@@ -30,9 +32,6 @@ static_assert(GS_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size must keep 256-b
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[GS_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_setup_mu;
-void* g_scratch_addr[kMaxDevices] = {};
 thread_local std::string g_noalloc_err;
 
 gs_status set_error(gs_status s, const std::string& msg) {
@@ -40,21 +39,14 @@ gs_status set_error(gs_status s, const std::string& msg) {
   return s;
 }
 
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
+// Device address of g_noalloc_scratch on the current device, looked up on every call
+// (see the file comment).
 gs_status scratch_address(void** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(GS_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return set_error(GS_EUNSUPPORTED, "device index above 63");
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(GS_ECUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(GS_ECUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+  *out = p;
   return GS_OK;
 }
 

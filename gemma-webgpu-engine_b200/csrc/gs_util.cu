@@ -82,6 +82,32 @@ cudaError_t launch_build_mask_row(int64_t vocab, const int32_t* legal, int64_t n
   return cudaGetLastError();
 }
 
+// maskReasoningLogits (src/runtime/gemma-session.ts:1331-1345) as two bitmask rows: row 0
+// allows the ids with token bytes, row 1 also the end-of-channel id.  One thread per id,
+// one warp ballot per word.
+__global__ void reasoning_rows_kernel(int64_t vocab, const uint8_t* has_bytes, int32_t end_id, uint32_t* rows,
+                                      int64_t words) {
+  const int64_t n = words * 32;
+  for (int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x); i0 < n; i0 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = i0 + threadIdx.x;  // (trip count uniform over the warp: n is a multiple of 32)
+    const bool b = i < vocab && has_bytes[i] != 0;
+    const uint32_t w = __ballot_sync(kFullMask, b);
+    if ((threadIdx.x & 31) == 0) {
+      const int64_t wi = i >> 5;
+      uint32_t w1 = w;
+      if (end_id >= 0 && end_id < vocab && (end_id >> 5) == wi) w1 |= 1u << (end_id & 31);
+      rows[wi] = w;
+      rows[words + wi] = w1;
+    }
+  }
+}
+
+cudaError_t launch_reasoning_rows(int64_t vocab, const uint8_t* has_bytes, int32_t end_id, uint32_t* rows,
+                                  int64_t words, cudaStream_t st) {
+  if (words > 0) reasoning_rows_kernel<<<148 * 4, 256, 0, st>>>(vocab, has_bytes, end_id, rows, words);
+  return cudaGetLastError();
+}
+
 __global__ void softcap_kernel(const float* in, float* out, int64_t n, float cap, float inv_cap) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     out[i] = softcap(in[i], cap, inv_cap);

@@ -133,37 +133,3 @@ def synthetic(vocab: int, hidden: int = 1536, rows: int = 1, seed: int = 61, inp
     act = (q * s).astype(np.float32)
     act_sum = act.sum(axis=1, dtype=np.float32)
     return packed, scales, act, act_sum
-
-
-if __name__ == "__main__":
-    import argparse
-    import importlib
-    ap = argparse.ArgumentParser(description="run the int2 LM head on cuda:0 over seeded synthetic inputs of the "
-                                             "reference's shape (V = 262144, hidden 1536)")
-    ap.add_argument("--rows", type=int, default=1)
-    ap.add_argument("--calls", type=int, default=3)
-    ap.add_argument("--vocab", type=int, default=262144)
-    ap.add_argument("--sample", action="store_true",
-                    help="activations -> tokens (gs_lm_head_sample; C1's filters without penalties, softcap 30)")
-    a = ap.parse_args()
-    import torch
-    pkg = importlib.import_module(__package__)
-    packed, scales, act, act_sum = synthetic(a.vocab, 1536, a.rows, seed=5)
-    head = GpuLmHead(pkg.GpuSampler(0), packed, scales, 0.02, 0.0)
-    x, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
-    if a.sample:
-        p = [dict(temperature=0.8, topK=40, topP=0.95, minP=0.0, typicalP=1.0, repetitionPenalty=1.0,
-                  presencePenalty=0.0, frequencyPenalty=0.0)]
-        st = torch.arange(a.rows, dtype=torch.float64, device=x.device)
-        for _ in range(a.calls):
-            res = head.sample(x, s, p, softcap=30.0, rng_state=st)
-        head.check()
-        torch.cuda.synchronize()
-        print("rows", a.rows, "ids", res.ids.tolist(), "fused calls", head.fused_calls)
-    else:
-        out = None
-        for _ in range(a.calls):
-            out = head.logits(x, s, out=out)
-        head.check()
-        torch.cuda.synchronize()
-        print("rows", a.rows, "logits[0, :4]", out[0, :4].tolist())

@@ -547,3 +547,40 @@ def build_mask_row(vocab: int, legal_token_ids: Sequence[int], termination_token
     if st != _lib.GS_OK:
         _raise(st, s.handle)
     return row
+
+
+# src/runtime/gemma-tokenizer.ts:19 and src/runtime/gemma-session.ts:124-125
+GEMMA_END_CHANNEL_TOKEN_ID = 101
+GEMMA_REQUIRED_REASONING_TOKENS = 16
+GEMMA_MAX_REQUIRED_REASONING_TOKENS = 64
+
+
+def reasoning_mask_rows(has_bytes, *, end_channel_id: int = GEMMA_END_CHANNEL_TOKEN_ID, device: int = 0,
+                        sampler: GpuSampler | None = None):
+    """maskReasoningLogits (src/runtime/gemma-session.ts:1331-1345) as a two-row bitmask
+    table (int32 words, [2, ceil(V/32)]): row 0 allows the ids whose tokenBytes is not null
+    (``has_bytes[id]`` true), row 1 also ``end_channel_id``.  Built once per vocabulary;
+    a required-reasoning step samples with ``reasoning_mask_state(...)`` as its row's mask
+    state over this table instead of masking a copy of the logits every token."""
+    import numpy as np
+    import torch
+    s = sampler or default_sampler(device)
+    dev = torch.device("cuda", device)
+    hb = torch.as_tensor(np.ascontiguousarray(np.asarray(has_bytes, dtype=bool).astype(np.uint8))).to(dev) \
+        if not isinstance(has_bytes, torch.Tensor) else has_bytes.to(device=dev, dtype=torch.uint8).contiguous()
+    vocab = hb.numel()
+    words = (vocab + 31) // 32
+    rows = torch.empty((2, words), dtype=torch.int32, device=dev)
+    st = s._L.gs_build_reasoning_mask_rows(s.handle, vocab, hb.data_ptr(), int(end_channel_id), rows.data_ptr(),
+                                           words, ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    if st != _lib.GS_OK:
+        _raise(st, s.handle)
+    return rows
+
+
+def reasoning_mask_state(reasoning_content_tokens: int) -> int:
+    """Row of the reasoning table for a required-reasoning step: the end-of-channel id is
+    allowed again once GEMMA_REQUIRED_REASONING_TOKENS reasoning tokens were sampled
+    (src/runtime/gemma-session.ts:676-687; at GEMMA_MAX_REQUIRED_REASONING_TOKENS the
+    caller emits the end-of-channel id without sampling)."""
+    return 1 if reasoning_content_tokens >= GEMMA_REQUIRED_REASONING_TOKENS else 0

@@ -230,47 +230,3 @@ def synthetic_dfa(nodes: int = 4096, seed: int = 52):
         transitions.append(ranges)
     finals = [n for n in range(nodes) if rng.random() < 0.2]
     return transitions, finals
-
-
-def run(name: str, rows: int | None = None, calls: int = 2, dtype=None, candidates: int = 0, prepared: bool = True,
-        mask: bool = True, history: bool = True, top_k: int | None = None):
-    """Samples configuration `name` `calls` times through GpuSampler on cuda:0 and
-    returns the last result (the driver the profiling summaries run under a profiler);
-    `mask` / `history` False drop the configuration's constraint table / penalty history,
-    `top_k` overrides its topK."""
-    import importlib
-    import torch
-    pkg = importlib.import_module(__package__)
-    dev = torch.device("cuda", 0)
-    wl = make(name, device=dev, rows=rows, dtype=dtype)
-    sampler = pkg.GpuSampler(0)
-    params = [dict(p, topK=top_k) for p in wl.params] if top_k is not None else wl.params
-    params = pkg.prepare_params(params) if prepared else params
-    kw = dict(softcap=wl.softcap, rng_state=wl.rng_state(dev), candidates=candidates)
-    if wl.history is not None and history:
-        kw.update(history=wl.history, history_len=wl.history_len)
-    if wl.mask_table is not None and mask:
-        kw.update(mask_table=wl.mask_table, mask_state=wl.mask_state)
-    res = None
-    for _ in range(calls):
-        res = sampler.sample(wl.logits, params, **kw)
-    torch.cuda.synchronize()
-    return res
-
-
-if __name__ == "__main__":
-    import argparse
-    ap = argparse.ArgumentParser(description="sample one of the configurations C1-C5 on cuda:0")
-    ap.add_argument("name", choices=["C1", "C2", "C3", "C4", "C5"])
-    ap.add_argument("--rows", type=int, default=None)
-    ap.add_argument("--calls", type=int, default=2)
-    ap.add_argument("--bf16", action="store_true")
-    ap.add_argument("--candidates", type=int, default=0)
-    ap.add_argument("--no-mask", action="store_true")
-    ap.add_argument("--no-history", action="store_true")
-    ap.add_argument("--topk", type=int, default=None)
-    a = ap.parse_args()
-    import torch
-    r = run(a.name, a.rows, a.calls, torch.bfloat16 if a.bf16 else None, a.candidates, mask=not a.no_mask,
-            history=not a.no_history, top_k=a.topk)
-    print(a.name, "rows", r.ids.shape[0], "first ids", r.ids[:4].tolist())

@@ -164,6 +164,19 @@ gs_status gs_build_mask_row(gs_ctx* ctx, int64_t vocab, const int32_t* legal, in
                             const int32_t* termination, int64_t n_termination, uint32_t* row_out,
                             void* stream);
 
+/* maskReasoningLogits (src/runtime/gemma-session.ts:1331-1345) as two rows of an
+ * allowed-token bitmask table (rows_out: device [2, mask_words] uint32).  Row 0 allows
+ * the ids whose tokenizer.tokenBytes(id) is not null (has_bytes: device [vocab] uint8,
+ * nonzero = has bytes); row 1 allows the same ids plus end_channel_id
+ * (GEMMA_END_CHANNEL_TOKEN_ID = 101, src/runtime/gemma-tokenizer.ts:19; ignored outside
+ * [0, vocab)), which generate() re-allows once GEMMA_REQUIRED_REASONING_TOKENS = 16
+ * reasoning tokens were sampled (src/runtime/gemma-session.ts:124,676-687).  Bits past
+ * the vocabulary are zero.  A required-reasoning step then samples with
+ * mask_state = (reasoning tokens >= 16) ? 1 : 0 over this table, exactly as the
+ * reference samples the masked copy of the logits. */
+gs_status gs_build_reasoning_mask_rows(gs_ctx* ctx, int64_t vocab, const uint8_t* has_bytes, int32_t end_channel_id,
+                                       uint32_t* rows_out, int64_t mask_words, void* stream);
+
 /* ---- Constraint bitmask builder: the [S, mask_words] table from a compiled DFA ----
  * Replaces CompiledGenerationConstraint.legalTokenIds (src/runtime/constraints.ts:56-92,
  * transitionByte :222-247, isViableConstraintState :254-292, findViableStates :294-314)
@@ -284,11 +297,16 @@ gs_status gs_softcap_digest(gs_ctx* ctx, uint64_t lo, uint64_t hi, float cap, ui
  * candidates: about 2.1 MiB for 4096 rows at topK 50, 1.1 MiB for 8 rows at topK 1024)
  * lives in one fixed device array of GS_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU
  * which loads the library keeps until the process exits.  Larger requests fail with
- * GS_EUNSUPPORTED.  It runs on the current device; its first call on a device looks up
- * the array's device address.  All calls share the array (the previous call's contents
- * stay in it; nothing needs clearing, every call writes what it reads), so calls whose
- * kernels overlap on the GPU race.  After a failure, gs_last_error(NULL) returns this
- * thread's message.
+ * GS_EUNSUPPORTED.  It runs on the current device and looks up the array's device
+ * address there on every call (a host-side lookup, so a device whose primary context was
+ * reset is served at the array's new address); the first call on a device also loads
+ * the library's module there, so make it before any stream capture.  All calls share the
+ * array (the previous call's contents stay in it; nothing needs clearing, every call
+ * writes what it reads), so calls whose kernels overlap on the GPU race.  Per-row params
+ * (params_count > 1) are uploaded from batch->params with cudaMemcpyAsync: from pageable
+ * host memory that copy is staged and can block the calling thread, so a caller that
+ * needs a fully asynchronous call passes a pinned host array or a single params entry.
+ * After a failure, gs_last_error(NULL) returns this thread's message.
  */
 #define GS_NOALLOC_SCRATCH_BYTES (8u << 20)
 gs_status gs_sample_noalloc(const gs_batch* batch, const gs_outputs* out, void* stream);

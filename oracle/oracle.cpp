@@ -12,6 +12,7 @@
 //   src/runtime/sampling.ts:82-90    cumulativeCut
 //   src/runtime/sampling.ts:92-96    argmax
 //   src/runtime/constraints.ts:159-173 maskConstraintLogits
+//   src/runtime/gemma-session.ts:1331-1345 maskReasoningLogits
 //   src/webgpu/decode-lm-head.ts:176-256 int2 LM head (the producer of the logits)
 //
 // Parity pins: tests/test_oracle_golden.py checks this file against every
@@ -460,18 +461,30 @@ uint64_t oracle_softcap_digest(uint64_t lo, uint64_t hi, float cap, float inv_ca
   return s;
 }
 
+// maskReasoningLogits (src/runtime/gemma-session.ts:1331-1345): a copy of the logits
+// with -inf at every id whose tokenBytes is null (has_bytes[id] == 0); with allow_end the
+// end-of-channel id keeps its raw value (a write outside the array is a no-op in JS).
+void oracle_mask_reasoning_logits(const float* raw_logits, int64_t vocab, const uint8_t* has_bytes,
+                                  int32_t allow_end, int64_t end_id, float* out) {
+  for (int64_t i = 0; i < vocab; ++i) out[i] = has_bytes[i] ? raw_logits[i] : -INFINITY;
+  if (allow_end && end_id >= 0 && end_id < vocab) out[end_id] = raw_logits[end_id];
+}
+
 // Batched driver used for the timed CPU baseline: rows are independent, so rows are
 // split over `threads` host threads.  history is [rows, history_stride] with per-row
 // lengths; mask_table/mask_state optional (state < 0 = unconstrained): masked ids are
 // -inf before penalties exactly as selectConstrainedToken does
-// (src/runtime/gemma-session.ts:1327-1328).  softcap 0 = off.
+// (src/runtime/gemma-session.ts:1327-1328).  softcap 0 = off.  With cand_count, each
+// row's final candidate list (at most cand_cap entries of [rows, cand_cap]) and its length
+// are written as oracle_sample_token writes them.
 void oracle_sample_rows(const float* logits, int64_t rows, int64_t vocab, int64_t row_stride,
                         float softcap,
                         const int32_t* history, int64_t history_stride, const int32_t* history_len,
                         const uint32_t* mask_table, int64_t mask_words, const int32_t* mask_state,
                         const OracleConfig* configs, int32_t per_row_config,
                         double* rng_state, const double* uniforms,
-                        int32_t* out_ids, OracleTrace* traces, int threads) {
+                        int32_t* out_ids, OracleTrace* traces, int threads,
+                        int32_t* cand_ids, double* cand_probs, int32_t* cand_count, int64_t cand_cap) {
   if (threads < 1) threads = 1;
   std::vector<std::thread> pool;
   for (int t = 0; t < threads; ++t) {
@@ -491,10 +504,14 @@ void oracle_sample_rows(const float* logits, int64_t rows, int64_t vocab, int64_
         const int32_t* h = history ? history + r * history_stride : nullptr;
         OracleTrace tr;
         int32_t id;
+        int32_t* ci = cand_count ? cand_ids + r * cand_cap : nullptr;
+        double* cp = cand_count ? cand_probs + r * cand_cap : nullptr;
+        int32_t* cc = cand_count ? cand_count + r : nullptr;
+        const int64_t cap = cand_count ? cand_cap : 0;
         if (uniforms) {
-          id = oracle_sample_token(row.data(), vocab, h, hl, c, uniforms[r], nullptr, nullptr, nullptr, 0, &tr);
+          id = oracle_sample_token(row.data(), vocab, h, hl, c, uniforms[r], ci, cp, cc, cap, &tr);
         } else {
-          id = oracle_sample_token_seeded(row.data(), vocab, h, hl, c, rng_state + r, nullptr, nullptr, nullptr, 0, &tr);
+          id = oracle_sample_token_seeded(row.data(), vocab, h, hl, c, rng_state + r, ci, cp, cc, cap, &tr);
         }
         out_ids[r] = id;
         if (traces) traces[r] = tr;

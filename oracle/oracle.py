@@ -93,9 +93,11 @@ def lib():
         L.oracle_constraint_masks.argtypes = [ctypes.c_int32, P, P, P, P, P, ctypes.c_int64, P, P, ctypes.c_int32,
                                               P, P, P, P, ctypes.c_int64, P, ctypes.c_int64, P, ctypes.c_int64, P]
         L.oracle_constraint_masks.restype = None
+        L.oracle_mask_reasoning_logits.argtypes = [P, ctypes.c_int64, P, ctypes.c_int32, ctypes.c_int64, P]
+        L.oracle_mask_reasoning_logits.restype = None
         L.oracle_sample_rows.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                          P, ctypes.c_int64, P, P, ctypes.c_int64, P,
-                                         P, ctypes.c_int32, P, P, P, P, ctypes.c_int]
+                                         P, ctypes.c_int32, P, P, P, P, ctypes.c_int, P, P, P, ctypes.c_int64]
         L.oracle_lm_head_shader_f32.argtypes = [P, P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int,
                                                 ctypes.c_float, P, ctypes.c_int64]
         L.oracle_lm_head_shader_f32.restype = None
@@ -189,6 +191,17 @@ def mask_constraint_logits(raw_logits, legal, termination) -> np.ndarray:
     return out
 
 
+def mask_reasoning_logits(raw_logits, has_bytes, allow_end: bool, end_id: int = 101) -> np.ndarray:
+    """maskReasoningLogits restated (src/runtime/gemma-session.ts:1331-1345)."""
+    x = _f32(raw_logits)
+    hb = np.ascontiguousarray(np.asarray(has_bytes, dtype=bool).astype(np.uint8))
+    assert hb.size == x.size
+    out = np.empty_like(x)
+    lib().oracle_mask_reasoning_logits(x.ctypes.data, x.size, hb.ctypes.data, 1 if allow_end else 0, int(end_id),
+                                       out.ctypes.data)
+    return out
+
+
 def softcap(x, cap: float) -> np.ndarray:
     a = _f32(x)
     out = np.empty_like(a)
@@ -267,9 +280,11 @@ def constraint_masks(dfa, vocab, node, pending_len=None, pending_bytes=None, ter
 def sample_rows(logits: np.ndarray, vocab: int, softcap_value: float, history: np.ndarray | None,
                 history_len: np.ndarray | None, mask_table: np.ndarray | None, mask_state: np.ndarray | None,
                 configs: list, rng_state: np.ndarray | None = None, uniforms: np.ndarray | None = None,
-                threads: int = 1):
+                threads: int = 1, cand_cap: int = 0):
     """Batched restatement (rows independent, split across host threads).
-    Returns (ids, traces, advanced rng_state)."""
+    Returns (ids, traces, advanced rng_state); with cand_cap > 0 also each row's final
+    candidate list as (ids [rows, cand_cap], probabilities [rows, cand_cap], counts [rows]),
+    a count above cand_cap meaning a list longer than the arrays."""
     logits = np.ascontiguousarray(logits, dtype=np.float32)
     rows = logits.shape[0]
     stride = logits.shape[1]
@@ -287,8 +302,16 @@ def sample_rows(logits: np.ndarray, vocab: int, softcap_value: float, history: n
     def ptr(a):
         return None if a is None else a.ctypes.data
 
+    cids = cprobs = ccount = None
+    if cand_cap > 0:
+        cids = np.zeros((rows, cand_cap), dtype=np.int32)
+        cprobs = np.zeros((rows, cand_cap), dtype=np.float64)
+        ccount = np.zeros(rows, dtype=np.int32)
     lib().oracle_sample_rows(logits.ctypes.data, rows, vocab, stride, float(softcap_value),
                              ptr(hist), 0 if hist is None else hist.shape[1], ptr(hlen),
                              ptr(mt), 0 if mt is None else mt.shape[1], ptr(ms),
-                             cfgs, per_row, ptr(st), ptr(un), ids.ctypes.data, traces, int(threads))
+                             cfgs, per_row, ptr(st), ptr(un), ids.ctypes.data, traces, int(threads),
+                             ptr(cids), ptr(cprobs), ptr(ccount), int(cand_cap))
+    if cand_cap > 0:
+        return ids, traces, st, (cids, cprobs, ccount)
     return ids, traces, st

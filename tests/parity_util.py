@@ -77,6 +77,24 @@ def oracle_rows(O, logits_np, vocab, softcap, params, *, history=None, history_l
     return ids, margins, cands, st
 
 
+def oracle_rows_batched(O, logits_np, vocab, softcap, params, *, history=None, history_len=None, mask_table=None,
+                        mask_state=None, rng_state=None, uniforms=None, cand_cap=64):
+    """oracle_rows over all host threads in one call (the batched restatement also writes
+    each row's candidate list): the same outputs at full batch sizes in seconds."""
+    rows = logits_np.shape[0]
+    ps = params if len(params) == rows else [params[0]] * rows
+    ids, traces, st, (cid, cpr, cnt) = O.sample_rows(
+        logits_np, vocab, softcap, history, history_len, mask_table, mask_state, ps, rng_state=rng_state,
+        uniforms=uniforms, threads=os.cpu_count() or 1, cand_cap=cand_cap)
+    cands = []
+    for r in range(rows):
+        n = int(cnt[r])
+        m = min(n, cand_cap)
+        cands.append((cid[r, :m].tolist(), cpr[r, :m].tolist(), n))
+    margins = np.array([min(t.margin_top_p, t.margin_draw, t.margin_min_p, t.margin_typical) for t in traces])
+    return ids, margins, cands, st
+
+
 def compare(gpu: GpuOut, ids, margins, cands, *, rng_after=None, label=""):
     """Asserts the parity bar; returns the number of boundary rows that differ."""
     from importlib import import_module

@@ -37,7 +37,8 @@ def _gs_outputs(L, out, cap):
     return o
 
 
-@pytest.mark.parametrize("name,rows,per_row", [("C4", 96, False), ("C5", 8, False), ("C3", 40, True)])
+@pytest.mark.parametrize("name,rows,per_row", [("C4", 96, False), ("C5", 8, False), ("C3", 40, True),
+                                               ("C2", 8, True)])
 def test_noalloc_matches_gs_sample_on_two_calls(pkg, name, rows, per_row):
     import torch
     L = pkg._lib
