@@ -458,10 +458,15 @@ int sm_count() {
   }
   return counts[dev];
 }
+bool dense_eligible(const StreamArgs& a, int dtype);
+cudaError_t launch_dense(const StreamArgs& a, int dtype, int rows, cudaStream_t st, int num_sms);
+
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
   const int units = rows * a.splits;
   if (units == 0) return cudaSuccess;
-  // pipelined kernel for small topK on aligned rows; the general kernel otherwise
+  // unconstrained batches without raw sums: the dense kernel; other aligned small-topK
+  // batches: the warp-pipelined kernel; the general kernel otherwise
+  if (a.kmax <= pipe_max_k() && dense_eligible(a, dtype)) return launch_dense(a, dtype, rows, st, sm_count());
   if (a.kmax <= pipe_max_k() && stream2_eligible(a, dtype, rows))
     return launch_stream2(a, dtype, rows, stream2_smem_bytes(a.chunk), st, sm_count());
   if (dtype == GS_DTYPE_F32) {
