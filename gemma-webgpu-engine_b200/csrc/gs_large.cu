@@ -43,7 +43,8 @@ namespace gs {
 namespace {
 
 constexpr int kNB = 4096;              // histogram bins
-constexpr double kRangeKeys = 40.0;    // bins span 40 units of logit/T below the maximum
+constexpr double kRangeKeys = 40.0;    // bins span at most 40 units of logit/T below the maximum
+constexpr double kMinRangeKeys = 1e-3; // ... and at least this many (all live values equal)
 constexpr int kCluster = 8;            // histogram CTAs per row (one cluster)
 constexpr int kHistThreads = 512;
 constexpr int kHistSub = 32768;        // ids per live-bitmap pass of a histogram CTA
@@ -77,6 +78,8 @@ struct LargeRow {
   int32_t mp_hi;
   float gat_lo;      // raw logits below this lie below every selected bin
   float Mx;          // maximum over live values (allowed and not penalised)
+  float bscale;      // bins per logit unit below Mx (the histogram kernel sets the row's bins)
+  float bwidth;      // logit units per bin
   float raw_m;
   double raw_s;
   double M;          // maximum key (logit/T) over live values and penalised entries
@@ -124,8 +127,20 @@ __device__ __forceinline__ int bin_of(float x, float Mx, float scale) {
   return b >= static_cast<float>(kNB - 1) ? kNB - 1 : static_cast<int>(b);
 }
 
-__device__ __forceinline__ float bin_scale(double T) { return static_cast<float>(static_cast<double>(kNB) / (kRangeKeys * T)); }
-__device__ __forceinline__ float bin_width_logit(double T) { return static_cast<float>(kRangeKeys * T / kNB); }
+// The row's bins: they span the live keys from the maximum Mx down to the minimum Mn (two
+// bins of slack for the float binning, so the deepest bin stays empty), or 40 key units
+// when the live keys spread wider (the deepest bin then gathers everything below, counted
+// with zero mass: e^-40 each), so that a flat row (high temperature, small spread) still
+// spreads its ids over the bins.
+__device__ __forceinline__ void bin_geometry(double T, float Mx, float Mn, float* scale, float* width) {
+  double r = kRangeKeys;
+  if (Mx > -INFINITY && Mn > -INFINITY && Mx < INFINITY && Mx >= Mn) {
+    const double fit = (static_cast<double>(Mx) - static_cast<double>(Mn)) / T * kNB / (kNB - 2);
+    if (fit < r) r = fit > kMinRangeKeys ? fit : kMinRangeKeys;
+  }
+  *scale = static_cast<float>(static_cast<double>(kNB) / (r * T));
+  *width = static_cast<float>(r * T / kNB);
+}
 
 // Ids of a histogram CTA: an eighth of the row, a multiple of 128.
 __host__ __device__ inline int64_t hist_chunk(int64_t V) {
@@ -292,7 +307,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   __shared__ float red_f[32];
   __shared__ int red_i[32];
   __shared__ double red_d[32];
-  __shared__ float s_max[4];  // this CTA's raw maxima of the live / all values, any live / any value
+  __shared__ float s_max[5];  // this CTA's raw maxima of the live / all values, any live / any value, live minimum
   extern __shared__ float queue[];  // [kHistQueue] live raw values of a sparse chunk
   cg::cluster_group cl = cg::this_cluster();
   const int rank = static_cast<int>(cl.block_rank());
@@ -302,7 +317,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   if (pp->mode != kModeLarge) return;  // the whole cluster (one row)
   const RowWs W = row_ws(A, row);
   const double T = pp->temperature;
-  const float scale = bin_scale(T), width = bin_width_logit(T), invT = static_cast<float>(1.0 / T);
+  const float invT = static_cast<float>(1.0 / T);
   const float a2_hi = pp->a2_hi, a2_lo = pp->a2_lo;
   const float qmul = static_cast<float>(ldexp(1.0, q_bits(A.vocab)));
   const int64_t V = A.vocab;
@@ -326,7 +341,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   const bool one_pass_bits = n <= kHistSub;  // the live bits stay valid for phase 1
 
   // ---- phase 0: maxima, allowed count, non-finite values (and the queue) ----
-  float lmax = -INFINITY, rmax = -INFINITY;
+  float lmax = -INFINITY, rmax = -INFINITY, lmin = INFINITY;
   int nallow = 0, bad = 0, any_l = 0, any_v = 0;
   int qn = -1;  // queued values; -1: phase 1 reads the chunk again
   for (int s0 = 0; s0 < n; s0 += kHistSub) {
@@ -394,6 +409,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
             const float x = DT == GS_DTYPE_F32 ? __uint_as_float(w[i]) : ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]));
             const bool l = (lb[u] >> i) & 1u;
             lmax = fmaxf(lmax, l ? x : -INFINITY);
+            lmin = fminf(lmin, l ? x : INFINITY);
             if (RAW) {
               rmax = fmaxf(rmax, x);
               bad |= !(x <= lim);
@@ -411,7 +427,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
       const float x = load_logit(base, DT, i);
       any_l |= l;
       any_v = 1;
-      if (l) lmax = fmaxf(lmax, x);
+      if (l) {
+        lmax = fmaxf(lmax, x);
+        lmin = fminf(lmin, x);
+      }
       if (RAW) rmax = fmaxf(rmax, x);
       if (RAW || l) bad |= !(x <= lim);
     }
@@ -421,11 +440,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     for (int i = tid; i < qn; i += bs) {
       const float x = queue[i];
       lmax = fmaxf(lmax, x);
+      lmin = fminf(lmin, x);
       bad |= !(x <= lim);
     }
     any_l = qn > 0;
   }
   lmax = block_max_f(lmax, red_f);
+  lmin = -block_max_f(-lmin, red_f);
   if (RAW) rmax = block_max_f(rmax, red_f);
   nallow = block_sum_i(nallow, red_i);
   bad = __syncthreads_or(bad);
@@ -436,13 +457,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     s_max[1] = rmax;
     s_max[2] = static_cast<float>(any_l);
     s_max[3] = static_cast<float>(any_v);
+    s_max[4] = lmin;
   }
   for (int b = tid; b < kNB; b += bs) {
     cnt[b] = 0;
     qs[b] = 0;
   }
   cl.sync();
-  float Mraw = -INFINITY, Rraw = -INFINITY;
+  float Mraw = -INFINITY, Rraw = -INFINITY, Nraw = INFINITY;
   bool row_l = false, row_v = false;
 #pragma unroll
   for (int r = 0; r < kCluster; ++r) {
@@ -451,9 +473,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     Rraw = fmaxf(Rraw, pm[1]);
     row_l |= pm[2] != 0.0f;
     row_v |= pm[3] != 0.0f;
+    Nraw = fminf(Nraw, pm[4]);
   }
   const float Mx = cap != 0.0f ? (row_l ? softcap(Mraw, cap, inv_cap) : -INFINITY) : Mraw;
   const float Rm = cap != 0.0f ? (row_v ? softcap(Rraw, cap, inv_cap) : -INFINITY) : Rraw;
+  const float Mn = cap != 0.0f ? (row_l ? softcap(Nraw, cap, inv_cap) : INFINITY) : Nraw;
+  float scale, width;
+  bin_geometry(T, Mx, Mn, &scale, &width);
+  if (rank == 0 && tid == 0) {
+    W.hdr->bscale = scale;
+    W.hdr->bwidth = width;
+  }
 
   // ---- phase 1: histogram and sums ----
   // Capped values, two at once (packed f32x2 arithmetic).
@@ -764,7 +794,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
 
   // ---- binned masses relative to M: live values from the histogram, then the
   //      penalised entries (fixed point, so that their sums are order-independent) ----
-  const float Mx = mx, scale = bin_scale(T), width = bin_width_logit(T);
+  const float Mx = mx, scale = W.hdr->bscale, width = W.hdr->bwidth;
   const double qunit = ldexp(1.0, -q_bits(V));
   unsigned long long* pfix = reinterpret_cast<unsigned long long*>(un);  // (the hash table is done)
   uint32_t* pcnt = reinterpret_cast<uint32_t*>(pfix + kNB);
@@ -1032,7 +1062,7 @@ __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __gr
   const int64_t lo = static_cast<int64_t>(part) * kGatherIds;
   if (lo >= V) return;
   const int n = static_cast<int>(V - lo < kGatherIds ? V - lo : kGatherIds);
-  const float Mx = Hp->Mx, scale = bin_scale(pp->temperature), glo = Hp->gat_lo;
+  const float Mx = Hp->Mx, scale = Hp->bscale, glo = Hp->gat_lo;
   const int32_t state = A.mask_state ? A.mask_state[row] : -1;
   const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
   const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
@@ -1138,7 +1168,7 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
   const RowWs W = row_ws(A, row);
   const LargeRow H = *W.hdr;
   const double T = pp->temperature, M = H.M, total = H.total;
-  const float Mx = H.Mx, scale = bin_scale(T);
+  const float Mx = H.Mx, scale = H.bscale;
   const int64_t V = A.vocab;
   const int32_t state = A.mask_state ? A.mask_state[row] : -1;
   const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
