@@ -463,43 +463,50 @@ def config_leg(pkg, W, sampler, dev, name, rows, dtype=None, mask=True, history=
 
 def c5_sharded_leg(pkg, W, sampler, dev, rank, world, steps=200):
     """C5 in the vocabulary-sharded layout on every rank: rank g holds ids
-    [g·V/N, (g+1)·V/N) of the 8 rows; per step gs_shard_partials, one all-gather of the
-    records (NCCL) and gs_shard_merge.  Device time per step and of the all-gather alone
-    (CUDA events, slowest rank), and whether every rank's ids equal whole-row sampling."""
-    import numpy as np
+    [g·V/N, (g+1)·V/N) of the 8 rows; per step gs_shard_sample (the library's own NCCL
+    exchange: partials, ncclAllGather of the records, merge).  Device time per step and of
+    the torch all-gather of the same records alone (CUDA events, slowest rank), and whether
+    every rank's ids equal whole-row sampling."""
     import torch
     import torch.distributed as dist
     SH = importlib.import_module(PKG + ".sharding")
     wl = W.make("C5", device=dev)
     rows = wl.rows
-    vs = SH.VocabShardedSampler(sampler, VOCAB)
-    off, size = vs.plan.offset, vs.plan.size
+    uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(SH.NcclShardedSampler.unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    ns = SH.NcclShardedSampler(sampler, VOCAB, rank, world, bytes(uid.cpu().numpy().tobytes()), timeout_ms=30000)
+    off, size = ns.plan.offset, ns.plan.size
     local = wl.logits[:, off:off + size].contiguous()
     params = pkg.prepare_params(wl.params)
     stream = torch.cuda.current_stream(dev)
     rng = wl.rng_state(dev)
-    whole = sampler.sample(wl.logits, params, softcap=wl.softcap, rng_state=wl.rng_state(dev))
-    res = vs.sample(local, params, softcap=wl.softcap, rng_state=rng)
+    rng_w = wl.rng_state(dev)
+    whole = sampler.sample(wl.logits, params, softcap=wl.softcap, rng_state=rng_w)
+    res = ns.sample(local, params, softcap=wl.softcap, rng_state=rng)
     torch.cuda.synchronize()
-    same = bool(torch.equal(res.ids, whole.ids))
+    same = bool(torch.equal(res.ids, whole.ids)) and bool(torch.equal(rng, rng_w))
     ok = torch.tensor([1 if same else 0], dtype=torch.int32, device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    rec = sampler.shard_partials(local, params, vocab_offset=off, vocab_total=VOCAB, softcap=wl.softcap)
-    rec_bytes = rec.numel()
+    ns.timeout_ms = 0  # (asynchronous steps inside the timed loop)
     for _ in range(5):
-        vs.sample(local, params, softcap=wl.softcap, rng_state=rng)
-    dist.barrier()
+        ns.sample(local, params, softcap=wl.softcap, rng_state=rng)
     torch.cuda.synchronize()
+    dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
-        vs.sample(local, params, softcap=wl.softcap, rng_state=rng)
+        ns.sample(local, params, softcap=wl.softcap, rng_state=rng)
     e1.record(stream)
     torch.cuda.synchronize()
     step_s = e0.elapsed_time(e1) / 1e3 / steps
-    ga = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    rec = sampler.shard_partials(local, params, vocab_offset=off, vocab_total=VOCAB, softcap=wl.softcap)
+    rec_bytes = rec.numel()
     for _ in range(3):
         SH.exchange_records(rec)
+    torch.cuda.synchronize()
+    ga = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     ga[0].record(stream)
     for _ in range(steps):
         SH.exchange_records(rec)
@@ -509,12 +516,14 @@ def c5_sharded_leg(pkg, W, sampler, dev, rank, world, steps=200):
     t = torch.tensor([step_s, ag_s], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_s, ag_s = float(t[0]), float(t[1])
-    del np
+    ns.close()
     return {"workload": f"C5: B={rows}, V={VOCAB} split into {world} contiguous shards of {size} ids, Gumbel(0,2) "
                         "+ 30 planted ties, T 1.5, topK 1024, topP 0.99",
             "us_per_step": step_s * 1e6, "rows_per_s": rows / step_s, "allgather_us": ag_s * 1e6,
             "record_bytes_per_rank": rec_bytes, "nccl_ranks": world, "matches_whole_row_sampling": bool(ok.item()),
-            "timing": "CUDA events around steps of partials + NCCL all-gather + merge, slowest rank"}
+            "exchange": "gs_shard_sample (the library's own ncclAllGather; NCCL loaded at run time)",
+            "timing": "CUDA events around steps of partials + NCCL all-gather + merge, slowest rank; allgather_us: "
+                      "torch.distributed all-gather of the same records alone"}
 
 
 def lm_head_leg(pkg, sampler, stream):

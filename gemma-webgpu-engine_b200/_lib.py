@@ -52,7 +52,8 @@ EXPORTS = (
     "gs_profile_read", "gs_sample_noalloc", "gs_constraint_create", "gs_constraint_destroy",
     "gs_constraint_last_error", "gs_constraint_build_masks", "gs_lm_head_create", "gs_lm_head_destroy",
     "gs_lm_head_last_error", "gs_lm_head_logits", "gs_lm_head_sample", "gs_lm_head_check",
-    "gs_lm_head_fused_calls", "gs_build_reasoning_mask_rows",
+    "gs_lm_head_fused_calls", "gs_build_reasoning_mask_rows", "gs_nccl_unique_id", "gs_nccl_create",
+    "gs_nccl_destroy", "gs_nccl_last_error", "gs_shard_sample",
 )
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -190,12 +191,18 @@ def lib() -> ctypes.CDLL:
     L.gs_shard_partials.argtypes = [P, ctypes.POINTER(GsBatch), i64, i64, i32, P, P]
     L.gs_shard_merge.argtypes = [P, ctypes.POINTER(GsBatch), i32, P, ctypes.POINTER(GsOutputs), P]
     L.gs_sample_noalloc.argtypes = [ctypes.POINTER(GsBatch), ctypes.POINTER(GsOutputs), P]
+    L.gs_nccl_unique_id.argtypes = [P]
+    L.gs_nccl_create.argtypes = [ctypes.c_int, P, i32, i32, i32, ctypes.POINTER(P)]
+    L.gs_nccl_destroy.argtypes = [P]
+    L.gs_nccl_last_error.argtypes = [P]
+    L.gs_nccl_last_error.restype = ctypes.c_char_p
+    L.gs_shard_sample.argtypes = [P, P, ctypes.POINTER(GsBatch), i64, i64, ctypes.POINTER(GsOutputs), i32, P]
     L.gs_profile_enable.argtypes = [P, i32]
     L.gs_profile_read.argtypes = [P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
                                   ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64)]
     for name in EXPORTS:
         if name not in ("gs_last_error", "gs_shard_record_bytes", "gs_constraint_last_error", "gs_lm_head_last_error",
-                        "gs_lm_head_fused_calls"):
+                        "gs_lm_head_fused_calls", "gs_nccl_last_error"):
             getattr(L, name).restype = ctypes.c_int
     L.gs_lm_head_fused_calls.restype = i64
     _lib = L

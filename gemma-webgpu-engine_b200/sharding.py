@@ -9,7 +9,8 @@ these are the B200 deployment of the same call):
 * vocabulary-sharded (small batches, e.g. C5): every rank holds a slice of every row's
   logits; ``GpuSampler.shard_partials`` streams the slice into a fixed-size record per row,
   one all-gather exchanges the records, and ``GpuSampler.shard_merge`` samples from them,
-  identically on every rank.
+  identically on every rank.  ``NcclShardedSampler`` does the same step with the
+  library's own NCCL exchange (gs_shard_sample), for hosts without a framework collective.
 
 The partition rules and the exchange are plain host logic (tested with gloo on CPU);
 the device work is the library's.
@@ -123,3 +124,74 @@ class VocabShardedSampler:
                                         vocab_total=p.vocab_total, history_stride=hstride, mask_table=mask_table,
                                         mask_state=mask_state, rng_state=rng_state, uniforms=uniforms,
                                         logprob=logprob, candidates=candidates, stream=stream)
+
+
+class NcclShardedSampler:
+    """Vocabulary-sharded sampling with the library's own NCCL exchange (gs_nccl_create +
+    gs_shard_sample): the same result as ``VocabShardedSampler`` without a framework
+    collective, the form an addon without torch binds.  Every rank constructs it with the
+    same ``unique_id`` (made once by ``NcclShardedSampler.unique_id()`` and sent to the
+    others by any means).  A rank that never joins ends set-up or a step with
+    ``SamplerError`` (GS_ETIMEOUT) after ``timeout_ms``; the communicator is then aborted and
+    a new sampler is needed."""
+
+    def __init__(self, sampler, vocab_total: int, rank: int, world: int, unique_id: bytes, timeout_ms: int = 30000):
+        import ctypes
+        from . import _lib
+        from .sampling import SamplerError
+        self._L = _lib.lib()
+        self._lib = _lib
+        self.sampler = sampler
+        self.timeout_ms = int(timeout_ms)
+        off, size = vocab_shards(vocab_total, world)[rank]
+        self.plan = ShardPlan(rank, world, vocab_total, off, size)
+        if len(unique_id) != 128:
+            raise ValueError("the communicator id is 128 bytes")
+        idb = (ctypes.c_char * 128).from_buffer_copy(unique_id)
+        self._comm = ctypes.c_void_p()
+        st = self._L.gs_nccl_create(sampler.device, idb, world, rank, self.timeout_ms, ctypes.byref(self._comm))
+        if st != _lib.GS_OK:
+            raise SamplerError(st, (self._L.gs_nccl_last_error(None) or b"").decode())
+
+    @staticmethod
+    def unique_id() -> bytes:
+        import ctypes
+        from . import _lib
+        from .sampling import SamplerError
+        L = _lib.lib()
+        idb = (ctypes.c_char * 128)()
+        st = L.gs_nccl_unique_id(idb)
+        if st != _lib.GS_OK:
+            raise SamplerError(st, (L.gs_nccl_last_error(None) or b"").decode())
+        return bytes(idb)
+
+    def sample(self, local_logits, params, *, softcap: float = 0.0, history=None, history_len=None, mask_table=None,
+               mask_state=None, rng_state=None, uniforms=None, logprob: bool = False, candidates: int = 0,
+               stream=None):
+        """``local_logits`` [rows, plan.size] is this rank's slice; the other arguments are
+        the whole rows' (as ``VocabShardedSampler.sample``).  Asynchronous on ``stream``
+        unless ``timeout_ms`` > 0, when the call waits for the step (bounded)."""
+        import ctypes
+        import torch
+        from .sampling import SamplerError
+        p = self.plan
+        if local_logits.shape[1] != p.size:
+            raise ValueError(f"rank {p.rank} holds {p.size} ids, got {local_logits.shape[1]}")
+        s = self.sampler
+        b, keep = s.make_batch(local_logits, params, softcap=softcap, history=history, history_len=history_len,
+                               mask_table=mask_table, mask_state=mask_state, rng_state=rng_state, uniforms=uniforms)
+        out, o = s.make_outputs(local_logits.shape[0], local_logits.device, logprob, candidates)
+        if stream is None:
+            stream = torch.cuda.current_stream(local_logits.device).cuda_stream
+        st = self._L.gs_shard_sample(s.handle, self._comm, ctypes.byref(b), p.offset, p.vocab_total, ctypes.byref(o),
+                                     self.timeout_ms, ctypes.c_void_p(stream))
+        del keep
+        if st != self._lib.GS_OK:
+            raise SamplerError(st, (self._L.gs_nccl_last_error(self._comm) or b"").decode())
+        return out
+
+    def close(self):
+        if self._comm:
+            self._L.gs_nccl_destroy(self._comm)
+            import ctypes
+            self._comm = ctypes.c_void_p()

@@ -28,7 +28,7 @@ typedef enum gs_status {
                            ("Generation constraint reached a tokenization dead end",
                            src/runtime/gemma-session.ts:1324-1326) */
   GS_ECUDA = 3,         /* a CUDA runtime call failed */
-  GS_ENCCL = 4,         /* reserved for the vocabulary-sharded exchange */
+  GS_ENCCL = 4,         /* the vocabulary-sharded exchange failed (gs_nccl_last_error) */
   GS_ETIMEOUT = 5,      /* a bounded device wait ran out */
   GS_ENOMEM = 6,        /* device allocation failed */
   GS_EUNSUPPORTED = 7,  /* request outside the implemented envelope (see gs_last_error) */
@@ -351,6 +351,41 @@ gs_status gs_shard_partials(gs_ctx* ctx, const gs_batch* shard, int64_t vocab_of
                             int32_t want_logprob, void* records, void* stream);
 gs_status gs_shard_merge(gs_ctx* ctx, const gs_batch* full, int32_t shards, const void* gathered_records,
                          const gs_outputs* out, void* stream);
+
+/*
+ * The same vocabulary-sharded step with the exchange done here, over NCCL (no reference
+ * counterpart: the reference samples on one device; this is what an addon without a host
+ * framework binds).  NCCL is loaded at run time: the copy the process has already loaded,
+ * else libnccl.so.2, or the library named by the environment variable GS_NCCL_LIBRARY.
+ *   gs_nccl_unique_id   one rank makes the communicator's id (host); the caller sends its
+ *                       128 bytes to the other ranks by any means;
+ *   gs_nccl_create      every rank joins with the same id, its rank and the device it
+ *                       samples on (< 0: the calling thread's current device); the
+ *                       communicator is non-blocking and set-up waits at most timeout_ms
+ *                       (<= 0: no limit) for the other ranks, else GS_ETIMEOUT;
+ *   gs_shard_sample     gs_shard_partials of the local shard into communicator-owned
+ *                       records, one ncclAllGather of them, gs_shard_merge, all on
+ *                       `stream` (arguments as for gs_shard_partials; every rank passes
+ *                       the same params, states and history_stride and gets the same
+ *                       ids).  The record buffers grow on the first call of a larger
+ *                       batch (allocates).  With timeout_ms > 0 the call also waits
+ *                       (host) until the step has completed on the stream, at most
+ *                       timeout_ms; a rank that never joins the exchange then ends it
+ *                       with GS_ETIMEOUT instead of a wait without end.
+ * After GS_ETIMEOUT or GS_ENCCL the communicator has been aborted: destroy it and create
+ * a new one.  gs_nccl_last_error(NULL) gives this thread's last message.
+ */
+typedef struct gs_nccl_id {
+  char internal[128];
+} gs_nccl_id;
+typedef struct gs_nccl gs_nccl;
+gs_status gs_nccl_unique_id(gs_nccl_id* id);
+gs_status gs_nccl_create(int device, const gs_nccl_id* id, int32_t nranks, int32_t rank, int32_t timeout_ms,
+                         gs_nccl** out);
+gs_status gs_nccl_destroy(gs_nccl* comm);
+const char* gs_nccl_last_error(const gs_nccl* comm);
+gs_status gs_shard_sample(gs_ctx* ctx, gs_nccl* comm, const gs_batch* shard, int64_t vocab_offset,
+                          int64_t vocab_total, const gs_outputs* out, int32_t timeout_ms, void* stream);
 
 #ifdef __cplusplus
 }
