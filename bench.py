@@ -283,7 +283,10 @@ def run_ours(args, rank, world, local):
         result["e2e"] = e2e_leg(args, pkg, sampler, dev, logits, hist, hlen, table, mstate, seeds, params, per,
                                 world)
     if world > 1 and not args.no_extras:
-        # every rank takes part: one all-gather of shard records per step
+        # every rank takes part: C4 as written (its 4096 rows split over the GPUs), then C5
+        # with one all-gather of shard records per step
+        result["c4_strong_split"] = strong_split_leg(pkg, sampler, dev, logits, hist, hlen, table, mstate, params,
+                                                     world)
         result["c5_vocab_sharded"] = c5_sharded_leg(pkg, W, sampler, dev, rank, world)
     if rank == 0 and not args.no_extras:
         del logits
@@ -459,6 +462,46 @@ def config_leg(pkg, W, sampler, dev, name, rows, dtype=None, mask=True, history=
     del xs, wl
     torch.cuda.empty_cache()
     return res
+
+
+def strong_split_leg(pkg, sampler, dev, logits, hist, hlen, table, mstate, params, world, steps=300):
+    """C4 as BASELINE states it: one batch of 4096 rows split evenly over the N GPUs
+    (4096/N rows per rank, each rank's first rows of its own batch), rows/s of the whole
+    batch over the slowest rank's device time, and the kernel split of rank 0."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    L = pkg._lib
+    per = GLOBAL_BATCH // world
+    x, h, hl, ms = logits[:per], hist[:per].contiguous(), hlen[:per].contiguous(), mstate[:per].contiguous()
+    rng = torch.zeros(per, dtype=torch.float64, device=dev) + pkg.SeededRandom(3000).state
+    stream = torch.cuda.current_stream(dev)
+    out = None
+    for _ in range(10):
+        out = sampler.sample(x, params, softcap=30.0, history=h, history_len=hl, mask_table=table, mask_state=ms,
+                             rng_state=rng, stream=stream.cuda_stream, out=out)
+    torch.cuda.synchronize()
+    dist.barrier()
+    L.lib().gs_profile_enable(sampler.handle, 1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        out = sampler.sample(x, params, softcap=30.0, history=h, history_len=hl, mask_table=table, mask_state=ms,
+                             rng_state=rng, stream=stream.cuda_stream, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    s_ms, s_n, m_ms, m_n = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double(), ctypes.c_int64()
+    L.lib().gs_profile_read(sampler.handle, ctypes.byref(s_ms), ctypes.byref(s_n), ctypes.byref(m_ms),
+                            ctypes.byref(m_n))
+    L.lib().gs_profile_enable(sampler.handle, 0)
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    return {"workload": f"C4: one batch of {GLOBAL_BATCH} rows split evenly, {per} rows per GPU", "n_gpus": world,
+            "value": GLOBAL_BATCH * steps / dt, "unit": UNIT, "ms_per_step": dt / steps * 1e3, "steps": steps,
+            "scaling": "strong", "rank0_kernel_split_us": {"streaming_pass": s_ms.value / max(1, s_n.value) * 1e3,
+                                                           "merge": m_ms.value / max(1, m_n.value) * 1e3},
+            "timing": "CUDA events, slowest rank; the driver's 1-GPU line is the N = 1 point"}
 
 
 def c5_sharded_leg(pkg, W, sampler, dev, rank, world, steps=200):
