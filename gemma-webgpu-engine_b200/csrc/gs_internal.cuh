@@ -113,6 +113,7 @@ struct FinalizeArgs {
   unsigned char* lws;     // [rows] blocks of lrow_bytes
   int64_t lrow_bytes;
   int32_t lslots;         // penalised-entry slots per row (the history stride)
+  int32_t lmoments;       // some histogram-path row has typical-p (its bins' first moments)
 };
 
 // Per-row record of one vocabulary shard (gs_shard_partials writes, gs_shard_merge reads):

@@ -61,6 +61,9 @@ constexpr int kGCap = 8192;            // entries of the selected bins per row
 constexpr int kWarpSortMax = 1024;     // larger bins are sorted by the whole CTA
 constexpr double kBoundary = 1e-6;
 constexpr double kSelMargin = 4e-6;    // relative slack when bins are picked from binned masses
+constexpr double kTypMargin = 1e-5;    // relative slack of the typical-p bounds (binned moments)
+constexpr int kMaxRanges = 12;         // bin ranges the select kernel marks per row
+constexpr int kSortSmem = 2048;        // typical-p: annulus entries sorted in shared memory
 constexpr float kMaxDelta = 0.0105f;   // bin width (40/4096 key units) plus slack
 constexpr size_t kSelUnion = (static_cast<size_t>(kNB + 1) * 12 + 15) / 16 * 16;  // select: start of its union
 static_assert(kNB / kCluster == kHistThreads, "one reduced bin per thread and cluster rank");
@@ -80,29 +83,52 @@ struct LargeRow {
   float Mx;          // maximum over live values (allowed and not penalised)
   float bscale;      // bins per logit unit below Mx (the histogram kernel sets the row's bins)
   float bwidth;      // logit units per bin
+  float Mn;          // minimum over live values
   float raw_m;
   double raw_s;
   double M;          // maximum key (logit/T) over live values and penalised entries
   double total;      // full-vocabulary normaliser relative to M
   double uniform;    // the draw's uniform
   double rng_next;   // the PRNG state after the draw
+  // typical-p (select): bounds of the surprise centre H - ln(total) (key units) and of
+  // the surprise level at the cut, and the bins [aL0, aL1], [aR0, aR1] (-1: none) that
+  // can hold the cut's two ends
+  double cc_lo, cc_hi, s_lo, s_hi;
+  int32_t typ;  // kTypNone, kTypCut, kTypAll
+  int32_t aL0, aL1, aR0, aR1;
+  int32_t iB0, iB1;  // bins between the two ends (every entry's surprise below s_lo), -1: none
+  // typical pre-pass (resolve kernel, phase 0): the run [t_r0, t_lend), the running
+  // probability before it, and the bins of its second gather (W.sel2)
+  int64_t t_r0, t_lend;
+  double t_c0;
+  int32_t g_need2;  // entries of the second gather's bins
+  float gat_lo2;    // as gat_lo, for the second gather
 };
+constexpr int kTypNone = 0;  // no typical-p cut (or one equal to a top-p cut)
+constexpr int kTypCut = 1;   // the cut lies in the annulus bins
+constexpr int kTypAll = 2;   // the typical set is every candidate
 static_assert(sizeof(LargeRow) <= 256, "header fits its slot");
 
-// Per-row workspace: header | the histogram CTAs' row statistics | selected-bin bitmap |
-// count prefix | mass prefix | penalised entries | gathered entries.
+// Per-row workspace: header | the histogram CTAs' row statistics | selected-bin bitmaps
+// (first and second gather) | count prefix | mass prefix | first-moment prefix | penalised
+// entries | gathered entries.
 constexpr size_t kOffStats = 256;
 constexpr size_t kOffSel = kOffStats + kCluster * sizeof(UnitStat);
-constexpr size_t kOffCpre = kOffSel + kNB / 8;
+constexpr size_t kOffSel2 = kOffSel + kNB / 8;
+constexpr size_t kOffCpre = kOffSel2 + kNB / 8;
 constexpr size_t kOffPpre = (kOffCpre + (kNB + 1) * 4 + 15) / 16 * 16;
-constexpr size_t kOffPen = (kOffPpre + (kNB + 1) * 8 + 15) / 16 * 16;
+constexpr size_t kOffM1 = (kOffPpre + (kNB + 1) * 8 + 15) / 16 * 16;
+constexpr size_t kOffPen = (kOffM1 + (kNB + 1) * 8 + 15) / 16 * 16;
 
 struct RowWs {
   LargeRow* hdr;
   UnitStat* hstat; // [kCluster] live maximum / sum, raw maximum / sum, allowed count, flags
   uint32_t* sel;   // [kNB / 32]
+  uint32_t* sel2;  // [kNB / 32] bins of the second gather (typical-p rows)
   uint32_t* cpre;  // [kNB + 1] entries before bin b (the hist kernel leaves counts here)
   double* ppre;    // [kNB + 1] probability before bin b (the hist kernel leaves q sums here)
+  double* m1pre;   // [kNB + 1] sum of e^(key - M)·(M - key) before bin b, typical-p rows (the
+                   // hist kernel leaves its fixed-point within-bin sums here)
   Ent* pen;        // [n_slots] penalised entries (id 0xffffffff: empty slot)
   uint2* gath;     // [kGCap] {float bits of the soft-capped logit, id}
 };
@@ -113,8 +139,10 @@ __device__ __forceinline__ RowWs row_ws(const FinalizeArgs& A, int row) {
   w.hdr = reinterpret_cast<LargeRow*>(b);
   w.hstat = reinterpret_cast<UnitStat*>(b + kOffStats);
   w.sel = reinterpret_cast<uint32_t*>(b + kOffSel);
+  w.sel2 = reinterpret_cast<uint32_t*>(b + kOffSel2);
   w.cpre = reinterpret_cast<uint32_t*>(b + kOffCpre);
   w.ppre = reinterpret_cast<double*>(b + kOffPpre);
+  w.m1pre = reinterpret_cast<double*>(b + kOffM1);
   w.pen = reinterpret_cast<Ent*>(b + kOffPen);
   w.gath = reinterpret_cast<uint2*>(b + kOffPen + static_cast<size_t>(A.lslots) * sizeof(Ent));
   return w;
@@ -268,7 +296,32 @@ __device__ void seg_sort(Ent* e, int n, int t, int nt) {
   }
 }
 
+// Ascending block-wide sort of n2 (a power of two) 64-bit keys, in shared or global
+// memory (the block's own rows: __syncthreads orders both).
+__device__ void bitonic_sort_u64(unsigned long long* v, int n2) {
+  for (int k = 2; k <= n2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long a = v[i], b = v[ixj];
+          if ((i & k) == 0 ? a > b : a < b) {
+            v[i] = b;
+            v[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
 }  // namespace
+
+// resolve: entries | exact probabilities | bin starts | typical-p sort keys
+static size_t large_resolve_smem_bytes() {
+  return static_cast<size_t>(kGCap) * (sizeof(Ent) + 8) + (kNB + 4) * 4 + static_cast<size_t>(kSortSmem) * 8;
+}
 
 size_t large_row_bytes(int64_t slots) {
   const size_t gath = kOffPen + static_cast<size_t>(slots) * sizeof(Ent);
@@ -279,7 +332,7 @@ size_t large_select_smem_bytes(int64_t history_stride) {
   int64_t h2 = 64;
   while (h2 < 2 * history_stride) h2 <<= 1;
   const size_t hash = static_cast<size_t>(h2) * 12;
-  const size_t pen_bins = static_cast<size_t>(kNB) * 12;  // fixed-point masses and counts of penalised entries
+  const size_t pen_bins = static_cast<size_t>(kNB) * 20;  // fixed-point masses, counts and first moments of penalised entries
   return kSelUnion + (hash > pen_bins ? hash : pen_bins);
 }
 
@@ -298,7 +351,10 @@ size_t large_select_smem_bytes(int64_t history_stride) {
 // workspace (counts over the count prefix array, q sums over the mass prefix array; the
 // select kernel rewrites both with the prefix sums), and each CTA writes its statistics.
 // RAW: the log-probability is wanted (phase 0 visits every id, and there is no queue).
-template <int DT, bool RAW>
+// MOM: some row of the batch has typical-p; those rows also sum, per bin, the first moment
+// r = round(dl·e^-dl·2^qbits) of their values (dl: the value's key distance below its
+// bin's top), kept in a second dynamic shared-memory array after the queue.
+template <int DT, bool RAW, bool MOM>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads, kHistMinBlocks)
     large_hist_kernel(const __grid_constant__ FinalizeArgs A) {
   __shared__ uint32_t cnt[kNB];
@@ -318,6 +374,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   const RowWs W = row_ws(A, row);
   const double T = pp->temperature;
   const float invT = static_cast<float>(1.0 / T);
+  uint32_t* rsum_bins = reinterpret_cast<uint32_t*>(queue + kHistQueue);  // [kNB] (MOM launches)
+  const bool mom = MOM && pp->typical_p < 1;  // (the whole cluster: one row)
   const float a2_hi = pp->a2_hi, a2_lo = pp->a2_lo;
   const float qmul = static_cast<float>(ldexp(1.0, q_bits(A.vocab)));
   const int64_t V = A.vocab;
@@ -462,6 +520,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   for (int b = tid; b < kNB; b += bs) {
     cnt[b] = 0;
     qs[b] = 0;
+    if (mom) rsum_bins[b] = 0;
   }
   cl.sync();
   float Mraw = -INFINITY, Rraw = -INFINITY, Nraw = INFINITY;
@@ -483,6 +542,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   if (rank == 0 && tid == 0) {
     W.hdr->bscale = scale;
     W.hdr->bwidth = width;
+    W.hdr->Mn = Mn;
   }
 
   // ---- phase 1: histogram and sums ----
@@ -527,6 +587,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     if (l1) {
       atomicAdd(&cnt[b1], 1u);
       if (q1) atomicAdd(&qs[b1], q1);
+    }
+    if (mom) {
+      // dl·e^-dl = dl - dl·(1 - e^-dl)
+      const float2 rm = __fmul2_rn(__ffma2_rn(make_float2(-dl.x, -dl.y), __fmul2_rn(dl, h), dl), make_float2(qmul, qmul));
+      const uint32_t r0 = b0 < kNB - 1 ? __float2uint_rn(rm.x) : 0u;
+      const uint32_t r1 = b1 < kNB - 1 ? __float2uint_rn(rm.y) : 0u;
+      if (l0 && r0) atomicAdd(&rsum_bins[b0], r0);
+      if (l1 && r1) atomicAdd(&rsum_bins[b1], r1);
     }
   };
   // (a thread adds at most 64 terms of at most 1 in float per sub-chunk, as the streaming
@@ -620,8 +688,48 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     }
     W.cpre[b] = c;
     reinterpret_cast<unsigned long long*>(W.ppre)[b] = q;
+    if (mom) {
+      unsigned long long r1 = 0;
+#pragma unroll
+      for (int r = 0; r < kCluster; ++r) r1 += cl.map_shared_rank(rsum_bins, r)[b];
+      reinterpret_cast<unsigned long long*>(W.m1pre)[b] = r1;
+    }
   }
   cl.sync();  // every CTA keeps its shared memory until its peers have read it
+}
+
+// Exclusive prefix sum, in place, of a[0, kNB) over kSelectThreads threads (four
+// consecutive bins per thread, a fixed order); a[kNB] gets the total.
+__device__ void bins_excl_scan_d(double* a, double* red) {
+  constexpr int kPer = kNB / kSelectThreads;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  double m[kPer];
+  double tm = 0.0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    m[i] = a[tid * kPer + i];
+    tm = __dadd_rn(tm, m[i]);
+  }
+  double im = tm;
+  for (int o = 1; o < 32; o <<= 1) {
+    const double u = __shfl_up_sync(kFullMask, im, o);
+    if (lane >= o) im = __dadd_rn(u, im);
+  }
+  if (lane == 31) red[warp] = im;
+  __syncthreads();
+  double bm = 0.0;
+  for (int w = 0; w < warp; ++w) bm = __dadd_rn(bm, red[w]);
+  double lm = __shfl_up_sync(kFullMask, im, 1);
+  if (lane == 0) lm = 0.0;
+  bm = __dadd_rn(bm, lm);
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    a[tid * kPer + i] = bm;
+    bm = __dadd_rn(bm, m[i]);
+  }
+  if (tid == kSelectThreads - 1) a[kNB] = bm;
+  __syncthreads();
 }
 
 // ============================================================================ select
@@ -637,8 +745,8 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   __shared__ float red_f[32];
   __shared__ int red_i[32];
   __shared__ unsigned s_flags;
-  __shared__ int s_rng[2][8];
-  __shared__ int s_nr, s_cb;
+  __shared__ int s_rng[2][kMaxRanges];
+  __shared__ int s_nr, s_cb0, s_cb;
   const int row = blockIdx.x, tid = threadIdx.x, bs = blockDim.x;
   const int lane = tid & 31, warp = tid >> 5;
   const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
@@ -717,7 +825,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
 
   // ---- penalised entries: slot j holds the id first seen at history position j ----
   const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
-  double pmax = -INFINITY;
+  double pmax = -INFINITY, pmin = INFINITY;
   for (int64_t j = tid; j < hl; j += bs) {
     Ent e{-INFINITY, 0xffffffffu, 0u};
     const int32_t v = hrow[j];
@@ -735,11 +843,13 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
         // kind holds the float32 rounding of the penalised logit, used only for binning
         e = Ent{__ddiv_rn(xp, T), static_cast<uint32_t>(v), __float_as_uint(static_cast<float>(xp))};
         pmax = fmax(pmax, e.key);
+        pmin = fmin(pmin, e.key);
       }
     }
     W.pen[j] = e;
   }
   pmax = block_max_d(pmax, red_d);
+  pmin = -block_max_d(-pmin, red_d);
   const double mxk = mx > -INFINITY ? __ddiv_rn(static_cast<double>(mx), T) : -INFINITY;
   const double M = fmax(mxk, pmax);
 
@@ -761,7 +871,6 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
     unsigned f = s_flags;
     if (has_mask && na == 0) f |= GS_FLAG_ERR_DEADEND;
     if (!(M > -INFINITY)) f |= GS_FLAG_ERR_NONFINITE;
-    if (pp->typical_p < 1) f |= GS_FLAG_ERR_UNSUPPORTED;  // typical-p over > 1024 candidates
     double u = 0.0, st_next = 0.0;
     if (!(f & GS_FLAG_ERRORS)) {
       if (A.uniforms) {
@@ -780,6 +889,8 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
     H->g_need = 0;
     H->mp_lo = -1;
     H->mp_hi = -1;
+    H->typ = kTypNone;
+    H->g_need2 = 0;
     H->Mx = mx;
     H->raw_m = rm;
     H->raw_s = rs;
@@ -797,19 +908,28 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   const float Mx = mx, scale = W.hdr->bscale, width = W.hdr->bwidth;
   const double qunit = ldexp(1.0, -q_bits(V));
   unsigned long long* pfix = reinterpret_cast<unsigned long long*>(un);  // (the hash table is done)
-  uint32_t* pcnt = reinterpret_cast<uint32_t*>(pfix + kNB);
+  unsigned long long* pm1 = pfix + kNB;                                // penalised first moments
+  uint32_t* pcnt = reinterpret_cast<uint32_t*>(pm1 + kNB);
+  const bool typ = pp->typical_p < 1;
   for (int b = tid; b < kNB; b += bs) {
     const uint32_t c = W.cpre[b];
     const unsigned long long q = reinterpret_cast<const unsigned long long*>(W.ppre)[b];
-    double m = 0.0;
+    double m = 0.0, m1v = 0.0;
     if (c && b < kNB - 1) {
       const double top = __dsub_rn(
           __ddiv_rn(__dsub_rn(static_cast<double>(Mx), static_cast<double>(b) * static_cast<double>(width)), T), M);
-      m = __dmul_rn(exp(top), __dsub_rn(static_cast<double>(c), static_cast<double>(q) * qunit));
+      const double et = exp(top), se = __dsub_rn(static_cast<double>(c), static_cast<double>(q) * qunit);
+      m = __dmul_rn(et, se);
+      // first moment, sum of e^(key - M)·(M - key) = e^top·((-top)·sum e^-dl + sum dl·e^-dl)
+      if (typ)
+        m1v = __dmul_rn(et, __dadd_rn(__dmul_rn(-top, se),
+                                      static_cast<double>(reinterpret_cast<const unsigned long long*>(W.m1pre)[b]) * qunit));
     }
+    if (typ) W.m1pre[b] = m1v;  // (the same thread read the histogram's sum)
     cnt[b] = c;
     md[b] = m;
     pfix[b] = 0;
+    pm1[b] = 0;
     pcnt[b] = 0;
   }
   __syncthreads();
@@ -818,7 +938,9 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
     if (e.id == 0xffffffffu || !(e.key > -INFINITY)) continue;
     const int b = bin_of(__uint_as_float(e.kind), Mx, scale);
     atomicAdd(&pcnt[b], 1u);
-    atomicAdd(&pfix[b], static_cast<unsigned long long>(__dmul_rn(exp(__dsub_rn(e.key, M)), 17592186044416.0) + 0.5));
+    const double ex = exp(__dsub_rn(e.key, M));
+    atomicAdd(&pfix[b], static_cast<unsigned long long>(__dmul_rn(ex, 17592186044416.0) + 0.5));
+    if (typ) atomicAdd(&pm1[b], static_cast<unsigned long long>(__dmul_rn(__dmul_rn(ex, __dsub_rn(M, e.key)), 17592186044416.0) + 0.5));
   }
   __syncthreads();
   // exclusive prefix over the bins, 4 consecutive bins per thread (fixed order)
@@ -884,6 +1006,15 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
     W.cpre[b] = cnt[b];
     W.ppre[b] = __ddiv_rn(md[b], total);
   }
+  double* m1 = reinterpret_cast<double*>(pfix);  // (pfix was read by the mass prefix)
+  if (typ) {
+    // first moments per bin: the live values' (above) and the penalised entries' (fixed
+    // point); their prefix over the bins into W.m1pre
+    for (int b = tid; b < kNB; b += bs) m1[b] = __dadd_rn(W.m1pre[b], static_cast<double>(pm1[b]) * 5.684341886080802e-14);
+    __syncthreads();
+    bins_excl_scan_d(m1, red_d);
+    for (int b = tid; b <= kNB; b += bs) W.m1pre[b] = m1[b];
+  }
 
   // ---- bins that can hold a crossing (thread 0) ----
   // Bins that must be gathered: the min-p threshold's neighbourhood, the bin where the
@@ -912,12 +1043,13 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
       return l;
     };
     const int64_t n_fin = cnt[kNB];
+    unsigned xflags = 0;
     int nr = 0;
     int64_t used = 0;
     auto rc = [&](int a, int b) -> int64_t { return a <= b ? static_cast<int64_t>(cnt[b + 1]) - cnt[a] : 0; };
     auto fits = [&](int a, int b) { return used + rc(a, b) <= kGCap; };
     auto add = [&](int a, int b) {
-      if (nr < 8 && a <= b) {
+      if (nr < kMaxRanges && a <= b) {
         s_rng[0][nr] = a;
         s_rng[1][nr] = b;
         ++nr;
@@ -939,11 +1071,126 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
       if (L1_lo > cnt[mp_lo]) L1_lo = cnt[mp_lo];
       if (L1_hi > cnt[mp_hi + 1]) L1_hi = cnt[mp_hi + 1];
     }
+    // typical-p: the reference's entropy is NaN when a candidate has probability 0 (an id
+    // whose key is -inf among [0, L1)); its surprise sort then keeps the order and the
+    // typical cut is a running-sum cut like top-p, so the two merge into one threshold
+    int typ_mode = kTypNone;
+    double tpe = pp->top_p;
+    if (typ && n_fin > 0) {
+      if (!(pp->min_p > 0) && klim > n_fin) {
+        tpe = fmin(tpe, pp->typical_p);
+      } else if (fmin(static_cast<double>(W.hdr->Mn) / T, pmin) - M < -700.0 &&
+                 bin_of_rank((L1_hi < n_fin ? L1_hi : n_fin) - 1) == kNB - 1) {
+        xflags |= GS_FLAG_ERR_UNSUPPORTED;  // a candidate's probability may underflow to 0
+      } else {
+        typ_mode = kTypCut;
+      }
+    }
+    int cb0 = 0, cb = -1;
+    if (typ_mode == kTypCut) {
+      // ---- typical-p (sampling.ts:49-55) over the candidates [0, L1) ----
+      // With p = e^(key - M)/total, -ln p = delta + ln total (delta = M - key), so the
+      // surprise |-ln p - H| is |delta - cc| with cc = H - ln total = sum_C p·delta -
+      // ln total·(1 - P_C): a run of consecutive ranks around the rank where delta
+      // crosses cc.  From the binned masses and moments: bounds [c0, c1] of cc, bounds
+      // [s_lo, s_hi] of the surprise level where the running sum (in surprise order)
+      // reaches typicalP, and the bins that can hold the run's two ends (gathered now).
+      const double lnZ = log(total);
+      auto cc_at = [&](int b) {  // cc for the candidates before bin b
+        return __dsub_rn(__ddiv_rn(m1[b], total), __dmul_rn(lnZ, __dsub_rn(P(kNB), P(b))));
+      };
+      const int bl = L1_lo >= n_fin ? kNB : bin_of_rank(L1_lo);          // every bin before bl is in C
+      const int bh = L1_hi >= n_fin ? last_bin : bin_of_rank(L1_hi - 1);  // no bin after bh is
+      double c0 = cc_at(bl), c1 = cc_at(bh + 1);
+      c0 -= kTypMargin * (1.0 + fabs(c0));
+      c1 += kTypMargin * (1.0 + fabs(c1));
+      const double wk = 1.0 / (static_cast<double>(scale) * T);          // key units per bin
+      const double offK = __dsub_rn(M, __ddiv_rn(static_cast<double>(Mx), T));  // delta at bin 0's top
+      // bin of key distance x; an entry of bin b has delta in [offK + (b-1)·wk, offK + (b+2)·wk)
+      // (one bin of slack for the float binning; bin 0 from delta 0, the deepest bin unbounded)
+      auto dfl = [&](double x) {
+        return static_cast<int>(fmin(fmax(floor((x - offK) / wk), -8.0), static_cast<double>(kNB + 8)));
+      };
+      auto fullmass = [&](double s) {  // bins certainly in C with every delta in (c1 - s, c0 + s)
+        const double lo = c1 - s, hi = c0 + s;
+        if (!(hi > lo)) return 0.0;
+        const int a = lo < 0 ? 0 : max(1, dfl(lo) + 2);
+        const int b = min(min(dfl(hi) - 2, kNB - 2), bl - 1);
+        return b >= a ? P(b + 1) - P(a) : 0.0;
+      };
+      auto touchmass = [&](double s) {  // bins possibly in C that can hold a delta in [c0 - s, c1 + s]
+        const int a = max(0, dfl(c0 - s) - 2);
+        const int b = min(min(dfl(c1 + s) + 2, kNB - 1), bh);
+        return b >= a ? P(b + 1) - P(a) : 0.0;
+      };
+      const double tq = pp->typical_p;
+      if (P(bh + 1) < tq * (1.0 - kTypMargin)) {
+        typ_mode = kTypAll;  // the running sum cannot reach typicalP: every candidate stays
+      } else {
+        const double smax = fmax(c1, offK + (bh + 2) * wk - c0) + 4 * wk;
+        double s_hi = smax, s_lo = 0.0;
+        if (fullmass(smax) >= tq * (1.0 + kTypMargin)) {
+          double a = 0.0, b = smax;
+          for (int it = 0; it < 48; ++it) {
+            const double m = 0.5 * (a + b);
+            if (fullmass(m) >= tq * (1.0 + kTypMargin)) b = m;
+            else a = m;
+          }
+          s_hi = b;
+        }
+        if (touchmass(0.0) < tq * (1.0 - kTypMargin)) {
+          double a = 0.0, b = s_hi;
+          for (int it = 0; it < 48; ++it) {
+            const double m = 0.5 * (a + b);
+            if (touchmass(m) < tq * (1.0 - kTypMargin)) a = m;
+            else b = m;
+          }
+          s_lo = a;
+        }
+        // the run's ends: deltas in [c0 - s_hi, c1 - s_lo] (left) and [c0 + s_lo, c1 + s_hi]
+        // (right); every entry between them has surprise < s_lo
+        int aL0 = -1, aL1 = -1, aR0 = -1, aR1 = -1, iB0 = -1, iB1 = -1;
+        if (c1 - s_lo >= 0) {
+          aL0 = c0 - s_hi < 0 ? 0 : max(0, dfl(c0 - s_hi) - 1);
+          aL1 = min(bh, max(0, dfl(c1 - s_lo) + 1));
+          if (aL0 > aL1) aL0 = aL1 = -1;
+        }
+        aR0 = max(0, dfl(c0 + s_lo) - 1);
+        aR1 = min(bh, dfl(c1 + s_hi) + 1);
+        if (aR0 > aR1) aR0 = aR1 = -1;
+        if (aL0 >= 0 && aR0 >= 0 && aR0 <= aL1 + 1) {  // the two ends share bins
+          aL1 = max(aL1, aR1);
+          aR0 = aR1 = -1;
+        } else {
+          iB0 = aL0 >= 0 ? aL1 + 1 : 0;
+          iB1 = aR0 >= 0 ? aR0 - 1 : bh;
+          if (iB0 > iB1) iB0 = iB1 = -1;
+        }
+        if (aL0 < 0 && aR0 < 0) aR0 = aR1 = -1;
+        add(aL0, aL1);
+        add(aR0, aR1);
+        if (klim < n_fin && klim <= L1_hi) add(bin_of_rank(klim - 1), bin_of_rank(klim));  // C's exact end
+        // (the bins of the top-p crossing, the draw and the candidate list follow once the
+        // run is exact: the typical pre-pass of the resolve kernel and a second gather)
+        LargeRow* Hw = W.hdr;
+        Hw->cc_lo = c0;
+        Hw->cc_hi = c1;
+        Hw->s_lo = s_lo;
+        Hw->s_hi = s_hi;
+        Hw->aL0 = aL0;
+        Hw->aL1 = aL1;
+        Hw->aR0 = aR0;
+        Hw->aR1 = aR1;
+        Hw->iB0 = iB0;
+        Hw->iB1 = iB1;
+      }
+    }
+    if (typ_mode != kTypCut) {
     double ct_lo = INFINITY, ct_hi = -INFINITY;
     bool tp_sure = false;
     int tp_hi = -1;
-    if (pp->top_p < 1 && n_fin > 0) {
-      const double t = pp->top_p;
+    if (tpe < 1 && n_fin > 0) {
+      const double t = tpe;
       const int b0 = bstart(t);
       if (b0 < kNB && cnt[b0] < L1_hi) {
         tp_hi = b0;
@@ -986,7 +1233,6 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
       if (m1 > e1 && fits(e1 + 1, m1)) add(e1 + 1, m1);
     }
     // head of the candidate list (kept when it fits beside the bins above)
-    int cb = -1;
     if (A.cand_ids && A.cand_cap > 0 && n_fin > 0) {
       int64_t l_hi = L1_hi;
       if (tp_hi >= 0 && static_cast<int64_t>(cnt[tp_hi + 1]) > l_hi) l_hi = cnt[tp_hi + 1];
@@ -996,8 +1242,15 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
       if (m > l_hi) m = l_hi;
       if (m > 0) cb = bin_of_rank(m - 1);
     }
+    }
+    W.hdr->typ = typ_mode;
     s_nr = nr;
+    s_cb0 = cb0;
     s_cb = cb;
+    if (xflags) {
+      s_flags |= xflags;
+      W.hdr->flags = s_flags;
+    }
     W.hdr->mp_lo = mp_lo;
     W.hdr->mp_hi = mp_hi;
     W.hdr->n_fin = static_cast<int32_t>(n_fin);
@@ -1019,8 +1272,9 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
       }
       if (with_cand && s_cb >= 0)
         for (int i = 0; i < 32; ++i)
-          if (w * 32 + i <= s_cb) m |= 1u << i;
+          if (w * 32 + i >= s_cb0 && w * 32 + i <= s_cb) m |= 1u << i;
       W.sel[w] = m;
+      W.sel2[w] = 0u;
       for (int i = 0; i < 32; ++i)
         if ((m >> i) & 1u) cntsel += static_cast<int>(cnt[w * 32 + i + 1] - cnt[w * 32 + i]);
     }
@@ -1045,8 +1299,10 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
 }
 
 // ============================================================================ gather
+// second: the typical pre-pass's bins (W.sel2), appended after the first gather's entries.
 template <int DT>
-__global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __grid_constant__ FinalizeArgs A, int parts) {
+__global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __grid_constant__ FinalizeArgs A, int parts,
+                                                                      int second) {
   constexpr int kParkVals = DT == GS_DTYPE_F32 ? 16 : 32;  // values a thread holds per step
   __shared__ uint32_t sel[kNB / 32];
   __shared__ uint32_t live[kGatherIds / 32];
@@ -1057,12 +1313,12 @@ __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __gr
   if (pp->mode != kModeLarge) return;
   const RowWs W = row_ws(A, row);
   LargeRow* Hp = W.hdr;
-  if ((Hp->flags & GS_FLAG_ERRORS) || Hp->g_need == 0) return;
+  if ((Hp->flags & GS_FLAG_ERRORS) || (second ? Hp->g_need2 : Hp->g_need) == 0) return;
   const int64_t V = A.vocab;
   const int64_t lo = static_cast<int64_t>(part) * kGatherIds;
   if (lo >= V) return;
   const int n = static_cast<int>(V - lo < kGatherIds ? V - lo : kGatherIds);
-  const float Mx = Hp->Mx, scale = Hp->bscale, glo = Hp->gat_lo;
+  const float Mx = Hp->Mx, scale = Hp->bscale, glo = second ? Hp->gat_lo2 : Hp->gat_lo;
   const int32_t state = A.mask_state ? A.mask_state[row] : -1;
   const bool has_mask = A.mask_table != nullptr && state >= 0 && state < A.mask_states;
   const uint32_t* mrow = has_mask ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
@@ -1075,7 +1331,8 @@ __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __gr
   if (hl > A.history_stride) hl = A.history_stride;
   if (hl < 0) hl = 0;
   const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
-  for (int w = tid; w < kNB / 32; w += bs) sel[w] = W.sel[w];
+  const uint32_t* wsel = second ? W.sel2 : W.sel;
+  for (int w = tid; w < kNB / 32; w += bs) sel[w] = wsel[w];
   build_live(live, mrow, lo, n, hrow, hl, tid, bs);
   const unsigned lane_lt = (1u << lane) - 1u;
   auto wanted = [&](float x) {
@@ -1148,13 +1405,18 @@ __global__ void __launch_bounds__(kGatherThreads) large_gather_kernel(const __gr
 }
 
 // ============================================================================ resolve
-template <int DT>
+// PH 0: the typical pre-pass (typical-p rows with an annulus cut only): the exact run and
+// the bins of its second gather.  PH 1: the crossings, the draw and the outputs.
+template <int DT, int PH>
 __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __grid_constant__ FinalizeArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
   Ent* E = reinterpret_cast<Ent*>(dsm);               // [kGCap] selected bins, bin by bin
   double* gp = reinterpret_cast<double*>(E + kGCap);  // [kGCap] exact probabilities
   int* seg = reinterpret_cast<int*>(gp + kGCap);      // [kNB + 1] start of each bin in E
+  unsigned long long* tsort = reinterpret_cast<unsigned long long*>(seg + kNB + 4);  // [kSortSmem] typical-p
   __shared__ uint32_t sel[kNB / 32];
+  __shared__ double red_d[32];
+  __shared__ int s_ti[4];
   __shared__ uint32_t nesel[kNB / 32];  // selected and non-empty
   __shared__ unsigned s_flags;
   __shared__ int red_i[32];
@@ -1167,6 +1429,7 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
   if (pp->mode != kModeLarge) return;
   const RowWs W = row_ws(A, row);
   const LargeRow H = *W.hdr;
+  if (PH == 0 && (H.typ != kTypCut || (H.flags & GS_FLAG_ERRORS))) return;
   const double T = pp->temperature, M = H.M, total = H.total;
   const float Mx = H.Mx, scale = H.bscale;
   const int64_t V = A.vocab;
@@ -1183,11 +1446,11 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
   auto selected = [&](int b) { return ((sel[b >> 5] >> (b & 31)) & 1u) != 0; };
 
   uint32_t tok = 0xffffffffu;
-  int64_t L = 0;
+  int64_t L = 0, R0 = 0;  // the final candidates: ranks [R0, L)
   const int64_t n_fin = H.n_fin;
   if (!(H.flags & GS_FLAG_ERRORS)) {
     // ---- place the selected bins' entries: bin b occupies E[seg[b], seg[b + 1]) ----
-    for (int w = tid; w < kNB / 32; w += bs) sel[w] = W.sel[w];
+    for (int w = tid; w < kNB / 32; w += bs) sel[w] = PH == 0 ? W.sel[w] : (W.sel[w] | W.sel2[w]);
     __syncthreads();
     {
       constexpr int kPer = kNB / kResolveThreads;
@@ -1369,6 +1632,274 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
     return r;
   };
 
+  // Sums over the gathered entries of bin b with ranks in [C[b], r): of p (returned) and of
+  // p·(M - key) (*m1).  All threads.
+  auto bin_part = [&](int b, int64_t r, double* m1) -> double {
+    const int off = seg[b], n = static_cast<int>(r - C[b]);
+    double sp = 0.0, sq = 0.0;
+    for (int i = tid; i < n; i += bs) {
+      sp = __dadd_rn(sp, gp[off + i]);
+      sq = __dadd_rn(sq, __dmul_rn(gp[off + i], __dsub_rn(M, E[off + i].key)));
+    }
+    sp = block_sum_d(sp, red_d);
+    if (m1) *m1 = block_sum_d(sq, red_d);
+    return sp;
+  };
+  // Running probability before rank r, -1 when r's bin was not gathered.  All threads.
+  auto prefix_at = [&](int64_t r) -> double {
+    if (r >= n_fin) return P[kNB];
+    const int b = bin_of_rank(r);
+    if (r == static_cast<int64_t>(C[b])) return P[b];
+    if (!selected(b)) return -1.0;
+    return __dadd_rn(P[b], bin_part(b, r, nullptr));
+  };
+  // typical-p (sampling.ts:49-55) over the candidates [0, L1): the entropy H from the
+  // binned first moments and the exact entries of L1's bin, the surprise |delta - cc| of
+  // every entry of the two end ranges (cc = H - ln total).  Entries below the select
+  // kernel's bound s_lo are kept whatever the order, entries above s_hi never are; those
+  // between are sorted by surprise with the rank as the tie break (the reference's stable
+  // sort), and the running sum continues from the mass of everything below s_lo until it
+  // reaches typicalP.  The set is the ranks [*r0, *lend); *c0 is the running probability
+  // before *r0.  A result outside the select kernel's bounds is reported as unsupported.
+  // All threads.
+  auto typical_cut = [&](int64_t L1, int64_t* r0, int64_t* lend, double* c0) {
+    const double tq = pp->typical_p;
+    const double lnZ = log(total);
+    const double* Q = W.m1pre;
+    auto fail = [&]() {
+      if (tid == 0) s_flags |= GS_FLAG_ERR_UNSUPPORTED;
+    };
+    double pc, qc, out;  // P_C, sum_C p·delta, 1 - P_C
+    if (L1 < n_fin) {
+      const int b1 = bin_of_rank(L1);
+      if (L1 == static_cast<int64_t>(C[b1])) {
+        pc = P[b1];
+        qc = __ddiv_rn(Q[b1], total);
+        out = __dsub_rn(P[kNB], P[b1]);
+      } else {
+        if (!selected(b1)) return fail();
+        double q1 = 0.0;
+        const double p1 = bin_part(b1, L1, &q1);
+        const double pb = bin_part(b1, C[b1 + 1], nullptr);
+        pc = __dadd_rn(P[b1], p1);
+        qc = __dadd_rn(__ddiv_rn(Q[b1], total), q1);
+        out = __dadd_rn(__dsub_rn(P[kNB], P[b1 + 1]), __dsub_rn(pb, p1));
+      }
+    } else {
+      pc = P[kNB];
+      qc = __ddiv_rn(Q[kNB], total);
+      out = 0.0;
+    }
+    const double cc = __dsub_rn(qc, __dmul_rn(lnZ, out));
+    if (!(cc >= H.cc_lo && cc <= H.cc_hi)) return fail();
+    // the end ranges must have been gathered
+    int bad = 0;
+    for (int b = tid; b < kNB; b += bs) {
+      const bool in_end = (H.aL0 >= 0 && b >= H.aL0 && b <= H.aL1) || (H.aR0 >= 0 && b >= H.aR0 && b <= H.aR1);
+      if (in_end && !selected(b) && C[b + 1] > C[b]) bad = 1;
+    }
+    if (__syncthreads_or(bad)) return fail();
+    auto range_n = [&](int a0, int a1) -> int {  // entries of bins [a0, a1] with rank < L1
+      if (a0 < 0) return 0;
+      const int64_t e = static_cast<int64_t>(C[a1 + 1]) < L1 ? static_cast<int64_t>(C[a1 + 1]) : L1;
+      return e > static_cast<int64_t>(C[a0]) ? static_cast<int>(e - C[a0]) : 0;
+    };
+    const int nL = range_n(H.aL0, H.aL1), nR = range_n(H.aR0, H.aR1), nA = nL + nR;
+    const int eL = H.aL0 >= 0 ? seg[H.aL0] : 0, eR = H.aR0 >= 0 ? seg[H.aR0] : 0;
+    int64_t iL = 0, iR = 0;  // inner ranks (surprise below s_lo)
+    double mbase = 0.0;
+    if (H.iB0 >= 0) {
+      iL = C[H.iB0];
+      iR = static_cast<int64_t>(C[H.iB1 + 1]) < L1 ? static_cast<int64_t>(C[H.iB1 + 1]) : L1;
+      if (iR > iL) mbase = __dsub_rn(iR == static_cast<int64_t>(C[H.iB1 + 1]) ? P[H.iB1 + 1] : pc, P[H.iB0]);
+      else iR = iL;
+    }
+    auto surprise = [&](int e) { return fabs(__dsub_rn(__dsub_rn(M, E[e].key), cc)); };
+    // split the end ranges' entries at s_lo and s_hi; the band's sort keys: the surprise's
+    // bits above the low 13 (a tie break 2^-39 relative) and the entry's position, which
+    // follows the rank
+    if (tid == 0) s_ti[1] = 0;
+    __syncthreads();
+    double mb = 0.0, s_below = -1.0;
+    int n_below = 0, n_above = 0, emin = INT_MAX, emax = -1;  // (positions are >= 0)
+    for (int i = tid; i < nA; i += bs) {
+      const int e = i < nL ? eL + i : eR + (i - nL);
+      const double sv = surprise(e);
+      if (sv < H.s_lo) {
+        mb = __dadd_rn(mb, gp[e]);
+        s_below = fmax(s_below, sv);
+        ++n_below;
+        emin = min(emin, e);
+        emax = max(emax, e);
+      } else if (sv <= H.s_hi) {
+        const int at = atomicAdd(&s_ti[1], 1);
+        if (at < kSortSmem)
+          tsort[at] = (static_cast<unsigned long long>(__double_as_longlong(sv)) & ~0x1fffull) |
+                      static_cast<unsigned long long>(e);
+      } else {
+        ++n_above;
+      }
+    }
+    mbase = __dadd_rn(mbase, block_sum_d(mb, red_d));
+    s_below = block_max_d(s_below, red_d);
+    n_below = block_sum_i(n_below, red_i);
+    n_above = block_sum_i(n_above, red_i);
+    const int nB = s_ti[1];
+    if (nB > kSortSmem || mbase >= tq) return fail();
+    const int n2 = pow2_ceil(nB > 0 ? nB : 1);
+    for (int i = nB + tid; i < n2; i += bs) tsort[i] = ~0ull;
+    __syncthreads();
+    bitonic_sort_u64(tsort, n2);
+    if (warp == 0) {
+      double c = mbase, c_at = 0.0, c_prev = 0.0;
+      int found = -1;
+      for (int i0 = 0; i0 < nB; i0 += 32) {
+        const int i = i0 + lane;
+        double v = i < nB ? gp[static_cast<int>(tsort[i] & 0x1fffull)] : 0.0;
+        for (int o = 1; o < 32; o <<= 1) {
+          const double t = __shfl_up_sync(kFullMask, v, o);
+          if (lane >= o) v = __dadd_rn(t, v);
+        }
+        const double cl = __dadd_rn(c, v);
+        const unsigned hit = __ballot_sync(kFullMask, i < nB && cl >= tq);
+        if (hit) {
+          const int f = __ffs(hit) - 1;
+          found = i0 + f;
+          c_at = __shfl_sync(kFullMask, cl, f);
+          const double pv = __shfl_sync(kFullMask, cl, f > 0 ? f - 1 : 0);
+          c_prev = f > 0 ? pv : c;
+          break;
+        }
+        c = __shfl_sync(kFullMask, cl, 31);
+      }
+      if (lane == 0) {
+        s_ti[0] = found;
+        s_resd[0] = c_at;
+        s_resd[1] = c_prev;
+      }
+    }
+    __syncthreads();
+    const int found = s_ti[0];
+    const int kept = found >= 0 ? found + 1 : nB;
+    if (found >= 0) {
+      if (tid == 0) {
+        // near ties at the cut: the running sum, and the surprise against the neighbours
+        // in the order (the next band entry or an entry above s_hi; the last entry below s_lo)
+        const double sx = surprise(static_cast<int>(tsort[found] & 0x1fffull));
+        const double tol = kBoundary * fmax(sx, 1.0);
+        double m = fmin(fabs(s_resd[0] - tq), fabs(s_resd[1] - tq));
+        bool near = m <= kBoundary * tq || (n_below > 0 && sx - s_below <= tol);
+        if (found + 1 < nB) near = near || surprise(static_cast<int>(tsort[found + 1] & 0x1fffull)) - sx <= tol;
+        else near = near || H.s_hi - sx <= tol;
+        if (near) s_flags |= GS_FLAG_BOUNDARY_TYPICAL;
+      }
+    } else if (n_above > 0) {
+      return fail();  // the running sum stays below typicalP through s_hi
+    }
+    // the run: the inner ranks, the entries below s_lo and the kept band entries
+    for (int i = tid; i < kept; i += bs) {
+      const int e = static_cast<int>(tsort[i] & 0x1fffull);
+      emin = min(emin, e);
+      emax = max(emax, e);
+    }
+    emin = block_min_i(emin, red_i);
+    emax = -block_min_i(-emax, red_i);
+    auto rank_of = [&](int e) -> int64_t {
+      return (H.aR0 >= 0 && e >= eR) ? static_cast<int64_t>(C[H.aR0]) + (e - eR) : static_cast<int64_t>(C[H.aL0]) + (e - eL);
+    };
+    int64_t rl = INT64_MAX, rr = -1;
+    if (iR > iL) {
+      rl = iL;
+      rr = iR - 1;
+    }
+    if (n_below + kept > 0) {
+      const int64_t a = rank_of(emin), b = rank_of(emax);
+      rl = rl < a ? rl : a;
+      rr = rr > b ? rr : b;
+    }
+    if (rr < rl || rr - rl + 1 != (iR - iL) + n_below + kept) return fail();
+    if (found < 0 && !(rl == 0 && rr + 1 == L1)) return fail();  // every candidate stays: all of [0, L1)
+    const double pl = prefix_at(rl);
+    if (pl < 0) return fail();
+    *r0 = rl;
+    *lend = rr + 1;
+    *c0 = pl;
+  };
+  // Typical pre-pass: with the run [r0, lend) exact, the bins of the top-p crossing, the
+  // draw, the run's last rank and the head of the candidate list that the first gather
+  // did not take become W.sel2, for the second gather.  All threads.
+  auto typical_bins = [&](int64_t r0, int64_t lend, double c0) {
+    const double cend = prefix_at(lend);
+    if (cend < 0) {
+      if (tid == 0) s_flags |= GS_FLAG_ERR_UNSUPPORTED;
+      return;
+    }
+    int ra[4], rb[4];
+    int nr = 0;
+    auto addr = [&](int a, int b) {
+      if (nr < 4 && a <= b) {
+        ra[nr] = a;
+        rb[nr] = b;
+        ++nr;
+      }
+    };
+    const int blast = bin_of_rank(lend - 1);
+    addr(blast, blast);
+    double e_lo = cend, e_hi = cend;  // C(L): the running sum through the last candidate
+    if (pp->top_p < 1) {
+      const double t = __dadd_rn(c0, pp->top_p);
+      if (t * (1 - kSelMargin) <= cend) {
+        const int b0 = min(bstart(t * (1 - kSelMargin)), blast), b1 = min(bstart(t * (1 + kSelMargin)), blast);
+        addr(b0, b1);
+        e_lo = fmin(cend, P[b0]);
+        e_hi = fmin(cend, P[b1 + 1]);
+      }
+    }
+    const double u = H.uniform;
+    const double y_lo = c0 + u * (e_lo - c0), y_hi = c0 + u * (e_hi - c0);
+    addr(min(bstart(y_lo * (1 - kSelMargin)), blast), min(bstart(y_hi * (1 + kSelMargin)), blast));
+    int cb0 = -1, cb1 = -1;
+    if (A.cand_ids && A.cand_cap > 0) {
+      cb0 = bin_of_rank(r0);
+      cb1 = bin_of_rank((lend - r0 < A.cand_cap ? lend : r0 + A.cand_cap) - 1);
+    }
+    auto build = [&](bool with_cand) -> int {
+      int c = 0;
+      for (int w = tid; w < kNB / 32; w += bs) {
+        uint32_t m = 0;
+        for (int i = 0; i < 32; ++i) {
+          const int b = w * 32 + i;
+          bool in = with_cand && b >= cb0 && b <= cb1;
+          for (int r = 0; r < nr; ++r) in = in || (b >= ra[r] && b <= rb[r]);
+          if (in && !((sel[w] >> i) & 1u) && C[b + 1] > C[b]) {
+            m |= 1u << i;
+            c += static_cast<int>(C[b + 1] - C[b]);
+          }
+        }
+        W.sel2[w] = m;
+      }
+      return block_sum_i(c, red_i);
+    };
+    bool wc = cb0 >= 0;
+    int need = build(wc);
+    if (H.g_need + need > kGCap && wc) {
+      wc = false;
+      need = build(false);
+    }
+    if (tid == 0) {
+      int bhi = wc ? cb1 : -1;
+      for (int r = 0; r < nr; ++r) bhi = rb[r] > bhi ? rb[r] : bhi;
+      LargeRow* Hw = W.hdr;
+      Hw->t_r0 = r0;
+      Hw->t_lend = lend;
+      Hw->t_c0 = c0;
+      Hw->g_need2 = need;
+      Hw->gat_lo2 = bhi >= 0 && bhi < kNB - 2 ? raw_below(Mx - static_cast<float>(bhi + 2) * H.bwidth, cap, inv_cap)
+                                            : -INFINITY;
+      if (H.g_need + need > kGCap) s_flags |= GS_FLAG_ERR_UNSUPPORTED;  // beyond the gather capacity
+    }
+  };
+
   __syncthreads();
   if (!(s_flags & GS_FLAG_ERRORS)) {
     const int64_t K = pp->top_k;
@@ -1389,15 +1920,32 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
       const int64_t Lm = static_cast<int64_t>(C[H.mp_lo]) + kept;
       L1 = L1 < Lm ? L1 : Lm;
     }
-    // ---- top-p (sampling.ts:56) ----
-    L = L1;
-    if (pp->top_p < 1) {
-      const int64_t j = locate(pp->top_p, L1);
+    // ---- typical-p (sampling.ts:49-55): the typical set is ranks [R0, Lend) ----
+    int64_t Lend = L1;
+    double C0 = 0.0;  // running probability before rank R0
+    // (no annulus cut: either none, or the entropy is NaN and the cut is a running-sum cut)
+    const double tpe = (pp->typical_p < 1 && H.typ == kTypNone) ? fmin(pp->top_p, pp->typical_p) : pp->top_p;
+    if (PH == 0) {
+      typical_cut(L1, &R0, &Lend, &C0);
+      __syncthreads();
+      if (!(s_flags & GS_FLAG_ERRORS)) typical_bins(R0, Lend, C0);
+    } else if (H.typ == kTypCut) {
+      R0 = H.t_r0;
+      Lend = H.t_lend;
+      C0 = H.t_c0;
+    }
+    __syncthreads();
+    if (PH == 1) {
+    // ---- top-p (sampling.ts:56) over [R0, Lend) ----
+    L = Lend;
+    if (tpe < 1 && !(s_flags & GS_FLAG_ERRORS)) {
+      const double t = __dadd_rn(C0, tpe);
+      const int64_t j = locate(t, Lend);
       if (j >= 0) {
         L = j + 1;
         if (tid == 0) {
-          const double m = fmin(fabs(s_resd[0] - pp->top_p), j > 0 ? fabs(s_resd[1] - pp->top_p) : INFINITY);
-          if (m <= kBoundary * pp->top_p) s_flags |= GS_FLAG_BOUNDARY_TOP_P;
+          const double m = fmin(fabs(s_resd[0] - t), j > R0 ? fabs(s_resd[1] - t) : INFINITY);
+          if (m <= kBoundary * tpe) s_flags |= GS_FLAG_BOUNDARY_TOP_P;
         }
       }
     }
@@ -1427,13 +1975,13 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
         }
       }
       __syncthreads();
-      CT = s_resd[2];
+      CT = __dsub_rn(s_resd[2], C0);
       last_id = static_cast<uint32_t>(s_res[1]);
       __syncthreads();
     } else {
       // every finite candidate: the binned total (within the boundary tolerance of the
       // exact running sum); the -inf group adds nothing
-      CT = P[kNB];
+      CT = __dsub_rn(P[kNB], C0);
       if (L == n_fin) {
         // the last finite candidate, needed only if the draw falls through
         last_known = false;
@@ -1449,13 +1997,14 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
     // ---- draw (sampling.ts:58-64) ----
     if (!(s_flags & GS_FLAG_ERRORS)) {
       const double cursor = __dmul_rn(H.uniform, CT);
+      const double target = __dadd_rn(C0, cursor);
       const int64_t lim = L < n_fin ? L : n_fin;
-      const int64_t j = locate(cursor, lim);
+      const int64_t j = locate(target, lim);
       if (j >= 0) {
         const int b = bin_of_rank(j);
         tok = E[seg[b] + static_cast<int>(j - C[b])].id;
         if (tid == 0) {
-          const double m = fmin(fabs(s_resd[0] - cursor), j > 0 ? fabs(s_resd[1] - cursor) : INFINITY);
+          const double m = fmin(fabs(s_resd[0] - target), j > R0 ? fabs(s_resd[1] - target) : INFINITY);
           if (m <= kBoundary * CT) s_flags |= GS_FLAG_BOUNDARY_DRAW;
         }
       } else {
@@ -1501,7 +2050,12 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
         }
       }
     }
+    }
     __syncthreads();
+  }
+  if (PH == 0) {
+    if (tid == 0) W.hdr->flags = s_flags;
+    return;
   }
 
   // ---- outputs ----
@@ -1510,7 +2064,7 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
   if (tid == 0) {
     A.ids[row] = err ? -1 : static_cast<int32_t>(tok);
     if (A.flags) A.flags[row] = fl;
-    if (A.cand_count) A.cand_count[row] = err ? 0 : static_cast<int32_t>(L);
+    if (A.cand_count) A.cand_count[row] = err ? 0 : static_cast<int32_t>(L - R0);
     if (!err && !A.uniforms && A.rng_state) A.rng_state[row] = H.rng_next;
     if (A.logprob) {
       double lp = NAN;
@@ -1523,17 +2077,20 @@ __global__ void __launch_bounds__(kResolveThreads) large_resolve_kernel(const __
     }
   }
   if (A.cand_ids) {
-    // the first min(L, cand_cap) candidates in order, when their bins were gathered
-    int64_t m = err ? 0 : (L < A.cand_cap ? L : A.cand_cap);
-    if (m > n_fin) m = n_fin;
-    int nw = 0;
+    // the first min(L - R0, cand_cap) candidates in order, when their bins were gathered
+    int64_t m = err ? 0 : (L - R0 < A.cand_cap ? L - R0 : A.cand_cap);
+    if (m > n_fin - R0) m = n_fin - R0;
+    int nw = 0, e0 = 0;
     if (m > 0) {
-      const int b = bin_of_rank(m - 1);
-      if (seg[b + 1] == static_cast<int>(C[b + 1])) nw = static_cast<int>(m);  // bins 0..b all gathered
+      const int b0 = bin_of_rank(R0), b1 = bin_of_rank(R0 + m - 1);
+      if (seg[b1 + 1] - seg[b0] == static_cast<int>(C[b1 + 1] - C[b0])) {  // bins b0..b1 all gathered
+        nw = static_cast<int>(m);
+        e0 = seg[b0] + static_cast<int>(R0 - C[b0]);
+      }
     }
     for (int i = tid; i < A.cand_cap; i += bs) {
-      A.cand_ids[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? static_cast<int32_t>(E[i].id) : -1;
-      if (A.cand_probs) A.cand_probs[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? gp[i] : 0.0;
+      A.cand_ids[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? static_cast<int32_t>(E[e0 + i].id) : -1;
+      if (A.cand_probs) A.cand_probs[static_cast<int64_t>(row) * A.cand_cap + i] = i < nw ? gp[e0 + i] : 0.0;
     }
   }
 }
@@ -1547,24 +2104,39 @@ void set_smem(Kern k, size_t bytes) {
 
 template <int DT>
 cudaError_t launch_large_t(const FinalizeArgs& a, int rows, size_t select_smem, cudaStream_t st) {
-  const size_t res_smem = static_cast<size_t>(kGCap) * (sizeof(Ent) + 8) + (kNB + 1) * 4;
+  const size_t res_smem = large_resolve_smem_bytes();
   static bool attr = false;
   if (!attr) {
     set_smem(large_select_kernel<DT>, large_select_smem_bytes(GS_MAX_HISTORY));
-    set_smem(large_resolve_kernel<DT>, res_smem);
-    set_smem(large_hist_kernel<DT, false>, static_cast<size_t>(kHistQueue) * sizeof(float));
-    set_smem(large_hist_kernel<DT, true>, static_cast<size_t>(kHistQueue) * sizeof(float));
+    set_smem(large_resolve_kernel<DT, 0>, res_smem);
+    set_smem(large_resolve_kernel<DT, 1>, res_smem);
+    const size_t q = static_cast<size_t>(kHistQueue) * sizeof(float), qm = q + static_cast<size_t>(kNB) * 4;
+    set_smem(large_hist_kernel<DT, false, false>, q);
+    set_smem(large_hist_kernel<DT, true, false>, q);
+    set_smem(large_hist_kernel<DT, false, true>, qm);
+    set_smem(large_hist_kernel<DT, true, true>, qm);
     attr = true;
   }
   const size_t hq_smem = static_cast<size_t>(kHistQueue) * sizeof(float);
-  if (a.want_raw)
-    large_hist_kernel<DT, true><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
-  else
-    large_hist_kernel<DT, false><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
+  const size_t hm_smem = hq_smem + static_cast<size_t>(kNB) * 4;
+  if (a.lmoments) {
+    if (a.want_raw)
+      large_hist_kernel<DT, true, true><<<rows * kCluster, kHistThreads, hm_smem, st>>>(a);
+    else
+      large_hist_kernel<DT, false, true><<<rows * kCluster, kHistThreads, hm_smem, st>>>(a);
+  } else if (a.want_raw) {
+    large_hist_kernel<DT, true, false><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
+  } else {
+    large_hist_kernel<DT, false, false><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
+  }
   large_select_kernel<DT><<<rows, kSelectThreads, select_smem, st>>>(a);
   const int parts = static_cast<int>((a.vocab + kGatherIds - 1) / kGatherIds);
-  large_gather_kernel<DT><<<rows * parts, kGatherThreads, 0, st>>>(a, parts);
-  large_resolve_kernel<DT><<<rows, kResolveThreads, res_smem, st>>>(a);
+  large_gather_kernel<DT><<<rows * parts, kGatherThreads, 0, st>>>(a, parts, 0);
+  if (a.lmoments) {  // typical-p rows: the exact run, then the bins that depend on it
+    large_resolve_kernel<DT, 0><<<rows, kResolveThreads, res_smem, st>>>(a);
+    large_gather_kernel<DT><<<rows * parts, kGatherThreads, 0, st>>>(a, parts, 1);
+  }
+  large_resolve_kernel<DT, 1><<<rows, kResolveThreads, res_smem, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -122,6 +122,7 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   L->kc = kc;
   L->kmax = kmax;
   L->any_large = ps.any_large;
+  L->any_typical_large = ps.any_typical_large;
   L->any_small = ps.any_small;
   L->any_sample = ps.any_sample;
   const int64_t units = static_cast<int64_t>(rows) * S;
@@ -155,6 +156,7 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
   L->kc = 0;
   L->kmax = ps.kmax;
   L->any_large = ps.any_large;
+  L->any_typical_large = false;
   L->any_small = ps.any_small;
   L->any_sample = ps.any_sample;
   L->plans_off = 0;
@@ -263,6 +265,7 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   fa.lws = ws + L.large_off;
   fa.lrow_bytes = static_cast<int64_t>(L.large_row);
   fa.lslots = static_cast<int32_t>(sa.history_stride);
+  fa.lmoments = L.any_typical_large ? 1 : 0;
   if (smode) {
     fa.shard_mode = smode;
     fa.shards = shard->shards;

@@ -57,6 +57,7 @@ struct Layout {
   int kc;
   int kmax;
   bool any_large;
+  bool any_typical_large;  // a histogram-path row with typical-p
   bool any_small;
   bool any_sample;
   size_t plans_off, stats_off, cands_off, rowtau_off, large_off, total;
@@ -69,11 +70,13 @@ struct Layout {
 struct PlanSummary {
   int kmax = 0;
   bool any_large = false;
+  bool any_typical_large = false;
   bool any_small = false;
   bool any_sample = false;
   void add(const RowPlan& p) {
     kmax = p.k_eff > kmax ? p.k_eff : kmax;
     any_large |= p.mode == kModeLarge;
+    any_typical_large |= p.mode == kModeLarge && p.typical_p < 1;
     any_small |= p.mode != kModeLarge;
     any_sample |= p.mode != kModeGreedy;
   }

@@ -107,3 +107,14 @@ def test_c1_256_sequential_steps(pkg, oracle, sampler):
         history.append(ref.token)
         assert float(st_gpu.item()) == st_ref, f"step {step}: rng state"
     assert boundary <= 2
+
+
+@pytest.mark.parametrize("case", [dict(typicalP=0.9, topP=1.0), dict(typicalP=0.6, topP=0.9),
+                                  dict(typicalP=0.95, topP=0.95, minP=0.02)], ids=["t0.9", "t0.6-p0.9", "t0.95-minp"])
+def test_c2_64_rows_typical_p(pkg, oracle, sampler, case):
+    """C2's 64 rows (262144 ids, 1024-id histories, penalties) with typical-p over the full
+    vocabulary: the annulus cut, the typical pre-pass and the second gather."""
+    base = W.make("C2", device="cpu", rows=1).params[0]
+    p = dict(base, **case)
+    gpu = _full(pkg, oracle, sampler, "C2", 64, cand_cap=2048, params=[p])
+    assert (gpu.flags & pkg._lib.FLAG_LARGE_PATH).all()

@@ -146,3 +146,57 @@ def test_c2_replay_is_bit_identical(sampler):
         torch.cuda.synchronize()
         outs.append([t.cpu().numpy().tobytes() for t in (r.ids, r.flags, r.logprob, r.cand_ids, r.cand_probs, rng)])
     assert outs[0] == outs[1]
+
+
+def _typical_rows(gpu, large):
+    assert (gpu.flags & large).all(), "rows left the histogram path"
+
+
+@pytest.mark.parametrize("case", [
+    dict(typicalP=0.9, topP=1.0, temperature=1.0),
+    dict(typicalP=0.5, topP=0.9, temperature=1.0),
+    dict(typicalP=0.2, topP=1.0, temperature=0.7),
+    dict(typicalP=0.95, topP=0.8, minP=0.01, temperature=1.1),
+    dict(typicalP=0.99, topP=1.0, minP=0.3, temperature=1.0),
+    dict(typicalP=0.9, topP=0.95, topK=5000, temperature=1.3),
+    dict(typicalP=0.7, topP=1.0, temperature=3.0),
+], ids=["t0.9", "t0.5-p0.9", "t0.2-cold", "t0.95-minp", "t0.99-minp-all", "t0.9-k5000", "t0.7-flat"])
+def test_typical_p(oracle, sampler, case):
+    """typical-p over the whole vocabulary: the surprise centre from the binned first
+    moments, the two ends of the typical run from the annulus bins."""
+    rng = np.random.default_rng(int(case["typicalP"] * 100) + int(case["temperature"] * 10))
+    V, rows = 65536, 8
+    x = (rng.standard_normal((rows, V)) * 2.0).astype(np.float32)
+    x[:, :64] += rng.random((rows, 64)).astype(np.float32) * 8.0  # a head above the bulk
+    gpu, large = _check(oracle, sampler, x, [_p(**case)], label=f"typical-{case}", seed=7)
+    _typical_rows(gpu, large)
+
+
+def test_typical_p_masked_and_penalised(oracle, sampler):
+    """Masked ids are -inf candidates: the reference's entropy is NaN and the typical cut
+    becomes a running-sum cut; with min-p (no -inf candidate) the annulus cut runs over
+    penalised entries."""
+    rng = np.random.default_rng(29)
+    V, rows, H = 65536, 8, 200
+    x = (rng.standard_normal((rows, V)) * 2.0).astype(np.float32)
+    table = _mask(rng, V, [0.2, 0.6])
+    mstate = np.array([r % 3 - 1 for r in range(rows)], dtype=np.int32)
+    hist = rng.integers(0, V, (rows, H)).astype(np.int32)
+    hist[:, :30] = np.argsort(-x, axis=1)[:, :30]
+    hlen = np.full(rows, H, dtype=np.int32)
+    for i, case in enumerate([dict(typicalP=0.8, topP=0.95), dict(typicalP=0.6, topP=0.7),
+                              dict(typicalP=0.9, topP=1.0, minP=0.001)]):
+        p = _p(temperature=0.9, repetitionPenalty=1.3, presencePenalty=0.3, frequencyPenalty=0.1,
+               repetitionWindow=H, **case)
+        gpu, large = _check(oracle, sampler, x, [p], hist=hist, hlen=hlen, table=table, mstate=mstate,
+                            label=f"typical-masked{i}", seed=11 + i)
+        _typical_rows(gpu, large)
+
+
+def test_typical_p_bf16_full_vocabulary(oracle, sampler):
+    import torch
+    rng = np.random.default_rng(31)
+    x = (rng.standard_normal((6, 262144)) * 2.5).astype(np.float32)
+    gpu, large = _check(oracle, sampler, x, [_p(typicalP=0.9, topP=0.95, temperature=1.0)], dtype=torch.bfloat16,
+                        label="typical-bf16")
+    _typical_rows(gpu, large)
