@@ -358,6 +358,8 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
                                           steps=100)
     legs["c3"] = config_leg(pkg, W, sampler, dev, "C3", 256, steps=200)
     legs["c2"] = config_leg(pkg, W, sampler, dev, "C2", 64, steps=200)
+    legs["c2_typical"] = config_leg(pkg, W, sampler, dev, "C2", 64, steps=200, override={"typicalP": 0.9},
+                                    label="c2_typical")
     res["configs"] = legs
     res["bf16"] = {k: legs["c4_bf16"][k] for k in ("value", "unit", "steps", "logits_gbps")}
     # ---- C1 latency: B=1, 256 sequential steps, fresh logits each step, one seeded stream
@@ -392,16 +394,18 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     return res
 
 
-def config_leg(pkg, W, sampler, dev, name, rows, dtype=None, mask=True, history=True, steps=100):
+def config_leg(pkg, W, sampler, dev, name, rows, dtype=None, mask=True, history=True, steps=100, override=None,
+               label=None):
     """One configuration at `rows` rows: rows/s, the path's kernel time split (streaming
     pass / merge or histogram path, CUDA events recorded by the library) and the HBM
     roofline of the dominant launches.  Inputs smaller than twice L2 are replicated and
-    the copies used in turn, so that every step reads its logits from HBM."""
+    the copies used in turn, so that every step reads its logits from HBM.  `override`:
+    sampling parameters replacing the configuration's (named by `label`)."""
     import torch
     import ctypes
     L = pkg._lib
     wl = W.make(name, device=dev, rows=rows, dtype=dtype)
-    params = pkg.prepare_params(wl.params)
+    params = pkg.prepare_params([dict(p, **override) for p in wl.params] if override else wl.params)
     kw = dict(softcap=wl.softcap)
     if history and wl.history is not None:
         kw.update(history=wl.history, history_len=wl.history_len)
@@ -445,8 +449,11 @@ def config_leg(pkg, W, sampler, dev, name, rows, dtype=None, mask=True, history=
         kern, kern_us = "gs::stream2_kernel (streaming pass)", stream_us
     achieved = rows * bpr / (kern_us / 1e6) / 1e9
     tpr = traffic_per_row(tag)
+    if label:
+        tag = label
     res = {
-        "workload": f"{name} x {rows} rows" + ("" if mask or wl.mask_table is None else ", no constraint mask"),
+        "workload": f"{name} x {rows} rows" + ("" if mask or wl.mask_table is None else ", no constraint mask") +
+                    (f", {label}: {override}" if override else ""),
         "value": rows * steps / dt, "unit": UNIT, "steps": steps, "us_per_step": dt / steps * 1e6,
         "logits_dtype": "bf16" if esz == 2 else "f32",
         "logits_gbps": rows * bpr * steps / dt / 1e9, "row_errors": errors,
