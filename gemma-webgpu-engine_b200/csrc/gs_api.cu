@@ -33,6 +33,7 @@ struct gs_ctx {
   unsigned char* io = nullptr;
   size_t io_bytes = 0;
   unsigned long long* digest = nullptr;
+  unsigned* step_done = nullptr;  // [kStepDoneRows] counters of the single-launch decode step (zeroed once)
   int32_t* tok_dev = nullptr;
   double* lp_dev = nullptr;
   size_t tok_cap = 0;
@@ -138,6 +139,8 @@ gs_status gs_create(int device, gs_ctx** out) {
   for (int k = 0; k < gs_ctx::kPlanSlots && e == cudaSuccess; ++k)
     e = cudaEventCreateWithFlags(&c->plans_ev[k], cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMalloc(&c->digest, sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&c->step_done, kStepDoneRows * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(c->step_done, 0, kStepDoneRows * sizeof(unsigned));
   if (e != cudaSuccess) {
     delete c;
     return GS_ECUDA;
@@ -153,6 +156,7 @@ gs_status gs_destroy(gs_ctx* c) {
   if (c->ws) cudaFree(c->ws);
   if (c->io) cudaFree(c->io);
   if (c->digest) cudaFree(c->digest);
+  if (c->step_done) cudaFree(c->step_done);
   if (c->tok_dev) cudaFree(c->tok_dev);
   if (c->lp_dev) cudaFree(c->lp_dev);
   for (int k = 0; k < gs_ctx::kPlanSlots; ++k) {
@@ -266,7 +270,8 @@ gs_status run_call(gs_ctx* c, const gs_batch* b, const gs_outputs* o, void* stre
     }
   }
   gs_outputs none{};
-  s = launch_sampling(b, o ? o : &none, L, plan0, dplans, c->ws, st, c->profile ? evs.data() : nullptr, &c->err, sh);
+  s = launch_sampling(b, o ? o : &none, L, plan0, dplans, c->ws, st, c->profile ? evs.data() : nullptr, &c->err, sh,
+                      c->step_done);
   if (s != GS_OK) return s;
   if (c->profile) c->ev_live.push_back(evs);
   return GS_OK;

@@ -9,6 +9,8 @@ namespace gs {
 
 enum RowMode : int32_t { kModeSmallK = 0, kModeGreedy = 1, kModeLarge = 2 };
 
+constexpr int kStepDoneRows = 8;  // rows the single-launch decode step serves (one counter each)
+
 // Per-row plan, derived on the host from gs_params (one DecodingConfig per row).
 struct RowPlan {
   double temperature;

@@ -18,7 +18,9 @@
 // device's primary context is reset and created again, when the array can move.
 //
 // Every call writes each scratch byte it later reads, so nothing has to start at zero;
-// the array keeps the previous call's contents.  All calls share the one array: two
+// the array keeps the previous call's contents.  The exception is the single-launch
+// decode step's per-row counters (g_noalloc_done): they start at zero when the module
+// loads, and the step's last CTA of each row sets its counter back to zero.  All calls share the one array: two
 // calls whose kernels overlap on the GPU (different streams, no ordering between them)
 // race on it and produce undefined results.
 #include <string>
@@ -31,6 +33,7 @@ namespace {
 static_assert(GS_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size must keep 256-byte alignment");
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[GS_NOALLOC_SCRATCH_BYTES];
+__device__ unsigned g_noalloc_done[kStepDoneRows];
 
 thread_local std::string g_noalloc_err;
 
@@ -101,7 +104,13 @@ extern "C" gs_status gs_sample_noalloc(const gs_batch* b, const gs_outputs* o, v
     if (e != cudaSuccess) return set_error(GS_ECUDA, std::string("plan kernel: ") + cudaGetErrorString(e));
     dplans = plans;
   }
-  s = launch_sampling(b, o, L, plan0, dplans, scratch + params_bytes, st, nullptr, &err);
+  void* done = nullptr;
+  if (L.step) {
+    const cudaError_t e = cudaGetSymbolAddress(&done, g_noalloc_done);
+    if (e != cudaSuccess) return set_error(GS_ECUDA, std::string("cudaGetSymbolAddress(counters): ") + cudaGetErrorString(e));
+  }
+  s = launch_sampling(b, o, L, plan0, dplans, scratch + params_bytes, st, nullptr, &err, nullptr,
+                      static_cast<unsigned*>(done));
   if (s != GS_OK) return set_error(s, err);
   return GS_OK;
 }

@@ -144,6 +144,12 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
     return fmt(err, GS_EUNSUPPORTED, "merge needs %zu bytes of shared memory (topK %d, history %lld)", L->fin_smem, kmax,
                static_cast<long long>(hs));
   L->large_smem = ps.any_large ? large_select_smem_bytes(hs) : 0;
+  L->step = step_eligible(b, kmax, ps.any_large, rows);
+  L->step_off = 0;
+  if (L->step) {
+    L->step_off = align_up(L->total, 256);
+    L->total = L->step_off + step_ws_bytes(rows, V, kmax);
+  }
   return GS_OK;
 }
 
@@ -165,6 +171,8 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
   L->rowtau_off = L->stats_off;
   L->large_off = L->stats_off;
   L->large_row = 0;
+  L->step = false;
+  L->step_off = 0;
   L->total = L->stats_off;
   L->stream_smem = 0;
   L->hist_cap = 1;
@@ -180,7 +188,18 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
 
 gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
                           const RowPlan* dplans, unsigned char* ws, cudaStream_t st, cudaEvent_t* events,
-                          std::string* err, const ShardInfo* shard) {
+                          std::string* err, const ShardInfo* shard, unsigned* step_done) {
+  if (L.step && step_done && !shard) {
+    // one launch: streaming, merge, filters and draw (gs_step.cu)
+    if (events) cudaEventRecord(events[0], st);
+    const cudaError_t e = launch_step(b, o, plan0, dplans, L.kmax, ws + L.step_off, step_done, st);
+    if (e != cudaSuccess) return fmt(err, GS_ECUDA, "decode step launch: %s", cudaGetErrorString(e));
+    if (events) {
+      cudaEventRecord(events[1], st);
+      cudaEventRecord(events[2], st);
+    }
+    return GS_OK;
+  }
   UnitStat* stats = reinterpret_cast<UnitStat*>(ws + L.stats_off);
   unsigned long long* cands = reinterpret_cast<unsigned long long*>(ws + L.cands_off);
   const int smode = shard ? shard->mode : 0;

@@ -62,6 +62,8 @@ struct Layout {
   bool any_sample;
   size_t plans_off, stats_off, cands_off, rowtau_off, large_off, total;
   size_t large_row;  // per-row workspace of the histogram path (0: no such row)
+  bool step;         // the single-launch decode step serves the batch (gs_step.cu)
+  size_t step_off;   // its records and sort scratch
   size_t stream_smem, fin_smem, large_smem;
   int hist_cap, ent_cap, pack_cap, work_cap;
 };
@@ -108,9 +110,17 @@ gs_status plan_merge_layout(const gs_batch* b, const PlanSummary& ps, const Shar
 // `events` (3 entries or nullptr) are recorded before the stream pass, before the
 // merge, and at the end.  `shard` (nullptr: an ordinary call) selects a sharded mode.
 // `ws` is the call's workspace (the layout's offsets are relative to it).
+// Single-launch decode step (gs_step.cu): a few rows without a constraint table or a
+// penalty history, topK <= 64; `done` holds kStepDoneRows per-row counters that start at
+// zero (the kernel resets them).
+bool step_eligible(const gs_batch* b, int kmax, bool any_large, int rows);
+size_t step_ws_bytes(int rows, int64_t vocab, int kmax);
+cudaError_t launch_step(const gs_batch* b, const gs_outputs* o, const RowPlan& plan0, const RowPlan* dplans, int kmax,
+                        unsigned char* ws, unsigned* done, cudaStream_t st);
+
 gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& L, const RowPlan& plan0,
                           const RowPlan* dplans, unsigned char* ws, cudaStream_t st, cudaEvent_t* events,
-                          std::string* err, const ShardInfo* shard = nullptr);
+                          std::string* err, const ShardInfo* shard = nullptr, unsigned* step_done = nullptr);
 
 // Message of this thread's last failed gs_sample_noalloc call.
 const char* noalloc_last_error();

@@ -1,0 +1,125 @@
+"""The single-launch decode step (csrc/gs_step.cu) against the oracle.
+
+Batches of at most eight rows without a constraint table or a penalty history, whose
+rows all have topK <= 64 (or temperature 0), run as one kernel: each 2048-id unit sorts
+its best packs, and the last unit of a row to finish merges the units' records (only the
+packs at or above the k-th largest unit maximum), then filters and draws in one warp.
+The cases put the row's best values in one unit, across units, in exact ties and in the
+partial last unit; they cover greedy rows, topK 1..64, min-p, typical-p, top-p, the soft
+cap on and off, -inf logits, bf16, log-probabilities, and calls whose row counts change
+from call to call (each row's counter is reset by its last unit)."""
+from __future__ import annotations
+
+import importlib
+
+import numpy as np
+import pytest
+
+import parity_util as PU
+
+pytestmark = pytest.mark.gpu
+
+W = importlib.import_module("gemma-webgpu-engine_b200.workloads")
+
+
+def _p(**kw):
+    p = {"temperature": 0.8, "topK": 40, "topP": 0.95, "minP": 0.0, "typicalP": 1.0, "repetitionPenalty": 1.0,
+         "presencePenalty": 0.0, "frequencyPenalty": 0.0, "repetitionWindow": 0}
+    p.update(kw)
+    return p
+
+
+def _check(oracle, sampler, x, params, *, softcap=30.0, dtype=None, label="", max_boundary=1, seed=0, cand_cap=64):
+    rows, V = x.shape
+    rng_state = np.array([pkg_seed(seed + r) for r in range(rows)])
+    gpu = PU.run_gpu(sampler, x, params, softcap=softcap, rng_state=rng_state, dtype=dtype, cand_cap=cand_cap)
+    xo = x
+    if dtype is not None:
+        import torch
+        xo = torch.from_numpy(x).to(dtype).float().numpy()
+    ids, margins, cands, st = PU.oracle_rows_batched(oracle, xo, V, softcap, params, rng_state=rng_state,
+                                                     cand_cap=cand_cap)
+    assert PU.compare(gpu, ids, margins, cands, rng_after=st, label=label) <= max_boundary
+    # log-probabilities: tokenLogProbability over the capped logits
+    for r in range(rows):
+        if gpu.ids[r] >= 0:
+            row = oracle.softcap(xo[r], softcap) if softcap else xo[r].astype(np.float32)
+            lp = oracle.token_log_probability(row, int(gpu.ids[r]))
+            assert abs(gpu.logprob[r] - lp) <= 1e-6 * max(1.0, abs(lp)), (label, r, gpu.logprob[r], lp)
+    return gpu
+
+
+def pkg_seed(s):
+    pkg = importlib.import_module("gemma-webgpu-engine_b200")
+    return pkg.SeededRandom(s).state
+
+
+def _rows(rng, rows, V, scale=2.0):
+    x = (rng.standard_normal((rows, V)) * scale).astype(np.float32)
+    if rows > 1:
+        x[1, 1000:1064] = 9.5            # exact ties among the best values, inside one unit
+    if rows > 2:
+        x[2, ::4099] += 12.0             # the best values spread one per unit
+    if rows > 3:
+        x[3, -5:] = 11.0                 # the best values in the last unit
+    if rows > 4:
+        x[4, :] *= 0.01                  # a flat row
+    if rows > 5:
+        x[5, 2040:2056] = 10.0           # ties across a unit boundary
+    return x
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("softcap", [30.0, 0.0], ids=["cap30", "nocap"])
+def test_step_rows_and_filters(oracle, sampler, dtype, softcap):
+    import torch
+    td = torch.bfloat16 if dtype == "bf16" else None
+    rng = np.random.default_rng(3 + (dtype == "bf16") + 2 * (softcap == 0))
+    V, rows = 262144, 8
+    x = _rows(rng, rows, V)
+    ps = [_p(temperature=0.0),
+          _p(topK=64, topP=1.0),
+          _p(topK=1),
+          _p(topK=7, minP=0.05),
+          _p(topK=40, typicalP=0.8),
+          _p(topK=50, topP=0.7, temperature=1.3),
+          _p(topK=33, minP=0.01, typicalP=0.9, topP=0.9),
+          _p(topK=64, temperature=0.4)]
+    _check(oracle, sampler, x, ps, softcap=softcap, dtype=td, label=f"step-{dtype}-{softcap}")
+
+
+@pytest.mark.parametrize("rows", [1, 2, 3, 5, 8])
+def test_step_row_counts_and_counter_reset(oracle, sampler, rows):
+    """Calls with changing row counts, back to back: every row's counter must be back at
+    zero for the next call (a stale count would merge before the units finish)."""
+    rng = np.random.default_rng(100 + rows)
+    V = 262144
+    for call in range(3):
+        x = _rows(rng, rows, V)
+        _check(oracle, sampler, x, [_p()], label=f"rows{rows}-call{call}", seed=7 * call)
+
+
+def test_step_negative_infinity_and_small_vocab(oracle, sampler):
+    rng = np.random.default_rng(41)
+    V, rows = 262144, 4
+    x = (rng.standard_normal((rows, V)) * 2.0).astype(np.float32)
+    x[0, rng.choice(V, V // 2, replace=False)] = -np.inf
+    x[1, :] = -np.inf
+    x[1, 17] = 3.0                       # a single finite id: the rest of the top 40 is -inf
+    _check(oracle, sampler, x, [_p(topK=40, topP=1.0)], softcap=0.0, label="neginf")
+    for V2 in (2048, 4096, 8192 + 4, 131072):
+        x2 = (rng.standard_normal((3, V2)) * 2.0).astype(np.float32)
+        _check(oracle, sampler, x2, [_p(topK=min(40, V2), topP=0.9)], label=f"V{V2}", seed=V2)
+
+
+def test_c1_steps_bit_identical_replay(sampler):
+    """The same C1 call twice gives the same bytes (ids, flags, candidates, states)."""
+    import torch
+    wl = W.make("C1", device="cuda")
+    outs = []
+    for _ in range(2):
+        st = wl.rng_state("cuda")
+        r = sampler.sample(wl.logits, wl.params, softcap=wl.softcap, rng_state=st, logprob=True, candidates=40)
+        torch.cuda.synchronize()
+        outs.append([t.cpu().numpy().tobytes() for t in (r.ids, r.flags, r.logprob, r.cand_ids, r.cand_probs, st)])
+    assert outs[0] == outs[1]
