@@ -380,11 +380,51 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
         evs[s + 1].record(stream)
     torch.cuda.synchronize()
     lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(steps))
+    # the kernels' own device time per step (the library's events around its launches)
+    import ctypes
+    Lb = pkg._lib.lib()
+    Lb.gs_profile_enable(sampler.handle, 1)
+    for s in range(steps):
+        o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream, out=o1)
+    torch.cuda.synchronize()
+    s_ms, s_n, m_ms, m_n = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double(), ctypes.c_int64()
+    Lb.gs_profile_read(sampler.handle, ctypes.byref(s_ms), ctypes.byref(s_n), ctypes.byref(m_ms), ctypes.byref(m_n))
+    Lb.gs_profile_enable(sampler.handle, 0)
+    kern_us = (s_ms.value + m_ms.value) / max(1, s_n.value) * 1e3
+    # the same 256 steps captured in one CUDA graph: no host work between the steps
+    graph_us = None
+    try:
+        gs = torch.cuda.Stream(dev)
+        gs.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gs):
+            for s in range(steps):
+                o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=gs.cuda_stream, out=o1)
+        with torch.cuda.stream(gs):
+            for _ in range(3):
+                graph.replay()
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        with torch.cuda.stream(gs):  # (replay launches on the current stream)
+            g0.record(gs)
+            for _ in range(reps):
+                graph.replay()
+            g1.record(gs)
+        torch.cuda.synchronize()
+        graph_us = g0.elapsed_time(g1) * 1e3 / (reps * steps)
+        del graph
+    except RuntimeError as e:  # a capture the runtime refuses: report the step times without it
+        print(f"latency_b1: graph capture failed: {e}", file=sys.stderr)
+        torch.cuda.synchronize()
     res["latency_b1"] = {"workload": "C1: B=1, V=262144, soft cap 30, T=0.8, topK 40, topP 0.95, seed 42, "
                                      "256 sequential steps",
                          "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],
-                         "timing": "CUDA events between consecutive gs_sample calls (device time, no graph; "
-                                   "256 distinct 1 MiB rows, 256 MiB > L2)"}
+                         "kernel_us": kern_us, "graph_us_per_step": graph_us,
+                         "timing": "p50/p95: CUDA events between consecutive gs_sample calls (device time, no "
+                                   "graph; 256 distinct 1 MiB rows, 256 MiB > L2); kernel_us: the library's events "
+                                   "around its launches, average per step; graph_us_per_step: the 256 calls "
+                                   "captured in one CUDA graph, replayed"}
     del lg
     # ---- CPU baseline (N = 1 only): the oracle on a bounded sample of the same rows
     if world == 1:

@@ -35,8 +35,12 @@ constexpr int kStepThreads = 512;                // four ids per thread
 constexpr int kStepWarps = kStepThreads / 32;    // sixteen sorted lists of 128 packs
 constexpr int kStepMaxK = 64;                    // topK the step handles
 constexpr int kStepMaxUnits = 512;               // vocabularies up to 1 M ids
-constexpr int kStepMaxPacks = 8192;              // units x k2 (the bound's worst case)
+constexpr int kStepRecPacks = 4;                  // record capacity: kStepRecPacks x k2 packs
+constexpr int kStepMaxPacks = kStepMaxK * kStepRecPacks * kStepMaxK;  // packs at or above the bound: k units' records
 constexpr int kStepSortSmem = 1024;              // candidate packs sorted in shared memory
+// shared memory: the exact fallback's lists at k2 = 64, or the last CTA's arrays
+constexpr int kStepSmemLast = kStepMaxUnits * (8 + 4 + 4) + 2 * kStepSortSmem * 8;
+constexpr int kStepSmemMax = kStepSmemLast > 2 * kStepWarps * kStepMaxK * 8 ? kStepSmemLast : 2 * kStepWarps * kStepMaxK * 8;
 
 struct StepArgs {
   const void* logits;
@@ -64,15 +68,41 @@ struct StepArgs {
   unsigned* done;                    // [rows] CTAs of the row finished
 };
 
-struct StepRec {  // one unit's record; k2 packs follow (sorted, descending; 0 = none)
+constexpr int kStepHead = 4;  // a unit's best packs kept sorted in its record
+
+struct StepRec {  // one unit's record; n packs follow (in no order)
   float m;        // max over the unit's capped logits, -inf if none
-  float pad0;
+  uint32_t flags;
   double s;       // sum 2^((x - m)·a2)
   double raw_s;   // sum e^(x - m) (every id is live: m is also the raw maximum)
-  uint32_t flags;
-  int32_t pad1;
+  unsigned long long head[kStepHead];  // the unit's best packs, descending (0: none)
+  int32_t n;      // packs that follow: every pack at or above the unit's bound (its k best among them)
+  int32_t pad;
 };
-static_assert(sizeof(StepRec) == 32, "record header");
+static_assert(sizeof(StepRec) == 64, "record header");
+
+// The warp's kStepHead best of the packs its lanes hold (every lane gets them, descending).
+__device__ __forceinline__ void warp_head(const unsigned long long* v, int nv, unsigned long long* out) {
+  unsigned long long c[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) c[q] = q < nv ? v[q] : 0ull;
+#pragma unroll
+  for (int r = 0; r < kStepHead; ++r) {
+    unsigned long long lm = c[0];
+#pragma unroll
+    for (int q = 1; q < 4; ++q) lm = c[q] > lm ? c[q] : lm;
+    unsigned long long wm = lm;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(kFullMask, wm, o);
+      wm = t > wm ? t : wm;
+    }
+    out[r] = wm;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (wm != 0ull && c[q] == wm) c[q] = 0ull;  // (packs are distinct: one lane holds it)
+  }
+}
 
 // Descending bitonic sort of 128 packs held four per lane (element lane·4 + q in v[q]).
 __device__ __forceinline__ void warp_sort128_desc(unsigned long long (&v)[4], int lane) {
@@ -106,6 +136,71 @@ __device__ __forceinline__ void warp_sort128_desc(unsigned long long (&v)[4], in
   }
 }
 
+// The K2 (a power of two, <= 64) best of two descending lists a and b of K2 packs, sorted
+// descending, by one warp: c[i] = max(a[i], b[K2-1-i]) is a bitonic sequence holding them,
+// then half-cleaners sort it.  Element i sits in lane i & 31, register i >> 5.
+__device__ __forceinline__ void warp_merge_top(const unsigned long long* a, const unsigned long long* b, int K2,
+                                               unsigned long long* out, int lane) {
+  unsigned long long c[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int i = q * 32 + lane;
+    c[q] = 0ull;
+    if (i < K2) {
+      const unsigned long long x = a[i], y = b[K2 - 1 - i];
+      c[q] = x > y ? x : y;
+    }
+  }
+  if (K2 == 64) {  // h = 32: the two registers of a lane
+    if (c[0] < c[1]) {
+      const unsigned long long t = c[0];
+      c[0] = c[1];
+      c[1] = t;
+    }
+  }
+  for (int h = (K2 < 32 ? K2 : 32) >> 1; h > 0; h >>= 1) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const unsigned long long p = __shfl_xor_sync(kFullMask, c[q], h);
+      c[q] = (lane & h) == 0 ? (c[q] > p ? c[q] : p) : (c[q] > p ? p : c[q]);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int i = q * 32 + lane;
+    if (i < K2) out[i] = c[q];
+  }
+}
+
+// warp_merge_top for 32-bit keys.
+__device__ __forceinline__ void warp_merge_top_u32(const uint32_t* a, const uint32_t* b, int K2, uint32_t* out,
+                                                   int lane) {
+  uint32_t c[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int i = q * 32 + lane;
+    c[q] = 0u;
+    if (i < K2) c[q] = max(a[i], b[K2 - 1 - i]);
+  }
+  if (K2 == 64 && c[0] < c[1]) {
+    const uint32_t t = c[0];
+    c[0] = c[1];
+    c[1] = t;
+  }
+  for (int h = (K2 < 32 ? K2 : 32) >> 1; h > 0; h >>= 1) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t p = __shfl_xor_sync(kFullMask, c[q], h);
+      c[q] = (lane & h) == 0 ? max(c[q], p) : min(c[q], p);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int i = q * 32 + lane;
+    if (i < K2) out[i] = c[q];
+  }
+}
+
 // Descending block-wide bitonic sort of n2 (a power of two) packs in shared or global
 // memory (this CTA's own: __syncthreads orders both).
 __device__ void block_sort_desc(unsigned long long* v, int n2) {
@@ -132,8 +227,12 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   __shared__ double red_d[32];
   __shared__ int red_i[32];
   __shared__ unsigned s_flags;
-  __shared__ int s_last, s_n;
-  __shared__ unsigned long long s_tau;
+  __shared__ int s_last, s_n, s_nq;
+  __shared__ unsigned long long s_tau, s_top;
+  __shared__ unsigned long long s_heads[kStepWarps * kStepHead], s_head[kStepHead];
+  __shared__ uint32_t s_wkey[kStepWarps];
+  __shared__ unsigned long long s_wtau[kStepWarps];
+  __shared__ int s_pre[kStepMaxUnits + 1];
   const int S = A.units;
   const int row = blockIdx.x / S, unit = blockIdx.x - row * S;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -183,7 +282,10 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     if (cap != 0.0f) x[q] = softcap(x[q], cap, inv_cap);
     mx = fmaxf(mx, x[q]);
   }
-  if (tid == 0) s_flags = 0u;
+  if (tid == 0) {
+    s_flags = 0u;
+    s_n = 0;
+  }
   const float m = block_max_f(mx, red_f);
   bad = __syncthreads_or(bad);
   float sa = 0.0f, sr = 0.0f;
@@ -196,59 +298,104 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       if (A.want_raw) sr += ex2_approx(fmaf(d, kL2eLo, d * kL2eHi));
     }
   }
-  const double s_unit = block_sum_d(static_cast<double>(sa), red_d);
-  const double r_unit = A.want_raw ? block_sum_d(static_cast<double>(sr), red_d) : 0.0;
-
-  // ---- 2. the unit's k2 best packs, sorted ----
-  unsigned long long v[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) v[q] = valid[q] ? make_pack(x[q], static_cast<uint32_t>(id0 + q)) : 0ull;
-  warp_sort128_desc(v, lane);
-  unsigned long long* la = reinterpret_cast<unsigned long long*>(dsm);  // [kStepWarps][K2], twice
-  unsigned long long* lb = la + kStepWarps * K2;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int i = lane * 4 + q;
-    if (i < K2) la[warp * K2 + i] = v[q];
-  }
-  __syncthreads();
-  for (int nl = kStepWarps; nl > 1; nl >>= 1) {
-    // lists 2j and 2j+1 -> list j: the larger of A[i] and B[K2-1-i] is a bitonic sequence
-    // holding the K2 best of both, then half-cleaners sort it
-    for (int t = tid; t < (nl >> 1) * K2; t += kStepThreads) {
-      const int j = t / K2, i = t - j * K2;
-      const unsigned long long a = la[(2 * j) * K2 + i], b = la[(2 * j + 1) * K2 + (K2 - 1 - i)];
-      lb[j * K2 + i] = a > b ? a : b;
+  // both sums in one reduction round (warps in order)
+  double s_unit = 0.0, r_unit = 0.0;
+  {
+    const double ws = warp_sum(static_cast<double>(sa)), wr = A.want_raw ? warp_sum(static_cast<double>(sr)) : 0.0;
+    if (lane == 0) {
+      red_d[warp] = ws;
+      red_d[kStepWarps + warp] = wr;
     }
     __syncthreads();
-    for (int h = K2 >> 1; h > 0; h >>= 1) {
-      for (int t = tid; t < (nl >> 1) * (K2 >> 1); t += kStepThreads) {
-        const int j = t / (K2 >> 1), r = t - j * (K2 >> 1);
-        const int i = ((r / h) * 2 * h) + (r % h);  // lower element of the pair (i, i + h)
-        unsigned long long* c = lb + j * K2;
-        const unsigned long long a = c[i], b = c[i + h];
-        if (a < b) {
-          c[i] = b;
-          c[i + h] = a;
-        }
-      }
-      __syncthreads();
+    for (int w = 0; w < kStepWarps; ++w) {
+      s_unit = __dadd_rn(s_unit, red_d[w]);
+      r_unit = __dadd_rn(r_unit, red_d[kStepWarps + w]);
     }
-    unsigned long long* t = la;
-    la = lb;
-    lb = t;
+  }
+
+  // ---- 2. a bound on the unit's k-th best value: each warp's c-th largest thread best
+  //      key (c = ceil(k / 16)), the least of the sixteen (16·c >= k threads hold a value at
+  //      or above it); the unit keeps its packs at or above it ----
+  unsigned long long v[4], tbest = 0ull;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    v[q] = valid[q] ? make_pack(x[q], static_cast<uint32_t>(id0 + q)) : 0ull;
+    tbest = v[q] > tbest ? v[q] : tbest;
+  }
+  // the unit's head: each warp's best four, then the best four of those
+  {
+    unsigned long long h[kStepHead];
+    warp_head(v, 4, h);
+    if (lane < kStepHead) s_heads[warp * kStepHead + lane] = lane == 0 ? h[0] : lane == 1 ? h[1] : lane == 2 ? h[2] : h[3];
+  }
+  uint32_t kk = static_cast<uint32_t>(tbest >> 32);  // (0: no value)
+#pragma unroll
+  for (int kw = 2; kw <= 32; kw <<= 1) {
+#pragma unroll
+    for (int j = kw >> 1; j > 0; j >>= 1) {
+      const uint32_t p = __shfl_xor_sync(kFullMask, kk, j);
+      kk = ((lane & j) == 0) == ((lane & kw) == 0) ? max(kk, p) : min(kk, p);
+    }
+  }
+  const int cw = (k + kStepWarps - 1) / kStepWarps;  // <= 4
+  if (lane == cw - 1) s_wkey[warp] = kk;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned long long hv[2] = {s_heads[lane], s_heads[32 + lane]};
+    warp_head(hv, 2, s_head);
+  }
+  kk = s_wkey[0];
+#pragma unroll
+  for (int w = 1; w < kStepWarps; ++w) kk = min(kk, s_wkey[w]);
+  unsigned char* rec = rec_row + static_cast<int64_t>(unit) * A.rec_bytes;
+  unsigned long long* rpk = reinterpret_cast<unsigned long long*>(rec + sizeof(StepRec));
+  const int cap_rec = kStepRecPacks * K2;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const bool take = v[q] != 0ull && static_cast<uint32_t>(v[q] >> 32) >= kk;
+    const unsigned bal = __ballot_sync(kFullMask, take);
+    if (!bal) continue;
+    const int leader = __ffs(bal) - 1;
+    int at = 0;
+    if (lane == leader) at = atomicAdd(&s_n, __popc(bal));
+    at = __shfl_sync(kFullMask, at, leader) + __popc(bal & ((1u << lane) - 1u));
+    if (take && at < cap_rec) rpk[at] = v[q];
+  }
+  __syncthreads();
+  int n_rec = s_n;
+  if (n_rec > cap_rec) {
+    // ties at the bound beyond the record: the unit's exact k2 best, sorted (each warp
+    // sorts its 128 packs, then the lists merge pairwise)
+    warp_sort128_desc(v, lane);
+    unsigned long long* la = reinterpret_cast<unsigned long long*>(dsm);  // [kStepWarps][K2], twice
+    unsigned long long* lb = la + kStepWarps * K2;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = lane * 4 + q;
+      if (i < K2) la[warp * K2 + i] = v[q];
+    }
+    __syncthreads();
+    for (int nl = kStepWarps; nl > 1; nl >>= 1) {
+      if (warp < (nl >> 1)) warp_merge_top(la + (2 * warp) * K2, la + (2 * warp + 1) * K2, K2, lb + warp * K2, lane);
+      __syncthreads();
+      unsigned long long* t = la;
+      la = lb;
+      lb = t;
+    }
+    for (int i = tid; i < K2; i += kStepThreads) rpk[i] = la[i];
+    n_rec = K2;
   }
 
   // ---- 3. the record, then a ticket ----
-  unsigned char* rec = rec_row + static_cast<int64_t>(unit) * A.rec_bytes;
-  unsigned long long* rpk = reinterpret_cast<unsigned long long*>(rec + sizeof(StepRec));
-  for (int i = tid; i < K2; i += kStepThreads) rpk[i] = la[i];
   if (tid == 0) {
     StepRec r{};
     r.m = m;
     r.s = m > -INFINITY ? s_unit : 0.0;
     r.raw_s = m > -INFINITY ? r_unit : 0.0;
     r.flags = bad ? GS_FLAG_ERR_NONFINITE : 0u;
+#pragma unroll
+    for (int i = 0; i < kStepHead; ++i) r.head[i] = s_head[i];
+    r.n = n_rec;
     *reinterpret_cast<StepRec*>(rec) = r;
   }
   __threadfence();
@@ -258,49 +405,105 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   if (!s_last) return;
   __threadfence();
 
-  // ---- 4. the last CTA of the row: statistics over the units ----
+  // ---- 4. the last CTA of the row: statistics (one unit per thread), the bound, the
+  //      packs at or above it ----
+  unsigned long long* umax = reinterpret_cast<unsigned long long*>(dsm);  // [kStepMaxUnits] each unit's best pack
+  int* un = reinterpret_cast<int*>(umax + kStepMaxUnits);                 // [kStepMaxUnits] its packs
+  int* qlist = un + kStepMaxUnits;                                        // [kStepMaxUnits] units that reach the bound
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(qlist + kStepMaxUnits);  // [kStepSortSmem]
+  unsigned long long* srt = cand + kStepSortSmem;                                          // [kStepSortSmem]
+  unsigned long long* scratch = A.sort_scratch + static_cast<int64_t>(row) * kStepMaxPacks;
   unsigned fl = 0;
-  float um = -INFINITY;
-  unsigned long long* umax = reinterpret_cast<unsigned long long*>(dsm);  // [S] each unit's best pack
-  int* ucnt = reinterpret_cast<int*>(umax + kStepMaxUnits);              // [S + 1] packs above the bound, prefix
-  unsigned long long* cand = reinterpret_cast<unsigned long long*>(ucnt + kStepMaxUnits + 8);  // [kStepSortSmem]
-  for (int u = tid; u < S; u += kStepThreads) {
-    const unsigned char* r = rec_row + static_cast<int64_t>(u) * A.rec_bytes;
-    const StepRec* st = reinterpret_cast<const StepRec*>(r);
-    fl |= __ldcg(&st->flags);
-    um = fmaxf(um, __ldcg(&st->m));
-    umax[u] = __ldcg(reinterpret_cast<const unsigned long long*>(r + sizeof(StepRec)));
+  float mu = -INFINITY;
+  double su = 0.0, ru = 0.0;
+  unsigned long long hd[kStepHead] = {0ull, 0ull, 0ull, 0ull};
+  if (tid < S) {
+    const StepRec* st = reinterpret_cast<const StepRec*>(rec_row + static_cast<int64_t>(tid) * A.rec_bytes);
+    mu = __ldcg(&st->m);
+    su = __ldcg(&st->s);
+    ru = __ldcg(&st->raw_s);
+    fl = __ldcg(&st->flags);
+#pragma unroll
+    for (int i = 0; i < kStepHead; ++i) hd[i] = __ldcg(&st->head[i]);
+    umax[tid] = hd[0];
+    un[tid] = __ldcg(&st->n);
   }
   if (fl) atomicOr(&s_flags, fl);
-  const float Mx = block_max_f(um, red_f);  // (the raw maximum too)
-  if (tid == 0) s_tau = 0ull;
+  if (tid == 0) {
+    s_n = 0;
+    s_nq = 0;
+    s_tau = 0ull;
+    s_top = 0ull;
+  }
+  const float Mx = block_max_f(mu, red_f);  // the raw maximum too (every id is live)
+  // the bound: the units' bests in groups of 32, each group sorted by one warp; with g
+  // groups, the least of the groups' c-th largest (c = ceil(k / g)) has g·c >= k unit bests
+  // at or above it (none when a group holds fewer than c, or c > 32)
+  {
+    const int g = (S + 31) >> 5, c = (k + g - 1) / g;
+    if (warp < g) {
+      const int u = warp * 32 + lane;
+      unsigned long long b = u < S ? umax[u] : 0ull;
+#pragma unroll
+      for (int kw = 2; kw <= 32; kw <<= 1) {
+#pragma unroll
+        for (int j = kw >> 1; j > 0; j >>= 1) {
+          const unsigned long long p = __shfl_xor_sync(kFullMask, b, j);
+          b = ((lane & j) == 0) == ((lane & kw) == 0) ? (b > p ? b : p) : (b > p ? p : b);
+        }
+      }
+      if (lane == 0 && b) atomicMax(&s_top, b);
+      if (c <= 32) {
+        const unsigned long long t = __shfl_sync(kFullMask, b, c - 1);
+        if (lane == 0) s_wtau[warp] = t;
+      }
+    }
+    __syncthreads();
+    if (tid == 0 && c <= 32) {
+      unsigned long long t = s_wtau[0];
+      for (int w = 1; w < g; ++w) t = s_wtau[w] < t ? s_wtau[w] : t;
+      s_tau = t;
+    }
+  }
   __syncthreads();
   fl = s_flags;
   if (greedy) fl |= GS_FLAG_GREEDY;
-  // the bound: the k-th largest unit maximum (none when fewer than k units hold packs)
-  for (int u = tid; u < S; u += kStepThreads) {
-    const unsigned long long mu = umax[u];
-    int above = 0;
-    for (int q = 0; q < S; ++q) above += umax[q] > mu;
-    if (mu != 0ull && above == k - 1) s_tau = mu;
+  const unsigned long long tau = s_tau;
+  // each unit's head packs at or above the bound; a unit whose whole head reaches it may
+  // hold more such packs: its record is read in full instead (below)
+  auto append = [&](bool take, unsigned long long p) {
+    const unsigned bal = __ballot_sync(kFullMask, take);
+    if (!bal) return;
+    const int leader = __ffs(bal) - 1;
+    int at = 0;
+    if (lane == leader) at = atomicAdd(&s_n, __popc(bal));
+    at = __shfl_sync(kFullMask, at, leader) + __popc(bal & ((1u << lane) - 1u));
+    if (take) {
+      if (at < kStepSortSmem) cand[at] = p;
+      if (at < kStepMaxPacks) scratch[at] = p;
+    }
+  };
+  for (int u0 = 0; u0 < S; u0 += kStepThreads) {  // (one round: S <= the block's threads)
+    const int u = u0 + tid;
+    const bool over = u < S && hd[kStepHead - 1] != 0ull && hd[kStepHead - 1] >= tau;
+#pragma unroll
+    for (int i = 0; i < kStepHead; ++i) append(u < S && !over && hd[i] != 0ull && hd[i] >= tau, hd[i]);
+    const unsigned bal = __ballot_sync(kFullMask, over);
+    if (bal) {
+      const int leader = __ffs(bal) - 1;
+      int at = 0;
+      if (lane == leader) at = atomicAdd(&s_nq, __popc(bal));
+      at = __shfl_sync(kFullMask, at, leader) + __popc(bal & ((1u << lane) - 1u));
+      if (over) qlist[at] = u;
+    }
   }
   __syncthreads();
-  const unsigned long long tau = s_tau;
-  // each unit's packs at or above the bound (its list is sorted: a binary search)
-  int c = 0;
-  if (tid < S) {
-    const unsigned long long* pk = reinterpret_cast<const unsigned long long*>(rec_row + static_cast<int64_t>(tid) * A.rec_bytes + sizeof(StepRec));
-    int lo = 0, hi = K2;  // first index whose pack is below the bound (or empty)
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      const unsigned long long p = __ldcg(pk + mid);
-      if (p != 0ull && p >= tau) lo = mid + 1;
-      else hi = mid;
-    }
-    c = lo;
-  }
+  const int nq = s_nq;
+  // their packs, flattened (an exclusive prefix of their counts), four loads per thread
+  // in flight; the packs at or above the bound are appended in no order
   {
-    int incl = c;
+    const int cu = tid < nq ? un[qlist[tid]] : 0;
+    int incl = cu;
     for (int o = 1; o < 32; o <<= 1) {
       const int t = __shfl_up_sync(kFullMask, incl, o);
       if (lane >= o) incl += t;
@@ -312,38 +515,75 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       if (w < warp) before += red_i[w];
       tot += red_i[w];
     }
-    if (tid < S) ucnt[tid] = before + incl - c;
-    if (tid == 0) s_n = tot;
+    if (tid < nq) s_pre[tid] = before + incl - cu;
+    if (tid == 0) s_pre[nq] = tot;
     __syncthreads();
   }
-  const int N = s_n;
-  unsigned long long* cbuf = N <= kStepSortSmem ? cand : A.sort_scratch + static_cast<int64_t>(row) * kStepMaxPacks;
-  const int n2 = pow2_ceil(N > 0 ? N : 1);
-  if (tid < S) {
-    const unsigned long long* pk = reinterpret_cast<const unsigned long long*>(rec_row + static_cast<int64_t>(tid) * A.rec_bytes + sizeof(StepRec));
-    for (int i = 0; i < c; ++i) cbuf[ucnt[tid] + i] = __ldcg(pk + i);
+  const int P = s_pre[nq];
+  for (int f0 = 0; f0 < P; f0 += 4 * kStepThreads) {
+    unsigned long long p[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int f = f0 + q * kStepThreads + tid;
+      p[q] = 0ull;
+      if (f < P) {
+        int lo = 0, hi = nq - 1;  // the last qi with s_pre[qi] <= f
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_pre[mid] <= f) lo = mid;
+          else hi = mid - 1;
+        }
+        const int u = qlist[lo];
+        p[q] = __ldcg(reinterpret_cast<const unsigned long long*>(rec_row + static_cast<int64_t>(u) * A.rec_bytes +
+                                                                   sizeof(StepRec)) + (f - s_pre[lo]));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) append(p[q] != 0ull && p[q] >= tau, p[q]);
   }
-  for (int i = N + tid; i < n2; i += kStepThreads) cbuf[i] = 0ull;
   __syncthreads();
+  const int N = s_n < kStepMaxPacks ? s_n : kStepMaxPacks;
   unsigned long long best[4] = {0ull, 0ull, 0ull, 0ull};  // warp 0: the row's best packs, lane·4 + q
-  if (n2 <= 128) {
+  if (N <= 512) {
+    // exact order by rank counting (the packs are distinct)
+    for (int i = tid; i < N; i += kStepThreads) {
+      const unsigned long long p = cand[i];
+      int r = 0;
+      for (int j = 0; j < N; ++j) r += cand[j] > p;
+      srt[r] = p;
+    }
+    __syncthreads();
     if (warp == 0) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) best[q] = lane * 4 + q < n2 ? cbuf[lane * 4 + q] : 0ull;
-      warp_sort128_desc(best, lane);
+      for (int q = 0; q < 4; ++q) best[q] = lane * 4 + q < N ? srt[lane * 4 + q] : 0ull;
     }
   } else {
+    unsigned long long* cbuf = N <= kStepSortSmem ? cand : scratch;
+    const int n2 = pow2_ceil(N);
+    for (int i = N + tid; i < n2; i += kStepThreads) cbuf[i] = 0ull;
+    __syncthreads();
     block_sort_desc(cbuf, n2);
     if (warp == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) best[q] = lane * 4 + q < N ? cbuf[lane * 4 + q] : 0ull;
     }
   }
-  __syncthreads();
+  // the full-vocabulary normaliser relative to the best key M (the best pack is the
+  // largest unit maximum) and the raw sum, one unit per thread
+  const unsigned long long top = s_top;
+  const double T = pp->temperature;
+  const double xtop = static_cast<double>(pack_value(top));
+  const double M = greedy ? xtop : __ddiv_rn(xtop, T);
+  double part = 0.0, rpart = 0.0;
+  if (tid < S && mu > -INFINITY) {
+    if (!greedy && M > -INFINITY) part = __dmul_rn(su, exp(__dsub_rn(__ddiv_rn(static_cast<double>(mu), T), M)));
+    if (A.want_raw) rpart = __dmul_rn(ru, exp(static_cast<double>(mu) - static_cast<double>(Mx)));
+  }
+  const double total = block_sum_d(part, red_d);
+  const double rs = A.want_raw ? block_sum_d(rpart, red_d) : 0.0;
   if (warp != 0) return;
 
   // ---- 5. one warp: probabilities, filters, draw, outputs ----
-  const double T = pp->temperature;
   const int nC = N < k ? N : k;
   WWork w;
   {
@@ -365,18 +605,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   }
   uint32_t tok = 0xffffffffu;
   int n_final = 0;
-  double rs = 0.0;
-  if (A.want_raw && Mx > -INFINITY) {
-    for (int u = lane; u < S; u += 32) {
-      const StepRec* st = reinterpret_cast<const StepRec*>(rec_row + static_cast<int64_t>(u) * A.rec_bytes);
-      const float mu = __ldcg(&st->m);
-      if (mu > -INFINITY) rs = __dadd_rn(rs, __dmul_rn(__ldcg(&st->raw_s), exp(static_cast<double>(mu) - static_cast<double>(Mx))));
-    }
-    rs = warp_sum(rs);
-  }
   if (!(fl & GS_FLAG_ERRORS)) {
-    const unsigned long long top = __shfl_sync(kFullMask, best[0], 0);
-    const double xtop = static_cast<double>(pack_value(top));
     if (greedy) {
       // argmax over the whole vocabulary: all -inf -> id 0 (sampling.ts:92-96)
       tok = (top == 0ull || !(xtop > -INFINITY)) ? 0u : pack_id(top);
@@ -386,17 +615,9 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       }
       n_final = 1;
     } else {
-      const double M = __ddiv_rn(xtop, T);
       if (!(M > -INFINITY)) {
         fl |= GS_FLAG_ERR_NONFINITE;  // every logit -inf: outside the domain
       } else {
-        double part = 0.0;
-        for (int u = lane; u < S; u += 32) {
-          const StepRec* st = reinterpret_cast<const StepRec*>(rec_row + static_cast<int64_t>(u) * A.rec_bytes);
-          const float mu = __ldcg(&st->m);
-          if (mu > -INFINITY) part = __dadd_rn(part, __dmul_rn(__ldcg(&st->s), exp(__dsub_rn(__ddiv_rn(static_cast<double>(mu), T), M))));
-        }
-        const double total = warp_sum(part);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int i = lane * 4 + q;
@@ -415,7 +636,36 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
           if (lane == 0) A.rng_state[row] = st;
         }
         __syncwarp();
-        tok = warp_filter_and_draw(w, nC, pp->min_p, pp->typical_p, pp->top_p, r, &n_final, &fl, lane);
+        if (!(pp->min_p > 0) && !(pp->typical_p < 1)) {
+          // top-p and the draw only: the draw's running sums over the kept prefix are the
+          // first entries of the top-p cut's (same prefix-sum order), so one scan serves both
+          warp_scan4_d(w.cp, w.cum, nC, lane);
+          int n = nC;
+          if (pp->top_p < 1) {
+            const double t = pp->top_p;
+            const int below = warp_count_below(w.cum, nC, t, lane);
+            n = below + 1 < nC ? below + 1 : nC;
+            double m = fabs(w.cum[n - 1] - t);
+            if (n >= 2) m = fmin(m, fabs(w.cum[n - 2] - t));
+            if (m <= kBoundaryRel * t) fl |= GS_FLAG_BOUNDARY_TOP_P;
+          }
+          const double ct = w.cum[n - 1];
+          const double cursor = __dmul_rn(r, ct);
+          const int below = warp_count_below(w.cum, n, cursor, lane);
+          if (below < n) {
+            tok = w.cid[below];
+          } else {
+            tok = w.cid[n - 1];
+            fl |= GS_FLAG_FELL_THROUGH;
+          }
+          const int j = below < n ? below : n - 1;
+          double m = fabs(w.cum[j] - cursor);
+          if (j >= 1) m = fmin(m, fabs(w.cum[j - 1] - cursor));
+          if (m <= kBoundaryRel * ct) fl |= GS_FLAG_BOUNDARY_DRAW;
+          n_final = n;
+        } else {
+          tok = warp_filter_and_draw(w, nC, pp->min_p, pp->typical_p, pp->top_p, r, &n_final, &fl, lane);
+        }
       }
     }
   }
@@ -460,13 +710,12 @@ bool step_eligible(const gs_batch* b, int kmax, bool any_large, int rows) {
   const int64_t esz = b->dtype == GS_DTYPE_F32 ? 4 : 2;
   if ((reinterpret_cast<uintptr_t>(b->logits) & 15) != 0 || (b->row_stride * esz) % 16 != 0) return false;
   const int64_t units = (b->vocab + kStepIds - 1) / kStepIds;
-  if (units > kStepMaxUnits) return false;
-  return units * pow2_at_least(kmax) <= kStepMaxPacks;
+  return units <= kStepMaxUnits;
 }
 
 size_t step_ws_bytes(int rows, int64_t vocab, int kmax) {
   const int64_t units = (vocab + kStepIds - 1) / kStepIds;
-  const size_t rec = sizeof(StepRec) + 8 * static_cast<size_t>(pow2_at_least(kmax));
+  const size_t rec = sizeof(StepRec) + 8 * static_cast<size_t>(kStepRecPacks) * pow2_at_least(kmax);
   return align_up(static_cast<size_t>(rows) * units * rec, 256) + static_cast<size_t>(rows) * kStepMaxPacks * 8;
 }
 
@@ -492,20 +741,24 @@ cudaError_t launch_step(const gs_batch* b, const gs_outputs* o, const RowPlan& p
   a.cand_cap = o->cand_cap;
   a.units = static_cast<int32_t>((b->vocab + kStepIds - 1) / kStepIds);
   a.k2 = pow2_at_least(kmax);
-  a.rec_bytes = static_cast<int32_t>(sizeof(StepRec) + 8 * static_cast<size_t>(a.k2));
+  a.rec_bytes = static_cast<int32_t>(sizeof(StepRec) + 8 * static_cast<size_t>(kStepRecPacks) * a.k2);
   a.recs = ws;
   a.sort_scratch = reinterpret_cast<unsigned long long*>(ws + align_up(static_cast<size_t>(b->rows) * a.units * a.rec_bytes, 256));
   a.done = done;
   // shared memory: the merge tree's two list sets, or the last CTA's arrays
   const size_t tree = 2 * static_cast<size_t>(kStepWarps) * a.k2 * 8;
-  const size_t last = static_cast<size_t>(kStepMaxUnits) * 8 + (kStepMaxUnits + 8) * 4 + static_cast<size_t>(kStepSortSmem) * 8;
+  const size_t last = kStepSmemLast;
   const size_t smem = tree > last ? tree : last;
   const int grid = b->rows * a.units;
+  static bool attr = false;  // (set once, outside any stream capture: the first call)
+  if (!attr) {
+    cudaFuncSetAttribute(step_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
+    cudaFuncSetAttribute(step_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
+    attr = true;
+  }
   if (b->dtype == GS_DTYPE_F32) {
-    cudaFuncSetAttribute(step_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     step_kernel<GS_DTYPE_F32><<<grid, kStepThreads, smem, st>>>(a);
   } else {
-    cudaFuncSetAttribute(step_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     step_kernel<GS_DTYPE_BF16><<<grid, kStepThreads, smem, st>>>(a);
   }
   return cudaGetLastError();

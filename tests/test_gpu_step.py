@@ -5,7 +5,8 @@ rows all have topK <= 64 (or temperature 0), run as one kernel: each 2048-id uni
 its best packs, and the last unit of a row to finish merges the units' records (only the
 packs at or above the k-th largest unit maximum), then filters and draws in one warp.
 The cases put the row's best values in one unit, across units, in exact ties and in the
-partial last unit; they cover greedy rows, topK 1..64, min-p, typical-p, top-p, the soft
+partial last unit, and a unit tied throughout (its record then holds its exact best);
+they cover greedy rows, topK 1..64, min-p, typical-p, top-p, the soft
 cap on and off, -inf logits, bf16, log-probabilities, and calls whose row counts change
 from call to call (each row's counter is reset by its last unit)."""
 from __future__ import annotations
@@ -66,6 +67,9 @@ def _rows(rng, rows, V, scale=2.0):
         x[4, :] *= 0.01                  # a flat row
     if rows > 5:
         x[5, 2040:2056] = 10.0           # ties across a unit boundary
+    if rows > 6:
+        x[6, 2048:4096] = 11.0           # a whole unit tied at the top: more ties at the unit's
+        #                                  bound than its record holds (the exact-sort fallback)
     return x
 
 
