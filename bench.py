@@ -367,7 +367,8 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     lg = torch.empty((steps, VOCAB), dtype=torch.float32, device=dev)
     for s in range(steps):
         lg[s] = W.make("C1", device=dev, step=s).logits[0]
-    p1 = W.base_params(temperature=0.8, topK=40, topP=0.95, repetitionWindow=0)
+    # (a decode loop converts its fixed config once: prepare_params)
+    p1 = pkg.prepare_params(W.base_params(temperature=0.8, topK=40, topP=0.95, repetitionWindow=0))
     st = torch.tensor([pkg.SeededRandom(42).state], dtype=torch.float64, device=dev)
     o1 = None
     for s in range(16):
@@ -375,9 +376,11 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     st.fill_(pkg.SeededRandom(42).state)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     evs[0].record(stream)
+    h0 = time.perf_counter()
     for s in range(steps):
         o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream, out=o1)
         evs[s + 1].record(stream)
+    host_us = (time.perf_counter() - h0) / steps * 1e6
     torch.cuda.synchronize()
     lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(steps))
     # the kernels' own device time per step (the library's events around its launches)
@@ -420,11 +423,13 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     res["latency_b1"] = {"workload": "C1: B=1, V=262144, soft cap 30, T=0.8, topK 40, topP 0.95, seed 42, "
                                      "256 sequential steps",
                          "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],
-                         "kernel_us": kern_us, "graph_us_per_step": graph_us,
+                         "kernel_us": kern_us, "graph_us_per_step": graph_us, "host_us_per_call": host_us,
                          "timing": "p50/p95: CUDA events between consecutive gs_sample calls (device time, no "
                                    "graph; 256 distinct 1 MiB rows, 256 MiB > L2); kernel_us: the library's events "
                                    "around its launches, average per step; graph_us_per_step: the 256 calls "
-                                   "captured in one CUDA graph, replayed"}
+                                   "captured in one CUDA graph, replayed (device time per step, no host work "
+                                   "between steps); host_us_per_call: the host time of one gs_sample call from "
+                                   "Python (params prepared once)"}
     del lg
     # ---- CPU baseline (N = 1 only): the oracle on a bounded sample of the same rows
     if world == 1:

@@ -223,15 +223,15 @@ __device__ void block_sort_desc(unsigned long long* v, int n2) {
 template <int DT>
 __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  __shared__ float red_f[kStepWarps];
-  __shared__ double red_d[32];
-  __shared__ int red_i[32];
-  __shared__ unsigned s_flags;
-  __shared__ int s_last, s_n, s_nq;
-  __shared__ unsigned long long s_tau, s_top;
-  __shared__ unsigned long long s_heads[kStepWarps * kStepHead], s_head[kStepHead];
+  __shared__ float s_wmax[kStepWarps];
+  __shared__ double s_wsum[kStepWarps], s_wraw[kStepWarps];
   __shared__ uint32_t s_wkey[kStepWarps];
-  __shared__ unsigned long long s_wtau[kStepWarps];
+  __shared__ unsigned long long s_head[kStepHead], s_gtop[kStepWarps];
+  __shared__ unsigned long long spk[kStepRecPacks * kStepMaxK];  // the record's packs
+  __shared__ double s_r, s_st;
+  __shared__ unsigned s_flags, s_wbad;
+  __shared__ int s_last, s_n, s_nq;
+  __shared__ int red_i[kStepWarps];
   __shared__ int s_pre[kStepMaxUnits + 1];
   const int S = A.units;
   const int row = blockIdx.x / S, unit = blockIdx.x - row * S;
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   const float lim = cap != 0.0f ? INFINITY : 3.40282347e38f;  // raw x is an error when !(x <= lim)
   unsigned char* rec_row = A.recs + static_cast<int64_t>(row) * S * A.rec_bytes;
 
-  // ---- 1. four ids per thread: capped logits, maximum, sums ----
+  // ---- 1. four ids per thread: capped logits; the unit maximum ----
   const int64_t id0 = static_cast<int64_t>(unit) * kStepIds + tid * 4;
   float x[4];
   bool valid[4];
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       x[q] = valid[q] ? load_logit(rowbase, DT, id0 + q) : 0.0f;
     }
   }
-  int bad = 0;
+  bool bad = false;
   float mx = -INFINITY;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -282,12 +282,21 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     if (cap != 0.0f) x[q] = softcap(x[q], cap, inv_cap);
     mx = fmaxf(mx, x[q]);
   }
+  {
+    const float wm = warp_max(mx);
+    if (lane == 0) s_wmax[warp] = wm;
+  }
   if (tid == 0) {
     s_flags = 0u;
+    s_wbad = 0u;
     s_n = 0;
   }
-  const float m = block_max_f(mx, red_f);
-  bad = __syncthreads_or(bad);
+  __syncthreads();
+  float m = s_wmax[0];
+#pragma unroll
+  for (int w = 1; w < kStepWarps; ++w) m = fmaxf(m, s_wmax[w]);
+
+  // ---- 2. the sums; the packs; each warp's head and its threads' best keys ----
   float sa = 0.0f, sr = 0.0f;
   if (m > -INFINITY) {
 #pragma unroll
@@ -298,36 +307,14 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       if (A.want_raw) sr += ex2_approx(fmaf(d, kL2eLo, d * kL2eHi));
     }
   }
-  // both sums in one reduction round (warps in order)
-  double s_unit = 0.0, r_unit = 0.0;
-  {
-    const double ws = warp_sum(static_cast<double>(sa)), wr = A.want_raw ? warp_sum(static_cast<double>(sr)) : 0.0;
-    if (lane == 0) {
-      red_d[warp] = ws;
-      red_d[kStepWarps + warp] = wr;
-    }
-    __syncthreads();
-    for (int w = 0; w < kStepWarps; ++w) {
-      s_unit = __dadd_rn(s_unit, red_d[w]);
-      r_unit = __dadd_rn(r_unit, red_d[kStepWarps + w]);
-    }
-  }
-
-  // ---- 2. a bound on the unit's k-th best value: each warp's c-th largest thread best
-  //      key (c = ceil(k / 16)), the least of the sixteen (16·c >= k threads hold a value at
-  //      or above it); the unit keeps its packs at or above it ----
   unsigned long long v[4], tbest = 0ull;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     v[q] = valid[q] ? make_pack(x[q], static_cast<uint32_t>(id0 + q)) : 0ull;
     tbest = v[q] > tbest ? v[q] : tbest;
   }
-  // the unit's head: each warp's best four, then the best four of those
-  {
-    unsigned long long h[kStepHead];
-    warp_head(v, 4, h);
-    if (lane < kStepHead) s_heads[warp * kStepHead + lane] = lane == 0 ? h[0] : lane == 1 ? h[1] : lane == 2 ? h[2] : h[3];
-  }
+  // a bound on the unit's k-th best value: each warp's c-th largest thread best key
+  // (c = ceil(k / 16)), the least of the sixteen (16·c >= k threads hold a value at or above it)
   uint32_t kk = static_cast<uint32_t>(tbest >> 32);  // (0: no value)
 #pragma unroll
   for (int kw = 2; kw <= 32; kw <<= 1) {
@@ -339,14 +326,20 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   }
   const int cw = (k + kStepWarps - 1) / kStepWarps;  // <= 4
   if (lane == cw - 1) s_wkey[warp] = kk;
-  __syncthreads();
-  if (warp == 0) {
-    const unsigned long long hv[2] = {s_heads[lane], s_heads[32 + lane]};
-    warp_head(hv, 2, s_head);
+  {
+    const double ws = warp_sum(static_cast<double>(sa)), wr = A.want_raw ? warp_sum(static_cast<double>(sr)) : 0.0;
+    if (lane == 0) {
+      s_wsum[warp] = ws;
+      s_wraw[warp] = wr;
+    }
   }
+  if (__any_sync(kFullMask, bad) && lane == 0) atomicOr(&s_wbad, 1u);
+  __syncthreads();
   kk = s_wkey[0];
 #pragma unroll
   for (int w = 1; w < kStepWarps; ++w) kk = min(kk, s_wkey[w]);
+  // the record keeps every pack whose key reaches the bound (at most kStepRecPacks·k2; a copy
+  // stays in shared memory for the head)
   unsigned char* rec = rec_row + static_cast<int64_t>(unit) * A.rec_bytes;
   unsigned long long* rpk = reinterpret_cast<unsigned long long*>(rec + sizeof(StepRec));
   const int cap_rec = kStepRecPacks * K2;
@@ -359,10 +352,47 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     int at = 0;
     if (lane == leader) at = atomicAdd(&s_n, __popc(bal));
     at = __shfl_sync(kFullMask, at, leader) + __popc(bal & ((1u << lane) - 1u));
-    if (take && at < cap_rec) rpk[at] = v[q];
+    if (take && at < cap_rec) {
+      rpk[at] = v[q];
+      spk[at] = v[q];
+    }
   }
   __syncthreads();
   int n_rec = s_n;
+  // the head: the best four of the record (the unit's best four when it holds four or more:
+  // they all reach the bound then), by warp 0
+  if (warp == 0 && n_rec <= cap_rec) {
+    unsigned long long cur[kStepHead] = {0ull, 0ull, 0ull, 0ull};  // (the same in every lane)
+    for (int b0 = 0; b0 < n_rec; b0 += 128) {
+      unsigned long long hv[4], h[kStepHead];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int i = b0 + q * 32 + lane;
+        hv[q] = i < n_rec ? spk[i] : 0ull;
+      }
+      warp_head(hv, 4, h);
+      // the best four of two descending lists of four: the larger of cur[i] and h[3 - i]
+      // (a bitonic sequence), then a sorting network
+#pragma unroll
+      for (int i = 0; i < kStepHead; ++i) cur[i] = cur[i] > h[kStepHead - 1 - i] ? cur[i] : h[kStepHead - 1 - i];
+      auto cs = [](unsigned long long& x, unsigned long long& y) {
+        if (x < y) {
+          const unsigned long long t = x;
+          x = y;
+          y = t;
+        }
+      };
+      cs(cur[0], cur[2]);
+      cs(cur[1], cur[3]);
+      cs(cur[0], cur[1]);
+      cs(cur[2], cur[3]);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < kStepHead; ++i) s_head[i] = cur[i];
+    }
+    __syncwarp();
+  }
   if (n_rec > cap_rec) {
     // ties at the bound beyond the record: the unit's exact k2 best, sorted (each warp
     // sorts its 128 packs, then the lists merge pairwise)
@@ -383,16 +413,23 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       lb = t;
     }
     for (int i = tid; i < K2; i += kStepThreads) rpk[i] = la[i];
+    if (tid < kStepHead) s_head[tid] = tid < K2 ? la[tid] : 0ull;
     n_rec = K2;
+    __syncthreads();
   }
 
   // ---- 3. the record, then a ticket ----
   if (tid == 0) {
+    double su = 0.0, ru = 0.0;
+    for (int w = 0; w < kStepWarps; ++w) {
+      su = __dadd_rn(su, s_wsum[w]);
+      ru = __dadd_rn(ru, s_wraw[w]);
+    }
     StepRec r{};
     r.m = m;
-    r.s = m > -INFINITY ? s_unit : 0.0;
-    r.raw_s = m > -INFINITY ? r_unit : 0.0;
-    r.flags = bad ? GS_FLAG_ERR_NONFINITE : 0u;
+    r.s = m > -INFINITY ? su : 0.0;
+    r.raw_s = m > -INFINITY ? ru : 0.0;
+    r.flags = s_wbad ? GS_FLAG_ERR_NONFINITE : 0u;
 #pragma unroll
     for (int i = 0; i < kStepHead; ++i) r.head[i] = s_head[i];
     r.n = n_rec;
@@ -404,16 +441,24 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  if (tid == kStepThreads - 1 && !greedy) {  // the draw's uniform, early (its load overlaps the records')
+    if (A.uniforms) {
+      s_r = A.uniforms[row];
+    } else {
+      double st = A.rng_state[row];
+      s_r = seeded_next(&st);
+      s_st = st;
+    }
+  }
 
-  // ---- 4. the last CTA of the row: statistics (one unit per thread), the bound, the
-  //      packs at or above it ----
-  unsigned long long* umax = reinterpret_cast<unsigned long long*>(dsm);  // [kStepMaxUnits] each unit's best pack
-  int* un = reinterpret_cast<int*>(umax + kStepMaxUnits);                 // [kStepMaxUnits] its packs
-  int* qlist = un + kStepMaxUnits;                                        // [kStepMaxUnits] units that reach the bound
+  // ---- 4. the last CTA of the row: one unit's record per thread; the bound; the
+  //      candidates ----
+  unsigned char* wwork = dsm;                                   // [4096] the warp filters' work
+  int* un = reinterpret_cast<int*>(dsm + 4096);                 // [kStepMaxUnits] record sizes
+  int* qlist = un + kStepMaxUnits;                              // [kStepMaxUnits] units read in full
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(qlist + kStepMaxUnits);  // [kStepSortSmem]
   unsigned long long* srt = cand + kStepSortSmem;                                          // [kStepSortSmem]
   unsigned long long* scratch = A.sort_scratch + static_cast<int64_t>(row) * kStepMaxPacks;
-  unsigned fl = 0;
   float mu = -INFINITY;
   double su = 0.0, ru = 0.0;
   unsigned long long hd[kStepHead] = {0ull, 0ull, 0ull, 0ull};
@@ -422,55 +467,71 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     mu = __ldcg(&st->m);
     su = __ldcg(&st->s);
     ru = __ldcg(&st->raw_s);
-    fl = __ldcg(&st->flags);
+    const unsigned f = __ldcg(&st->flags);
 #pragma unroll
     for (int i = 0; i < kStepHead; ++i) hd[i] = __ldcg(&st->head[i]);
-    umax[tid] = hd[0];
     un[tid] = __ldcg(&st->n);
+    if (f) atomicOr(&s_flags, f);
   }
-  if (fl) atomicOr(&s_flags, fl);
   if (tid == 0) {
     s_n = 0;
     s_nq = 0;
-    s_tau = 0ull;
-    s_top = 0ull;
   }
-  const float Mx = block_max_f(mu, red_f);  // the raw maximum too (every id is live)
-  // the bound: the units' bests in groups of 32, each group sorted by one warp; with g
-  // groups, the least of the groups' c-th largest (c = ceil(k / g)) has g·c >= k unit bests
-  // at or above it (none when a group holds fewer than c, or c > 32)
-  {
-    const int g = (S + 31) >> 5, c = (k + g - 1) / g;
-    if (warp < g) {
-      const int u = warp * 32 + lane;
-      unsigned long long b = u < S ? umax[u] : 0ull;
+  // the bound: the units' best keys in groups of 32, each group sorted by one warp; with g
+  // groups, the least of the groups' c-th largest key (c = ceil(k / g)) has g·c >= k unit
+  // bests at or above it (none when c > 32 or a group holds fewer than c)
+  const int g = (S + 31) >> 5, cg = (k + g - 1) / g;
+  if (warp < g) {
+    const unsigned long long b = hd[0];  // (thread u holds unit u's record)
+    uint32_t key = static_cast<uint32_t>(b >> 32);
 #pragma unroll
-      for (int kw = 2; kw <= 32; kw <<= 1) {
+    for (int kw = 2; kw <= 32; kw <<= 1) {
 #pragma unroll
-        for (int j = kw >> 1; j > 0; j >>= 1) {
-          const unsigned long long p = __shfl_xor_sync(kFullMask, b, j);
-          b = ((lane & j) == 0) == ((lane & kw) == 0) ? (b > p ? b : p) : (b > p ? p : b);
-        }
-      }
-      if (lane == 0 && b) atomicMax(&s_top, b);
-      if (c <= 32) {
-        const unsigned long long t = __shfl_sync(kFullMask, b, c - 1);
-        if (lane == 0) s_wtau[warp] = t;
+      for (int j = kw >> 1; j > 0; j >>= 1) {
+        const uint32_t p = __shfl_xor_sync(kFullMask, key, j);
+        key = ((lane & j) == 0) == ((lane & kw) == 0) ? max(key, p) : min(key, p);
       }
     }
-    __syncthreads();
-    if (tid == 0 && c <= 32) {
-      unsigned long long t = s_wtau[0];
-      for (int w = 1; w < g; ++w) t = s_wtau[w] < t ? s_wtau[w] : t;
-      s_tau = t;
+    unsigned long long wt = b;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(kFullMask, wt, o);
+      wt = t > wt ? t : wt;
+    }
+    const uint32_t kc = __shfl_sync(kFullMask, key, cg <= 32 ? cg - 1 : 0);
+    if (lane == 0) {
+      s_wkey[warp] = cg <= 32 ? kc : 0u;
+      s_gtop[warp] = wt;
     }
   }
   __syncthreads();
-  fl = s_flags;
+  uint32_t tk = s_wkey[0];
+  unsigned long long top = s_gtop[0];
+  for (int w = 1; w < g; ++w) {
+    tk = min(tk, s_wkey[w]);
+    top = s_gtop[w] > top ? s_gtop[w] : top;
+  }
+  unsigned fl = s_flags;
   if (greedy) fl |= GS_FLAG_GREEDY;
-  const unsigned long long tau = s_tau;
-  // each unit's head packs at or above the bound; a unit whose whole head reaches it may
-  // hold more such packs: its record is read in full instead (below)
+  const double T = pp->temperature;
+  const float Mx = pack_value(top);  // the row's maximum (raw maximum too: every id is live)
+  const double xtop = static_cast<double>(Mx);
+  const double M = greedy ? xtop : __ddiv_rn(xtop, T);
+  // per unit: the normaliser's and the raw sum's terms; its head packs whose key reaches the
+  // bound, or, when its whole head does (it may hold more), the unit for a full read
+  {
+    double part = 0.0, rpart = 0.0;
+    if (tid < S && mu > -INFINITY) {
+      if (!greedy && M > -INFINITY) part = __dmul_rn(su, exp(__dsub_rn(__ddiv_rn(static_cast<double>(mu), T), M)));
+      if (A.want_raw) rpart = __dmul_rn(ru, exp(static_cast<double>(mu) - static_cast<double>(Mx)));
+    }
+    part = warp_sum(part);
+    rpart = warp_sum(rpart);
+    if (lane == 0) {
+      s_wsum[warp] = part;
+      s_wraw[warp] = rpart;
+    }
+  }
   auto append = [&](bool take, unsigned long long p) {
     const unsigned bal = __ballot_sync(kFullMask, take);
     if (!bal) return;
@@ -483,25 +544,30 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       if (at < kStepMaxPacks) scratch[at] = p;
     }
   };
-  for (int u0 = 0; u0 < S; u0 += kStepThreads) {  // (one round: S <= the block's threads)
-    const int u = u0 + tid;
-    const bool over = u < S && hd[kStepHead - 1] != 0ull && hd[kStepHead - 1] >= tau;
+  auto reaches = [&](unsigned long long p) { return p != 0ull && static_cast<uint32_t>(p >> 32) >= tk; };
+  {
+    const bool over = tid < S && reaches(hd[kStepHead - 1]);
 #pragma unroll
-    for (int i = 0; i < kStepHead; ++i) append(u < S && !over && hd[i] != 0ull && hd[i] >= tau, hd[i]);
+    for (int i = 0; i < kStepHead; ++i) append(tid < S && !over && reaches(hd[i]), hd[i]);
     const unsigned bal = __ballot_sync(kFullMask, over);
     if (bal) {
       const int leader = __ffs(bal) - 1;
       int at = 0;
       if (lane == leader) at = atomicAdd(&s_nq, __popc(bal));
       at = __shfl_sync(kFullMask, at, leader) + __popc(bal & ((1u << lane) - 1u));
-      if (over) qlist[at] = u;
+      if (over) qlist[at] = tid;
     }
   }
   __syncthreads();
+  double total = 0.0, rs = 0.0;
+  for (int w = 0; w < kStepWarps; ++w) {
+    total = __dadd_rn(total, s_wsum[w]);
+    rs = __dadd_rn(rs, s_wraw[w]);
+  }
   const int nq = s_nq;
-  // their packs, flattened (an exclusive prefix of their counts), four loads per thread
-  // in flight; the packs at or above the bound are appended in no order
-  {
+  if (nq > 0) {
+    // the full records of those units, flattened (an exclusive prefix of their sizes), four
+    // loads per thread in flight
     const int cu = tid < nq ? un[qlist[tid]] : 0;
     int incl = cu;
     for (int o = 1; o < 32; o <<= 1) {
@@ -518,32 +584,31 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     if (tid < nq) s_pre[tid] = before + incl - cu;
     if (tid == 0) s_pre[nq] = tot;
     __syncthreads();
-  }
-  const int P = s_pre[nq];
-  for (int f0 = 0; f0 < P; f0 += 4 * kStepThreads) {
-    unsigned long long p[4];
+    const int P = s_pre[nq];
+    for (int f0 = 0; f0 < P; f0 += 4 * kStepThreads) {
+      unsigned long long p[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int f = f0 + q * kStepThreads + tid;
-      p[q] = 0ull;
-      if (f < P) {
-        int lo = 0, hi = nq - 1;  // the last qi with s_pre[qi] <= f
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (s_pre[mid] <= f) lo = mid;
-          else hi = mid - 1;
+      for (int q = 0; q < 4; ++q) {
+        const int f = f0 + q * kStepThreads + tid;
+        p[q] = 0ull;
+        if (f < P) {
+          int lo = 0, hi = nq - 1;  // the last qi with s_pre[qi] <= f
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_pre[mid] <= f) lo = mid;
+            else hi = mid - 1;
+          }
+          p[q] = __ldcg(reinterpret_cast<const unsigned long long*>(rec_row + static_cast<int64_t>(qlist[lo]) * A.rec_bytes +
+                                                                     sizeof(StepRec)) + (f - s_pre[lo]));
         }
-        const int u = qlist[lo];
-        p[q] = __ldcg(reinterpret_cast<const unsigned long long*>(rec_row + static_cast<int64_t>(u) * A.rec_bytes +
-                                                                   sizeof(StepRec)) + (f - s_pre[lo]));
       }
-    }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) append(p[q] != 0ull && p[q] >= tau, p[q]);
+      for (int q = 0; q < 4; ++q) append(reaches(p[q]), p[q]);
+    }
+    __syncthreads();
   }
-  __syncthreads();
   const int N = s_n < kStepMaxPacks ? s_n : kStepMaxPacks;
-  unsigned long long best[4] = {0ull, 0ull, 0ull, 0ull};  // warp 0: the row's best packs, lane·4 + q
+  const unsigned long long* sorted;
   if (N <= 512) {
     // exact order by rank counting (the packs are distinct)
     for (int i = tid; i < N; i += kStepThreads) {
@@ -552,42 +617,23 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       for (int j = 0; j < N; ++j) r += cand[j] > p;
       srt[r] = p;
     }
-    __syncthreads();
-    if (warp == 0) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) best[q] = lane * 4 + q < N ? srt[lane * 4 + q] : 0ull;
-    }
+    sorted = srt;
   } else {
     unsigned long long* cbuf = N <= kStepSortSmem ? cand : scratch;
     const int n2 = pow2_ceil(N);
     for (int i = N + tid; i < n2; i += kStepThreads) cbuf[i] = 0ull;
     __syncthreads();
     block_sort_desc(cbuf, n2);
-    if (warp == 0) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) best[q] = lane * 4 + q < N ? cbuf[lane * 4 + q] : 0ull;
-    }
+    sorted = cbuf;
   }
-  // the full-vocabulary normaliser relative to the best key M (the best pack is the
-  // largest unit maximum) and the raw sum, one unit per thread
-  const unsigned long long top = s_top;
-  const double T = pp->temperature;
-  const double xtop = static_cast<double>(pack_value(top));
-  const double M = greedy ? xtop : __ddiv_rn(xtop, T);
-  double part = 0.0, rpart = 0.0;
-  if (tid < S && mu > -INFINITY) {
-    if (!greedy && M > -INFINITY) part = __dmul_rn(su, exp(__dsub_rn(__ddiv_rn(static_cast<double>(mu), T), M)));
-    if (A.want_raw) rpart = __dmul_rn(ru, exp(static_cast<double>(mu) - static_cast<double>(Mx)));
-  }
-  const double total = block_sum_d(part, red_d);
-  const double rs = A.want_raw ? block_sum_d(rpart, red_d) : 0.0;
+  __syncthreads();
   if (warp != 0) return;
 
   // ---- 5. one warp: probabilities, filters, draw, outputs ----
   const int nC = N < k ? N : k;
   WWork w;
   {
-    unsigned char* p = reinterpret_cast<unsigned char*>(cand);  // (the candidates now sit in registers)
+    unsigned char* p = wwork;
     const int kc2 = K2;
     w.cp = reinterpret_cast<double*>(p);
     p += kc2 * 8;
@@ -619,22 +665,17 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
         fl |= GS_FLAG_ERR_NONFINITE;  // every logit -inf: outside the domain
       } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int i = lane * 4 + q;
+        for (int q = 0; q < kStepMaxK / 32; ++q) {  // (independent chains)
+          const int i = q * 32 + lane;
           if (i < nC) {
-            const double key = __ddiv_rn(static_cast<double>(pack_value(best[q])), T);
-            w.cid[i] = pack_id(best[q]);
+            const unsigned long long pk = sorted[i];
+            const double key = __ddiv_rn(static_cast<double>(pack_value(pk)), T);
+            w.cid[i] = pack_id(pk);
             w.cp[i] = __ddiv_rn(exp(__dsub_rn(key, M)), total);
           }
         }
-        double r;
-        if (A.uniforms) {
-          r = A.uniforms[row];
-        } else {
-          double st = A.rng_state[row];
-          r = seeded_next(&st);
-          if (lane == 0) A.rng_state[row] = st;
-        }
+        const double r = s_r;
+        if (!A.uniforms && lane == 0) A.rng_state[row] = s_st;
         __syncwarp();
         if (!(pp->min_p > 0) && !(pp->typical_p < 1)) {
           // top-p and the draw only: the draw's running sums over the kept prefix are the
