@@ -4,18 +4,22 @@
 //
 // One CTA per 2048-id unit of a row (512 threads, four ids each, one 16-byte load):
 //   1. the unit's soft-capped logits, their maximum m and the sums of 2^((x - m)·log2e/T)
-//      and e^(x - m) (block reductions in a fixed order);
-//   2. the unit's best packs (key32(x) << 32 | ~id: logit descending, lower id first):
-//      each warp sorts its 128 packs in registers (a bitonic network over the lanes), and
-//      the sixteen sorted lists are merged pairwise down to the unit's k2 best, sorted;
-//   3. the unit's record (statistics and sorted packs) goes to the workspace and the CTA
-//      takes a ticket from the row's counter; the last CTA of the row merges the records:
-//      the k-th largest unit maximum bounds the row's k-th best pack (k units hold a
-//      pack at or above it), so only each unit's packs at or above that bound are read
-//      (a handful per row) and sorted; then the maximum, the full-vocabulary normaliser,
-//      probabilities, min-p, typical-p, top-p and the seeded draw run in one warp
-//      (gs_warp_filter.cuh, the warp merge's code), and the counter is reset for the next
-//      call.
+//      and e^(x - m);
+//   2. a bound on the unit's k-th best key: each warp sorts its threads' best keys, and
+//      the least of the warps' ceil(k/16)-th largest has 16·ceil(k/16) >= k threads, so
+//      at least k values, at or above it.  Every pack (key32(x) << 32 | ~id: logit
+//      descending, lower id first) at or above it goes to the unit's record, in no
+//      order; warp 0 takes the record's best four (the head).  More ties at the bound
+//      than the record holds: the unit's exact k2 best instead (warps sort their packs in
+//      registers, the sixteen lists merge pairwise);
+//   3. a release fence and a ticket on the row's counter; the last CTA of the row merges:
+//      one record per thread, a bound on the row's k-th best pack (units' bests in groups
+//      of 32, the least of the groups' ceil(k/g)-th largest), each unit's head packs at
+//      or above it (a unit whose whole head reaches the bound is read in full), exact
+//      order by rank counting; then one warp computes the probabilities and runs min-p,
+//      typical-p, top-p and the seeded draw (gs_warp_filter.cuh, the warp merge's code;
+//      one prefix scan when only top-p and the draw apply), writes the outputs and resets
+//      the counter for the next call.
 // The merge's arithmetic is the other merges' (same double operations, same order of the
 // filters' prefix sums); only the order in which the normaliser's unit terms are added
 // differs (a few ulp, far inside the 1e-6 parity bar).

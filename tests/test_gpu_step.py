@@ -1,14 +1,15 @@
 """The single-launch decode step (csrc/gs_step.cu) against the oracle.
 
 Batches of at most eight rows without a constraint table or a penalty history, whose
-rows all have topK <= 64 (or temperature 0), run as one kernel: each 2048-id unit sorts
-its best packs, and the last unit of a row to finish merges the units' records (only the
-packs at or above the k-th largest unit maximum), then filters and draws in one warp.
-The cases put the row's best values in one unit, across units, in exact ties and in the
-partial last unit, and a unit tied throughout (its record then holds its exact best);
-they cover greedy rows, topK 1..64, min-p, typical-p, top-p, the soft
-cap on and off, -inf logits, bf16, log-probabilities, and calls whose row counts change
-from call to call (each row's counter is reset by its last unit)."""
+rows all have topK <= 64 (or temperature 0), run as one kernel: each 2048-id unit keeps
+its packs at or above a bound on its k-th best (and its best four), and the last unit of
+a row to finish merges the records above a bound on the row's k-th best, then filters
+and draws in one warp.  The cases put the row's best values in one unit, across units,
+in exact ties and in the partial last unit, and a unit tied throughout (more ties at its
+bound than its record holds: its exact best instead); they cover greedy rows, topK
+1..64, min-p, typical-p, top-p, the soft cap on and off, -inf logits, bf16,
+log-probabilities, and calls whose row counts change from call to call (each row's
+counter is reset by its last unit)."""
 from __future__ import annotations
 
 import importlib
