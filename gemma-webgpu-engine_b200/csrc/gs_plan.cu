@@ -83,10 +83,16 @@ gs_status check_batch(const gs_batch* b, const gs_outputs* o, std::string* err, 
 gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::string* err) {
   const int rows = b->rows;
   const int kmax = ps.kmax;
-  // Vocabulary splits.  The warp-per-unit streaming kernel (small topK, aligned rows)
-  // wants about four units per warp of the GPU, chunks of 2048..65536 ids; the general
-  // kernel wants about four CTAs per SM and chunks of >= 4096 ids.  Both keep at most
-  // 16384 streamed candidates per row for the merge.
+  // Vocabulary splits.  The warp-per-unit streaming kernels (small topK, aligned rows)
+  // want one wave of units: the most units per row (a power of two) that keep the batch
+  // within the GPU's warp slots (16 per SM), since a unit has fixed costs (its penalised
+  // list, the first sub-tile's threshold, its candidate list and statistics) that longer
+  // units spread.  (Measured at C3's 256 masked rows: 8 units a row 139 us a step, 64 units
+  // 201 us; C4's 4096 rows: one unit a row 773 us, four 827 us.)  A unit keeps at most 256
+  // penalised ids in its sorted list (more: a per-tile scan of the history), so a history
+  // of more than 256 ids is spread at about 128 ids a unit.  The general kernel wants
+  // about four CTAs per SM and chunks of >= 4096 ids.  Both keep at most 16384 streamed
+  // candidates per row for the merge.
   const int64_t V = b->vocab;
   const int esz = b->dtype == GS_DTYPE_F32 ? 4 : 2;
   const bool aligned = (reinterpret_cast<uintptr_t>(b->logits) & 15) == 0 && ((b->row_stride * esz) & 15) == 0 &&
@@ -98,16 +104,20 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  const int target_units = warp_kernel ? sms * 16 * 4 : sms * 4;
   const int64_t min_chunk = warp_kernel ? 2048 : 4096;
   const int64_t granule = warp_kernel ? 1024 : 4096;
+  auto can_split = [&](int s) { return V / (2 * s) >= min_chunk && 2 * s * std::max(kmax, 1) <= 16384 && s < 1024; };
   int S = 1;
-  while (static_cast<int64_t>(rows) * S < target_units && V / (2 * S) >= min_chunk && 2 * S * std::max(kmax, 1) <= 16384 &&
-         S < 1024)
-    S *= 2;
   if (warp_kernel) {
+    const int64_t slots = static_cast<int64_t>(sms) * 16;
+    while (static_cast<int64_t>(rows) * S * 2 <= slots && can_split(S)) S *= 2;
+    const int64_t hs = b->history ? b->history_stride : 0;
+    if (hs > 256)
+      while (hs > 128 * static_cast<int64_t>(S) && can_split(S)) S *= 2;
     const int64_t need = (V + pipe_max_chunk() - 1) / pipe_max_chunk();
     while (S < need) S *= 2;
+  } else {
+    while (static_cast<int64_t>(rows) * S < static_cast<int64_t>(sms) * 4 && can_split(S)) S *= 2;
   }
   int64_t chunk = (V + S - 1) / S;
   chunk = (chunk + granule - 1) / granule * granule;
