@@ -66,7 +66,7 @@ constexpr int kMaxRanges = 12;         // bin ranges the select kernel marks per
 constexpr int kSortSmem = 2048;        // typical-p: annulus entries sorted in shared memory
 constexpr float kMaxDelta = 0.0105f;   // bin width (40/4096 key units) plus slack
 constexpr size_t kSelUnion = (static_cast<size_t>(kNB + 1) * 12 + 15) / 16 * 16;  // select: start of its union
-static_assert(kNB / kCluster == kHistThreads, "one reduced bin per thread and cluster rank");
+static_assert(kNB / kCluster == kHistThreads, "one reduced bin per thread and cluster rank (512-thread CTAs)");
 static_assert(kNB == 4 * kSelectThreads && kNB == 4 * kResolveThreads, "four bins per thread");
 
 // Per-row header shared by the four kernels (256-byte slot).
@@ -354,11 +354,15 @@ size_t large_select_smem_bytes(int64_t history_stride) {
 // MOM: some row of the batch has typical-p; those rows also sum, per bin, the first moment
 // r = round(dl·e^-dl·2^qbits) of their values (dl: the value's key distance below its
 // bin's top), kept in a second dynamic shared-memory array after the queue.
-template <int DT, bool RAW, bool MOM>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads, kHistMinBlocks)
+// TPB: threads per CTA.  512 (three CTAs per SM) with the queue, for batches with a
+// constraint table (sparse chunks); 256 (six per SM, no queue) otherwise, so that a
+// batch's 8-CTA clusters fit in one wave.
+template <int DT, bool RAW, bool MOM, int TPB>
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(TPB, TPB == kHistThreads ? kHistMinBlocks : 2 * kHistMinBlocks)
     large_hist_kernel(const __grid_constant__ FinalizeArgs A) {
-  __shared__ uint32_t cnt[kNB];
-  __shared__ uint32_t qs[kNB];
+  constexpr bool kQueue = TPB == kHistThreads;
+  static_assert((kNB / kCluster) % TPB == 0, "whole bins per thread in the cluster reduction");
+  __shared__ unsigned long long cq[kNB];  // per bin: count << 32 | sum of q
   __shared__ uint32_t live[kHistSub / 32];
   __shared__ float red_f[32];
   __shared__ int red_i[32];
@@ -374,7 +378,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   const RowWs W = row_ws(A, row);
   const double T = pp->temperature;
   const float invT = static_cast<float>(1.0 / T);
-  uint32_t* rsum_bins = reinterpret_cast<uint32_t*>(queue + kHistQueue);  // [kNB] (MOM launches)
+  uint32_t* rsum_bins = reinterpret_cast<uint32_t*>(queue + (kQueue ? kHistQueue : 0));  // [kNB] (MOM launches)
   const bool mom = MOM && pp->typical_p < 1;  // (the whole cluster: one row)
   const float a2_hi = pp->a2_hi, a2_lo = pp->a2_lo;
   const float qmul = static_cast<float>(ldexp(1.0, q_bits(A.vocab)));
@@ -407,7 +411,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     const unsigned char* base = rowbase + (lo + s0) * ESZ;
     __syncthreads();
     build_live(live, mrow, lo + s0, sn, hrow, hl, tid, bs, &nallow);
-    if (!RAW && one_pass_bits) {
+    if (!RAW && one_pass_bits && kQueue) {
       // each thread takes a run of live words; their values land at its scan offset
       const int words = (sn + 31) >> 5;
       const int wpt = (words + bs - 1) / bs;
@@ -518,8 +522,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     s_max[4] = lmin;
   }
   for (int b = tid; b < kNB; b += bs) {
-    cnt[b] = 0;
-    qs[b] = 0;
+    cq[b] = 0ull;
     if (mom) rsum_bins[b] = 0;
   }
   cl.sync();
@@ -580,14 +583,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
     const float2 om = __fmul2_rn(__fmul2_rn(dl, h), make_float2(qmul, qmul));
     const uint32_t q0 = b0 < kNB - 1 ? __float2uint_rn(om.x) : 0u;
     const uint32_t q1 = b1 < kNB - 1 ? __float2uint_rn(om.y) : 0u;
-    if (l0) {
-      atomicAdd(&cnt[b0], 1u);
-      if (q0) atomicAdd(&qs[b0], q0);
-    }
-    if (l1) {
-      atomicAdd(&cnt[b1], 1u);
-      if (q1) atomicAdd(&qs[b1], q1);
-    }
+    // (a CTA's sum of q stays below 2^32: no carry into the count)
+    if (l0) atomicAdd(&cq[b0], (1ull << 32) | q0);
+    if (l1) atomicAdd(&cq[b1], (1ull << 32) | q1);
     if (mom) {
       // dl·e^-dl = dl - dl·(1 - e^-dl)
       const float2 rm = __fmul2_rn(__ffma2_rn(make_float2(-dl.x, -dl.y), __fmul2_rn(dl, h), dl), make_float2(qmul, qmul));
@@ -678,21 +676,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kHistThreads,
   }
   cl.sync();
   {
-    const int b = rank * kHistThreads + tid;
-    uint32_t c = 0;
-    unsigned long long q = 0;
+    for (int b = rank * (kNB / kCluster) + tid; b < (rank + 1) * (kNB / kCluster); b += TPB) {
+      uint32_t c = 0;
+      unsigned long long q = 0;
 #pragma unroll
-    for (int r = 0; r < kCluster; ++r) {
-      c += cl.map_shared_rank(cnt, r)[b];
-      q += cl.map_shared_rank(qs, r)[b];
-    }
-    W.cpre[b] = c;
-    reinterpret_cast<unsigned long long*>(W.ppre)[b] = q;
-    if (mom) {
-      unsigned long long r1 = 0;
+      for (int r = 0; r < kCluster; ++r) {
+        const unsigned long long v = cl.map_shared_rank(cq, r)[b];
+        c += static_cast<uint32_t>(v >> 32);
+        q += v & 0xffffffffull;
+      }
+      W.cpre[b] = c;
+      reinterpret_cast<unsigned long long*>(W.ppre)[b] = q;
+      if (mom) {
+        unsigned long long r1 = 0;
 #pragma unroll
-      for (int r = 0; r < kCluster; ++r) r1 += cl.map_shared_rank(rsum_bins, r)[b];
-      reinterpret_cast<unsigned long long*>(W.m1pre)[b] = r1;
+        for (int r = 0; r < kCluster; ++r) r1 += cl.map_shared_rank(rsum_bins, r)[b];
+        reinterpret_cast<unsigned long long*>(W.m1pre)[b] = r1;
+      }
     }
   }
   cl.sync();  // every CTA keeps its shared memory until its peers have read it
@@ -907,6 +907,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   //      penalised entries (fixed point, so that their sums are order-independent) ----
   const float Mx = mx, scale = W.hdr->bscale, width = W.hdr->bwidth;
   const double qunit = ldexp(1.0, -q_bits(V));
+  const double inv_total = 1.0 / total, invT = 1.0 / T;  // (binned values: products suffice)
   unsigned long long* pfix = reinterpret_cast<unsigned long long*>(un);  // (the hash table is done)
   unsigned long long* pm1 = pfix + kNB;                                // penalised first moments
   uint32_t* pcnt = reinterpret_cast<uint32_t*>(pm1 + kNB);
@@ -917,7 +918,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
     double m = 0.0, m1v = 0.0;
     if (c && b < kNB - 1) {
       const double top = __dsub_rn(
-          __ddiv_rn(__dsub_rn(static_cast<double>(Mx), static_cast<double>(b) * static_cast<double>(width)), T), M);
+          __dmul_rn(__dsub_rn(static_cast<double>(Mx), static_cast<double>(b) * static_cast<double>(width)), invT), M);
       const double et = exp(top), se = __dsub_rn(static_cast<double>(c), static_cast<double>(q) * qunit);
       m = __dmul_rn(et, se);
       // first moment, sum of e^(key - M)·(M - key) = e^top·((-top)·sum e^-dl + sum dl·e^-dl)
@@ -1004,7 +1005,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   }
   for (int b = tid; b <= kNB; b += bs) {
     W.cpre[b] = cnt[b];
-    W.ppre[b] = __ddiv_rn(md[b], total);
+    W.ppre[b] = __dmul_rn(md[b], inv_total);  // (bin choice and walk bases: binned values)
   }
   double* m1 = reinterpret_cast<double*>(pfix);  // (pfix was read by the mass prefix)
   if (typ) {
@@ -1023,7 +1024,7 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   // within the slack of those edges (where the exact running sum could fall on either
   // side) are added while the list stays within the gather capacity.
   if (tid == 0) {
-    auto P = [&](int b) { return __ddiv_rn(md[b], total); };
+    auto P = [&](int b) { return __dmul_rn(md[b], inv_total); };
     auto bstart = [&](double t) {  // first bin b with P(b + 1) >= t, kNB if none
       int l = 0, h = kNB;
       while (l < h) {
@@ -1259,24 +1260,24 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
   // bitmap of the selected bins and its entry count; the candidate range goes in last,
   // and only when the total stays within the gather capacity
   const int nr = s_nr;
+  // the bits of bins [a, b] within word w
+  auto word_bits = [](int w, int a, int b) -> uint32_t {
+    const int lo = a > w * 32 ? a : w * 32, hi = b < w * 32 + 31 ? b : w * 32 + 31;
+    if (lo > hi) return 0u;
+    return static_cast<uint32_t>(((1ull << (hi - lo + 1)) - 1ull) << (lo - w * 32));
+  };
   auto mark = [&](bool with_cand) {
     int cntsel = 0;
     for (int w = tid; w < kNB / 32; w += bs) {
       uint32_t m = 0;
-      for (int r = 0; r < nr; ++r) {
-        const int a = s_rng[0][r], b = s_rng[1][r];
-        for (int i = 0; i < 32; ++i) {
-          const int bin = w * 32 + i;
-          if (bin >= a && bin <= b) m |= 1u << i;
-        }
-      }
-      if (with_cand && s_cb >= 0)
-        for (int i = 0; i < 32; ++i)
-          if (w * 32 + i >= s_cb0 && w * 32 + i <= s_cb) m |= 1u << i;
+      for (int r = 0; r < nr; ++r) m |= word_bits(w, s_rng[0][r], s_rng[1][r]);
+      if (with_cand && s_cb >= 0) m |= word_bits(w, s_cb0, s_cb);
       W.sel[w] = m;
       W.sel2[w] = 0u;
-      for (int i = 0; i < 32; ++i)
-        if ((m >> i) & 1u) cntsel += static_cast<int>(cnt[w * 32 + i + 1] - cnt[w * 32 + i]);
+      for (uint32_t t = m; t; t &= t - 1u) {
+        const int bin = w * 32 + __ffs(t) - 1;
+        cntsel += static_cast<int>(cnt[bin + 1] - cnt[bin]);
+      }
     }
     return block_sum_i(cntsel, red_i);
   };
@@ -2111,23 +2112,39 @@ cudaError_t launch_large_t(const FinalizeArgs& a, int rows, size_t select_smem, 
     set_smem(large_resolve_kernel<DT, 0>, res_smem);
     set_smem(large_resolve_kernel<DT, 1>, res_smem);
     const size_t q = static_cast<size_t>(kHistQueue) * sizeof(float), qm = q + static_cast<size_t>(kNB) * 4;
-    set_smem(large_hist_kernel<DT, false, false>, q);
-    set_smem(large_hist_kernel<DT, true, false>, q);
-    set_smem(large_hist_kernel<DT, false, true>, qm);
-    set_smem(large_hist_kernel<DT, true, true>, qm);
+    const size_t m = static_cast<size_t>(kNB) * 4;
+    set_smem(large_hist_kernel<DT, false, false, kHistThreads>, q);
+    set_smem(large_hist_kernel<DT, true, false, kHistThreads>, q);
+    set_smem(large_hist_kernel<DT, false, true, kHistThreads>, qm);
+    set_smem(large_hist_kernel<DT, true, true, kHistThreads>, qm);
+    set_smem(large_hist_kernel<DT, false, false, kHistThreads / 2>, 0);
+    set_smem(large_hist_kernel<DT, true, false, kHistThreads / 2>, 0);
+    set_smem(large_hist_kernel<DT, false, true, kHistThreads / 2>, m);
+    set_smem(large_hist_kernel<DT, true, true, kHistThreads / 2>, m);
     attr = true;
   }
-  const size_t hq_smem = static_cast<size_t>(kHistQueue) * sizeof(float);
-  const size_t hm_smem = hq_smem + static_cast<size_t>(kNB) * 4;
-  if (a.lmoments) {
-    if (a.want_raw)
-      large_hist_kernel<DT, true, true><<<rows * kCluster, kHistThreads, hm_smem, st>>>(a);
-    else
-      large_hist_kernel<DT, false, true><<<rows * kCluster, kHistThreads, hm_smem, st>>>(a);
-  } else if (a.want_raw) {
-    large_hist_kernel<DT, true, false><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
+  const int grid = rows * kCluster;
+  if (a.mask_table) {  // sparse chunks: 512-thread CTAs with the queue
+    const size_t hq = static_cast<size_t>(kHistQueue) * sizeof(float) + (a.lmoments ? static_cast<size_t>(kNB) * 4 : 0);
+    if (a.lmoments) {
+      if (a.want_raw) large_hist_kernel<DT, true, true, kHistThreads><<<grid, kHistThreads, hq, st>>>(a);
+      else large_hist_kernel<DT, false, true, kHistThreads><<<grid, kHistThreads, hq, st>>>(a);
+    } else if (a.want_raw) {
+      large_hist_kernel<DT, true, false, kHistThreads><<<grid, kHistThreads, hq, st>>>(a);
+    } else {
+      large_hist_kernel<DT, false, false, kHistThreads><<<grid, kHistThreads, hq, st>>>(a);
+    }
   } else {
-    large_hist_kernel<DT, false, false><<<rows * kCluster, kHistThreads, hq_smem, st>>>(a);
+    constexpr int T2 = kHistThreads / 2;
+    const size_t hm = a.lmoments ? static_cast<size_t>(kNB) * 4 : 0;
+    if (a.lmoments) {
+      if (a.want_raw) large_hist_kernel<DT, true, true, T2><<<grid, T2, hm, st>>>(a);
+      else large_hist_kernel<DT, false, true, T2><<<grid, T2, hm, st>>>(a);
+    } else if (a.want_raw) {
+      large_hist_kernel<DT, true, false, T2><<<grid, T2, hm, st>>>(a);
+    } else {
+      large_hist_kernel<DT, false, false, T2><<<grid, T2, hm, st>>>(a);
+    }
   }
   large_select_kernel<DT><<<rows, kSelectThreads, select_smem, st>>>(a);
   const int parts = static_cast<int>((a.vocab + kGatherIds - 1) / kGatherIds);
