@@ -420,8 +420,31 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     except RuntimeError as e:  # a capture the runtime refuses: report the step times without it
         print(f"latency_b1: graph capture failed: {e}", file=sys.stderr)
         torch.cuda.synchronize()
+    # the reference's default decode config (src/runtime/decoding.ts:16-29): C1's settings with
+    # a 1.05 repetition penalty over a 64-id window (a fixed window here: the work per step
+    # does not depend on which ids it holds)
+    pw = pkg.prepare_params(W.base_params(temperature=0.8, topK=40, topP=0.95, repetitionPenalty=1.05,
+                                          repetitionWindow=64))
+    hw = torch.randint(0, VOCAB, (1, 64), dtype=torch.int32, device=dev,
+                       generator=torch.Generator(device=dev).manual_seed(64))
+    hwl = torch.full((1,), 64, dtype=torch.int32, device=dev)
+    for s in range(16):
+        o1 = sampler.sample(lg[s:s + 1], pw, softcap=30.0, history=hw, history_len=hwl, rng_state=st,
+                            stream=stream.cuda_stream, out=o1)
+    ew = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ew[0].record(stream)
+    for s in range(steps):
+        o1 = sampler.sample(lg[s:s + 1], pw, softcap=30.0, history=hw, history_len=hwl, rng_state=st,
+                            stream=stream.cuda_stream, out=o1)
+        ew[s + 1].record(stream)
+    torch.cuda.synchronize()
+    latw = sorted(ew[i].elapsed_time(ew[i + 1]) * 1e3 for i in range(steps))
     res["latency_b1"] = {"workload": "C1: B=1, V=262144, soft cap 30, T=0.8, topK 40, topP 0.95, seed 42, "
                                      "256 sequential steps",
+                         "default_config_p50_us": latw[len(latw) // 2],
+                         "default_config_p95_us": latw[int(len(latw) * 0.95)],
+                         "default_config": "DEFAULT_DECODING_CONFIG: the same with repetitionPenalty 1.05 over a "
+                                           "64-id window (fixed ids)",
                          "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],
                          "kernel_us": kern_us, "graph_us_per_step": graph_us, "host_us_per_call": host_us,
                          "timing": "p50/p95: CUDA events between consecutive gs_sample calls (device time, no "

@@ -38,13 +38,21 @@ constexpr int kStepIds = 2048;                   // ids per unit (one CTA)
 constexpr int kStepThreads = 512;                // four ids per thread
 constexpr int kStepWarps = kStepThreads / 32;    // sixteen sorted lists of 128 packs
 constexpr int kStepMaxK = 64;                    // topK the step handles
+constexpr int kStepMaxHist = 512;                // penalty history ids per row
+constexpr int kStepHashLg = 10, kStepHash = 1 << kStepHashLg;  // the last CTA's history hash
 constexpr int kStepMaxUnits = 512;               // vocabularies up to 1 M ids
 constexpr int kStepRecPacks = 4;                  // record capacity: kStepRecPacks x k2 packs
 constexpr int kStepMaxPacks = kStepMaxK * kStepRecPacks * kStepMaxK;  // packs at or above the bound: k units' records
 constexpr int kStepSortSmem = 1024;              // candidate packs sorted in shared memory
 // shared memory: the exact fallback's lists at k2 = 64, or the last CTA's arrays
 constexpr int kStepSmemLast = kStepMaxUnits * (8 + 4 + 4) + 2 * kStepSortSmem * 8;
-constexpr int kStepSmemMax = kStepSmemLast > 2 * kStepWarps * kStepMaxK * 8 ? kStepSmemLast : 2 * kStepWarps * kStepMaxK * 8;
+// with a penalty history, after those: the hash (keys, first positions, counts), the
+// penalised entries, and the entries to order and their order
+constexpr int kStepSmemHist =
+    kStepSmemLast + 3 * kStepHash * 4 + kStepMaxHist * 16 + 2 * (kStepMaxHist + kStepMaxK) * 16;
+constexpr int kStepSmemMax = kStepSmemHist;
+static_assert(kStepSmemLast >= 2 * kStepWarps * kStepMaxK * 8, "the exact fallback's lists fit the last CTA's space");
+static_assert(2 * kStepMaxHist <= kStepHash && kStepMaxHist <= kStepThreads, "history hash load and one slot per thread");
 
 struct StepArgs {
   const void* logits;
@@ -70,18 +78,21 @@ struct StepArgs {
   unsigned char* recs;               // [rows][units] records
   unsigned long long* sort_scratch;  // [rows][kStepMaxPacks] (a row with many packs above the bound)
   unsigned* done;                    // [rows] CTAs of the row finished
+  const int32_t* history;            // [rows][history_stride] penalty history ids, or nullptr
+  const int32_t* history_len;
+  int64_t history_stride;            // <= kStepMaxHist
 };
 
 constexpr int kStepHead = 4;  // a unit's best packs kept sorted in its record
 
 struct StepRec {  // one unit's record; n packs follow (in no order)
-  float m;        // max over the unit's capped logits, -inf if none
+  float m;        // max over the unit's live capped logits (not in the penalty history), -inf if none
+  float raw_m;    // max over every id of the unit
+  double s;       // sum 2^((x - m)·a2) over live ids
+  double raw_s;   // sum e^(x - raw_m) over every id
+  unsigned long long head[kStepHead];  // the unit's best live packs, descending (0: none)
+  int32_t n;      // packs that follow: every live pack at or above the unit's bound (its k best among them)
   uint32_t flags;
-  double s;       // sum 2^((x - m)·a2)
-  double raw_s;   // sum e^(x - m) (every id is live: m is also the raw maximum)
-  unsigned long long head[kStepHead];  // the unit's best packs, descending (0: none)
-  int32_t n;      // packs that follow: every pack at or above the unit's bound (its k best among them)
-  int32_t pad;
 };
 static_assert(sizeof(StepRec) == 64, "record header");
 
@@ -205,6 +216,12 @@ __device__ __forceinline__ void warp_merge_top_u32(const uint32_t* a, const uint
   }
 }
 
+__device__ __forceinline__ double warp_max_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFullMask, v, o));
+  return v;
+}
+
 // Descending block-wide bitonic sort of n2 (a power of two) packs in shared or global
 // memory (this CTA's own: __syncthreads orders both).
 __device__ void block_sort_desc(unsigned long long* v, int n2) {
@@ -227,7 +244,8 @@ __device__ void block_sort_desc(unsigned long long* v, int n2) {
 template <int DT>
 __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  __shared__ float s_wmax[kStepWarps];
+  __shared__ float s_wmax[kStepWarps], s_wrmax[kStepWarps];
+  __shared__ uint32_t s_dead[kStepIds / 32];
   __shared__ double s_wsum[kStepWarps], s_wraw[kStepWarps];
   __shared__ uint32_t s_wkey[kStepWarps];
   __shared__ unsigned long long s_head[kStepHead], s_gtop[kStepWarps];
@@ -277,18 +295,45 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       x[q] = valid[q] ? load_logit(rowbase, DT, id0 + q) : 0.0f;
     }
   }
+  // the row's penalty history ids in this unit are not live (the last CTA scores them)
+  int hl = 0;
+  if (A.history) {
+    hl = A.history_len[row];
+    hl = hl < 0 ? 0 : (hl > A.history_stride ? static_cast<int>(A.history_stride) : hl);
+  }
+  bool live[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) live[q] = valid[q];
+  if (hl > 0) {  // (block-uniform)
+    if (tid < kStepIds / 32) s_dead[tid] = 0u;
+    __syncthreads();
+    const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
+    const int64_t base = static_cast<int64_t>(unit) * kStepIds;
+    for (int i = tid; i < hl; i += kStepThreads) {
+      const int64_t off = static_cast<int64_t>(hrow[i]) - base;
+      if (off >= 0 && off < kStepIds) atomicOr(&s_dead[off >> 5], 1u << (off & 31));
+    }
+    __syncthreads();
+    const uint32_t dw = s_dead[tid >> 3] >> ((tid & 7) * 4);  // this thread's four ids
+#pragma unroll
+    for (int q = 0; q < 4; ++q) live[q] = valid[q] && !((dw >> q) & 1u);
+  }
   bool bad = false;
-  float mx = -INFINITY;
+  float mx = -INFINITY, mraw = -INFINITY;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     if (!valid[q]) continue;
     bad |= !(x[q] <= lim);
     if (cap != 0.0f) x[q] = softcap(x[q], cap, inv_cap);
-    mx = fmaxf(mx, x[q]);
+    mraw = fmaxf(mraw, x[q]);
+    if (live[q]) mx = fmaxf(mx, x[q]);
   }
   {
-    const float wm = warp_max(mx);
-    if (lane == 0) s_wmax[warp] = wm;
+    const float wm = warp_max(mx), wr = warp_max(mraw);
+    if (lane == 0) {
+      s_wmax[warp] = wm;
+      s_wrmax[warp] = wr;
+    }
   }
   if (tid == 0) {
     s_flags = 0u;
@@ -296,25 +341,31 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     s_n = 0;
   }
   __syncthreads();
-  float m = s_wmax[0];
+  float m = s_wmax[0], mr = s_wrmax[0];
 #pragma unroll
-  for (int w = 1; w < kStepWarps; ++w) m = fmaxf(m, s_wmax[w]);
+  for (int w = 1; w < kStepWarps; ++w) {
+    m = fmaxf(m, s_wmax[w]);
+    mr = fmaxf(mr, s_wrmax[w]);
+  }
 
   // ---- 2. the sums; the packs; each warp's head and its threads' best keys ----
   float sa = 0.0f, sr = 0.0f;
-  if (m > -INFINITY) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      if (!valid[q] || !(x[q] > -INFINITY)) continue;
+  for (int q = 0; q < 4; ++q) {
+    if (!valid[q] || !(x[q] > -INFINITY)) continue;
+    if (live[q] && m > -INFINITY) {
       const float d = x[q] - m;
       sa += ex2_approx(fmaf(d, pp->a2_lo, d * pp->a2_hi));
-      if (A.want_raw) sr += ex2_approx(fmaf(d, kL2eLo, d * kL2eHi));
+    }
+    if (A.want_raw && mr > -INFINITY) {
+      const float g = x[q] - mr;
+      sr += ex2_approx(fmaf(g, kL2eLo, g * kL2eHi));
     }
   }
   unsigned long long v[4], tbest = 0ull;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    v[q] = valid[q] ? make_pack(x[q], static_cast<uint32_t>(id0 + q)) : 0ull;
+    v[q] = live[q] ? make_pack(x[q], static_cast<uint32_t>(id0 + q)) : 0ull;
     tbest = v[q] > tbest ? v[q] : tbest;
   }
   // a bound on the unit's k-th best value: each warp's c-th largest thread best key
@@ -431,8 +482,9 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     }
     StepRec r{};
     r.m = m;
+    r.raw_m = mr;
     r.s = m > -INFINITY ? su : 0.0;
-    r.raw_s = m > -INFINITY ? ru : 0.0;
+    r.raw_s = mr > -INFINITY ? ru : 0.0;
     r.flags = s_wbad ? GS_FLAG_ERR_NONFINITE : 0u;
 #pragma unroll
     for (int i = 0; i < kStepHead; ++i) r.head[i] = s_head[i];
@@ -463,12 +515,13 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(qlist + kStepMaxUnits);  // [kStepSortSmem]
   unsigned long long* srt = cand + kStepSortSmem;                                          // [kStepSortSmem]
   unsigned long long* scratch = A.sort_scratch + static_cast<int64_t>(row) * kStepMaxPacks;
-  float mu = -INFINITY;
+  float mu = -INFINITY, rmu = -INFINITY;
   double su = 0.0, ru = 0.0;
   unsigned long long hd[kStepHead] = {0ull, 0ull, 0ull, 0ull};
   if (tid < S) {
     const StepRec* st = reinterpret_cast<const StepRec*>(rec_row + static_cast<int64_t>(tid) * A.rec_bytes);
     mu = __ldcg(&st->m);
+    rmu = __ldcg(&st->raw_m);
     su = __ldcg(&st->s);
     ru = __ldcg(&st->raw_s);
     const unsigned f = __ldcg(&st->flags);
@@ -497,38 +550,96 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       }
     }
     unsigned long long wt = b;
+    float wr = rmu;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long t = __shfl_xor_sync(kFullMask, wt, o);
       wt = t > wt ? t : wt;
+      wr = fmaxf(wr, __shfl_xor_sync(kFullMask, wr, o));
     }
     const uint32_t kc = __shfl_sync(kFullMask, key, cg <= 32 ? cg - 1 : 0);
     if (lane == 0) {
       s_wkey[warp] = cg <= 32 ? kc : 0u;
       s_gtop[warp] = wt;
+      s_wrmax[warp] = wr;
     }
   }
   __syncthreads();
   uint32_t tk = s_wkey[0];
   unsigned long long top = s_gtop[0];
+  float Mx = s_wrmax[0];  // the row's raw maximum (every id)
   for (int w = 1; w < g; ++w) {
     tk = min(tk, s_wkey[w]);
     top = s_gtop[w] > top ? s_gtop[w] : top;
+    Mx = fmaxf(Mx, s_wrmax[w]);
   }
   unsigned fl = s_flags;
   if (greedy) fl |= GS_FLAG_GREEDY;
   const double T = pp->temperature;
-  const float Mx = pack_value(top);  // the row's maximum (raw maximum too: every id is live)
-  const double xtop = static_cast<double>(Mx);
-  const double M = greedy ? xtop : __ddiv_rn(xtop, T);
+  const double xtop = static_cast<double>(pack_value(top));
+  double M = top == 0ull ? -INFINITY : (greedy ? xtop : __ddiv_rn(xtop, T));
+  // penalised entries (sampling.ts:21-30): the distinct history ids, counted in a shared
+  // hash, each scored exactly in double at its first position's slot
+  Ent* pent = reinterpret_cast<Ent*>(dsm + kStepSmemLast + 3 * kStepHash * 4);  // [kStepMaxHist]
+  if (hl > 0) {  // (block-uniform)
+    uint32_t* hk = reinterpret_cast<uint32_t*>(dsm + kStepSmemLast);
+    uint32_t* hfirst = hk + kStepHash;
+    uint32_t* hcnt = hfirst + kStepHash;
+    for (int i = tid; i < kStepHash; i += kStepThreads) {
+      hk[i] = 0xffffffffu;
+      hfirst[i] = 0xffffffffu;
+      hcnt[i] = 0u;
+    }
+    __syncthreads();
+    const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
+    auto slot_of = [&](uint32_t v, bool insert) {
+      uint32_t sl = (v * 2654435761u) >> (32 - kStepHashLg);
+      for (;;) {  // at most kStepMaxHist distinct ids in 2·kStepMaxHist slots: a free slot exists
+        const uint32_t kv = insert ? atomicCAS(&hk[sl], 0xffffffffu, v) : hk[sl];
+        if (kv == 0xffffffffu || kv == v) return sl;
+        sl = (sl + 1) & (kStepHash - 1);
+      }
+    };
+    for (int i = tid; i < hl; i += kStepThreads) {
+      const uint32_t v = static_cast<uint32_t>(hrow[i]);  // (negative ids are >= 2^31 here)
+      if (v >= static_cast<uint64_t>(A.vocab)) continue;
+      const uint32_t sl = slot_of(v, true);
+      atomicAdd(&hcnt[sl], 1u);
+      atomicMin(&hfirst[sl], static_cast<uint32_t>(i));
+    }
+    __syncthreads();
+    double pmax = -INFINITY;
+    const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
+    for (int i = tid; i < hl; i += kStepThreads) {
+      Ent e{-INFINITY, 0xffffffffu, 0xffffffffu};
+      const uint32_t v = static_cast<uint32_t>(hrow[i]);
+      if (v < static_cast<uint64_t>(A.vocab)) {
+        const uint32_t sl = slot_of(v, false);
+        if (hfirst[sl] == static_cast<uint32_t>(i)) {
+          float xv = load_logit(rowbase, DT, v);
+          if (cap != 0.0f) xv = softcap(xv, cap, inv_cap);
+          const double xp = penalise(static_cast<double>(xv), static_cast<double>(hcnt[sl]), rp, pres, freq);
+          e = Ent{greedy ? xp : __ddiv_rn(xp, T), v, 1u};
+          pmax = fmax(pmax, e.key);
+        }
+      }
+      pent[i] = e;
+    }
+    pmax = warp_max_d(pmax);
+    if (lane == 0) s_wsum[warp] = pmax;
+    __syncthreads();
+    for (int w = 0; w < kStepWarps; ++w) M = fmax(M, s_wsum[w]);
+    __syncthreads();
+  }
   // per unit: the normaliser's and the raw sum's terms; its head packs whose key reaches the
   // bound, or, when its whole head does (it may hold more), the unit for a full read
   {
     double part = 0.0, rpart = 0.0;
-    if (tid < S && mu > -INFINITY) {
-      if (!greedy && M > -INFINITY) part = __dmul_rn(su, exp(__dsub_rn(__ddiv_rn(static_cast<double>(mu), T), M)));
-      if (A.want_raw) rpart = __dmul_rn(ru, exp(static_cast<double>(mu) - static_cast<double>(Mx)));
-    }
+    if (tid < S && mu > -INFINITY && !greedy && M > -INFINITY)
+      part = __dmul_rn(su, exp(__dsub_rn(__ddiv_rn(static_cast<double>(mu), T), M)));
+    if (tid < S && rmu > -INFINITY && A.want_raw) rpart = __dmul_rn(ru, exp(static_cast<double>(rmu) - static_cast<double>(Mx)));
+    if (tid < hl && !greedy && M > -INFINITY && pent[tid].id != 0xffffffffu)
+      part = __dadd_rn(part, exp(__dsub_rn(pent[tid].key, M)));  // (hl <= kStepMaxHist = the block's threads)
     part = warp_sum(part);
     rpart = warp_sum(rpart);
     if (lane == 0) {
@@ -631,10 +742,48 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     sorted = cbuf;
   }
   __syncthreads();
+  // with penalised entries: the k best live packs and the penalised entries in the
+  // reference's order (key descending, lower id first), by rank counting
+  const Ent* sents = nullptr;
+  int ne = 0;
+  if (hl > 0) {
+    Ent* ents = pent + kStepMaxHist;        // [kStepMaxHist + kStepMaxK]
+    Ent* sw = ents + kStepMaxHist + kStepMaxK;  // [kStepMaxHist + kStepMaxK]
+    const int nL = N < k ? N : k;
+    for (int i = tid; i < nL; i += kStepThreads) {
+      const unsigned long long p = sorted[i];
+      const double xv = static_cast<double>(pack_value(p));
+      ents[i] = Ent{greedy ? xv : __ddiv_rn(xv, T), pack_id(p), 0u};
+    }
+    if (tid == 0) s_nq = 0;
+    __syncthreads();
+    {
+      const bool take = tid < hl && pent[tid].id != 0xffffffffu;
+      const unsigned bal = __ballot_sync(kFullMask, take);
+      if (bal) {
+        const int leader = __ffs(bal) - 1;
+        int at = 0;
+        if (lane == leader) at = atomicAdd(&s_nq, __popc(bal));
+        at = __shfl_sync(kFullMask, at, leader) + __popc(bal & ((1u << lane) - 1u));
+        if (take) ents[nL + at] = pent[tid];
+      }
+    }
+    __syncthreads();
+    ne = nL + s_nq;
+    for (int i = tid; i < ne; i += kStepThreads) {
+      const Ent e = ents[i];
+      int r = 0;
+      for (int j = 0; j < ne; ++j) r += ent_before(ents[j], e);
+      sw[r] = e;
+    }
+    __syncthreads();
+    sents = sw;
+  }
   if (warp != 0) return;
 
   // ---- 5. one warp: probabilities, filters, draw, outputs ----
-  const int nC = N < k ? N : k;
+  const int nAll = sents ? ne : N;
+  const int nC = nAll < k ? nAll : k;
   WWork w;
   {
     unsigned char* p = wwork;
@@ -658,7 +807,8 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   if (!(fl & GS_FLAG_ERRORS)) {
     if (greedy) {
       // argmax over the whole vocabulary: all -inf -> id 0 (sampling.ts:92-96)
-      tok = (top == 0ull || !(xtop > -INFINITY)) ? 0u : pack_id(top);
+      if (sents) tok = (ne == 0 || !(sents[0].key > -INFINITY)) ? 0u : sents[0].id;
+      else tok = (top == 0ull || !(xtop > -INFINITY)) ? 0u : pack_id(top);
       if (lane == 0) {
         w.cid[0] = tok;
         w.cp[0] = 1.0;
@@ -672,9 +822,17 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
         for (int q = 0; q < kStepMaxK / 32; ++q) {  // (independent chains)
           const int i = q * 32 + lane;
           if (i < nC) {
-            const unsigned long long pk = sorted[i];
-            const double key = __ddiv_rn(static_cast<double>(pack_value(pk)), T);
-            w.cid[i] = pack_id(pk);
+            double key;
+            uint32_t id;
+            if (sents) {
+              key = sents[i].key;
+              id = sents[i].id;
+            } else {
+              const unsigned long long pk = sorted[i];
+              key = __ddiv_rn(static_cast<double>(pack_value(pk)), T);
+              id = pack_id(pk);
+            }
+            w.cid[i] = id;
             w.cp[i] = __ddiv_rn(exp(__dsub_rn(key, M)), total);
           }
         }
@@ -750,7 +908,8 @@ int pow2_at_least(int n) {
 
 bool step_eligible(const gs_batch* b, int kmax, bool any_large, int rows) {
   if (rows < 1 || rows > kStepDoneRows || any_large || kmax < 1 || kmax > kStepMaxK) return false;
-  if (b->mask_table || b->history) return false;
+  if (b->mask_table) return false;
+  if (b->history && b->history_stride > kStepMaxHist) return false;
   if (b->dtype != GS_DTYPE_F32 && b->dtype != GS_DTYPE_BF16) return false;
   const int64_t esz = b->dtype == GS_DTYPE_F32 ? 4 : 2;
   if ((reinterpret_cast<uintptr_t>(b->logits) & 15) != 0 || (b->row_stride * esz) % 16 != 0) return false;
@@ -790,9 +949,12 @@ cudaError_t launch_step(const gs_batch* b, const gs_outputs* o, const RowPlan& p
   a.recs = ws;
   a.sort_scratch = reinterpret_cast<unsigned long long*>(ws + align_up(static_cast<size_t>(b->rows) * a.units * a.rec_bytes, 256));
   a.done = done;
+  a.history = b->history;
+  a.history_len = b->history ? b->history_len : nullptr;
+  a.history_stride = b->history ? b->history_stride : 0;
   // shared memory: the merge tree's two list sets, or the last CTA's arrays
   const size_t tree = 2 * static_cast<size_t>(kStepWarps) * a.k2 * 8;
-  const size_t last = kStepSmemLast;
+  const size_t last = b->history ? kStepSmemHist : kStepSmemLast;
   const size_t smem = tree > last ? tree : last;
   const int grid = b->rows * a.units;
   static bool attr = false;  // (set once, outside any stream capture: the first call)

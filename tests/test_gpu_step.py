@@ -128,3 +128,40 @@ def test_c1_steps_bit_identical_replay(sampler):
         torch.cuda.synchronize()
         outs.append([t.cpu().numpy().tobytes() for t in (r.ids, r.flags, r.logprob, r.cand_ids, r.cand_probs, st)])
     assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_step_penalty_history(oracle, sampler, dtype):
+    """Rows with a penalty history (stride <= 512: the decode default is a 64-id window
+    at 1.05): the history ids leave the units' streams and the last CTA scores them
+    exactly; histories that are empty, one id, full of repeats, made of the row's best
+    ids, and at the stride's limit."""
+    import torch
+    td = torch.bfloat16 if dtype == "bf16" else None
+    rng = np.random.default_rng(57 + (dtype == "bf16"))
+    V, rows, H = 262144, 6, 512
+    x = _rows(rng, rows, V)
+    hist = rng.integers(0, V, (rows, H)).astype(np.int32)
+    order = np.argsort(-x, axis=1)
+    hist[1, :1] = order[1, :1]                         # the best id only
+    hist[2, :64] = order[2, :64]                       # the row's 64 best ids
+    hist[3, :200] = np.repeat(order[3, :20], 10)       # twenty ids, ten times each
+    hist[4, :] = order[4, :512]                        # the 512 best
+    hist[5, ::3] = 7                                   # one id repeated, the rest random
+    hlen = np.array([0, 1, 64, 200, 512, 512], dtype=np.int32)
+    ps = [_p(temperature=0.0, repetitionPenalty=1.3, repetitionWindow=H),
+          _p(topK=40, repetitionPenalty=1.05, repetitionWindow=H),
+          _p(topK=64, topP=0.9, repetitionPenalty=1.3, presencePenalty=0.4, frequencyPenalty=0.2, repetitionWindow=H),
+          _p(topK=20, minP=0.02, repetitionPenalty=1.2, frequencyPenalty=0.5, repetitionWindow=H),
+          _p(topK=50, typicalP=0.9, repetitionPenalty=1.1, presencePenalty=0.5, frequencyPenalty=0.3, repetitionWindow=H),
+          _p(temperature=0.0, presencePenalty=2.0, repetitionWindow=H)]
+    rng_state = np.array([pkg_seed(900 + r) for r in range(rows)])
+    gpu = PU.run_gpu(sampler, x, ps, softcap=30.0, history=hist, history_len=hlen, rng_state=rng_state, dtype=td,
+                     cand_cap=64)
+    xo = x if td is None else torch.from_numpy(x).to(td).float().numpy()
+    ids, margins, cands, st = PU.oracle_rows_batched(oracle, xo, V, 30.0, ps, history=hist, history_len=hlen,
+                                                     rng_state=rng_state, cand_cap=64)
+    assert PU.compare(gpu, ids, margins, cands, rng_after=st, label=f"step-hist-{dtype}") <= 1
+    for r in range(rows):
+        lp = oracle.token_log_probability(oracle.softcap(xo[r], 30.0), int(gpu.ids[r]))
+        assert abs(gpu.logprob[r] - lp) <= 1e-6 * max(1.0, abs(lp)), (r, gpu.logprob[r], lp)
