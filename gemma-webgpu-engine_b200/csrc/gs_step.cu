@@ -269,6 +269,13 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   unsigned char* rec_row = A.recs + static_cast<int64_t>(row) * S * A.rec_bytes;
 
   // ---- 1. four ids per thread: capped logits; the unit maximum ----
+  // (the history's length and this thread's history position load with the logits)
+  int hl = 0;
+  int32_t hid = -1;
+  if (A.history) {
+    hl = A.history_len[row];
+    if (tid < A.history_stride) hid = A.history[static_cast<int64_t>(row) * A.history_stride + tid];
+  }
   const int64_t id0 = static_cast<int64_t>(unit) * kStepIds + tid * 4;
   float x[4];
   bool valid[4];
@@ -296,23 +303,15 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     }
   }
   // the row's penalty history ids in this unit are not live (the last CTA scores them)
-  int hl = 0;
-  if (A.history) {
-    hl = A.history_len[row];
-    hl = hl < 0 ? 0 : (hl > A.history_stride ? static_cast<int>(A.history_stride) : hl);
-  }
+  hl = hl < 0 ? 0 : (hl > A.history_stride ? static_cast<int>(A.history_stride) : hl);
   bool live[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) live[q] = valid[q];
-  if (hl > 0) {  // (block-uniform)
+  if (hl > 0) {  // (block-uniform; hl <= kStepMaxHist: one history position per thread)
     if (tid < kStepIds / 32) s_dead[tid] = 0u;
     __syncthreads();
-    const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
-    const int64_t base = static_cast<int64_t>(unit) * kStepIds;
-    for (int i = tid; i < hl; i += kStepThreads) {
-      const int64_t off = static_cast<int64_t>(hrow[i]) - base;
-      if (off >= 0 && off < kStepIds) atomicOr(&s_dead[off >> 5], 1u << (off & 31));
-    }
+    const int64_t off = static_cast<int64_t>(hid) - static_cast<int64_t>(unit) * kStepIds;
+    if (tid < hl && off >= 0 && off < kStepIds) atomicOr(&s_dead[off >> 5], 1u << (off & 31));
     __syncthreads();
     const uint32_t dw = s_dead[tid >> 3] >> ((tid & 7) * 4);  // this thread's four ids
 #pragma unroll
@@ -497,6 +496,18 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // the history ids and their capped logits, early (random loads that overlap the records')
+  uint32_t hv = 0xffffffffu;
+  float hx = 0.0f;
+  if (tid < hl) {
+    hv = static_cast<uint32_t>(hid);  // (negative ids are >= 2^31 here)
+    if (hv < static_cast<uint64_t>(A.vocab)) {
+      hx = load_logit(rowbase, DT, hv);
+      if (cap != 0.0f) hx = softcap(hx, cap, inv_cap);
+    } else {
+      hv = 0xffffffffu;
+    }
+  }
   if (tid == kStepThreads - 1 && !greedy) {  // the draw's uniform, early (its load overlaps the records')
     if (A.uniforms) {
       s_r = A.uniforms[row];
@@ -581,49 +592,44 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   // penalised entries (sampling.ts:21-30): the distinct history ids, counted in a shared
   // hash, each scored exactly in double at its first position's slot
   Ent* pent = reinterpret_cast<Ent*>(dsm + kStepSmemLast + 3 * kStepHash * 4);  // [kStepMaxHist]
-  if (hl > 0) {  // (block-uniform)
+  if (hl > 0) {  // (block-uniform; hl <= kStepMaxHist: one history position per thread)
+    int lg = 6;  // a table of at least twice the history's length
+    while ((1 << lg) < 2 * hl) ++lg;
+    const uint32_t nslot = 1u << lg;
     uint32_t* hk = reinterpret_cast<uint32_t*>(dsm + kStepSmemLast);
     uint32_t* hfirst = hk + kStepHash;
     uint32_t* hcnt = hfirst + kStepHash;
-    for (int i = tid; i < kStepHash; i += kStepThreads) {
+    for (uint32_t i = tid; i < nslot; i += kStepThreads) {
       hk[i] = 0xffffffffu;
       hfirst[i] = 0xffffffffu;
       hcnt[i] = 0u;
     }
     __syncthreads();
-    const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
     auto slot_of = [&](uint32_t v, bool insert) {
-      uint32_t sl = (v * 2654435761u) >> (32 - kStepHashLg);
-      for (;;) {  // at most kStepMaxHist distinct ids in 2·kStepMaxHist slots: a free slot exists
+      uint32_t sl = (v * 2654435761u) >> (32 - lg);
+      for (;;) {  // at most hl distinct ids in >= 2·hl slots: a free slot exists
         const uint32_t kv = insert ? atomicCAS(&hk[sl], 0xffffffffu, v) : hk[sl];
         if (kv == 0xffffffffu || kv == v) return sl;
-        sl = (sl + 1) & (kStepHash - 1);
+        sl = (sl + 1) & (nslot - 1);
       }
     };
-    for (int i = tid; i < hl; i += kStepThreads) {
-      const uint32_t v = static_cast<uint32_t>(hrow[i]);  // (negative ids are >= 2^31 here)
-      if (v >= static_cast<uint64_t>(A.vocab)) continue;
-      const uint32_t sl = slot_of(v, true);
+    uint32_t sl = 0;
+    if (hv != 0xffffffffu) {
+      sl = slot_of(hv, true);
       atomicAdd(&hcnt[sl], 1u);
-      atomicMin(&hfirst[sl], static_cast<uint32_t>(i));
+      atomicMin(&hfirst[sl], static_cast<uint32_t>(tid));
     }
     __syncthreads();
     double pmax = -INFINITY;
     const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
-    for (int i = tid; i < hl; i += kStepThreads) {
+    if (tid < hl) {
       Ent e{-INFINITY, 0xffffffffu, 0xffffffffu};
-      const uint32_t v = static_cast<uint32_t>(hrow[i]);
-      if (v < static_cast<uint64_t>(A.vocab)) {
-        const uint32_t sl = slot_of(v, false);
-        if (hfirst[sl] == static_cast<uint32_t>(i)) {
-          float xv = load_logit(rowbase, DT, v);
-          if (cap != 0.0f) xv = softcap(xv, cap, inv_cap);
-          const double xp = penalise(static_cast<double>(xv), static_cast<double>(hcnt[sl]), rp, pres, freq);
-          e = Ent{greedy ? xp : __ddiv_rn(xp, T), v, 1u};
-          pmax = fmax(pmax, e.key);
-        }
+      if (hv != 0xffffffffu && hfirst[sl] == static_cast<uint32_t>(tid)) {
+        const double xp = penalise(static_cast<double>(hx), static_cast<double>(hcnt[sl]), rp, pres, freq);
+        e = Ent{greedy ? xp : __ddiv_rn(xp, T), hv, 1u};
+        pmax = e.key;
       }
-      pent[i] = e;
+      pent[tid] = e;
     }
     pmax = warp_max_d(pmax);
     if (lane == 0) s_wsum[warp] = pmax;
