@@ -367,28 +367,40 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     lg = torch.empty((steps, VOCAB), dtype=torch.float32, device=dev)
     for s in range(steps):
         lg[s] = W.make("C1", device=dev, step=s).logits[0]
-    # (a decode loop converts its fixed config once: prepare_params)
+    # (a decode loop converts its fixed config once, prepare_params, and binds its call,
+    # GpuSampler.bind: the call's structures are built once, each step sets the logits)
     p1 = pkg.prepare_params(W.base_params(temperature=0.8, topK=40, topP=0.95, repetitionWindow=0))
     st = torch.tensor([pkg.SeededRandom(42).state], dtype=torch.float64, device=dev)
+    step1 = sampler.bind(lg[0:1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream)
+
+    def time_loop(call):
+        for s in range(16):
+            call(s)
+        st.fill_(pkg.SeededRandom(42).state)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        evs[0].record(stream)
+        h0 = time.perf_counter()
+        for s in range(steps):
+            call(s)
+            evs[s + 1].record(stream)
+        host = (time.perf_counter() - h0) / steps * 1e6
+        torch.cuda.synchronize()
+        return sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(steps)), host
+
+    lat, host_us = time_loop(lambda s: step1(lg[s:s + 1]))
     o1 = None
-    for s in range(16):
+
+    def via_sample(s):
+        nonlocal o1
         o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream, out=o1)
-    st.fill_(pkg.SeededRandom(42).state)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
-    evs[0].record(stream)
-    h0 = time.perf_counter()
-    for s in range(steps):
-        o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream, out=o1)
-        evs[s + 1].record(stream)
-    host_us = (time.perf_counter() - h0) / steps * 1e6
-    torch.cuda.synchronize()
-    lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(steps))
+
+    lat_s, host_s = time_loop(via_sample)
     # the kernels' own device time per step (the library's events around its launches)
     import ctypes
     Lb = pkg._lib.lib()
     Lb.gs_profile_enable(sampler.handle, 1)
     for s in range(steps):
-        o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream, out=o1)
+        step1(lg[s:s + 1])
     torch.cuda.synchronize()
     s_ms, s_n, m_ms, m_n = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double(), ctypes.c_int64()
     Lb.gs_profile_read(sampler.handle, ctypes.byref(s_ms), ctypes.byref(s_n), ctypes.byref(m_ms), ctypes.byref(m_n))
@@ -399,10 +411,11 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     try:
         gs = torch.cuda.Stream(dev)
         gs.wait_stream(stream)
+        stepg = sampler.bind(lg[0:1], p1, softcap=30.0, rng_state=st, stream=gs.cuda_stream)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=gs):
             for s in range(steps):
-                o1 = sampler.sample(lg[s:s + 1], p1, softcap=30.0, rng_state=st, stream=gs.cuda_stream, out=o1)
+                stepg(lg[s:s + 1])
         with torch.cuda.stream(gs):
             for _ in range(3):
                 graph.replay()
@@ -428,31 +441,25 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     hw = torch.randint(0, VOCAB, (1, 64), dtype=torch.int32, device=dev,
                        generator=torch.Generator(device=dev).manual_seed(64))
     hwl = torch.full((1,), 64, dtype=torch.int32, device=dev)
-    for s in range(16):
-        o1 = sampler.sample(lg[s:s + 1], pw, softcap=30.0, history=hw, history_len=hwl, rng_state=st,
-                            stream=stream.cuda_stream, out=o1)
-    ew = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
-    ew[0].record(stream)
-    for s in range(steps):
-        o1 = sampler.sample(lg[s:s + 1], pw, softcap=30.0, history=hw, history_len=hwl, rng_state=st,
-                            stream=stream.cuda_stream, out=o1)
-        ew[s + 1].record(stream)
-    torch.cuda.synchronize()
-    latw = sorted(ew[i].elapsed_time(ew[i + 1]) * 1e3 for i in range(steps))
+    stepw = sampler.bind(lg[0:1], pw, softcap=30.0, history=hw, history_len=hwl, rng_state=st,
+                         stream=stream.cuda_stream)
+    latw, _ = time_loop(lambda s: stepw(lg[s:s + 1]))
     res["latency_b1"] = {"workload": "C1: B=1, V=262144, soft cap 30, T=0.8, topK 40, topP 0.95, seed 42, "
                                      "256 sequential steps",
+                         "sample_api_p50_us": lat_s[len(lat_s) // 2], "sample_api_host_us_per_call": host_s,
                          "default_config_p50_us": latw[len(latw) // 2],
                          "default_config_p95_us": latw[int(len(latw) * 0.95)],
                          "default_config": "DEFAULT_DECODING_CONFIG: the same with repetitionPenalty 1.05 over a "
                                            "64-id window (fixed ids)",
                          "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],
                          "kernel_us": kern_us, "graph_us_per_step": graph_us, "host_us_per_call": host_us,
-                         "timing": "p50/p95: CUDA events between consecutive gs_sample calls (device time, no "
-                                   "graph; 256 distinct 1 MiB rows, 256 MiB > L2); kernel_us: the library's events "
-                                   "around its launches, average per step; graph_us_per_step: the 256 calls "
+                         "timing": "p50/p95: CUDA events between consecutive decode-loop calls (GpuSampler.bind: "
+                                   "gs_sample with the call's structures built once; device time, no graph; 256 "
+                                   "distinct 1 MiB rows, 256 MiB > L2); sample_api_*: the same through "
+                                   "GpuSampler.sample (structures rebuilt each call); kernel_us: the library's "
+                                   "events around its launches, average per step; graph_us_per_step: the 256 calls "
                                    "captured in one CUDA graph, replayed (device time per step, no host work "
-                                   "between steps); host_us_per_call: the host time of one gs_sample call from "
-                                   "Python (params prepared once)"}
+                                   "between steps); host_us_per_call: host time of one bound call from Python"}
     del lg
     # ---- CPU baseline (N = 1 only): the oracle on a bounded sample of the same rows
     if world == 1:

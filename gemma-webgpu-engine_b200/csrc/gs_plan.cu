@@ -10,6 +10,7 @@
 namespace gs {
 
 int pipe_max_k();
+int sm_count();
 int64_t pipe_max_chunk();
 
 namespace {
@@ -98,12 +99,7 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   const bool aligned = (reinterpret_cast<uintptr_t>(b->logits) & 15) == 0 && ((b->row_stride * esz) & 15) == 0 &&
                        (!b->mask_table || ((reinterpret_cast<uintptr_t>(b->mask_table) & 15) == 0 && (b->mask_words & 3) == 0));
   const bool warp_kernel = kmax <= pipe_max_k() && aligned;
-  int sms = 148;
-  {
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  const int sms = sm_count();  // (cached per device)
   const int64_t min_chunk = warp_kernel ? 2048 : 4096;
   const int64_t granule = warp_kernel ? 1024 : 4096;
   auto can_split = [&](int s) { return V / (2 * s) >= min_chunk && 2 * s * std::max(kmax, 1) <= 16384 && s < 1024; };

@@ -165,3 +165,28 @@ def test_step_penalty_history(oracle, sampler, dtype):
     for r in range(rows):
         lp = oracle.token_log_probability(oracle.softcap(xo[r], 30.0), int(gpu.ids[r]))
         assert abs(gpu.logprob[r] - lp) <= 1e-6 * max(1.0, abs(lp)), (r, gpu.logprob[r], lp)
+
+
+def test_bound_call_matches_sample(pkg, sampler):
+    """GpuSampler.bind (the decode-loop call: structures built once, the logits set per
+    call) gives the bytes GpuSampler.sample gives, and refuses logits of another shape."""
+    import torch
+    lg = torch.stack([W.make("C1", device="cuda", step=s).logits[0] for s in range(6)])
+    p = pkg.prepare_params(W.base_params(temperature=0.8, topK=40, topP=0.95, repetitionPenalty=1.05,
+                                         repetitionWindow=64))
+    hist = torch.randint(0, lg.shape[1], (1, 64), dtype=torch.int32, device="cuda")
+    hlen = torch.full((1,), 64, dtype=torch.int32, device="cuda")
+    st1 = torch.tensor([pkg.SeededRandom(42).state], dtype=torch.float64, device="cuda")
+    st2 = st1.clone()
+    step = sampler.bind(lg[0:1], p, softcap=30.0, history=hist, history_len=hlen, rng_state=st1, logprob=True,
+                        candidates=40)
+    for s in range(6):
+        a = step(lg[s:s + 1])
+        b = sampler.sample(lg[s:s + 1], p, softcap=30.0, history=hist, history_len=hlen, rng_state=st2,
+                           logprob=True, candidates=40)
+        torch.cuda.synchronize()
+        for x, y in ((a.ids, b.ids), (a.flags, b.flags), (a.logprob, b.logprob), (a.cand_ids, b.cand_ids),
+                     (a.cand_probs, b.cand_probs), (a.cand_count, b.cand_count), (st1, st2)):
+            assert x.cpu().numpy().tobytes() == y.cpu().numpy().tobytes(), s
+    with pytest.raises(ValueError):
+        step(lg[0:2])
