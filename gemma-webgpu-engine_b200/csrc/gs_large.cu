@@ -355,10 +355,10 @@ size_t large_select_smem_bytes(int64_t history_stride) {
 // r = round(dl·e^-dl·2^qbits) of their values (dl: the value's key distance below its
 // bin's top), kept in a second dynamic shared-memory array after the queue.
 // TPB: threads per CTA.  512 (three CTAs per SM) with the queue, for batches with a
-// constraint table (sparse chunks); 256 (six per SM, no queue) otherwise, so that a
-// batch's 8-CTA clusters fit in one wave.
+// constraint table (sparse chunks); 256 (four per SM, no queue, 64 registers) otherwise, so
+// that a batch of up to 74 rows' 8-CTA clusters fits in one wave.
 template <int DT, bool RAW, bool MOM, int TPB>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(TPB, TPB == kHistThreads ? kHistMinBlocks : 2 * kHistMinBlocks)
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(TPB, TPB == kHistThreads ? kHistMinBlocks : kHistMinBlocks + 1)
     large_hist_kernel(const __grid_constant__ FinalizeArgs A) {
   constexpr bool kQueue = TPB == kHistThreads;
   static_assert((kNB / kCluster) % TPB == 0, "whole bins per thread in the cluster reduction");
