@@ -444,11 +444,22 @@ def extras(args, pkg, W, sampler, dev, logits, hist, hlen, table, mstate, seeds,
     stepw = sampler.bind(lg[0:1], pw, softcap=30.0, history=hw, history_len=hwl, rng_state=st,
                          stream=stream.cuda_stream)
     latw, _ = time_loop(lambda s: stepw(lg[s:s + 1]))
+    # the same under a constraint row (about half the vocabulary allowed; the JSON / tool-call
+    # decoding of the reference's constrained generate)
+    gm = torch.Generator(device=dev).manual_seed(65)
+    mt = torch.randint(-2**31, 2**31 - 1, (1, VOCAB // 32), dtype=torch.int32, device=dev, generator=gm)
+    ms = torch.zeros(1, dtype=torch.int32, device=dev)
+    stepm = sampler.bind(lg[0:1], pw, softcap=30.0, history=hw, history_len=hwl, mask_table=mt, mask_state=ms,
+                         rng_state=st, stream=stream.cuda_stream)
+    latm, _ = time_loop(lambda s: stepm(lg[s:s + 1]))
     res["latency_b1"] = {"workload": "C1: B=1, V=262144, soft cap 30, T=0.8, topK 40, topP 0.95, seed 42, "
                                      "256 sequential steps",
                          "sample_api_p50_us": lat_s[len(lat_s) // 2], "sample_api_host_us_per_call": host_s,
                          "default_config_p50_us": latw[len(latw) // 2],
                          "default_config_p95_us": latw[int(len(latw) * 0.95)],
+                         "constrained_p50_us": latm[len(latm) // 2],
+                         "constrained_p95_us": latm[int(len(latm) * 0.95)],
+                         "constrained": "the default config under a constraint row allowing about half the ids",
                          "default_config": "DEFAULT_DECODING_CONFIG: the same with repetitionPenalty 1.05 over a "
                                            "64-id window (fixed ids)",
                          "p50_us": lat[len(lat) // 2], "p95_us": lat[int(len(lat) * 0.95)],

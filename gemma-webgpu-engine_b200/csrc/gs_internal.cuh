@@ -1,5 +1,6 @@
 // Internal types shared by the kernels and the host side of libgsampler.
 #pragma once
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -131,6 +132,19 @@ inline int64_t shard_record_bytes(int kcap, int hcap) {
 // Launch helpers implemented in gs_kernels.cu.
 cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem, cudaStream_t st);
 int sm_count();  // SMs of the current device
+// True until mark_device_done(seen) has run on the current device: a kernel's dynamic
+// shared-memory attribute is a per-device setting, so a process that drives several
+// GPUs sets it once on each (devices 0..63).
+inline bool device_todo(const std::atomic<uint64_t>& seen) {
+  int d = 0;
+  cudaGetDevice(&d);
+  return !((seen.load(std::memory_order_acquire) >> (d & 63)) & 1u);
+}
+inline void mark_device_done(std::atomic<uint64_t>& seen) {
+  int d = 0;
+  cudaGetDevice(&d);
+  seen.fetch_or(1ull << (d & 63), std::memory_order_release);
+}
 int ctx_device(const gs_ctx* c);                 // the device a context is bound to
 void ctx_set_error(gs_ctx* c, const char* msg);  // the message gs_last_error returns
 size_t stream_smem_bytes(int64_t chunk, int kc);

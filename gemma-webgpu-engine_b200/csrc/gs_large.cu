@@ -2106,8 +2106,8 @@ void set_smem(Kern k, size_t bytes) {
 template <int DT>
 cudaError_t launch_large_t(const FinalizeArgs& a, int rows, size_t select_smem, cudaStream_t st) {
   const size_t res_smem = large_resolve_smem_bytes();
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};  // (set on each device's first call)
+  if (device_todo(attr)) {
     set_smem(large_select_kernel<DT>, large_select_smem_bytes(GS_MAX_HISTORY));
     set_smem(large_resolve_kernel<DT, 0>, res_smem);
     set_smem(large_resolve_kernel<DT, 1>, res_smem);
@@ -2121,7 +2121,7 @@ cudaError_t launch_large_t(const FinalizeArgs& a, int rows, size_t select_smem, 
     set_smem(large_hist_kernel<DT, true, false, kHistThreads / 2>, 0);
     set_smem(large_hist_kernel<DT, false, true, kHistThreads / 2>, m);
     set_smem(large_hist_kernel<DT, true, true, kHistThreads / 2>, m);
-    attr = true;
+    mark_device_done(attr);
   }
   const int grid = rows * kCluster;
   if (a.mask_table) {  // sparse chunks: 512-thread CTAs with the queue

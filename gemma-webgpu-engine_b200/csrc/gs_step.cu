@@ -81,6 +81,10 @@ struct StepArgs {
   const int32_t* history;            // [rows][history_stride] penalty history ids, or nullptr
   const int32_t* history_len;
   int64_t history_stride;            // <= kStepMaxHist
+  const uint32_t* mask_table;        // [mask_states][mask_words] allowed-id bitmask rows, or nullptr
+  int32_t mask_states;
+  int64_t mask_words;
+  const int32_t* mask_state;         // [rows] row of the table (< 0: unconstrained)
 };
 
 constexpr int kStepHead = 4;  // a unit's best packs kept sorted in its record
@@ -93,8 +97,10 @@ struct StepRec {  // one unit's record; n packs follow (in no order)
   unsigned long long head[kStepHead];  // the unit's best live packs, descending (0: none)
   int32_t n;      // packs that follow: every live pack at or above the unit's bound (its k best among them)
   uint32_t flags;
+  int32_t n_allowed;  // ids the constraint row allows
+  int32_t pad;
 };
-static_assert(sizeof(StepRec) == 64, "record header");
+static_assert(sizeof(StepRec) == 72, "record header");
 
 // The warp's kStepHead best of the packs its lanes hold (every lane gets them, descending).
 __device__ __forceinline__ void warp_head(const unsigned long long* v, int nv, unsigned long long* out) {
@@ -187,35 +193,6 @@ __device__ __forceinline__ void warp_merge_top(const unsigned long long* a, cons
   }
 }
 
-// warp_merge_top for 32-bit keys.
-__device__ __forceinline__ void warp_merge_top_u32(const uint32_t* a, const uint32_t* b, int K2, uint32_t* out,
-                                                   int lane) {
-  uint32_t c[2];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int i = q * 32 + lane;
-    c[q] = 0u;
-    if (i < K2) c[q] = max(a[i], b[K2 - 1 - i]);
-  }
-  if (K2 == 64 && c[0] < c[1]) {
-    const uint32_t t = c[0];
-    c[0] = c[1];
-    c[1] = t;
-  }
-  for (int h = (K2 < 32 ? K2 : 32) >> 1; h > 0; h >>= 1) {
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const uint32_t p = __shfl_xor_sync(kFullMask, c[q], h);
-      c[q] = (lane & h) == 0 ? max(c[q], p) : min(c[q], p);
-    }
-  }
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int i = q * 32 + lane;
-    if (i < K2) out[i] = c[q];
-  }
-}
-
 __device__ __forceinline__ double warp_max_d(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFullMask, v, o));
@@ -241,8 +218,67 @@ __device__ void block_sort_desc(unsigned long long* v, int n2) {
     }
 }
 
-template <int DT>
-__global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constant__ StepArgs A) {
+// The row's allowed-id bitmask (maskConstraintLogits: disallowed ids are -inf), or
+// nullptr when the row has no constraint (no table, or a state of -1 / past the table:
+// the latter is flagged invalid by the units).
+__device__ __forceinline__ const uint32_t* step_mask_row(const StepArgs& A, int row) {
+  if (A.mask_table == nullptr || A.mask_state == nullptr) return nullptr;
+  const int32_t state = A.mask_state[row];
+  return state >= 0 && state < A.mask_states ? A.mask_table + static_cast<int64_t>(state) * A.mask_words : nullptr;
+}
+
+// Fewer allowed ids than topK: the slots after the ordered entries' finite ones are the
+// -inf ids (masked ones and -inf logits) in ascending id order, as the reference's
+// stable descending sort leaves them (gemma-webgpu-engine/src/sampling.js:41-58 sorts the
+// masked logits of maskConstraintLogits, :88-103).  One warp; returns the new count.
+__device__ __noinline__ int step_fill_masked(Ent* sents, int ne, int k, const uint32_t* mrow, int64_t vocab,
+                                             int* mids, Ent* tail) {
+  const int lane = threadIdx.x & 31;
+  const int nwords = static_cast<int>((vocab + 31) >> 5);
+  int fill = 0;
+  for (int w0 = 0; w0 < nwords && fill < k; w0 += 32) {  // (warp-uniform)
+    const int wi = w0 + lane;
+    uint32_t zero = 0u;
+    if (wi < nwords) {
+      zero = ~__ldg(mrow + wi);
+      if (wi == nwords - 1 && (vocab & 31)) zero &= (1u << (vocab & 31)) - 1u;
+    }
+    const int c = __popc(zero);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += u;
+    }
+    int base = fill + incl - c;
+    for (uint32_t z = zero; z; z &= z - 1u) {
+      if (base < k) mids[base] = wi * 32 + __ffs(z) - 1;
+      ++base;
+    }
+    fill += __shfl_sync(kFullMask, incl, 31);
+  }
+  __syncwarp();
+  const int n_masked = fill < k ? fill : k;
+  int j0 = 0;  // the -inf tail of the ordered entries, merged with the masked ids by id
+  while (j0 < ne && sents[j0].key > -INFINITY) ++j0;
+  int t = 0;
+  if (lane == 0) {
+    int a = j0, b = 0;
+    while (j0 + t < k && (a < ne || b < n_masked)) {
+      if (b >= n_masked || (a < ne && sents[a].id < static_cast<uint32_t>(mids[b]))) tail[t++] = sents[a++];
+      else tail[t++] = Ent{-INFINITY, static_cast<uint32_t>(mids[b++]), 2u};
+    }
+    for (int i = 0; i < t; ++i) sents[j0 + i] = tail[i];
+  }
+  t = __shfl_sync(kFullMask, t, 0);
+  __syncwarp();
+  return j0 + t;
+}
+
+// MINB: CTAs per SM the register budget allows (1: up to 128 registers a thread, for
+// grids of at most one CTA per SM; 2: 64 registers, for batches of several rows).
+template <int DT, int MINB>
+__global__ void __launch_bounds__(kStepThreads, MINB) step_kernel(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ float s_wmax[kStepWarps], s_wrmax[kStepWarps];
   __shared__ uint32_t s_dead[kStepIds / 32];
@@ -276,7 +312,13 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     hl = A.history_len[row];
     if (tid < A.history_stride) hid = A.history[static_cast<int64_t>(row) * A.history_stride + tid];
   }
+  // the constraint row (sampling over maskConstraintLogits: disallowed ids are -inf)
   const int64_t id0 = static_cast<int64_t>(unit) * kStepIds + tid * 4;
+  uint32_t allow4 = 0xfu;
+  {
+    const uint32_t* mrow = step_mask_row(A, row);
+    if (mrow != nullptr && id0 < A.vocab) allow4 = (__ldg(mrow + (id0 >> 5)) >> (id0 & 31)) & 0xfu;
+  }
   float x[4];
   bool valid[4];
   if (id0 + 3 < A.vocab) {
@@ -306,7 +348,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   hl = hl < 0 ? 0 : (hl > A.history_stride ? static_cast<int>(A.history_stride) : hl);
   bool live[4];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) live[q] = valid[q];
+  for (int q = 0; q < 4; ++q) live[q] = valid[q] && ((allow4 >> q) & 1u);
   if (hl > 0) {  // (block-uniform; hl <= kStepMaxHist: one history position per thread)
     if (tid < kStepIds / 32) s_dead[tid] = 0u;
     __syncthreads();
@@ -315,7 +357,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     __syncthreads();
     const uint32_t dw = s_dead[tid >> 3] >> ((tid & 7) * 4);  // this thread's four ids
 #pragma unroll
-    for (int q = 0; q < 4; ++q) live[q] = valid[q] && !((dw >> q) & 1u);
+    for (int q = 0; q < 4; ++q) live[q] = live[q] && !((dw >> q) & 1u);
   }
   bool bad = false;
   float mx = -INFINITY, mraw = -INFINITY;
@@ -382,9 +424,14 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   if (lane == cw - 1) s_wkey[warp] = kk;
   {
     const double ws = warp_sum(static_cast<double>(sa)), wr = A.want_raw ? warp_sum(static_cast<double>(sr)) : 0.0;
+    int na = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) na += valid[q] && ((allow4 >> q) & 1u);
+    na = warp_sum_i(na);
     if (lane == 0) {
       s_wsum[warp] = ws;
       s_wraw[warp] = wr;
+      red_i[warp] = na;
     }
   }
   if (__any_sync(kFullMask, bad) && lane == 0) atomicOr(&s_wbad, 1u);
@@ -480,11 +527,17 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
       ru = __dadd_rn(ru, s_wraw[w]);
     }
     StepRec r{};
+    int na = 0;
+    for (int w = 0; w < kStepWarps; ++w) na += red_i[w];
+    r.n_allowed = na;
     r.m = m;
     r.raw_m = mr;
     r.s = m > -INFINITY ? su : 0.0;
     r.raw_s = mr > -INFINITY ? ru : 0.0;
-    r.flags = s_wbad ? GS_FLAG_ERR_NONFINITE : 0u;
+    r.flags = (s_wbad ? GS_FLAG_ERR_NONFINITE : 0u) |
+              (A.mask_table != nullptr && A.mask_state != nullptr && A.mask_state[row] >= A.mask_states
+                   ? GS_FLAG_ERR_INVALID
+                   : 0u);
 #pragma unroll
     for (int i = 0; i < kStepHead; ++i) r.head[i] = s_head[i];
     r.n = n_rec;
@@ -496,14 +549,18 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  const uint32_t* mrow = step_mask_row(A, row);
+  const bool has_mask = mrow != nullptr;
   // the history ids and their capped logits, early (random loads that overlap the records')
   uint32_t hv = 0xffffffffu;
   float hx = 0.0f;
+  bool hallow = true;  // the history id is allowed by the constraint row
   if (tid < hl) {
     hv = static_cast<uint32_t>(hid);  // (negative ids are >= 2^31 here)
     if (hv < static_cast<uint64_t>(A.vocab)) {
       hx = load_logit(rowbase, DT, hv);
       if (cap != 0.0f) hx = softcap(hx, cap, inv_cap);
+      if (has_mask) hallow = (__ldg(mrow + (hv >> 5)) >> (hv & 31)) & 1u;
     } else {
       hv = 0xffffffffu;
     }
@@ -528,6 +585,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   unsigned long long* scratch = A.sort_scratch + static_cast<int64_t>(row) * kStepMaxPacks;
   float mu = -INFINITY, rmu = -INFINITY;
   double su = 0.0, ru = 0.0;
+  int na_u = 0;
   unsigned long long hd[kStepHead] = {0ull, 0ull, 0ull, 0ull};
   if (tid < S) {
     const StepRec* st = reinterpret_cast<const StepRec*>(rec_row + static_cast<int64_t>(tid) * A.rec_bytes);
@@ -539,6 +597,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
 #pragma unroll
     for (int i = 0; i < kStepHead; ++i) hd[i] = __ldcg(&st->head[i]);
     un[tid] = __ldcg(&st->n);
+    na_u = __ldcg(&st->n_allowed);
     if (f) atomicOr(&s_flags, f);
   }
   if (tid == 0) {
@@ -562,20 +621,25 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     }
     unsigned long long wt = b;
     float wr = rmu;
+    int wn = na_u;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long t = __shfl_xor_sync(kFullMask, wt, o);
       wt = t > wt ? t : wt;
       wr = fmaxf(wr, __shfl_xor_sync(kFullMask, wr, o));
+      wn += __shfl_xor_sync(kFullMask, wn, o);
     }
     const uint32_t kc = __shfl_sync(kFullMask, key, cg <= 32 ? cg - 1 : 0);
     if (lane == 0) {
       s_wkey[warp] = cg <= 32 ? kc : 0u;
       s_gtop[warp] = wt;
       s_wrmax[warp] = wr;
+      red_i[warp] = wn;
     }
   }
   __syncthreads();
+  int64_t na_row = 0;  // ids the constraint row allows
+  for (int w = 0; w < g; ++w) na_row += red_i[w];
   uint32_t tk = s_wkey[0];
   unsigned long long top = s_gtop[0];
   float Mx = s_wrmax[0];  // the row's raw maximum (every id)
@@ -586,6 +650,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   }
   unsigned fl = s_flags;
   if (greedy) fl |= GS_FLAG_GREEDY;
+  if (has_mask && na_row == 0) fl |= GS_FLAG_ERR_DEADEND;
   const double T = pp->temperature;
   const double xtop = static_cast<double>(pack_value(top));
   double M = top == 0ull ? -INFINITY : (greedy ? xtop : __ddiv_rn(xtop, T));
@@ -624,7 +689,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
     if (tid < hl) {
       Ent e{-INFINITY, 0xffffffffu, 0xffffffffu};
-      if (hv != 0xffffffffu && hfirst[sl] == static_cast<uint32_t>(tid)) {
+      if (hv != 0xffffffffu && hallow && hfirst[sl] == static_cast<uint32_t>(tid)) {
         const double xp = penalise(static_cast<double>(hx), static_cast<double>(hcnt[sl]), rp, pres, freq);
         e = Ent{greedy ? xp : __ddiv_rn(xp, T), hv, 1u};
         pmax = e.key;
@@ -750,9 +815,9 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
   __syncthreads();
   // with penalised entries: the k best live packs and the penalised entries in the
   // reference's order (key descending, lower id first), by rank counting
-  const Ent* sents = nullptr;
+  Ent* sents = nullptr;
   int ne = 0;
-  if (hl > 0) {
+  if (hl > 0 || has_mask) {  // (block-uniform)
     Ent* ents = pent + kStepMaxHist;        // [kStepMaxHist + kStepMaxK]
     Ent* sw = ents + kStepMaxHist + kStepMaxK;  // [kStepMaxHist + kStepMaxK]
     const int nL = N < k ? N : k;
@@ -764,7 +829,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
     if (tid == 0) s_nq = 0;
     __syncthreads();
     {
-      const bool take = tid < hl && pent[tid].id != 0xffffffffu;
+      const bool take = tid < hl && hl > 0 && pent[tid].id != 0xffffffffu;
       const unsigned bal = __ballot_sync(kFullMask, take);
       if (bal) {
         const int leader = __ffs(bal) - 1;
@@ -789,7 +854,10 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const __grid_constan
 
   // ---- 5. one warp: probabilities, filters, draw, outputs ----
   const int nAll = sents ? ne : N;
-  const int nC = nAll < k ? nAll : k;
+  int nC = nAll < k ? nAll : k;
+  if (sents && has_mask && !greedy && ne < k && na_row < A.vocab)
+    nC = step_fill_masked(sents, ne, k, mrow, A.vocab, reinterpret_cast<int*>(wwork + 2560),
+                          reinterpret_cast<Ent*>(wwork + 2816));
   WWork w;
   {
     unsigned char* p = wwork;
@@ -914,7 +982,6 @@ int pow2_at_least(int n) {
 
 bool step_eligible(const gs_batch* b, int kmax, bool any_large, int rows) {
   if (rows < 1 || rows > kStepDoneRows || any_large || kmax < 1 || kmax > kStepMaxK) return false;
-  if (b->mask_table) return false;
   if (b->history && b->history_stride > kStepMaxHist) return false;
   if (b->dtype != GS_DTYPE_F32 && b->dtype != GS_DTYPE_BF16) return false;
   const int64_t esz = b->dtype == GS_DTYPE_F32 ? 4 : 2;
@@ -958,21 +1025,32 @@ cudaError_t launch_step(const gs_batch* b, const gs_outputs* o, const RowPlan& p
   a.history = b->history;
   a.history_len = b->history ? b->history_len : nullptr;
   a.history_stride = b->history ? b->history_stride : 0;
+  a.mask_table = b->mask_table;
+  a.mask_states = b->mask_states;
+  a.mask_words = b->mask_words;
+  a.mask_state = b->mask_table ? b->mask_state : nullptr;
   // shared memory: the merge tree's two list sets, or the last CTA's arrays
   const size_t tree = 2 * static_cast<size_t>(kStepWarps) * a.k2 * 8;
-  const size_t last = b->history ? kStepSmemHist : kStepSmemLast;
+  const size_t last = (b->history || b->mask_table) ? kStepSmemHist : kStepSmemLast;
   const size_t smem = tree > last ? tree : last;
   const int grid = b->rows * a.units;
-  static bool attr = false;  // (set once, outside any stream capture: the first call)
-  if (!attr) {
-    cudaFuncSetAttribute(step_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
-    cudaFuncSetAttribute(step_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
-    attr = true;
+  static std::atomic<uint64_t> attr{0};  // (set on each device's first call)
+  if (device_todo(attr)) {
+    cudaFuncSetAttribute(step_kernel<GS_DTYPE_F32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
+    cudaFuncSetAttribute(step_kernel<GS_DTYPE_BF16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
+    cudaFuncSetAttribute(step_kernel<GS_DTYPE_F32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
+    cudaFuncSetAttribute(step_kernel<GS_DTYPE_BF16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemMax);
+    mark_device_done(attr);
   }
+  // one CTA per SM at most (a B = 1 call at V = 262144: 128 units): the larger register
+  // budget (no spills); more: two CTAs per SM, halving the waves of an 8-row batch
+  const bool one = grid <= sm_count();
   if (b->dtype == GS_DTYPE_F32) {
-    step_kernel<GS_DTYPE_F32><<<grid, kStepThreads, smem, st>>>(a);
+    if (one) step_kernel<GS_DTYPE_F32, 1><<<grid, kStepThreads, smem, st>>>(a);
+    else step_kernel<GS_DTYPE_F32, 2><<<grid, kStepThreads, smem, st>>>(a);
   } else {
-    step_kernel<GS_DTYPE_BF16><<<grid, kStepThreads, smem, st>>>(a);
+    if (one) step_kernel<GS_DTYPE_BF16, 1><<<grid, kStepThreads, smem, st>>>(a);
+    else step_kernel<GS_DTYPE_BF16, 2><<<grid, kStepThreads, smem, st>>>(a);
   }
   return cudaGetLastError();
 }

@@ -470,17 +470,17 @@ cudaError_t launch_stream(const StreamArgs& a, int dtype, int rows, size_t smem,
   if (a.kmax <= pipe_max_k() && stream2_eligible(a, dtype, rows))
     return launch_stream2(a, dtype, rows, stream2_smem_bytes(a.chunk), st, sm_count());
   if (dtype == GS_DTYPE_F32) {
-    static bool attr = false;
-    if (!attr) {
+    static std::atomic<uint64_t> attr{0};  // (set on each device's first call)
+    if (device_todo(attr)) {
       cudaFuncSetAttribute(stream_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      attr = true;
+      mark_device_done(attr);
     }
     stream_kernel<GS_DTYPE_F32><<<units, kStreamThreads, smem, st>>>(a);
   } else {
-    static bool attr = false;
-    if (!attr) {
+    static std::atomic<uint64_t> attr{0};  // (set on each device's first call)
+    if (device_todo(attr)) {
       cudaFuncSetAttribute(stream_kernel<GS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      attr = true;
+      mark_device_done(attr);
     }
     stream_kernel<GS_DTYPE_BF16><<<units, kStreamThreads, smem, st>>>(a);
   }

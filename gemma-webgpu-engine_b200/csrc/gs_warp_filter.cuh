@@ -193,7 +193,6 @@ __device__ inline uint32_t warp_filter_and_draw(WWork& w, int n, double min_p, d
     }
     __syncwarp();
     warp_sort_kv(w.skey, w.sval, k2, lane);
-    uint32_t* ids_tmp = reinterpret_cast<uint32_t*>(w.skey);
     double pt[kWFilterMax / 32];
     uint32_t it[kWFilterMax / 32];
 #pragma unroll
@@ -214,7 +213,6 @@ __device__ inline uint32_t warp_filter_and_draw(WWork& w, int n, double min_p, d
         w.cid[j] = it[q];
       }
     }
-    (void)ids_tmp;
     __syncwarp();
     n = keep;
   }
