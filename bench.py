@@ -531,8 +531,10 @@ def config_leg(pkg, W, sampler, dev, name, rows, dtype=None, mask=True, history=
         ("_unmasked" if (name == "C4" and not mask) else "")
     if large:
         kern, kern_us = "histogram path (large_hist, large_select, large_gather, large_resolve)", merge_us
-    else:
+    elif mask and wl.mask_table is not None:
         kern, kern_us = "gs::stream2_kernel (streaming pass)", stream_us
+    else:
+        kern, kern_us = "gs::dense_kernel (streaming pass)", stream_us
     achieved = rows * bpr / (kern_us / 1e6) / 1e9
     tpr = traffic_per_row(tag)
     if label:
@@ -704,16 +706,24 @@ def lm_head_leg(pkg, sampler, stream):
                presencePenalty=0.0, frequencyPenalty=0.0)]
     st = torch.tensor([pkg.SeededRandom(42).state], dtype=torch.float64, device=a_all.device)
     a1, s1 = a_all[:1].contiguous(), s_all[:1].contiguous()
-    for _ in range(3):
-        head.sample(a1, s1, p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(65)]
-    evs[0].record(stream)
-    for i in range(64):
-        head.sample(a1, s1, p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream)
-        evs[i + 1].record(stream)
-    torch.cuda.synchronize()
-    lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(64))
-    fused = head.fused_calls
+
+    def route_p50(route):
+        head.set_route(route)
+        f0 = head.fused_calls
+        for _ in range(3):
+            head.sample(a1, s1, p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream)
+        evs[0].record(stream)
+        for i in range(64):
+            head.sample(a1, s1, p1, softcap=30.0, rng_state=st, stream=stream.cuda_stream)
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+        lat = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(64))
+        return lat, head.fused_calls - f0
+
+    lat, fused = route_p50("auto")
+    lat_f, _ = route_p50("fused")
+    head.set_route("auto")
     # the same step as two calls (logits to HBM, then gs_sample), for comparison
     lg1 = torch.empty((1, V), dtype=torch.float32, device=a_all.device)
     st2 = st.clone()
@@ -728,10 +738,12 @@ def lm_head_leg(pkg, sampler, stream):
     torch.cuda.synchronize()
     lat2 = sorted(evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(64))
     out["sample_b1"] = {"p50_us": lat[32], "p95_us": lat[int(64 * 0.95)],
-                        "route": "fused (logits kept on chip, shard-record merge)" if fused >= 64 else "scratch",
-                        "two_step_p50_us": lat2[32],
-                        "timing": "CUDA events between consecutive gs_lm_head_sample calls (LM head + sampling); "
-                                  "two_step: gs_lm_head_logits then gs_sample per step"}
+                        "route": "fused (logits kept on chip, shard-record merge)" if fused >= 67
+                                 else "two-step inside the call (GEMV, then the single-launch decode step)",
+                        "fused_route_p50_us": lat_f[32], "two_step_p50_us": lat2[32],
+                        "timing": "CUDA events between consecutive gs_lm_head_sample calls (LM head + sampling; "
+                                  "default route, then the fused route forced); two_step: gs_lm_head_logits then "
+                                  "gs_sample per step"}
     head.close()
     # the oracle's exact LM head on the host (one core), one row
     c0 = time.perf_counter()

@@ -26,6 +26,10 @@ GS_ENONFINITE = 9
 GS_DTYPE_F32 = 0
 GS_DTYPE_BF16 = 1
 
+LM_ROUTE_AUTO = 0
+LM_ROUTE_FUSED = 1
+LM_ROUTE_TWO_STEP = 2
+
 FLAG_BOUNDARY_TOP_P = 1 << 0
 FLAG_BOUNDARY_DRAW = 1 << 1
 FLAG_BOUNDARY_MIN_P = 1 << 2
@@ -53,7 +57,7 @@ EXPORTS = (
     "gs_constraint_last_error", "gs_constraint_build_masks", "gs_lm_head_create", "gs_lm_head_destroy",
     "gs_lm_head_last_error", "gs_lm_head_logits", "gs_lm_head_sample", "gs_lm_head_check",
     "gs_lm_head_fused_calls", "gs_build_reasoning_mask_rows", "gs_nccl_unique_id", "gs_nccl_create",
-    "gs_nccl_destroy", "gs_nccl_last_error", "gs_shard_sample",
+    "gs_nccl_destroy", "gs_nccl_last_error", "gs_shard_sample", "gs_lm_head_set_route",
 )
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -183,6 +187,7 @@ def lib() -> ctypes.CDLL:
     L.gs_lm_head_logits.argtypes = [P, P, i64, P, i32, P, i64, P]
     L.gs_lm_head_check.argtypes = [P, ctypes.POINTER(i32)]
     L.gs_lm_head_fused_calls.argtypes = [P]
+    L.gs_lm_head_set_route.argtypes = [P, i32]
     L.gs_lm_head_sample.argtypes = [P, P, i64, P, ctypes.POINTER(GsBatch), ctypes.POINTER(GsOutputs), P]
     L.gs_softcap.argtypes = [P, P, P, i64, f32, P]
     L.gs_softcap_digest.argtypes = [P, u64, u64, f32, ctypes.POINTER(u64)]

@@ -72,6 +72,7 @@ struct gs_lm_head {
   unsigned char* records = nullptr;
   size_t records_bytes = 0;
   int64_t fused_calls = 0;
+  int32_t route = GS_LM_ROUTE_AUTO;
   int num_sms = 0;
   std::string err;
 };
@@ -1516,6 +1517,17 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
       kcap = pl.k_eff > kcap ? pl.k_eff : kcap;
     }
   }
+  if (fused && h->route == GS_LM_ROUTE_TWO_STEP) fused = false;
+  if (fused && h->route == GS_LM_ROUTE_AUTO) {
+    // the two-step route is faster wherever its gs_sample takes the single-launch decode
+    // step (one launch after the GEMV against the records kernel plus a 147-record merge)
+    gs_batch b2 = *batch;
+    b2.logits = nullptr;  // (the scratch it would sample: 256-byte aligned)
+    b2.dtype = GS_DTYPE_F32;
+    b2.vocab = h->vocab;
+    b2.row_stride = h->vocab;
+    if (step_eligible(&b2, kcap, false, rows)) fused = false;
+  }
   const int tps = static_cast<int>((h->tiles + h->num_sms - 1) / h->num_sms);
   const int shards = static_cast<int>((h->tiles + tps - 1) / tps);
   const int nb = rows <= 1 ? 1 : 2;
@@ -1631,6 +1643,14 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
 }
 
 int64_t gs_lm_head_fused_calls(const gs_lm_head* h) { return h ? h->fused_calls : -1; }
+
+gs_status gs_lm_head_set_route(gs_lm_head* h, int32_t route) {
+  if (!h) return GS_EINVAL;
+  if (route != GS_LM_ROUTE_AUTO && route != GS_LM_ROUTE_FUSED && route != GS_LM_ROUTE_TWO_STEP)
+    return lfail(h, GS_EINVAL, "route must be GS_LM_ROUTE_AUTO, GS_LM_ROUTE_FUSED or GS_LM_ROUTE_TWO_STEP");
+  h->route = route;
+  return GS_OK;
+}
 
 gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out) {
   if (!h || !timed_out) return GS_EINVAL;

@@ -20,7 +20,8 @@ from .sampling import SamplerError
 class GpuLmHead:
     """Packed weights resident on the sampler's device (gs_lm_head_create)."""
 
-    def __init__(self, sampler, packed, row_scales, input_scale: float = 0.0, output_scale: float = 0.0):
+    def __init__(self, sampler, packed, row_scales, input_scale: float = 0.0, output_scale: float = 0.0,
+                 route: str = "auto"):
         self._L = _lib.lib()
         packed = np.ascontiguousarray(packed, np.uint32)
         if packed.ndim != 2:
@@ -39,6 +40,18 @@ class GpuLmHead:
         if st != _lib.GS_OK:
             msg = (self._L.gs_last_error(sampler.handle) or b"").decode()
             raise ValueError(msg) if st == _lib.GS_EINVAL else SamplerError(st, msg)
+        self.set_route(route)
+
+    def set_route(self, route: str):
+        """Route of sample(): "auto" (the fused route only where it measured faster than
+        logits + gs_sample), "fused" (wherever it applies) or "two-step" (never)."""
+        codes = {"auto": _lib.LM_ROUTE_AUTO, "fused": _lib.LM_ROUTE_FUSED, "two-step": _lib.LM_ROUTE_TWO_STEP}
+        if route not in codes:
+            raise ValueError(f"route must be one of {sorted(codes)}")
+        st = self._L.gs_lm_head_set_route(self._h, codes[route])
+        if st != _lib.GS_OK:
+            raise SamplerError(st, (self._L.gs_lm_head_last_error(self._h) or b"").decode())
+        self.route = route
 
     def close(self):
         if self._h:

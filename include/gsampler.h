@@ -260,6 +260,11 @@ gs_status gs_lm_head_check(gs_lm_head* h, int32_t* timed_out);
  * LM head pass to sampleToken, decode-model.ts:135-139 then sampling.ts:18), sampled as by
  * gs_sample on the context the head was created on.  batch->logits must be NULL,
  * batch->vocab 0 or the head's vocab; dtype and row_stride are set here.
+ * Route (gs_lm_head_set_route): GS_LM_ROUTE_AUTO (the default) takes the fused route
+ * only where it measured faster than the two-step route, i.e. for batches the two-step
+ * route cannot serve with the single-launch decode step (a penalty history longer than
+ * 512 ids at one row); GS_LM_ROUTE_FUSED takes it wherever it applies;
+ * GS_LM_ROUTE_TWO_STEP never.
  * Fused route (1 or 2 rows, input_scale != 0, a penalty history only at one row with a
  * history_stride of at most 4096, every row greedy or 1 <= topK <= 64): the logits stay on chip; each block of vocabulary ids writes the
  * record of a vocabulary shard (its statistics and top-k candidates, as
@@ -277,6 +282,13 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
 /* Number of gs_lm_head_sample calls on `h` that took the fused route (diagnostics; no
  * reference counterpart).  -1 for a NULL handle. */
 int64_t gs_lm_head_fused_calls(const gs_lm_head* h);
+/* Route of gs_lm_head_sample on `h` (no reference counterpart: the reference always
+ * reads the logits back and samples them on the host).  GS_EINVAL for a NULL handle or
+ * an unknown route. */
+#define GS_LM_ROUTE_AUTO 0
+#define GS_LM_ROUTE_FUSED 1
+#define GS_LM_ROUTE_TWO_STEP 2
+gs_status gs_lm_head_set_route(gs_lm_head* h, int32_t route);
 
 /* Elementwise soft cap, the same routine the sampling pass applies (no reference
  * counterpart: the reference never applies its declared cap). */

@@ -63,6 +63,7 @@ def test_lm_head_entry_points_reject_null_handles(pkg):
     assert L.gs_lm_head_fused_calls(None) == -1
     assert L.gs_lm_head_sample(None, None, 0, None, None, None, None) == pkg._lib.GS_EINVAL
     assert L.gs_lm_head_logits(None, None, 0, None, 0, None, 0, None) == pkg._lib.GS_EINVAL
+    assert L.gs_lm_head_set_route(None, pkg._lib.LM_ROUTE_FUSED) == pkg._lib.GS_EINVAL
 
 
 def test_prepare_params_matches_per_config_conversion():

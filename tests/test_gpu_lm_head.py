@@ -211,7 +211,7 @@ def test_fused_matches_oracle(sampler, vocab, rows, topk, masked, hidden, out_sc
     logits = O.lm_head(packed, scales, act, act_sum, out_scale=out_scale, in_scale=0.02)
     ids, margins, cands, st = oracle_rows(O, logits, vocab, 30.0, [dict(params[0], repetitionWindow=0)],
                                           mask_table=table, mask_state=state, rng_state=rng)
-    h = LM.GpuLmHead(sampler, packed, scales, 0.02, out_scale)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, out_scale, route="fused")
     try:
         r = torch.from_numpy(rng).cuda()
         mk = {} if table is None else dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(),
@@ -238,7 +238,7 @@ def test_fused_matches_two_step(sampler, rows, temperature, topk, masked):
     if masked:
         table, state = _mask(vocab, rows, 17 + rows, density=0.3)
         mk = dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(), mask_state=torch.from_numpy(state).cuda())
-    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0, route="fused")
     try:
         a, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
         r1 = torch.tensor([float(70 + i) for i in range(rows)], dtype=torch.float64, device="cuda")
@@ -264,7 +264,7 @@ def test_fused_error_rows_and_routes(sampler):
     packed, scales, act, act_sum = LM.synthetic(vocab, 1536, 2, seed=5, input_scale=0.02)
     table, state = _mask(vocab, 2, 9, states=8)
     L = pkg._lib
-    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0, route="fused")
     try:
         a = torch.from_numpy(act).cuda()
         for case in ("state", "nan"):
@@ -302,6 +302,38 @@ def test_fused_error_rows_and_routes(sampler):
         h.close()
 
 
+def test_route_choice(sampler):
+    # auto: the two-step route where gs_sample takes the single-launch decode step (no
+    # history, or one of at most 512 ids), the fused route for one row with a longer
+    # history; "two-step" never fuses; both routes give the same ids
+    vocab = 262144
+    packed, scales, act, act_sum = LM.synthetic(vocab, 1536, 1, seed=12, input_scale=0.02)
+    a, s = torch.from_numpy(act).cuda(), torch.from_numpy(act_sum).cuda()
+    g = np.random.default_rng(3)
+    long_hist = torch.from_numpy(g.integers(0, vocab, (1, 1024)).astype(np.int32)).cuda()
+    short_hist = long_hist[:, :256].contiguous()
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    try:
+        assert h.route == "auto"
+        ids = {}
+        for route, hist, fused in (("auto", None, 0), ("auto", short_hist, 0), ("auto", long_hist, 1),
+                                   ("two-step", long_hist, 0), ("fused", None, 1)):
+            h.set_route(route)
+            before = h.fused_calls
+            kw = {} if hist is None else dict(history=hist, history_len=torch.tensor([hist.shape[1]], dtype=torch.int32,
+                                                                                       device="cuda"))
+            res = h.sample(a, s, [C1_PARAMS], softcap=30.0, rng_state=torch.tensor([9.0], dtype=torch.float64,
+                                                                                   device="cuda"), **kw)
+            torch.cuda.synchronize()
+            assert h.fused_calls - before == fused, (route, None if hist is None else hist.shape[1])
+            ids.setdefault(None if hist is None else hist.shape[1], set()).add(int(res.ids[0]))
+        assert all(len(v) == 1 for v in ids.values()), ids
+        with pytest.raises(ValueError):
+            h.set_route("fastest")
+    finally:
+        h.close()
+
+
 @pytest.mark.parametrize("topk,masked,temperature", [(40, False, 0.8), (64, True, 0.8), (40, False, 0.0), (5, True, 1.2)])
 def test_fused_history_matches_oracle(sampler, topk, masked, temperature):
     # one row with a penalty history (repeated ids, the row's best ids, a negative id, ids
@@ -319,7 +351,7 @@ def test_fused_history_matches_oracle(sampler, topk, masked, temperature):
     ids, margins, cands, st = oracle_rows(O, logits, vocab, 30.0, [dict(params[0], repetitionWindow=len(hist))],
                                           history=history, history_len=history_len, mask_table=table,
                                           mask_state=state, rng_state=rng)
-    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0)
+    h = LM.GpuLmHead(sampler, packed, scales, 0.02, 0.0, route="fused")
     try:
         r = torch.from_numpy(rng).cuda()
         mk = {} if table is None else dict(mask_table=torch.from_numpy(table.view(np.int32)).cuda(),
