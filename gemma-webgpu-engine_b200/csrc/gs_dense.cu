@@ -12,15 +12,18 @@
 //     sum of the squares per sub-tile (a sum that is not below 1 means a value at or past
 //     the cap, an infinity or a NaN: only then are the sub-tile's values checked one by
 //     one and the out-of-range ones redone by the full routine);
-//   * the per-vector maximum (the candidate test, the sum's running reference and the
-//     lane maximum all derive from it);
+//   * the lane's maximum of its 16 values (the candidate test, the sum's running
+//     reference and the unit's maximum all derive from it);
 //   * the sum of 2^((x - m)·log2e/T) in packed arithmetic.
-// Penalised ids are few (at most the history length per row), so they are not masked per
-// element: a tile holding some marks their positions in a per-lane bit word, and only
-// the sub-tiles containing one take the per-element path, where they become -inf (dead).
-// A sub-tile with candidates (values at or above the running top-k threshold) writes its
-// capped values over the lane's own slots of the stage it has just read, from which the
-// candidates are offered one per lane per round, so the soft cap is never computed twice.
+// Penalised ids are few (at most the history length per row): their tiles are known from
+// the unit's sorted list (a warp-uniform test per tile), and only there do the lanes
+// holding one set it to -inf (dead).  Top-k candidates are not extracted where they are
+// read: a lane whose maximum reaches the running threshold queues its 16 capped values
+// (with their tile, lane and dead bits) in a 16-chunk per-warp queue, and a full queue is
+// tested against the threshold of that moment one chunk per lane, the survivors offered
+// to the candidate buffer; the buffer is cut back to the k best (radix select) once it
+// holds 2k + 32 packs, which raises the threshold.  The per-id cost of a sub-tile with a
+// candidate is then a ballot and four 16-byte stores instead of a per-element extraction.
 #include "gs_device.cuh"
 #include "gs_block.cuh"
 #include "gs_internal.cuh"
@@ -35,8 +38,9 @@ constexpr int kDThreads = kDWarps * 32;
 constexpr int kDTileBytes = 2048;             // ids per tile: 512 f32 / 1024 bf16 (4 vectors per lane)
 constexpr int kDStages = 5;                   // per-warp ring: four tiles in flight ahead of the one read
 constexpr int kDPenCap = 256;                 // sorted penalised offsets per unit (else scanned per tile)
-constexpr int kDWarpCand = 256;               // per-warp candidate buffer
-constexpr int kDWarpBytes = kDStages * kDTileBytes + kDPenCap * 4 + kDWarpCand * 8 + 256 * 4;
+constexpr int kDWarpCand = 160;               // per-warp candidate buffer
+constexpr int kDPend = 16;                    // queued lane chunks (16 capped values, a tag, dead bits)
+constexpr int kDWarpBytes = kDStages * kDTileBytes + kDPenCap * 4 + kDWarpCand * 8 + kDPend * (64 + 8);
 constexpr int kDMaxK = 112;
 
 static_assert(kDWarpBytes % 128 == 0, "per-warp slices keep 128-byte alignment");
@@ -133,10 +137,14 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
   unsigned char* ring = dsm + warp * kDWarpBytes;
   uint32_t* pen = reinterpret_cast<uint32_t*>(ring + kDStages * kDTileBytes);
   unsigned long long* wbuf = reinterpret_cast<unsigned long long*>(pen + kDPenCap);
-  unsigned* whist = reinterpret_cast<unsigned*>(wbuf + kDWarpCand);
+  float* pendf = reinterpret_cast<float*>(wbuf + kDWarpCand);
+  uint32_t* ptag = reinterpret_cast<uint32_t*>(pendf + kDPend * 16);
+  uint32_t* pdead = ptag + kDPend;
   const unsigned char* logits = static_cast<const unsigned char*>(A.logits);
   const float cap = A.softcap, inv_cap = A.inv_softcap;
   const unsigned lane_lt = (1u << lane) - 1u;
+  const uint32_t ring0 = smem_addr(ring) + static_cast<uint32_t>(lane) * 16u;  // this lane's slot of stage 0
+  const uint32_t ring_end = ring0 + kDStages * kDTileBytes;
 
   for (int unit = dense_next_unit(A, first_unit, n_units, total_warps); unit < n_units;
        unit = dense_next_unit(A, unit + total_warps, n_units, total_warps)) {
@@ -146,23 +154,28 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
     const int gn = static_cast<int>(ghi > glo ? ghi - glo : 0);
     const int nfull = gn / TE;  // full tiles; a shorter last tile is read element by element
     const unsigned char* rowp = logits + (static_cast<int64_t>(row) * A.row_stride + glo) * ESZ;
-    const uint4* rv = reinterpret_cast<const uint4*>(rowp);
 
-    // this lane's vectors of tile t into stage t % kDStages (one commit group per tile,
-    // empty past the last full tile, so that the group count stays in step)
-    auto issue = [&](int t) {
-      if (t < nfull) {
-        const uint32_t dst = smem_addr(ring + (t % kDStages) * kDTileBytes) + lane * 16u;
-        const uint4* src = rv + static_cast<int64_t>(t) * (TE / VE) + lane;
+    // Tiles go into the ring in order: this lane's four vectors of the next tile into the
+    // next stage (one commit group per tile, empty past the last full tile, so that the
+    // group count stays in step).
+    const unsigned char* src = rowp + lane * 16;
+    uint32_t wr = ring0;
+    int issued = 0;
+    auto issue = [&]() {
+      if (issued < nfull) {
 #pragma unroll
         for (int q = 0; q < VPT; ++q)
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + q * 512u), "l"(src + q * 32) : "memory");
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(wr + q * 512u), "l"(src + q * 512) : "memory");
+        src += kDTileBytes;
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
+      ++issued;
+      wr += kDTileBytes;
+      if (wr == ring_end) wr = ring0;
     };
     // the unit's first tiles are in flight while its penalty list is built
 #pragma unroll
-    for (int t = 0; t < kDStages - 1; ++t) issue(t);
+    for (int t = 0; t < kDStages - 1; ++t) issue();
 
     const RowPlan* pp = A.plans ? A.plans + row : &A.plan0;
     const int k_eff = pp->k_eff;
@@ -209,30 +222,44 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
     }
     __syncwarp();
     int pen_cur = 0;
+    // the next tile holding a penalised id (warp-uniform; every tile when scanning)
+    int dead_t = pen_scan ? 0 : (pen_n > 0 ? static_cast<int>(pen[0] / TE) : INT_MAX);
 
     float m_t = -INFINITY;                    // warp-uniform running reference of the sum
+    float m_lim = -INFINITY;                  // m_t + dlim
     float lmx = -INFINITY;                    // this lane's maximum of the live values
     double s_t = 0.0;                         // this lane's sum relative to m_t
     uint32_t bad = 0;
     int wcnt = 0;                             // warp-uniform candidate count
+    int pend_n = 0;                           // warp-uniform pending chunk count
     unsigned long long wtau = 0;              // packs <= wtau cannot be among the unit's k best
+    float tau_x = -INFINITY;                  // the value of wtau's key (the candidate test)
     unsigned long long bp = 0;                // k = 1: the lane's best pack ...
     float bx = -INFINITY;                     // ... and its value
-    int wcap = 4 * k_eff + 64;
+    int wcap = 2 * k_eff + 32;
     wcap = wcap > kDWarpCand - 32 ? kDWarpCand - 32 : wcap;
     unsigned long long* rtau = A.row_tau ? A.row_tau + row : nullptr;
 
-    auto compact = [&]() {
+    auto set_tau = [&](unsigned long long v) {  // warp-uniform
+      if (v > wtau) {
+        wtau = v;
+        tau_x = key32_value(static_cast<uint32_t>(wtau >> 32));
+      }
+    };
+    // the k best of the buffer (radix select; `hist` is 1 KB of this warp's shared memory
+    // that nothing else uses at the time)
+    auto compact = [&](unsigned* hist) {
       __syncwarp();
-      const unsigned long long kth = warp_select_packs(wbuf, wcnt, k_eff, whist, lane);
-      wtau = kth > wtau ? kth : wtau;
+      const unsigned long long kth = warp_select_packs(wbuf, wcnt, k_eff, hist, lane);
+      set_tau(kth);
       wcnt = k_eff;
       if (rtau && lane == 0) atomicMax(rtau, kth);
+      __syncwarp();
     };
     // One pack per lane into the candidate buffer (the whole warp calls).  True when this
     // lane's pack is settled (stored, below the threshold, or none); false when the buffer
     // was full and it must be offered again.
-    auto offer = [&](bool has, unsigned long long pk) -> bool {
+    auto offer = [&](bool has, unsigned long long pk, unsigned* hist) -> bool {
       const bool keep = has && pk > wtau;
       const unsigned kb = __ballot_sync(kFullMask, keep);
       const int nk = __popc(kb);
@@ -241,16 +268,50 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
       if (keep && rank < space) wbuf[wcnt + rank] = pk;
       wcnt += nk < space ? nk : space;
       const bool done = !keep || rank < space;
-      if (nk > space) compact();
+      if (nk > space) compact(hist);
       return done;
+    };
+    // The pending chunks (a lane's 16 capped values whose maximum reached the threshold
+    // when they were read) against the current threshold: one chunk per lane, its values
+    // at or above it offered to the buffer.  Tag: tile << 8 | sub-tile << 5 | lane; the
+    // chunk's penalised positions (-inf there, but not candidates) beside it.
+    auto flush = [&](unsigned* hist) {
+      __syncwarp();
+      uint32_t sb = 0u, tag = 0u;
+      if (lane < pend_n) {
+        const float4* cv = reinterpret_cast<const float4*>(pendf + lane * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = cv[q];
+          sb |= (v.x >= tau_x ? 1u : 0u) << (q * 4);
+          sb |= (v.y >= tau_x ? 1u : 0u) << (q * 4 + 1);
+          sb |= (v.z >= tau_x ? 1u : 0u) << (q * 4 + 2);
+          sb |= (v.w >= tau_x ? 1u : 0u) << (q * 4 + 3);
+        }
+        tag = ptag[lane];
+        sb &= ~pdead[lane];
+      }
+      const int ct = static_cast<int>(tag >> 8), cs = static_cast<int>((tag >> 5) & 7u), cl = static_cast<int>(tag & 31u);
+      while (__any_sync(kFullMask, sb != 0u)) {
+        const bool has = sb != 0u;
+        unsigned long long pk = 0ull;
+        if (has) {
+          const int e = __ffs(sb) - 1;
+          const int off = ct * TE + ((cs * VPS + e / VE) * 32 + cl) * VE + e % VE;
+          pk = make_pack(pendf[lane * 16 + e], id_base + static_cast<uint32_t>(off));
+        }
+        if (offer(has, pk, hist) && has) sb &= sb - 1u;
+      }
+      pend_n = 0;
+      __syncwarp();
     };
     auto rescale = [&](float mt) {  // warp-uniform
       if (mt > m_t) {
         if (m_t > -INFINITY) s_t = __dmul_rn(s_t, exp2(__dmul_rn(static_cast<double>(m_t) - static_cast<double>(mt), a2)));
         m_t = mt;
+        m_lim = m_t + dlim;
       }
     };
-    auto tau_value = [&]() { return wtau ? key32_value(static_cast<uint32_t>(wtau >> 32)) : -INFINITY; };
 
     // Dead bits of tile t (penalised ids): bit sub*16 + j*VE + i of the owning lane.  The
     // sorted list is walked by the whole warp (its next entry is the same for every lane).
@@ -276,19 +337,34 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
       return dead;
     };
 
-    // One full tile from its stage `st`.  Float32 sub-tiles with candidates write their
-    // capped values over the lane's own slots of the stage (read before), the scratch the
-    // candidates are taken from; bfloat16 stages keep their 2-byte values and a candidate
-    // is capped again from there.
-    auto tile = [&](unsigned char* st, int t) {
-      const int t0 = t * TE;
-      const uint32_t dead = dead_bits(t0, TE);
-#pragma unroll 1
+    // ---- the unit's full tiles: kDStages - 1 in flight while one is worked on ----
+    unsigned long long rt_next = rtau && k_eff > 1 ? *reinterpret_cast<volatile unsigned long long*>(rtau) : 0ull;
+    uint32_t rd = ring0;
+    unsigned char* const ring_lane = ring + lane * 16;
+    for (int t = 0; t < nfull; ++t) {
+      issue();  // (into the stage read at t - 1)
+      asm volatile("cp.async.wait_group %0;" ::"n"(kDStages - 1) : "memory");
+      unsigned char* st = ring_lane + (rd - ring0);    // this lane's slot of the stage read now
+      unsigned* sthist = reinterpret_cast<unsigned*>(ring + (rd - ring0));  // the stage as scratch (1 KB)
+      if (rtau && k_eff > 1) {  // the row's shared bound, read one tile ahead
+        set_tau(rt_next);
+        rt_next = *reinterpret_cast<volatile unsigned long long*>(rtau);
+      }
+      uint32_t dead = 0u;
+      const bool dead_tile = t == dead_t;  // (warp-uniform)
+      if (dead_tile) {
+        dead = dead_bits(t * TE, TE);
+        dead_t = pen_scan ? t + 1 : (pen_cur < pen_n ? static_cast<int>(pen[pen_cur] / TE) : INT_MAX);
+      }
+      uint4 raw[VPT];  // this lane's vectors of the tile
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) raw[j] = *reinterpret_cast<const uint4*>(st + j * 512);
+#pragma unroll
       for (int sub = 0; sub < NSUB; ++sub) {
         const uint32_t dsub = (dead >> (sub * 16)) & 0xffffu;
         float x[VPS][VE];
 #pragma unroll
-        for (int j = 0; j < VPS; ++j) LD::vec(st + ((sub * VPS + j) * 32 + lane) * 16, x[j]);
+        for (int j = 0; j < VPS; ++j) LD::vec(reinterpret_cast<const unsigned char*>(&raw[sub * VPS + j]), x[j]);
         bool rbad = false;  // a value outside the polynomial's range, an infinity or a NaN
         if (cap != 0.0f) {
           float2 za = make_float2(0.0f, 0.0f);
@@ -312,40 +388,41 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
           rbad = !(fabsf(xa.x + xa.y) < INFINITY);  // a NaN or an infinity (or a huge sum)
         }
         if (__any_sync(kFullMask, rbad)) {
-          // per element: dead ids -> -inf, out-of-range values -> the full routine, NaN -> error
+          // out-of-range values -> the full routine, NaN -> error
 #pragma unroll
           for (int j = 0; j < VPS; ++j) {
             float r[VE];
-            LD::vec(st + ((sub * VPS + j) * 32 + lane) * 16, r);
+            if constexpr (DT == GS_DTYPE_F32) {
+              LD::vec(st + j * 512, r);  // (f32: the stage still holds the raw tile)
+            } else {
+              LD::vec(reinterpret_cast<const unsigned char*>(&raw[sub * VPS + j]), r);
+            }
 #pragma unroll
             for (int i = 0; i < VE; ++i) {
-              if ((dsub >> (j * VE + i)) & 1u) {
-                x[j][i] = -INFINITY;
-              } else {
-                if (cap != 0.0f) {
-                  const float y = __fmul_rn(r[i], inv_cap);
-                  if (!(__fmul_rn(y, y) < kSoftcapPolyZ)) x[j][i] = dense_softcap_slow(r[i], cap, inv_cap);
-                }
-                if (x[j][i] != x[j][i]) bad |= 1u;
+              if (cap != 0.0f) {
+                const float y = __fmul_rn(r[i], inv_cap);
+                if (!(__fmul_rn(y, y) < kSoftcapPolyZ)) x[j][i] = dense_softcap_slow(r[i], cap, inv_cap);
               }
+              if (x[j][i] != x[j][i] && !((dsub >> (j * VE + i)) & 1u)) bad |= 1u;
             }
           }
-        } else if (__any_sync(kFullMask, dsub != 0u)) {
-          // penalised ids only: dead -> -inf
+        }
+        if (dead_tile && __any_sync(kFullMask, dsub != 0u)) {
+          // penalised ids -> -inf (the vectors holding one)
 #pragma unroll
           for (int j = 0; j < VPS; ++j)
+            if ((dsub >> (j * VE)) & ((1u << VE) - 1u)) {
 #pragma unroll
-            for (int i = 0; i < VE; ++i)
-              if ((dsub >> (j * VE + i)) & 1u) x[j][i] = -INFINITY;
+              for (int i = 0; i < VE; ++i)
+                if ((dsub >> (j * VE + i)) & 1u) x[j][i] = -INFINITY;
+            }
         }
-        float vmx[VPS];
         float tmax = -INFINITY;
 #pragma unroll
         for (int j = 0; j < VPS; ++j) {
           float m = x[j][0];
 #pragma unroll
           for (int i = 1; i < VE; ++i) m = fmaxf(m, x[j][i]);
-          vmx[j] = m;
           tmax = fmaxf(tmax, m);
         }
         if (k_eff == 1) {
@@ -362,7 +439,7 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
                 }
             if (fj >= 0) {
               bx = tmax;
-              bp = make_pack(tmax, id_base + static_cast<uint32_t>(t0 + ((sub * VPS + fj) * 32 + lane) * VE + fi));
+              bp = make_pack(tmax, id_base + static_cast<uint32_t>(t * TE + ((sub * VPS + fj) * 32 + lane) * VE + fi));
             }
           }
         } else if (k_eff > 1) {
@@ -371,7 +448,9 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
             // search such that at least k live values there are >= value(K)
             int c = 0;
 #pragma unroll
-            for (int j = 0; j < VPS; ++j) c += VE - __popc((dsub >> (j * VE)) & ((1u << VE) - 1u));
+            for (int j = 0; j < VPS; ++j)
+#pragma unroll
+              for (int i = 0; i < VE; ++i) c += x[j][i] > -INFINITY ? 1 : 0;
             const int nlv = static_cast<int>(__reduce_add_sync(kFullMask, static_cast<unsigned>(c)));
             if (nlv >= k_eff) {
               const uint32_t kneg = key32(-INFINITY);
@@ -394,84 +473,36 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
               }
               if (klo != kneg) {
                 const unsigned long long t0b = (static_cast<unsigned long long>(klo) << 32) - 1ull;  // key >= klo
-                wtau = t0b > wtau ? t0b : wtau;
+                set_tau(t0b);
                 if (rtau && lane == 0) atomicMax(rtau, t0b);
               }
             }
           }
-          const float tau_x = tau_value();
-          if (__any_sync(kFullMask, tmax >= tau_x)) {  // (a sub-tile without candidates skips this)
-            uint32_t sb = 0;
+          // lanes whose maximum reaches the threshold queue their 16 values
+          unsigned bq = __ballot_sync(kFullMask, tmax >= tau_x);
+          while (bq) {
+            if (pend_n == kDPend) flush(sthist);
+            const int room = kDPend - pend_n;
+            const int rank = __popc(bq & lane_lt);
+            const bool go = ((bq >> lane) & 1u) && rank < room;
+            if (go) {
+              const int c = pend_n + rank;
+              float4* pv = reinterpret_cast<float4*>(pendf + c * 16);
 #pragma unroll
-            for (int j = 0; j < VPS; ++j)
-              if (vmx[j] >= tau_x) {
+              for (int j = 0; j < VPS; ++j)
 #pragma unroll
-                for (int i = 0; i < VE; ++i)
-                  if (!((dsub >> (j * VE + i)) & 1u) && x[j][i] >= tau_x) sb |= 1u << (j * VE + i);
-              }
-            if (__any_sync(kFullMask, sb != 0u)) {
-              const float* sc = reinterpret_cast<const float*>(st);
-              if constexpr (DT == GS_DTYPE_F32) {
-                if (sb) {
-#pragma unroll
-                  for (int j = 0; j < VPS; ++j)
-                    *reinterpret_cast<float4*>(st + (j * 32 + lane) * 16) = make_float4(x[j][0], x[j][1], x[j][2], x[j][3]);
-                }
-              }
-              // the candidate's capped value and pack, from bit b of this sub-tile
-              auto cand_pack = [&](int b) -> unsigned long long {
-                const int j = b / VE, i = b % VE;
-                const int e = ((sub * VPS + j) * 32 + lane) * VE + i;  // element within the tile
-                float xv;
-                if constexpr (DT == GS_DTYPE_F32) {
-                  xv = sc[(j * 32 + lane) * 4 + i];
-                } else {
-                  xv = LD::one(st + e * ESZ);
-                  if (cap != 0.0f) xv = softcap(xv, cap, inv_cap);
-                }
-                return make_pack(xv, id_base + static_cast<uint32_t>(t0 + e));
-              };
-              // all of the sub-tile's candidates at once, when they fit: one ballot when every
-              // lane has at most one, else positions from a warp scan
-              const unsigned multi = __ballot_sync(kFullMask, (sb & (sb - 1u)) != 0u);
-              if (multi == 0u) {
-                const unsigned has = __ballot_sync(kFullMask, sb != 0u);
-                const int n1 = __popc(has);
-                if (wcnt + n1 <= kDWarpCand) {
-                  if (sb) wbuf[wcnt + __popc(has & lane_lt)] = cand_pack(__ffs(sb) - 1);
-                  wcnt += n1;
-                  sb = 0u;
-                }
-              }
-              const int c = __popc(sb);
-              int incl = c;
-#pragma unroll
-              for (int o = 1; o < 32; o <<= 1) {
-                const int u = __shfl_up_sync(kFullMask, incl, o);
-                if (lane >= o) incl += u;
-              }
-              const int total = __shfl_sync(kFullMask, incl, 31);
-              if (total == 0) {
-              } else if (wcnt + total <= kDWarpCand) {
-                int pos = wcnt + incl - c;
-                // (a pack at or just below the threshold is stored too: a real candidate the
-                // merge orders like the others, never one of the k best's places)
-                for (uint32_t m = sb; m; m &= m - 1u) wbuf[pos++] = cand_pack(__ffs(m) - 1);
-                wcnt += total;
-              } else {
-                // not enough room: one candidate per lane per round, compacting as needed
-                while (__any_sync(kFullMask, sb != 0u)) {
-                  const bool has = sb != 0u;
-                  const unsigned long long pk = has ? cand_pack(__ffs(sb) - 1) : 0ull;
-                  if (offer(has, pk) && has) sb &= sb - 1u;
-                }
-              }
+                for (int i = 0; i < VE; i += 4) pv[(j * VE + i) / 4] = make_float4(x[j][i], x[j][i + 1], x[j][i + 2], x[j][i + 3]);
+              ptag[c] = static_cast<uint32_t>(t) << 8 | static_cast<uint32_t>(sub) << 5 | static_cast<uint32_t>(lane);
+              pdead[c] = dsub;
             }
+            const int nb = __popc(bq);
+            pend_n += nb < room ? nb : room;
+            bq &= ~__ballot_sync(kFullMask, go);
           }
         }
         if (do_sum) {
           lmx = fmaxf(lmx, tmax);
-          if (__any_sync(kFullMask, tmax > m_t + dlim)) rescale(warp_max(tmax));
+          if (__any_sync(kFullMask, tmax > m_lim)) rescale(warp_max(tmax));
           if (m_t > -INFINITY) {
             // NaN and +inf reach the sum (as NaN); dead ids are -inf and add 0
             float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
@@ -501,11 +532,19 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
               if (x[j][i] != x[j][i]) bad |= 1u;
         }
       }
-      if (k_eff > 1 && wcnt > wcap) compact();
-    };
+      if (k_eff > 1 && wcnt > wcap) compact(sthist);
+      __syncwarp();  // (the stage is refilled by the next issue)
+      rd += kDTileBytes;
+      if (rd == ring_end) rd = ring0;
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // (empty groups past the last tile)
+    __syncwarp();
+    unsigned* rhist = reinterpret_cast<unsigned*>(ring);  // the ring is idle from here on
+    if (k_eff > 1 && pend_n > 0) flush(rhist);
 
     // Partial tile (the row's last, shorter than a tile): element by element from HBM.
-    auto scalar_tile = [&](int t0, int cnt) {
+    if (gn > nfull * TE) {
+      const int t0 = nfull * TE, cnt = gn - nfull * TE;
       const uint32_t dead_unused = dead_bits(t0, cnt);  // (advances the penalty cursor)
       (void)dead_unused;
       auto live_at = [&](int64_t off) {
@@ -552,38 +591,20 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_kernel(const __grid_consta
             }
           }
         } else if (k_eff > 1) {
-          const float tau_x = tau_value();
           bool pend = live && x >= tau_x;
           const unsigned long long pk = pend ? make_pack(x, id) : 0ull;
-          while (__any_sync(kFullMask, pend)) pend = !offer(pend, pk);
+          while (__any_sync(kFullMask, pend)) pend = !offer(pend, pk, rhist);
         }
       }
       s_t += static_cast<double>(acc);
-    };
-
-    // ---- the unit's tiles: kDStages - 1 in flight while one is worked on ----
-    unsigned long long rt_next = rtau && k_eff > 1 ? *reinterpret_cast<volatile unsigned long long*>(rtau) : 0ull;
-    auto row_bound = [&]() {  // the row's shared bound, read one tile ahead
-      if (rtau && k_eff > 1) {
-        wtau = rt_next > wtau ? rt_next : wtau;
-        rt_next = *reinterpret_cast<volatile unsigned long long*>(rtau);
-      }
-    };
-    for (int t = 0; t < nfull; ++t) {
-      issue(t + kDStages - 1);  // (into the stage read at t - 1: this lane's own slots)
-      asm volatile("cp.async.wait_group %0;" ::"n"(kDStages - 1) : "memory");
-      row_bound();
-      tile(ring + (t % kDStages) * kDTileBytes, t);
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");  // (empty groups past the last tile)
-    if (gn > nfull * TE) scalar_tile(nfull * TE, gn - nfull * TE);
 
     // ---- unit outputs ----
     __syncwarp();
     UnitStat* out = A.stats + unit;
     int ncand = 0;
     if (k_eff > 1) {
-      if (wcnt > k_eff) compact();
+      if (wcnt > k_eff) compact(rhist);
       ncand = wcnt;
       unsigned long long* dst = A.cands + static_cast<int64_t>(unit) * A.kcap;
       for (int i = lane; i < wcnt; i += 32) dst[i] = wbuf[i];
