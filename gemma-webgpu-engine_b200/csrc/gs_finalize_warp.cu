@@ -153,13 +153,35 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
   if (has_mask && na == 0) fl |= GS_FLAG_ERR_DEADEND;
   if (greedy) fl |= GS_FLAG_GREEDY;
 
-  // ---- 1. penalised ids ----
+  // Loads that depend on nothing below are issued here, so that their latencies overlap
+  // instead of adding up: the history ids (up to 32·kWHistPer of them stay in registers
+  // for both history passes) and, for a row of one unit, its candidate packs.
   int hl = 0;
-  if (!(fl & GS_FLAG_ERRORS)) {
+  {
     int64_t h64 = A.history_len ? A.history_len[row] : 0;
     if (h64 > A.history_stride) h64 = A.history_stride;
     if (h64 < 0) h64 = 0;
     hl = static_cast<int>(h64);
+  }
+  const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
+  const bool hreg = hl <= 32 * kWHistPer;
+  uint32_t hv[kWHistPer];
+#pragma unroll
+  for (int q = 0; q < kWHistPer; ++q) {
+    const int i = q * 32 + lane;
+    hv[q] = hreg && i < hl ? static_cast<uint32_t>(hrow[i]) : kNone;
+  }
+  const bool pre_packs = S == 1 && nc <= 32 * kWPackPer;
+  unsigned long long pre[kWPackPer];
+#pragma unroll
+  for (int q = 0; q < kWPackPer; ++q) {
+    const int pidx = q * 32 + lane;
+    pre[q] = pre_packs && pidx < nc ? A.cands[static_cast<int64_t>(row) * A.kcap + pidx] : 0ull;
+  }
+
+  // ---- 1. penalised ids ----
+  if (fl & GS_FLAG_ERRORS) hl = 0;
+  if (!(fl & GS_FLAG_ERRORS)) {
     if (hl > 0) {
       uint32_t* hk = reinterpret_cast<uint32_t*>(R);
       uint32_t* hp = hk + hcap;
@@ -170,10 +192,13 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
         hc[i] = 0u;
       }
       __syncwarp();
-      const int32_t* h = A.history + static_cast<int64_t>(row) * A.history_stride;
-      for (int i = lane; i < hl; i += 32) {
-        const uint32_t v = static_cast<uint32_t>(h[i]);  // negative ids are >= 2^31 here
-        if (v >= static_cast<uint64_t>(A.vocab)) continue;
+      const int32_t* h = hrow;
+      // (registers: the mask words of the ids are requested before the hash is built)
+      uint32_t mwv[kWHistPer];
+#pragma unroll
+      for (int q = 0; q < kWHistPer; ++q)
+        mwv[q] = hreg && has_mask && hv[q] < static_cast<uint64_t>(A.vocab) ? __ldg(mrow + (hv[q] >> 5)) : ~0u;
+      auto insert = [&](uint32_t v, int i) {
         uint32_t slot = w_hash(v, hlg);
         for (;;) {  // at most hl distinct ids in 2·hl+ slots: a free slot exists
           const uint32_t prev = atomicCAS(&hk[slot], kNone, v);
@@ -182,6 +207,16 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
         }
         atomicMin(&hp[slot], static_cast<uint32_t>(i));
         atomicAdd(&hc[slot], 1u);
+      };
+      if (hreg) {
+#pragma unroll
+        for (int q = 0; q < kWHistPer; ++q)
+          if (hv[q] < static_cast<uint64_t>(A.vocab)) insert(hv[q], q * 32 + lane);  // (negative ids are >= 2^31)
+      } else {
+        for (int i = lane; i < hl; i += 32) {
+          const uint32_t v = static_cast<uint32_t>(h[i]);
+          if (v < static_cast<uint64_t>(A.vocab)) insert(v, i);
+        }
       }
       __syncwarp();
       const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
@@ -198,7 +233,7 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
           v[q] = kNone;
           cnt[q] = 0;
           if (i < hl) {
-            v[q] = static_cast<uint32_t>(h[i]);
+            v[q] = hreg ? hv[q] : static_cast<uint32_t>(h[i]);
             if (v[q] < static_cast<uint64_t>(A.vocab)) {
               uint32_t slot = w_hash(v[q], hlg);
               while (hk[slot] != v[q]) slot = (slot + 1) & (hcap - 1);
@@ -209,7 +244,8 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
         }
         bool allow[kWHistPer];
 #pragma unroll
-        for (int q = 0; q < kWHistPer; ++q) allow[q] = first[q] && !(has_mask && !w_mask_allows(mrow, v[q]));
+        for (int q = 0; q < kWHistPer; ++q)
+          allow[q] = first[q] && !(has_mask && !(hreg ? (mwv[q] >> (v[q] & 31)) & 1u : w_mask_allows(mrow, v[q])));
         float x[kWHistPer];
 #pragma unroll
         for (int q = 0; q < kWHistPer; ++q) x[q] = allow[q] ? load_logit(rowbase, DT, v[q]) : 0.0f;
@@ -281,7 +317,7 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
               hi = mid;
             }
           }
-          pk[q] = A.cands[(static_cast<int64_t>(row) * S + lo) * kcap + (pidx - uo_s[lo])];
+          pk[q] = pre_packs ? pre[q] : A.cands[(static_cast<int64_t>(row) * S + lo) * kcap + (pidx - uo_s[lo])];
         }
       }
 #pragma unroll
