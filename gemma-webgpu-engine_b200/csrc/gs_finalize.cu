@@ -477,8 +477,11 @@ __global__ void __launch_bounds__(kFinalizeMaxThreads) finalize_kernel(const __g
 
 cudaError_t launch_finalize(const FinalizeArgs& a, int dtype, int rows, size_t smem, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
-  // Few rows (fewer CTAs than SMs): more threads per row shorten each row's chain.
-  const int threads = rows < sm_count() ? kFinalizeMaxThreads : kFinalizeThreads;
+  // Fewer rows than two per SM: more threads per row shorten each row's chain.  Measured
+  // at C3's settings (one B200, merge time): 64 rows 39.2 us with 1024 threads, 35.3 with
+  // 512; 128 rows 41.1 / 38.3; 256 rows 44.8 with 256 threads, 39.1 with 512, 74.8 with
+  // 1024 (one CTA per SM).  A handful of rows keep 1024.
+  const int threads = rows < 32 ? kFinalizeMaxThreads : (rows < 2 * sm_count() ? 512 : kFinalizeThreads);
   if (dtype == GS_DTYPE_F32) {
     const cudaError_t e = cudaFuncSetAttribute(finalize_kernel<GS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(smem));

@@ -1,7 +1,7 @@
 """Parity at the benchmark configurations' full sizes, on the code paths the bench times.
 
 The bench samples C4 at 4096 rows per GPU, where the merge runs one warp per row
-(finalize_warp_kernel, taken when a batch has at least two rows per SM); C2's 64 rows
+(finalize_warp_kernel, taken when a batch has at least five rows per SM); C2's 64 rows
 run the histogram path (topK 0) and C3's 256 rows the block merge.  These tests run the
 configurations at BASELINE.json's batch sizes through the C ABI and compare every row
 with the CPU oracle on the same bytes: candidate ids and order bit-exact, probabilities

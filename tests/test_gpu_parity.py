@@ -314,13 +314,13 @@ def test_stream_tile_modes(pkg, oracle, sampler, dtype, k, temp, logprob):
 
 
 def test_warp_merge_many_rows(pkg, oracle, sampler):
-    """Enough rows for the warp-per-row merge (>= 2 per SM), per-row params mixing
+    """Enough rows for the warp-per-row merge (>= 5 per SM on a 148-SM B200), per-row params mixing
     greedy, topK 1..128, min-p, typical-p and top-p, with histories (repeats, masked and
     out-of-range ids) and masks of graded density, including states allowing fewer ids
     than topK (the masked-id filler)."""
     import torch
     rng = np.random.default_rng(77)
-    V, rows, H = 32768, 320, 96
+    V, rows, H = 32768, 800, 96
     x = (rng.standard_normal((rows, V)) * 2.5).astype(np.float32)
     x[5, 100:140] = 11.0  # exact ties
     dens = [0.0004, 0.003, 0.05, 0.5]
