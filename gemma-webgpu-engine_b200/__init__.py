@@ -22,6 +22,7 @@ from .sampling import (  # noqa: F401
     SamplerError,
     SeededRandom,
     build_mask_row,
+    compact_history,
     default_sampler,
     mask_constraint_logits,
     params_from_config,

@@ -126,6 +126,7 @@ class GsBatch(ctypes.Structure):
         ("mask_state", ctypes.c_void_p),
         ("rng_state", ctypes.c_void_p),
         ("uniforms", ctypes.c_void_p),
+        ("history_count", ctypes.c_void_p),
     ]
 
 

@@ -317,6 +317,8 @@ gs_status gs_sample_host(gs_ctx* c, const gs_batch* hb, const gs_outputs* ho, vo
   const size_t o_logits = take(static_cast<size_t>(rows) * hb->row_stride * esz);
   const size_t o_hist = hb->history ? take(static_cast<size_t>(rows) * hb->history_stride * 4) : 0;
   const size_t o_hlen = hb->history ? take(static_cast<size_t>(rows) * 4) : 0;
+  const bool hcounts = hb->history && hb->history_count;
+  const size_t o_hcnt = hcounts ? take(static_cast<size_t>(rows) * hb->history_stride * 4) : 0;
   const size_t o_mstate = hb->mask_table ? take(static_cast<size_t>(rows) * 4) : 0;
   const size_t o_rng = hb->rng_state ? take(static_cast<size_t>(rows) * 8) : 0;
   const size_t o_uni = hb->uniforms ? take(static_cast<size_t>(rows) * 8) : 0;
@@ -335,6 +337,7 @@ gs_status gs_sample_host(gs_ctx* c, const gs_batch* hb, const gs_outputs* ho, vo
   cudaError_t e = h2d(o_logits, hb->logits, static_cast<size_t>(rows) * hb->row_stride * esz);
   if (hb->history && e == cudaSuccess) e = h2d(o_hist, hb->history, static_cast<size_t>(rows) * hb->history_stride * 4);
   if (hb->history && e == cudaSuccess) e = h2d(o_hlen, hb->history_len, static_cast<size_t>(rows) * 4);
+  if (hcounts && e == cudaSuccess) e = h2d(o_hcnt, hb->history_count, static_cast<size_t>(rows) * hb->history_stride * 4);
   if (hb->mask_table && e == cudaSuccess) e = h2d(o_mstate, hb->mask_state, static_cast<size_t>(rows) * 4);
   if (hb->rng_state && e == cudaSuccess) e = h2d(o_rng, hb->rng_state, static_cast<size_t>(rows) * 8);
   if (hb->uniforms && e == cudaSuccess) e = h2d(o_uni, hb->uniforms, static_cast<size_t>(rows) * 8);
@@ -343,6 +346,7 @@ gs_status gs_sample_host(gs_ctx* c, const gs_batch* hb, const gs_outputs* ho, vo
   db.logits = io + o_logits;
   db.history = hb->history ? reinterpret_cast<const int32_t*>(io + o_hist) : nullptr;
   db.history_len = hb->history ? reinterpret_cast<const int32_t*>(io + o_hlen) : nullptr;
+  db.history_count = hcounts ? reinterpret_cast<const int32_t*>(io + o_hcnt) : nullptr;
   db.mask_state = hb->mask_table ? reinterpret_cast<const int32_t*>(io + o_mstate) : nullptr;
   db.rng_state = hb->rng_state ? reinterpret_cast<double*>(io + o_rng) : nullptr;
   db.uniforms = hb->uniforms ? reinterpret_cast<const double*>(io + o_uni) : nullptr;

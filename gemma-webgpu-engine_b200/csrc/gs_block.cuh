@@ -61,6 +61,27 @@ __device__ inline void bitonic_sort_kv(unsigned long long* key, uint32_t* val, i
   }
 }
 
+// Ascending block-wide sort of n2 (a power of two) 64-bit values, in shared or global
+// memory (the block's own rows: __syncthreads orders both).
+__device__ inline void bitonic_sort_u64(unsigned long long* v, int n2) {
+  for (int k = 2; k <= n2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long a = v[i], b = v[ixj];
+          const bool up = (i & k) == 0;
+          if (up ? a > b : a < b) {
+            v[i] = b;
+            v[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // Ascending sort of plain 32-bit values.
 __device__ inline void bitonic_sort_u32(uint32_t* v, int n2) {
   for (int k = 2; k <= n2; k <<= 1) {

@@ -196,27 +196,40 @@ __global__ void __launch_bounds__(kFinalizeMaxThreads) finalize_kernel(const __g
     if (hl < 0) hl = 0;
     if (hl > 0) {
       uint32_t* hs = reinterpret_cast<uint32_t*>(r1);
+      // with counts: 64-bit words id << 32 | occurrences, sorted the same way
+      unsigned long long* hw = reinterpret_cast<unsigned long long*>(r1);
+      const int32_t* hcn = A.history_count ? A.history_count + static_cast<int64_t>(row) * A.history_stride : nullptr;
       const int h2 = pow2_ceil(static_cast<int>(hl));
       const int32_t* h = A.history + static_cast<int64_t>(row) * A.history_stride;
-      for (int i = tid; i < h2; i += bs) hs[i] = i < hl ? static_cast<uint32_t>(h[i]) : 0xffffffffu;
-      __syncthreads();
-      bitonic_sort_u32(hs, h2);
+      if (hcn) {
+        for (int i = tid; i < h2; i += bs)
+          hw[i] = i < hl ? (static_cast<unsigned long long>(static_cast<uint32_t>(h[i])) << 32) |
+                               static_cast<uint32_t>(max(hcn[i], 1))
+                         : ~0ull;
+        __syncthreads();
+        bitonic_sort_u64(hw, h2);
+      } else {
+        for (int i = tid; i < h2; i += bs) hs[i] = i < hl ? static_cast<uint32_t>(h[i]) : 0xffffffffu;
+        __syncthreads();
+        bitonic_sort_u32(hs, h2);
+      }
+      auto id_at = [&](int i) -> uint32_t { return hcn ? static_cast<uint32_t>(hw[i] >> 32) : hs[i]; };
       const double rp = pp->repetition_penalty, pres = pp->presence_penalty, freq = pp->frequency_penalty;
       // entry i belongs to sorted history position i (a fixed slot, so the normaliser's
       // summation order does not depend on thread timing); unused slots have kind ~0
       for (int i = tid; i < hl; i += bs) {
-        const uint32_t v = hs[i];  // global id (negative ids are >= 2^31 here)
+        const uint32_t v = id_at(i);  // global id (negative ids are >= 2^31 here)
         const int64_t lv = static_cast<int64_t>(v) - A.vocab_offset;  // local to this call's logits
         Ent e{-INFINITY, 0xffffffffu, 0xffffffffu};
         float x = 0.0f;
-        const bool first = lv >= 0 && lv < A.vocab && !(i > 0 && hs[i - 1] == v);
+        const bool first = lv >= 0 && lv < A.vocab && !(i > 0 && id_at(i - 1) == v);
         if (first && !(has_mask && !mask_allows(mrow, static_cast<uint32_t>(lv)))) {  // masked: -inf either way
-          int cnt = 1;
-          while (i + cnt < hl && hs[i + cnt] == v) ++cnt;
+          double cnt = 0.0;
+          for (int j = i; j < hl && id_at(j) == v; ++j) cnt += hcn ? static_cast<double>(hw[j] & 0xffffffffu) : 1.0;
           x = load_logit(rowbase, DT, lv);
           if (A.softcap != 0.0f) x = softcap(x, A.softcap, A.inv_softcap);
           if (!(x < INFINITY)) atomicOr(&F.flags, GS_FLAG_ERR_NONFINITE);  // NaN or +inf
-          const double xp = penalise(static_cast<double>(x), static_cast<double>(cnt), rp, pres, freq);
+          const double xp = penalise(static_cast<double>(x), cnt, rp, pres, freq);
           e = Ent{greedy ? xp : __ddiv_rn(xp, T), v, 1u};
         }
         ent_all[i] = e;

@@ -165,11 +165,13 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
   }
   const int32_t* hrow = A.history + static_cast<int64_t>(row) * A.history_stride;
   const bool hreg = hl <= 32 * kWHistPer;
-  uint32_t hv[kWHistPer];
+  const int32_t* hcrow = A.history_count ? A.history_count + static_cast<int64_t>(row) * A.history_stride : nullptr;
+  uint32_t hv[kWHistPer], hcv[kWHistPer];  // ids and the occurrences each stands for
 #pragma unroll
   for (int q = 0; q < kWHistPer; ++q) {
     const int i = q * 32 + lane;
     hv[q] = hreg && i < hl ? static_cast<uint32_t>(hrow[i]) : kNone;
+    hcv[q] = hcrow && hreg && i < hl ? static_cast<uint32_t>(max(hcrow[i], 1)) : 1u;
   }
   const bool pre_packs = S == 1 && nc <= 32 * kWPackPer;
   unsigned long long pre[kWPackPer];
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
 #pragma unroll
       for (int q = 0; q < kWHistPer; ++q)
         mwv[q] = hreg && has_mask && hv[q] < static_cast<uint64_t>(A.vocab) ? __ldg(mrow + (hv[q] >> 5)) : ~0u;
-      auto insert = [&](uint32_t v, int i) {
+      auto insert = [&](uint32_t v, int i, uint32_t c) {
         uint32_t slot = w_hash(v, hlg);
         for (;;) {  // at most hl distinct ids in 2·hl+ slots: a free slot exists
           const uint32_t prev = atomicCAS(&hk[slot], kNone, v);
@@ -206,16 +208,16 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
           slot = (slot + 1) & (hcap - 1);
         }
         atomicMin(&hp[slot], static_cast<uint32_t>(i));
-        atomicAdd(&hc[slot], 1u);
+        atomicAdd(&hc[slot], c);
       };
       if (hreg) {
 #pragma unroll
         for (int q = 0; q < kWHistPer; ++q)
-          if (hv[q] < static_cast<uint64_t>(A.vocab)) insert(hv[q], q * 32 + lane);  // (negative ids are >= 2^31)
+          if (hv[q] < static_cast<uint64_t>(A.vocab)) insert(hv[q], q * 32 + lane, hcv[q]);  // (negative ids are >= 2^31)
       } else {
         for (int i = lane; i < hl; i += 32) {
           const uint32_t v = static_cast<uint32_t>(h[i]);
-          if (v < static_cast<uint64_t>(A.vocab)) insert(v, i);
+          if (v < static_cast<uint64_t>(A.vocab)) insert(v, i, hcrow ? static_cast<uint32_t>(max(hcrow[i], 1)) : 1u);
         }
       }
       __syncwarp();

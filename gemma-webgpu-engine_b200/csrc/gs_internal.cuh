@@ -73,6 +73,7 @@ struct StreamArgs {
 
 struct FinalizeArgs {
   const void* logits;
+  const int32_t* history_count;  // [rows, history_stride] occurrences per entry, or nullptr (one each)
   int64_t vocab;          // ids are [0, vocab) of this call
   int64_t row_stride;
   float softcap;

@@ -296,26 +296,6 @@ __device__ void seg_sort(Ent* e, int n, int t, int nt) {
   }
 }
 
-// Ascending block-wide sort of n2 (a power of two) 64-bit keys, in shared or global
-// memory (the block's own rows: __syncthreads orders both).
-__device__ void bitonic_sort_u64(unsigned long long* v, int n2) {
-  for (int k = 2; k <= n2; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const unsigned long long a = v[i], b = v[ixj];
-          if ((i & k) == 0 ? a > b : a < b) {
-            v[i] = b;
-            v[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-}
-
 }  // namespace
 
 // resolve: entries | exact probabilities | bin starts | typical-p sort keys
@@ -814,11 +794,12 @@ __global__ void __launch_bounds__(kSelectThreads) large_select_kernel(const __gr
       s = (s + 1) & static_cast<uint32_t>(h2 - 1);
     }
   };
+  const int32_t* hcrow = A.history_count ? A.history_count + static_cast<int64_t>(row) * A.history_stride : nullptr;
   for (int64_t j = tid; j < hl; j += bs) {
     const int32_t v = hrow[j];
     if (v < 0 || v >= V) continue;
     const int s = find_slot(static_cast<uint32_t>(v), true);
-    atomicAdd(&hcnt[s], 1);
+    atomicAdd(&hcnt[s], hcrow ? max(hcrow[j], 1) : 1);
     atomicMin(&hfirst[s], static_cast<int>(j));
   }
   __syncthreads();

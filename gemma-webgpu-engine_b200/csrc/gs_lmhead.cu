@@ -1499,7 +1499,9 @@ gs_status gs_lm_head_sample(gs_lm_head* h, const float* activation, int64_t ld_a
                // a penalty history at one row only: the records are then combined into one, and the
                // merge plans its penalised slots as gs_sample does for one row (147 shards' slots
                // would not fit its shared memory)
-               (!batch->history || (rows == 1 && batch->history_stride >= 1 && batch->history_stride <= kRecMaxHistory));
+               (!batch->history || (rows == 1 && batch->history_stride >= 1 && batch->history_stride <= kRecMaxHistory)) &&
+               // (history counts: the two-step route, whose kernels read them)
+               !(batch->history && batch->history_count);
   int kcap = 1;
   RecArgs ra{};
   if (fused) {

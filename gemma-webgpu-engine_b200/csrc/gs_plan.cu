@@ -145,7 +145,9 @@ gs_status plan_layout(const gs_batch* b, const PlanSummary& ps, Layout* L, std::
   L->pack_cap = S > 1 ? S * kcap : 0;
   L->ent_cap = pow2ceil(std::max<int64_t>(std::min<int64_t>(static_cast<int64_t>(S) * kcap, kmax) + hs, 1));
   L->work_cap = std::min(pow2ceil(std::max(kmax, 1)), 1024);
-  L->fin_smem = finalize_smem_bytes(L->hist_cap, L->ent_cap, L->pack_cap, L->work_cap);
+  // (with history counts the block merge sorts 64-bit (id, count) words: twice the bytes)
+  L->fin_smem = finalize_smem_bytes(L->hist_cap * (b->history && b->history_count ? 2 : 1), L->ent_cap, L->pack_cap,
+                                    L->work_cap);
   if (L->fin_smem > 220 * 1024)
     return fmt(err, GS_EUNSUPPORTED, "merge needs %zu bytes of shared memory (topK %d, history %lld)", L->fin_smem, kmax,
                static_cast<long long>(hs));
@@ -271,6 +273,8 @@ gs_status launch_sampling(const gs_batch* b, const gs_outputs* o, const Layout& 
   fa.plan0 = plan0;
   fa.history = sa.history;
   fa.history_len = sa.history_len;
+  // (the merge of gathered shard records reads no history: its records hold the scores)
+  fa.history_count = smode == 2 || !b->history ? nullptr : b->history_count;
   fa.history_stride = sa.history_stride;
   fa.mask_table = sa.mask_table;
   fa.mask_states = b->mask_states;

@@ -80,6 +80,7 @@ struct StepArgs {
   unsigned* done;                    // [rows] CTAs of the row finished
   const int32_t* history;            // [rows][history_stride] penalty history ids, or nullptr
   const int32_t* history_len;
+  const int32_t* history_count;      // [rows][history_stride] occurrences per entry, or nullptr (one each)
   int64_t history_stride;            // <= kStepMaxHist
   const uint32_t* mask_table;        // [mask_states][mask_words] allowed-id bitmask rows, or nullptr
   int32_t mask_states;
@@ -308,9 +309,13 @@ __global__ void __launch_bounds__(kStepThreads, MINB) step_kernel(const __grid_c
   // (the history's length and this thread's history position load with the logits)
   int hl = 0;
   int32_t hid = -1;
+  uint32_t hcn = 1u;  // occurrences the entry stands for
   if (A.history) {
     hl = A.history_len[row];
-    if (tid < A.history_stride) hid = A.history[static_cast<int64_t>(row) * A.history_stride + tid];
+    if (tid < A.history_stride) {
+      hid = A.history[static_cast<int64_t>(row) * A.history_stride + tid];
+      if (A.history_count) hcn = static_cast<uint32_t>(max(A.history_count[static_cast<int64_t>(row) * A.history_stride + tid], 1));
+    }
   }
   // the constraint row (sampling over maskConstraintLogits: disallowed ids are -inf)
   const int64_t id0 = static_cast<int64_t>(unit) * kStepIds + tid * 4;
@@ -681,7 +686,7 @@ __global__ void __launch_bounds__(kStepThreads, MINB) step_kernel(const __grid_c
     uint32_t sl = 0;
     if (hv != 0xffffffffu) {
       sl = slot_of(hv, true);
-      atomicAdd(&hcnt[sl], 1u);
+      atomicAdd(&hcnt[sl], hcn);
       atomicMin(&hfirst[sl], static_cast<uint32_t>(tid));
     }
     __syncthreads();
@@ -1024,6 +1029,7 @@ cudaError_t launch_step(const gs_batch* b, const gs_outputs* o, const RowPlan& p
   a.done = done;
   a.history = b->history;
   a.history_len = b->history ? b->history_len : nullptr;
+  a.history_count = b->history ? b->history_count : nullptr;
   a.history_stride = b->history ? b->history_stride : 0;
   a.mask_table = b->mask_table;
   a.mask_states = b->mask_states;

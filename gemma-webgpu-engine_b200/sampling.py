@@ -125,6 +125,18 @@ def prepare_params(params):
 _params_array = prepare_params
 
 
+def compact_history(history: Sequence[int]) -> tuple[list, list]:
+    """A window as its distinct ids in order of first occurrence and the number of times
+    each occurs: the form ``history`` + ``history_count`` take.  The penalties depend only
+    on each id's count in the window (src/runtime/sampling.ts:21-30), so a window longer
+    than MAX_HISTORY entries samples the same way in this form."""
+    counts: dict = {}
+    for t in history:
+        t = int(t)
+        counts[t] = counts.get(t, 0) + 1
+    return list(counts.keys()), list(counts.values())
+
+
 def windowed_history(history: Sequence[int], window: int) -> list:
     """history.slice(-config.repetitionWindow), or [] for a zero window (sampling.ts:22-24)."""
     if window == 0:
@@ -184,7 +196,7 @@ class GpuSampler:
         return raw.decode() if raw else ""
 
     def make_batch(self, logits, params, *, softcap: float = 0.0, history=None, history_len=None,
-                   mask_table=None, mask_state=None, rng_state=None, uniforms=None):
+                   mask_table=None, mask_state=None, rng_state=None, uniforms=None, history_count=None):
         import torch
         if logits.dim() != 2:
             raise ValueError("logits must be [rows, vocab]")
@@ -211,6 +223,13 @@ class GpuSampler:
             b.history = history.data_ptr()
             b.history_len = history_len.data_ptr()
             b.history_stride = history.stride(0) if history.shape[0] > 1 else history.shape[1]
+            if history_count is not None:
+                if history_count.dtype != torch.int32 or tuple(history_count.shape) != tuple(history.shape) or \
+                        history_count.stride() != history.stride():
+                    raise ValueError("history_count must be int32 with the history's shape and strides")
+                b.history_count = history_count.data_ptr()
+        elif history_count is not None:
+            raise ValueError("history_count needs a history")
         if mask_table is not None:
             b.mask_table = mask_table.data_ptr()
             b.mask_states = mask_table.shape[0]
@@ -247,13 +266,15 @@ class GpuSampler:
 
     def sample(self, logits, params, *, softcap: float = 0.0, history=None, history_len=None, mask_table=None,
                mask_state=None, rng_state=None, uniforms=None, logprob: bool = False, candidates: int = 0,
-               stream=None, out: SampleResult | None = None) -> SampleResult:
+               stream=None, out: SampleResult | None = None, history_count=None) -> SampleResult:
         """Batched sampling of device-resident logits [rows, vocab] (gs_sample).  Asynchronous on
-        ``stream`` (torch's current stream when None); outputs are device tensors."""
+        ``stream`` (torch's current stream when None); outputs are device tensors.
+        ``history_count`` (int32, the history's shape): the occurrences each history entry
+        stands for (a window given as ``compact_history``'s distinct ids and counts)."""
         import torch
         b, keep = self.make_batch(logits, params, softcap=softcap, history=history, history_len=history_len,
                                   mask_table=mask_table, mask_state=mask_state, rng_state=rng_state,
-                                  uniforms=uniforms)
+                                  uniforms=uniforms, history_count=history_count)
         dev = logits.device
         out, o = self.make_outputs(logits.shape[0], dev, logprob, candidates, out)
         if stream is None:
@@ -266,7 +287,7 @@ class GpuSampler:
 
     def bind(self, logits, params, *, softcap: float = 0.0, history=None, history_len=None, mask_table=None,
              mask_state=None, rng_state=None, uniforms=None, logprob: bool = False, candidates: int = 0,
-             stream=None) -> "BoundSample":
+             stream=None, history_count=None) -> "BoundSample":
         """A reusable ``sample`` call for a decode loop: every argument but the logits is
         fixed (the params, the history, mask and state tensors are read afresh on the
         device at each call, so their contents may change; their storage may not).  Each
@@ -274,7 +295,7 @@ class GpuSampler:
         output tensors, rewritten."""
         return BoundSample(self, logits, params, softcap=softcap, history=history, history_len=history_len,
                            mask_table=mask_table, mask_state=mask_state, rng_state=rng_state, uniforms=uniforms,
-                           logprob=logprob, candidates=candidates, stream=stream)
+                           logprob=logprob, candidates=candidates, stream=stream, history_count=history_count)
 
     # ---------------------------------------------------------------- vocabulary shards
     def shard_record_bytes(self, params, vocab_total: int, history_stride: int = 0) -> int:
@@ -372,7 +393,8 @@ class GpuSampler:
     def sample_host(self, logits: np.ndarray, params, *, softcap: float = 0.0, history: np.ndarray | None = None,
                     history_len: np.ndarray | None = None, mask_table=None, mask_state: np.ndarray | None = None,
                     rng_state: np.ndarray | None = None, uniforms: np.ndarray | None = None, logprob: bool = False,
-                    candidates: int = 0, stream: int = 0, dtype: int = _lib.GS_DTYPE_F32):
+                    candidates: int = 0, stream: int = 0, dtype: int = _lib.GS_DTYPE_F32,
+                    history_count: np.ndarray | None = None):
         """gs_sample_host: every buffer in host memory (numpy) except ``mask_table`` (a device tensor:
         compiled constraint tables stay resident).  Synchronous; raises the reference's error for
         the first failing row.  ``rng_state`` (float64) is advanced in place."""
@@ -393,6 +415,11 @@ class GpuSampler:
             b.history = history.ctypes.data
             b.history_len = history_len.ctypes.data
             b.history_stride = history.strides[0] // 4
+            if history_count is not None:
+                if history_count.dtype != np.int32 or history_count.shape != history.shape or \
+                        history_count.strides != history.strides:
+                    raise ValueError("history_count must be int32 with the history's shape and strides")
+                b.history_count = history_count.ctypes.data
         if mask_table is not None:
             b.mask_table = mask_table.data_ptr()
             b.mask_states = mask_table.shape[0]
@@ -451,6 +478,12 @@ def sample_token(raw_logits, history: Sequence[int], config: dict, random: Seede
     if n == 0:
         raise ValueError("Cannot sample empty logits")
     recent = windowed_history(history, int(config["repetitionWindow"]))
+    counts = None
+    if len(recent) > _lib.MAX_HISTORY:  # a long window: its distinct ids with their counts
+        recent, counts = compact_history(recent)
+        if len(recent) > _lib.MAX_HISTORY:
+            raise SamplerError(_lib.GS_EUNSUPPORTED,
+                               f"repetition window holds more than {_lib.MAX_HISTORY} distinct ids")
     params = params_from_config(config)
     use_state = isinstance(random, SeededRandom)
     uniform = None
@@ -462,10 +495,12 @@ def sample_token(raw_logits, history: Sequence[int], config: dict, random: Seede
         logits = raw_logits.reshape(1, -1)
         hist = torch.tensor([recent if recent else [0]], dtype=torch.int32, device=dev)
         hlen = torch.tensor([len(recent)], dtype=torch.int32, device=dev)
+        hcnt = None if counts is None else torch.tensor([counts], dtype=torch.int32, device=dev)
         rng = torch.tensor([random.state if use_state else 0.0], dtype=torch.float64, device=dev)
         uni = torch.tensor([uniform if uniform is not None else 0.0], dtype=torch.float64, device=dev)
         res = s.sample(logits, params, softcap=softcap, history=hist, history_len=hlen,
-                       rng_state=rng if use_state else None, uniforms=None if use_state else uni)
+                       rng_state=rng if use_state else None, uniforms=None if use_state else uni,
+                       history_count=hcnt)
         flags = int(res.flags.cpu().item())
         tok = int(res.ids.cpu().item())
         _raise_row_flags(flags)
@@ -476,10 +511,12 @@ def sample_token(raw_logits, history: Sequence[int], config: dict, random: Seede
     x = np.ascontiguousarray(np.asarray(raw_logits, dtype=np.float32).reshape(1, -1))
     hist = np.asarray([recent if recent else [0]], dtype=np.int32)
     hlen = np.asarray([len(recent)], dtype=np.int32)
+    hcnt = None if counts is None else np.asarray([counts], dtype=np.int32)
     rng = np.asarray([random.state if use_state else 0.0], dtype=np.float64)
     uni = np.asarray([uniform if uniform is not None else 0.0], dtype=np.float64)
     res = s.sample_host(x, params, softcap=softcap, history=hist, history_len=hlen,
-                        rng_state=rng if use_state else None, uniforms=None if use_state else uni)
+                        rng_state=rng if use_state else None, uniforms=None if use_state else uni,
+                        history_count=hcnt)
     if use_state:
         random.state = float(rng[0])
     return int(res.ids[0])
@@ -490,13 +527,14 @@ class BoundSample:
     logits pointer and runs gs_sample (about 2 us of host time instead of ~12)."""
 
     def __init__(self, sampler, logits, params, *, softcap, history, history_len, mask_table, mask_state, rng_state,
-                 uniforms, logprob, candidates, stream):
+                 uniforms, logprob, candidates, stream, history_count=None):
         import torch
         self._sampler = sampler
         self._b, self._keep = sampler.make_batch(logits, params, softcap=softcap, history=history,
                                                  history_len=history_len, mask_table=mask_table,
-                                                 mask_state=mask_state, rng_state=rng_state, uniforms=uniforms)
-        self._args = (history, history_len, mask_table, mask_state, rng_state, uniforms)  # (kept alive)
+                                                 mask_state=mask_state, rng_state=rng_state, uniforms=uniforms,
+                                                 history_count=history_count)
+        self._args = (history, history_len, mask_table, mask_state, rng_state, uniforms, history_count)  # (kept alive)
         self.out, self._o = sampler.make_outputs(logits.shape[0], logits.device, logprob, candidates)
         if stream is None:
             stream = torch.cuda.current_stream(logits.device).cuda_stream

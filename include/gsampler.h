@@ -56,7 +56,10 @@ enum {
 };
 
 #define GS_MAX_TOP_K 1024     /* topK above this (or 0) runs the histogram path */
-#define GS_MAX_HISTORY 4096   /* ids per row after the repetition window is applied */
+#define GS_MAX_HISTORY 4096   /* history entries per row after the repetition window is
+                                 applied; with gs_batch.history_count an entry stands for
+                                 any number of occurrences, so the window itself is not
+                                 bounded by this */
 
 /*
  * DecodingConfig fields that sampleToken reads (src/runtime/decoding.ts:1-14).  The
@@ -94,6 +97,12 @@ typedef struct gs_batch {
   const int32_t* mask_state;  /* [rows] row -> state; < 0 = unconstrained; or NULL */
   double* rng_state;          /* [rows] SeededRandom states (the JS number), in/out */
   const double* uniforms;     /* [rows] pre-drawn random() values; overrides rng_state */
+  /* [rows, history_stride] occurrences each history entry stands for, or NULL (each entry
+   * is one occurrence).  The penalties depend only on each id's count in the window
+   * (src/runtime/sampling.ts:21-30), so a window longer than GS_MAX_HISTORY can be passed
+   * as its distinct ids (in order of first occurrence) with their counts.  Values below 1
+   * count as 1.  No reference counterpart: the reference counts a JS array each call. */
+  const int32_t* history_count;
 } gs_batch;
 
 typedef struct gs_outputs {

@@ -28,7 +28,8 @@ class GpuOut:
 
 
 def run_gpu(sampler, logits_np, params, *, softcap=0.0, history=None, history_len=None, mask_table=None,
-            mask_state=None, rng_state=None, uniforms=None, cand_cap=2048, dtype=None, logprob=True):
+            mask_state=None, rng_state=None, uniforms=None, cand_cap=2048, dtype=None, logprob=True,
+            history_count=None):
     import torch
     dev = torch.device("cuda", 0)
     x = torch.from_numpy(np.ascontiguousarray(logits_np)).to(dev)
@@ -40,7 +41,7 @@ def run_gpu(sampler, logits_np, params, *, softcap=0.0, history=None, history_le
                          history_len=t(history_len, torch.int32),
                          mask_table=t(None if mask_table is None else mask_table.view(np.int32), torch.int32),
                          mask_state=t(mask_state, torch.int32), rng_state=rng, uniforms=t(uniforms, torch.float64),
-                         logprob=logprob, candidates=cand_cap)
+                         logprob=logprob, candidates=cand_cap, history_count=t(history_count, torch.int32))
     torch.cuda.synchronize()
     return GpuOut(
         ids=res.ids.cpu().numpy(), flags=res.flags.cpu().numpy().view(np.uint32),

@@ -78,3 +78,18 @@ def test_prepare_params_matches_per_config_conversion():
     b = (S.GsParams * len(ps))(*[S.params_from_config(p) for p in ps])
     assert bytes(a) == bytes(b)
     assert S.prepare_params(a) is a
+
+
+def test_compact_history_keeps_first_occurrence_order_and_counts(pkg):
+    """A window as distinct ids in order of first occurrence with their counts (the form
+    gs_batch.history_count takes); out-of-range and negative ids are kept as entries, as
+    the reference's Map keeps them (src/runtime/sampling.ts:21-27)."""
+    import collections
+    rng = __import__("numpy").random.default_rng(3)
+    window = [int(v) for v in rng.integers(-3, 50, 5000)]
+    ids, counts = pkg.compact_history(window)
+    assert len(ids) == len(set(window))
+    assert ids == list(dict.fromkeys(window))
+    c = collections.Counter(window)
+    assert counts == [c[i] for i in ids]
+    assert pkg.compact_history([]) == ([], [])
