@@ -61,6 +61,38 @@ __device__ inline void bitonic_sort_kv(unsigned long long* key, uint32_t* val, i
   }
 }
 
+// Descending bitonic sort of n2 (a power of two, <= 128) packs held in registers, element
+// q·32 + lane in v[q] (padding 0 sorts last): exchanges across lanes by shuffles, across a
+// lane's registers by compile-time swaps.
+static __device__ __forceinline__ void warp_sort_desc_regs(unsigned long long (&v)[4], int n2, int lane) {
+  auto cx = [&](unsigned long long& a, unsigned long long& b, bool desc) {  // a: the lower index
+    const bool sw = desc ? a < b : a > b;
+    const unsigned long long t = a;
+    a = sw ? b : a;
+    b = sw ? t : b;
+  };
+  for (int k = 2; k <= n2; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 64) {
+        cx(v[0], v[2], (lane & k) == 0);
+        cx(v[1], v[3], ((32 + lane) & k) == 0);
+      } else if (j == 32) {
+        cx(v[0], v[1], (lane & k) == 0);
+        if (n2 > 64) cx(v[2], v[3], ((64 + lane) & k) == 0);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (q * 32 < n2) {
+            const unsigned long long p = __shfl_xor_sync(kFullMask, v[q], j);
+            const int i = q * 32 + lane;
+            const bool desc = (i & k) == 0, lo = (i & j) == 0;
+            v[q] = desc == lo ? (v[q] > p ? v[q] : p) : (v[q] < p ? v[q] : p);
+          }
+        }
+      }
+    }
+}
+
 // Ascending block-wide sort of n2 (a power of two) 64-bit values, in shared or global
 // memory (the block's own rows: __syncthreads orders both).
 __device__ inline void bitonic_sort_u64(unsigned long long* v, int n2) {

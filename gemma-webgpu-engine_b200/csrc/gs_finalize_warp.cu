@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
     hcv[q] = hcrow && hreg && i < hl ? static_cast<uint32_t>(max(hcrow[i], 1)) : 1u;
   }
   const bool pre_packs = S == 1 && nc <= 32 * kWPackPer;
+  const bool packs_sorted = pre_packs && nc <= 128;  // (sorted in registers in phase 2)
   unsigned long long pre[kWPackPer];
 #pragma unroll
   for (int q = 0; q < kWPackPer; ++q) {
@@ -301,6 +302,16 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
       if (lane == 0) uo_s[S] = run;  // == nc
       __syncwarp();
     }
+    if (packs_sorted) {
+      // a one-unit row's packs (at most 128, in registers): sorted here, largest first, so
+      // that the entries below are in the reference's order unless a penalised one joins
+      unsigned long long v[4] = {pre[0], pre[1], pre[2], pre[3]};
+      int n2 = 2;
+      while (n2 < nc) n2 <<= 1;
+      warp_sort_desc_regs(v, n2, lane);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) pre[q] = v[q];
+    }
     for (int p0 = 0; p0 < nc; p0 += 32 * kWPackPer) {  // warp-uniform
       unsigned long long pk[kWPackPer];
 #pragma unroll
@@ -387,21 +398,28 @@ __global__ void __launch_bounds__(kWWarps * 32) finalize_warp_kernel(const __gri
       const double x = static_cast<double>(pack_value(kth));
       thr = greedy ? x : __ddiv_rn(x, T);
     }
+    int pen_kept = 0;  // penalised entries among them
     for (int i0 = 0; i0 < n_all; i0 += 32) {  // in place, order-preserving
       const int i = i0 + lane;
       Ent e{-INFINITY, kNone, kNone};
       if (i < n_all) e = ent[i];
       const bool keep = i < n_all && e.kind != kNone && e.key >= thr;
       const unsigned b = __ballot_sync(kFullMask, keep);
+      pen_kept += __popc(__ballot_sync(kFullMask, keep && e.kind == 1u));
       __syncwarp();
       if (keep) ent[ns + __popc(b & lane_lt)] = e;
       ns += __popc(b);
       __syncwarp();
     }
-    const int n2 = pow2_ceil(ns > 0 ? ns : 1);
-    for (int i = ns + lane; i < n2; i += 32) ent[i] = Ent{-INFINITY, kNone, kNone};
-    __syncwarp();
-    warp_sort_ent(ent, n2, lane);
+    // A row of one unit holds its streamed entries in the reference's order already (its
+    // packs sorted in phase 2 and kept in list order: at most k of them, no selection);
+    // only penalised entries among them need the sort.
+    if (!(packs_sorted && pen_kept == 0)) {
+      const int n2 = pow2_ceil(ns > 0 ? ns : 1);
+      for (int i = ns + lane; i < n2; i += 32) ent[i] = Ent{-INFINITY, kNone, kNone};
+      __syncwarp();
+      warp_sort_ent(ent, n2, lane);
+    }
   }
 
   // ---- 4. top-k, filters, draw ----
