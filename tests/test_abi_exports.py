@@ -93,3 +93,23 @@ def test_compact_history_keeps_first_occurrence_order_and_counts(pkg):
     c = collections.Counter(window)
     assert counts == [c[i] for i in ids]
     assert pkg.compact_history([]) == ([], [])
+
+
+def test_history_count_must_match_the_history(pkg):
+    """history_count is read beside history with the same strides: mismatches are refused
+    on the host (no device needed)."""
+    import pytest
+    import torch
+    s = object.__new__(pkg.GpuSampler)  # make_batch needs no context
+    logits = torch.zeros((2, 64), dtype=torch.float32)
+    hist = torch.zeros((2, 8), dtype=torch.int32)
+    hlen = torch.full((2,), 8, dtype=torch.int32)
+    p = [dict(temperature=1.0, topK=5, topP=1.0, minP=0.0, typicalP=1.0, repetitionPenalty=1.1,
+              presencePenalty=0.0, frequencyPenalty=0.0)]
+    b, _ = s.make_batch(logits, p, history=hist, history_len=hlen, history_count=torch.ones((2, 8), dtype=torch.int32))
+    assert b.history_count != 0
+    for bad in (torch.ones((2, 7), dtype=torch.int32), torch.ones((2, 8), dtype=torch.int64)):
+        with pytest.raises(ValueError):
+            s.make_batch(logits, p, history=hist, history_len=hlen, history_count=bad)
+    with pytest.raises(ValueError):
+        s.make_batch(logits, p, history_count=torch.ones((2, 8), dtype=torch.int32))
