@@ -21,11 +21,22 @@
 
 namespace {
 
-gs_ctx* g_ctx = nullptr;
+// One gs_ctx per Node environment (the main thread and each worker thread), kept as the
+// environment's instance data and destroyed with it.
+void destroy_ctx(napi_env, void* data, void*) {
+  if (data) gs_destroy(static_cast<gs_ctx*>(data));
+}
 
-void destroy_ctx(void*) {
-  if (g_ctx) gs_destroy(g_ctx);
-  g_ctx = nullptr;
+gs_ctx* env_ctx(napi_env env, gs_status* st) {
+  void* data = nullptr;
+  *st = GS_OK;
+  if (napi_get_instance_data(env, &data) == napi_ok && data) return static_cast<gs_ctx*>(data);
+  const char* dev = std::getenv("GS_DEVICE");
+  gs_ctx* c = nullptr;
+  *st = gs_create(dev ? std::atoi(dev) : 0, &c);
+  if (*st != GS_OK) return nullptr;
+  napi_set_instance_data(env, c, destroy_ctx, nullptr);
+  return c;
 }
 
 napi_value throw_error(napi_env env, const std::string& msg) {
@@ -94,12 +105,9 @@ napi_value SampleHost(napi_env env, napi_callback_info info) {
   double softcap = 0.0;
   if (argc > 5) napi_get_value_double(env, argv[5], &softcap);
 
-  if (!g_ctx) {
-    const char* dev = std::getenv("GS_DEVICE");
-    const gs_status s = gs_create(dev ? std::atoi(dev) : 0, &g_ctx);
-    if (s != GS_OK) return throw_error(env, "gs_create failed (status " + std::to_string(s) + ")");
-    napi_add_env_cleanup_hook(env, destroy_ctx, nullptr);
-  }
+  gs_status cs = GS_OK;
+  gs_ctx* ctx = env_ctx(env, &cs);
+  if (!ctx) return throw_error(env, "gs_create failed (status " + std::to_string(cs) + ")");
   int32_t hlen = static_cast<int32_t>(n_ids);
   gs_batch b{};
   b.logits = logits;
@@ -122,10 +130,10 @@ napi_value SampleHost(napi_env env, napi_callback_info info) {
   gs_outputs o{};
   o.ids = &id;
   o.flags = &flags;
-  const gs_status s = gs_sample_host(g_ctx, &b, &o, nullptr);
+  const gs_status s = gs_sample_host(ctx, &b, &o, nullptr);
   if (s == GS_EEMPTY) return throw_error(env, "Cannot sample empty logits");
   if (s != GS_OK) {
-    const char* m = gs_last_error(g_ctx);
+    const char* m = gs_last_error(ctx);
     return throw_error(env, m && *m ? m : "gs_sample_host failed (status " + std::to_string(s) + ")");
   }
   if (const char* m = flag_error(flags)) return throw_error(env, m);

@@ -11,7 +11,19 @@
 // it would.
 import { createRequire } from "node:module";
 
-import type { DecodingConfig } from "../src/runtime/decoding";
+// The DecodingConfig fields sampleToken reads (src/runtime/decoding.ts:1-14); the
+// reference's own DecodingConfig is assignable to it.
+export interface DecodingConfig {
+  temperature: number;
+  topK: number;
+  topP: number;
+  minP: number;
+  typicalP: number;
+  repetitionPenalty: number;
+  repetitionWindow: number;
+  presencePenalty: number;
+  frequencyPenalty: number;
+}
 
 interface GsamplerAddon {
   sampleHost(

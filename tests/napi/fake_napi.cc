@@ -29,7 +29,8 @@ struct napi_env__ {
   std::vector<std::unique_ptr<napi_value__>> values;
   std::string error;
   bool thrown = false;
-  std::vector<std::pair<void (*)(void*), void*>> cleanup;
+  void* instance = nullptr;
+  napi_finalize instance_fin = nullptr;
   napi_value make() {
     values.emplace_back(new napi_value__());
     return values.back().get();
@@ -90,8 +91,13 @@ napi_status napi_create_function(napi_env env, const char*, size_t, napi_callbac
   (*r)->fn = cb;
   return napi_ok;
 }
-napi_status napi_add_env_cleanup_hook(napi_env env, void (*f)(void*), void* arg) {
-  env->cleanup.emplace_back(f, arg);
+napi_status napi_set_instance_data(napi_env env, void* data, napi_finalize fin, void*) {
+  env->instance = data;
+  env->instance_fin = fin;
+  return napi_ok;
+}
+napi_status napi_get_instance_data(napi_env env, void** data) {
+  *data = env->instance;
   return napi_ok;
 }
 napi_value napi_register_module_v1(napi_env, napi_value);
@@ -145,6 +151,6 @@ int main(int argc, char** argv) {
   } else {
     std::printf("id %d\n", static_cast<int>(r->num));
   }
-  for (auto& c : env.cleanup) c.first(c.second);
+  if (env.instance_fin) env.instance_fin(&env, env.instance, nullptr);  // (the environment's teardown)
   return 0;
 }

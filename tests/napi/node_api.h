@@ -12,6 +12,7 @@ typedef enum { napi_ok } napi_status;
 typedef enum { napi_int8_array, napi_uint8_array, napi_uint8_clamped_array, napi_int16_array, napi_uint16_array,
                napi_int32_array, napi_uint32_array, napi_float32_array, napi_float64_array } napi_typedarray_type;
 typedef napi_value (*napi_callback)(napi_env, napi_callback_info);
+typedef void (*napi_finalize)(napi_env, void*, void*);
 #define NAPI_AUTO_LENGTH SIZE_MAX
 extern "C" {
 napi_status napi_get_cb_info(napi_env, napi_callback_info, size_t*, napi_value*, napi_value*, void**);
@@ -23,7 +24,8 @@ napi_status napi_get_value_double(napi_env, napi_value, double*);
 napi_status napi_create_int32(napi_env, int32_t, napi_value*);
 napi_status napi_throw_error(napi_env, const char*, const char*);
 napi_status napi_create_function(napi_env, const char*, size_t, napi_callback, void*, napi_value*);
-napi_status napi_add_env_cleanup_hook(napi_env, void (*)(void*), void*);
+napi_status napi_set_instance_data(napi_env, void*, napi_finalize, void*);
+napi_status napi_get_instance_data(napi_env, void**);
 }
 #define NAPI_MODULE(name, init) extern "C" napi_value napi_register_module_v1(napi_env e, napi_value x) { return init(e, x); }
 #define NODE_GYP_MODULE_NAME gsampler
