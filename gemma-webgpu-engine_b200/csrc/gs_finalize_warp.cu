@@ -8,14 +8,17 @@
 // 4-items-per-lane prefix sums as the block version, so their decisions match it.
 //
 //   0. unit partials (lanes over the row's units)
-//   1. penalised ids: a shared-memory hash counts each history id's occurrences and keeps
-//      its first position; the entry of a distinct, allowed id is scored exactly
-//      (src/runtime/sampling.ts:26-30) in the slot of that first position
+//   1. penalised ids: a shared-memory hash counts each history id's occurrences (or adds
+//      the counts of gs_batch.history_count) and keeps its first position; the entry of a
+//      distinct, allowed id is scored exactly (src/runtime/sampling.ts:26-30) in the slot
+//      of that first position
 //   2. the units' candidate packs stream through a 256-entry buffer (threshold test,
-//      radix-select compaction) down to the row's k best
+//      radix-select compaction) down to the row's k best; a row of one unit (its packs
+//      prefetched into registers) sorts them there first, largest first
 //   3. maximum M, the penalised ids' normaliser terms (fixed slot order), then the entries
 //      that can reach the top k (key >= the k-th streamed candidate's) are compacted in
-//      place and sorted (logit/T desc, lower id first: src/runtime/sampling.ts:33-35)
+//      place and sorted (logit/T desc, lower id first: src/runtime/sampling.ts:33-35) --
+//      unless they are a one-unit row's sorted packs with no penalised entry among them
 //   4. top-k, masked-id filler, probabilities, min-p, typical-p, top-p, seeded draw
 //      (src/runtime/sampling.ts:44-64,82-90), log-probability, outputs
 #include "gs_device.cuh"
