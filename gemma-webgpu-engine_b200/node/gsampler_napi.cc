@@ -13,6 +13,7 @@
 // reference's messages.
 #include <node_api.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstdlib>
 #include <string>
@@ -98,6 +99,11 @@ napi_value SampleHost(napi_env env, napi_callback_info info) {
   p.frequency_penalty = number_prop(env, argv[3], "frequencyPenalty", &ok);
   const double top_k = number_prop(env, argv[3], "topK", &ok);
   if (!ok) return throw_error(env, "config must hold the DecodingConfig numbers");
+  // (gs_params.top_k is an int32: a topK that is not a non-negative integer is refused
+  // here with validateDecodingConfig's message, src/runtime/decoding.ts:35; the other
+  // fields are checked by the library)
+  if (!(top_k >= 0.0 && std::isfinite(top_k) && std::floor(top_k) == top_k))
+    return throw_error(env, "topK must be a non-negative integer");
   // topK beyond int32 keeps the whole vocabulary, as topK >= vocab does in the reference
   p.top_k = top_k > 2147483647.0 ? 2147483647 : static_cast<int32_t>(top_k);
   double uniform = 0.0;

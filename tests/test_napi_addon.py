@@ -49,6 +49,9 @@ def test_argument_errors_before_any_device_work(driver, tmp_path):
     assert call(driver, tmp_path, [], [], [], CFG, 0.5) == "Cannot sample empty logits"
     many = list(range(5000))
     assert "4096 distinct ids" in call(driver, tmp_path, [1.0, 2.0], many, [1] * len(many), CFG, 0.5)
+    for bad in (2.5, -1.0, float("nan"), float("inf")):  # validateDecodingConfig's topK rule
+        assert call(driver, tmp_path, [1.0, 2.0], [], [], dict(CFG, topK=bad), 0.5) == \
+            "topK must be a non-negative integer", bad
 
 
 @pytest.mark.gpu
