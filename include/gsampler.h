@@ -101,7 +101,8 @@ typedef struct gs_batch {
    * is one occurrence).  The penalties depend only on each id's count in the window
    * (src/runtime/sampling.ts:21-30), so a window longer than GS_MAX_HISTORY can be passed
    * as its distinct ids (in order of first occurrence) with their counts.  Values below 1
-   * count as 1.  No reference counterpart: the reference counts a JS array each call. */
+   * count as 1; the occurrences of one id, summed over its entries, must stay below 2^31.
+   * No reference counterpart: the reference counts a JS array each call. */
   const int32_t* history_count;
 } gs_batch;
 
